@@ -1,0 +1,98 @@
+/* ref_harness.c — drives the UNMODIFIED CachePotato engine (compiled from its own sources into
+ * oracle/_ref/libcpref.so by oracle/Makefile) on in-memory synthetic layers.
+ *
+ * TEST INFRASTRUCTURE ONLY: the reference side of the parity tests and the CPU baseline the
+ * benchmark times. This file is ours; the engine sources it links are the reference's, read in
+ * place and never copied.
+ *
+ * refh_qwen3_moe builds a QW3Layer (engine/blocks/qwen3_moe.h:21-69) whose attention half is
+ * all-zero f32 weights with one query and one KV head of width 2: q = k = v = 0 exactly, so the
+ * attention output is exactly 0 and the layer's MoE half (qwen3_moe.c:170-223) sees hh = x.
+ * It then calls the reference's qwen3_layer_kv as run_layers does (engine/api/cachepotato.c:149-166).
+ */
+#include "blocks/qwen3_moe.h"
+#include "kernels/kernels.h"
+#include "kernels/parallel.h"
+
+#include <stdlib.h>
+#include <string.h>
+
+int refh_init_threads(int n) { return cp_threads_init(n, 0); }
+int refh_threads(void) { return cp_threads(); }
+
+#define REFH_HD 2
+
+int refh_qwen3_moe(const float *ln2, const float *wgate, const void *const *exp, int exp_enc,
+                   int D, int F, int E, int K, float eps,
+                   const float *x, int T, float *mlp, float *router, int *topk_idx) {
+    QW3Layer m;
+    memset(&m, 0, sizeof m);
+    m.d_model = D; m.n_heads = 1; m.n_kv = 1; m.head_dim = REFH_HD;
+    m.d_exp = F; m.n_experts = E; m.topk = K; m.vocab = 0;
+    m.rope_theta = 1000000.0f; m.rms_eps = eps;
+
+    float *zeros = calloc((size_t)REFH_HD * D * 2 + 2 * REFH_HD, sizeof(float));
+    float *ones = malloc(sizeof(float) * (size_t)D);
+    QW3T *tab = calloc((size_t)E * 3, sizeof(QW3T));
+    if (!zeros || !ones || !tab) { free(zeros); free(ones); free(tab); return -2; }
+    for (int i = 0; i < D; i++) ones[i] = 1.0f;
+    float *hd_ones = zeros + (size_t)REFH_HD * D * 2;
+    hd_ones[0] = hd_ones[1] = hd_ones[2] = hd_ones[3] = 1.0f;
+
+    m.ln1 = ones;
+    m.ln2 = ln2;
+    m.q_norm = hd_ones;
+    m.k_norm = hd_ones + REFH_HD;
+    m.Wq.p = zeros; m.Wk.p = zeros; m.Wv.p = zeros;          /* (2, D) each, all zero */
+    m.Wo.p = zeros + (size_t)REFH_HD * D;                    /* (D, 2), all zero */
+    m.Wq.enc = m.Wk.enc = m.Wv.enc = m.Wo.enc = QW3_ENC_F32;
+    m.Wgate.p = wgate; m.Wgate.enc = QW3_ENC_F32;
+    for (int i = 0; i < E * 3; i++) { tab[i].p = exp[i]; tab[i].enc = exp_enc; }
+    m.exp = tab;
+
+    QW3KV kv;
+    QW3Out o;
+    int rc = -2;
+    if (qwen3_kv_alloc(&kv, &m, T) == 0) {
+        if (qwen3_layer_alloc(&o, &m, T) == 0) {
+            rc = qwen3_layer_kv(&m, x, T, 0, &kv, &o);
+            if (rc == 0) {
+                if (mlp) memcpy(mlp, o.mlp, sizeof(float) * (size_t)T * D);
+                if (router) memcpy(router, o.router, sizeof(float) * (size_t)T * E);
+                if (topk_idx) memcpy(topk_idx, o.topk_idx, sizeof(int) * (size_t)T * K);
+            }
+            qwen3_layer_free(&o);
+        }
+        qwen3_kv_free(&kv);
+    }
+    free(zeros); free(ones); free(tab);
+    return rc;
+}
+
+/* Externally routed experts through the reference's own qwen3_mm and silu: the expert loop of
+   qwen3_moe.c:199-222 with the routing decided by the caller (prefill / expert-parallel
+   workloads draw their token->expert assignment directly). */
+int refh_moe_apply(const void *const *exp, int exp_enc, int D, int F, const float *xn, int T,
+                   int K, const int *idx, const float *wt, float *mlp) {
+    int mx = F > D ? F : D;
+    float *gu = malloc(sizeof(float) * (size_t)mx);
+    float *hh = malloc(sizeof(float) * (size_t)mx);
+    if (!gu || !hh) { free(gu); free(hh); return -2; }
+    for (int t = 0; t < T; t++) {
+        const float *xt = xn + (size_t)t * D;
+        for (int j = 0; j < K; j++) {
+            const int e = idx[(size_t)t * K + j];
+            QW3T wg = { exp[(size_t)e * 3 + 0], exp_enc };
+            QW3T wu = { exp[(size_t)e * 3 + 1], exp_enc };
+            QW3T wd = { exp[(size_t)e * 3 + 2], exp_enc };
+            qwen3_mm(&wg, gu, xt, D, F);
+            qwen3_mm(&wu, hh, xt, D, F);
+            for (int i = 0; i < F; i++) gu[i] = silu(gu[i]) * hh[i];
+            qwen3_mm(&wd, hh, gu, F, D);
+            const float w = wt[(size_t)t * K + j];
+            for (int i = 0; i < D; i++) mlp[(size_t)t * D + i] += w * hh[i];
+        }
+    }
+    free(gu); free(hh);
+    return 0;
+}
