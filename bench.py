@@ -1,0 +1,370 @@
+#!/usr/bin/env python3
+"""Benchmark: Qwen3-30B-A3B-shaped MoE decode (Q4_0 experts) on B200.
+
+Workload: decode batch of 64 tokens through a stack of 48 distinct
+MoE layers (hidden 2048, 128 experts, top-8, intermediate 768, Q4_0 experts, f32 router whose
+rows are scaled so the expert load follows Zipf(1.1)). One step = one batch through all 48
+layers (router, experts, combine, residual), weights resident in HBM.
+
+  value   tok/s with activations already on the device (CUDA graph of the 48 layers)
+  e2e     tok/s through the host-buffer C entry point cpg_run_moe_layers: each step copies
+          the batch from pinned host memory, runs the layers, copies the result back
+  roofline  the gate/up expert kernel (the dominant launch), algorithmic bytes / its measured
+          duration (CUDA events inside the decode graph), against MEASURED_PEAKS.json
+  cpu_baseline  the reference engine (oracle/_ref: the reference's own C sources) on the host
+          cores, a bounded sample of the same workload
+
+--impl reference times the reference engine alone (rank 0), on the same metric and config.
+Multi-GPU: one process per GPU under torchrun; every rank runs its own replica (decode does not
+shard: 22 MB of weights per layer per token), value = all ranks' tokens / max-over-ranks time.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "decode tok/s & MoE-layer HBM GB/s (Qwen3-30B-A3B shape, Q4) at 1/2/4/8 B200"
+D, F, E, K = 2048, 768, 128, 8
+ENC_Q4 = 4
+MAT_BYTES = F * D // 32 * 18                     # 884,736
+REGION_BYTES = 3 * MAT_BYTES                     # 2,654,208 per expert (Wg | Wu | Wd)
+ROUTER_BYTES = E * D * 4
+LN_BYTES = D * 4
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--tokens", type=int, default=64)
+    ap.add_argument("--layers", type=int, default=48)
+    ap.add_argument("--zipf", type=float, default=1.1)
+    ap.add_argument("--seed", type=int, default=1234)
+    ap.add_argument("--cpu-sample-layers", type=int, default=2)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            j = json.load(f)
+        return float(j["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+# ------------------------------------------------------------------ clocks
+class Clocks:
+    """nvidia-smi sampling during the timed region."""
+
+    def __init__(self, dev: int):
+        self.dev, self.p, self.path = dev, None, None
+
+    def start(self):
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        self.path = f"/tmp/cpg_clocks_{os.getpid()}.csv"
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--id={self.dev}", f"--query-gpu={q}",
+                                       "--format=csv,noheader,nounits", "-lms", "200"],
+                                      stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.p = None
+
+    def stop(self):
+        if not self.p:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.p.terminate()
+        self.p.wait()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            f = [c.strip() for c in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        os.unlink(self.path)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx,
+                "samples": len(sm), "reasons": sorted(reasons)}
+
+
+# ------------------------------------------------------------------ device memory views
+class DevPtr:
+    """A raw device range as a torch tensor (via __cuda_array_interface__)."""
+
+    def __init__(self, ptr: int, nbytes: int, typestr: str = "|u1"):
+        item = int(typestr[-1])
+        self.__cuda_array_interface__ = {"shape": (nbytes // item,), "typestr": typestr,
+                                         "data": (ptr, False), "version": 2, "strides": None}
+
+
+def view(torch, ptr, nbytes, dtype="f4"):
+    ts = {"f4": "<f4", "u1": "|u1"}[dtype]
+    return torch.as_tensor(DevPtr(ptr, nbytes, ts), device="cuda")
+
+
+# ------------------------------------------------------------------ our implementation
+def build_stack(torch, L, T, zipf, seed, lib, Q):
+    """48 layers in the HBM region store, routers calibrated on the chained activations."""
+    from cachepotato_b200.workload import calibrate_router_scales, load_stats
+    layer_bytes = LN_BYTES + ROUTER_BYTES + E * REGION_BYTES
+    lib.cpg_store_close()
+    Q.check(lib.cpg_store_open(L * layer_bytes))
+    base = int(lib.cpg_store_base())
+    g = torch.Generator(device="cuda")
+    layers, stats = [], []
+    x = torch.randn((T, D), generator=g.manual_seed(seed), device="cuda", dtype=torch.float32)
+    x0 = x.clone()
+    for l in range(L):
+        off = l * layer_bytes
+        r_ln = lib.cpg_store_add_region(off, LN_BYTES, 0)
+        r_wg = lib.cpg_store_add_region(off + LN_BYTES, ROUTER_BYTES, 0)
+        r_ex = [lib.cpg_store_add_region(off + LN_BYTES + ROUTER_BYTES + e * REGION_BYTES, REGION_BYTES, 1)
+                for e in range(E)]
+        ln2 = view(torch, lib.cpg_store_region_get(r_ln), LN_BYTES)
+        ln2.fill_(1.0)
+        wg = view(torch, lib.cpg_store_region_get(r_wg), ROUTER_BYTES).view(E, D)
+        wg.copy_(torch.randn((E, D), generator=g.manual_seed(seed * 1000 + 2 * l + 1), device="cuda") * 0.02)
+        w32 = torch.randn(E * 3 * F * D, generator=g.manual_seed(seed * 1000 + 2 * l + 2), device="cuda")
+        w32.mul_(0.02)
+        Q.check(lib.cpg_quantize(lib.cpg_store_region_get(r_ex[0]), w32.data_ptr(), ENC_Q4, w32.numel(), None))
+        del w32
+        # Zipf calibration on this layer's actual input
+        xn = x * torch.rsqrt((x * x).mean(-1, keepdim=True) + 1e-6)
+        z = (xn @ wg.T).double().cpu().numpy()
+        s = calibrate_router_scales(z, K, zipf, seed=seed + l)
+        wg.mul_(torch.from_numpy(s).cuda()[:, None])
+        ptrs = []
+        for e in range(E):
+            b = lib.cpg_store_region_get(r_ex[e])
+            ptrs += [b, b + MAT_BYTES, b + 2 * MAT_BYTES]
+        layer = Q.MoELayer(ln2, wg, ENC_Q4, D, F, E, K, blob=None, expert_ptrs=ptrs)
+        out = layer.forward(x)
+        stats.append(load_stats(out.topk_idx.cpu().numpy(), E))
+        x = out.x_out
+        layers.append(layer)
+    torch.cuda.synchronize()
+    return layers, x0, stats
+
+
+def run_ours(args, rank, world, torch, dist):
+    from cachepotato_b200 import _lib
+    from cachepotato_b200 import qwen3 as Q
+    lib = _lib.lib()
+    T, L = args.tokens, args.layers
+    layers, x0, stats = build_stack(torch, L, T, args.zipf, args.seed, lib, Q)
+    ctx = Q.DecodeContext(layers[0], max_T=T, device=torch.cuda.current_device())
+    arr = ctx.layer_array(layers)
+    s = torch.cuda.ExternalStream(ctx.stream_ptr())
+    xbuf = view(torch, ctx.x_ptr(), T * D * 4).view(T, D)
+    xbytes = T * D * 4
+
+    def device_step():
+        with torch.cuda.stream(s):
+            xbuf.copy_(x0)                     # this step's batch enters the stack
+        ctx.run_device(arr, L, T)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    # ---- value: device-resident steps
+    for _ in range(args.warmup):
+        device_step()
+    barrier()
+    clocks = Clocks(torch.cuda.current_device())
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for _ in range(args.steps):
+        device_step()
+    e1.record(s)
+    barrier()
+    ms = e0.elapsed_time(e1)
+    # ---- the same steps with per-phase events inside the graph (roofline of each kernel)
+    ctx.profile(True)
+    phase = np.zeros(4)
+    for _ in range(max(1, args.warmup // 2)):
+        device_step()
+    for _ in range(args.steps):
+        device_step()
+        phase += np.array(ctx.phase_ms())
+    ctx.profile(False)
+    barrier()
+    clk = clocks.stop()
+    # ---- e2e: host buffers through cpg_run_moe_layers (H2D + layers + D2H each step)
+    pinned = [torch.empty((T, D), dtype=torch.float32).pin_memory() for _ in range(args.steps + args.warmup)]
+    x0h = x0.cpu()
+    for p in pinned:
+        p.copy_(x0h)
+    for i in range(args.warmup):
+        ctx.run_host_ptr(arr, L, pinned[i].data_ptr(), T)
+    barrier()
+    h0, h1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    h0.record(s)
+    for i in range(args.steps):
+        ctx.run_host_ptr(arr, L, pinned[args.warmup + i].data_ptr(), T)
+    h1.record(s)
+    barrier()
+    ms_e2e = h0.elapsed_time(h1)
+    # same final activations on both paths (the host path is the same graph)
+    dev_out = xbuf.cpu()
+    assert torch.equal(dev_out, pinned[-1]), "host-buffer path disagrees with the device path"
+
+    # max over ranks
+    t = torch.tensor([ms, ms_e2e], dtype=torch.float64, device="cuda")
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, ms_e2e = float(t[0]), float(t[1])
+    if rank != 0:
+        return None
+
+    U = [st["distinct_experts"] for st in stats]
+    step_bytes = sum(LN_BYTES + ROUTER_BYTES + u * REGION_BYTES + 2 * T * D * 4 for u in U)
+    gateup_bytes = sum(u * 2 * MAT_BYTES + T * D * 2 + T * K * F * 2 for u in U)
+    ms_step = ms / args.steps
+    hbm, kind = peaks()
+    gateup_ms_per_step = phase[1] / args.steps
+    achieved = gateup_bytes / (gateup_ms_per_step * 1e-3) / 1e9
+    tok_s = world * T * args.steps / (ms * 1e-3)
+    e2e_tok_s = world * T * args.steps / (ms_e2e * 1e-3)
+    res = {
+        "metric": METRIC, "value": round(tok_s, 1), "unit": "tok/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "q4_0 x f16 -> f32 (fp16 tensor-core MMA, fp32 accumulate)", "data": "synthetic",
+        "config": {"workload": "Qwen3-30B-A3B MoE decode: 64-token batch through 48 stacked MoE layers "
+                               "(BASELINE configs[1], Q4_0 experts, Zipf(1.1)-calibrated f32 router)",
+                   "tokens_per_step_per_gpu": T, "layers": L, "d_model": D, "d_exp": F, "experts": E,
+                   "topk": K, "expert_encoding": "Q4_0", "parallelism": f"replicas x{world}",
+                   "l2": "inputs larger than L2: each step streams ~13 GB of distinct expert weights"},
+        "moe_layer_hbm_gbs": round(step_bytes / (ms_step * 1e-3) / 1e9, 1),
+        "routing": {"distinct_experts_per_layer_mean": round(float(np.mean(U)), 1),
+                    "max_expert_load_mean": round(float(np.mean([st["max_load"] for st in stats])), 1)},
+        "phase_ms_per_step": {"router": round(phase[0] / args.steps, 4), "gate_up": round(phase[1] / args.steps, 4),
+                              "down": round(phase[2] / args.steps, 4), "combine": round(phase[3] / args.steps, 4)},
+        "roofline": {"bound": "hbm", "kernel": "k_experts<Q4,GATEUP>", "achieved": round(achieved, 1),
+                     "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),
+                     "peak_kind": kind,
+                     "algorithmic_bytes_per_launch": int(gateup_bytes / L), "traffic": None},
+        "e2e": {"value": round(e2e_tok_s, 1), "unit": "tok/s", "h2d_bytes_per_step": xbytes,
+                "d2h_bytes_per_step": xbytes},
+        "gpu_launches": 4 * L * args.steps,
+        "clocks": clk,
+    }
+    return res
+
+
+# ------------------------------------------------------------------ reference (CPU)
+def reference_sample(n_layers: int, T: int, zipf: float, seed: int, steps: int, warmup: int):
+    """The reference engine (oracle/_ref) on n_layers distinct layers, T tokens per pass."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    from cachepotato_b200.workload import calibrate_router_scales, rmsnorm_rows
+    ref = O.Reference(threads=os.cpu_count() or 1)
+    orc = O.Oracle()
+    x = orc.normal(T * D, seed, 1.0).reshape(T, D)
+    layers = []
+    xi = x
+    for l in range(n_layers):          # routers calibrated on the chained activations
+        L0 = O.SynthLayer(D, F, E, K, O.ENC_Q4, seed=seed + 17 * l, oracle=orc)
+        s = calibrate_router_scales(rmsnorm_rows(xi) @ L0.wgate.T, K, zipf, seed=seed + l)
+        L0.wgate *= s[:, None]
+        layers.append(L0)
+        xi = xi + ref.qwen3_moe(L0, xi)["mlp"]
+    times = []
+    for i in range(warmup + steps):
+        xi = x.copy()
+        t0 = time.perf_counter()
+        for L0 in layers:
+            r = ref.qwen3_moe(L0, xi)
+            xi = xi + r["mlp"]
+        dt = time.perf_counter() - t0
+        if i >= warmup:
+            times.append(dt)
+    per_layer = float(np.sum(times)) / (len(times) * n_layers)
+    return per_layer, ref.threads
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return None
+    T, L = args.tokens, args.layers
+    per_layer, threads = reference_sample(args.cpu_sample_layers, T, args.zipf, args.seed,
+                                          args.steps, args.warmup)
+    tok_s = T / (per_layer * L)
+    return {
+        "metric": METRIC, "impl": "reference", "value": round(tok_s, 3), "unit": "tok/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per_layer * L * 1e3, 2),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "q4_0 x f32 (AVX2 FMA)",
+        "data": "synthetic",
+        "config": {"workload": "Qwen3-30B-A3B MoE decode: 64-token batch through 48 stacked MoE layers "
+                               "(BASELINE configs[1], Q4_0 experts, Zipf(1.1)-calibrated f32 router)",
+                   "tokens_per_step_per_gpu": T, "layers": L, "parallelism": "reference engine, 1 process"},
+        "cpu_baseline": {"value": round(tok_s, 3), "unit": "tok/s", "cores": threads, "kind": "reference",
+                         "sample": f"{args.cpu_sample_layers} of {L} layers per step, T={T}; "
+                                   f"per-layer time x {L}"},
+        "e2e": {"value": round(tok_s, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        res = run_reference(args, rank)
+        if res is not None:
+            print(json.dumps(res), flush=True)
+        return
+    import torch
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    res = run_ours(args, rank, world, torch, dist)
+    if rank == 0 and not args.no_cpu_baseline and world == 1:
+        per_layer, threads = reference_sample(args.cpu_sample_layers, args.tokens, args.zipf,
+                                              args.seed, 2, 1)
+        res["cpu_baseline"] = {"value": round(args.tokens / (per_layer * args.layers), 3), "unit": "tok/s",
+                               "cores": threads, "kind": "reference",
+                               "sample": f"reference engine, {args.cpu_sample_layers} layers x 2 reps, "
+                                         f"T={args.tokens}, per-layer time x {args.layers}"}
+    if res is not None:
+        print(json.dumps(res), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,191 @@
+// matvec.cu — out[t] = W·x[t] for f32 / Q8_0 / Q4_0 row-major W, fp32 arithmetic throughout.
+//
+// The kernel-level entry points of the reference (matmul_wx, matmul_wx_q8, matmul_wx_q4 in
+// engine/kernels/kernels.c:84-95, 368-396, 514-540): each weight is decoded to (float)q * d
+// exactly and multiply-added in fp32, so results agree with the reference within its own
+// kernel-gate tolerance (rel 1e-5, tools/verify_q8_kernels.py). One warp per output row;
+// lanes take 64-value group pairs (36 B for Q4, 68 B for Q8, 4-byte aligned), x is staged in
+// shared memory, up to 8 vectors share each weight load.
+#include "common.cuh"
+
+namespace cpg {
+
+constexpr int MV_WARPS = 8;
+constexpr int MV_TOK = 8;          // vectors per pass (accumulators per lane)
+
+__device__ __forceinline__ int sext4(uint32_t v) { return (int)(v << 28) >> 28; }
+
+template <int ENC>
+__device__ __forceinline__ void row_partial(const uint8_t *__restrict__ row, int n_in,
+                                            const float *__restrict__ xs, int ntok, float acc[MV_TOK],
+                                            bool aligned4) {
+    const int lane = threadIdx.x & 31;
+    if (ENC == CPG_ENC_F32) {
+        const float *w = reinterpret_cast<const float *>(row);
+        for (int k = lane * 4; k < n_in; k += 128) {
+            const float4 wv = *reinterpret_cast<const float4 *>(w + k);
+#pragma unroll
+            for (int t = 0; t < MV_TOK; ++t) {
+                if (t < ntok) {
+                    const float4 xv = *reinterpret_cast<const float4 *>(xs + t * n_in + k);
+                    acc[t] = fmaf(wv.x, xv.x, acc[t]);
+                    acc[t] = fmaf(wv.y, xv.y, acc[t]);
+                    acc[t] = fmaf(wv.z, xv.z, acc[t]);
+                    acc[t] = fmaf(wv.w, xv.w, acc[t]);
+                }
+            }
+        }
+        return;
+    }
+    constexpr int GB = ENC == CPG_ENC_Q4 ? 18 : 34;
+    const int ng = n_in / 32;
+    if (aligned4 && (ng % 2) == 0) {
+        constexpr int NW = GB / 2;                      // words per group pair: 9 or 17
+        const int np = ng / 2;                          // x staged as xs[t][k][p] (k < 64)
+        for (int p = lane; p < np; p += 32) {
+            const uint32_t *wp = reinterpret_cast<const uint32_t *>(row + (size_t)p * 2 * GB);
+            uint32_t w[NW];
+#pragma unroll
+            for (int i = 0; i < NW; ++i) w[i] = __ldg(wp + i);
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+                const int b0 = half * GB;               // byte offset of this group in the span
+                const uint32_t sb = (w[b0 / 4] >> ((b0 % 4) * 8)) & 0xFFFFu;
+                const float d = f16_bits_to_f32(sb);
+                const float *xp = xs + (half * 32) * np + p;   // element (half*32 + k) at xp[k*np]
+                if (ENC == CPG_ENC_Q4) {
+#pragma unroll
+                    for (int k = 0; k < 16; ++k) {
+                        const int bo = b0 + 2 + k;
+                        const uint32_t byte = (w[bo / 4] >> ((bo % 4) * 8)) & 0xFFu;
+                        const float lo = __fmul_rn((float)sext4(byte), d);
+                        const float hi = __fmul_rn((float)sext4(byte >> 4), d);
+#pragma unroll
+                        for (int t = 0; t < MV_TOK; ++t) {
+                            if (t < ntok) {
+                                acc[t] = fmaf(lo, xp[t * n_in + k * np], acc[t]);
+                                acc[t] = fmaf(hi, xp[t * n_in + (k + 16) * np], acc[t]);
+                            }
+                        }
+                    }
+                } else {
+#pragma unroll
+                    for (int k = 0; k < 32; ++k) {
+                        const int bo = b0 + 2 + k;
+                        const int q = (int)(int8_t)((w[bo / 4] >> ((bo % 4) * 8)) & 0xFFu);
+                        const float v = __fmul_rn((float)q, d);
+#pragma unroll
+                        for (int t = 0; t < MV_TOK; ++t)
+                            if (t < ntok) acc[t] = fmaf(v, xp[t * n_in + k * np], acc[t]);
+                    }
+                }
+            }
+        }
+    } else {
+        // any alignment: one group per lane, byte loads; x staged as xs[t][k][g] (k < 32)
+        for (int g = lane; g < ng; g += 32) {
+            const uint8_t *blk = row + (size_t)g * GB;
+            const float d = f16_bits_to_f32((uint32_t)blk[0] | ((uint32_t)blk[1] << 8));
+            const float *xp = xs + g;
+            if (ENC == CPG_ENC_Q4) {
+                for (int k = 0; k < 16; ++k) {
+                    const uint32_t byte = blk[2 + k];
+                    const float lo = __fmul_rn((float)sext4(byte), d);
+                    const float hi = __fmul_rn((float)sext4(byte >> 4), d);
+#pragma unroll
+                    for (int t = 0; t < MV_TOK; ++t) {
+                        if (t < ntok) {
+                            acc[t] = fmaf(lo, xp[t * n_in + k * ng], acc[t]);
+                            acc[t] = fmaf(hi, xp[t * n_in + (k + 16) * ng], acc[t]);
+                        }
+                    }
+                }
+            } else {
+                for (int k = 0; k < 32; ++k) {
+                    const float v = __fmul_rn((float)(int8_t)blk[2 + k], d);
+#pragma unroll
+                    for (int t = 0; t < MV_TOK; ++t)
+                        if (t < ntok) acc[t] = fmaf(v, xp[t * n_in + k * ng], acc[t]);
+                }
+            }
+        }
+    }
+}
+
+template <int ENC>
+__global__ void __launch_bounds__(MV_WARPS * 32)
+k_matvec(float *__restrict__ out, const float *__restrict__ x, const uint8_t *__restrict__ w,
+         int n_in, int n_out, int T, int tok_per_cta, long rowbytes) {
+    extern __shared__ float xs[];                       // (tok_per_cta, n_in), lane-friendly order
+    const int t0 = blockIdx.y * tok_per_cta;
+    const int nt = min(tok_per_cta, T - t0);
+    const bool aligned4 = (((uintptr_t)w | (uintptr_t)rowbytes) & 3) == 0;
+    // element e of a vector goes to: f32 -> e; Q pairs -> (e%64)*np + e/64; Q groups -> (e%32)*ng + e/32
+    const int ng = n_in / 32;
+    const bool pairs = ENC != CPG_ENC_F32 && aligned4 && (ng % 2) == 0;
+    for (int i = threadIdx.x; i < nt * n_in; i += blockDim.x) {
+        const int t = i / n_in, e = i - t * n_in;
+        int o = e;
+        if (ENC != CPG_ENC_F32) o = pairs ? (e % 64) * (ng / 2) + e / 64 : (e % 32) * ng + e / 32;
+        xs[t * n_in + o] = x[(size_t)(t0 + t) * n_in + e];
+    }
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int r = blockIdx.x * MV_WARPS + warp; r < n_out; r += gridDim.x * MV_WARPS) {
+        const uint8_t *row = w + (size_t)r * rowbytes;
+        for (int tc = 0; tc < nt; tc += MV_TOK) {
+            float acc[MV_TOK];
+#pragma unroll
+            for (int t = 0; t < MV_TOK; ++t) acc[t] = 0.0f;
+            row_partial<ENC>(row, n_in, xs + tc * n_in, min(MV_TOK, nt - tc), acc, aligned4);
+#pragma unroll
+            for (int t = 0; t < MV_TOK; ++t) {
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) acc[t] += __shfl_xor_sync(0xffffffffu, acc[t], o);
+            }
+            if (lane == 0) {
+#pragma unroll
+                for (int t = 0; t < MV_TOK; ++t)
+                    if (tc + t < nt) out[(size_t)(t0 + tc + t) * n_out + r] = acc[t];
+            }
+        }
+    }
+}
+
+int matvec_launch(float *out, const float *x, cpg_tensor w, int n_in, int n_out, int T,
+                  cudaStream_t s) {
+    CPG_REQUIRE(out && x && w.p, "cpg_matvec: null pointer");
+    CPG_REQUIRE(n_in > 0 && n_out > 0 && T > 0, "cpg_matvec: empty shape (%d, %d, T=%d)", n_in, n_out, T);
+    CPG_REQUIRE(w.enc == CPG_ENC_F32 || w.enc == CPG_ENC_Q4 || w.enc == CPG_ENC_Q8,
+                "cpg_matvec: unknown encoding %d", w.enc);
+    CPG_REQUIRE(w.enc == CPG_ENC_F32 ? n_in % 4 == 0 : n_in % 32 == 0,
+                "cpg_matvec: n_in=%d not a multiple of the group size", n_in);
+    if (w.enc == CPG_ENC_F32)
+        CPG_REQUIRE(((uintptr_t)w.p & 15) == 0, "cpg_matvec: f32 weights must be 16-byte aligned");
+    const long rb = row_bytes(w.enc, n_in);
+    // tokens per CTA: as many as fit 96 KB of staged x
+    int tpc = (int)((96 * 1024) / ((long)n_in * 4));
+    CPG_REQUIRE(tpc >= 1, "cpg_matvec: n_in=%d too large to stage", n_in);
+    if (tpc > T) tpc = T;
+    const size_t smem = (size_t)tpc * n_in * sizeof(float);
+    const int ty = (T + tpc - 1) / tpc;
+    int gx = (n_out + MV_WARPS - 1) / MV_WARPS;
+    const int cap = sm_count() * 8;
+    if (gx > cap) gx = cap;
+    dim3 grid(gx, ty);
+    auto *kq4 = k_matvec<CPG_ENC_Q4>;
+    auto *kq8 = k_matvec<CPG_ENC_Q8>;
+    auto *kf = k_matvec<CPG_ENC_F32>;
+    auto *k = w.enc == CPG_ENC_Q4 ? kq4 : w.enc == CPG_ENC_Q8 ? kq8 : kf;
+    CPG_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024));
+    k<<<grid, MV_WARPS * 32, smem, s>>>(out, x, (const uint8_t *)w.p, n_in, n_out, T, tpc, rb);
+    CPG_CUDA(cudaGetLastError());
+    return CPG_OK;
+}
+
+}  // namespace cpg
+
+extern "C" int cpg_matvec(float *out, const float *x, cpg_tensor w, int n_in, int n_out, int T,
+                          void *stream) {
+    return cpg::matvec_launch(out, x, w, n_in, n_out, T, (cudaStream_t)stream);
+}

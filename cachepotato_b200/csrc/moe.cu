@@ -1,0 +1,839 @@
+// moe.cu — the Qwen3-MoE block (engine/blocks/qwen3_moe.c:169-223) on B200.
+//
+// Four launches per layer, all enqueued on one stream and free of host syncs:
+//   k_router   RMSNorm(x + attn), f32 router GEMV, softmax over experts, strict-'>' top-k,
+//              renormalisation (qwen3_moe.c:178-197); the last CTA of each token tile routes
+//              its tokens and the last tile groups the (token, slot) pairs by expert.
+//   k_experts<GATEUP>  per (expert, 16-row tile): gate and up GEMMs over that expert's tokens,
+//              h = silu(g)·u (qwen3_moe.c:217-219)
+//   k_experts<DOWN>    per (expert, 32-row tile): y = Wd·h (qwen3_moe.c:220)
+//   k_combine  mlp += sum_j wt_j·y_j in selection order (qwen3_moe.c:221) and the residual
+//              x + (attn + mlp) of run_layers (engine/api/cachepotato.c:157-159)
+//
+// Expert kernels: a producer warp streams weight rows from HBM into shared memory with 1D
+// TMA bulk copies (no multicast) through an mbarrier ring; four consumer warps decode Q4_0 /
+// Q8_0 groups in registers (exact integers in fp16) and feed mma.m16n8k16 with fp32
+// accumulators; the group scale is applied in fp32 after each group's MMAs. Tokens are the
+// N dimension (8 per MMA tile), weights are read exactly once per layer.
+#include <math.h>
+
+#include "common.cuh"
+#include "layout.cuh"
+
+namespace cpg {
+
+// ------------------------------------------------------------------ constants and layouts
+constexpr int R_TB = 8;          // router: tokens per CTA (one warp per token)
+constexpr int R_EB = 4;          // router: experts per CTA (two warps per expert)
+constexpr int R_THREADS = 256;
+constexpr int MAX_E = 256;
+constexpr int MAX_K = 32;
+
+constexpr int KIND_GATEUP = 0;
+constexpr int KIND_DOWN = 1;
+constexpr int EX_NW = 4;         // consumer warps per CTA
+constexpr int EX_NCH = 8;        // 8-column MMA tiles per pass (64 tokens)
+
+// workspace words
+enum { WS_STATUS = 0, WS_DONE_TILES = 1, WS_ITEMS_GATEUP = 2, WS_ITEMS_DOWN = 3, WS_HDR_INTS = 16 };
+
+struct WsLayout {
+    size_t tile_cnt, ex_cnt, ex_off, ex_list, n_active, pairs, topk, wt, logits, xn, h, y, total;
+    size_t memset_bytes;
+};
+
+static size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+static WsLayout ws_layout(int D, int F, int E, int K, int T) {
+    WsLayout L{};
+    size_t o = WS_HDR_INTS * sizeof(int);
+    L.tile_cnt = o; o += sizeof(int) * (size_t)((T + R_TB - 1) / R_TB);
+    L.memset_bytes = o;
+    o = align_up(o, 256);
+    L.ex_cnt = o; o += sizeof(int) * E;
+    L.ex_off = o; o += sizeof(int) * E;
+    L.ex_list = o; o += sizeof(int) * E;
+    L.n_active = o; o += sizeof(int);
+    o = align_up(o, 256);
+    L.pairs = o; o = align_up(o + sizeof(int) * (size_t)T * K, 256);
+    L.topk = o; o = align_up(o + sizeof(int) * (size_t)T * K, 256);
+    L.wt = o; o = align_up(o + sizeof(float) * (size_t)T * K, 256);
+    L.logits = o; o = align_up(o + sizeof(float) * (size_t)T * E, 256);
+    L.xn = o; o = align_up(o + sizeof(__half) * (size_t)T * D, 256);
+    L.h = o; o = align_up(o + sizeof(__half) * (size_t)T * K * F, 256);
+    L.y = o; o = align_up(o + sizeof(float) * (size_t)T * K * D, 256);
+    L.total = o;
+    return L;
+}
+
+__constant__ Perm64 c_perm[2] = {kPermQ4, kPermQ8};
+__device__ __forceinline__ const Perm64 &perm_of(int enc) { return c_perm[enc == CPG_ENC_Q4 ? 0 : 1]; }
+
+// ------------------------------------------------------------------ router
+struct RouterArgs {
+    const float *x, *attn, *ln2, *wgate;
+    int T, D, E, K;
+    float eps;
+    int xn_enc;                  // permutation of the xn copy the gate/up kernel reads
+    float *logits;
+    int *topk;
+    float *wt;
+    __half *xn_perm;
+    int *status;                 // workspace header
+    int *tile_cnt;
+    int *ex_cnt, *ex_off, *ex_list, *n_active, *pairs;
+};
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// softmax + top-k + renormalisation for one token, one warp (qwen3_moe.c:181-197)
+__device__ void route_token(const RouterArgs &a, int t) {
+    const int lane = threadIdx.x & 31;
+    constexpr int PL = MAX_E / 32;
+    float p[PL];
+    float mx = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < PL; ++i) {
+        const int e = lane + 32 * i;
+        p[i] = e < a.E ? __ldcg(a.logits + (size_t)t * a.E + e) : -INFINITY;
+        mx = fmaxf(mx, p[i]);
+    }
+    mx = warp_max(mx);
+    float sum = 0.0f;
+#pragma unroll
+    for (int i = 0; i < PL; ++i) {
+        const int e = lane + 32 * i;
+        p[i] = e < a.E ? expf(p[i] - mx) : 0.0f;
+        sum += p[i];
+    }
+    sum = warp_sum(sum);
+#pragma unroll
+    for (int i = 0; i < PL; ++i) p[i] = __fdiv_rn(p[i], sum);
+    uint32_t taken = 0;                       // bit i: expert lane + 32 i already selected
+    float sel_p[MAX_K];
+    int sel_e[MAX_K];
+    for (int j = 0; j < a.K; ++j) {
+        float bv = -1.0f;
+        int be = 0x7fffffff;
+#pragma unroll
+        for (int i = 0; i < PL; ++i) {
+            const int e = lane + 32 * i;
+            if (e < a.E && !((taken >> i) & 1u) && p[i] > bv) { bv = p[i]; be = e; }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {     // larger prob wins, equal prob: lower id (strict '>')
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oe = __shfl_xor_sync(0xffffffffu, be, o);
+            if (ov > bv || (ov == bv && oe < be)) { bv = ov; be = oe; }
+        }
+        if ((be & 31) == lane) taken |= 1u << (be >> 5);
+        if (j < MAX_K) { sel_p[j] = bv; sel_e[j] = be; }
+    }
+    if (lane == 0) {
+        float s = 0.0f;
+        for (int j = 0; j < a.K; ++j) s += sel_p[j];
+        for (int j = 0; j < a.K; ++j) {
+            a.topk[(size_t)t * a.K + j] = sel_e[j];
+            a.wt[(size_t)t * a.K + j] = __fdiv_rn(sel_p[j], s);
+        }
+    }
+}
+
+// group (token, slot) pairs by expert, tokens ascending inside an expert; one CTA
+__device__ void group_pairs(const RouterArgs &a) {
+    __shared__ int s_cnt[MAX_E], s_off[MAX_E], s_base[MAX_E];
+    __shared__ uint32_t s_mask[MAX_E];
+    const int tid = threadIdx.x;
+    for (int e = tid; e < a.E; e += blockDim.x) { s_cnt[e] = 0; s_base[e] = 0; }
+    __syncthreads();
+    const int TK = a.T * a.K;
+    for (int i = tid; i < TK; i += blockDim.x) atomicAdd(&s_cnt[__ldcg(a.topk + i)], 1);
+    __syncthreads();
+    if (tid == 0) {
+        int o = 0, u = 0;
+        for (int e = 0; e < a.E; ++e) {
+            s_off[e] = o;
+            o += s_cnt[e];
+            a.ex_cnt[e] = s_cnt[e];
+            a.ex_off[e] = s_off[e];
+            if (s_cnt[e] > 0) a.ex_list[u++] = e;
+        }
+        *a.n_active = u;
+    }
+    __syncthreads();
+    for (int c0 = 0; c0 < a.T; c0 += 32) {
+        for (int e = tid; e < a.E; e += blockDim.x) s_mask[e] = 0;
+        __syncthreads();
+        for (int i = tid; i < 32 * a.K; i += blockDim.x) {
+            const int tl = i / a.K, t = c0 + tl;
+            if (t < a.T) atomicOr(&s_mask[__ldcg(a.topk + (size_t)t * a.K + i % a.K)], 1u << tl);
+        }
+        __syncthreads();
+        for (int i = tid; i < 32 * a.K; i += blockDim.x) {
+            const int tl = i / a.K, j = i % a.K, t = c0 + tl;
+            if (t < a.T) {
+                const int e = __ldcg(a.topk + (size_t)t * a.K + j);
+                const int r = s_base[e] + __popc(s_mask[e] & ((1u << tl) - 1u));
+                a.pairs[s_off[e] + r] = t * a.K + j;
+            }
+        }
+        __syncthreads();
+        for (int e = tid; e < a.E; e += blockDim.x) s_base[e] += __popc(s_mask[e]);
+        __syncthreads();
+    }
+}
+
+__global__ void __launch_bounds__(R_THREADS) k_router(RouterArgs a) {
+    extern __shared__ float xs[];                         // (R_TB, D): hh, then xn
+    __shared__ float part[2][R_EB][R_TB];
+    __shared__ float s_inv[R_TB];
+    __shared__ int s_last;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int t0 = blockIdx.y * R_TB, nt = min(R_TB, a.T - t0);
+    const int e0 = blockIdx.x * R_EB;
+    const int D = a.D;
+
+    // hh = x + attn (qwen3_moe.c:178)
+    {
+        const float4 *x4 = reinterpret_cast<const float4 *>(a.x + (size_t)t0 * D);
+        const float4 *a4 = a.attn ? reinterpret_cast<const float4 *>(a.attn + (size_t)t0 * D) : nullptr;
+        float4 *s4 = reinterpret_cast<float4 *>(xs);
+        for (int i = tid; i < nt * D / 4; i += R_THREADS) {
+            float4 v = x4[i];
+            if (a4) {
+                const float4 b = a4[i];
+                v.x += b.x; v.y += b.y; v.z += b.z; v.w += b.w;
+            }
+            s4[i] = v;
+        }
+    }
+    __syncthreads();
+    // rmsnorm (kernels.c:408-413): inv = 1 / sqrt(sum(x^2)/n + eps); xn = x * inv * g
+    if (warp < nt) {
+        float ss = 0.0f;
+        for (int k = lane; k < D; k += 32) ss = fmaf(xs[warp * D + k], xs[warp * D + k], ss);
+        ss = warp_sum(ss);
+        if (lane == 0) s_inv[warp] = __fdiv_rn(1.0f, __fsqrt_rn(__fdiv_rn(ss, (float)D) + a.eps));
+    }
+    __syncthreads();
+    for (int i = tid; i < nt * D; i += R_THREADS) {
+        const int t = i / D, k = i - t * D;
+        xs[i] = __fmul_rn(__fmul_rn(xs[i], s_inv[t]), a.ln2[k]);
+    }
+    __syncthreads();
+    if (blockIdx.x == 0) {
+        // fp16 copy of xn in the expert kernels' K order
+        const Perm64 &pm = perm_of(a.xn_enc);
+        for (int i = tid; i < nt * D; i += R_THREADS) {
+            const int t = i / D, pos = i - t * D;
+            const int k = (pos & ~63) + pm.pos_to_elem[pos & 63];
+            a.xn_perm[(size_t)(t0 + t) * D + pos] = __float2half_rn(xs[t * D + k]);
+        }
+    }
+    // logits = Wgate·xn (matmul_wx, kernels.c:84-95): warp -> (expert e0 + w%4, half w/4)
+    {
+        const int el = warp & 3, half = warp >> 2, e = e0 + el;
+        float acc[R_TB];
+#pragma unroll
+        for (int t = 0; t < R_TB; ++t) acc[t] = 0.0f;
+        if (e < a.E) {
+            const int k0 = half * (D / 2), k1 = k0 + D / 2;
+            const float4 *w4 = reinterpret_cast<const float4 *>(a.wgate + (size_t)e * D);
+            for (int k = k0 + lane * 4; k < k1; k += 128) {
+                const float4 w = __ldg(w4 + k / 4);
+#pragma unroll
+                for (int t = 0; t < R_TB; ++t) {
+                    if (t < nt) {
+                        const float4 v = *reinterpret_cast<const float4 *>(xs + t * D + k);
+                        acc[t] = fmaf(w.x, v.x, acc[t]);
+                        acc[t] = fmaf(w.y, v.y, acc[t]);
+                        acc[t] = fmaf(w.z, v.z, acc[t]);
+                        acc[t] = fmaf(w.w, v.w, acc[t]);
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int t = 0; t < R_TB; ++t) {
+            const float v = warp_sum(acc[t]);
+            if (lane == 0) part[half][el][t] = v;
+        }
+    }
+    __syncthreads();
+    if (tid < R_EB * R_TB) {
+        const int el = tid / R_TB, t = tid % R_TB;
+        if (t < nt && e0 + el < a.E)
+            a.logits[(size_t)(t0 + t) * a.E + e0 + el] = part[0][el][t] + part[1][el][t];
+    }
+    // last CTA of this token tile routes its tokens
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) s_last = atomicAdd(a.tile_cnt + blockIdx.y, 1) == (int)gridDim.x - 1;
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    if (warp < nt) route_token(a, t0 + warp);
+    // last tile groups all pairs by expert
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) s_last = atomicAdd(a.status + WS_DONE_TILES, 1) == (int)gridDim.y - 1;
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    group_pairs(a);
+}
+
+// ------------------------------------------------------------------ experts
+struct ExpertArgs {
+    const uint8_t *const *ptrs;  // (E, 3) device matrix pointers
+    int D, F, K;
+    const int *ex_cnt, *ex_off, *ex_list, *n_active, *pairs;
+    const __half *bsrc;          // GATEUP: xn_perm (T, D); DOWN: h_perm (pairs, F)
+    __half *h_out;               // GATEUP output (pairs, F), permuted for Wd
+    float *y_out;                // DOWN output (T*K, D), row = t*K + j
+    int h_enc;                   // encoding of Wd (permutation of h_out)
+    int *status;
+    int *item_ctr;
+    int stages;
+    int rs;                      // shared-memory row stride (bytes)
+};
+
+template <int ENC, int KIND>
+struct ExCfg {
+    static constexpr int GB = ENC == CPG_ENC_Q4 ? 18 : 34;
+    static constexpr int WPP = GB / 2;                 // 32-bit words per group pair
+    static constexpr int MATS = KIND == KIND_GATEUP ? 2 : 1;
+    static constexpr int MT = KIND == KIND_GATEUP ? 1 : 2;
+    static constexpr int COMBOS = MATS * MT;           // 16-row tiles per item
+    static constexpr int KS = EX_NW / COMBOS;          // K split across warps
+    static constexpr int ROWS = 16 * MT;               // output rows per item per matrix
+};
+
+struct StageMeta { int item, m, off, cnt; };
+
+template <int ENC>
+__device__ __forceinline__ void load_pair_words(const uint32_t *row, int P, int t, uint32_t &w1,
+                                                uint32_t &w2, uint32_t &w3, uint32_t &w4, float &d0,
+                                                float &d1) {
+    if (ENC == CPG_ENC_Q4) {
+        const uint32_t *s = row + P * 9;
+        const uint32_t wa = s[1 + t], w0 = s[0], wq = s[4], wb = s[5 + t];
+        w1 = t == 3 ? __byte_perm(w0, wq, 0x5432) : wa;
+        w2 = wb;
+        w3 = 0; w4 = 0;
+        d0 = __half2float(__ushort_as_half((unsigned short)(w0 & 0xFFFFu)));
+        d1 = __half2float(__ushort_as_half((unsigned short)(wq >> 16)));
+    } else {
+        const uint32_t *s = row + P * 17;
+        const uint32_t wa = s[1 + t], wb = s[5 + t], w0 = s[0], w8 = s[8], wc = s[9 + t], wd = s[13 + t];
+        w1 = wa;
+        w2 = t == 3 ? __byte_perm(w0, w8, 0x5432) : wb;
+        w3 = wc;
+        w4 = wd;
+        d0 = __half2float(__ushort_as_half((unsigned short)(w0 & 0xFFFFu)));
+        d1 = __half2float(__ushort_as_half((unsigned short)(w8 >> 16)));
+    }
+}
+
+// Q4 word -> two k16 steps of one row: {lo(b0),lo(b2)}, {hi(b0),hi(b2)}, {lo(b1),lo(b3)}, {hi(b1),hi(b3)}
+__device__ __forceinline__ void q4_word(uint32_t w, uint32_t &sA0, uint32_t &sA2, uint32_t &sB0, uint32_t &sB2) {
+    const uint32_t k1032 = 0x64086408u, k1_16 = 0x2C002C00u, km72 = 0xD480D480u;
+    const uint32_t w2 = w >> 8;
+    sA0 = hsub2_u32(lop3_and_xor(w, 0x000F000Fu, 0x64086408u), k1032);
+    sA2 = hfma2_u32(lop3_and_xor(w, 0x00F000F0u, 0x64806480u), k1_16, km72);
+    sB0 = hsub2_u32(lop3_and_xor(w2, 0x000F000Fu, 0x64086408u), k1032);
+    sB2 = hfma2_u32(lop3_and_xor(w2, 0x00F000F0u, 0x64806480u), k1_16, km72);
+}
+
+// Q8 word -> one k16 step of one row: {b0,b1}, {b2,b3}
+__device__ __forceinline__ void q8_word(uint32_t w, uint32_t &s0, uint32_t &s2) {
+    const uint32_t x = w ^ 0x80808080u, k1152 = 0x64806480u;
+    s0 = hsub2_u32(__byte_perm(x, 0x64646464u, 0x4140), k1152);
+    s2 = hsub2_u32(__byte_perm(x, 0x64646464u, 0x4342), k1152);
+}
+
+template <int ENC, int KIND>
+__global__ void __launch_bounds__((1 + EX_NW) * 32) k_experts(ExpertArgs a) {
+    using C = ExCfg<ENC, KIND>;
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int S = a.stages, RS = a.rs;
+    const int K_in = KIND == KIND_GATEUP ? a.D : a.F;
+    const int n_rows = KIND == KIND_GATEUP ? a.F : a.D;
+    const int RB = (K_in / 32) * C::GB;
+    const int NP = K_in / 64;
+    const int stage_bytes = C::COMBOS * 16 * RS;
+    float *red = reinterpret_cast<float *>(smem + (size_t)S * stage_bytes);     // (NW, NCH, 32, 4)
+    StageMeta *meta = reinterpret_cast<StageMeta *>(red + EX_NW * EX_NCH * 128);
+    uint64_t *full = reinterpret_cast<uint64_t *>(meta + S);
+    uint64_t *empty = full + S;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int tiles_per_expert = n_rows / C::ROWS;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], EX_NW);
+        }
+        fence_mbar_init();
+    }
+    __syncthreads();
+
+    if (warp == 0) {
+        // ---------------- producer: one thread streams weight rows into the stage ring
+        if (lane != 0) return;
+        const int total = *a.n_active * tiles_per_expert;
+        int it = 0;
+        bool ok = true;
+        for (;; ++it) {
+            const int st = it % S;
+            const uint32_t ph = (uint32_t)(it / S) & 1u;
+            if (it >= S && !mbar_wait(&empty[st], ph ^ 1u)) {
+                atomicCAS(a.status + WS_STATUS, ST_OK, ST_TIMEOUT_EMPTY);
+                ok = false;
+                break;
+            }
+            const int item = atomicAdd(a.item_ctr, 1);
+            if (item >= total) {
+                meta[st].item = -1;
+                mbar_arrive(&full[st]);
+                ++it;
+                break;
+            }
+            const int u = item / tiles_per_expert, m = item - u * tiles_per_expert;
+            const int e = a.ex_list[u];
+            meta[st] = StageMeta{item, m, a.ex_off[e], a.ex_cnt[e]};
+            mbar_arrive_expect_tx(&full[st], (uint32_t)(C::COMBOS * 16 * RB));
+            uint8_t *dst = smem + (size_t)st * stage_bytes;
+#pragma unroll
+            for (int c = 0; c < C::COMBOS; ++c) {
+                const int mat = KIND == KIND_GATEUP ? c : 2;          // gate, up / down
+                const int r0 = m * C::ROWS + (KIND == KIND_GATEUP ? 0 : c * 16);
+                const uint8_t *src = a.ptrs[e * 3 + mat] + (size_t)r0 * RB;
+                uint8_t *d = dst + c * 16 * RS;
+                if (RS == RB) {
+                    bulk_g2s(d, src, 16 * RB, &full[st]);
+                } else {
+                    for (int r = 0; r < 16; ++r) bulk_g2s(d + r * RS, src + (size_t)r * RB, RB, &full[st]);
+                }
+            }
+        }
+        // keep the CTA alive until every issued copy has landed (also on the timeout path)
+        if (!ok) {
+            for (int k = 1; k <= S && it - k >= 0; ++k) {
+                const int j = it - k;
+                mbar_wait(&full[j % S], (uint32_t)(j / S) & 1u);
+            }
+        }
+        return;
+    }
+
+    // ---------------- consumers
+    const int cw = warp - 1;
+    const int combo = cw % C::COMBOS, kp = cw / C::COMBOS;
+    const int g = lane >> 2, t = lane & 3;
+    const Perm64 &hperm = perm_of(a.h_enc);
+    __shared__ int s_abort;
+    if (threadIdx.x == 32) s_abort = 0;
+    named_bar_sync(1, EX_NW * 32);
+    for (int it = 0;; ++it) {
+        const int st = it % S;
+        const uint32_t ph = (uint32_t)(it / S) & 1u;
+        // every consumer warp reaches the barrier (the wait is bounded), so a timeout seen by
+        // any warp ends the loop for all of them at the same point
+        if (!mbar_wait(&full[st], ph) && lane == 0) {
+            s_abort = 1;
+            atomicCAS(a.status + WS_STATUS, ST_OK, ST_TIMEOUT_FULL);
+        }
+        named_bar_sync(1, EX_NW * 32);
+        if (s_abort) break;
+        const StageMeta md = meta[st];
+        if (md.item < 0) break;
+        const uint32_t *rows = reinterpret_cast<const uint32_t *>(smem + (size_t)st * stage_bytes + combo * 16 * RS);
+        const uint32_t *rowg = rows + (g * RS) / 4;
+        const uint32_t *rowg8 = rows + ((g + 8) * RS) / 4;
+        const int ntiles = (md.cnt + 7) / 8;
+        for (int nc0 = 0; nc0 < ntiles; nc0 += EX_NCH) {
+            const int ntl = min(EX_NCH, ntiles - nc0);
+            // B row pointers for column g of each n-tile (nullptr = zero padding)
+            const __half *brow[EX_NCH];
+#pragma unroll
+            for (int nt = 0; nt < EX_NCH; ++nt) {
+                const int col = (nc0 + nt) * 8 + g;
+                brow[nt] = nullptr;
+                if (nt < ntl && col < md.cnt) {
+                    const int p = md.off + col;
+                    if (KIND == KIND_GATEUP) brow[nt] = a.bsrc + (size_t)(a.pairs[p] / a.K) * a.D;
+                    else brow[nt] = a.bsrc + (size_t)p * a.F;
+                }
+            }
+            float acc[EX_NCH][4];
+#pragma unroll
+            for (int nt = 0; nt < EX_NCH; ++nt)
+#pragma unroll
+                for (int c = 0; c < 4; ++c) acc[nt][c] = 0.0f;
+
+            for (int P = kp; P < NP; P += C::KS) {
+                uint32_t fr[4][4];       // [k16 step][a0..a3]
+                float dj[2], dj1[2];     // scales: group j / j+1, rows g / g+8
+                {
+                    uint32_t w1, w2, w3, w4;
+                    load_pair_words<ENC>(rowg, P, t, w1, w2, w3, w4, dj[0], dj1[0]);
+                    if (ENC == CPG_ENC_Q4) {
+                        q4_word(w1, fr[0][0], fr[0][2], fr[1][0], fr[1][2]);
+                        q4_word(w2, fr[2][0], fr[2][2], fr[3][0], fr[3][2]);
+                    } else {
+                        q8_word(w1, fr[0][0], fr[0][2]);
+                        q8_word(w2, fr[1][0], fr[1][2]);
+                        q8_word(w3, fr[2][0], fr[2][2]);
+                        q8_word(w4, fr[3][0], fr[3][2]);
+                    }
+                    load_pair_words<ENC>(rowg8, P, t, w1, w2, w3, w4, dj[1], dj1[1]);
+                    if (ENC == CPG_ENC_Q4) {
+                        q4_word(w1, fr[0][1], fr[0][3], fr[1][1], fr[1][3]);
+                        q4_word(w2, fr[2][1], fr[2][3], fr[3][1], fr[3][3]);
+                    } else {
+                        q8_word(w1, fr[0][1], fr[0][3]);
+                        q8_word(w2, fr[1][1], fr[1][3]);
+                        q8_word(w3, fr[2][1], fr[2][3]);
+                        q8_word(w4, fr[3][1], fr[3][3]);
+                    }
+                }
+#pragma unroll
+                for (int nt = 0; nt < EX_NCH; ++nt) {
+                    if (nt < ntl) {
+                        uint4 b01 = make_uint4(0, 0, 0, 0), b23 = make_uint4(0, 0, 0, 0);
+                        if (brow[nt]) {
+                            const uint4 *bp = reinterpret_cast<const uint4 *>(brow[nt] + P * 64 + t * 16);
+                            b01 = __ldg(bp);
+                            b23 = __ldg(bp + 1);
+                        }
+                        const float z[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                        float sj[4], sj1[4];
+                        mma_16816(sj, fr[0], b01.x, b01.y, z);
+                        mma_16816(sj, fr[1], b01.z, b01.w, sj);
+                        mma_16816(sj1, fr[2], b23.x, b23.y, z);
+                        mma_16816(sj1, fr[3], b23.z, b23.w, sj1);
+#pragma unroll
+                        for (int c = 0; c < 4; ++c) {
+                            acc[nt][c] = fmaf(dj[c >> 1], sj[c], acc[nt][c]);
+                            acc[nt][c] = fmaf(dj1[c >> 1], sj1[c], acc[nt][c]);
+                        }
+                    }
+                }
+            }
+            if (nc0 + EX_NCH >= ntiles) {
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty[st]);     // this warp is done with the stage
+            }
+            // cross-warp reduction of the K split, then the epilogue
+#pragma unroll
+            for (int nt = 0; nt < EX_NCH; ++nt)
+                if (nt < ntl)
+                    *reinterpret_cast<float4 *>(red + ((cw * EX_NCH + nt) * 32 + lane) * 4) =
+                        make_float4(acc[nt][0], acc[nt][1], acc[nt][2], acc[nt][3]);
+            named_bar_sync(1, EX_NW * 32);
+            const int ctid = threadIdx.x - 32;
+            if (KIND == KIND_GATEUP) {
+                // element (nt, l, c): gate = combo 0, up = combo 1; K parts at warps combo + 2*kp
+                for (int i = ctid; i < ntl * 128; i += EX_NW * 32) {
+                    const int nt = i >> 7, l = (i >> 2) & 31, c = i & 3;
+                    float gsum = 0.0f, usum = 0.0f;
+#pragma unroll
+                    for (int k = 0; k < C::KS; ++k) {
+                        gsum += red[(((0 + 2 * k) * EX_NCH + nt) * 32 + l) * 4 + c];
+                        usum += red[(((1 + 2 * k) * EX_NCH + nt) * 32 + l) * 4 + c];
+                    }
+                    const int col = (nc0 + nt) * 8 + 2 * (l & 3) + (c & 1);
+                    if (col < md.cnt) {
+                        const int row = md.m * 16 + (l >> 2) + 8 * (c >> 1);          // feature in [0, F)
+                        const float silu = gsum / (1.0f + expf(-gsum));             // kernels.c:416
+                        const float h = silu * usum;                                 // qwen3_moe.c:219
+                        const int pos = (row & ~63) + hperm.elem_to_pos[row & 63];
+                        a.h_out[(size_t)(md.off + col) * a.F + pos] = __float2half_rn(h);
+                    }
+                }
+            } else {
+                for (int i = ctid; i < C::COMBOS * ntl * 128; i += EX_NW * 32) {
+                    const int cb = i / (ntl * 128), r = i - cb * ntl * 128;
+                    const int nt = r >> 7, l = (r >> 2) & 31, c = r & 3;
+                    float v = 0.0f;
+#pragma unroll
+                    for (int k = 0; k < C::KS; ++k) v += red[(((cb + C::COMBOS * k) * EX_NCH + nt) * 32 + l) * 4 + c];
+                    const int col = (nc0 + nt) * 8 + 2 * (l & 3) + (c & 1);
+                    if (col < md.cnt) {
+                        const int row = md.m * C::ROWS + cb * 16 + (l >> 2) + 8 * (c >> 1);   // in [0, D)
+                        a.y_out[(size_t)a.pairs[md.off + col] * a.D + row] = v;
+                    }
+                }
+            }
+            named_bar_sync(1, EX_NW * 32);
+        }
+        if (ntiles == 0) {                              // cannot happen for an active expert
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[st]);
+        }
+    }
+}
+
+// ------------------------------------------------------------------ combine
+__global__ void k_combine(const float *__restrict__ x, const float *__restrict__ attn, int T, int D, int K,
+                          const float *__restrict__ wt, const float *__restrict__ y, float *mlp, float *x_out) {
+    const int n4 = T * D / 4;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += gridDim.x * blockDim.x) {
+        const int t = (i * 4) / D, k = i * 4 - t * D;
+        float4 acc = mlp ? reinterpret_cast<const float4 *>(mlp)[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int j = 0; j < K; ++j) {            // qwen3_moe.c:221, selection order, no fusion
+            const float w = wt[t * K + j];
+            const float4 v = *reinterpret_cast<const float4 *>(y + ((size_t)t * K + j) * D + k);
+            acc.x = __fadd_rn(acc.x, __fmul_rn(w, v.x));
+            acc.y = __fadd_rn(acc.y, __fmul_rn(w, v.y));
+            acc.z = __fadd_rn(acc.z, __fmul_rn(w, v.z));
+            acc.w = __fadd_rn(acc.w, __fmul_rn(w, v.w));
+        }
+        if (mlp) reinterpret_cast<float4 *>(mlp)[i] = acc;
+        if (x_out) {
+            const float4 xv = reinterpret_cast<const float4 *>(x)[i];
+            float4 av = attn ? reinterpret_cast<const float4 *>(attn)[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+            reinterpret_cast<float4 *>(x_out)[i] =
+                make_float4(xv.x + (av.x + acc.x), xv.y + (av.y + acc.y), xv.z + (av.z + acc.z), xv.w + (av.w + acc.w));
+        }
+    }
+}
+
+// ------------------------------------------------------------------ host side
+struct KernelPlan {
+    int stages = 0, rs = 0, ctas = 0;
+    size_t smem = 0;
+};
+
+}  // namespace cpg
+
+struct cpg_moe_layer {
+    int D, F, E, K;
+    float eps;
+    int enc;                       // expert encoding (Q4 or Q8)
+    const float *ln2;
+    const float *wgate;
+    const uint8_t **d_ptrs;        // device (E, 3)
+    cpg::KernelPlan gateup, down;
+};
+
+namespace cpg {
+
+static int smem_row_stride(int rb) { return (rb / 16) % 2 == 0 ? rb + 16 : rb; }
+
+template <int ENC, int KIND>
+static int plan_kernel(int K_in, KernelPlan &p) {
+    using C = ExCfg<ENC, KIND>;
+    const int rb = (K_in / 32) * C::GB;
+    p.rs = smem_row_stride(rb);
+    const int stage = C::COMBOS * 16 * p.rs;
+    const size_t fixed = sizeof(float) * EX_NW * EX_NCH * 128 + 8 * (sizeof(StageMeta) + 16) + 128;
+    int S = (int)((110 * 1024 - fixed) / stage);
+    if (S < 2) S = 2;
+    if (S > 8) S = 8;
+    while (S > 1 && fixed + (size_t)S * stage > 227 * 1024) --S;
+    CPG_REQUIRE(S >= 1, "expert kernel: a %d-byte stage does not fit in shared memory", stage);
+    p.stages = S;
+    p.smem = (size_t)S * stage + sizeof(float) * EX_NW * EX_NCH * 128 + S * sizeof(StageMeta) + 2 * S * sizeof(uint64_t);
+    auto *k = k_experts<ENC, KIND>;
+    CPG_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem));
+    int per_sm = 0;
+    CPG_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, (1 + EX_NW) * 32, p.smem));
+    CPG_REQUIRE(per_sm >= 1, "expert kernel: no CTA fits on an SM");
+    p.ctas = per_sm * sm_count();
+    return CPG_OK;
+}
+
+static int launch_experts(const cpg_moe_layer *L, int KIND, const ExpertArgs &a, int max_items, cudaStream_t s) {
+    const KernelPlan &p = KIND == KIND_GATEUP ? L->gateup : L->down;
+    const int grid = max_items < p.ctas ? (max_items > 0 ? max_items : 1) : p.ctas;
+    ExpertArgs b = a;
+    b.stages = p.stages;
+    b.rs = p.rs;
+    const dim3 block((1 + EX_NW) * 32);
+    if (L->enc == CPG_ENC_Q4) {
+        if (KIND == KIND_GATEUP) k_experts<CPG_ENC_Q4, KIND_GATEUP><<<grid, block, p.smem, s>>>(b);
+        else k_experts<CPG_ENC_Q4, KIND_DOWN><<<grid, block, p.smem, s>>>(b);
+    } else {
+        if (KIND == KIND_GATEUP) k_experts<CPG_ENC_Q8, KIND_GATEUP><<<grid, block, p.smem, s>>>(b);
+        else k_experts<CPG_ENC_Q8, KIND_DOWN><<<grid, block, p.smem, s>>>(b);
+    }
+    CPG_CUDA(cudaGetLastError());
+    return CPG_OK;
+}
+
+}  // namespace cpg
+
+namespace cpg {
+int layer_dims(const cpg_moe_layer *L, int *D, int *F, int *E, int *K) {
+    CPG_REQUIRE(L, "null layer");
+    *D = L->D; *F = L->F; *E = L->E; *K = L->K;
+    return CPG_OK;
+}
+}  // namespace cpg
+
+using namespace cpg;
+
+extern "C" int cpg_moe_layer_create(const cpg_moe_desc *d, cpg_moe_layer **out) {
+    CPG_REQUIRE(d && out, "cpg_moe_layer_create: null argument");
+    *out = nullptr;
+    CPG_REQUIRE(d->d_model > 0 && d->d_model % 256 == 0, "d_model=%d must be a positive multiple of 256", d->d_model);
+    CPG_REQUIRE(d->d_exp > 0 && d->d_exp % 256 == 0, "d_exp=%d must be a positive multiple of 256", d->d_exp);
+    CPG_REQUIRE(d->n_experts > 0 && d->n_experts <= MAX_E, "n_experts=%d outside [1, %d]", d->n_experts, MAX_E);
+    CPG_REQUIRE(d->topk > 0 && d->topk <= MAX_K && d->topk <= d->n_experts, "topk=%d outside [1, min(%d, n_experts)]", d->topk, MAX_K);
+    CPG_REQUIRE(d->ln2 && d->wgate.p && d->experts, "cpg_moe_layer_create: null tensor");
+    CPG_REQUIRE(d->wgate.enc == CPG_ENC_F32, "router weights must be f32 (the reference keeps Wgate f32)");
+    CPG_REQUIRE(((uintptr_t)d->wgate.p & 15) == 0, "router weights must be 16-byte aligned");
+    const int enc = d->experts[0].enc;
+    CPG_REQUIRE(enc == CPG_ENC_Q4 || enc == CPG_ENC_Q8, "expert encoding %d is not Q4_0/Q8_0", enc);
+    const int E = d->n_experts;
+    const uint8_t **h = (const uint8_t **)malloc(sizeof(void *) * 3 * E);
+    CPG_REQUIRE(h != nullptr, "host allocation failed");
+    for (int i = 0; i < 3 * E; ++i) {
+        if (!d->experts[i].p || d->experts[i].enc != enc || ((uintptr_t)d->experts[i].p & 15)) {
+            free(h);
+            CPG_REQUIRE(false, "expert tensor %d (expert %d kind %d): null, unaligned or encoding != %d", i, i / 3, i % 3, enc);
+        }
+        h[i] = (const uint8_t *)d->experts[i].p;
+    }
+    cpg_moe_layer *L = new cpg_moe_layer();
+    L->D = d->d_model; L->F = d->d_exp; L->E = E; L->K = d->topk; L->eps = d->rms_eps;
+    L->enc = enc; L->ln2 = d->ln2; L->wgate = (const float *)d->wgate.p;
+    cudaError_t ce = cudaMalloc((void **)&L->d_ptrs, sizeof(void *) * 3 * E);
+    if (ce == cudaSuccess) ce = cudaMemcpy(L->d_ptrs, h, sizeof(void *) * 3 * E, cudaMemcpyHostToDevice);
+    free(h);
+    if (ce != cudaSuccess) {
+        cudaFree(L->d_ptrs);
+        delete L;
+        return cuda_fail(ce, "cpg_moe_layer_create: expert table upload");
+    }
+    int rc;
+    if (enc == CPG_ENC_Q4) {
+        rc = plan_kernel<CPG_ENC_Q4, KIND_GATEUP>(L->D, L->gateup);
+        if (rc == CPG_OK) rc = plan_kernel<CPG_ENC_Q4, KIND_DOWN>(L->F, L->down);
+    } else {
+        rc = plan_kernel<CPG_ENC_Q8, KIND_GATEUP>(L->D, L->gateup);
+        if (rc == CPG_OK) rc = plan_kernel<CPG_ENC_Q8, KIND_DOWN>(L->F, L->down);
+    }
+    if (rc == CPG_OK) {
+        const int rsmem = R_TB * L->D * (int)sizeof(float);
+        CPG_REQUIRE(rsmem <= 200 * 1024, "d_model=%d too large for the router kernel", L->D);
+        cudaError_t e2 = cudaFuncSetAttribute(k_router, cudaFuncAttributeMaxDynamicSharedMemorySize, rsmem);
+        if (e2 != cudaSuccess) rc = cuda_fail(e2, "router smem attribute");
+    }
+    if (rc != CPG_OK) {
+        cudaFree(L->d_ptrs);
+        delete L;
+        return rc;
+    }
+    *out = L;
+    return CPG_OK;
+}
+
+extern "C" void cpg_moe_layer_destroy(cpg_moe_layer *L) {
+    if (!L) return;
+    cudaFree(L->d_ptrs);
+    delete L;
+}
+
+extern "C" size_t cpg_moe_workspace_bytes(const cpg_moe_layer *L, int max_T) {
+    if (!L || max_T <= 0) return 0;
+    return ws_layout(L->D, L->F, L->E, L->K, max_T).total;
+}
+
+namespace cpg {
+// ev (optional, 5 events): recorded before the router, gate/up, down and combine launches and
+// after the combine, so a caller can time each phase on the stream it runs on.
+int moe_forward_impl(const cpg_moe_layer *L, const float *x, const float *attn, int T, float *mlp,
+                     float *x_out, int *topk_idx, float *wt, float *router, void *ws, size_t ws_bytes,
+                     cudaStream_t s, cudaEvent_t *ev);
+}
+
+extern "C" int cpg_moe_forward(const cpg_moe_layer *L, const float *x, const float *attn, int T,
+                               float *mlp, float *x_out, int *topk_idx, float *wt, float *router,
+                               void *ws, size_t ws_bytes, void *stream) {
+    return moe_forward_impl(L, x, attn, T, mlp, x_out, topk_idx, wt, router, ws, ws_bytes,
+                            (cudaStream_t)stream, nullptr);
+}
+
+int cpg::moe_forward_impl(const cpg_moe_layer *L, const float *x, const float *attn, int T, float *mlp,
+                          float *x_out, int *topk_idx, float *wt, float *router, void *ws, size_t ws_bytes,
+                          cudaStream_t s, cudaEvent_t *ev) {
+    CPG_REQUIRE(L && x && ws, "cpg_moe_forward: null argument");
+    CPG_REQUIRE(T > 0, "cpg_moe_forward: T=%d", T);
+    const WsLayout W = ws_layout(L->D, L->F, L->E, L->K, T);
+    CPG_REQUIRE(ws_bytes >= W.total, "cpg_moe_forward: workspace %zu < %zu bytes for T=%d", ws_bytes, W.total, T);
+    CPG_REQUIRE((((uintptr_t)x | (uintptr_t)attn | (uintptr_t)mlp | (uintptr_t)x_out | (uintptr_t)ws) & 15) == 0,
+                "cpg_moe_forward: buffers must be 16-byte aligned");
+    uint8_t *w = (uint8_t *)ws;
+    int *hdr = (int *)w;
+    if (ev) CPG_CUDA(cudaEventRecord(ev[0], s));
+    CPG_CUDA(cudaMemsetAsync(w, 0, W.memset_bytes, s));
+
+    RouterArgs ra{};
+    ra.x = x; ra.attn = attn; ra.ln2 = L->ln2; ra.wgate = L->wgate;
+    ra.T = T; ra.D = L->D; ra.E = L->E; ra.K = L->K; ra.eps = L->eps; ra.xn_enc = L->enc;
+    ra.logits = router ? router : (float *)(w + W.logits);
+    ra.topk = topk_idx ? topk_idx : (int *)(w + W.topk);
+    ra.wt = wt ? wt : (float *)(w + W.wt);
+    ra.xn_perm = (__half *)(w + W.xn);
+    ra.status = hdr;
+    ra.tile_cnt = (int *)(w + W.tile_cnt);
+    ra.ex_cnt = (int *)(w + W.ex_cnt); ra.ex_off = (int *)(w + W.ex_off);
+    ra.ex_list = (int *)(w + W.ex_list); ra.n_active = (int *)(w + W.n_active);
+    ra.pairs = (int *)(w + W.pairs);
+    dim3 rgrid((L->E + R_EB - 1) / R_EB, (T + R_TB - 1) / R_TB);
+    k_router<<<rgrid, R_THREADS, (size_t)R_TB * L->D * sizeof(float), s>>>(ra);
+    CPG_CUDA(cudaGetLastError());
+
+    ExpertArgs ea{};
+    ea.ptrs = L->d_ptrs; ea.D = L->D; ea.F = L->F; ea.K = L->K;
+    ea.ex_cnt = ra.ex_cnt; ea.ex_off = ra.ex_off; ea.ex_list = ra.ex_list; ea.n_active = ra.n_active;
+    ea.pairs = ra.pairs; ea.h_enc = L->enc; ea.status = hdr;
+    const int max_active = T * L->K < L->E ? T * L->K : L->E;
+
+    ea.bsrc = ra.xn_perm;
+    ea.h_out = (__half *)(w + W.h);
+    ea.item_ctr = hdr + WS_ITEMS_GATEUP;
+    if (ev) CPG_CUDA(cudaEventRecord(ev[1], s));
+    int rc = launch_experts(L, KIND_GATEUP, ea, max_active * (L->F / 16), s);
+    if (rc) return rc;
+
+    ea.bsrc = (const __half *)(w + W.h);
+    ea.y_out = (float *)(w + W.y);
+    ea.item_ctr = hdr + WS_ITEMS_DOWN;
+    if (ev) CPG_CUDA(cudaEventRecord(ev[2], s));
+    rc = launch_experts(L, KIND_DOWN, ea, max_active * (L->D / 32), s);
+    if (rc) return rc;
+
+    const int n4 = T * L->D / 4;
+    int cgrid = (n4 + 255) / 256;
+    if (cgrid > sm_count() * 8) cgrid = sm_count() * 8;
+    if (ev) CPG_CUDA(cudaEventRecord(ev[3], s));
+    k_combine<<<cgrid, 256, 0, s>>>(x, attn, T, L->D, L->K, ra.wt, (const float *)(w + W.y), mlp, x_out);
+    CPG_CUDA(cudaGetLastError());
+    if (ev) CPG_CUDA(cudaEventRecord(ev[4], s));
+    return CPG_OK;
+}
+
+extern "C" int cpg_moe_check(const void *ws, void *stream) {
+    CPG_REQUIRE(ws, "cpg_moe_check: null workspace");
+    int st = 0;
+    CPG_CUDA(cudaStreamSynchronize((cudaStream_t)stream));
+    CPG_CUDA(cudaMemcpy(&st, ws, sizeof(int), cudaMemcpyDeviceToHost));
+    if (st != ST_OK) {
+        set_error("device-side wait timed out (status %d)", st);
+        return CPG_ETIMEOUT;
+    }
+    return CPG_OK;
+}

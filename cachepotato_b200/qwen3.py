@@ -1,0 +1,244 @@
+"""Host-side mirror of the reference interface for the Qwen3-MoE expert path.
+
+Names follow the reference: the kernel entry points of engine/kernels/kernels.h
+(matmul_wx, matmul_wx_q8, matmul_wx_q4, q8_dequant_row, q4_dequant_row) take host numpy
+arrays, overwrite `out` and raise on failure; qwen3_mm is the encoding dispatch of
+engine/blocks/qwen3_moe.c:36-40; MoELayer is the MoE half of QW3Layer / qwen3_layer_kv
+(engine/blocks/qwen3_moe.h:21-95). Device memory is torch CUDA tensors (plumbing only); every
+computation runs in libcpg_b200.so.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import numpy as np
+
+from . import _lib
+from ._lib import ENC_F32, ENC_Q4, ENC_Q8, GROUP_BYTES, MoeDesc, Tensor, check, lib
+
+
+def row_bytes(enc: int, n_in: int) -> int:
+    return 4 * n_in if enc == ENC_F32 else (n_in // 32) * GROUP_BYTES[enc]
+
+
+def _np_ptr(a: np.ndarray) -> int:
+    return a.ctypes.data
+
+
+# ------------------------------------------------------------------ kernels.h mirror (host)
+def _host_mm(fn, out: np.ndarray, x: np.ndarray, w: np.ndarray, n_in: int, n_out: int) -> None:
+    assert out.dtype == np.float32 and out.flags.c_contiguous and out.size >= n_out
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    fn(_np_ptr(out), _np_ptr(x), _np_ptr(np.ascontiguousarray(w)), n_in, n_out)
+    err = _lib.last_error()          # the void drop-ins clear it on entry
+    if err:
+        raise _lib.CpgError(_lib.CPG_EINVAL, err)
+
+
+def matmul_wx(out: np.ndarray, x: np.ndarray, w: np.ndarray, n_in: int, n_out: int) -> None:
+    """out[i] = sum_k w[i*n_in+k] x[k] (engine/kernels/kernels.c:84)."""
+    _host_mm(lib().cpg_matmul_wx, out, x, np.ascontiguousarray(w, dtype=np.float32), n_in, n_out)
+
+
+def matmul_wx_q8(out: np.ndarray, x: np.ndarray, w: np.ndarray, n_in: int, n_out: int) -> None:
+    """Q8_0 row-major W·x (engine/kernels/kernels.c:368)."""
+    _host_mm(lib().cpg_matmul_wx_q8, out, x, w, n_in, n_out)
+
+
+def matmul_wx_q4(out: np.ndarray, x: np.ndarray, w: np.ndarray, n_in: int, n_out: int) -> None:
+    """Q4_0 row-major W·x (engine/kernels/kernels.c:514)."""
+    _host_mm(lib().cpg_matmul_wx_q4, out, x, w, n_in, n_out)
+
+
+def _host_dq(fn, blocks: np.ndarray, out: np.ndarray, n: int) -> None:
+    assert out.dtype == np.float32 and out.size >= n
+    fn(_np_ptr(np.ascontiguousarray(blocks, dtype=np.uint8)), _np_ptr(out), n)
+    err = _lib.last_error()
+    if err:
+        raise _lib.CpgError(_lib.CPG_EINVAL, err)
+
+
+def q8_dequant_row(blocks: np.ndarray, out: np.ndarray, n: int) -> None:
+    """Bit-exact Q8_0 decode (engine/kernels/kernels.c:143)."""
+    _host_dq(lib().cpg_q8_dequant_row, blocks, out, n)
+
+
+def q4_dequant_row(blocks: np.ndarray, out: np.ndarray, n: int) -> None:
+    """Bit-exact Q4_0 decode (engine/kernels/kernels.c:463)."""
+    _host_dq(lib().cpg_q4_dequant_row, blocks, out, n)
+
+
+# ------------------------------------------------------------------ device entry points
+def _torch():
+    import torch
+    return torch
+
+
+def _stream_ptr(stream) -> int:
+    torch = _torch()
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return int(s.cuda_stream)
+
+
+def dequant(blocks, n: int, enc: int, stream=None):
+    """Device decode of n values -> float32 tensor (bit-exact with the reference)."""
+    torch = _torch()
+    out = torch.empty(n, dtype=torch.float32, device=blocks.device)
+    check(lib().cpg_dequant(out.data_ptr(), blocks.data_ptr(), enc, n, _stream_ptr(stream)))
+    return out
+
+
+def quantize(x, enc: int, stream=None):
+    """Device encode of a float32 tensor -> uint8 blocks (bit-exact with format/q4.py, q8.py)."""
+    torch = _torch()
+    x = x.contiguous()
+    out = torch.empty(x.numel() // 32 * GROUP_BYTES[enc], dtype=torch.uint8, device=x.device)
+    check(lib().cpg_quantize(out.data_ptr(), x.data_ptr(), enc, x.numel(), _stream_ptr(stream)))
+    return out
+
+
+def qwen3_mm(w, enc: int, x, n_in: int, n_out: int, stream=None):
+    """out (T, n_out) = W·x[t] for x (T, n_in) on the device (qwen3_moe.c:36-40)."""
+    torch = _torch()
+    x = x.contiguous().view(-1, n_in)
+    T = x.shape[0]
+    out = torch.empty((T, n_out), dtype=torch.float32, device=x.device)
+    check(lib().cpg_matvec(out.data_ptr(), x.data_ptr(), Tensor(w.data_ptr(), enc), n_in, n_out, T,
+                           _stream_ptr(stream)))
+    return out
+
+
+@dataclass
+class MoEOutputs:
+    mlp: object
+    x_out: object
+    router: object
+    topk_idx: object
+    wt: object
+
+
+class MoELayer:
+    """The MoE half of one Qwen3 layer, weights resident on the device.
+
+    ln2 (d_model) f32, wgate (n_experts, d_model) f32, and the experts either as one blob
+    with a fixed region stride (Wg | Wu | Wd per expert, as CPW1 v4 lays them out) or as a
+    list of 3*n_experts device pointers.
+    """
+
+    def __init__(self, ln2, wgate, enc: int, d_model: int, d_exp: int, n_experts: int, topk: int,
+                 eps: float = 1e-6, blob=None, expert_ptrs=None, keep=()):
+        self.d_model, self.d_exp, self.n_experts, self.topk, self.enc, self.eps = (
+            d_model, d_exp, n_experts, topk, enc, eps)
+        mat = d_exp * d_model // 32 * GROUP_BYTES[enc]
+        self.mat_bytes, self.region_bytes = mat, 3 * mat
+        if expert_ptrs is None:
+            base = blob.data_ptr()
+            expert_ptrs = [base + e * 3 * mat + k * mat for e in range(n_experts) for k in range(3)]
+        tab = (Tensor * (3 * n_experts))()
+        for i, p in enumerate(expert_ptrs):
+            tab[i] = Tensor(p, enc)
+        desc = MoeDesc(d_model, d_exp, n_experts, topk, eps, ln2.data_ptr(), Tensor(wgate.data_ptr(), ENC_F32),
+                       ctypes.cast(tab, ctypes.POINTER(Tensor)))
+        h = ctypes.c_void_p()
+        check(lib().cpg_moe_layer_create(ctypes.byref(desc), ctypes.byref(h)))
+        self.handle = h
+        self._keep = (ln2, wgate, blob, tab) + tuple(keep)   # keep device memory alive
+
+    def __del__(self):
+        h = getattr(self, "handle", None)
+        if h is not None and h.value:
+            try:
+                lib().cpg_moe_layer_destroy(h)
+            except Exception:
+                pass
+            self.handle = None
+
+    def workspace_bytes(self, max_T: int) -> int:
+        return int(lib().cpg_moe_workspace_bytes(self.handle, max_T))
+
+    def workspace(self, max_T: int):
+        torch = _torch()
+        return torch.zeros(self.workspace_bytes(max_T), dtype=torch.uint8, device="cuda")
+
+    def forward(self, x, attn=None, *, ws=None, mlp=None, want_x_out=True, stream=None,
+                check_status=True) -> MoEOutputs:
+        """qwen3_layer_kv's MoE half for x (T, d_model) on the device."""
+        torch = _torch()
+        x = x.contiguous()
+        T = x.shape[0]
+        if ws is None:
+            ws = self.workspace(T)
+        dev = x.device
+        router = torch.empty((T, self.n_experts), dtype=torch.float32, device=dev)
+        topk = torch.empty((T, self.topk), dtype=torch.int32, device=dev)
+        wt = torch.empty((T, self.topk), dtype=torch.float32, device=dev)
+        if mlp is None:
+            mlp = torch.zeros((T, self.d_model), dtype=torch.float32, device=dev)
+        x_out = torch.empty_like(x) if want_x_out else None
+        sp = _stream_ptr(stream)
+        check(lib().cpg_moe_forward(self.handle, x.data_ptr(), None if attn is None else attn.contiguous().data_ptr(),
+                                    T, mlp.data_ptr(), None if x_out is None else x_out.data_ptr(),
+                                    topk.data_ptr(), wt.data_ptr(), router.data_ptr(), ws.data_ptr(),
+                                    ws.numel(), sp))
+        if check_status:
+            check(lib().cpg_moe_check(ws.data_ptr(), sp))
+        return MoEOutputs(mlp, x_out, router, topk, wt)
+
+
+class DecodeContext:
+    """cpg_ctx: the host-buffer decode loop (run_layers' MoE half, cachepotato.c:149-166)."""
+
+    def __init__(self, shape_layer: MoELayer, max_T: int, device: int = 0):
+        h = ctypes.c_void_p()
+        check(lib().cpg_ctx_create(device, max_T, shape_layer.handle, ctypes.byref(h)))
+        self.handle = h
+        self.topk = shape_layer.topk
+
+    def stream_ptr(self) -> int:
+        return int(lib().cpg_ctx_stream(self.handle) or 0)
+
+    def run(self, layers, x: np.ndarray, want_topk: bool = False):
+        """x (T, d_model) host f32 (ideally pinned), updated in place: x += mlp_l per layer."""
+        assert x.dtype == np.float32 and x.flags.c_contiguous
+        L, T = len(layers), x.shape[0]
+        arr = (ctypes.c_void_p * L)(*[l.handle.value for l in layers])
+        topk = np.empty((L, T, self.topk), np.int32) if want_topk else None
+        check(lib().cpg_run_moe_layers(self.handle, arr, L, x.ctypes.data, T,
+                                       None if topk is None else topk.ctypes.data))
+        return topk
+
+    @staticmethod
+    def layer_array(layers):
+        return (ctypes.c_void_p * len(layers))(*[l.handle.value for l in layers])
+
+    def run_host_ptr(self, arr, L: int, x_ptr: int, T: int) -> None:
+        """cpg_run_moe_layers on a host pointer (e.g. a pinned torch tensor)."""
+        check(lib().cpg_run_moe_layers(self.handle, arr, L, x_ptr, T, None))
+
+    def run_device(self, arr, L: int, T: int) -> None:
+        """cpg_ctx_run: the layers on the context's device activations, no copies, no sync."""
+        check(lib().cpg_ctx_run(self.handle, arr, L, T))
+
+    def x_ptr(self) -> int:
+        return int(lib().cpg_ctx_x(self.handle))
+
+    def topk_ptr(self) -> int:
+        return int(lib().cpg_ctx_topk(self.handle))
+
+    def profile(self, on: bool) -> None:
+        check(lib().cpg_ctx_profile(self.handle, 1 if on else 0))
+
+    def phase_ms(self):
+        out = (ctypes.c_float * 4)()
+        check(lib().cpg_ctx_phase_ms(self.handle, out))
+        return [float(v) for v in out]
+
+    def __del__(self):
+        h = getattr(self, "handle", None)
+        if h is not None and h.value:
+            try:
+                lib().cpg_ctx_destroy(h)
+            except Exception:
+                pass
+            self.handle = None

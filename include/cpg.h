@@ -1,0 +1,161 @@
+/* cpg.h — C ABI of cachepotato_b200: the Qwen3-MoE expert hot path of CachePotato on B200.
+ *
+ * Plain C: pointers, sizes and int status codes; no CUDA or torch types. `stream` arguments
+ * are a cudaStream_t passed as void* (NULL = the legacy default stream). Device pointers are
+ * CUDA global memory; "host" entry points take ordinary host memory and are synchronous.
+ *
+ * Status codes: every int-returning entry returns CPG_OK (0) or a negative CPG_E* code and
+ * leaves a message for cpg_last_error(). The drop-ins with the reference's void signatures
+ * report failures on stderr and through cpg_last_error(), as the reference reports through
+ * stderr (engine/kernels/kernels.h has no error channel).
+ *
+ * Each declaration names the reference interface it replaces (paths relative to the
+ * CachePotato source tree).
+ */
+#ifndef CPG_H
+#define CPG_H
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define CPG_OK        0
+#define CPG_EINVAL   (-1)   /* bad argument or unsupported shape */
+#define CPG_ECUDA    (-2)   /* a CUDA runtime call failed */
+#define CPG_ETIMEOUT (-3)   /* a bounded device-side wait ran out (status word set) */
+#define CPG_ENOMEM   (-4)   /* device or pinned allocation failed */
+#define CPG_ENCCL    (-5)   /* collective failure (expert-parallel path) */
+#define CPG_ESTATE   (-6)   /* call out of order (e.g. store not open) */
+
+/* Tensor encodings: the same codes as QW3_ENC_* (engine/blocks/qwen3_moe.h:15-17). */
+#define CPG_ENC_F32 0
+#define CPG_ENC_Q8  8       /* Q8_0: 34-byte group = fp16 scale + 32 int8 (format/SPEC.md) */
+#define CPG_ENC_Q4  4       /* Q4_0: 18-byte group = fp16 scale + 16 bytes of nibbles */
+
+/* A weight tensor: pointer + encoding. Mirrors QW3T (engine/blocks/qwen3_moe.h:19). */
+typedef struct { const void *p; int enc; } cpg_tensor;
+
+/* Message of the last failure on this host thread ("" if none). */
+const char *cpg_last_error(void);
+/* Library version, major*10000 + minor*100 + patch. */
+int cpg_version(void);
+
+/* ============================================================== kernel drop-ins (host)
+ * Same signatures and meaning as engine/kernels/kernels.h:17,21-24 and kernels.c:368 /
+ * kernels.c:514: out = W·x with W row-major (n_out, n_in) in the given encoding, n_in % 32 == 0,
+ * out OVERWRITTEN. Host pointers, synchronous. When `w` lies inside the range mirrored by
+ * cpg_store_open_v4 the resident device copy is used (translated by offset, like
+ * pager_region_get); otherwise the rows are copied to the device for the call. */
+void cpg_matmul_wx(float *out, const float *x, const float *w, int n_in, int n_out);       /* kernels.c:84 */
+void cpg_matmul_wx_q8(float *out, const float *x, const uint8_t *w, int n_in, int n_out);  /* kernels.c:368 */
+void cpg_matmul_wx_q4(float *out, const float *x, const uint8_t *w, int n_in, int n_out);  /* kernels.c:514 */
+/* Bit-exact decoders: kernels.c:143 (Q8_0) and kernels.c:463 (Q4_0); n % 32 == 0. */
+void cpg_q8_dequant_row(const uint8_t *blocks, float *out, int n);
+void cpg_q4_dequant_row(const uint8_t *blocks, float *out, int n);
+
+/* ============================================================== device-pointer kernels */
+/* Decode n values (n % 32 == 0) of a Q4_0/Q8_0 block stream, bit-exact with kernels.c:143/463. */
+int cpg_dequant(float *out, const uint8_t *blocks, int enc, long n, void *stream);
+/* Encode n f32 values (n % 32 == 0) to Q4_0/Q8_0 blocks, bit-exact with format/q4.py:30-57 and
+   format/q8.py:35-58 (the reference's encoders). */
+int cpg_quantize(uint8_t *blocks, const float *x, int enc, long n, void *stream);
+/* T independent products out[t] = W·x[t], x (T, n_in) and out (T, n_out) row-major f32,
+   f32 accumulation (kernels.c:84-95 / 287-396 / 480-540 arithmetic). Replaces qwen3_mm
+   (engine/blocks/qwen3_moe.c:36-40) for device-resident tensors. */
+int cpg_matvec(float *out, const float *x, cpg_tensor w, int n_in, int n_out, int T, void *stream);
+
+/* ============================================================== region store
+ * HBM-resident replacement for the pager's region table (engine/pager/pager.h:51-66).
+ * One store per process and device, like the pager (pager.c:195-214). The whole data section
+ * of a mapped CPW1 v4 file is copied to HBM once, through pinned staging buffers; region ids
+ * are region-table indices exactly as pager_add_region hands them out. */
+int cpg_store_open_v4(const void *map_base, size_t map_len, size_t data_off);          /* pager_open_v4 */
+/* An empty store of `bytes` bytes (synthetic workloads); fill it through cpg_store_base(). */
+int cpg_store_open(size_t bytes);
+int cpg_store_add_region(size_t off, size_t len, int is_expert);                       /* pager_add_region: id or <0 */
+const void *cpg_store_region_get(int id);                                             /* pager_region_get: device address */
+/* Device address of a host pointer inside the mirrored mapping, NULL if outside. */
+const void *cpg_store_translate(const void *host_ptr);
+void *cpg_store_base(void);
+size_t cpg_store_bytes(void);
+typedef struct { long regions, expert_regions; long resident_bytes; long h2d_bytes; } cpg_store_totals_t;
+int cpg_store_totals(cpg_store_totals_t *out);                                         /* pager_totals */
+void cpg_store_close(void);
+
+/* ============================================================== MoE block
+ * The MoE half of qwen3_layer_kv (engine/blocks/qwen3_moe.c:169-223) plus the residual add of
+ * run_layers (engine/api/cachepotato.c:157-159):
+ *   hh = x + attn; xn = rmsnorm(hh, ln2, eps); logits = Wgate·xn; p = softmax(logits);
+ *   top-k by strict '>' (lower id wins ties), wt = p[idx] / sum(p[idx]);
+ *   for j in selection order: mlp += wt_j · Wd_e·(silu(Wg_e·xn) · (Wu_e·xn)).
+ * Expert GEMVs run on tensor cores with fp16 operands (exact Q4/Q8 integers, fp16-rounded
+ * activations) and fp32 accumulation; the block output matches the f32 reference within
+ * max|d|/max|ref| <= 1e-3. */
+typedef struct {
+    int d_model;              /* 2048 for Qwen3-30B-A3B; multiple of 256 */
+    int d_exp;                /* 768; multiple of 256 */
+    int n_experts;            /* 128; <= 256 */
+    int topk;                 /* 8; <= 32 */
+    float rms_eps;            /* 1e-6 */
+    const float *ln2;         /* device (d_model) */
+    cpg_tensor wgate;         /* device (n_experts, d_model), CPG_ENC_F32 */
+    const cpg_tensor *experts;/* HOST array (n_experts*3) of DEVICE tensors, [e*3+kind], kind
+                                 0 gate (d_exp,d_model), 1 up (d_exp,d_model), 2 down
+                                 (d_model,d_exp); one encoding (Q4 or Q8) for all of them.
+                                 Mirrors QW3Layer.exp (qwen3_moe.h:28-34). */
+} cpg_moe_desc;
+
+typedef struct cpg_moe_layer cpg_moe_layer;
+
+/* Validate a layer and upload its expert table (qwen3_bind_layer, qwen3_moe.c:462-586). */
+int cpg_moe_layer_create(const cpg_moe_desc *desc, cpg_moe_layer **out);
+void cpg_moe_layer_destroy(cpg_moe_layer *layer);
+/* Scratch bytes one forward of up to max_T tokens needs (the caller allocates it). */
+size_t cpg_moe_workspace_bytes(const cpg_moe_layer *layer, int max_T);
+
+/* One MoE block on device memory, enqueued on `stream` (no allocation, no host sync).
+ *   x (T,d_model) in; attn (T,d_model) or NULL (= zero);
+ *   mlp (T,d_model) or NULL: ACCUMULATED (+=), as QW3Out.mlp (qwen3_moe.h:73), caller zeroes;
+ *   x_out (T,d_model) or NULL: x + (attn + mlp), mlp being the accumulated value above (the
+ *     residual of run_layers); may alias x;
+ *   topk_idx (T,topk) int, wt (T,topk), router (T,n_experts) logits: optional outputs.
+ * The status word in the workspace records device-side timeouts; read it with
+ * cpg_moe_check(). */
+int cpg_moe_forward(const cpg_moe_layer *layer, const float *x, const float *attn, int T,
+                    float *mlp, float *x_out, int *topk_idx, float *wt, float *router,
+                    void *ws, size_t ws_bytes, void *stream);
+/* Synchronise `stream` and return CPG_OK, or CPG_ETIMEOUT if a bounded wait in the last
+   forward on this workspace gave up. */
+int cpg_moe_check(const void *ws, void *stream);
+
+/* ============================================================== decode loop (host buffers)
+ * A context owns a stream, a workspace and device activation buffers on one device. */
+typedef struct cpg_ctx cpg_ctx;
+int cpg_ctx_create(int device, int max_T, const cpg_moe_layer *shape, cpg_ctx **out);
+void cpg_ctx_destroy(cpg_ctx *ctx);
+void *cpg_ctx_stream(cpg_ctx *ctx);
+/* The MoE half of run_layers (engine/api/cachepotato.c:149-166) over L layers, host in and
+ * out: x (T,d_model) in HOST memory is updated in place, x += mlp_l for l = 0..L-1 (the
+ * attention half is the caller's). Copies x to the device, runs the layers (replayed from a
+ * CUDA graph after the first call with the same layers and T), copies x back; synchronous.
+ * topk_out (L,T,topk) host int, optional. */
+int cpg_run_moe_layers(cpg_ctx *ctx, cpg_moe_layer *const *layers, int L, float *x, int T,
+                       int *topk_out);
+/* The same L layers on the context's device activations cpg_ctx_x(ctx) (T, d_model), enqueued
+ * on cpg_ctx_stream(ctx) without copies or synchronisation (device-resident decode). */
+int cpg_ctx_run(cpg_ctx *ctx, cpg_moe_layer *const *layers, int L, int T);
+float *cpg_ctx_x(cpg_ctx *ctx);
+/* (L, T, topk) device ids of the last run. */
+int *cpg_ctx_topk(cpg_ctx *ctx);
+/* Phase timing: when enabled, the decode graph records CUDA events around the router,
+ * gate/up, down and combine launches of every layer; cpg_ctx_phase_ms sums each phase over
+ * the layers of the last run (synchronises the stream). */
+int cpg_ctx_profile(cpg_ctx *ctx, int enable);
+int cpg_ctx_phase_ms(cpg_ctx *ctx, float *ms4);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

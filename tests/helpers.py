@@ -1,0 +1,41 @@
+"""Test helpers: put an oracle SynthLayer on the device and compare routing by the reference's
+agreement rule (expert ids identical except where the top-k margin is below 1e-6)."""
+import numpy as np
+
+TOPK_MARGIN = 1e-6     # ids may differ only where the margin is below this
+BLOCK_TOL = 1e-3       # max|d| / max|ref| for block outputs (fp16 tensor-core operands)
+KERNEL_TOL = 1e-5      # fp32 matvec kernels (tools/verify_q8_kernels.py tolerance)
+
+
+def device_layer(layer, torch=None):
+    """MoELayer over a copy of SynthLayer `layer` in device memory."""
+    import torch as _t
+    from cachepotato_b200.qwen3 import MoELayer
+    torch = torch or _t
+    ln2 = torch.from_numpy(layer.ln2).cuda()
+    wg = torch.from_numpy(layer.wgate).cuda()
+    blob = torch.from_numpy(layer.blob).cuda()
+    return MoELayer(ln2, wg, layer.enc, layer.d_model, layer.d_exp, layer.n_experts, layer.topk,
+                    eps=layer.eps, blob=blob)
+
+
+def probs_from_logits(logits):
+    z = logits.astype(np.float64)
+    z = np.exp(z - z.max(-1, keepdims=True))
+    return z / z.sum(-1, keepdims=True)
+
+
+def check_topk(got_idx, want_idx, want_logits, K):
+    """Per token: same ordered ids, or a difference explained by a sub-1e-6 probability margin
+    (the reference's top-k picks by strict '>' in descending order, qwen3_moe.c:184-194)."""
+    p = probs_from_logits(want_logits)
+    bad = []
+    for t in range(got_idx.shape[0]):
+        if np.array_equal(got_idx[t], want_idx[t]):
+            continue
+        ps = np.sort(p[t])[::-1]
+        # any swap needs two probabilities within the margin among the top K+1
+        close = np.min(np.abs(np.diff(ps[:K + 1]))) < TOPK_MARGIN
+        if not close:
+            bad.append(t)
+    return bad
