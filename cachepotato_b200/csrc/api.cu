@@ -37,6 +37,27 @@ int sm_count() {
     return cached[dev];
 }
 
+int smem_optin() {
+    static int cached[64] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 227 * 1024;
+    if (!cached[dev]) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess || n <= 0)
+            n = 227 * 1024;
+        cached[dev] = n;
+    }
+    return cached[dev];
+}
+
+int allow_max_smem(const void *kernel) {
+    cudaFuncAttributes fa;
+    CPG_CUDA(cudaFuncGetAttributes(&fa, kernel));
+    CPG_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  smem_optin() - (int)fa.sharedSizeBytes));
+    return CPG_OK;
+}
+
 int matvec_launch(float *out, const float *x, cpg_tensor w, int n_in, int n_out, int T, cudaStream_t s);
 
 // ------------------------------------------------------------------ region store

@@ -28,6 +28,11 @@ int cuda_fail(cudaError_t e, const char *what);
     } while (0)
 
 int sm_count();
+// Largest dynamic shared memory a block may opt into on this device (227 KB on B200).
+int smem_optin();
+// Raise a kernel's dynamic shared-memory limit to the device maximum minus its static shared
+// memory (never lowered, so launches sized for one layer cannot be broken by a later, smaller one).
+int allow_max_smem(const void *kernel);
 
 inline long group_bytes(int enc) { return enc == CPG_ENC_Q4 ? 18 : enc == CPG_ENC_Q8 ? 34 : 0; }
 inline long row_bytes(int enc, long n_in) {

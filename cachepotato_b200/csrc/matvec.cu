@@ -177,7 +177,8 @@ int matvec_launch(float *out, const float *x, cpg_tensor w, int n_in, int n_out,
     auto *kq8 = k_matvec<CPG_ENC_Q8>;
     auto *kf = k_matvec<CPG_ENC_F32>;
     auto *k = w.enc == CPG_ENC_Q4 ? kq4 : w.enc == CPG_ENC_Q8 ? kq8 : kf;
-    CPG_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024));
+    const int rc = allow_max_smem((const void *)k);
+    if (rc) return rc;
     k<<<grid, MV_WARPS * 32, smem, s>>>(out, x, (const uint8_t *)w.p, n_in, n_out, T, tpc, rb);
     CPG_CUDA(cudaGetLastError());
     return CPG_OK;

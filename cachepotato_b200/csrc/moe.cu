@@ -646,7 +646,9 @@ static int plan_kernel(int K_in, KernelPlan &p) {
     p.stages = S;
     p.smem = (size_t)S * stage + sizeof(float) * EX_NW * EX_NCH * 128 + S * sizeof(StageMeta) + 2 * S * sizeof(uint64_t);
     auto *k = k_experts<ENC, KIND>;
-    CPG_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem));
+    CPG_REQUIRE((int)p.smem <= smem_optin(), "expert kernel: %zu bytes of shared memory exceed the device limit", p.smem);
+    int rc = allow_max_smem((const void *)k);
+    if (rc) return rc;
     int per_sm = 0;
     CPG_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, (1 + EX_NW) * 32, p.smem));
     CPG_REQUIRE(per_sm >= 1, "expert kernel: no CTA fits on an SM");
@@ -727,9 +729,12 @@ extern "C" int cpg_moe_layer_create(const cpg_moe_desc *d, cpg_moe_layer **out) 
     }
     if (rc == CPG_OK) {
         const int rsmem = R_TB * L->D * (int)sizeof(float);
-        CPG_REQUIRE(rsmem <= 200 * 1024, "d_model=%d too large for the router kernel", L->D);
-        cudaError_t e2 = cudaFuncSetAttribute(k_router, cudaFuncAttributeMaxDynamicSharedMemorySize, rsmem);
-        if (e2 != cudaSuccess) rc = cuda_fail(e2, "router smem attribute");
+        if (rsmem > smem_optin() - 8 * 1024) {
+            set_error("d_model=%d too large for the router kernel", L->D);
+            rc = CPG_EINVAL;
+        } else {
+            rc = allow_max_smem((const void *)k_router);
+        }
     }
     if (rc != CPG_OK) {
         cudaFree(L->d_ptrs);
@@ -777,7 +782,7 @@ int cpg::moe_forward_impl(const cpg_moe_layer *L, const float *x, const float *a
                 "cpg_moe_forward: buffers must be 16-byte aligned");
     uint8_t *w = (uint8_t *)ws;
     int *hdr = (int *)w;
-    if (ev) CPG_CUDA(cudaEventRecord(ev[0], s));
+    if (ev) CPG_CUDA(cudaEventRecordWithFlags(ev[0], s, cudaEventRecordExternal));
     CPG_CUDA(cudaMemsetAsync(w, 0, W.memset_bytes, s));
 
     RouterArgs ra{};
@@ -805,24 +810,24 @@ int cpg::moe_forward_impl(const cpg_moe_layer *L, const float *x, const float *a
     ea.bsrc = ra.xn_perm;
     ea.h_out = (__half *)(w + W.h);
     ea.item_ctr = hdr + WS_ITEMS_GATEUP;
-    if (ev) CPG_CUDA(cudaEventRecord(ev[1], s));
+    if (ev) CPG_CUDA(cudaEventRecordWithFlags(ev[1], s, cudaEventRecordExternal));
     int rc = launch_experts(L, KIND_GATEUP, ea, max_active * (L->F / 16), s);
     if (rc) return rc;
 
     ea.bsrc = (const __half *)(w + W.h);
     ea.y_out = (float *)(w + W.y);
     ea.item_ctr = hdr + WS_ITEMS_DOWN;
-    if (ev) CPG_CUDA(cudaEventRecord(ev[2], s));
+    if (ev) CPG_CUDA(cudaEventRecordWithFlags(ev[2], s, cudaEventRecordExternal));
     rc = launch_experts(L, KIND_DOWN, ea, max_active * (L->D / 32), s);
     if (rc) return rc;
 
     const int n4 = T * L->D / 4;
     int cgrid = (n4 + 255) / 256;
     if (cgrid > sm_count() * 8) cgrid = sm_count() * 8;
-    if (ev) CPG_CUDA(cudaEventRecord(ev[3], s));
+    if (ev) CPG_CUDA(cudaEventRecordWithFlags(ev[3], s, cudaEventRecordExternal));
     k_combine<<<cgrid, 256, 0, s>>>(x, attn, T, L->D, L->K, ra.wt, (const float *)(w + W.y), mlp, x_out);
     CPG_CUDA(cudaGetLastError());
-    if (ev) CPG_CUDA(cudaEventRecord(ev[4], s));
+    if (ev) CPG_CUDA(cudaEventRecordWithFlags(ev[4], s, cudaEventRecordExternal));
     return CPG_OK;
 }
 

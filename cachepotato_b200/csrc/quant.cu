@@ -4,6 +4,15 @@
 
 namespace cpg {
 
+// (float)q * d with the host's (x86 SSE) NaN rules, so that decoding is bit-exact for every
+// byte pattern, not only for finite scales: a NaN scale propagates quieted with its payload,
+// and 0 * inf gives the default NaN 0xFFC00000 (the GPU would return its canonical NaN).
+__device__ __forceinline__ float mul_hostnan(float q, float d) {
+    const float v = __fmul_rn(q, d);
+    if (!isnan(v)) return v;
+    return isnan(d) ? __uint_as_float(__float_as_uint(d) | 0x00400000u) : __uint_as_float(0xFFC00000u);
+}
+
 // engine/kernels/kernels.c:143-151 (Q8_0) and 463-477 (Q4_0). The group scale is fp16 and the
 // quantised value an integer, so q * d in fp32 is exact: there is one right answer.
 template <int ENC>
@@ -17,7 +26,7 @@ __global__ void k_dequant(float *__restrict__ out, const uint8_t *__restrict__ b
         if (ENC == CPG_ENC_Q8) {
             float v[32];
 #pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = __fmul_rn((float)(int8_t)blk[2 + i], d);
+            for (int i = 0; i < 32; ++i) v[i] = mul_hostnan((float)(int8_t)blk[2 + i], d);
 #pragma unroll
             for (int i = 0; i < 8; ++i) o[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
         } else {
@@ -27,8 +36,8 @@ __global__ void k_dequant(float *__restrict__ out, const uint8_t *__restrict__ b
                 const int b = blk[2 + k];
                 const int lo = (b & 0x0F) > 7 ? (b & 0x0F) - 16 : (b & 0x0F);
                 const int hi = (b >> 4) > 7 ? (b >> 4) - 16 : (b >> 4);
-                v[k] = __fmul_rn((float)lo, d);
-                v[k + 16] = __fmul_rn((float)hi, d);
+                v[k] = mul_hostnan((float)lo, d);
+                v[k + 16] = mul_hostnan((float)hi, d);
             }
 #pragma unroll
             for (int i = 0; i < 8; ++i) o[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
@@ -55,30 +64,34 @@ __global__ void k_quantize(uint8_t *__restrict__ blocks, const float *__restrict
         for (int i = 0; i < 32; ++i) amax = fabsf(v[i]) > amax ? fabsf(v[i]) : amax;
         // Q4: amax/8 is exact; Q8: amax/127 is an fp32 division (numpy's float32 result)
         const float d = amax > 0.0f ? (ENC == CPG_ENC_Q4 ? amax * 0.125f : __fdiv_rn(amax, 127.0f)) : 0.0f;
-        const __half dh = __float2half_rn(d);
-        const float dq = __half2float(dh);
-        const uint16_t bits = __half_as_ushort(dh);
-        uint8_t *blk = blocks + g * GB;
-        blk[0] = (uint8_t)(bits & 0xFF);
-        blk[1] = (uint8_t)(bits >> 8);
+        const uint32_t bits = (uint32_t)__half_as_ushort(__float2half_rn(d));
+        const float dq = f16_bits_to_f32(bits);
+        const float lo = ENC == CPG_ENC_Q4 ? -8.0f : -127.0f;
+        const float hi = ENC == CPG_ENC_Q4 ? 7.0f : 127.0f;
         int q[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
             int qi = 0;
             if (dq > 0.0f) {
                 const float r = rintf(__fdiv_rn(v[i], dq));
-                const float lo = ENC == CPG_ENC_Q4 ? -8.0f : -127.0f;
-                const float hi = ENC == CPG_ENC_Q4 ? 7.0f : 127.0f;
-                qi = (int)(r < lo ? lo : r > hi ? hi : r);
+                qi = (int)fminf(fmaxf(r, lo), hi);
             }
             q[i] = qi;
         }
+        // the group as 16-bit words (groups are 2-byte aligned): scale, then payload bytes
+        uint16_t *dst = reinterpret_cast<uint16_t *>(blocks + g * GB);
+        dst[0] = (uint16_t)bits;
         if (ENC == CPG_ENC_Q8) {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) blk[2 + i] = (uint8_t)(int8_t)q[i];
+            for (int i = 0; i < 16; ++i)
+                dst[1 + i] = (uint16_t)((q[2 * i] & 0xFF) | ((q[2 * i + 1] & 0xFF) << 8));
         } else {
 #pragma unroll
-            for (int k = 0; k < 16; ++k) blk[2 + k] = (uint8_t)((q[k] & 0xF) | ((q[k + 16] & 0xF) << 4));
+            for (int i = 0; i < 8; ++i) {
+                const uint32_t b0 = (uint32_t)((q[2 * i] & 0xF) | ((q[2 * i + 16] & 0xF) << 4));
+                const uint32_t b1 = (uint32_t)((q[2 * i + 1] & 0xF) | ((q[2 * i + 17] & 0xF) << 4));
+                dst[1 + i] = (uint16_t)(b0 | (b1 << 8));
+            }
         }
     }
 }
@@ -111,7 +124,8 @@ extern "C" int cpg_quantize(uint8_t *blocks, const float *x, int enc, long n, vo
     CPG_REQUIRE(blocks && x, "cpg_quantize: null pointer");
     CPG_REQUIRE(n >= 0 && n % 32 == 0, "cpg_quantize: n=%ld is not a multiple of 32", n);
     CPG_REQUIRE(enc == CPG_ENC_Q4 || enc == CPG_ENC_Q8, "cpg_quantize: encoding %d is not Q4/Q8", enc);
-    CPG_REQUIRE(((uintptr_t)x & 15) == 0, "cpg_quantize: x must be 16-byte aligned");
+    CPG_REQUIRE(((uintptr_t)x & 15) == 0 && ((uintptr_t)blocks & 1) == 0,
+                "cpg_quantize: x must be 16-byte and blocks 2-byte aligned");
     if (n == 0) return CPG_OK;
     const long ng = n / 32;
     cudaStream_t s = (cudaStream_t)stream;

@@ -46,7 +46,8 @@ def test_dequant_random_blocks_bit_exact(q, orc, enc):
     blocks = rng.integers(0, 256, size=4096 * gb, dtype=np.uint8)
     got = q.dequant(torch.from_numpy(blocks).cuda(), 4096 * 32, enc).cpu().numpy()
     want = orc.dequant(blocks, 4096 * 32, enc)
-    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+    diff = np.nonzero(got.view(np.uint32) != want.view(np.uint32))[0]
+    assert diff.size == 0, (diff.size, [(hex(got.view(np.uint32)[i]), hex(want.view(np.uint32)[i])) for i in diff[:4]])
 
 
 @pytest.mark.parametrize("tag,enc", [("q4", O.ENC_Q4), ("q8", O.ENC_Q8)])
@@ -56,7 +57,9 @@ def test_quantize_reference_kats(q, golden, tag, enc):
         if key + "_x" not in kats:
             continue
         got = q.quantize(torch.from_numpy(kats[key + "_x"]).cuda(), enc).cpu().numpy()
-        assert np.array_equal(got, kats[key + "_blocks"]), key
+        want = kats[key + "_blocks"]
+        bad = np.nonzero(got != want)[0]
+        assert bad.size == 0, (key, bad.size, bad[:8].tolist(), got[bad[:8]].tolist(), want[bad[:8]].tolist())
 
 
 @pytest.mark.parametrize("enc", [O.ENC_Q4, O.ENC_Q8])
@@ -67,7 +70,9 @@ def test_quantize_matches_oracle_at_scale(q, orc, enc):
     x[64:96] *= 1e4                                    # saturating
     x[96:128] = 1e-9                                   # scale rounds to fp16 zero
     got = q.quantize(torch.from_numpy(x).cuda(), enc).cpu().numpy()
-    assert np.array_equal(got, orc.quantize(x, enc))
+    want = orc.quantize(x, enc)
+    bad = np.nonzero(got != want)[0]
+    assert bad.size == 0, (bad.size, bad[:8].tolist(), got[bad[:8]].tolist(), want[bad[:8]].tolist())
 
 
 @pytest.mark.parametrize("case", MG.MATVEC_CASES, ids=[c[0] for c in MG.MATVEC_CASES])
@@ -146,6 +151,7 @@ def test_region_store_translates_host_mapping(q, orc):
         out_dev = torch.empty(n, dtype=torch.float32, device="cuda")
         _lib.check(L.cpg_dequant(out_dev.data_ptr(), r1, O.ENC_Q4, n, None))
         torch.cuda.synchronize()
-        assert np.array_equal(out_dev.cpu().numpy(), orc.dequant(np.ascontiguousarray(w[::-1]), n, O.ENC_Q4))
+        want = orc.dequant(np.ascontiguousarray(w[::-1]), n, O.ENC_Q4)     # NaN scales possible
+        assert np.array_equal(out_dev.cpu().numpy().view(np.uint32), want.view(np.uint32))
     finally:
         L.cpg_store_close()
