@@ -22,7 +22,7 @@ EXPORTS = [
     "cpg_store_open_v4", "cpg_store_open", "cpg_store_add_region", "cpg_store_region_get",
     "cpg_store_translate", "cpg_store_base", "cpg_store_bytes", "cpg_store_totals", "cpg_store_close",
     "cpg_moe_layer_create", "cpg_moe_layer_destroy", "cpg_moe_workspace_bytes", "cpg_moe_forward",
-    "cpg_moe_check",
+    "cpg_moe_check", "cpg_moe_forward_noalloc",
     "cpg_ctx_create", "cpg_ctx_destroy", "cpg_ctx_stream", "cpg_run_moe_layers",
     "cpg_ctx_run", "cpg_ctx_x", "cpg_ctx_topk", "cpg_ctx_profile", "cpg_ctx_phase_ms",
 ]
@@ -76,6 +76,7 @@ _SIGS = {
     "cpg_moe_workspace_bytes": (_sz, [_vp, _i]),
     "cpg_moe_forward": (_i, [_vp, _vp, _vp, _i, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
     "cpg_moe_check": (_i, [_vp, _vp]),
+    "cpg_moe_forward_noalloc": (_i, [_vp, _vp, _vp, _i, _vp, _vp, _vp, _vp, _vp, _vp]),
     "cpg_ctx_create": (_i, [_i, _i, _vp, ctypes.POINTER(_vp)]),
     "cpg_ctx_destroy": (None, [_vp]),
     "cpg_ctx_stream": (_vp, [_vp]),

@@ -130,6 +130,20 @@ int cpg_moe_forward(const cpg_moe_layer *layer, const float *x, const float *att
    forward on this workspace gave up. */
 int cpg_moe_check(const void *ws, void *stream);
 
+/* cpg_moe_forward without a caller workspace, for callers that cannot allocate device memory
+ * where they run the block (an engine whose host program owns all device memory through its
+ * own pool, a stream being captured into a CUDA graph in global capture mode, a decode loop
+ * that may not stall on the allocator). No counterpart in the reference (its CPU engine mallocs
+ * scratch per call, qwen3_moe.c:98-108). Scratch comes from a fixed 8 MiB array in the
+ * library's device image (enough for 64 tokens of a Qwen3-30B-A3B layer); larger T is rejected
+ * with CPG_EINVAL. Allocates nothing. The first call on a device looks up the array's address
+ * (make it before any stream capture). All calls share the array: calls that overlap on the
+ * GPU race, so serialise them (one stream, or events). Device-side timeouts are recorded in the
+ * array and not reported here; use cpg_moe_forward + cpg_moe_check when they must be read. */
+int cpg_moe_forward_noalloc(const cpg_moe_layer *layer, const float *x, const float *attn, int T,
+                            float *mlp, float *x_out, int *topk_idx, float *wt, float *router,
+                            void *stream);
+
 /* ============================================================== decode loop (host buffers)
  * A context owns a stream, a workspace and device activation buffers on one device. */
 typedef struct cpg_ctx cpg_ctx;
