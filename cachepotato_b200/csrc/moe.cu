@@ -31,14 +31,15 @@ constexpr int MAX_K = 32;
 
 constexpr int KIND_GATEUP = 0;
 constexpr int KIND_DOWN = 1;
-constexpr int EX_NW = 4;         // consumer warps per CTA
-constexpr int EX_NCH = 8;        // 8-column MMA tiles per pass (64 tokens)
+constexpr int EX_NW = 8;         // consumer warps per CTA
+constexpr int EX_NCH = 2;        // 8-column MMA tiles per item
+constexpr int EX_NCHUNK = 8 * EX_NCH;   // tokens per item (an expert with more is split)
 
 // workspace words
 enum { WS_STATUS = 0, WS_DONE_TILES = 1, WS_ITEMS_GATEUP = 2, WS_ITEMS_DOWN = 3, WS_HDR_INTS = 16 };
 
 struct WsLayout {
-    size_t tile_cnt, ex_cnt, ex_off, ex_list, n_active, pairs, topk, wt, logits, xn, h, y, total;
+    size_t tile_cnt, n_active, act, act_ptr, pairs, topk, wt, logits, xn, h, y, total;
     size_t memset_bytes;
 };
 
@@ -50,11 +51,10 @@ static WsLayout ws_layout(int D, int F, int E, int K, int T) {
     L.tile_cnt = o; o += sizeof(int) * (size_t)((T + R_TB - 1) / R_TB);
     L.memset_bytes = o;
     o = align_up(o, 256);
-    L.ex_cnt = o; o += sizeof(int) * E;
-    L.ex_off = o; o += sizeof(int) * E;
-    L.ex_list = o; o += sizeof(int) * E;
     L.n_active = o; o += sizeof(int);
     o = align_up(o, 256);
+    L.act = o; o = align_up(o + sizeof(int4) * (size_t)(E + 1), 256);
+    L.act_ptr = o; o = align_up(o + sizeof(void *) * 3 * (size_t)E, 256);
     L.pairs = o; o = align_up(o + sizeof(int) * (size_t)T * K, 256);
     L.topk = o; o = align_up(o + sizeof(int) * (size_t)T * K, 256);
     L.wt = o; o = align_up(o + sizeof(float) * (size_t)T * K, 256);
@@ -81,7 +81,10 @@ struct RouterArgs {
     __half *xn_perm;
     int *status;                 // workspace header
     int *tile_cnt;
-    int *ex_cnt, *ex_off, *ex_list, *n_active, *pairs;
+    const uint8_t *const *ptrs;  // (E, 3) expert matrix pointers
+    int *n_active, *pairs;
+    int4 *act;                   // active experts ascending: (e, pair offset, tokens, token chunks before)
+    const uint8_t **act_ptr;     // (U, 3) their gate/up/down pointers
 };
 
 __device__ __forceinline__ float warp_sum(float v) {
@@ -150,7 +153,7 @@ __device__ void route_token(const RouterArgs &a, int t) {
 
 // group (token, slot) pairs by expert, tokens ascending inside an expert; one CTA
 __device__ void group_pairs(const RouterArgs &a) {
-    __shared__ int s_cnt[MAX_E], s_off[MAX_E], s_base[MAX_E];
+    __shared__ int s_cnt[MAX_E], s_off[MAX_E], s_base[MAX_E], s_uidx[MAX_E], s_chp[MAX_E];
     __shared__ uint32_t s_mask[MAX_E];
     const int tid = threadIdx.x;
     for (int e = tid; e < a.E; e += blockDim.x) { s_cnt[e] = 0; s_base[e] = 0; }
@@ -158,18 +161,29 @@ __device__ void group_pairs(const RouterArgs &a) {
     const int TK = a.T * a.K;
     for (int i = tid; i < TK; i += blockDim.x) atomicAdd(&s_cnt[__ldcg(a.topk + i)], 1);
     __syncthreads();
-    if (tid == 0) {
-        int o = 0, u = 0;
+    if (tid == 0) {                      // shared-memory scan only: offsets, active index, chunks
+        int o = 0, u = 0, chp = 0;
         for (int e = 0; e < a.E; ++e) {
             s_off[e] = o;
+            s_chp[e] = chp;
+            s_uidx[e] = s_cnt[e] > 0 ? u : -1;
             o += s_cnt[e];
-            a.ex_cnt[e] = s_cnt[e];
-            a.ex_off[e] = s_off[e];
-            if (s_cnt[e] > 0) a.ex_list[u++] = e;
+            chp += (s_cnt[e] + EX_NCHUNK - 1) / EX_NCHUNK;
+            u += s_cnt[e] > 0;
         }
+        a.act[u] = make_int4(-1, o, 0, chp);
         *a.n_active = u;
     }
     __syncthreads();
+    for (int e = tid; e < a.E; e += blockDim.x) {     // one thread per expert: loads in parallel
+        const int u = s_uidx[e];
+        if (u >= 0) {
+            a.act[u] = make_int4(e, s_off[e], s_cnt[e], s_chp[e]);
+            a.act_ptr[3 * u + 0] = a.ptrs[3 * e + 0];
+            a.act_ptr[3 * u + 1] = a.ptrs[3 * e + 1];
+            a.act_ptr[3 * u + 2] = a.ptrs[3 * e + 2];
+        }
+    }
     for (int c0 = 0; c0 < a.T; c0 += 32) {
         for (int e = tid; e < a.E; e += blockDim.x) s_mask[e] = 0;
         __syncthreads();
@@ -195,10 +209,12 @@ __device__ void group_pairs(const RouterArgs &a) {
 __global__ void __launch_bounds__(R_THREADS) k_router(RouterArgs a) {
     extern __shared__ float xs[];                         // (R_TB, D): hh, then xn
     __shared__ float part[2][R_EB][R_TB];
-    __shared__ float s_inv[R_TB];
     __shared__ int s_last;
+    __shared__ uint8_t s_p2e[64];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int t0 = blockIdx.y * R_TB, nt = min(R_TB, a.T - t0);
+    if (tid < 64) s_p2e[tid] = perm_of(a.xn_enc).pos_to_elem[tid];
+    __syncthreads();
     const int e0 = blockIdx.x * R_EB;
     const int D = a.D;
 
@@ -217,28 +233,24 @@ __global__ void __launch_bounds__(R_THREADS) k_router(RouterArgs a) {
         }
     }
     __syncthreads();
-    // rmsnorm (kernels.c:408-413): inv = 1 / sqrt(sum(x^2)/n + eps); xn = x * inv * g
+    // rmsnorm (kernels.c:408-413): inv = 1 / sqrt(sum(x^2)/n + eps); xn = x * inv * g.
+    // One warp per token throughout, so no index division is needed.
     if (warp < nt) {
+        float *row = xs + warp * D;
         float ss = 0.0f;
-        for (int k = lane; k < D; k += 32) ss = fmaf(xs[warp * D + k], xs[warp * D + k], ss);
+        for (int k = lane; k < D; k += 32) ss = fmaf(row[k], row[k], ss);
         ss = warp_sum(ss);
-        if (lane == 0) s_inv[warp] = __fdiv_rn(1.0f, __fsqrt_rn(__fdiv_rn(ss, (float)D) + a.eps));
-    }
-    __syncthreads();
-    for (int i = tid; i < nt * D; i += R_THREADS) {
-        const int t = i / D, k = i - t * D;
-        xs[i] = __fmul_rn(__fmul_rn(xs[i], s_inv[t]), a.ln2[k]);
-    }
-    __syncthreads();
-    if (blockIdx.x == 0) {
-        // fp16 copy of xn in the expert kernels' K order
-        const Perm64 &pm = perm_of(a.xn_enc);
-        for (int i = tid; i < nt * D; i += R_THREADS) {
-            const int t = i / D, pos = i - t * D;
-            const int k = (pos & ~63) + pm.pos_to_elem[pos & 63];
-            a.xn_perm[(size_t)(t0 + t) * D + pos] = __float2half_rn(xs[t * D + k]);
+        const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fdiv_rn(ss, (float)D) + a.eps));
+        for (int k = lane; k < D; k += 32) row[k] = __fmul_rn(__fmul_rn(row[k], inv), a.ln2[k]);
+        __syncwarp();
+        if (blockIdx.x == 0) {
+            // fp16 copy of xn in the expert kernels' K order
+            __half *dst = a.xn_perm + (size_t)(t0 + warp) * D;
+            for (int pos = lane; pos < D; pos += 32)
+                dst[pos] = __float2half_rn(row[(pos & ~63) + s_p2e[pos & 63]]);
         }
     }
+    __syncthreads();
     // logits = Wgate·xn (matmul_wx, kernels.c:84-95): warp -> (expert e0 + w%4, half w/4)
     {
         const int el = warp & 3, half = warp >> 2, e = e0 + el;
@@ -248,6 +260,7 @@ __global__ void __launch_bounds__(R_THREADS) k_router(RouterArgs a) {
         if (e < a.E) {
             const int k0 = half * (D / 2), k1 = k0 + D / 2;
             const float4 *w4 = reinterpret_cast<const float4 *>(a.wgate + (size_t)e * D);
+#pragma unroll 8
             for (int k = k0 + lane * 4; k < k1; k += 128) {
                 const float4 w = __ldg(w4 + k / 4);
 #pragma unroll
@@ -294,15 +307,16 @@ __global__ void __launch_bounds__(R_THREADS) k_router(RouterArgs a) {
 
 // ------------------------------------------------------------------ experts
 struct ExpertArgs {
-    const uint8_t *const *ptrs;  // (E, 3) device matrix pointers
     int D, F, K;
-    const int *ex_cnt, *ex_off, *ex_list, *n_active, *pairs;
+    const int *n_active, *pairs;
+    const int4 *act;             // active-expert table from the router (see RouterArgs)
+    const uint8_t *const *act_ptr;
     const __half *bsrc;          // GATEUP: xn_perm (T, D); DOWN: h_perm (pairs, F)
     __half *h_out;               // GATEUP output (pairs, F), permuted for Wd
     float *y_out;                // DOWN output (T*K, D), row = t*K + j
     int h_enc;                   // encoding of Wd (permutation of h_out)
     int *status;
-    int *item_ctr;
+    int *item_ctr;               // dynamic work counter (zeroed with the header)
     int stages;
     int rs;                      // shared-memory row stride (bytes)
 };
@@ -310,15 +324,14 @@ struct ExpertArgs {
 template <int ENC, int KIND>
 struct ExCfg {
     static constexpr int GB = ENC == CPG_ENC_Q4 ? 18 : 34;
-    static constexpr int WPP = GB / 2;                 // 32-bit words per group pair
     static constexpr int MATS = KIND == KIND_GATEUP ? 2 : 1;
-    static constexpr int MT = KIND == KIND_GATEUP ? 1 : 2;
-    static constexpr int COMBOS = MATS * MT;           // 16-row tiles per item
-    static constexpr int KS = EX_NW / COMBOS;          // K split across warps
-    static constexpr int ROWS = 16 * MT;               // output rows per item per matrix
+    static constexpr int MT = KIND == KIND_GATEUP ? 1 : 4;   // 16-row tiles per matrix per item
+    static constexpr int COMBOS = MATS * MT;                  // 16-row tiles per item
+    static constexpr int KS = EX_NW / COMBOS;                 // K split across warps
+    static constexpr int ROWS = 16 * MT;                      // output rows per item per matrix
 };
 
-struct StageMeta { int item, m, off, cnt; };
+struct StageMeta { int item, m, off, cnt; };     // off/cnt: this item's token chunk
 
 template <int ENC>
 __device__ __forceinline__ void load_pair_words(const uint32_t *row, int P, int t, uint32_t &w1,
@@ -361,10 +374,30 @@ __device__ __forceinline__ void q8_word(uint32_t w, uint32_t &s0, uint32_t &s2) 
     s2 = hsub2_u32(__byte_perm(x, 0x64646464u, 0x4342), k1152);
 }
 
+// Item -> (active expert u, row tile m, token chunk c). Items run expert-major, then row tile,
+// then chunk, so the chunks of one weight tile are fetched back to back (the later fetches hit
+// L2). items_before(u) = tiles * chunks_before(u), from the router's table in shared memory.
+__device__ __forceinline__ void decode_item(const int4 *act, int U, int tiles, int item, int &u, int &m, int &c) {
+    int lo = 0, hi = U;                       // last u with items_before(u) <= item
+    while (hi - lo > 1) {
+        const int mid = (lo + hi) >> 1;
+        if (tiles * act[mid].w <= item) lo = mid; else hi = mid;
+    }
+    u = lo;
+    const int nch = act[u + 1].w - act[u].w;
+    const int local = item - tiles * act[u].w;
+    m = local / nch;
+    c = local - m * nch;
+}
+
 template <int ENC, int KIND>
-__global__ void __launch_bounds__((1 + EX_NW) * 32) k_experts(ExpertArgs a) {
+__global__ void __launch_bounds__((1 + EX_NW) * 32, 2) k_experts(ExpertArgs a) {
     using C = ExCfg<ENC, KIND>;
     extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ Perm64 s_perm;
+    __shared__ int s_abort;
+    __shared__ int4 s_act[MAX_E + 1];
+    __shared__ const uint8_t *s_ptr[MAX_E][C::MATS];
     const int S = a.stages, RS = a.rs;
     const int K_in = KIND == KIND_GATEUP ? a.D : a.F;
     const int n_rows = KIND == KIND_GATEUP ? a.F : a.D;
@@ -376,7 +409,7 @@ __global__ void __launch_bounds__((1 + EX_NW) * 32) k_experts(ExpertArgs a) {
     uint64_t *full = reinterpret_cast<uint64_t *>(meta + S);
     uint64_t *empty = full + S;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int tiles_per_expert = n_rows / C::ROWS;
+    const int tiles = n_rows / C::ROWS;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
@@ -384,13 +417,28 @@ __global__ void __launch_bounds__((1 + EX_NW) * 32) k_experts(ExpertArgs a) {
             mbar_init(&empty[s], EX_NW);
         }
         fence_mbar_init();
+        s_abort = 0;
+    }
+    if (threadIdx.x < 64) {
+        const Perm64 &pm = perm_of(a.h_enc);
+        s_perm.pos_to_elem[threadIdx.x] = pm.pos_to_elem[threadIdx.x];
+        s_perm.elem_to_pos[threadIdx.x] = pm.elem_to_pos[threadIdx.x];
+    }
+    const int U = *a.n_active;
+    for (int u = threadIdx.x; u <= U; u += blockDim.x) {
+        s_act[u] = a.act[u];
+        if (u < U) {
+#pragma unroll
+            for (int mat = 0; mat < C::MATS; ++mat)
+                s_ptr[u][mat] = a.act_ptr[3 * u + (KIND == KIND_GATEUP ? mat : 2)];
+        }
     }
     __syncthreads();
+    const int total = tiles * s_act[U].w;
 
     if (warp == 0) {
         // ---------------- producer: one thread streams weight rows into the stage ring
         if (lane != 0) return;
-        const int total = *a.n_active * tiles_per_expert;
         int it = 0;
         bool ok = true;
         for (;; ++it) {
@@ -408,17 +456,19 @@ __global__ void __launch_bounds__((1 + EX_NW) * 32) k_experts(ExpertArgs a) {
                 ++it;
                 break;
             }
-            const int u = item / tiles_per_expert, m = item - u * tiles_per_expert;
-            const int e = a.ex_list[u];
-            meta[st] = StageMeta{item, m, a.ex_off[e], a.ex_cnt[e]};
+            int u, m, c;
+            decode_item(s_act, U, tiles, item, u, m, c);
+            const int4 ex = s_act[u];
+            const int c0 = c * EX_NCHUNK;
+            meta[st] = StageMeta{item, m, ex.y + c0, min(EX_NCHUNK, ex.z - c0)};
             mbar_arrive_expect_tx(&full[st], (uint32_t)(C::COMBOS * 16 * RB));
             uint8_t *dst = smem + (size_t)st * stage_bytes;
 #pragma unroll
-            for (int c = 0; c < C::COMBOS; ++c) {
-                const int mat = KIND == KIND_GATEUP ? c : 2;          // gate, up / down
-                const int r0 = m * C::ROWS + (KIND == KIND_GATEUP ? 0 : c * 16);
-                const uint8_t *src = a.ptrs[e * 3 + mat] + (size_t)r0 * RB;
-                uint8_t *d = dst + c * 16 * RS;
+            for (int cb = 0; cb < C::COMBOS; ++cb) {
+                const int mat = KIND == KIND_GATEUP ? cb : 0;         // gate, up / down
+                const int r0 = m * C::ROWS + (KIND == KIND_GATEUP ? 0 : cb * 16);
+                const uint8_t *src = s_ptr[u][mat] + (size_t)r0 * RB;
+                uint8_t *d = dst + cb * 16 * RS;
                 if (RS == RB) {
                     bulk_g2s(d, src, 16 * RB, &full[st]);
                 } else {
@@ -440,10 +490,6 @@ __global__ void __launch_bounds__((1 + EX_NW) * 32) k_experts(ExpertArgs a) {
     const int cw = warp - 1;
     const int combo = cw % C::COMBOS, kp = cw / C::COMBOS;
     const int g = lane >> 2, t = lane & 3;
-    const Perm64 &hperm = perm_of(a.h_enc);
-    __shared__ int s_abort;
-    if (threadIdx.x == 32) s_abort = 0;
-    named_bar_sync(1, EX_NW * 32);
     for (int it = 0;; ++it) {
         const int st = it % S;
         const uint32_t ph = (uint32_t)(it / S) & 1u;
@@ -460,127 +506,133 @@ __global__ void __launch_bounds__((1 + EX_NW) * 32) k_experts(ExpertArgs a) {
         const uint32_t *rows = reinterpret_cast<const uint32_t *>(smem + (size_t)st * stage_bytes + combo * 16 * RS);
         const uint32_t *rowg = rows + (g * RS) / 4;
         const uint32_t *rowg8 = rows + ((g + 8) * RS) / 4;
-        const int ntiles = (md.cnt + 7) / 8;
-        for (int nc0 = 0; nc0 < ntiles; nc0 += EX_NCH) {
-            const int ntl = min(EX_NCH, ntiles - nc0);
-            // B row pointers for column g of each n-tile (nullptr = zero padding)
-            const __half *brow[EX_NCH];
+        const bool two = md.cnt > 8;                 // second 8-token MMA tile in use
+        // B rows for column g of each tile (nullptr = zero padding)
+        const __half *brow0 = nullptr, *brow1 = nullptr;
+        if (g < md.cnt) {
+            const int p = md.off + g;
+            brow0 = KIND == KIND_GATEUP ? a.bsrc + (size_t)(a.pairs[p] / a.K) * a.D : a.bsrc + (size_t)p * a.F;
+        }
+        if (8 + g < md.cnt) {
+            const int p = md.off + 8 + g;
+            brow1 = KIND == KIND_GATEUP ? a.bsrc + (size_t)(a.pairs[p] / a.K) * a.D : a.bsrc + (size_t)p * a.F;
+        }
+        float acc[EX_NCH][4];
+#pragma unroll
+        for (int nt = 0; nt < EX_NCH; ++nt)
+#pragma unroll
+            for (int c = 0; c < 4; ++c) acc[nt][c] = 0.0f;
+
+        // B fragments one group pair ahead of the MMAs
+        uint4 nb[EX_NCH][2];
+        auto load_b = [&](int P, uint4 (&b)[EX_NCH][2]) {
+            b[0][0] = b[0][1] = b[1][0] = b[1][1] = make_uint4(0, 0, 0, 0);
+            if (P < NP) {
+                if (brow0) {
+                    const uint4 *bp = reinterpret_cast<const uint4 *>(brow0 + P * 64 + t * 16);
+                    b[0][0] = __ldg(bp);
+                    b[0][1] = __ldg(bp + 1);
+                }
+                if (brow1) {
+                    const uint4 *bp = reinterpret_cast<const uint4 *>(brow1 + P * 64 + t * 16);
+                    b[1][0] = __ldg(bp);
+                    b[1][1] = __ldg(bp + 1);
+                }
+            }
+        };
+        load_b(kp, nb);
+        for (int P = kp; P < NP; P += C::KS) {
+            uint4 cb[EX_NCH][2];
+#pragma unroll
+            for (int nt = 0; nt < EX_NCH; ++nt) { cb[nt][0] = nb[nt][0]; cb[nt][1] = nb[nt][1]; }
+            load_b(P + C::KS, nb);
+            uint32_t fr[4][4];       // [k16 step][a0..a3]
+            float dj[2], dj1[2];     // scales: group j / j+1, rows g / g+8
+            {
+                uint32_t w1, w2, w3, w4;
+                load_pair_words<ENC>(rowg, P, t, w1, w2, w3, w4, dj[0], dj1[0]);
+                if (ENC == CPG_ENC_Q4) {
+                    q4_word(w1, fr[0][0], fr[0][2], fr[1][0], fr[1][2]);
+                    q4_word(w2, fr[2][0], fr[2][2], fr[3][0], fr[3][2]);
+                } else {
+                    q8_word(w1, fr[0][0], fr[0][2]);
+                    q8_word(w2, fr[1][0], fr[1][2]);
+                    q8_word(w3, fr[2][0], fr[2][2]);
+                    q8_word(w4, fr[3][0], fr[3][2]);
+                }
+                load_pair_words<ENC>(rowg8, P, t, w1, w2, w3, w4, dj[1], dj1[1]);
+                if (ENC == CPG_ENC_Q4) {
+                    q4_word(w1, fr[0][1], fr[0][3], fr[1][1], fr[1][3]);
+                    q4_word(w2, fr[2][1], fr[2][3], fr[3][1], fr[3][3]);
+                } else {
+                    q8_word(w1, fr[0][1], fr[0][3]);
+                    q8_word(w2, fr[1][1], fr[1][3]);
+                    q8_word(w3, fr[2][1], fr[2][3]);
+                    q8_word(w4, fr[3][1], fr[3][3]);
+                }
+            }
 #pragma unroll
             for (int nt = 0; nt < EX_NCH; ++nt) {
-                const int col = (nc0 + nt) * 8 + g;
-                brow[nt] = nullptr;
-                if (nt < ntl && col < md.cnt) {
-                    const int p = md.off + col;
-                    if (KIND == KIND_GATEUP) brow[nt] = a.bsrc + (size_t)(a.pairs[p] / a.K) * a.D;
-                    else brow[nt] = a.bsrc + (size_t)p * a.F;
-                }
-            }
-            float acc[EX_NCH][4];
+                if (nt == 0 || two) {
+                    const float z[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                    float sj[4], sj1[4];
+                    mma_16816(sj, fr[0], cb[nt][0].x, cb[nt][0].y, z);
+                    mma_16816(sj, fr[1], cb[nt][0].z, cb[nt][0].w, sj);
+                    mma_16816(sj1, fr[2], cb[nt][1].x, cb[nt][1].y, z);
+                    mma_16816(sj1, fr[3], cb[nt][1].z, cb[nt][1].w, sj1);
 #pragma unroll
-            for (int nt = 0; nt < EX_NCH; ++nt)
-#pragma unroll
-                for (int c = 0; c < 4; ++c) acc[nt][c] = 0.0f;
-
-            for (int P = kp; P < NP; P += C::KS) {
-                uint32_t fr[4][4];       // [k16 step][a0..a3]
-                float dj[2], dj1[2];     // scales: group j / j+1, rows g / g+8
-                {
-                    uint32_t w1, w2, w3, w4;
-                    load_pair_words<ENC>(rowg, P, t, w1, w2, w3, w4, dj[0], dj1[0]);
-                    if (ENC == CPG_ENC_Q4) {
-                        q4_word(w1, fr[0][0], fr[0][2], fr[1][0], fr[1][2]);
-                        q4_word(w2, fr[2][0], fr[2][2], fr[3][0], fr[3][2]);
-                    } else {
-                        q8_word(w1, fr[0][0], fr[0][2]);
-                        q8_word(w2, fr[1][0], fr[1][2]);
-                        q8_word(w3, fr[2][0], fr[2][2]);
-                        q8_word(w4, fr[3][0], fr[3][2]);
-                    }
-                    load_pair_words<ENC>(rowg8, P, t, w1, w2, w3, w4, dj[1], dj1[1]);
-                    if (ENC == CPG_ENC_Q4) {
-                        q4_word(w1, fr[0][1], fr[0][3], fr[1][1], fr[1][3]);
-                        q4_word(w2, fr[2][1], fr[2][3], fr[3][1], fr[3][3]);
-                    } else {
-                        q8_word(w1, fr[0][1], fr[0][3]);
-                        q8_word(w2, fr[1][1], fr[1][3]);
-                        q8_word(w3, fr[2][1], fr[2][3]);
-                        q8_word(w4, fr[3][1], fr[3][3]);
-                    }
-                }
-#pragma unroll
-                for (int nt = 0; nt < EX_NCH; ++nt) {
-                    if (nt < ntl) {
-                        uint4 b01 = make_uint4(0, 0, 0, 0), b23 = make_uint4(0, 0, 0, 0);
-                        if (brow[nt]) {
-                            const uint4 *bp = reinterpret_cast<const uint4 *>(brow[nt] + P * 64 + t * 16);
-                            b01 = __ldg(bp);
-                            b23 = __ldg(bp + 1);
-                        }
-                        const float z[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-                        float sj[4], sj1[4];
-                        mma_16816(sj, fr[0], b01.x, b01.y, z);
-                        mma_16816(sj, fr[1], b01.z, b01.w, sj);
-                        mma_16816(sj1, fr[2], b23.x, b23.y, z);
-                        mma_16816(sj1, fr[3], b23.z, b23.w, sj1);
-#pragma unroll
-                        for (int c = 0; c < 4; ++c) {
-                            acc[nt][c] = fmaf(dj[c >> 1], sj[c], acc[nt][c]);
-                            acc[nt][c] = fmaf(dj1[c >> 1], sj1[c], acc[nt][c]);
-                        }
+                    for (int c = 0; c < 4; ++c) {
+                        acc[nt][c] = fmaf(dj[c >> 1], sj[c], acc[nt][c]);
+                        acc[nt][c] = fmaf(dj1[c >> 1], sj1[c], acc[nt][c]);
                     }
                 }
             }
-            if (nc0 + EX_NCH >= ntiles) {
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&empty[st]);     // this warp is done with the stage
-            }
-            // cross-warp reduction of the K split, then the epilogue
-#pragma unroll
-            for (int nt = 0; nt < EX_NCH; ++nt)
-                if (nt < ntl)
-                    *reinterpret_cast<float4 *>(red + ((cw * EX_NCH + nt) * 32 + lane) * 4) =
-                        make_float4(acc[nt][0], acc[nt][1], acc[nt][2], acc[nt][3]);
-            named_bar_sync(1, EX_NW * 32);
-            const int ctid = threadIdx.x - 32;
-            if (KIND == KIND_GATEUP) {
-                // element (nt, l, c): gate = combo 0, up = combo 1; K parts at warps combo + 2*kp
-                for (int i = ctid; i < ntl * 128; i += EX_NW * 32) {
-                    const int nt = i >> 7, l = (i >> 2) & 31, c = i & 3;
-                    float gsum = 0.0f, usum = 0.0f;
-#pragma unroll
-                    for (int k = 0; k < C::KS; ++k) {
-                        gsum += red[(((0 + 2 * k) * EX_NCH + nt) * 32 + l) * 4 + c];
-                        usum += red[(((1 + 2 * k) * EX_NCH + nt) * 32 + l) * 4 + c];
-                    }
-                    const int col = (nc0 + nt) * 8 + 2 * (l & 3) + (c & 1);
-                    if (col < md.cnt) {
-                        const int row = md.m * 16 + (l >> 2) + 8 * (c >> 1);          // feature in [0, F)
-                        const float silu = gsum / (1.0f + expf(-gsum));             // kernels.c:416
-                        const float h = silu * usum;                                 // qwen3_moe.c:219
-                        const int pos = (row & ~63) + hperm.elem_to_pos[row & 63];
-                        a.h_out[(size_t)(md.off + col) * a.F + pos] = __float2half_rn(h);
-                    }
-                }
-            } else {
-                for (int i = ctid; i < C::COMBOS * ntl * 128; i += EX_NW * 32) {
-                    const int cb = i / (ntl * 128), r = i - cb * ntl * 128;
-                    const int nt = r >> 7, l = (r >> 2) & 31, c = r & 3;
-                    float v = 0.0f;
-#pragma unroll
-                    for (int k = 0; k < C::KS; ++k) v += red[(((cb + C::COMBOS * k) * EX_NCH + nt) * 32 + l) * 4 + c];
-                    const int col = (nc0 + nt) * 8 + 2 * (l & 3) + (c & 1);
-                    if (col < md.cnt) {
-                        const int row = md.m * C::ROWS + cb * 16 + (l >> 2) + 8 * (c >> 1);   // in [0, D)
-                        a.y_out[(size_t)a.pairs[md.off + col] * a.D + row] = v;
-                    }
-                }
-            }
-            named_bar_sync(1, EX_NW * 32);
         }
-        if (ntiles == 0) {                              // cannot happen for an active expert
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[st]);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[st]);     // this warp is done with the stage
+        // cross-warp reduction of the K split, then the epilogue
+        const int ntl = two ? 2 : 1;
+#pragma unroll
+        for (int nt = 0; nt < EX_NCH; ++nt)
+            if (nt < ntl)
+                *reinterpret_cast<float4 *>(red + ((cw * EX_NCH + nt) * 32 + lane) * 4) =
+                    make_float4(acc[nt][0], acc[nt][1], acc[nt][2], acc[nt][3]);
+        named_bar_sync(1, EX_NW * 32);
+        const int ctid = threadIdx.x - 32;
+        if (KIND == KIND_GATEUP) {
+            // element (nt, l, c): gate = combo 0, up = combo 1; K parts at warps combo + 2*kp
+            for (int i = ctid; i < ntl * 128; i += EX_NW * 32) {
+                const int nt = i >> 7, l = (i >> 2) & 31, c = i & 3;
+                float gsum = 0.0f, usum = 0.0f;
+#pragma unroll
+                for (int k = 0; k < C::KS; ++k) {
+                    gsum += red[(((0 + 2 * k) * EX_NCH + nt) * 32 + l) * 4 + c];
+                    usum += red[(((1 + 2 * k) * EX_NCH + nt) * 32 + l) * 4 + c];
+                }
+                const int col = nt * 8 + 2 * (l & 3) + (c & 1);
+                if (col < md.cnt) {
+                    const int row = md.m * 16 + (l >> 2) + 8 * (c >> 1);          // feature in [0, F)
+                    const float silu = gsum / (1.0f + expf(-gsum));             // kernels.c:416
+                    const float h = silu * usum;                                 // qwen3_moe.c:219
+                    const int pos = (row & ~63) + s_perm.elem_to_pos[row & 63];
+                    a.h_out[(size_t)(md.off + col) * a.F + pos] = __float2half_rn(h);
+                }
+            }
+        } else {
+            for (int i = ctid; i < C::COMBOS * ntl * 128; i += EX_NW * 32) {
+                const int cbx = i / (ntl * 128), r = i - cbx * ntl * 128;
+                const int nt = r >> 7, l = (r >> 2) & 31, c = r & 3;
+                float v = 0.0f;
+#pragma unroll
+                for (int k = 0; k < C::KS; ++k) v += red[(((cbx + C::COMBOS * k) * EX_NCH + nt) * 32 + l) * 4 + c];
+                const int col = nt * 8 + 2 * (l & 3) + (c & 1);
+                if (col < md.cnt) {
+                    const int row = md.m * C::ROWS + cbx * 16 + (l >> 2) + 8 * (c >> 1);   // in [0, D)
+                    a.y_out[(size_t)a.pairs[md.off + col] * a.D + row] = v;
+                }
+            }
         }
+        named_bar_sync(1, EX_NW * 32);
     }
 }
 
@@ -634,19 +686,22 @@ static int smem_row_stride(int rb) { return (rb / 16) % 2 == 0 ? rb + 16 : rb; }
 template <int ENC, int KIND>
 static int plan_kernel(int K_in, KernelPlan &p) {
     using C = ExCfg<ENC, KIND>;
+    auto *k = k_experts<ENC, KIND>;
     const int rb = (K_in / 32) * C::GB;
     p.rs = smem_row_stride(rb);
     const int stage = C::COMBOS * 16 * p.rs;
     const size_t fixed = sizeof(float) * EX_NW * EX_NCH * 128 + 8 * (sizeof(StageMeta) + 16) + 128;
-    int S = (int)((110 * 1024 - fixed) / stage);
+    cudaFuncAttributes fa;
+    CPG_CUDA(cudaFuncGetAttributes(&fa, k));
+    const size_t limit = (size_t)smem_optin() - fa.sharedSizeBytes;
+    // two CTAs per SM (latency hiding comes from warps); stages fill about 100 KB per CTA
+    int S = (int)((100 * 1024 - fixed) / stage);
     if (S < 2) S = 2;
     if (S > 8) S = 8;
-    while (S > 1 && fixed + (size_t)S * stage > 227 * 1024) --S;
-    CPG_REQUIRE(S >= 1, "expert kernel: a %d-byte stage does not fit in shared memory", stage);
+    while (S > 1 && fixed + (size_t)S * stage > limit) --S;
+    CPG_REQUIRE(fixed + (size_t)S * stage <= limit, "expert kernel: a %d-byte stage does not fit in shared memory", stage);
     p.stages = S;
     p.smem = (size_t)S * stage + sizeof(float) * EX_NW * EX_NCH * 128 + S * sizeof(StageMeta) + 2 * S * sizeof(uint64_t);
-    auto *k = k_experts<ENC, KIND>;
-    CPG_REQUIRE((int)p.smem <= smem_optin(), "expert kernel: %zu bytes of shared memory exceed the device limit", p.smem);
     int rc = allow_max_smem((const void *)k);
     if (rc) return rc;
     int per_sm = 0;
@@ -794,16 +849,18 @@ int cpg::moe_forward_impl(const cpg_moe_layer *L, const float *x, const float *a
     ra.xn_perm = (__half *)(w + W.xn);
     ra.status = hdr;
     ra.tile_cnt = (int *)(w + W.tile_cnt);
-    ra.ex_cnt = (int *)(w + W.ex_cnt); ra.ex_off = (int *)(w + W.ex_off);
-    ra.ex_list = (int *)(w + W.ex_list); ra.n_active = (int *)(w + W.n_active);
+    ra.ptrs = L->d_ptrs;
+    ra.n_active = (int *)(w + W.n_active);
+    ra.act = (int4 *)(w + W.act);
+    ra.act_ptr = (const uint8_t **)(w + W.act_ptr);
     ra.pairs = (int *)(w + W.pairs);
     dim3 rgrid((L->E + R_EB - 1) / R_EB, (T + R_TB - 1) / R_TB);
     k_router<<<rgrid, R_THREADS, (size_t)R_TB * L->D * sizeof(float), s>>>(ra);
     CPG_CUDA(cudaGetLastError());
 
     ExpertArgs ea{};
-    ea.ptrs = L->d_ptrs; ea.D = L->D; ea.F = L->F; ea.K = L->K;
-    ea.ex_cnt = ra.ex_cnt; ea.ex_off = ra.ex_off; ea.ex_list = ra.ex_list; ea.n_active = ra.n_active;
+    ea.D = L->D; ea.F = L->F; ea.K = L->K;
+    ea.n_active = ra.n_active; ea.act = ra.act; ea.act_ptr = ra.act_ptr;
     ea.pairs = ra.pairs; ea.h_enc = L->enc; ea.status = hdr;
     const int max_active = T * L->K < L->E ? T * L->K : L->E;
 
