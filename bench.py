@@ -234,11 +234,31 @@ def run_ours(args, rank, world, torch, dist):
     dev_out = xbuf.cpu()
     assert torch.equal(dev_out, pinned[-1]), "host-buffer path disagrees with the device path"
 
+    # ---- batch-1 decode on the same stack (the north-star decode target: one token per step)
+    x1 = x0[:1].clone()
+    xb1 = xbuf[:1]
+
+    def step1():
+        with torch.cuda.stream(s):
+            xb1.copy_(x1)
+        ctx.run_device(arr, L, 1)
+
+    for _ in range(args.warmup):
+        step1()
+    barrier()
+    b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    b0.record(s)
+    for _ in range(args.steps):
+        step1()
+    b1.record(s)
+    barrier()
+    ms_b1 = b0.elapsed_time(b1)
+
     # max over ranks
-    t = torch.tensor([ms, ms_e2e], dtype=torch.float64, device="cuda")
+    t = torch.tensor([ms, ms_e2e, ms_b1], dtype=torch.float64, device="cuda")
     if dist is not None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms, ms_e2e = float(t[0]), float(t[1])
+    ms, ms_e2e, ms_b1 = float(t[0]), float(t[1]), float(t[2])
     if rank != 0:
         return None
 
@@ -248,6 +268,7 @@ def run_ours(args, rank, world, torch, dist):
     ms_step = ms / args.steps
     hbm, kind = peaks()
     gateup_ms_per_step = phase[1] / args.steps
+    b1_bytes = L * (LN_BYTES + ROUTER_BYTES + K * REGION_BYTES + 2 * D * 4)
     achieved = gateup_bytes / (gateup_ms_per_step * 1e-3) / 1e9
     tok_s = world * T * args.steps / (ms * 1e-3)
     e2e_tok_s = world * T * args.steps / (ms_e2e * 1e-3)
@@ -272,6 +293,11 @@ def run_ours(args, rank, world, torch, dist):
                      "algorithmic_bytes_per_launch": int(gateup_bytes / L), "traffic": None},
         "e2e": {"value": round(e2e_tok_s, 1), "unit": "tok/s", "h2d_bytes_per_step": xbytes,
                 "d2h_bytes_per_step": xbytes},
+        "decode_batch1": {"value": round(world * args.steps / (ms_b1 * 1e-3), 1), "unit": "tok/s",
+                          "ms_per_step": round(ms_b1 / args.steps, 4),
+                          "hbm_gbs": round(b1_bytes / (ms_b1 / args.steps * 1e-3) / 1e9, 1),
+                          "frac": round(b1_bytes / (ms_b1 / args.steps * 1e-3) / 1e9 / hbm, 4),
+                          "bytes_per_step": b1_bytes},
         "gpu_launches": 4 * L * args.steps,
         "clocks": clk,
     }

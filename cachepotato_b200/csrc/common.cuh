@@ -5,6 +5,8 @@
 #include <stdint.h>
 #include <stdio.h>
 
+#include <utility>
+
 #include "cpg.h"
 
 namespace cpg {
@@ -39,7 +41,30 @@ inline long row_bytes(int enc, long n_in) {
     return enc == CPG_ENC_F32 ? 4 * n_in : (n_in / 32) * group_bytes(enc);
 }
 
+// Launch with programmatic dependent launch: the kernel may start while the previous kernel on
+// the stream drains; it must call pdl_wait() before touching anything that kernel produces.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                              Args &&...args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 // ------------------------------------------------------------------ device helpers
+
+// Wait until the grid this one depends on has completed and its writes are visible.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Let the next kernel on the stream start launching (it still waits in pdl_wait()).
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
 
 // fp16 bits -> f32 by bit manipulation, NaN payloads and subnormals preserved exactly as
 // the reference decoder does (engine/kernels/kernels.c:109-130).

@@ -24,7 +24,6 @@ namespace cpg {
 
 // ------------------------------------------------------------------ constants and layouts
 constexpr int R_TB = 8;          // router: tokens per CTA (one warp per token)
-constexpr int R_EB = 4;          // router: experts per CTA (two warps per expert)
 constexpr int R_THREADS = 256;
 constexpr int MAX_E = 256;
 constexpr int MAX_K = 32;
@@ -39,8 +38,7 @@ constexpr int EX_NCHUNK = 8 * EX_NCH;   // tokens per item (an expert with more 
 enum { WS_STATUS = 0, WS_DONE_TILES = 1, WS_ITEMS_GATEUP = 2, WS_ITEMS_DOWN = 3, WS_HDR_INTS = 16 };
 
 struct WsLayout {
-    size_t tile_cnt, n_active, act, act_ptr, pairs, topk, wt, logits, xn, h, y, total;
-    size_t memset_bytes;
+    size_t zero_row, n_active, act, act_ptr, pairs, topk, wt, logits, xn, h, y, total;
 };
 
 static size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
@@ -48,8 +46,8 @@ static size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 static WsLayout ws_layout(int D, int F, int E, int K, int T) {
     WsLayout L{};
     size_t o = WS_HDR_INTS * sizeof(int);
-    L.tile_cnt = o; o += sizeof(int) * (size_t)((T + R_TB - 1) / R_TB);
-    L.memset_bytes = o;
+    o = align_up(o, 256);
+    L.zero_row = o; o += sizeof(__half) * (size_t)(D > F ? D : F);   // operand for padded tokens
     o = align_up(o, 256);
     L.n_active = o; o += sizeof(int);
     o = align_up(o, 256);
@@ -75,12 +73,14 @@ struct RouterArgs {
     int T, D, E, K;
     float eps;
     int xn_enc;                  // permutation of the xn copy the gate/up kernel reads
+    int F;
+    int eb;                      // experts per CTA
     float *logits;
     int *topk;
     float *wt;
     __half *xn_perm;
-    int *status;                 // workspace header
-    int *tile_cnt;
+    int *status;                 // workspace header (status word, counters)
+    __half *zero_row;
     const uint8_t *const *ptrs;  // (E, 3) expert matrix pointers
     int *n_active, *pairs;
     int4 *act;                   // active experts ascending: (e, pair offset, tokens, token chunks before)
@@ -152,27 +152,54 @@ __device__ void route_token(const RouterArgs &a, int t) {
 }
 
 // group (token, slot) pairs by expert, tokens ascending inside an expert; one CTA
+__device__ __forceinline__ int warp_incl_scan(int v) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int n = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += n;
+    }
+    return v;
+}
+
+// Group (token, slot) pairs by expert, tokens ascending inside an expert, and publish the
+// active-expert table the expert kernels schedule from. One CTA; top-k ids staged in shared
+// memory (they fit for decode batches; larger batches read them from global memory).
 __device__ void group_pairs(const RouterArgs &a) {
     __shared__ int s_cnt[MAX_E], s_off[MAX_E], s_base[MAX_E], s_uidx[MAX_E], s_chp[MAX_E];
     __shared__ uint32_t s_mask[MAX_E];
-    const int tid = threadIdx.x;
-    for (int e = tid; e < a.E; e += blockDim.x) { s_cnt[e] = 0; s_base[e] = 0; }
-    __syncthreads();
+    __shared__ int s_tk[R_TB * 8 * MAX_K];
+    __shared__ int s_tot[3];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int TK = a.T * a.K;
-    for (int i = tid; i < TK; i += blockDim.x) atomicAdd(&s_cnt[__ldcg(a.topk + i)], 1);
+    const bool staged = TK <= R_TB * 8 * MAX_K;
+    for (int e = tid; e < a.E; e += blockDim.x) { s_cnt[e] = 0; s_base[e] = 0; }
+    if (staged)
+        for (int i = tid; i < TK; i += blockDim.x) s_tk[i] = __ldcg(a.topk + i);
     __syncthreads();
-    if (tid == 0) {                      // shared-memory scan only: offsets, active index, chunks
+    const int *tk = staged ? s_tk : a.topk;
+    for (int i = tid; i < TK; i += blockDim.x) atomicAdd(&s_cnt[staged ? tk[i] : __ldcg(a.topk + i)], 1);
+    __syncthreads();
+    if (warp == 0) {                     // exclusive scans over experts, 32 at a time
         int o = 0, u = 0, chp = 0;
-        for (int e = 0; e < a.E; ++e) {
-            s_off[e] = o;
-            s_chp[e] = chp;
-            s_uidx[e] = s_cnt[e] > 0 ? u : -1;
-            o += s_cnt[e];
-            chp += (s_cnt[e] + EX_NCHUNK - 1) / EX_NCHUNK;
-            u += s_cnt[e] > 0;
+        for (int e0 = 0; e0 < a.E; e0 += 32) {
+            const int e = e0 + lane;
+            const int c = e < a.E ? s_cnt[e] : 0;
+            const int ch = (c + EX_NCHUNK - 1) / EX_NCHUNK, act = c > 0;
+            const int ic = warp_incl_scan(c), ich = warp_incl_scan(ch), ia = warp_incl_scan(act);
+            if (e < a.E) {
+                s_off[e] = o + ic - c;
+                s_chp[e] = chp + ich - ch;
+                s_uidx[e] = act ? u + ia - 1 : -1;
+            }
+            o += __shfl_sync(0xffffffffu, ic, 31);
+            chp += __shfl_sync(0xffffffffu, ich, 31);
+            u += __shfl_sync(0xffffffffu, ia, 31);
         }
-        a.act[u] = make_int4(-1, o, 0, chp);
-        *a.n_active = u;
+        if (lane == 0) {
+            a.act[u] = make_int4(-1, o, 0, chp);
+            *a.n_active = u;
+        }
     }
     __syncthreads();
     for (int e = tid; e < a.E; e += blockDim.x) {     // one thread per expert: loads in parallel
@@ -184,20 +211,25 @@ __device__ void group_pairs(const RouterArgs &a) {
             a.act_ptr[3 * u + 2] = a.ptrs[3 * e + 2];
         }
     }
+    (void)s_tot;
     for (int c0 = 0; c0 < a.T; c0 += 32) {
         for (int e = tid; e < a.E; e += blockDim.x) s_mask[e] = 0;
         __syncthreads();
         for (int i = tid; i < 32 * a.K; i += blockDim.x) {
             const int tl = i / a.K, t = c0 + tl;
-            if (t < a.T) atomicOr(&s_mask[__ldcg(a.topk + (size_t)t * a.K + i % a.K)], 1u << tl);
+            if (t < a.T) {
+                const int idx = t * a.K + i % a.K;
+                atomicOr(&s_mask[staged ? tk[idx] : __ldcg(a.topk + idx)], 1u << tl);
+            }
         }
         __syncthreads();
         for (int i = tid; i < 32 * a.K; i += blockDim.x) {
             const int tl = i / a.K, j = i % a.K, t = c0 + tl;
             if (t < a.T) {
-                const int e = __ldcg(a.topk + (size_t)t * a.K + j);
+                const int idx = t * a.K + j;
+                const int e = staged ? tk[idx] : __ldcg(a.topk + idx);
                 const int r = s_base[e] + __popc(s_mask[e] & ((1u << tl) - 1u));
-                a.pairs[s_off[e] + r] = t * a.K + j;
+                a.pairs[s_off[e] + r] = idx;
             }
         }
         __syncthreads();
@@ -208,21 +240,29 @@ __device__ void group_pairs(const RouterArgs &a) {
 
 __global__ void __launch_bounds__(R_THREADS) k_router(RouterArgs a) {
     extern __shared__ float xs[];                         // (R_TB, D): hh, then xn
-    __shared__ float part[2][R_EB][R_TB];
     __shared__ int s_last;
     __shared__ uint8_t s_p2e[64];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int t0 = blockIdx.y * R_TB, nt = min(R_TB, a.T - t0);
     if (tid < 64) s_p2e[tid] = perm_of(a.xn_enc).pos_to_elem[tid];
-    __syncthreads();
-    const int e0 = blockIdx.x * R_EB;
+    const int e0 = blockIdx.x * a.eb;
     const int D = a.D;
+    pdl_wait();                                           // x comes from the previous kernel
+    pdl_launch_dependents();
+    if (blockIdx.x == 0 && blockIdx.y == 0) {
+        // per-forward state: status word and counters, the padding operand row
+        if (tid < WS_HDR_INTS) a.status[tid] = 0;
+        for (int i = tid; i < (D > a.F ? D : a.F) / 2; i += R_THREADS)
+            reinterpret_cast<uint32_t *>(a.zero_row)[i] = 0u;
+    }
+    __syncthreads();
 
     // hh = x + attn (qwen3_moe.c:178)
     {
         const float4 *x4 = reinterpret_cast<const float4 *>(a.x + (size_t)t0 * D);
         const float4 *a4 = a.attn ? reinterpret_cast<const float4 *>(a.attn + (size_t)t0 * D) : nullptr;
         float4 *s4 = reinterpret_cast<float4 *>(xs);
+#pragma unroll 8
         for (int i = tid; i < nt * D / 4; i += R_THREADS) {
             float4 v = x4[i];
             if (a4) {
@@ -241,7 +281,8 @@ __global__ void __launch_bounds__(R_THREADS) k_router(RouterArgs a) {
         for (int k = lane; k < D; k += 32) ss = fmaf(row[k], row[k], ss);
         ss = warp_sum(ss);
         const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fdiv_rn(ss, (float)D) + a.eps));
-        for (int k = lane; k < D; k += 32) row[k] = __fmul_rn(__fmul_rn(row[k], inv), a.ln2[k]);
+#pragma unroll 8
+        for (int k = lane; k < D; k += 32) row[k] = __fmul_rn(__fmul_rn(row[k], inv), __ldg(a.ln2 + k));
         __syncwarp();
         if (blockIdx.x == 0) {
             // fp16 copy of xn in the expert kernels' K order
@@ -251,54 +292,49 @@ __global__ void __launch_bounds__(R_THREADS) k_router(RouterArgs a) {
         }
     }
     __syncthreads();
-    // logits = Wgate·xn (matmul_wx, kernels.c:84-95): warp -> (expert e0 + w%4, half w/4)
-    {
-        const int el = warp & 3, half = warp >> 2, e = e0 + el;
+    // logits = Wgate·xn (matmul_wx, kernels.c:84-95): warp w owns experts e0 + w, e0 + w + 8, ...
+    for (int el = warp; el < a.eb; el += R_THREADS / 32) {
+        const int e = e0 + el;
+        if (e >= a.E) break;
         float acc[R_TB];
 #pragma unroll
         for (int t = 0; t < R_TB; ++t) acc[t] = 0.0f;
-        if (e < a.E) {
-            const int k0 = half * (D / 2), k1 = k0 + D / 2;
-            const float4 *w4 = reinterpret_cast<const float4 *>(a.wgate + (size_t)e * D);
-#pragma unroll 8
-            for (int k = k0 + lane * 4; k < k1; k += 128) {
-                const float4 w = __ldg(w4 + k / 4);
+        const float4 *w4 = reinterpret_cast<const float4 *>(a.wgate + (size_t)e * D);
+#pragma unroll 4
+        for (int k = lane * 4; k < D; k += 128) {
+            const float4 w = __ldg(w4 + k / 4);
 #pragma unroll
-                for (int t = 0; t < R_TB; ++t) {
-                    if (t < nt) {
-                        const float4 v = *reinterpret_cast<const float4 *>(xs + t * D + k);
-                        acc[t] = fmaf(w.x, v.x, acc[t]);
-                        acc[t] = fmaf(w.y, v.y, acc[t]);
-                        acc[t] = fmaf(w.z, v.z, acc[t]);
-                        acc[t] = fmaf(w.w, v.w, acc[t]);
-                    }
+            for (int t = 0; t < R_TB; ++t) {
+                if (t < nt) {
+                    const float4 v = *reinterpret_cast<const float4 *>(xs + t * D + k);
+                    acc[t] = fmaf(w.x, v.x, acc[t]);
+                    acc[t] = fmaf(w.y, v.y, acc[t]);
+                    acc[t] = fmaf(w.z, v.z, acc[t]);
+                    acc[t] = fmaf(w.w, v.w, acc[t]);
                 }
             }
         }
 #pragma unroll
         for (int t = 0; t < R_TB; ++t) {
             const float v = warp_sum(acc[t]);
-            if (lane == 0) part[half][el][t] = v;
+            if (lane == 0 && t < nt) a.logits[(size_t)(t0 + t) * a.E + e] = v;
         }
     }
-    __syncthreads();
-    if (tid < R_EB * R_TB) {
-        const int el = tid / R_TB, t = tid % R_TB;
-        if (t < nt && e0 + el < a.E)
-            a.logits[(size_t)(t0 + t) * a.E + e0 + el] = part[0][el][t] + part[1][el][t];
-    }
-    // last CTA of this token tile routes its tokens
+}
+
+// Softmax, top-k and renormalisation for a tile of tokens (one warp per token); the last CTA
+// to finish groups all (token, slot) pairs by expert.
+constexpr int RT_THREADS = 512;
+__global__ void __launch_bounds__(RT_THREADS) k_route(RouterArgs a) {
+    __shared__ int s_last;
+    pdl_wait();                                           // logits from k_router
+    pdl_launch_dependents();
+    const int warp = threadIdx.x >> 5;
+    const int t = blockIdx.x * (RT_THREADS / 32) + warp;
+    if (t < a.T) route_token(a, t);
     __threadfence();
     __syncthreads();
-    if (tid == 0) s_last = atomicAdd(a.tile_cnt + blockIdx.y, 1) == (int)gridDim.x - 1;
-    __syncthreads();
-    if (!s_last) return;
-    __threadfence();
-    if (warp < nt) route_token(a, t0 + warp);
-    // last tile groups all pairs by expert
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) s_last = atomicAdd(a.status + WS_DONE_TILES, 1) == (int)gridDim.y - 1;
+    if (threadIdx.x == 0) s_last = atomicAdd(a.status + WS_DONE_TILES, 1) == (int)gridDim.x - 1;
     __syncthreads();
     if (!s_last) return;
     __threadfence();
@@ -315,6 +351,7 @@ struct ExpertArgs {
     __half *h_out;               // GATEUP output (pairs, F), permuted for Wd
     float *y_out;                // DOWN output (T*K, D), row = t*K + j
     int h_enc;                   // encoding of Wd (permutation of h_out)
+    const __half *zero_row;      // operand row for padded token columns (zeroed with the header)
     int *status;
     int *item_ctr;               // dynamic work counter (zeroed with the header)
     int stages;
@@ -390,6 +427,81 @@ __device__ __forceinline__ void decode_item(const int4 *act, int U, int tiles, i
     c = local - m * nch;
 }
 
+
+// Operand fragments of group pair P for the NTL token tiles (32 contiguous bytes per thread).
+template <int NTL>
+__device__ __forceinline__ void load_b(const __half *const (&brow)[EX_NCH], int P, uint4 (&b)[EX_NCH][2]) {
+#pragma unroll
+    for (int nt = 0; nt < NTL; ++nt) {
+        const uint4 *bp = reinterpret_cast<const uint4 *>(brow[nt] + P * 64);
+        b[nt][0] = __ldg(bp);
+        b[nt][1] = __ldg(bp + 1);
+    }
+}
+
+// One group pair (64 K values) of rows g and g+8: decode, then 4 MMAs per token tile and the
+// fp32 group-scale accumulation.
+template <int ENC, int NTL>
+__device__ __forceinline__ void group_pair_mma(const uint32_t *rowg, const uint32_t *rowg8, int P, int t,
+                                               const uint4 (&b)[EX_NCH][2], float (&acc)[EX_NCH][4]) {
+    uint32_t fr[4][4];       // [k16 step][a0..a3]
+    float dj[2], dj1[2];     // scales: group j / j+1, rows g / g+8
+    uint32_t w1, w2, w3, w4;
+    load_pair_words<ENC>(rowg, P, t, w1, w2, w3, w4, dj[0], dj1[0]);
+    if (ENC == CPG_ENC_Q4) {
+        q4_word(w1, fr[0][0], fr[0][2], fr[1][0], fr[1][2]);
+        q4_word(w2, fr[2][0], fr[2][2], fr[3][0], fr[3][2]);
+    } else {
+        q8_word(w1, fr[0][0], fr[0][2]);
+        q8_word(w2, fr[1][0], fr[1][2]);
+        q8_word(w3, fr[2][0], fr[2][2]);
+        q8_word(w4, fr[3][0], fr[3][2]);
+    }
+    load_pair_words<ENC>(rowg8, P, t, w1, w2, w3, w4, dj[1], dj1[1]);
+    if (ENC == CPG_ENC_Q4) {
+        q4_word(w1, fr[0][1], fr[0][3], fr[1][1], fr[1][3]);
+        q4_word(w2, fr[2][1], fr[2][3], fr[3][1], fr[3][3]);
+    } else {
+        q8_word(w1, fr[0][1], fr[0][3]);
+        q8_word(w2, fr[1][1], fr[1][3]);
+        q8_word(w3, fr[2][1], fr[2][3]);
+        q8_word(w4, fr[3][1], fr[3][3]);
+    }
+#pragma unroll
+    for (int nt = 0; nt < NTL; ++nt) {
+        const float z[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        float sj[4], sj1[4];
+        mma_16816(sj, fr[0], b[nt][0].x, b[nt][0].y, z);
+        mma_16816(sj, fr[1], b[nt][0].z, b[nt][0].w, sj);
+        mma_16816(sj1, fr[2], b[nt][1].x, b[nt][1].y, z);
+        mma_16816(sj1, fr[3], b[nt][1].z, b[nt][1].w, sj1);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            acc[nt][c] = fmaf(dj[c >> 1], sj[c], acc[nt][c]);
+            acc[nt][c] = fmaf(dj1[c >> 1], sj1[c], acc[nt][c]);
+        }
+    }
+}
+
+// This warp's share of the K split (group pairs kp, kp+KS, ...), operands loaded one group pair
+// ahead into two alternating buffers.
+template <int ENC, int KS, int NTL>
+__device__ __forceinline__ void expert_item_loop(const uint32_t *rowg, const uint32_t *rowg8,
+                                                 const __half *const (&brow)[EX_NCH], int NP, int kp, int t,
+                                                 float (&acc)[EX_NCH][4]) {
+    uint4 b0[EX_NCH][2], b1[EX_NCH][2];
+    load_b<NTL>(brow, kp, b0);
+    for (int P = kp; P < NP; P += 2 * KS) {
+        const int P1 = P + KS;
+        load_b<NTL>(brow, P1 < NP ? P1 : P, b1);
+        group_pair_mma<ENC, NTL>(rowg, rowg8, P, t, b0, acc);
+        if (P1 >= NP) break;
+        const int P2 = P1 + KS;
+        load_b<NTL>(brow, P2 < NP ? P2 : P1, b0);
+        group_pair_mma<ENC, NTL>(rowg, rowg8, P1, t, b1, acc);
+    }
+}
+
 template <int ENC, int KIND>
 __global__ void __launch_bounds__((1 + EX_NW) * 32, 2) k_experts(ExpertArgs a) {
     using C = ExCfg<ENC, KIND>;
@@ -424,6 +536,8 @@ __global__ void __launch_bounds__((1 + EX_NW) * 32, 2) k_experts(ExpertArgs a) {
         s_perm.pos_to_elem[threadIdx.x] = pm.pos_to_elem[threadIdx.x];
         s_perm.elem_to_pos[threadIdx.x] = pm.elem_to_pos[threadIdx.x];
     }
+    pdl_wait();                                  // routing table from k_route / h from gate-up
+    pdl_launch_dependents();
     const int U = *a.n_active;
     for (int u = threadIdx.x; u <= U; u += blockDim.x) {
         s_act[u] = a.act[u];
@@ -507,87 +621,25 @@ __global__ void __launch_bounds__((1 + EX_NW) * 32, 2) k_experts(ExpertArgs a) {
         const uint32_t *rowg = rows + (g * RS) / 4;
         const uint32_t *rowg8 = rows + ((g + 8) * RS) / 4;
         const bool two = md.cnt > 8;                 // second 8-token MMA tile in use
-        // B rows for column g of each tile (nullptr = zero padding)
-        const __half *brow0 = nullptr, *brow1 = nullptr;
-        if (g < md.cnt) {
-            const int p = md.off + g;
-            brow0 = KIND == KIND_GATEUP ? a.bsrc + (size_t)(a.pairs[p] / a.K) * a.D : a.bsrc + (size_t)p * a.F;
-        }
-        if (8 + g < md.cnt) {
-            const int p = md.off + 8 + g;
-            brow1 = KIND == KIND_GATEUP ? a.bsrc + (size_t)(a.pairs[p] / a.K) * a.D : a.bsrc + (size_t)p * a.F;
+        // operand rows for column g of both 8-token tiles (the zero row pads short chunks)
+        const __half *brow[EX_NCH];
+#pragma unroll
+        for (int nt = 0; nt < EX_NCH; ++nt) {
+            const int col = nt * 8 + g;
+            brow[nt] = a.zero_row;
+            if (col < md.cnt) {
+                const int p = md.off + col;
+                brow[nt] = KIND == KIND_GATEUP ? a.bsrc + (size_t)(a.pairs[p] / a.K) * a.D : a.bsrc + (size_t)p * a.F;
+            }
+            brow[nt] += t * 16;
         }
         float acc[EX_NCH][4];
 #pragma unroll
         for (int nt = 0; nt < EX_NCH; ++nt)
 #pragma unroll
             for (int c = 0; c < 4; ++c) acc[nt][c] = 0.0f;
-
-        // B fragments one group pair ahead of the MMAs
-        uint4 nb[EX_NCH][2];
-        auto load_b = [&](int P, uint4 (&b)[EX_NCH][2]) {
-            b[0][0] = b[0][1] = b[1][0] = b[1][1] = make_uint4(0, 0, 0, 0);
-            if (P < NP) {
-                if (brow0) {
-                    const uint4 *bp = reinterpret_cast<const uint4 *>(brow0 + P * 64 + t * 16);
-                    b[0][0] = __ldg(bp);
-                    b[0][1] = __ldg(bp + 1);
-                }
-                if (brow1) {
-                    const uint4 *bp = reinterpret_cast<const uint4 *>(brow1 + P * 64 + t * 16);
-                    b[1][0] = __ldg(bp);
-                    b[1][1] = __ldg(bp + 1);
-                }
-            }
-        };
-        load_b(kp, nb);
-        for (int P = kp; P < NP; P += C::KS) {
-            uint4 cb[EX_NCH][2];
-#pragma unroll
-            for (int nt = 0; nt < EX_NCH; ++nt) { cb[nt][0] = nb[nt][0]; cb[nt][1] = nb[nt][1]; }
-            load_b(P + C::KS, nb);
-            uint32_t fr[4][4];       // [k16 step][a0..a3]
-            float dj[2], dj1[2];     // scales: group j / j+1, rows g / g+8
-            {
-                uint32_t w1, w2, w3, w4;
-                load_pair_words<ENC>(rowg, P, t, w1, w2, w3, w4, dj[0], dj1[0]);
-                if (ENC == CPG_ENC_Q4) {
-                    q4_word(w1, fr[0][0], fr[0][2], fr[1][0], fr[1][2]);
-                    q4_word(w2, fr[2][0], fr[2][2], fr[3][0], fr[3][2]);
-                } else {
-                    q8_word(w1, fr[0][0], fr[0][2]);
-                    q8_word(w2, fr[1][0], fr[1][2]);
-                    q8_word(w3, fr[2][0], fr[2][2]);
-                    q8_word(w4, fr[3][0], fr[3][2]);
-                }
-                load_pair_words<ENC>(rowg8, P, t, w1, w2, w3, w4, dj[1], dj1[1]);
-                if (ENC == CPG_ENC_Q4) {
-                    q4_word(w1, fr[0][1], fr[0][3], fr[1][1], fr[1][3]);
-                    q4_word(w2, fr[2][1], fr[2][3], fr[3][1], fr[3][3]);
-                } else {
-                    q8_word(w1, fr[0][1], fr[0][3]);
-                    q8_word(w2, fr[1][1], fr[1][3]);
-                    q8_word(w3, fr[2][1], fr[2][3]);
-                    q8_word(w4, fr[3][1], fr[3][3]);
-                }
-            }
-#pragma unroll
-            for (int nt = 0; nt < EX_NCH; ++nt) {
-                if (nt == 0 || two) {
-                    const float z[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-                    float sj[4], sj1[4];
-                    mma_16816(sj, fr[0], cb[nt][0].x, cb[nt][0].y, z);
-                    mma_16816(sj, fr[1], cb[nt][0].z, cb[nt][0].w, sj);
-                    mma_16816(sj1, fr[2], cb[nt][1].x, cb[nt][1].y, z);
-                    mma_16816(sj1, fr[3], cb[nt][1].z, cb[nt][1].w, sj1);
-#pragma unroll
-                    for (int c = 0; c < 4; ++c) {
-                        acc[nt][c] = fmaf(dj[c >> 1], sj[c], acc[nt][c]);
-                        acc[nt][c] = fmaf(dj1[c >> 1], sj1[c], acc[nt][c]);
-                    }
-                }
-            }
-        }
+        if (two) expert_item_loop<ENC, C::KS, 2>(rowg, rowg8, brow, NP, kp, t, acc);
+        else expert_item_loop<ENC, C::KS, 1>(rowg, rowg8, brow, NP, kp, t, acc);
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[st]);     // this warp is done with the stage
         // cross-warp reduction of the K split, then the epilogue
@@ -639,17 +691,33 @@ __global__ void __launch_bounds__((1 + EX_NW) * 32, 2) k_experts(ExpertArgs a) {
 // ------------------------------------------------------------------ combine
 __global__ void k_combine(const float *__restrict__ x, const float *__restrict__ attn, int T, int D, int K,
                           const float *__restrict__ wt, const float *__restrict__ y, float *mlp, float *x_out) {
+    pdl_wait();                                  // y from the down-projection kernel
+    pdl_launch_dependents();
     const int n4 = T * D / 4;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += gridDim.x * blockDim.x) {
         const int t = (i * 4) / D, k = i * 4 - t * D;
         float4 acc = mlp ? reinterpret_cast<const float4 *>(mlp)[i] : make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int j = 0; j < K; ++j) {            // qwen3_moe.c:221, selection order, no fusion
-            const float w = wt[t * K + j];
-            const float4 v = *reinterpret_cast<const float4 *>(y + ((size_t)t * K + j) * D + k);
-            acc.x = __fadd_rn(acc.x, __fmul_rn(w, v.x));
-            acc.y = __fadd_rn(acc.y, __fmul_rn(w, v.y));
-            acc.z = __fadd_rn(acc.z, __fmul_rn(w, v.z));
-            acc.w = __fadd_rn(acc.w, __fmul_rn(w, v.w));
+        const float *wt_t = wt + t * K;
+        const float *y_t = y + (size_t)t * K * D + k;
+        for (int j0 = 0; j0 < K; j0 += 8) {      // qwen3_moe.c:221: selection order, no fusion
+            float4 v[8];
+            float w[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                if (j0 + j < K) {
+                    v[j] = __ldg(reinterpret_cast<const float4 *>(y_t + (size_t)(j0 + j) * D));
+                    w[j] = __ldg(wt_t + j0 + j);
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                if (j0 + j < K) {
+                    acc.x = __fadd_rn(acc.x, __fmul_rn(w[j], v[j].x));
+                    acc.y = __fadd_rn(acc.y, __fmul_rn(w[j], v[j].y));
+                    acc.z = __fadd_rn(acc.z, __fmul_rn(w[j], v[j].z));
+                    acc.w = __fadd_rn(acc.w, __fmul_rn(w[j], v[j].w));
+                }
+            }
         }
         if (mlp) reinterpret_cast<float4 *>(mlp)[i] = acc;
         if (x_out) {
@@ -718,14 +786,9 @@ static int launch_experts(const cpg_moe_layer *L, int KIND, const ExpertArgs &a,
     b.stages = p.stages;
     b.rs = p.rs;
     const dim3 block((1 + EX_NW) * 32);
-    if (L->enc == CPG_ENC_Q4) {
-        if (KIND == KIND_GATEUP) k_experts<CPG_ENC_Q4, KIND_GATEUP><<<grid, block, p.smem, s>>>(b);
-        else k_experts<CPG_ENC_Q4, KIND_DOWN><<<grid, block, p.smem, s>>>(b);
-    } else {
-        if (KIND == KIND_GATEUP) k_experts<CPG_ENC_Q8, KIND_GATEUP><<<grid, block, p.smem, s>>>(b);
-        else k_experts<CPG_ENC_Q8, KIND_DOWN><<<grid, block, p.smem, s>>>(b);
-    }
-    CPG_CUDA(cudaGetLastError());
+    auto *k = L->enc == CPG_ENC_Q4 ? (KIND == KIND_GATEUP ? k_experts<CPG_ENC_Q4, KIND_GATEUP> : k_experts<CPG_ENC_Q4, KIND_DOWN>)
+                                   : (KIND == KIND_GATEUP ? k_experts<CPG_ENC_Q8, KIND_GATEUP> : k_experts<CPG_ENC_Q8, KIND_DOWN>);
+    CPG_CUDA(launch_pdl(k, dim3(grid), block, p.smem, s, b));
     return CPG_OK;
 }
 
@@ -838,52 +901,55 @@ int cpg::moe_forward_impl(const cpg_moe_layer *L, const float *x, const float *a
     uint8_t *w = (uint8_t *)ws;
     int *hdr = (int *)w;
     if (ev) CPG_CUDA(cudaEventRecordWithFlags(ev[0], s, cudaEventRecordExternal));
-    CPG_CUDA(cudaMemsetAsync(w, 0, W.memset_bytes, s));
 
     RouterArgs ra{};
     ra.x = x; ra.attn = attn; ra.ln2 = L->ln2; ra.wgate = L->wgate;
-    ra.T = T; ra.D = L->D; ra.E = L->E; ra.K = L->K; ra.eps = L->eps; ra.xn_enc = L->enc;
+    ra.T = T; ra.D = L->D; ra.F = L->F; ra.E = L->E; ra.K = L->K; ra.eps = L->eps; ra.xn_enc = L->enc;
     ra.logits = router ? router : (float *)(w + W.logits);
     ra.topk = topk_idx ? topk_idx : (int *)(w + W.topk);
     ra.wt = wt ? wt : (float *)(w + W.wt);
     ra.xn_perm = (__half *)(w + W.xn);
     ra.status = hdr;
-    ra.tile_cnt = (int *)(w + W.tile_cnt);
+    ra.zero_row = (__half *)(w + W.zero_row);
     ra.ptrs = L->d_ptrs;
     ra.n_active = (int *)(w + W.n_active);
     ra.act = (int4 *)(w + W.act);
     ra.act_ptr = (const uint8_t **)(w + W.act_ptr);
     ra.pairs = (int *)(w + W.pairs);
-    dim3 rgrid((L->E + R_EB - 1) / R_EB, (T + R_TB - 1) / R_TB);
-    k_router<<<rgrid, R_THREADS, (size_t)R_TB * L->D * sizeof(float), s>>>(ra);
-    CPG_CUDA(cudaGetLastError());
+    // few tokens: spread the 1 MiB router over more CTAs; many: normalise each token fewer times
+    ra.eb = T <= R_TB ? 4 : 16;
+    const dim3 rgrid((L->E + ra.eb - 1) / ra.eb, (T + R_TB - 1) / R_TB);
+    CPG_CUDA(launch_pdl(k_router, rgrid, dim3(R_THREADS), (size_t)R_TB * L->D * sizeof(float), s, ra));
+    CPG_CUDA(launch_pdl(k_route, dim3((T + RT_THREADS / 32 - 1) / (RT_THREADS / 32)), dim3(RT_THREADS), 0, s, ra));
 
     ExpertArgs ea{};
     ea.D = L->D; ea.F = L->F; ea.K = L->K;
     ea.n_active = ra.n_active; ea.act = ra.act; ea.act_ptr = ra.act_ptr;
+    ea.zero_row = ra.zero_row;
     ea.pairs = ra.pairs; ea.h_enc = L->enc; ea.status = hdr;
     const int max_active = T * L->K < L->E ? T * L->K : L->E;
+    const int max_chunks = max_active + T * L->K / EX_NCHUNK;
 
     ea.bsrc = ra.xn_perm;
     ea.h_out = (__half *)(w + W.h);
     ea.item_ctr = hdr + WS_ITEMS_GATEUP;
     if (ev) CPG_CUDA(cudaEventRecordWithFlags(ev[1], s, cudaEventRecordExternal));
-    int rc = launch_experts(L, KIND_GATEUP, ea, max_active * (L->F / 16), s);
+    int rc = launch_experts(L, KIND_GATEUP, ea, max_chunks * (L->F / 16), s);
     if (rc) return rc;
 
     ea.bsrc = (const __half *)(w + W.h);
     ea.y_out = (float *)(w + W.y);
     ea.item_ctr = hdr + WS_ITEMS_DOWN;
     if (ev) CPG_CUDA(cudaEventRecordWithFlags(ev[2], s, cudaEventRecordExternal));
-    rc = launch_experts(L, KIND_DOWN, ea, max_active * (L->D / 32), s);
+    rc = launch_experts(L, KIND_DOWN, ea, max_chunks * (L->D / 64), s);
     if (rc) return rc;
 
     const int n4 = T * L->D / 4;
     int cgrid = (n4 + 255) / 256;
     if (cgrid > sm_count() * 8) cgrid = sm_count() * 8;
     if (ev) CPG_CUDA(cudaEventRecordWithFlags(ev[3], s, cudaEventRecordExternal));
-    k_combine<<<cgrid, 256, 0, s>>>(x, attn, T, L->D, L->K, ra.wt, (const float *)(w + W.y), mlp, x_out);
-    CPG_CUDA(cudaGetLastError());
+    CPG_CUDA(launch_pdl(k_combine, dim3(cgrid), dim3(256), 0, s, x, attn, T, L->D, L->K, (const float *)ra.wt,
+                        (const float *)(w + W.y), mlp, x_out));
     if (ev) CPG_CUDA(cudaEventRecordWithFlags(ev[4], s, cudaEventRecordExternal));
     return CPG_OK;
 }
