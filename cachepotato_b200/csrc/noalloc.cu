@@ -2,9 +2,7 @@
 //
 // Some callers of this library cannot call cudaMalloc at the point where they run the MoE
 // block: a C engine embedded in a host program that owns every byte of device memory through
-// its own pool, a stream that is being captured into a CUDA graph in global capture mode (an
-// allocation there invalidates the capture), or a latency-critical decode loop that may not
-// stall on the allocator. cpg_moe_forward_noalloc serves them from a scratch array that is part
+// its own pool, or a latency-critical decode loop that may not stall on the allocator. cpg_moe_forward_noalloc serves them from a scratch array that is part
 // of the library's own device image: nothing is allocated per call.
 //
 // The array is fixed in size (kStaticScratchBytes, 8 MiB: 64 tokens of a Qwen3-30B-A3B layer

@@ -1,6 +1,6 @@
 """cpg_moe_forward_noalloc: the MoE block for callers that cannot allocate device memory where
-they run it (an engine whose host program owns all device memory, a stream under graph capture
-in global mode, a decode loop that may not wait on the allocator). Its scratch is a fixed array
+they run it (an engine whose host program owns all device memory, a decode loop that may not
+wait on the allocator). Its scratch is a fixed array
 inside the library, so its output must match the workspace entry point's, call after call.
 
 Collected last on purpose (file name), so a failure here cannot hide any other test."""
