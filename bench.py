@@ -13,6 +13,9 @@ layers (router, experts, combine, residual), weights resident in HBM.
           duration (CUDA events inside the decode graph), against MEASURED_PEAKS.json
   cpu_baseline  the reference engine (oracle/_ref: the reference's own C sources) on the host
           cores, a bounded sample of the same workload
+  prefill   configs[3]: 4096 Zipf(1.2)-routed tokens through one Q4_0 MoE block per step on the
+          tcgen05 grouped GEMM (cpg_moe_apply), tok/s and TFLOP/s, roofline of the gate/up GEMM
+          against the measured tensor peak
 
 --impl reference times the reference engine alone (rank 0), on the same metric and config.
 Multi-GPU: one process per GPU under torchrun; every rank runs its own replica (decode does not
@@ -54,6 +57,7 @@ def parse():
     ap.add_argument("--seed", type=int, default=1234)
     ap.add_argument("--cpu-sample-layers", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--prefill-tokens", type=int, default=4096, help="0 skips the prefill section")
     return ap.parse_args()
 
 
@@ -64,6 +68,15 @@ def peaks():
             j = json.load(f)
         return float(j["hbm_gbs"]), "measured"
     return 6650.0, "fallback"
+
+
+def tensor_peak():
+    """fp16/bf16 dense tensor throughput (TFLOP/s): the measured burst figure (a kernel timed alone)."""
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured (bf16 cuBLAS burst)"
+    return 1590.0, "fallback"
 
 
 # ------------------------------------------------------------------ clocks
@@ -254,11 +267,15 @@ def run_ours(args, rank, world, torch, dist):
     barrier()
     ms_b1 = b0.elapsed_time(b1)
 
+    # ---- prefill: Zipf(1.2)-routed tokens through one MoE block per step
+    pf = prefill_bench(args, layers, torch, lib, Q, s, barrier) if args.prefill_tokens > 0 else None
+    ms_pf = pf.pop("_ms") if pf else 0.0
+
     # max over ranks
-    t = torch.tensor([ms, ms_e2e, ms_b1], dtype=torch.float64, device="cuda")
+    t = torch.tensor([ms, ms_e2e, ms_b1, ms_pf], dtype=torch.float64, device="cuda")
     if dist is not None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms, ms_e2e, ms_b1 = float(t[0]), float(t[1]), float(t[2])
+    ms, ms_e2e, ms_b1, ms_pf = float(t[0]), float(t[1]), float(t[2]), float(t[3])
     if rank != 0:
         return None
 
@@ -301,7 +318,71 @@ def run_ours(args, rank, world, torch, dist):
         "gpu_launches": 4 * L * args.steps,
         "clocks": clk,
     }
+    if pf:
+        pf["value"] = round(world * args.prefill_tokens * args.steps / (ms_pf * 1e-3), 1)
+        pf["ms_per_step"] = round(ms_pf / args.steps, 4)
+        pf["tflops"] = round(pf["flops_per_step"] / (ms_pf / args.steps * 1e-3) / 1e12, 1)
+        res["prefill"] = pf
     return res
+
+
+def prefill_bench(args, layers, torch, lib, Q, s, barrier):
+    """T tokens (default 4096) whose expert assignment is drawn Zipf-Mandelbrot(1.2)
+    go through one Q4_0 MoE block per step (token sort, tcgen05 gate/up and down grouped GEMMs,
+    combine: cpg_moe_apply). Steps rotate over the 48 stacked layers, so each step reads a
+    different layer's 340 MB of experts (larger than L2)."""
+    from cachepotato_b200.workload import zipf_assignment
+    T, n = args.prefill_tokens, len(layers)
+    idx, wt = zipf_assignment(T, E, K, 1.2, 20.0, args.seed + 77)
+    counts = np.bincount(idx.ravel(), minlength=E)
+    g = torch.Generator(device="cuda").manual_seed(args.seed + 78)
+    x = torch.randn((T, D), generator=g, device="cuda")
+    xn = x * torch.rsqrt((x * x).mean(-1, keepdim=True) + 1e-6)
+    idx_d, wt_d = torch.from_numpy(idx).cuda(), torch.from_numpy(wt).cuda()
+    ws = torch.empty(int(lib.cpg_moe_apply_workspace_bytes(layers[0].handle, T)), dtype=torch.uint8, device="cuda")
+    mlp = torch.zeros((T, D), dtype=torch.float32, device="cuda")
+    torch.cuda.synchronize()
+
+    def step(i, phase=None):
+        Q.moe_apply(layers[i % n], xn, idx_d, wt_d, ws=ws, mlp=mlp, stream=s, check_status=False,
+                    phase_ms=phase)
+
+    for i in range(max(3, args.warmup)):
+        step(i)
+    Q.check(lib.cpg_moe_apply_check(ws.data_ptr(), s.cuda_stream))
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for i in range(args.steps):
+        step(i)
+    e1.record(s)
+    barrier()
+    ms = e0.elapsed_time(e1)
+    Q.check(lib.cpg_moe_apply_check(ws.data_ptr(), s.cuda_stream))
+    # per-phase times (events inside the call; synchronising, so a separate pass)
+    phase, ph = np.zeros(4), [0.0] * 4
+    for i in range(args.steps):
+        step(i, ph)
+        phase += np.array(ph)
+    phase /= args.steps
+    P = T * K
+    fl_gu, fl_dn = 2.0 * P * D * 2 * F, 2.0 * P * F * D
+    peak, kind = tensor_peak()
+    ach = fl_gu / (phase[1] * 1e-3) / 1e12
+    return {
+        "_ms": ms, "unit": "tok/s", "flops_per_step": fl_gu + fl_dn,
+        "config": {"workload": "configs[3]: 4096-token prefill through one Q4_0 MoE block, expert assignment "
+                               "Zipf-Mandelbrot(s=1.2, q=20) Gumbel-top-8, steps rotate over 48 layers",
+                   "tokens": T, "expert_tokens_min": int(counts.min()), "expert_tokens_max": int(counts.max()),
+                   "dtype": "q4_0 decoded to f16 in SMEM x f16 activations -> f32 (tcgen05 kind::f16)"},
+        "phase_ms": {"sort": round(phase[0], 4), "gate_up": round(phase[1], 4), "down": round(phase[2], 4),
+                     "combine": round(phase[3], 4)},
+        "roofline": {"bound": "tensor", "kernel": "k_gemm_tc<0> (gate/up)", "achieved": round(ach, 1),
+                     "peak": peak, "unit": "TFLOP/s", "frac": round(ach / peak, 4), "peak_kind": kind,
+                     "algorithmic_flops_per_launch": fl_gu,
+                     "down_tflops": round(fl_dn / (phase[2] * 1e-3) / 1e12, 1)},
+        "gpu_launches_per_step": 5,
+    }
 
 
 # ------------------------------------------------------------------ reference (CPU)

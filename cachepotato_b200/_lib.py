@@ -25,6 +25,7 @@ EXPORTS = [
     "cpg_moe_check", "cpg_moe_forward_noalloc",
     "cpg_ctx_create", "cpg_ctx_destroy", "cpg_ctx_stream", "cpg_run_moe_layers",
     "cpg_ctx_run", "cpg_ctx_x", "cpg_ctx_topk", "cpg_ctx_profile", "cpg_ctx_phase_ms",
+    "cpg_moe_apply_workspace_bytes", "cpg_moe_apply", "cpg_moe_apply_check", "cpg_moe_apply_profile",
 ]
 
 
@@ -82,6 +83,10 @@ _SIGS = {
     "cpg_ctx_stream": (_vp, [_vp]),
     "cpg_run_moe_layers": (_i, [_vp, ctypes.POINTER(_vp), _i, _vp, _i, _vp]),
     "cpg_ctx_run": (_i, [_vp, ctypes.POINTER(_vp), _i, _i]),
+    "cpg_moe_apply_workspace_bytes": (_sz, [_vp, _i]),
+    "cpg_moe_apply": (_i, [_vp, _vp, _i, _vp, _vp, _vp, _vp, _sz, _vp]),
+    "cpg_moe_apply_check": (_i, [_vp, _vp]),
+    "cpg_moe_apply_profile": (_i, [_vp, _vp, _i, _vp, _vp, _vp, _vp, _sz, _vp, ctypes.POINTER(ctypes.c_float)]),
     "cpg_ctx_x": (_vp, [_vp]),
     "cpg_ctx_topk": (_vp, [_vp]),
     "cpg_ctx_profile": (_i, [_vp, _i]),

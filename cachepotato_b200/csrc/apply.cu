@@ -1,0 +1,251 @@
+// apply.cu — experts applied to externally routed tokens (prefill, expert-parallel receive side):
+// the expert loop of engine/blocks/qwen3_moe.c:199-222 with the routing given by the caller.
+//
+//   k_apply_prep   xn f32 -> fp16 rows, validate ids, per-block expert histogram
+//   k_apply_group  deterministic token sort: pairs grouped by expert, tokens ascending, plus the
+//                  active-expert table the GEMMs schedule from
+//   k_gemm_tc<0>   gate/up grouped GEMM on tcgen05, h = silu(g)·u
+//   k_gemm_tc<1>   down grouped GEMM on tcgen05, y per (token, slot)
+//   k_combine      mlp += sum_j wt_j·y_j in selection order
+#include "gemm_tc.cuh"
+
+namespace cpg {
+
+int layer_dims(const cpg_moe_layer *L, int *D, int *F, int *E, int *K);
+int layer_ptrs(const cpg_moe_layer *L, const uint8_t *const **ptrs, int *enc);
+__global__ void k_combine(const float *__restrict__ x, const float *__restrict__ attn, int T, int D, int K,
+                          const float *__restrict__ wt, const float *__restrict__ y, float *mlp, float *x_out);
+
+constexpr int AP_BLOCK = 256;            // tokens per grouping block
+constexpr int AP_MAX_E = 256;
+constexpr int TC_BN_TOK = 128;           // token tile of the tcgen05 GEMM
+
+struct ApplyWs {
+    size_t status, n_active, act, act_ptr, blk_cnt, pairs, xh, h, y, total;
+};
+
+static size_t al(size_t v) { return (v + 255) / 256 * 256; }
+
+static ApplyWs apply_layout(int D, int F, int E, int K, int T) {
+    ApplyWs w{};
+    size_t o = 0;
+    const int nblk = (T + AP_BLOCK - 1) / AP_BLOCK;
+    w.status = o; o = al(o + 16 * sizeof(int));
+    w.n_active = o; o = al(o + sizeof(int));
+    w.act = o; o = al(o + sizeof(int4) * (E + 1));
+    w.act_ptr = o; o = al(o + sizeof(void *) * 3 * E);
+    w.blk_cnt = o; o = al(o + sizeof(int) * (size_t)nblk * E);
+    w.pairs = o; o = al(o + sizeof(int) * (size_t)T * K);
+    w.xh = o; o = al(o + sizeof(__half) * (size_t)T * D);
+    w.h = o; o = al(o + sizeof(__half) * (size_t)T * K * F);
+    w.y = o; o = al(o + sizeof(float) * (size_t)T * K * D);
+    w.total = o;
+    return w;
+}
+
+// xn -> fp16 (row-major), per-block expert counts, id validation
+__global__ void __launch_bounds__(AP_BLOCK) k_apply_prep(const float *__restrict__ xn, int T, int D, int E, int K,
+                                                          const int *__restrict__ idx, __half *__restrict__ xh,
+                                                          int *__restrict__ blk_cnt, int *status) {
+    __shared__ int s_cnt[AP_MAX_E];
+    const int b = blockIdx.x, t0 = b * AP_BLOCK;
+    for (int e = threadIdx.x; e < E; e += blockDim.x) s_cnt[e] = 0;
+    if (b == 0 && threadIdx.x < 16) status[threadIdx.x] = 0;
+    __syncthreads();
+    const int nt = min(AP_BLOCK, T - t0);
+    for (int i = threadIdx.x; i < nt * K; i += blockDim.x) {
+        const int e = idx[(size_t)t0 * K + i];
+        if (e >= 0 && e < E) atomicAdd(&s_cnt[e], 1);
+        else atomicExch(status, ST_BAD_ITEM);
+    }
+    // fp16 copy of this block's rows
+    const float4 *src = reinterpret_cast<const float4 *>(xn + (size_t)t0 * D);
+    uint2 *dst = reinterpret_cast<uint2 *>(xh + (size_t)t0 * D);
+    for (int i = threadIdx.x; i < nt * D / 4; i += blockDim.x) {
+        const float4 v = src[i];
+        const __half2 lo = __floats2half2_rn(v.x, v.y), hi = __floats2half2_rn(v.z, v.w);
+        dst[i] = make_uint2(*reinterpret_cast<const uint32_t *>(&lo), *reinterpret_cast<const uint32_t *>(&hi));
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < E; e += blockDim.x) blk_cnt[(size_t)b * E + e] = s_cnt[e];
+}
+
+// Deterministic counting sort of the (token, slot) pairs by expert. Block b places its pairs at
+// off[e] + (pairs of e in blocks < b) + (pairs of e from earlier tokens of block b).
+__global__ void __launch_bounds__(AP_BLOCK) k_apply_group(int T, int E, int K, const int *__restrict__ idx,
+                                                           const int *__restrict__ blk_cnt, int nblk,
+                                                           const uint8_t *const *ptrs, int *pairs, int4 *act,
+                                                           const uint8_t **act_ptr, int *n_active, float *y, int D) {
+    __shared__ int s_base[AP_MAX_E], s_tot[AP_MAX_E], s_off[AP_MAX_E];
+    __shared__ uint32_t s_mask[AP_MAX_E];
+    const int b = blockIdx.x, t0 = b * AP_BLOCK, tid = threadIdx.x;
+    for (int e = tid; e < E; e += blockDim.x) {
+        int before = 0, tot = 0;
+        for (int c = 0; c < nblk; ++c) {
+            const int v = blk_cnt[(size_t)c * E + e];
+            before += c < b ? v : 0;
+            tot += v;
+        }
+        s_base[e] = before;
+        s_tot[e] = tot;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        int o = 0;
+        for (int e = 0; e < E; ++e) { s_off[e] = o; o += s_tot[e]; }
+    }
+    __syncthreads();
+    if (b == 0 && tid == 0) {               // active-expert table (ascending expert id)
+        int u = 0;
+        for (int e = 0; e < E; ++e) {
+            if (s_tot[e] > 0) {
+                act[u] = make_int4(e, s_off[e], s_tot[e], 0);
+                act_ptr[3 * u + 0] = ptrs[3 * e + 0];
+                act_ptr[3 * u + 1] = ptrs[3 * e + 1];
+                act_ptr[3 * u + 2] = ptrs[3 * e + 2];
+                ++u;
+            }
+        }
+        act[u] = make_int4(-1, s_off[E - 1] + s_tot[E - 1], 0, 0);
+        *n_active = u;
+    }
+    const int nt = min(AP_BLOCK, T - t0);
+    for (int c0 = 0; c0 < nt; c0 += 32) {
+        for (int e = tid; e < E; e += blockDim.x) s_mask[e] = 0;
+        __syncthreads();
+        for (int i = tid; i < 32 * K; i += blockDim.x) {
+            const int tl = i / K, t = t0 + c0 + tl;
+            if (c0 + tl < nt) {
+                const int e = idx[(size_t)t * K + i % K];
+                if (e >= 0 && e < E) atomicOr(&s_mask[e], 1u << tl);
+            }
+        }
+        __syncthreads();
+        for (int i = tid; i < 32 * K; i += blockDim.x) {
+            const int tl = i / K, j = i % K, t = t0 + c0 + tl;
+            if (c0 + tl < nt) {
+                const int slot = t * K + j;
+                const int e = idx[slot];
+                if (e >= 0 && e < E) {
+                    const int r = s_base[e] + __popc(s_mask[e] & ((1u << tl) - 1u));
+                    pairs[s_off[e] + r] = slot;
+                } else {
+                    for (int k = 0; k < D; ++k) y[(size_t)slot * D + k] = 0.0f;   // contributes nothing
+                }
+            }
+        }
+        __syncthreads();
+        for (int e = tid; e < E; e += blockDim.x) s_base[e] += __popc(s_mask[e]);
+        __syncthreads();
+    }
+}
+
+}  // namespace cpg
+
+using namespace cpg;
+
+extern "C" size_t cpg_moe_apply_workspace_bytes(const cpg_moe_layer *layer, int max_T) {
+    int D, F, E, K;
+    if (!layer || max_T <= 0 || layer_dims(layer, &D, &F, &E, &K) != CPG_OK) return 0;
+    return apply_layout(D, F, E, K, max_T).total;
+}
+
+// ev: null, or 5 events recorded around the sort, gate/up, down and combine phases
+static int apply_impl(const cpg_moe_layer *layer, const float *xn, int T, const int *topk_idx, const float *wt,
+                      float *mlp, void *ws, size_t ws_bytes, cudaStream_t s, cudaEvent_t *ev) {
+    CPG_REQUIRE(layer && xn && topk_idx && wt && mlp && ws, "cpg_moe_apply: null argument");
+    CPG_REQUIRE(T > 0, "cpg_moe_apply: T=%d", T);
+    int D, F, E, K, enc;
+    const uint8_t *const *ptrs;
+    int rc = layer_dims(layer, &D, &F, &E, &K);
+    if (rc == CPG_OK) rc = layer_ptrs(layer, &ptrs, &enc);
+    if (rc) return rc;
+    CPG_REQUIRE(enc == CPG_ENC_Q4, "cpg_moe_apply: the tcgen05 grouped GEMM takes Q4_0 experts");
+    CPG_REQUIRE(E <= AP_MAX_E, "cpg_moe_apply: n_experts=%d > %d", E, AP_MAX_E);
+    CPG_REQUIRE(F % 128 == 0 && D % 256 == 0, "cpg_moe_apply: d_exp %% 128 and d_model %% 256 must be 0");
+    const ApplyWs W = apply_layout(D, F, E, K, T);
+    CPG_REQUIRE(ws_bytes >= W.total, "cpg_moe_apply: workspace %zu < %zu bytes for T=%d", ws_bytes, W.total, T);
+    CPG_REQUIRE((((uintptr_t)xn | (uintptr_t)mlp | (uintptr_t)ws) & 15) == 0, "cpg_moe_apply: 16-byte alignment");
+    uint8_t *w = (uint8_t *)ws;
+    int *status = (int *)(w + W.status);
+    const int nblk = (T + AP_BLOCK - 1) / AP_BLOCK;
+    if (ev) CPG_CUDA(cudaEventRecord(ev[0], s));
+    k_apply_prep<<<nblk, AP_BLOCK, 0, s>>>(xn, T, D, E, K, topk_idx, (__half *)(w + W.xh), (int *)(w + W.blk_cnt), status);
+    CPG_CUDA(cudaGetLastError());
+    k_apply_group<<<nblk, AP_BLOCK, 0, s>>>(T, E, K, topk_idx, (const int *)(w + W.blk_cnt), nblk, ptrs,
+                                            (int *)(w + W.pairs), (int4 *)(w + W.act), (const uint8_t **)(w + W.act_ptr),
+                                            (int *)(w + W.n_active), (float *)(w + W.y), D);
+    CPG_CUDA(cudaGetLastError());
+    TcArgs a{};
+    a.n_active = (const int *)(w + W.n_active);
+    a.act = (const int4 *)(w + W.act);
+    a.act_ptr = (const uint8_t *const *)(w + W.act_ptr);
+    a.pairs = (const int *)(w + W.pairs);
+    a.D = D; a.F = F; a.K = K;
+    a.status = status;
+    const int max_tok_tiles = (T * K + TC_BN_TOK - 1) / TC_BN_TOK + (E < T * K ? E : T * K);
+    a.bsrc = (const __half *)(w + W.xh);
+    a.h_out = (__half *)(w + W.h);
+    if (ev) CPG_CUDA(cudaEventRecord(ev[1], s));
+    rc = gemm_tc_launch(0, a, max_tok_tiles * (F / 128), s);
+    if (rc) return rc;
+    a.bsrc = (const __half *)(w + W.h);
+    a.y_out = (float *)(w + W.y);
+    if (ev) CPG_CUDA(cudaEventRecord(ev[2], s));
+    rc = gemm_tc_launch(1, a, max_tok_tiles * (D / 256), s);
+    if (rc) return rc;
+    if (ev) CPG_CUDA(cudaEventRecord(ev[3], s));
+    const int n4 = T * D / 4;
+    int cgrid = (n4 + 255) / 256;
+    if (cgrid > sm_count() * 8) cgrid = sm_count() * 8;
+    k_combine<<<cgrid, 256, 0, s>>>(nullptr, nullptr, T, D, K, wt, (const float *)(w + W.y), mlp, nullptr);
+    CPG_CUDA(cudaGetLastError());
+    if (ev) CPG_CUDA(cudaEventRecord(ev[4], s));
+    return CPG_OK;
+}
+
+extern "C" int cpg_moe_apply(const cpg_moe_layer *layer, const float *xn, int T, const int *topk_idx,
+                             const float *wt, float *mlp, void *ws, size_t ws_bytes, void *stream) {
+    return apply_impl(layer, xn, T, topk_idx, wt, mlp, ws, ws_bytes, (cudaStream_t)stream, nullptr);
+}
+
+extern "C" int cpg_moe_apply_profile(const cpg_moe_layer *layer, const float *xn, int T, const int *topk_idx,
+                                     const float *wt, float *mlp, void *ws, size_t ws_bytes, void *stream,
+                                     float *phase_ms) {
+    CPG_REQUIRE(phase_ms, "cpg_moe_apply_profile: null phase_ms");
+    cudaEvent_t ev[5] = {};
+    for (int i = 0; i < 5; ++i) {
+        const cudaError_t ce = cudaEventCreate(&ev[i]);
+        if (ce != cudaSuccess) {
+            for (int j = 0; j < i; ++j) cudaEventDestroy(ev[j]);
+            return cuda_fail(ce, "cpg_moe_apply_profile: event");
+        }
+    }
+    int rc = apply_impl(layer, xn, T, topk_idx, wt, mlp, ws, ws_bytes, (cudaStream_t)stream, ev);
+    if (rc == CPG_OK) {
+        const cudaError_t ce = cudaEventSynchronize(ev[4]);
+        if (ce != cudaSuccess) rc = cuda_fail(ce, "cpg_moe_apply_profile: synchronize");
+        for (int i = 0; rc == CPG_OK && i < 4; ++i) {
+            const cudaError_t e2 = cudaEventElapsedTime(&phase_ms[i], ev[i], ev[i + 1]);
+            if (e2 != cudaSuccess) rc = cuda_fail(e2, "cpg_moe_apply_profile: elapsed time");
+        }
+    }
+    for (int i = 0; i < 5; ++i) cudaEventDestroy(ev[i]);
+    return rc;
+}
+
+extern "C" int cpg_moe_apply_check(const void *ws, void *stream) {
+    CPG_REQUIRE(ws, "cpg_moe_apply_check: null workspace");
+    int st = 0;
+    CPG_CUDA(cudaStreamSynchronize((cudaStream_t)stream));
+    CPG_CUDA(cudaMemcpy(&st, ws, sizeof(int), cudaMemcpyDeviceToHost));
+    if (st == ST_BAD_ITEM) {
+        set_error("cpg_moe_apply: expert id outside [0, n_experts) (those slots contributed zero)");
+        return CPG_EINVAL;
+    }
+    if (st != ST_OK) {
+        set_error("device-side wait timed out (status %d)", st);
+        return CPG_ETIMEOUT;
+    }
+    return CPG_OK;
+}

@@ -800,6 +800,12 @@ int layer_dims(const cpg_moe_layer *L, int *D, int *F, int *E, int *K) {
     *D = L->D; *F = L->F; *E = L->E; *K = L->K;
     return CPG_OK;
 }
+int layer_ptrs(const cpg_moe_layer *L, const uint8_t *const **ptrs, int *enc) {
+    CPG_REQUIRE(L, "null layer");
+    *ptrs = L->d_ptrs;
+    *enc = L->enc;
+    return CPG_OK;
+}
 }  // namespace cpg
 
 using namespace cpg;

@@ -186,6 +186,34 @@ class MoELayer:
         return MoEOutputs(mlp, x_out, router, topk, wt)
 
 
+def moe_apply(layer: "MoELayer", xn, topk_idx, wt, *, ws=None, mlp=None, stream=None, check_status=True,
+              phase_ms=None):
+    """Routed experts on the tensor cores (prefill): mlp += sum_j wt[t,j] * expert_j(xn[t]).
+    phase_ms: optional list, receives [sort, gate_up, down, combine] in ms (synchronising)."""
+    torch = _torch()
+    xn = xn.contiguous()
+    T = xn.shape[0]
+    idx = topk_idx.to(torch.int32).contiguous()
+    wt = wt.to(torch.float32).contiguous()
+    if ws is None:
+        ws = torch.empty(int(lib().cpg_moe_apply_workspace_bytes(layer.handle, T)), dtype=torch.uint8,
+                         device=xn.device)
+    if mlp is None:
+        mlp = torch.zeros((T, layer.d_model), dtype=torch.float32, device=xn.device)
+    sp = _stream_ptr(stream)
+    if phase_ms is None:
+        check(lib().cpg_moe_apply(layer.handle, xn.data_ptr(), T, idx.data_ptr(), wt.data_ptr(), mlp.data_ptr(),
+                                  ws.data_ptr(), ws.numel(), sp))
+    else:
+        ph = (ctypes.c_float * 4)()
+        check(lib().cpg_moe_apply_profile(layer.handle, xn.data_ptr(), T, idx.data_ptr(), wt.data_ptr(),
+                                          mlp.data_ptr(), ws.data_ptr(), ws.numel(), sp, ph))
+        phase_ms[:] = list(ph)
+    if check_status:
+        check(lib().cpg_moe_apply_check(ws.data_ptr(), sp))
+    return mlp
+
+
 class DecodeContext:
     """cpg_ctx: the host-buffer decode loop (run_layers' MoE half, cachepotato.c:149-166)."""
 

@@ -51,6 +51,22 @@ def calibrate_router_scales(z: np.ndarray, K: int, s: float, seed: int, iters: i
     return best.astype(np.float32)
 
 
+def zipf_assignment(T: int, E: int, K: int, s: float, q: float, seed: int):
+    """Prefill routing drawn directly (no router): K distinct experts per token by Gumbel-top-k
+    over Zipf-Mandelbrot popularities p_r ∝ (r + q)^-s with the ranks shuffled over expert ids;
+    weights = softmax of the drawn scores renormalised over the chosen K. With T=4096, E=128,
+    K=8, s=1.2, q=20 the expert groups hold roughly 90-900 tokens."""
+    rng = np.random.default_rng(seed)
+    logp = -s * np.log(np.arange(1, E + 1) + q)
+    perm = rng.permutation(E)
+    g = logp[None, :] + rng.gumbel(size=(T, E))
+    top = np.argsort(-g, axis=1)[:, :K]
+    sc = np.take_along_axis(g, top, 1)
+    w = np.exp(sc - sc.max(1, keepdims=True))
+    w = (w / w.sum(1, keepdims=True)).astype(np.float32)
+    return perm[top].astype(np.int32), w
+
+
 def load_stats(topk: np.ndarray, E: int) -> dict:
     """Realised per-expert load of topk ids (any shape) -> summary used in reports."""
     c = np.bincount(np.asarray(topk).ravel(), minlength=E)

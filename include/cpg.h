@@ -132,17 +132,37 @@ int cpg_moe_check(const void *ws, void *stream);
 
 /* cpg_moe_forward without a caller workspace, for callers that cannot allocate device memory
  * where they run the block (an engine whose host program owns all device memory through its
- * own pool, a stream being captured into a CUDA graph in global capture mode, a decode loop
- * that may not stall on the allocator). No counterpart in the reference (its CPU engine mallocs
+ * own pool, a decode loop that may not stall on the allocator). No counterpart in the reference (its CPU engine mallocs
  * scratch per call, qwen3_moe.c:98-108). Scratch comes from a fixed 8 MiB array in the
  * library's device image (enough for 64 tokens of a Qwen3-30B-A3B layer); larger T is rejected
  * with CPG_EINVAL. Allocates nothing. The first call on a device looks up the array's address
- * (make it before any stream capture). All calls share the array: calls that overlap on the
+ * once. All calls share the array: calls that overlap on the
  * GPU race, so serialise them (one stream, or events). Device-side timeouts are recorded in the
  * array and not reported here; use cpg_moe_forward + cpg_moe_check when they must be read. */
 int cpg_moe_forward_noalloc(const cpg_moe_layer *layer, const float *x, const float *attn, int T,
                             float *mlp, float *x_out, int *topk_idx, float *wt, float *router,
                             void *stream);
+
+/* ============================================================== prefill: routed experts
+ * The expert loop of qwen3_moe.c:199-222 with the routing supplied by the caller (prefill
+ * batches whose token->expert assignment is drawn directly, the receive side of expert
+ * parallelism): for every token t and slot j, mlp[t] += wt[t,j] · Wd·(silu(Wg·xn[t]) · (Wu·xn[t]))
+ * with e = topk_idx[t,j], slots added in order j = 0..topk-1. xn (T,d_model) f32 device, already
+ * normalised; topk_idx (T,topk) int; wt (T,topk) f32; mlp (T,d_model) accumulated. Tokens are
+ * sorted by expert (deterministically, tokens ascending) and each expert's tokens run through a
+ * grouped GEMM on the tcgen05 tensor cores: Q4_0 weights decoded to fp16 (q·d rounded once),
+ * fp16 activations, fp32 accumulation in tensor memory. Q4_0 experts; d_exp % 128 == 0. */
+size_t cpg_moe_apply_workspace_bytes(const cpg_moe_layer *layer, int max_T);
+int cpg_moe_apply(const cpg_moe_layer *layer, const float *xn, int T, const int *topk_idx,
+                  const float *wt, float *mlp, void *ws, size_t ws_bytes, void *stream);
+/* Synchronise; CPG_EINVAL if an expert id was outside [0, n_experts) (those slots contributed
+   zero), CPG_ETIMEOUT if a bounded device wait gave up. */
+int cpg_moe_apply_check(const void *ws, void *stream);
+/* cpg_moe_apply with CUDA events around its phases; synchronises and writes phase_ms[4]:
+   token sort, gate/up GEMM, down GEMM, combine (milliseconds). */
+int cpg_moe_apply_profile(const cpg_moe_layer *layer, const float *xn, int T, const int *topk_idx,
+                          const float *wt, float *mlp, void *ws, size_t ws_bytes, void *stream,
+                          float *phase_ms);
 
 /* ============================================================== decode loop (host buffers)
  * A context owns a stream, a workspace and device activation buffers on one device. */

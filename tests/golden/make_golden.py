@@ -54,7 +54,7 @@ MATVEC_CASES = [
     ("q8_small", O.ENC_Q8, 64, 40, 37),
     ("f32_router", O.ENC_F32, 2048, 128, 38),
 ]
-APPLY_CASE = ("apply_q4", 256, 64, 16, 4, O.ENC_Q4, 5, 41)
+APPLY_CASE = ("apply_q4", 256, 256, 16, 4, O.ENC_Q4, 40, 41)
 
 
 def moe_inputs(d_model, T, seed, orc):
