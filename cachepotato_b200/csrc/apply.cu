@@ -1,9 +1,10 @@
 // apply.cu — experts applied to externally routed tokens (prefill, expert-parallel receive side):
 // the expert loop of engine/blocks/qwen3_moe.c:199-222 with the routing given by the caller.
 //
-//   k_apply_prep   xn f32 -> fp16 rows, validate ids, per-block expert histogram
+//   k_apply_prep   validate ids, per-block expert histogram
 //   k_apply_group  deterministic token sort: pairs grouped by expert, tokens ascending, plus the
 //                  active-expert table the GEMMs schedule from
+//   k_apply_gather the token rows in that order as fp16 (the gate/up GEMM's tensor-TMA source)
 //   k_gemm_tc<0>   gate/up grouped GEMM on tcgen05, h = silu(g)·u
 //   k_gemm_tc<1>   down grouped GEMM on tcgen05, y per (token, slot)
 //   k_combine      mlp += sum_j wt_j·y_j in selection order
@@ -13,6 +14,7 @@ namespace cpg {
 
 int layer_dims(const cpg_moe_layer *L, int *D, int *F, int *E, int *K);
 int layer_ptrs(const cpg_moe_layer *L, const uint8_t *const **ptrs, int *enc);
+int layer_weight_maps(const cpg_moe_layer *L, const void **maps);
 __global__ void k_combine(const float *__restrict__ x, const float *__restrict__ attn, int T, int D, int K,
                           const float *__restrict__ wt, const float *__restrict__ y, float *mlp, float *x_out);
 
@@ -21,7 +23,7 @@ constexpr int AP_MAX_E = 256;
 constexpr int TC_BN_TOK = 128;           // token tile of the tcgen05 GEMM
 
 struct ApplyWs {
-    size_t status, n_active, act, act_ptr, blk_cnt, pairs, xh, h, y, total;
+    size_t status, n_active, act, act_ptr, blk_cnt, pairs, xs, h, y, total;
 };
 
 static size_t al(size_t v) { return (v + 255) / 256 * 256; }
@@ -36,16 +38,15 @@ static ApplyWs apply_layout(int D, int F, int E, int K, int T) {
     w.act_ptr = o; o = al(o + sizeof(void *) * 3 * E);
     w.blk_cnt = o; o = al(o + sizeof(int) * (size_t)nblk * E);
     w.pairs = o; o = al(o + sizeof(int) * (size_t)T * K);
-    w.xh = o; o = al(o + sizeof(__half) * (size_t)T * D);
+    w.xs = o; o = al(o + sizeof(__half) * (size_t)T * K * D);
     w.h = o; o = al(o + sizeof(__half) * (size_t)T * K * F);
     w.y = o; o = al(o + sizeof(float) * (size_t)T * K * D);
     w.total = o;
     return w;
 }
 
-// xn -> fp16 (row-major), per-block expert counts, id validation
-__global__ void __launch_bounds__(AP_BLOCK) k_apply_prep(const float *__restrict__ xn, int T, int D, int E, int K,
-                                                          const int *__restrict__ idx, __half *__restrict__ xh,
+// per-block expert counts, id validation
+__global__ void __launch_bounds__(AP_BLOCK) k_apply_prep(int T, int E, int K, const int *__restrict__ idx,
                                                           int *__restrict__ blk_cnt, int *status) {
     __shared__ int s_cnt[AP_MAX_E];
     const int b = blockIdx.x, t0 = b * AP_BLOCK;
@@ -57,14 +58,6 @@ __global__ void __launch_bounds__(AP_BLOCK) k_apply_prep(const float *__restrict
         const int e = idx[(size_t)t0 * K + i];
         if (e >= 0 && e < E) atomicAdd(&s_cnt[e], 1);
         else atomicExch(status, ST_BAD_ITEM);
-    }
-    // fp16 copy of this block's rows
-    const float4 *src = reinterpret_cast<const float4 *>(xn + (size_t)t0 * D);
-    uint2 *dst = reinterpret_cast<uint2 *>(xh + (size_t)t0 * D);
-    for (int i = threadIdx.x; i < nt * D / 4; i += blockDim.x) {
-        const float4 v = src[i];
-        const __half2 lo = __floats2half2_rn(v.x, v.y), hi = __floats2half2_rn(v.z, v.w);
-        dst[i] = make_uint2(*reinterpret_cast<const uint32_t *>(&lo), *reinterpret_cast<const uint32_t *>(&hi));
     }
     __syncthreads();
     for (int e = threadIdx.x; e < E; e += blockDim.x) blk_cnt[(size_t)b * E + e] = s_cnt[e];
@@ -140,6 +133,27 @@ __global__ void __launch_bounds__(AP_BLOCK) k_apply_group(int T, int E, int K, c
     }
 }
 
+// xs[p] = fp16(xn[token of pair p]) for the valid pairs (one warp per row, 8 values per lane step)
+__global__ void __launch_bounds__(256) k_apply_gather(const float *__restrict__ xn, int D, int K,
+                                                       const int *__restrict__ pairs, const int4 *__restrict__ act,
+                                                       const int *__restrict__ n_active, __half *__restrict__ xs,
+                                                       int max_pairs) {
+    const int n_valid = act[*n_active].y;
+    const int lane = threadIdx.x & 31;
+    for (int p = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; p < n_valid && p < max_pairs;
+         p += (gridDim.x * blockDim.x) >> 5) {
+        const float4 *src = reinterpret_cast<const float4 *>(xn + (size_t)(pairs[p] / K) * D);
+        uint4 *dst = reinterpret_cast<uint4 *>(xs + (size_t)p * D);
+        for (int i = lane; i < D / 8; i += 32) {
+            const float4 a = src[2 * i], b = src[2 * i + 1];
+            const __half2 h0 = __floats2half2_rn(a.x, a.y), h1 = __floats2half2_rn(a.z, a.w);
+            const __half2 h2 = __floats2half2_rn(b.x, b.y), h3 = __floats2half2_rn(b.z, b.w);
+            dst[i] = make_uint4(*reinterpret_cast<const uint32_t *>(&h0), *reinterpret_cast<const uint32_t *>(&h1),
+                                *reinterpret_cast<const uint32_t *>(&h2), *reinterpret_cast<const uint32_t *>(&h3));
+        }
+    }
+}
+
 }  // namespace cpg
 
 using namespace cpg;
@@ -162,7 +176,7 @@ static int apply_impl(const cpg_moe_layer *layer, const float *xn, int T, const 
     if (rc) return rc;
     CPG_REQUIRE(enc == CPG_ENC_Q4, "cpg_moe_apply: the tcgen05 grouped GEMM takes Q4_0 experts");
     CPG_REQUIRE(E <= AP_MAX_E, "cpg_moe_apply: n_experts=%d > %d", E, AP_MAX_E);
-    CPG_REQUIRE(F % 128 == 0 && D % 256 == 0, "cpg_moe_apply: d_exp %% 128 and d_model %% 256 must be 0");
+    CPG_REQUIRE(F % 256 == 0 && D % 256 == 0, "cpg_moe_apply: d_exp %% 256 and d_model %% 256 must be 0");
     const ApplyWs W = apply_layout(D, F, E, K, T);
     CPG_REQUIRE(ws_bytes >= W.total, "cpg_moe_apply: workspace %zu < %zu bytes for T=%d", ws_bytes, W.total, T);
     CPG_REQUIRE((((uintptr_t)xn | (uintptr_t)mlp | (uintptr_t)ws) & 15) == 0, "cpg_moe_apply: 16-byte alignment");
@@ -170,29 +184,36 @@ static int apply_impl(const cpg_moe_layer *layer, const float *xn, int T, const 
     int *status = (int *)(w + W.status);
     const int nblk = (T + AP_BLOCK - 1) / AP_BLOCK;
     if (ev) CPG_CUDA(cudaEventRecord(ev[0], s));
-    k_apply_prep<<<nblk, AP_BLOCK, 0, s>>>(xn, T, D, E, K, topk_idx, (__half *)(w + W.xh), (int *)(w + W.blk_cnt), status);
+    k_apply_prep<<<nblk, AP_BLOCK, 0, s>>>(T, E, K, topk_idx, (int *)(w + W.blk_cnt), status);
     CPG_CUDA(cudaGetLastError());
     k_apply_group<<<nblk, AP_BLOCK, 0, s>>>(T, E, K, topk_idx, (const int *)(w + W.blk_cnt), nblk, ptrs,
                                             (int *)(w + W.pairs), (int4 *)(w + W.act), (const uint8_t **)(w + W.act_ptr),
                                             (int *)(w + W.n_active), (float *)(w + W.y), D);
     CPG_CUDA(cudaGetLastError());
+    {
+        const int P = T * K;
+        int ggrid = (P + 7) / 8;
+        if (ggrid > sm_count() * 8) ggrid = sm_count() * 8;
+        k_apply_gather<<<ggrid, 256, 0, s>>>(xn, D, K, (const int *)(w + W.pairs), (const int4 *)(w + W.act),
+                                             (const int *)(w + W.n_active), (__half *)(w + W.xs), P);
+        CPG_CUDA(cudaGetLastError());
+    }
     TcArgs a{};
     a.n_active = (const int *)(w + W.n_active);
     a.act = (const int4 *)(w + W.act);
-    a.act_ptr = (const uint8_t *const *)(w + W.act_ptr);
+    rc = layer_weight_maps(layer, &a.wmaps);
+    if (rc) return rc;
     a.pairs = (const int *)(w + W.pairs);
     a.D = D; a.F = F; a.K = K;
     a.status = status;
     const int max_tok_tiles = (T * K + TC_BN_TOK - 1) / TC_BN_TOK + (E < T * K ? E : T * K);
-    a.bsrc = (const __half *)(w + W.xh);
     a.h_out = (__half *)(w + W.h);
-    if (ev) CPG_CUDA(cudaEventRecord(ev[1], s));
-    rc = gemm_tc_launch(0, a, max_tok_tiles * (F / 128), s);
-    if (rc) return rc;
-    a.bsrc = (const __half *)(w + W.h);
     a.y_out = (float *)(w + W.y);
+    if (ev) CPG_CUDA(cudaEventRecord(ev[1], s));
+    rc = gemm_tc_launch(0, a, (const __half *)(w + W.xs), T * K, max_tok_tiles * (F / 128), s);
+    if (rc) return rc;
     if (ev) CPG_CUDA(cudaEventRecord(ev[2], s));
-    rc = gemm_tc_launch(1, a, max_tok_tiles * (D / 256), s);
+    rc = gemm_tc_launch(1, a, (const __half *)(w + W.h), T * K, max_tok_tiles * (D / 256), s);
     if (rc) return rc;
     if (ev) CPG_CUDA(cudaEventRecord(ev[3], s));
     const int n4 = T * D / 4;

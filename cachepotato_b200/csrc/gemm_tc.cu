@@ -2,16 +2,26 @@
 // other large batches where each expert sees many tokens.
 //
 // Per tile: 256 weight rows (gate 128 + up 128 of one expert, or 256 rows of its down matrix) ×
-// 128 tokens of that expert, K streamed 64 values per stage. Eight math warps decode Q4_0
-// groups straight from the v4 rows in global memory into fp16 (q·d rounded once to fp16) in
-// shared memory, in the K-major no-swizzle canonical layout the tensor core reads, and stage the
-// tokens' fp16 activation rows beside them. One thread issues tcgen05.mma (M=128, N=128, K=16,
-// fp16 × fp16 → fp32 in TMEM) twice per K step, one per 128-row half, and commits each stage to
-// an mbarrier that frees it. The epilogue reads the accumulators with tcgen05.ld:
-//   gate/up: h = silu(g)·u (engine/blocks/qwen3_moe.c:217-219), fp16, one row per (token, slot);
-//   down:    y per (token, slot) in fp32, combined in selection order by k_combine.
-// Every mbarrier wait is bounded; a timeout records a status code and all roles leave together.
+// 128 tokens of that expert, K streamed 64 values per stage. Roles (one CTA per SM):
+//   warp 0      owns the TMEM allocation; one thread loads raw Q4_0 rows into a two-slot
+//               shared-memory ring with 2D tensor TMA boxes of 128 rows × 144 bytes (four stages
+//               of K) over each expert matrix: two requests per group, where one small copy per
+//               row queued 256 requests on the copy engine and starved the tensor core
+//   warp 1      one thread issues tcgen05.mma (M=128, N=128, K=16, fp16 × fp16 → fp32 in TMEM),
+//               twice per K step (one per 128-row half), and commits each stage to the mbarrier
+//               that frees it
+//   warp 2      one thread loads the token tile of each stage with a 2D tensor TMA (128-byte
+//               swizzle) from the expert-sorted fp16 activation rows
+//   warps 3-10  decode each raw row from shared memory into fp16 (q·d rounded once) in the
+//               K-major no-swizzle canonical layout, then run the epilogue from TMEM:
+//                 gate/up: h = silu(g)·u (engine/blocks/qwen3_moe.c:217-219), fp16 per pair
+//                 down:    y per (token, slot) in fp32, combined in selection order by k_combine
+// Every mbarrier wait is bounded; a timeout records a status code, all roles leave together, and
+// the copy engines' last transfers are waited for (bounded) before the CTA exits.
+#include <cuda.h>
 #include <math.h>
+
+#include <mutex>
 
 #include "gemm_tc.cuh"
 
@@ -21,25 +31,43 @@ constexpr int TC_BM = 128;                  // rows per MMA (one TMEM lane per r
 constexpr int TC_BN = 128;                  // tokens per tile (MMA N, TMEM columns per half)
 constexpr int TC_BK = 64;                   // K per stage (4 MMAs of K=16)
 constexpr int TC_STAGES = 3;
-constexpr int TC_MATH_WARPS = 8;
-constexpr int TC_THREADS = (2 + TC_MATH_WARPS) * 32;   // warp 0: TMEM owner, warp 1: MMA issuer
-constexpr int TC_A_BYTES = 2 * TC_BM * TC_BK * 2;      // 32 KB: two 128-row halves, fp16
-constexpr int TC_B_BYTES = TC_BN * TC_BK * 2;          // 16 KB
+constexpr int TC_ROWS = 2 * TC_BM;          // weight rows per tile
+constexpr int TC_GRP = 4;                   // K stages per raw group
+constexpr int TC_RAW_ROW = TC_GRP * 36;     // 144 bytes: four Q4_0 group pairs of one row
+constexpr int TC_RAW_BYTES = TC_ROWS * TC_RAW_ROW;                  // 36 KB per raw slot
+constexpr int TC_RAW_SLOTS = 2;
+constexpr int TC_A_BYTES = TC_ROWS * TC_BK * 2;                     // 32 KB: two 128-row halves
+constexpr int TC_B_BYTES = TC_BN * TC_BK * 2;                       // 16 KB
 constexpr int TC_STAGE_BYTES = TC_A_BYTES + TC_B_BYTES;
-constexpr int TC_SBO = (TC_BK / 8) * 128;              // bytes between 8-row core-matrix groups
-constexpr int TC_LBO = 128;                            // bytes between 8-column core matrices
-constexpr int TC_TMEM_COLS = 2 * TC_BN;                // two fp32 accumulators of 128 columns
+constexpr int TC_STAGE0 = TC_RAW_SLOTS * TC_RAW_BYTES;              // operand stages follow the raw ring
+constexpr int TC_SMEM = TC_STAGE0 + TC_STAGES * TC_STAGE_BYTES;     // 216 KB (+1 KB alignment slack)
+constexpr int TC_MATH_WARPS = 8;
+constexpr int TC_FIRST_MATH = 3;
+constexpr int TC_THREADS = (TC_FIRST_MATH + TC_MATH_WARPS) * 32;
+constexpr int TC_SBO = (TC_BK / 8) * 128;   // no-swizzle A: bytes between 8-row core-matrix groups
+constexpr int TC_LBO = 128;                 // no-swizzle A: bytes between 8-column core matrices
+constexpr int TC_TMEM_COLS = 2 * TC_BN;     // two fp32 accumulators of 128 columns
 constexpr int TC_MAX_E = 256;
+static_assert(TC_STAGE0 % 1024 == 0 && TC_STAGE_BYTES % 1024 == 0 && TC_A_BYTES % 1024 == 0,
+              "operand tiles must stay 1024-byte aligned");
 
-// ---------------------------------------------------------------- tcgen05 wrappers
+// ---------------------------------------------------------------- tcgen05 / TMA wrappers
+// SM100 shared-memory matrix descriptor, K-major, no swizzle: start, LBO, SBO in 16-byte units,
+// version 1 (bit 46), base offset 0, layout type 0.
 __device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
-    // SM100 shared-memory matrix descriptor, K-major, no swizzle: start, LBO, SBO in 16-byte
-    // units, version 1 (bit 46), base offset 0, layout type 0.
     return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
            ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);
 }
 
-// kind::f16 instruction descriptor: fp32 accumulate, fp16 A and B, both K-major, M=128, N.
+// K-major, 128-byte swizzle (the layout a SWIZZLE_128B tensor TMA writes): rows of 128 bytes,
+// 8-row groups 1024 bytes apart (SBO), LBO unused (1), layout type 2. Advancing K by 16 fp16
+// values inside the 128-byte row moves the start address by 32 bytes.
+__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
+    return (uint64_t)((saddr >> 4) & 0x3FFFu) | (1ull << 16) | ((uint64_t)(1024 >> 4) << 32) | (1ull << 46) |
+           (2ull << 61);
+}
+
+// kind::f16 instruction descriptor: fp32 accumulate, fp16 A and B, both K-major, M, N.
 __host__ __device__ constexpr uint32_t umma_idesc_f16(int M, int N) {
     return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
@@ -61,6 +89,14 @@ __device__ __forceinline__ void umma_commit(uint64_t *bar) {
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// 2D tensor TMA load (no multicast) of the box at (x, y) into shared memory, completing on bar.
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+        ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
 
 // 32 consecutive fp32 columns of this warp's 32 TMEM lanes.
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
@@ -89,15 +125,12 @@ __device__ __forceinline__ bool tc_wait(uint64_t *bar, uint32_t parity, volatile
     return false;
 }
 
-// Q4_0 group pair (36 bytes, 4-byte aligned) of one row -> 64 fp16 values q*d in K order,
-// as 8 chunks of 8 values (16 bytes each).
-__device__ __forceinline__ void q4_pair_to_f16(const uint32_t *src, uint4 (&out)[8]) {
-    uint32_t w[9];
-#pragma unroll
-    for (int i = 0; i < 9; ++i) w[i] = __ldg(src + i);
+// Q4_0 group pair (36 bytes as 9 words: scale d0 + 16 quant bytes, scale d1 + 16 quant bytes)
+// -> 64 fp16 values q*d in K order, as 8 chunks of 8 values (16 bytes each).
+__device__ __forceinline__ void q4_pair_to_f16(const uint32_t *w, uint4 (&out)[8]) {
     const uint32_t d0 = w[0] & 0xFFFFu, d1 = w[4] >> 16;
     const uint32_t s0 = d0 | (d0 << 16), s1 = d1 | (d1 << 16);
-    // quant bytes of group j: w0[2..3], w1..w3, w4[0..1]; of group j+1: w5..w8
+    // quant bytes of the first group: w0[2..3], w1..w3, w4[0..1]; of the second: w5..w8
     const uint32_t qa[4] = {__byte_perm(w[0], w[1], 0x5432), __byte_perm(w[1], w[2], 0x5432),
                             __byte_perm(w[2], w[3], 0x5432), __byte_perm(w[3], w[4], 0x5432)};
     const uint32_t qb[4] = {w[5], w[6], w[7], w[8]};
@@ -131,38 +164,45 @@ __device__ __forceinline__ void q4_pair_to_f16(const uint32_t *src, uint4 (&out)
     }
 }
 
-// canonical K-major no-swizzle offset of the 16-byte chunk (row r, chunk c) in a tile
+// canonical K-major no-swizzle offset of the 16-byte chunk (row r, chunk c) in a 128-row half
 __device__ __forceinline__ uint32_t canon_off(int r, int c) {
     return (uint32_t)((r >> 3) * TC_SBO + c * TC_LBO + (r & 7) * 16);
 }
 
 template <int KIND>
-__global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(TcArgs a) {
+__global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const TcArgs a, const __grid_constant__ CUtensorMap tmap_b) {
     // The runtime places dynamic shared memory after the static variables, 16-byte aligned only,
-    // so the operand tiles are moved up to the next 1024-byte boundary here (the launch adds the
-    // slack). The declaration states 16 so that the compiler cannot assume more and fold this away.
+    // so the tiles are moved up to the next 1024-byte boundary here (the launch adds the slack).
+    // The declaration states 16 so that the compiler cannot assume more and fold this away.
     extern __shared__ __align__(16) uint8_t smem_raw[];
     uint8_t *const smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-    __shared__ uint64_t full_bar[TC_STAGES], empty_bar[TC_STAGES], acc_full, acc_empty, drain_bar;
+    __shared__ uint64_t raw_full[TC_RAW_SLOTS], raw_empty[TC_RAW_SLOTS];
+    __shared__ uint64_t a_full[TC_STAGES], b_full[TC_STAGES], empty_bar[TC_STAGES];
+    __shared__ uint64_t acc_full, acc_empty, drain_bar;
     __shared__ uint32_t s_tmem;
     __shared__ int s_abort;
     __shared__ int4 s_act[TC_MAX_E + 1];
-    __shared__ const uint8_t *s_ptr[TC_MAX_E][2];
     __shared__ int s_tpre[TC_MAX_E + 1];        // token tiles before active expert u
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int K_in = KIND == 0 ? a.D : a.F;
     const int n_rows = KIND == 0 ? a.F : a.D;
-    const int MT = KIND == 0 ? n_rows / TC_BM : n_rows / (2 * TC_BM);   // row tiles per expert
-    const int KST = K_in / TC_BK;                                         // K stages per tile
-    const long rowbytes = (long)(K_in / 32) * 18;
+    const int MT = KIND == 0 ? n_rows / TC_BM : n_rows / TC_ROWS;   // row tiles per expert
+    const int KST = K_in / TC_BK;                                   // K stages per tile
+    const int NG = KST / TC_GRP;                                    // raw groups per tile
+    constexpr int NMATH = TC_MATH_WARPS * 32;
 
     if (threadIdx.x == 0) {
+        for (int s = 0; s < TC_RAW_SLOTS; ++s) {
+            mbar_init(&raw_full[s], 1);
+            mbar_init(&raw_empty[s], NMATH);
+        }
         for (int s = 0; s < TC_STAGES; ++s) {
-            mbar_init(&full_bar[s], TC_MATH_WARPS * 32);
+            mbar_init(&a_full[s], NMATH);
+            mbar_init(&b_full[s], 1);
             mbar_init(&empty_bar[s], 1);
         }
         mbar_init(&acc_full, 1);
-        mbar_init(&acc_empty, TC_MATH_WARPS * 32);
+        mbar_init(&acc_empty, NMATH);
         mbar_init(&drain_bar, 1);
         fence_mbar_init();
         s_abort = 0;
@@ -173,13 +213,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(TcArgs a) {
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
     const int U = *a.n_active;
-    for (int u = threadIdx.x; u <= U; u += blockDim.x) {
-        s_act[u] = a.act[u];
-        if (u < U) {
-            s_ptr[u][0] = a.act_ptr[3 * u + (KIND == 0 ? 0 : 2)];
-            s_ptr[u][1] = a.act_ptr[3 * u + 1];
-        }
-    }
+    for (int u = threadIdx.x; u <= U; u += blockDim.x) s_act[u] = a.act[u];
     __syncthreads();
     if (threadIdx.x == 0) {
         int acc = 0;
@@ -198,7 +232,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(TcArgs a) {
     const uint32_t sbase = smem_u32(smem);
 
     // tile -> (active expert u, row tile m, token tile n); token tiles innermost so the tiles of
-    // one weight block run back to back and its second read hits L2
+    // one weight block run back to back and its later reads hit L2
     auto decode = [&](int tile, int &u, int &m, int &n) {
         int lo = 0, hi = U;
         while (hi - lo > 1) {
@@ -212,7 +246,38 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(TcArgs a) {
         n = local - m * ntn;
     };
 
-    if (warp == 1) {
+    if (warp == 0) {
+        // ---------------- raw weight producer (one thread): two 128-row boxes per group
+        if (lane == 0) {
+            const CUtensorMap *maps = reinterpret_cast<const CUtensorMap *>(a.wmaps);
+            int git = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; ok && tile < total; tile += gridDim.x) {
+                int u, m, n;
+                decode(tile, u, m, n);
+                const int e = s_act[u].x;
+                const CUtensorMap *m0 = maps + 3 * e + (KIND == 0 ? 0 : 2);
+                const CUtensorMap *m1 = KIND == 0 ? maps + 3 * e + 1 : m0;
+                const int y0 = KIND == 0 ? m * TC_BM : m * TC_ROWS;
+                const int y1 = KIND == 0 ? m * TC_BM : m * TC_ROWS + TC_BM;
+                for (int g = 0; g < NG; ++g, ++git) {
+                    const int slot = git & 1;
+                    if (git >= TC_RAW_SLOTS &&
+                        !tc_wait(&raw_empty[slot], (uint32_t)((git >> 1) - 1) & 1u, abort_flag, a.status, ST_TIMEOUT_EMPTY)) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t *dst = smem + slot * TC_RAW_BYTES;
+                    mbar_arrive_expect_tx(&raw_full[slot], TC_RAW_BYTES);
+                    tma_load_2d(dst, m0, g * TC_RAW_ROW, y0, &raw_full[slot]);
+                    tma_load_2d(dst + TC_BM * TC_RAW_ROW, m1, g * TC_RAW_ROW, y1, &raw_full[slot]);
+                }
+            }
+            // the last groups' copies must land before the CTA may exit (bounded)
+            for (int q = git > TC_RAW_SLOTS ? git - TC_RAW_SLOTS : 0; q < git; ++q)
+                mbar_wait(&raw_full[q & 1], (uint32_t)(q >> 1) & 1u);
+        }
+    } else if (warp == 1) {
         // ---------------- MMA issuer (one thread)
         if (lane == 0) {
             const uint32_t idesc = umma_idesc_f16(TC_BM, TC_BN);
@@ -223,15 +288,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(TcArgs a) {
                 bool ok = true;
                 for (int ks = 0; ks < KST; ++ks, ++it) {
                     const int st = it % TC_STAGES;
-                    if (!tc_wait(&full_bar[st], (uint32_t)(it / TC_STAGES) & 1u, abort_flag, a.status, ST_TIMEOUT_FULL)) {
+                    const uint32_t par = (uint32_t)(it / TC_STAGES) & 1u;
+                    if (!tc_wait(&b_full[st], par, abort_flag, a.status, ST_TIMEOUT_FULL) ||
+                        !tc_wait(&a_full[st], par, abort_flag, a.status, ST_TIMEOUT_FULL)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t sa = sbase + st * TC_STAGE_BYTES, sb = sa + TC_A_BYTES;
+                    const uint32_t sa = sbase + TC_STAGE0 + st * TC_STAGE_BYTES, sb = sa + TC_A_BYTES;
 #pragma unroll
                     for (int kk = 0; kk < TC_BK / 16; ++kk) {
-                        const uint64_t bdesc = umma_desc(sb + kk * 2 * TC_LBO, TC_LBO, TC_SBO);
+                        const uint64_t bdesc = umma_desc_sw128(sb + kk * 32);
 #pragma unroll
                         for (int h = 0; h < 2; ++h) {
                             const uint64_t adesc = umma_desc(sa + h * (TC_BM / 8) * TC_SBO + kk * 2 * TC_LBO, TC_LBO, TC_SBO);
@@ -247,53 +314,78 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(TcArgs a) {
             umma_commit(&drain_bar);
             mbar_wait(&drain_bar, 0);
         }
-    } else if (warp >= 2) {
-        // ---------------- math warps: decode weights, stage tokens, epilogue
-        const int mt = threadIdx.x - 64;                   // 0..255
+    } else if (warp == 2) {
+        // ---------------- token-tile producer (one thread): 2D tensor TMA per stage
+        if (lane == 0) {
+            int it = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; ok && tile < total; tile += gridDim.x) {
+                int u, m, n;
+                decode(tile, u, m, n);
+                const int row0 = s_act[u].y + n * TC_BN;
+                for (int ks = 0; ks < KST; ++ks, ++it) {
+                    const int st = it % TC_STAGES;
+                    if (it >= TC_STAGES &&
+                        !tc_wait(&empty_bar[st], (uint32_t)(it / TC_STAGES - 1) & 1u, abort_flag, a.status, ST_TIMEOUT_EMPTY)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&b_full[st], TC_B_BYTES);
+                    tma_load_2d(smem + TC_STAGE0 + st * TC_STAGE_BYTES + TC_A_BYTES, &tmap_b, ks * TC_BK, row0, &b_full[st]);
+                }
+            }
+            for (int q = it > TC_STAGES ? it - TC_STAGES : 0; q < it; ++q)
+                mbar_wait(&b_full[q % TC_STAGES], (uint32_t)(q / TC_STAGES) & 1u);
+        }
+    } else {
+        // ---------------- math warps: decode weights into the A operand, epilogue
+        const int mt = threadIdx.x - TC_FIRST_MATH * 32;   // weight row of the tile, 0..255
         const int quad = warp & 3;                         // TMEM lane quadrant this warp may access
-        const int colhalf = (warp - 2) >> 2;               // epilogue columns [64*colhalf, +64)
-        int it = 0, ti = 0;
+        const int colhalf = (warp - TC_FIRST_MATH) >> 2;   // epilogue columns [64*colhalf, +64)
+        const int hr = mt >> 7, rr = mt & 127;             // half, row within half
+        int it = 0, git = 0, ti = 0;
         for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++ti) {
             int u, m, n;
             decode(tile, u, m, n);
             const int4 ex = s_act[u];
             const int off = ex.y + n * TC_BN;
             const int cnt = min(TC_BN, ex.z - n * TC_BN);
-            // this thread's weight row (one of 256) and token half-row
-            const int r = mt;                              // A row 0..255
-            const uint8_t *wrow;
-            if (KIND == 0) wrow = s_ptr[u][r >> 7] + (size_t)(m * TC_BM + (r & 127)) * rowbytes;
-            else wrow = s_ptr[u][0] + (size_t)(m * 2 * TC_BM + r) * rowbytes;
-            const int bt = mt >> 1, bhalf = mt & 1;         // token row bt, chunks 4*bhalf..+3
-            const __half *brow = nullptr;
-            if (bt < cnt) {
-                const int p = off + bt;
-                brow = KIND == 0 ? a.bsrc + (size_t)(a.pairs[p] / a.K) * a.D : a.bsrc + (size_t)p * a.F;
-            }
             bool ok = true;
-            for (int ks = 0; ks < KST; ++ks, ++it) {
-                const int st = it % TC_STAGES;
-                if (it >= TC_STAGES &&
-                    !tc_wait(&empty_bar[st], (uint32_t)(it / TC_STAGES - 1) & 1u, abort_flag, a.status, ST_TIMEOUT_EMPTY)) {
+            for (int g = 0; g < NG && ok; ++g, ++git) {
+                const int slot = git & 1;
+                if (!tc_wait(&raw_full[slot], (uint32_t)(git >> 1) & 1u, abort_flag, a.status, ST_TIMEOUT_FULL)) {
                     ok = false;
                     break;
                 }
-                uint8_t *sa = smem + st * TC_STAGE_BYTES, *sb = sa + TC_A_BYTES;
-                uint4 v[8];
-                q4_pair_to_f16(reinterpret_cast<const uint32_t *>(wrow + (size_t)ks * 36), v);
-                const int hr = r >> 7, rr = r & 127;       // half, row within half
+                uint32_t w[36];
+                const uint4 *src = reinterpret_cast<const uint4 *>(smem + slot * TC_RAW_BYTES + mt * TC_RAW_ROW);
 #pragma unroll
-                for (int c = 0; c < 8; ++c)
-                    *reinterpret_cast<uint4 *>(sa + hr * (TC_BM / 8) * TC_SBO + canon_off(rr, c)) = v[c];
-#pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    const int cc = bhalf * 4 + c;
-                    uint4 bv = make_uint4(0, 0, 0, 0);
-                    if (brow) bv = __ldg(reinterpret_cast<const uint4 *>(brow + ks * TC_BK + cc * 8));
-                    *reinterpret_cast<uint4 *>(sb + canon_off(bt, cc)) = bv;
+                for (int i = 0; i < 9; ++i) {
+                    const uint4 v = src[i];
+                    w[4 * i] = v.x; w[4 * i + 1] = v.y; w[4 * i + 2] = v.z; w[4 * i + 3] = v.w;
                 }
-                fence_async_smem();                        // generic-proxy writes -> tensor core
-                mbar_arrive(&full_bar[st]);
+#pragma unroll
+                for (int j = 0; j < TC_GRP; ++j) {
+                    const int st = (it + j) % TC_STAGES;
+                    if (it + j >= TC_STAGES &&
+                        !tc_wait(&empty_bar[st], (uint32_t)((it + j) / TC_STAGES - 1) & 1u, abort_flag, a.status,
+                                 ST_TIMEOUT_EMPTY)) {
+                        ok = false;
+                        break;
+                    }
+                    uint4 v[8];
+                    q4_pair_to_f16(&w[9 * j], v);
+                    uint8_t *sa = smem + TC_STAGE0 + st * TC_STAGE_BYTES + hr * (TC_BM / 8) * TC_SBO;
+#pragma unroll
+                    for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4 *>(sa + canon_off(rr, c)) = v[c];
+                    fence_async_smem();                    // generic-proxy writes -> tensor core
+                    mbar_arrive(&a_full[st]);
+                }
+                // The slot is released only after all four stages are decoded: the TMA engine
+                // (async proxy) refills it, and a release right after the shared-memory loads let
+                // the refill overtake them (corrupted rows measured on B200).
+                mbar_arrive(&raw_empty[slot]);
+                it += TC_GRP;
             }
             if (!__all_sync(0xffffffffu, ok)) break;
             // epilogue: wait for the accumulators, read this warp's 32 rows (tcgen05.ld is
@@ -322,7 +414,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(TcArgs a) {
                     for (int j = 0; j < 32; ++j) {
                         const int col = c0 + j;
                         if (col < cnt) {
-                            float *yr = a.y_out + (size_t)a.pairs[off + col] * a.D + m * 2 * TC_BM;
+                            float *yr = a.y_out + (size_t)a.pairs[off + col] * a.D + m * TC_ROWS;
                             yr[row] = g[j];
                             yr[TC_BM + row] = w2[j];
                         }
@@ -342,13 +434,88 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(TcArgs a) {
     }
 }
 
-int gemm_tc_launch(int kind, const TcArgs &a, int max_tiles, cudaStream_t s) {
+// ---------------------------------------------------------------- host side
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_tiled() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+
+int gemm_tc_build_weight_maps(const uint8_t *const *h_ptrs, int E, int D, int F, void **d_maps) {
+    EncodeTiledFn enc = encode_tiled();
+    if (!enc) {
+        set_error("grouped GEMM: cuTensorMapEncodeTiled is unavailable from the driver");
+        return CPG_ECUDA;
+    }
+    CUtensorMap *h = (CUtensorMap *)malloc(sizeof(CUtensorMap) * 3 * (size_t)E);
+    CPG_REQUIRE(h != nullptr, "host allocation failed");
+    for (int i = 0; i < 3 * E; ++i) {
+        const int kind = i % 3;                               // 0 gate, 1 up: (F, D); 2 down: (D, F)
+        const int n_in = kind == 2 ? F : D, n_out = kind == 2 ? D : F;
+        const cuuint64_t rb = (cuuint64_t)(n_in / 32) * 18;
+        const cuuint64_t dims[2] = {rb, (cuuint64_t)n_out};
+        const cuuint64_t strides[1] = {rb};
+        const cuuint32_t box[2] = {TC_RAW_ROW, TC_BM};
+        const cuuint32_t estr[2] = {1, 1};
+        const CUresult r = enc(&h[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t *>(h_ptrs[i]), dims, strides,
+                               box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) {
+            free(h);
+            set_error("grouped GEMM: tensor map of expert %d kind %d failed (%d)", i / 3, kind, (int)r);
+            return CPG_ECUDA;
+        }
+    }
+    void *d = nullptr;
+    cudaError_t ce = cudaMalloc(&d, sizeof(CUtensorMap) * 3 * (size_t)E);
+    if (ce == cudaSuccess) ce = cudaMemcpy(d, h, sizeof(CUtensorMap) * 3 * (size_t)E, cudaMemcpyHostToDevice);
+    free(h);
+    if (ce != cudaSuccess) {
+        cudaFree(d);
+        return cuda_fail(ce, "grouped GEMM: tensor map upload");
+    }
+    *d_maps = d;
+    return CPG_OK;
+}
+
+int gemm_tc_launch(int kind, const TcArgs &a, const __half *b, int b_rows, int max_tiles, cudaStream_t s) {
+    const int kdim = kind == 0 ? a.D : a.F;
+    CPG_REQUIRE(kdim % (TC_BK * TC_GRP) == 0, "grouped GEMM: K=%d must be a multiple of %d", kdim, TC_BK * TC_GRP);
+    CPG_REQUIRE(((uintptr_t)b & 15) == 0, "grouped GEMM: token rows must be 16-byte aligned");
+    EncodeTiledFn enc = encode_tiled();
+    if (!enc) {
+        set_error("grouped GEMM: cuTensorMapEncodeTiled is unavailable from the driver");
+        return CPG_ECUDA;
+    }
+    CUtensorMap map;
+    const cuuint64_t dims[2] = {(cuuint64_t)kdim, (cuuint64_t)b_rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)kdim * 2};
+    const cuuint32_t box[2] = {TC_BK, TC_BN};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = enc(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half *>(b), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        set_error("grouped GEMM: cuTensorMapEncodeTiled failed (%d)", (int)r);
+        return CPG_ECUDA;
+    }
     auto *k = kind == 0 ? k_gemm_tc<0> : k_gemm_tc<1>;
-    const size_t smem = (size_t)TC_STAGES * TC_STAGE_BYTES + 1024;
+    const size_t smem = (size_t)TC_SMEM + 1024;
     CPG_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     int grid = sm_count();
     if (max_tiles < grid) grid = max_tiles > 0 ? max_tiles : 1;
-    k<<<grid, TC_THREADS, smem, s>>>(a);
+    k<<<grid, TC_THREADS, smem, s>>>(a, map);
     CPG_CUDA(cudaGetLastError());
     return CPG_OK;
 }

@@ -17,6 +17,9 @@
 // N dimension (8 per MMA tile), weights are read exactly once per layer.
 #include <math.h>
 
+#include <mutex>
+#include <vector>
+
 #include "common.cuh"
 #include "layout.cuh"
 
@@ -744,6 +747,10 @@ struct cpg_moe_layer {
     const float *ln2;
     const float *wgate;
     const uint8_t **d_ptrs;        // device (E, 3)
+    std::vector<const uint8_t *> h_ptrs;   // host copy of the same table
+    void *d_wmaps = nullptr;       // device (E, 3) TMA tensor maps of the expert matrices, built
+                                   // on the first tcgen05 call (cpg_moe_apply)
+    std::mutex wmaps_mu;
     cpg::KernelPlan gateup, down;
 };
 
@@ -806,6 +813,18 @@ int layer_ptrs(const cpg_moe_layer *L, const uint8_t *const **ptrs, int *enc) {
     *enc = L->enc;
     return CPG_OK;
 }
+int gemm_tc_build_weight_maps(const uint8_t *const *h_ptrs, int E, int D, int F, void **d_maps);
+int layer_weight_maps(const cpg_moe_layer *Lc, const void **maps) {
+    CPG_REQUIRE(Lc, "null layer");
+    cpg_moe_layer *L = const_cast<cpg_moe_layer *>(Lc);
+    std::lock_guard<std::mutex> g(L->wmaps_mu);
+    if (!L->d_wmaps) {
+        const int rc = gemm_tc_build_weight_maps(L->h_ptrs.data(), L->E, L->D, L->F, &L->d_wmaps);
+        if (rc) return rc;
+    }
+    *maps = L->d_wmaps;
+    return CPG_OK;
+}
 }  // namespace cpg
 
 using namespace cpg;
@@ -835,6 +854,7 @@ extern "C" int cpg_moe_layer_create(const cpg_moe_desc *d, cpg_moe_layer **out) 
     cpg_moe_layer *L = new cpg_moe_layer();
     L->D = d->d_model; L->F = d->d_exp; L->E = E; L->K = d->topk; L->eps = d->rms_eps;
     L->enc = enc; L->ln2 = d->ln2; L->wgate = (const float *)d->wgate.p;
+    L->h_ptrs.assign(h, h + 3 * E);
     cudaError_t ce = cudaMalloc((void **)&L->d_ptrs, sizeof(void *) * 3 * E);
     if (ce == cudaSuccess) ce = cudaMemcpy(L->d_ptrs, h, sizeof(void *) * 3 * E, cudaMemcpyHostToDevice);
     free(h);
@@ -872,6 +892,7 @@ extern "C" int cpg_moe_layer_create(const cpg_moe_desc *d, cpg_moe_layer **out) 
 extern "C" void cpg_moe_layer_destroy(cpg_moe_layer *L) {
     if (!L) return;
     cudaFree(L->d_ptrs);
+    if (L->d_wmaps) cudaFree(L->d_wmaps);
     delete L;
 }
 
