@@ -2,18 +2,20 @@
 // other large batches where each expert sees many tokens.
 //
 // Per tile: 256 weight rows (gate 128 + up 128 of one expert, or 256 rows of its down matrix) ×
-// 128 tokens of that expert, K streamed 64 values per stage. Roles (one CTA per SM):
+// up to 256 tokens of that expert (MMA N = the tile's token count rounded up to 16), K streamed 32
+// values per stage through four stages. Roles (one CTA per SM):
 //   warp 0      owns the TMEM allocation; one thread loads raw Q4_0 rows into a two-slot
-//               shared-memory ring with 2D tensor TMA boxes of 128 rows × 144 bytes (four stages
+//               shared-memory ring with 2D tensor TMA boxes of 128 rows × 144 bytes (eight stages
 //               of K) over each expert matrix: two requests per group, where one small copy per
 //               row queued 256 requests on the copy engine and starved the tensor core
-//   warp 1      one thread issues tcgen05.mma (M=128, N=128, K=16, fp16 × fp16 → fp32 in TMEM),
+//   warp 1      one thread issues tcgen05.mma (M=128, N≤256, K=16, fp16 × fp16 → fp32 in TMEM),
 //               twice per K step (one per 128-row half), and commits each stage to the mbarrier
 //               that frees it
-//   warp 2      one thread loads the token tile of each stage with a 2D tensor TMA (128-byte
-//               swizzle) from the expert-sorted fp16 activation rows
+//   warp 2      one thread loads the token tile of each stage with a 2D tensor TMA (64-byte
+//               swizzle, a 128- or 256-row box) from the expert-sorted fp16 activation rows
 //   warps 3-10  decode each raw row from shared memory into fp16 (q·d rounded once) in the
-//               K-major no-swizzle canonical layout, then run the epilogue from TMEM:
+//               K-major no-swizzle canonical layout, one Q4_0 group pair per two stages, then run
+//               the epilogue from TMEM:
 //                 gate/up: h = silu(g)·u (engine/blocks/qwen3_moe.c:217-219), fp16 per pair
 //                 down:    y per (token, slot) in fp32, combined in selection order by k_combine
 // Every mbarrier wait is bounded; a timeout records a status code, all roles leave together, and
@@ -28,25 +30,26 @@
 namespace cpg {
 
 constexpr int TC_BM = 128;                  // rows per MMA (one TMEM lane per row)
-constexpr int TC_BN = 128;                  // tokens per tile (MMA N, TMEM columns per half)
-constexpr int TC_BK = 64;                   // K per stage (4 MMAs of K=16)
-constexpr int TC_STAGES = 3;
+constexpr int TC_BN = 256;                  // tokens per tile (MMA N at most, TMEM columns per half)
+constexpr int TC_BN_SMALL = 128;            // token box for tiles of at most 128 tokens
+constexpr int TC_BK = 32;                   // K per stage (one Q4_0 group; 2 MMAs of K=16 per half)
+constexpr int TC_STAGES = 4;
 constexpr int TC_ROWS = 2 * TC_BM;          // weight rows per tile
-constexpr int TC_GRP = 4;                   // K stages per raw group
-constexpr int TC_RAW_ROW = TC_GRP * 36;     // 144 bytes: four Q4_0 group pairs of one row
+constexpr int TC_GRP = 8;                   // K stages per raw group
+constexpr int TC_RAW_ROW = 144;             // bytes per row per raw group: four Q4_0 group pairs
 constexpr int TC_RAW_BYTES = TC_ROWS * TC_RAW_ROW;                  // 36 KB per raw slot
 constexpr int TC_RAW_SLOTS = 2;
-constexpr int TC_A_BYTES = TC_ROWS * TC_BK * 2;                     // 32 KB: two 128-row halves
+constexpr int TC_A_BYTES = TC_ROWS * TC_BK * 2;                     // 16 KB: two 128-row halves
 constexpr int TC_B_BYTES = TC_BN * TC_BK * 2;                       // 16 KB
 constexpr int TC_STAGE_BYTES = TC_A_BYTES + TC_B_BYTES;
 constexpr int TC_STAGE0 = TC_RAW_SLOTS * TC_RAW_BYTES;              // operand stages follow the raw ring
-constexpr int TC_SMEM = TC_STAGE0 + TC_STAGES * TC_STAGE_BYTES;     // 216 KB (+1 KB alignment slack)
+constexpr int TC_SMEM = TC_STAGE0 + TC_STAGES * TC_STAGE_BYTES;     // 200 KB (+1 KB alignment slack)
 constexpr int TC_MATH_WARPS = 8;
 constexpr int TC_FIRST_MATH = 3;
 constexpr int TC_THREADS = (TC_FIRST_MATH + TC_MATH_WARPS) * 32;
 constexpr int TC_SBO = (TC_BK / 8) * 128;   // no-swizzle A: bytes between 8-row core-matrix groups
 constexpr int TC_LBO = 128;                 // no-swizzle A: bytes between 8-column core matrices
-constexpr int TC_TMEM_COLS = 2 * TC_BN;     // two fp32 accumulators of 128 columns
+constexpr int TC_TMEM_COLS = 2 * TC_BN;     // two fp32 accumulators of 256 columns (all of TMEM)
 constexpr int TC_MAX_E = 256;
 static_assert(TC_STAGE0 % 1024 == 0 && TC_STAGE_BYTES % 1024 == 0 && TC_A_BYTES % 1024 == 0,
               "operand tiles must stay 1024-byte aligned");
@@ -59,12 +62,12 @@ __device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint
            ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);
 }
 
-// K-major, 128-byte swizzle (the layout a SWIZZLE_128B tensor TMA writes): rows of 128 bytes,
-// 8-row groups 1024 bytes apart (SBO), LBO unused (1), layout type 2. Advancing K by 16 fp16
-// values inside the 128-byte row moves the start address by 32 bytes.
-__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
-    return (uint64_t)((saddr >> 4) & 0x3FFFu) | (1ull << 16) | ((uint64_t)(1024 >> 4) << 32) | (1ull << 46) |
-           (2ull << 61);
+// K-major, 64-byte swizzle (the layout a SWIZZLE_64B tensor TMA writes): rows of 64 bytes,
+// 8-row groups 512 bytes apart (SBO), LBO unused (1), layout type 4. Advancing K by 16 fp16
+// values inside the 64-byte row moves the start address by 32 bytes.
+__device__ __forceinline__ uint64_t umma_desc_sw64(uint32_t saddr) {
+    return (uint64_t)((saddr >> 4) & 0x3FFFu) | (1ull << 16) | ((uint64_t)(512 >> 4) << 32) | (1ull << 46) |
+           (4ull << 61);
 }
 
 // kind::f16 instruction descriptor: fp32 accumulate, fp16 A and B, both K-major, M, N.
@@ -170,7 +173,8 @@ __device__ __forceinline__ uint32_t canon_off(int r, int c) {
 }
 
 template <int KIND>
-__global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const TcArgs a, const __grid_constant__ CUtensorMap tmap_b) {
+__global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const TcArgs a, const __grid_constant__ CUtensorMap tmap_b,
+                                                       const __grid_constant__ CUtensorMap tmap_b_small) {
     // The runtime places dynamic shared memory after the static variables, 16-byte aligned only,
     // so the tiles are moved up to the next 1024-byte boundary here (the launch adds the slack).
     // The declaration states 16 so that the compiler cannot assume more and fold this away.
@@ -207,7 +211,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const TcArgs a, const
         fence_mbar_init();
         s_abort = 0;
     }
-    if (warp == 0) {                                   // TMEM: 256 fp32 columns
+    if (warp == 0) {                                   // TMEM: 512 fp32 columns
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
                      ::"r"(smem_u32(&s_tmem)), "r"(TC_TMEM_COLS));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
@@ -280,9 +284,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const TcArgs a, const
     } else if (warp == 1) {
         // ---------------- MMA issuer (one thread)
         if (lane == 0) {
-            const uint32_t idesc = umma_idesc_f16(TC_BM, TC_BN);
             int it = 0, ti = 0;
             for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++ti) {
+                int u, m, n;
+                decode(tile, u, m, n);
+                const int cnt = min(TC_BN, s_act[u].z - n * TC_BN);
+                const uint32_t idesc = umma_idesc_f16(TC_BM, (cnt + 15) & ~15);
                 if (ti > 0 && !tc_wait(&acc_empty, (uint32_t)(ti - 1) & 1u, abort_flag, a.status, ST_TIMEOUT_EMPTY)) break;
                 tc_fence_after();
                 bool ok = true;
@@ -298,7 +305,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const TcArgs a, const
                     const uint32_t sa = sbase + TC_STAGE0 + st * TC_STAGE_BYTES, sb = sa + TC_A_BYTES;
 #pragma unroll
                     for (int kk = 0; kk < TC_BK / 16; ++kk) {
-                        const uint64_t bdesc = umma_desc_sw128(sb + kk * 32);
+                        const uint64_t bdesc = umma_desc_sw64(sb + kk * 32);
 #pragma unroll
                         for (int h = 0; h < 2; ++h) {
                             const uint64_t adesc = umma_desc(sa + h * (TC_BM / 8) * TC_SBO + kk * 2 * TC_LBO, TC_LBO, TC_SBO);
@@ -323,6 +330,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const TcArgs a, const
                 int u, m, n;
                 decode(tile, u, m, n);
                 const int row0 = s_act[u].y + n * TC_BN;
+                const bool small = s_act[u].z - n * TC_BN <= TC_BN_SMALL;
+                const CUtensorMap *bmap = small ? &tmap_b_small : &tmap_b;
+                const uint32_t bbytes = small ? TC_B_BYTES / 2 : TC_B_BYTES;
                 for (int ks = 0; ks < KST; ++ks, ++it) {
                     const int st = it % TC_STAGES;
                     if (it >= TC_STAGES &&
@@ -330,8 +340,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const TcArgs a, const
                         ok = false;
                         break;
                     }
-                    mbar_arrive_expect_tx(&b_full[st], TC_B_BYTES);
-                    tma_load_2d(smem + TC_STAGE0 + st * TC_STAGE_BYTES + TC_A_BYTES, &tmap_b, ks * TC_BK, row0, &b_full[st]);
+                    mbar_arrive_expect_tx(&b_full[st], bbytes);
+                    tma_load_2d(smem + TC_STAGE0 + st * TC_STAGE_BYTES + TC_A_BYTES, bmap, ks * TC_BK, row0, &b_full[st]);
                 }
             }
             for (int q = it > TC_STAGES ? it - TC_STAGES : 0; q < it; ++q)
@@ -341,7 +351,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const TcArgs a, const
         // ---------------- math warps: decode weights into the A operand, epilogue
         const int mt = threadIdx.x - TC_FIRST_MATH * 32;   // weight row of the tile, 0..255
         const int quad = warp & 3;                         // TMEM lane quadrant this warp may access
-        const int colhalf = (warp - TC_FIRST_MATH) >> 2;   // epilogue columns [64*colhalf, +64)
+        const int colhalf = (warp - TC_FIRST_MATH) >> 2;   // epilogue columns [128*colhalf, +128)
         const int hr = mt >> 7, rr = mt & 127;             // half, row within half
         int it = 0, git = 0, ti = 0;
         for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++ti) {
@@ -365,23 +375,29 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const TcArgs a, const
                     w[4 * i] = v.x; w[4 * i + 1] = v.y; w[4 * i + 2] = v.z; w[4 * i + 3] = v.w;
                 }
 #pragma unroll
-                for (int j = 0; j < TC_GRP; ++j) {
-                    const int st = (it + j) % TC_STAGES;
-                    if (it + j >= TC_STAGES &&
-                        !tc_wait(&empty_bar[st], (uint32_t)((it + j) / TC_STAGES - 1) & 1u, abort_flag, a.status,
-                                 ST_TIMEOUT_EMPTY)) {
+                for (int j = 0; j < TC_GRP / 2; ++j) {     // group pair j -> stages it+2j, it+2j+1
+                    const int i0 = it + 2 * j, i1 = i0 + 1;
+                    const int st0 = i0 % TC_STAGES, st1 = i1 % TC_STAGES;
+                    if (i0 >= TC_STAGES &&
+                        (!tc_wait(&empty_bar[st0], (uint32_t)(i0 / TC_STAGES - 1) & 1u, abort_flag, a.status, ST_TIMEOUT_EMPTY) ||
+                         !tc_wait(&empty_bar[st1], (uint32_t)(i1 / TC_STAGES - 1) & 1u, abort_flag, a.status, ST_TIMEOUT_EMPTY))) {
                         ok = false;
                         break;
                     }
                     uint4 v[8];
                     q4_pair_to_f16(&w[9 * j], v);
-                    uint8_t *sa = smem + TC_STAGE0 + st * TC_STAGE_BYTES + hr * (TC_BM / 8) * TC_SBO;
+                    uint8_t *sa0 = smem + TC_STAGE0 + st0 * TC_STAGE_BYTES + hr * (TC_BM / 8) * TC_SBO;
+                    uint8_t *sa1 = smem + TC_STAGE0 + st1 * TC_STAGE_BYTES + hr * (TC_BM / 8) * TC_SBO;
 #pragma unroll
-                    for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4 *>(sa + canon_off(rr, c)) = v[c];
+                    for (int c = 0; c < 4; ++c) {
+                        *reinterpret_cast<uint4 *>(sa0 + canon_off(rr, c)) = v[c];
+                        *reinterpret_cast<uint4 *>(sa1 + canon_off(rr, c)) = v[4 + c];
+                    }
                     fence_async_smem();                    // generic-proxy writes -> tensor core
-                    mbar_arrive(&a_full[st]);
+                    mbar_arrive(&a_full[st0]);
+                    mbar_arrive(&a_full[st1]);
                 }
-                // The slot is released only after all four stages are decoded: the TMA engine
+                // The slot is released only after all its stages are decoded: the TMA engine
                 // (async proxy) refills it, and a release right after the shared-memory loads let
                 // the refill overtake them (corrupted rows measured on B200).
                 mbar_arrive(&raw_empty[slot]);
@@ -394,7 +410,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const TcArgs a, const
             if (!__all_sync(0xffffffffu, got)) break;
             tc_fence_after();
             const int row = quad * 32 + lane;              // accumulator row (TMEM lane)
-            for (int c0 = colhalf * 64; c0 < colhalf * 64 + 64; c0 += 32) {
+            for (int c0 = colhalf * (TC_BN / 2); c0 < colhalf * (TC_BN / 2) + TC_BN / 2 && c0 < cnt; c0 += 32) {
                 float g[32], w2[32];
                 tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + c0, g);
                 tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + TC_BN + c0, w2);
@@ -404,8 +420,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const TcArgs a, const
                     for (int j = 0; j < 32; ++j) {
                         const int col = c0 + j;
                         if (col < cnt) {
+                            // silu(g)*u with the fast exponential and division: h is rounded to
+                            // fp16 next, so their few-ulp error stays far below that rounding
                             const float gv = g[j];
-                            const float h = gv / (1.0f + expf(-gv)) * w2[j];   // silu(g)*u
+                            const float h = __fdividef(gv, 1.0f + __expf(-gv)) * w2[j];
                             a.h_out[(size_t)(off + col) * a.F + feat] = __float2half_rn(h);
                         }
                     }
@@ -498,24 +516,26 @@ int gemm_tc_launch(int kind, const TcArgs &a, const __half *b, int b_rows, int m
         set_error("grouped GEMM: cuTensorMapEncodeTiled is unavailable from the driver");
         return CPG_ECUDA;
     }
-    CUtensorMap map;
+    CUtensorMap map[2];
     const cuuint64_t dims[2] = {(cuuint64_t)kdim, (cuuint64_t)b_rows};
     const cuuint64_t strides[1] = {(cuuint64_t)kdim * 2};
-    const cuuint32_t box[2] = {TC_BK, TC_BN};
     const cuuint32_t estr[2] = {1, 1};
-    const CUresult r = enc(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half *>(b), dims, strides, box, estr,
-                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) {
-        set_error("grouped GEMM: cuTensorMapEncodeTiled failed (%d)", (int)r);
-        return CPG_ECUDA;
+    for (int i = 0; i < 2; ++i) {
+        const cuuint32_t box[2] = {TC_BK, (cuuint32_t)(i == 0 ? TC_BN : TC_BN_SMALL)};
+        const CUresult r = enc(&map[i], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half *>(b), dims, strides, box,
+                               estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) {
+            set_error("grouped GEMM: cuTensorMapEncodeTiled failed (%d)", (int)r);
+            return CPG_ECUDA;
+        }
     }
     auto *k = kind == 0 ? k_gemm_tc<0> : k_gemm_tc<1>;
     const size_t smem = (size_t)TC_SMEM + 1024;
     CPG_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     int grid = sm_count();
     if (max_tiles < grid) grid = max_tiles > 0 ? max_tiles : 1;
-    k<<<grid, TC_THREADS, smem, s>>>(a, map);
+    k<<<grid, TC_THREADS, smem, s>>>(a, map[0], map[1]);
     CPG_CUDA(cudaGetLastError());
     return CPG_OK;
 }
