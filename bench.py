@@ -13,6 +13,9 @@ layers (router, experts, combine, residual), weights resident in HBM.
           duration (CUDA events inside the decode graph), against MEASURED_PEAKS.json
   cpu_baseline  the reference engine (oracle/_ref: the reference's own C sources) on the host
           cores, a bounded sample of the same workload
+  decode_q8_batch1  configs[0]: one token through 48 stacked layers with Q8_0 experts (plain
+          N(0,0.02) router), tok/s and HBM GB/s against the measured copy bandwidth, with the
+          reference engine's time on the same workload (bounded sample) beside it
   prefill   configs[3]: 4096 Zipf(1.2)-routed tokens through one Q4_0 MoE block per step on the
           tcgen05 grouped GEMM (cpg_moe_apply), tok/s and TFLOP/s, roofline of the gate/up GEMM
           against the measured tensor peak
@@ -38,8 +41,9 @@ sys.path.insert(0, ROOT)
 
 METRIC = "decode tok/s & MoE-layer HBM GB/s (Qwen3-30B-A3B shape, Q4) at 1/2/4/8 B200"
 D, F, E, K = 2048, 768, 128, 8
-ENC_Q4 = 4
+ENC_Q4, ENC_Q8 = 4, 8
 MAT_BYTES = F * D // 32 * 18                     # 884,736
+MAT_BYTES_Q8 = F * D // 32 * 34                  # 1,671,168
 REGION_BYTES = 3 * MAT_BYTES                     # 2,654,208 per expert (Wg | Wu | Wd)
 ROUTER_BYTES = E * D * 4
 LN_BYTES = D * 4
@@ -58,6 +62,7 @@ def parse():
     ap.add_argument("--cpu-sample-layers", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--prefill-tokens", type=int, default=4096, help="0 skips the prefill section")
+    ap.add_argument("--no-q8", action="store_true", help="skip the Q8 batch-1 section")
     return ap.parse_args()
 
 
@@ -267,15 +272,19 @@ def run_ours(args, rank, world, torch, dist):
     barrier()
     ms_b1 = b0.elapsed_time(b1)
 
+    # ---- batch-1 decode with Q8_0 experts (its own 48-layer stack)
+    q8 = None if args.no_q8 else q8_batch1_bench(args, torch, lib, Q, barrier)
+    ms_q8 = q8.pop("_ms") if q8 else 0.0
+
     # ---- prefill: Zipf(1.2)-routed tokens through one MoE block per step
     pf = prefill_bench(args, layers, torch, lib, Q, s, barrier) if args.prefill_tokens > 0 else None
     ms_pf = pf.pop("_ms") if pf else 0.0
 
     # max over ranks
-    t = torch.tensor([ms, ms_e2e, ms_b1, ms_pf], dtype=torch.float64, device="cuda")
+    t = torch.tensor([ms, ms_e2e, ms_b1, ms_pf, ms_q8], dtype=torch.float64, device="cuda")
     if dist is not None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms, ms_e2e, ms_b1, ms_pf = float(t[0]), float(t[1]), float(t[2]), float(t[3])
+    ms, ms_e2e, ms_b1, ms_pf, ms_q8 = (float(v) for v in t.tolist())
     if rank != 0:
         return None
 
@@ -318,12 +327,64 @@ def run_ours(args, rank, world, torch, dist):
         "gpu_launches": 4 * L * args.steps,
         "clocks": clk,
     }
+    if q8:
+        per = ms_q8 / args.steps
+        q8["value"] = round(world * args.steps / (ms_q8 * 1e-3), 1)
+        q8["ms_per_step"] = round(per, 4)
+        q8["hbm_gbs"] = round(q8["bytes_per_step"] / (per * 1e-3) / 1e9, 1)
+        q8["frac"] = round(q8["hbm_gbs"] / hbm, 4)
+        res["decode_q8_batch1"] = q8
     if pf:
         pf["value"] = round(world * args.prefill_tokens * args.steps / (ms_pf * 1e-3), 1)
         pf["ms_per_step"] = round(ms_pf / args.steps, 4)
         pf["tflops"] = round(pf["flops_per_step"] / (ms_pf / args.steps * 1e-3) / 1e12, 1)
         res["prefill"] = pf
     return res
+
+
+def q8_batch1_bench(args, torch, lib, Q, barrier):
+    """one token per step through args.layers distinct layers whose 128 experts are
+    Q8_0 (weights ~N(0,0.02) quantised on the device by cpg_quantize), f32 router ~N(0,0.02),
+    ln2 = 1. The layer stack (30.8 GB for 48 layers) is larger than L2, so every step streams the
+    8 selected experts of each layer from HBM."""
+    L = args.layers
+    g = torch.Generator(device="cuda")
+    layers = []
+    for l in range(L):
+        blob = torch.empty(E * 3 * MAT_BYTES_Q8, dtype=torch.uint8, device="cuda")
+        w32 = torch.randn(E * 3 * F * D, generator=g.manual_seed(args.seed * 3000 + l), device="cuda")
+        w32.mul_(0.02)
+        Q.check(lib.cpg_quantize(blob.data_ptr(), w32.data_ptr(), ENC_Q8, w32.numel(), None))
+        del w32
+        ln2 = torch.ones(D, device="cuda")
+        wg = torch.randn((E, D), generator=g.manual_seed(args.seed * 3000 + 500 + l), device="cuda") * 0.02
+        layers.append(Q.MoELayer(ln2, wg, ENC_Q8, D, F, E, K, blob=blob))
+    ctx = Q.DecodeContext(layers[0], max_T=1, device=torch.cuda.current_device())
+    arr = ctx.layer_array(layers)
+    s = torch.cuda.ExternalStream(ctx.stream_ptr())
+    xbuf = view(torch, ctx.x_ptr(), D * 4).view(1, D)
+    x1 = torch.randn((1, D), generator=g.manual_seed(args.seed + 91), device="cuda")
+
+    def step():
+        with torch.cuda.stream(s):
+            xbuf.copy_(x1)
+        ctx.run_device(arr, L, 1)
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for _ in range(args.steps):
+        step()
+    e1.record(s)
+    barrier()
+    ms = e0.elapsed_time(e1)
+    del ctx
+    return {"_ms": ms, "unit": "tok/s",
+            "bytes_per_step": L * (LN_BYTES + ROUTER_BYTES + K * 3 * MAT_BYTES_Q8 + 2 * D * 4),
+            "config": {"workload": f"configs[0]: decode batch 1 through {L} stacked Q8_0 MoE layers "
+                                   "(plain N(0,0.02) f32 router)", "expert_encoding": "Q8_0"}}
 
 
 def prefill_bench(args, layers, torch, lib, Q, s, barrier):
@@ -386,8 +447,9 @@ def prefill_bench(args, layers, torch, lib, Q, s, barrier):
 
 
 # ------------------------------------------------------------------ reference (CPU)
-def reference_sample(n_layers: int, T: int, zipf: float, seed: int, steps: int, warmup: int):
-    """The reference engine (oracle/_ref) on n_layers distinct layers, T tokens per pass."""
+def reference_sample(n_layers: int, T: int, zipf, seed: int, steps: int, warmup: int, enc: int = ENC_Q4):
+    """The reference engine (oracle/_ref) on n_layers distinct layers, T tokens per pass; routers
+    Zipf-calibrated on the chained activations unless zipf is None."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
     from cachepotato_b200.workload import calibrate_router_scales, rmsnorm_rows
@@ -397,9 +459,10 @@ def reference_sample(n_layers: int, T: int, zipf: float, seed: int, steps: int, 
     layers = []
     xi = x
     for l in range(n_layers):          # routers calibrated on the chained activations
-        L0 = O.SynthLayer(D, F, E, K, O.ENC_Q4, seed=seed + 17 * l, oracle=orc)
-        s = calibrate_router_scales(rmsnorm_rows(xi) @ L0.wgate.T, K, zipf, seed=seed + l)
-        L0.wgate *= s[:, None]
+        L0 = O.SynthLayer(D, F, E, K, enc, seed=seed + 17 * l, oracle=orc)
+        if zipf is not None:
+            s = calibrate_router_scales(rmsnorm_rows(xi) @ L0.wgate.T, K, zipf, seed=seed + l)
+            L0.wgate *= s[:, None]
         layers.append(L0)
         xi = xi + ref.qwen3_moe(L0, xi)["mlp"]
     times = []
@@ -466,6 +529,12 @@ def main():
                                "cores": threads, "kind": "reference",
                                "sample": f"reference engine, {args.cpu_sample_layers} layers x 2 reps, "
                                          f"T={args.tokens}, per-layer time x {args.layers}"}
+        if "decode_q8_batch1" in res:
+            pl8, th8 = reference_sample(args.cpu_sample_layers, 1, None, args.seed + 5, 3, 1, ENC_Q8)
+            res["decode_q8_batch1"]["cpu_baseline"] = {
+                "value": round(1.0 / (pl8 * args.layers), 3), "unit": "tok/s", "cores": th8, "kind": "reference",
+                "sample": f"reference engine, Q8_0 experts, {args.cpu_sample_layers} layers x 3 reps, T=1, "
+                          f"per-layer time x {args.layers}"}
     if res is not None:
         print(json.dumps(res), flush=True)
     if dist is not None:
