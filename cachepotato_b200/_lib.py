@@ -26,6 +26,8 @@ EXPORTS = [
     "cpg_ctx_create", "cpg_ctx_destroy", "cpg_ctx_stream", "cpg_run_moe_layers",
     "cpg_ctx_run", "cpg_ctx_x", "cpg_ctx_topk", "cpg_ctx_profile", "cpg_ctx_phase_ms",
     "cpg_moe_apply_workspace_bytes", "cpg_moe_apply", "cpg_moe_apply_check", "cpg_moe_apply_profile",
+    "cpg_moe_apply_rows", "cpg_ep_unique_id", "cpg_ep_create", "cpg_ep_destroy", "cpg_ep_workspace_bytes",
+    "cpg_moe_ep", "cpg_moe_ep_check",
 ]
 
 
@@ -87,6 +89,13 @@ _SIGS = {
     "cpg_moe_apply": (_i, [_vp, _vp, _i, _vp, _vp, _vp, _vp, _sz, _vp]),
     "cpg_moe_apply_check": (_i, [_vp, _vp]),
     "cpg_moe_apply_profile": (_i, [_vp, _vp, _i, _vp, _vp, _vp, _vp, _sz, _vp, ctypes.POINTER(ctypes.c_float)]),
+    "cpg_moe_apply_rows": (_i, [_vp, _vp, _i, _vp, _vp, _vp, _vp, _sz, _vp]),
+    "cpg_ep_unique_id": (_i, [_vp]),
+    "cpg_ep_create": (_i, [_i, _i, _vp, ctypes.POINTER(_vp)]),
+    "cpg_ep_destroy": (None, [_vp]),
+    "cpg_ep_workspace_bytes": (_sz, [_vp, _vp, _i]),
+    "cpg_moe_ep": (_i, [_vp, _vp, _vp, _i, _vp, _vp, _vp, _vp, _sz, _vp]),
+    "cpg_moe_ep_check": (_i, [_vp, _vp]),
     "cpg_ctx_x": (_vp, [_vp]),
     "cpg_ctx_topk": (_vp, [_vp]),
     "cpg_ctx_profile": (_i, [_vp, _i]),

@@ -7,7 +7,9 @@
 //   k_apply_gather the token rows in that order as fp16 (the gate/up GEMM's tensor-TMA source)
 //   k_gemm_tc<0>   gate/up grouped GEMM on tcgen05, h = silu(g)·u
 //   k_gemm_tc<1>   down grouped GEMM on tcgen05, y per (token, slot)
-//   k_combine      mlp += sum_j wt_j·y_j in selection order
+//   k_apply_combine out (+)= sum_j wt_j·y_j over the valid slots, in selection order
+// Slots whose expert id is outside [0, n_experts) contribute nothing: an error for
+// cpg_moe_apply, empty slots (id -1) by design for cpg_moe_apply_rows (expert-parallel receive).
 #include "gemm_tc.cuh"
 
 namespace cpg {
@@ -15,12 +17,10 @@ namespace cpg {
 int layer_dims(const cpg_moe_layer *L, int *D, int *F, int *E, int *K);
 int layer_ptrs(const cpg_moe_layer *L, const uint8_t *const **ptrs, int *enc);
 int layer_weight_maps(const cpg_moe_layer *L, const void **maps);
-__global__ void k_combine(const float *__restrict__ x, const float *__restrict__ attn, int T, int D, int K,
-                          const float *__restrict__ wt, const float *__restrict__ y, float *mlp, float *x_out);
 
 constexpr int AP_BLOCK = 256;            // tokens per grouping block
 constexpr int AP_MAX_E = 256;
-constexpr int TC_BN_TOK = 128;           // token tile of the tcgen05 GEMM
+constexpr int TC_BN_TOK = 256;           // token tile of the tcgen05 GEMM
 
 struct ApplyWs {
     size_t status, n_active, act, act_ptr, blk_cnt, pairs, xs, h, y, total;
@@ -45,9 +45,9 @@ static ApplyWs apply_layout(int D, int F, int E, int K, int T) {
     return w;
 }
 
-// per-block expert counts, id validation
+// per-block expert counts, id validation (negative ids are empty slots when empty_ok)
 __global__ void __launch_bounds__(AP_BLOCK) k_apply_prep(int T, int E, int K, const int *__restrict__ idx,
-                                                          int *__restrict__ blk_cnt, int *status) {
+                                                          int *__restrict__ blk_cnt, int *status, int empty_ok) {
     __shared__ int s_cnt[AP_MAX_E];
     const int b = blockIdx.x, t0 = b * AP_BLOCK;
     for (int e = threadIdx.x; e < E; e += blockDim.x) s_cnt[e] = 0;
@@ -57,7 +57,7 @@ __global__ void __launch_bounds__(AP_BLOCK) k_apply_prep(int T, int E, int K, co
     for (int i = threadIdx.x; i < nt * K; i += blockDim.x) {
         const int e = idx[(size_t)t0 * K + i];
         if (e >= 0 && e < E) atomicAdd(&s_cnt[e], 1);
-        else atomicExch(status, ST_BAD_ITEM);
+        else if (!(empty_ok && e < 0)) atomicExch(status, ST_BAD_ITEM);
     }
     __syncthreads();
     for (int e = threadIdx.x; e < E; e += blockDim.x) blk_cnt[(size_t)b * E + e] = s_cnt[e];
@@ -68,7 +68,7 @@ __global__ void __launch_bounds__(AP_BLOCK) k_apply_prep(int T, int E, int K, co
 __global__ void __launch_bounds__(AP_BLOCK) k_apply_group(int T, int E, int K, const int *__restrict__ idx,
                                                            const int *__restrict__ blk_cnt, int nblk,
                                                            const uint8_t *const *ptrs, int *pairs, int4 *act,
-                                                           const uint8_t **act_ptr, int *n_active, float *y, int D) {
+                                                           const uint8_t **act_ptr, int *n_active) {
     __shared__ int s_base[AP_MAX_E], s_tot[AP_MAX_E], s_off[AP_MAX_E];
     __shared__ uint32_t s_mask[AP_MAX_E];
     const int b = blockIdx.x, t0 = b * AP_BLOCK, tid = threadIdx.x;
@@ -122,8 +122,6 @@ __global__ void __launch_bounds__(AP_BLOCK) k_apply_group(int T, int E, int K, c
                 if (e >= 0 && e < E) {
                     const int r = s_base[e] + __popc(s_mask[e] & ((1u << tl) - 1u));
                     pairs[s_off[e] + r] = slot;
-                } else {
-                    for (int k = 0; k < D; ++k) y[(size_t)slot * D + k] = 0.0f;   // contributes nothing
                 }
             }
         }
@@ -133,17 +131,24 @@ __global__ void __launch_bounds__(AP_BLOCK) k_apply_group(int T, int E, int K, c
     }
 }
 
-// xs[p] = fp16(xn[token of pair p]) for the valid pairs (one warp per row, 8 values per lane step)
-__global__ void __launch_bounds__(256) k_apply_gather(const float *__restrict__ xn, int D, int K,
-                                                       const int *__restrict__ pairs, const int4 *__restrict__ act,
-                                                       const int *__restrict__ n_active, __half *__restrict__ xs,
-                                                       int max_pairs) {
+// xs[p] = fp16(xn[token of pair p]) for the valid pairs (one warp per row, 8 values per lane
+// step); from fp16 rows xh instead when xn is null
+__global__ void __launch_bounds__(256) k_apply_gather(const float *__restrict__ xn, const __half *__restrict__ xh,
+                                                       int D, int K, const int *__restrict__ pairs,
+                                                       const int4 *__restrict__ act, const int *__restrict__ n_active,
+                                                       __half *__restrict__ xs, int max_pairs) {
     const int n_valid = act[*n_active].y;
     const int lane = threadIdx.x & 31;
     for (int p = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; p < n_valid && p < max_pairs;
          p += (gridDim.x * blockDim.x) >> 5) {
-        const float4 *src = reinterpret_cast<const float4 *>(xn + (size_t)(pairs[p] / K) * D);
+        const size_t row = (size_t)(pairs[p] / K) * D;
         uint4 *dst = reinterpret_cast<uint4 *>(xs + (size_t)p * D);
+        if (!xn) {
+            const uint4 *src16 = reinterpret_cast<const uint4 *>(xh + row);
+            for (int i = lane; i < D / 8; i += 32) dst[i] = src16[i];
+            continue;
+        }
+        const float4 *src = reinterpret_cast<const float4 *>(xn + row);
         for (int i = lane; i < D / 8; i += 32) {
             const float4 a = src[2 * i], b = src[2 * i + 1];
             const __half2 h0 = __floats2half2_rn(a.x, a.y), h1 = __floats2half2_rn(a.z, a.w);
@@ -151,6 +156,29 @@ __global__ void __launch_bounds__(256) k_apply_gather(const float *__restrict__ 
             dst[i] = make_uint4(*reinterpret_cast<const uint32_t *>(&h0), *reinterpret_cast<const uint32_t *>(&h1),
                                 *reinterpret_cast<const uint32_t *>(&h2), *reinterpret_cast<const uint32_t *>(&h3));
         }
+    }
+}
+
+// out[t] (+)= sum_j wt[t,j]·y[t*K+j] over slots with a valid id, in selection order with one
+// rounding per product and per sum (qwen3_moe.c:221); accumulate = 0 starts from zero.
+__global__ void __launch_bounds__(256) k_apply_combine(int T, int D, int K, int E, const int *__restrict__ idx,
+                                                        const float *__restrict__ wt, const float *__restrict__ y,
+                                                        float *out, int accumulate) {
+    const int n4 = T * D / 4;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += gridDim.x * blockDim.x) {
+        const int t = (i * 4) / D, k = i * 4 - t * D;
+        float4 acc = accumulate ? reinterpret_cast<const float4 *>(out)[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int j = 0; j < K; ++j) {
+            const int e = __ldg(idx + (size_t)t * K + j);
+            if (e < 0 || e >= E) continue;
+            const float w = __ldg(wt + (size_t)t * K + j);
+            const float4 v = __ldg(reinterpret_cast<const float4 *>(y + ((size_t)t * K + j) * D + k));
+            acc.x = __fadd_rn(acc.x, __fmul_rn(w, v.x));
+            acc.y = __fadd_rn(acc.y, __fmul_rn(w, v.y));
+            acc.z = __fadd_rn(acc.z, __fmul_rn(w, v.z));
+            acc.w = __fadd_rn(acc.w, __fmul_rn(w, v.w));
+        }
+        reinterpret_cast<float4 *>(out)[i] = acc;
     }
 }
 
@@ -164,10 +192,13 @@ extern "C" size_t cpg_moe_apply_workspace_bytes(const cpg_moe_layer *layer, int 
     return apply_layout(D, F, E, K, max_T).total;
 }
 
-// ev: null, or 5 events recorded around the sort, gate/up, down and combine phases
-static int apply_impl(const cpg_moe_layer *layer, const float *xn, int T, const int *topk_idx, const float *wt,
-                      float *mlp, void *ws, size_t ws_bytes, cudaStream_t s, cudaEvent_t *ev) {
-    CPG_REQUIRE(layer && xn && topk_idx && wt && mlp && ws, "cpg_moe_apply: null argument");
+// Input rows: xn (f32) or xh (fp16). empty_ok: negative ids are empty slots, not errors.
+// accumulate: mlp += the block output, else mlp = it. ev: null, or 5 events recorded around the
+// sort, gate/up, down and combine phases.
+static int apply_impl(const cpg_moe_layer *layer, const float *xn, const __half *xh, int T, const int *topk_idx,
+                      const float *wt, float *mlp, int accumulate, int empty_ok, void *ws, size_t ws_bytes,
+                      cudaStream_t s, cudaEvent_t *ev) {
+    CPG_REQUIRE(layer && (xn || xh) && topk_idx && wt && mlp && ws, "cpg_moe_apply: null argument");
     CPG_REQUIRE(T > 0, "cpg_moe_apply: T=%d", T);
     int D, F, E, K, enc;
     const uint8_t *const *ptrs;
@@ -179,22 +210,23 @@ static int apply_impl(const cpg_moe_layer *layer, const float *xn, int T, const 
     CPG_REQUIRE(F % 256 == 0 && D % 256 == 0, "cpg_moe_apply: d_exp %% 256 and d_model %% 256 must be 0");
     const ApplyWs W = apply_layout(D, F, E, K, T);
     CPG_REQUIRE(ws_bytes >= W.total, "cpg_moe_apply: workspace %zu < %zu bytes for T=%d", ws_bytes, W.total, T);
-    CPG_REQUIRE((((uintptr_t)xn | (uintptr_t)mlp | (uintptr_t)ws) & 15) == 0, "cpg_moe_apply: 16-byte alignment");
+    CPG_REQUIRE((((uintptr_t)xn | (uintptr_t)xh | (uintptr_t)mlp | (uintptr_t)ws) & 15) == 0,
+                "cpg_moe_apply: 16-byte alignment");
     uint8_t *w = (uint8_t *)ws;
     int *status = (int *)(w + W.status);
     const int nblk = (T + AP_BLOCK - 1) / AP_BLOCK;
     if (ev) CPG_CUDA(cudaEventRecord(ev[0], s));
-    k_apply_prep<<<nblk, AP_BLOCK, 0, s>>>(T, E, K, topk_idx, (int *)(w + W.blk_cnt), status);
+    k_apply_prep<<<nblk, AP_BLOCK, 0, s>>>(T, E, K, topk_idx, (int *)(w + W.blk_cnt), status, empty_ok);
     CPG_CUDA(cudaGetLastError());
     k_apply_group<<<nblk, AP_BLOCK, 0, s>>>(T, E, K, topk_idx, (const int *)(w + W.blk_cnt), nblk, ptrs,
                                             (int *)(w + W.pairs), (int4 *)(w + W.act), (const uint8_t **)(w + W.act_ptr),
-                                            (int *)(w + W.n_active), (float *)(w + W.y), D);
+                                            (int *)(w + W.n_active));
     CPG_CUDA(cudaGetLastError());
     {
         const int P = T * K;
         int ggrid = (P + 7) / 8;
         if (ggrid > sm_count() * 8) ggrid = sm_count() * 8;
-        k_apply_gather<<<ggrid, 256, 0, s>>>(xn, D, K, (const int *)(w + W.pairs), (const int4 *)(w + W.act),
+        k_apply_gather<<<ggrid, 256, 0, s>>>(xn, xh, D, K, (const int *)(w + W.pairs), (const int4 *)(w + W.act),
                                              (const int *)(w + W.n_active), (__half *)(w + W.xs), P);
         CPG_CUDA(cudaGetLastError());
     }
@@ -219,7 +251,7 @@ static int apply_impl(const cpg_moe_layer *layer, const float *xn, int T, const 
     const int n4 = T * D / 4;
     int cgrid = (n4 + 255) / 256;
     if (cgrid > sm_count() * 8) cgrid = sm_count() * 8;
-    k_combine<<<cgrid, 256, 0, s>>>(nullptr, nullptr, T, D, K, wt, (const float *)(w + W.y), mlp, nullptr);
+    k_apply_combine<<<cgrid, 256, 0, s>>>(T, D, K, E, topk_idx, wt, (const float *)(w + W.y), mlp, accumulate);
     CPG_CUDA(cudaGetLastError());
     if (ev) CPG_CUDA(cudaEventRecord(ev[4], s));
     return CPG_OK;
@@ -227,7 +259,14 @@ static int apply_impl(const cpg_moe_layer *layer, const float *xn, int T, const 
 
 extern "C" int cpg_moe_apply(const cpg_moe_layer *layer, const float *xn, int T, const int *topk_idx,
                              const float *wt, float *mlp, void *ws, size_t ws_bytes, void *stream) {
-    return apply_impl(layer, xn, T, topk_idx, wt, mlp, ws, ws_bytes, (cudaStream_t)stream, nullptr);
+    return apply_impl(layer, xn, nullptr, T, topk_idx, wt, mlp, 1, 0, ws, ws_bytes, (cudaStream_t)stream, nullptr);
+}
+
+extern "C" int cpg_moe_apply_rows(const cpg_moe_layer *layer, const void *rows_f16, int R, const int *slot_expert,
+                                  const float *slot_wt, float *out, void *ws, size_t ws_bytes, void *stream) {
+    CPG_REQUIRE(rows_f16, "cpg_moe_apply_rows: null rows");
+    return apply_impl(layer, nullptr, (const __half *)rows_f16, R, slot_expert, slot_wt, out, 0, 1, ws, ws_bytes,
+                      (cudaStream_t)stream, nullptr);
 }
 
 extern "C" int cpg_moe_apply_profile(const cpg_moe_layer *layer, const float *xn, int T, const int *topk_idx,
@@ -242,7 +281,7 @@ extern "C" int cpg_moe_apply_profile(const cpg_moe_layer *layer, const float *xn
             return cuda_fail(ce, "cpg_moe_apply_profile: event");
         }
     }
-    int rc = apply_impl(layer, xn, T, topk_idx, wt, mlp, ws, ws_bytes, (cudaStream_t)stream, ev);
+    int rc = apply_impl(layer, xn, nullptr, T, topk_idx, wt, mlp, 1, 0, ws, ws_bytes, (cudaStream_t)stream, ev);
     if (rc == CPG_OK) {
         const cudaError_t ce = cudaEventSynchronize(ev[4]);
         if (ce != cudaSuccess) rc = cuda_fail(ce, "cpg_moe_apply_profile: synchronize");

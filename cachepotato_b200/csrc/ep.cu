@@ -1,0 +1,338 @@
+// ep.cu — expert parallelism for batched MoE layers across the GPUs of one node.
+//
+// The reference engine has no counterpart (it runs the expert loop token by token on one host,
+// engine/blocks/qwen3_moe.c:199-222); the layout follows the partitioning the batched configs
+// call for: rank r owns experts [r·E_l, (r+1)·E_l) (E_l = n_experts of its local layer) and T
+// tokens of the batch (the same T on every rank). Per layer:
+//   k_ep_plan       per owner: which local tokens have a slot there, their position in the send
+//                   buffer (tokens ascending), and per-slot metadata (local expert id or -1, weight)
+//   k_ep_pack_rows  each token's normalised row as fp16, once per owner that needs it
+//   NCCL            send/recv of rows + metadata to every owner (fixed capacity of T rows per
+//                   peer, so no counts round trip and no host synchronisation)
+//   apply_rows      the owner's tcgen05 grouped GEMMs over all received rows; each row's slots
+//                   combined in selection order into one f32 partial row
+//   NCCL            the partial rows back to their sources
+//   k_ep_combine    mlp[t] += the partial rows of t's owners, ascending owner rank
+// NCCL comes from the process (a torch process already holds it) or from the system library,
+// resolved at run time, so the library itself links no NCCL.
+#include <dlfcn.h>
+#include <nccl.h>
+
+#include <mutex>
+
+#include "common.cuh"
+
+namespace cpg {
+
+int layer_dims(const cpg_moe_layer *L, int *D, int *F, int *E, int *K);
+
+struct NcclApi {
+    decltype(&ncclGetUniqueId) get_unique_id = nullptr;
+    decltype(&ncclCommInitRank) init_rank = nullptr;
+    decltype(&ncclCommDestroy) destroy = nullptr;
+    decltype(&ncclGroupStart) group_start = nullptr;
+    decltype(&ncclGroupEnd) group_end = nullptr;
+    decltype(&ncclSend) send = nullptr;
+    decltype(&ncclRecv) recv = nullptr;
+    decltype(&ncclGetErrorString) err_str = nullptr;
+    bool ok = false;
+};
+
+static const NcclApi &nccl() {
+    static NcclApi api;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+        if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+        if (!h) return;
+        api.get_unique_id = (decltype(api.get_unique_id))dlsym(h, "ncclGetUniqueId");
+        api.init_rank = (decltype(api.init_rank))dlsym(h, "ncclCommInitRank");
+        api.destroy = (decltype(api.destroy))dlsym(h, "ncclCommDestroy");
+        api.group_start = (decltype(api.group_start))dlsym(h, "ncclGroupStart");
+        api.group_end = (decltype(api.group_end))dlsym(h, "ncclGroupEnd");
+        api.send = (decltype(api.send))dlsym(h, "ncclSend");
+        api.recv = (decltype(api.recv))dlsym(h, "ncclRecv");
+        api.err_str = (decltype(api.err_str))dlsym(h, "ncclGetErrorString");
+        api.ok = api.get_unique_id && api.init_rank && api.destroy && api.group_start && api.group_end && api.send &&
+                 api.recv && api.err_str;
+    });
+    return api;
+}
+
+#define CPG_NCCL(call)                                                                            \
+    do {                                                                                          \
+        const ncclResult_t r_ = (call);                                                           \
+        if (r_ != ncclSuccess) {                                                                  \
+            ::cpg::set_error("%s: %s", #call, nccl().err_str(r_));                                \
+            return CPG_ENCCL;                                                                     \
+        }                                                                                         \
+    } while (0)
+
+constexpr int EP_PLAN_THREADS = 1024;
+constexpr int EP_MAX_K = 32;
+
+struct EpWs {
+    size_t status, send_rows, send_ide, send_wt, recv_rows, recv_ide, recv_wt, pos, out_rows, back, apply, total;
+};
+
+static size_t al(size_t v) { return (v + 255) / 256 * 256; }
+
+static EpWs ep_layout(int G, int T, int D, int K, size_t apply_bytes) {
+    EpWs w{};
+    size_t o = 0;
+    const size_t R = (size_t)G * T;
+    w.status = o; o = al(o + 16 * sizeof(int));
+    w.send_rows = o; o = al(o + R * D * sizeof(__half));
+    w.send_ide = o; o = al(o + R * K * sizeof(int));
+    w.send_wt = o; o = al(o + R * K * sizeof(float));
+    w.recv_rows = o; o = al(o + R * D * sizeof(__half));
+    w.recv_ide = o; o = al(o + R * K * sizeof(int));
+    w.recv_wt = o; o = al(o + R * K * sizeof(float));
+    w.pos = o; o = al(o + (size_t)T * G * sizeof(int));
+    w.out_rows = o; o = al(o + R * D * sizeof(float));
+    w.back = o; o = al(o + R * D * sizeof(float));
+    w.apply = o; o = al(o + apply_bytes);
+    w.total = o;
+    return w;
+}
+
+// Block-wide exclusive scan of 0/1 flags (EP_PLAN_THREADS threads); returns the prefix of this
+// thread and writes the block total to *total.
+__device__ __forceinline__ int block_excl_scan(int flag, int *s_warp, int *total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const unsigned ball = __ballot_sync(0xffffffffu, flag);
+    const int in_warp = __popc(ball & ((1u << lane) - 1u));
+    if (lane == 0) s_warp[warp] = __popc(ball);
+    __syncthreads();
+    if (warp == 0) {
+        int v = lane < nw ? s_warp[lane] : 0;
+        int inc = v;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int n = __shfl_up_sync(0xffffffffu, inc, o);
+            if (lane >= o) inc += n;
+        }
+        if (lane < nw) s_warp[lane] = inc - v;
+        if (lane == 31) s_warp[32] = inc;
+    }
+    __syncthreads();
+    const int r = s_warp[warp] + in_warp;
+    *total = s_warp[32];
+    __syncthreads();
+    return r;
+}
+
+// One block per owner rank p: send positions (tokens ascending) and per-slot metadata.
+__global__ void __launch_bounds__(EP_PLAN_THREADS) k_ep_plan(int T, int K, int G, int E_l, const int *__restrict__ idx,
+                                                              const float *__restrict__ wt, int *__restrict__ pos,
+                                                              int *__restrict__ send_ide, float *__restrict__ send_wt,
+                                                              int *status) {
+    __shared__ int s_warp[33];
+    const int p = blockIdx.x;
+    const int E_tot = E_l * G;
+    int base = 0;
+    for (int t0 = 0; t0 < T; t0 += blockDim.x) {
+        const int t = t0 + threadIdx.x;
+        int flag = 0;
+        if (t < T)
+            for (int j = 0; j < K; ++j) {
+                const int e = idx[(size_t)t * K + j];
+                if (e < 0 || e >= E_tot) {
+                    if (p == 0) atomicExch(status, ST_BAD_ITEM);
+                    continue;
+                }
+                flag |= (e / E_l == p);
+            }
+        int tot;
+        const int r = block_excl_scan(flag, s_warp, &tot);
+        if (t < T) {
+            const int q = base + r;
+            pos[(size_t)t * G + p] = flag ? q : -1;
+            if (flag) {
+                const size_t m = ((size_t)p * T + q) * K;
+                for (int j = 0; j < K; ++j) {
+                    const int e = idx[(size_t)t * K + j];
+                    const bool mine = e >= 0 && e < E_tot && e / E_l == p;
+                    send_ide[m + j] = mine ? e - p * E_l : -1;
+                    send_wt[m + j] = mine ? wt[(size_t)t * K + j] : 0.0f;
+                }
+            }
+        }
+        base += tot;
+    }
+    // capacity rows past the last token carry no slots
+    for (size_t i = (size_t)base * K + threadIdx.x; i < (size_t)T * K; i += blockDim.x) {
+        send_ide[(size_t)p * T * K + i] = -1;
+        send_wt[(size_t)p * T * K + i] = 0.0f;
+    }
+}
+
+// One warp per token: its row as fp16 into the send buffer of every owner that needs it.
+__global__ void __launch_bounds__(256) k_ep_pack_rows(int T, int D, int G, const float *__restrict__ xn,
+                                                       const int *__restrict__ pos, __half *__restrict__ send_rows) {
+    const int lane = threadIdx.x & 31;
+    for (int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; t < T; t += (gridDim.x * blockDim.x) >> 5) {
+        const float4 *src = reinterpret_cast<const float4 *>(xn + (size_t)t * D);
+        for (int i = lane; i < D / 8; i += 32) {
+            const float4 a = src[2 * i], b = src[2 * i + 1];
+            const __half2 h0 = __floats2half2_rn(a.x, a.y), h1 = __floats2half2_rn(a.z, a.w);
+            const __half2 h2 = __floats2half2_rn(b.x, b.y), h3 = __floats2half2_rn(b.z, b.w);
+            const uint4 v = make_uint4(*reinterpret_cast<const uint32_t *>(&h0), *reinterpret_cast<const uint32_t *>(&h1),
+                                       *reinterpret_cast<const uint32_t *>(&h2), *reinterpret_cast<const uint32_t *>(&h3));
+            for (int p = 0; p < G; ++p) {
+                const int q = __ldg(pos + (size_t)t * G + p);
+                if (q >= 0) reinterpret_cast<uint4 *>(send_rows + ((size_t)p * T + q) * D)[i] = v;
+            }
+        }
+    }
+}
+
+// mlp[t] += partial rows of t's owners in ascending owner rank (one rounding per add).
+__global__ void __launch_bounds__(256) k_ep_combine(int T, int D, int G, const int *__restrict__ pos,
+                                                     const float *__restrict__ back, float *mlp) {
+    const int n4 = T * D / 4;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += gridDim.x * blockDim.x) {
+        const int t = (i * 4) / D, k = i * 4 - t * D;
+        float4 acc = reinterpret_cast<const float4 *>(mlp)[i];
+        for (int p = 0; p < G; ++p) {
+            const int q = __ldg(pos + (size_t)t * G + p);
+            if (q < 0) continue;
+            const float4 v = __ldg(reinterpret_cast<const float4 *>(back + ((size_t)p * T + q) * D + k));
+            acc.x = __fadd_rn(acc.x, v.x);
+            acc.y = __fadd_rn(acc.y, v.y);
+            acc.z = __fadd_rn(acc.z, v.z);
+            acc.w = __fadd_rn(acc.w, v.w);
+        }
+        reinterpret_cast<float4 *>(mlp)[i] = acc;
+    }
+}
+
+}  // namespace cpg
+
+struct cpg_ep {
+    int G, rank, device;
+    ncclComm_t comm;
+};
+
+using namespace cpg;
+
+extern "C" int cpg_ep_unique_id(void *out) {
+    CPG_REQUIRE(out, "cpg_ep_unique_id: null output");
+    if (!nccl().ok) {
+        set_error("NCCL is not available (libnccl.so.2 not found in the process or on the library path)");
+        return CPG_ENCCL;
+    }
+    ncclUniqueId id;
+    CPG_NCCL(nccl().get_unique_id(&id));
+    memcpy(out, &id, sizeof(id));
+    return CPG_OK;
+}
+
+extern "C" int cpg_ep_create(int nranks, int rank, const void *unique_id, cpg_ep **out) {
+    CPG_REQUIRE(out && unique_id, "cpg_ep_create: null argument");
+    *out = nullptr;
+    CPG_REQUIRE(nranks >= 1 && rank >= 0 && rank < nranks, "cpg_ep_create: rank %d of %d", rank, nranks);
+    if (!nccl().ok) {
+        set_error("NCCL is not available (libnccl.so.2 not found in the process or on the library path)");
+        return CPG_ENCCL;
+    }
+    ncclUniqueId id;
+    memcpy(&id, unique_id, sizeof(id));
+    cpg_ep *ep = new cpg_ep();
+    ep->G = nranks;
+    ep->rank = rank;
+    cudaGetDevice(&ep->device);
+    const ncclResult_t r = nccl().init_rank(&ep->comm, nranks, id, rank);
+    if (r != ncclSuccess) {
+        set_error("ncclCommInitRank: %s", nccl().err_str(r));
+        delete ep;
+        return CPG_ENCCL;
+    }
+    *out = ep;
+    return CPG_OK;
+}
+
+extern "C" void cpg_ep_destroy(cpg_ep *ep) {
+    if (!ep) return;
+    nccl().destroy(ep->comm);
+    delete ep;
+}
+
+extern "C" size_t cpg_ep_workspace_bytes(const cpg_ep *ep, const cpg_moe_layer *local_layer, int T) {
+    int D, F, E, K;
+    if (!ep || !local_layer || T <= 0 || layer_dims(local_layer, &D, &F, &E, &K) != CPG_OK) return 0;
+    return ep_layout(ep->G, T, D, K, cpg_moe_apply_workspace_bytes(local_layer, ep->G * T)).total;
+}
+
+extern "C" int cpg_moe_ep(cpg_ep *ep, const cpg_moe_layer *local_layer, const float *xn, int T, const int *topk_idx,
+                          const float *wt, float *mlp, void *ws, size_t ws_bytes, void *stream) {
+    CPG_REQUIRE(ep && local_layer && xn && topk_idx && wt && mlp && ws, "cpg_moe_ep: null argument");
+    CPG_REQUIRE(T > 0, "cpg_moe_ep: T=%d", T);
+    int D, F, E_l, K;
+    int rc = layer_dims(local_layer, &D, &F, &E_l, &K);
+    if (rc) return rc;
+    CPG_REQUIRE(K <= EP_MAX_K, "cpg_moe_ep: topk %d > %d", K, EP_MAX_K);
+    const int G = ep->G;
+    const size_t apply_bytes = cpg_moe_apply_workspace_bytes(local_layer, G * T);
+    const EpWs W = ep_layout(G, T, D, K, apply_bytes);
+    CPG_REQUIRE(ws_bytes >= W.total, "cpg_moe_ep: workspace %zu < %zu bytes", ws_bytes, W.total);
+    CPG_REQUIRE((((uintptr_t)xn | (uintptr_t)mlp | (uintptr_t)ws) & 15) == 0, "cpg_moe_ep: 16-byte alignment");
+    cudaStream_t s = (cudaStream_t)stream;
+    uint8_t *w = (uint8_t *)ws;
+    int *status = (int *)(w + W.status);
+    CPG_CUDA(cudaMemsetAsync(status, 0, 16 * sizeof(int), s));
+    int *pos = (int *)(w + W.pos);
+    k_ep_plan<<<G, EP_PLAN_THREADS, 0, s>>>(T, K, G, E_l, topk_idx, wt, pos, (int *)(w + W.send_ide),
+                                            (float *)(w + W.send_wt), status);
+    CPG_CUDA(cudaGetLastError());
+    int pgrid = (T + 7) / 8;
+    if (pgrid > sm_count() * 8) pgrid = sm_count() * 8;
+    k_ep_pack_rows<<<pgrid, 256, 0, s>>>(T, D, G, xn, pos, (__half *)(w + W.send_rows));
+    CPG_CUDA(cudaGetLastError());
+
+    // dispatch: rows + metadata to every owner (this rank's own share goes through NCCL too)
+    const size_t row_b = (size_t)T * D * sizeof(__half), meta_n = (size_t)T * K;
+    const NcclApi &n = nccl();
+    CPG_NCCL(n.group_start());
+    for (int p = 0; p < G; ++p) {
+        CPG_NCCL(n.send(w + W.send_rows + p * row_b, row_b, ncclUint8, p, ep->comm, s));
+        CPG_NCCL(n.send((int *)(w + W.send_ide) + p * meta_n, meta_n, ncclInt32, p, ep->comm, s));
+        CPG_NCCL(n.send((float *)(w + W.send_wt) + p * meta_n, meta_n, ncclFloat32, p, ep->comm, s));
+        CPG_NCCL(n.recv(w + W.recv_rows + p * row_b, row_b, ncclUint8, p, ep->comm, s));
+        CPG_NCCL(n.recv((int *)(w + W.recv_ide) + p * meta_n, meta_n, ncclInt32, p, ep->comm, s));
+        CPG_NCCL(n.recv((float *)(w + W.recv_wt) + p * meta_n, meta_n, ncclFloat32, p, ep->comm, s));
+    }
+    CPG_NCCL(n.group_end());
+
+    // the owner's experts over every received row (empty slots are -1)
+    rc = cpg_moe_apply_rows(local_layer, w + W.recv_rows, G * T, (const int *)(w + W.recv_ide),
+                            (const float *)(w + W.recv_wt), (float *)(w + W.out_rows), w + W.apply, apply_bytes, s);
+    if (rc) return rc;
+
+    // return: one partial row per (token, owner)
+    const size_t out_n = (size_t)T * D;
+    CPG_NCCL(n.group_start());
+    for (int p = 0; p < G; ++p) {
+        CPG_NCCL(n.send((float *)(w + W.out_rows) + p * out_n, out_n, ncclFloat32, p, ep->comm, s));
+        CPG_NCCL(n.recv((float *)(w + W.back) + p * out_n, out_n, ncclFloat32, p, ep->comm, s));
+    }
+    CPG_NCCL(n.group_end());
+
+    int cgrid = (T * D / 4 + 255) / 256;
+    if (cgrid > sm_count() * 8) cgrid = sm_count() * 8;
+    k_ep_combine<<<cgrid, 256, 0, s>>>(T, D, G, pos, (const float *)(w + W.back), mlp);
+    CPG_CUDA(cudaGetLastError());
+    return CPG_OK;
+}
+
+extern "C" int cpg_moe_ep_check(const void *ws, void *stream) {
+    CPG_REQUIRE(ws, "cpg_moe_ep_check: null workspace");
+    int st = 0;
+    CPG_CUDA(cudaStreamSynchronize((cudaStream_t)stream));
+    CPG_CUDA(cudaMemcpy(&st, ws, sizeof(int), cudaMemcpyDeviceToHost));
+    if (st == ST_BAD_ITEM) {
+        set_error("cpg_moe_ep: expert id outside [0, n_ranks * local experts) (those slots contributed zero)");
+        return CPG_EINVAL;
+    }
+    return CPG_OK;
+}

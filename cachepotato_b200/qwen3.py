@@ -214,6 +214,79 @@ def moe_apply(layer: "MoELayer", xn, topk_idx, wt, *, ws=None, mlp=None, stream=
     return mlp
 
 
+def moe_apply_rows(layer: "MoELayer", rows_f16, slot_expert, slot_wt, *, ws=None, out=None, stream=None,
+                   check_status=True):
+    """cpg_moe_apply_rows: out[r] = sum over the valid slots (id >= 0) of wt * expert(rows[r])."""
+    torch = _torch()
+    rows = rows_f16.contiguous()
+    R = rows.shape[0]
+    ide = slot_expert.to(torch.int32).contiguous()
+    wt = slot_wt.to(torch.float32).contiguous()
+    if ws is None:
+        ws = torch.empty(int(lib().cpg_moe_apply_workspace_bytes(layer.handle, R)), dtype=torch.uint8,
+                         device=rows.device)
+    if out is None:
+        out = torch.empty((R, layer.d_model), dtype=torch.float32, device=rows.device)
+    sp = _stream_ptr(stream)
+    check(lib().cpg_moe_apply_rows(layer.handle, rows.data_ptr(), R, ide.data_ptr(), wt.data_ptr(), out.data_ptr(),
+                                   ws.data_ptr(), ws.numel(), sp))
+    if check_status:
+        check(lib().cpg_moe_apply_check(ws.data_ptr(), sp))
+    return out
+
+
+class ExpertParallel:
+    """cpg_ep: one rank of an expert-parallel group (one process per GPU). Rank r's local layer
+    holds experts [r*E_l, (r+1)*E_l) of the full layer; every rank passes the same T."""
+
+    @staticmethod
+    def unique_id() -> bytes:
+        buf = ctypes.create_string_buffer(128)
+        check(lib().cpg_ep_unique_id(buf))
+        return buf.raw
+
+    def __init__(self, nranks: int, rank: int, uid: bytes):
+        assert len(uid) == 128
+        h = ctypes.c_void_p()
+        check(lib().cpg_ep_create(nranks, rank, ctypes.create_string_buffer(uid, 128), ctypes.byref(h)))
+        self.handle, self.nranks, self.rank = h, nranks, rank
+
+    def workspace(self, local_layer: "MoELayer", T: int):
+        torch = _torch()
+        return torch.empty(int(lib().cpg_ep_workspace_bytes(self.handle, local_layer.handle, T)), dtype=torch.uint8,
+                           device="cuda")
+
+    def forward(self, local_layer: "MoELayer", xn, topk_idx, wt, *, mlp=None, ws=None, stream=None,
+                check_status=True):
+        """mlp += the MoE block over this rank's T tokens (global expert ids in topk_idx)."""
+        torch = _torch()
+        xn = xn.contiguous()
+        T = xn.shape[0]
+        idx = topk_idx.to(torch.int32).contiguous()
+        wt = wt.to(torch.float32).contiguous()
+        if ws is None:
+            ws = self.workspace(local_layer, T)
+        if mlp is None:
+            mlp = torch.zeros((T, local_layer.d_model), dtype=torch.float32, device=xn.device)
+        sp = _stream_ptr(stream)
+        check(lib().cpg_moe_ep(self.handle, local_layer.handle, xn.data_ptr(), T, idx.data_ptr(), wt.data_ptr(),
+                               mlp.data_ptr(), ws.data_ptr(), ws.numel(), sp))
+        if check_status:
+            check(lib().cpg_moe_ep_check(ws.data_ptr(), sp))
+        return mlp
+
+    def close(self) -> None:
+        if self.handle is not None and self.handle.value:
+            lib().cpg_ep_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 class DecodeContext:
     """cpg_ctx: the host-buffer decode loop (run_layers' MoE half, cachepotato.c:149-166)."""
 

@@ -163,6 +163,35 @@ int cpg_moe_apply_check(const void *ws, void *stream);
 int cpg_moe_apply_profile(const cpg_moe_layer *layer, const float *xn, int T, const int *topk_idx,
                           const float *wt, float *mlp, void *ws, size_t ws_bytes, void *stream,
                           float *phase_ms);
+/* The same experts over R fp16 rows (R, d_model) with per-row slot lists: slot_expert (R, topk)
+   holds a local expert id or -1 for an empty slot, slot_wt (R, topk) its weight. out (R, d_model)
+   f32 is overwritten with sum over the row's valid slots of wt·expert(row), in slot order. This
+   is the receive side of cpg_moe_ep; workspace: cpg_moe_apply_workspace_bytes(layer, R). */
+int cpg_moe_apply_rows(const cpg_moe_layer *layer, const void *rows_f16, int R, const int *slot_expert,
+                       const float *slot_wt, float *out, void *ws, size_t ws_bytes, void *stream);
+
+/* ============================================================== expert parallelism (NCCL)
+ * Batched MoE layers with the experts sharded across the GPUs of one node: rank r owns experts
+ * [r·E_l, (r+1)·E_l), where E_l = n_experts of the local layer it passes, and T tokens of the
+ * batch (the same T on every rank). No counterpart in the reference (single-host engine).
+ * One process per GPU; NCCL is resolved at run time from the process or the system library.
+ * cpg_ep_unique_id on one rank, shared with the others by the caller (128 bytes), then
+ * cpg_ep_create on every rank with the device current. */
+typedef struct cpg_ep cpg_ep;
+int cpg_ep_unique_id(void *out128);
+int cpg_ep_create(int nranks, int rank, const void *unique_id128, cpg_ep **out);
+void cpg_ep_destroy(cpg_ep *ep);
+size_t cpg_ep_workspace_bytes(const cpg_ep *ep, const cpg_moe_layer *local_layer, int T);
+/* mlp[t] += sum_j wt[t,j] · expert_{topk_idx[t,j]}(xn[t]) with global expert ids, the experts
+ * computed on their owners: each token's row travels once per owner (fp16), each owner returns
+ * one f32 row per token combining that token's slots on it in slot order, and the source adds
+ * the owners' rows in ascending rank. Collective: every rank calls it in the same order.
+ * Returns CPG_ENCCL on an NCCL error. */
+int cpg_moe_ep(cpg_ep *ep, const cpg_moe_layer *local_layer, const float *xn, int T, const int *topk_idx,
+               const float *wt, float *mlp, void *ws, size_t ws_bytes, void *stream);
+/* Synchronise; CPG_EINVAL if an expert id was outside [0, nranks·E_l) (those slots contributed
+   zero). */
+int cpg_moe_ep_check(const void *ws, void *stream);
 
 /* ============================================================== decode loop (host buffers)
  * A context owns a stream, a workspace and device activation buffers on one device. */

@@ -266,3 +266,16 @@ class SynthLayer:
     def expert_matrix(self, e: int, kind: int) -> np.ndarray:
         o = e * self.region_bytes + kind * self.mat_bytes
         return self.blob[o:o + self.mat_bytes]
+
+    def shard(self, r: int, G: int) -> "SynthLayer":
+        """Experts [r*E/G, (r+1)*E/G) as a layer of their own (the local layer of rank r of an
+        expert-parallel group); the blob is a view of this layer's."""
+        assert self.n_experts % G == 0
+        E_l = self.n_experts // G
+        sub = object.__new__(SynthLayer)
+        sub.__dict__.update(self.__dict__)
+        sub.n_experts = E_l
+        sub.wgate = np.ascontiguousarray(self.wgate[r * E_l:(r + 1) * E_l])
+        sub.blob = self.blob[r * E_l * self.region_bytes:(r + 1) * E_l * self.region_bytes]
+        sub._ptrs = None
+        return sub
