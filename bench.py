@@ -16,6 +16,9 @@ layers (router, experts, combine, residual), weights resident in HBM.
   decode_q8_batch1  configs[0]: one token through 48 stacked layers with Q8_0 experts (plain
           N(0,0.02) router), tok/s and HBM GB/s against the measured copy bandwidth, with the
           reference engine's time on the same workload (bounded sample) beside it
+  expert_parallel  configs[4]: 2048 tokens (2048/N per rank) through the 48 stacked layers with
+          the 128 experts sharded 128/N per GPU (cpg_moe_ep: NCCL dispatch and combine), uniform
+          top-8 routing; tok/s, ms per layer, and the binding roof (HBM, tensor or NVLink)
   prefill   configs[3]: 4096 Zipf(1.2)-routed tokens through one Q4_0 MoE block per step on the
           tcgen05 grouped GEMM (cpg_moe_apply), tok/s and TFLOP/s, roofline of the gate/up GEMM
           against the measured tensor peak
@@ -63,6 +66,7 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--prefill-tokens", type=int, default=4096, help="0 skips the prefill section")
     ap.add_argument("--no-q8", action="store_true", help="skip the Q8 batch-1 section")
+    ap.add_argument("--ep-tokens", type=int, default=2048, help="0 skips the expert-parallel section")
     return ap.parse_args()
 
 
@@ -179,6 +183,7 @@ def build_stack(torch, L, T, zipf, seed, lib, Q):
             b = lib.cpg_store_region_get(r_ex[e])
             ptrs += [b, b + MAT_BYTES, b + 2 * MAT_BYTES]
         layer = Q.MoELayer(ln2, wg, ENC_Q4, D, F, E, K, blob=None, expert_ptrs=ptrs)
+        layer.ptr_list = ptrs
         out = layer.forward(x)
         stats.append(load_stats(out.topk_idx.cpu().numpy(), E))
         x = out.x_out
@@ -276,15 +281,19 @@ def run_ours(args, rank, world, torch, dist):
     q8 = None if args.no_q8 else q8_batch1_bench(args, torch, lib, Q, barrier)
     ms_q8 = q8.pop("_ms") if q8 else 0.0
 
+    # ---- expert parallelism across the ranks (a collective: every rank takes part)
+    ep = ep_bench(args, layers, torch, lib, Q, dist, rank, world, barrier) if args.ep_tokens > 0 else None
+    ms_ep = ep.pop("_ms") if ep else 0.0
+
     # ---- prefill: Zipf(1.2)-routed tokens through one MoE block per step
     pf = prefill_bench(args, layers, torch, lib, Q, s, barrier) if args.prefill_tokens > 0 else None
     ms_pf = pf.pop("_ms") if pf else 0.0
 
     # max over ranks
-    t = torch.tensor([ms, ms_e2e, ms_b1, ms_pf, ms_q8], dtype=torch.float64, device="cuda")
+    t = torch.tensor([ms, ms_e2e, ms_b1, ms_pf, ms_q8, ms_ep], dtype=torch.float64, device="cuda")
     if dist is not None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms, ms_e2e, ms_b1, ms_pf, ms_q8 = (float(v) for v in t.tolist())
+    ms, ms_e2e, ms_b1, ms_pf, ms_q8, ms_ep = (float(v) for v in t.tolist())
     if rank != 0:
         return None
 
@@ -334,6 +343,17 @@ def run_ours(args, rank, world, torch, dist):
         q8["hbm_gbs"] = round(q8["bytes_per_step"] / (per * 1e-3) / 1e9, 1)
         q8["frac"] = round(q8["hbm_gbs"] / hbm, 4)
         res["decode_q8_batch1"] = q8
+    if ep:
+        per_layer = ms_ep / args.steps / L
+        ep["value"] = round(args.ep_tokens * args.steps / (ms_ep * 1e-3), 1)
+        ep["ms_per_step"] = round(ms_ep / args.steps, 4)
+        ep["ms_per_layer"] = round(per_layer, 5)
+        roof = ep.pop("_roof_ms")
+        bind = max(roof, key=roof.get)
+        ep["roofline"] = {"bound": bind, "roof_ms_per_layer": {k: round(v, 5) for k, v in roof.items()},
+                          "frac": round(roof[bind] / per_layer, 4),
+                          "peaks": {"hbm_gbs": hbm, "tensor_tflops": tensor_peak()[0], "nvlink_gbs": 770.0}}
+        res["expert_parallel"] = ep
     if pf:
         pf["value"] = round(world * args.prefill_tokens * args.steps / (ms_pf * 1e-3), 1)
         pf["ms_per_step"] = round(ms_pf / args.steps, 4)
@@ -385,6 +405,71 @@ def q8_batch1_bench(args, torch, lib, Q, barrier):
             "bytes_per_step": L * (LN_BYTES + ROUTER_BYTES + K * 3 * MAT_BYTES_Q8 + 2 * D * 4),
             "config": {"workload": f"configs[0]: decode batch 1 through {L} stacked Q8_0 MoE layers "
                                    "(plain N(0,0.02) f32 router)", "expert_encoding": "Q8_0"}}
+
+
+def ep_bench(args, layers, torch, lib, Q, dist, rank, world, barrier):
+    """configs[4]: args.ep_tokens tokens split evenly over the ranks go through the stacked layers;
+    rank r holds experts [r*128/N, (r+1)*128/N) of every layer (pointers into its region store)
+    and runs x += MoE(x) per layer with cpg_moe_ep (NCCL dispatch of fp16 rows to the expert
+    owners, tcgen05 experts there, f32 partial rows back). Routing: 8 distinct experts per token
+    drawn uniformly (seeded per layer), weights uniform in [0.1, 1.1) renormalised."""
+    G = world
+    assert E % G == 0 and args.ep_tokens % G == 0
+    T, E_l, L = args.ep_tokens // G, E // G, len(layers)
+    ln2 = torch.ones(D, device="cuda")
+    wg = torch.zeros((E_l, D), device="cuda")
+    local = [Q.MoELayer(ln2, wg, ENC_Q4, D, F, E_l, K, blob=None,
+                        expert_ptrs=l.ptr_list[rank * E_l * 3:(rank + 1) * E_l * 3]) for l in layers]
+    idx_l, wt_l, remote_rows = [], [], 0
+    for l in range(L):
+        rng = np.random.default_rng(args.seed * 7 + l)
+        idx = np.argsort(rng.random((args.ep_tokens, E)), axis=1)[:, :K].astype(np.int32)
+        wt = rng.random((args.ep_tokens, K)).astype(np.float32) + 0.1
+        wt /= wt.sum(1, keepdims=True)
+        mine = slice(rank * T, (rank + 1) * T)
+        idx_l.append(torch.from_numpy(idx[mine].copy()).cuda())
+        wt_l.append(torch.from_numpy(wt[mine].copy()).cuda())
+        owners = idx[mine] // E_l                       # distinct remote owners per token
+        remote_rows += sum(len(set(o.tolist()) - {rank}) for o in owners)
+    uid = [Q.ExpertParallel.unique_id() if rank == 0 else None]
+    if dist is not None:
+        dist.broadcast_object_list(uid, src=0)
+    ep = Q.ExpertParallel(G, rank, uid[0])
+    ws = ep.workspace(local[0], T)
+    g = torch.Generator(device="cuda").manual_seed(args.seed * 11 + rank)
+    x0 = torch.randn((T, D), generator=g, device="cuda")
+    x = x0.clone()
+
+    def step():
+        x.copy_(x0)
+        for l in range(L):
+            ep.forward(local[l], x, idx_l[l], wt_l[l], mlp=x, ws=ws, check_status=False)
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    Q.check(lib.cpg_moe_ep_check(ws.data_ptr(), None))
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        step()
+    e1.record()
+    barrier()
+    ms = e0.elapsed_time(e1)
+    Q.check(lib.cpg_moe_ep_check(ws.data_ptr(), None))
+    ep.close()
+    pairs = args.ep_tokens * K / G                      # per GPU, uniform routing
+    link_bytes = remote_rows / L * D * (2 + 4)          # per layer: fp16 rows out, f32 rows back
+    roof = {"hbm": E_l * REGION_BYTES / (peaks()[0] * 1e9) * 1e3,
+            "tensor": pairs * 3 * 2 * F * D / (tensor_peak()[0] * 1e12) * 1e3,
+            "nvlink": link_bytes / 770e9 * 1e3}
+    return {"_ms": ms, "_roof_ms": roof, "unit": "tok/s",
+            "config": {"workload": f"configs[4]: {args.ep_tokens} tokens x {L} stacked Q4_0 MoE layers, experts "
+                                   f"sharded {E_l} per GPU over {G} GPU(s), uniform top-8 routing",
+                       "tokens_per_rank": T, "experts_per_rank": E_l, "scaling": "strong",
+                       "remote_rows_per_layer_rank0": round(remote_rows / L, 1),
+                       "transfer": "fixed capacity: T fp16 rows + metadata out and T f32 rows back per peer"},
+            "gpu_launches_per_layer": 9}
 
 
 def prefill_bench(args, layers, torch, lib, Q, s, barrier):
