@@ -28,6 +28,8 @@ EXPORTS = [
     "cpg_moe_apply_workspace_bytes", "cpg_moe_apply", "cpg_moe_apply_check", "cpg_moe_apply_profile",
     "cpg_moe_apply_rows", "cpg_ep_unique_id", "cpg_ep_create", "cpg_ep_destroy", "cpg_ep_workspace_bytes",
     "cpg_moe_ep", "cpg_moe_ep_check",
+    "cpg_qwen3_create", "cpg_qwen3_destroy", "cpg_qwen3_prefill", "cpg_qwen3_step", "cpg_qwen3_generate",
+    "cpg_qwen3_logits", "cpg_qwen3_stream", "cpg_qwen3_position",
 ]
 
 
@@ -46,6 +48,19 @@ class MoeDesc(ctypes.Structure):
     _fields_ = [("d_model", ctypes.c_int), ("d_exp", ctypes.c_int), ("n_experts", ctypes.c_int),
                 ("topk", ctypes.c_int), ("rms_eps", ctypes.c_float), ("ln2", ctypes.c_void_p),
                 ("wgate", Tensor), ("experts", ctypes.POINTER(Tensor))]
+
+
+class Qwen3Attn(ctypes.Structure):
+    _fields_ = [("ln1", ctypes.c_void_p), ("q_norm", ctypes.c_void_p), ("k_norm", ctypes.c_void_p),
+                ("wq", Tensor), ("wk", Tensor), ("wv", Tensor), ("wo", Tensor)]
+
+
+class Qwen3Desc(ctypes.Structure):
+    _fields_ = [("d_model", ctypes.c_int), ("n_heads", ctypes.c_int), ("n_kv", ctypes.c_int),
+                ("head_dim", ctypes.c_int), ("vocab", ctypes.c_int), ("n_layers", ctypes.c_int),
+                ("max_ctx", ctypes.c_int), ("rope_theta", ctypes.c_float), ("rms_eps", ctypes.c_float),
+                ("embed", Tensor), ("lm_head", Tensor), ("final_norm", ctypes.c_void_p),
+                ("attn", ctypes.POINTER(Qwen3Attn)), ("moe", ctypes.POINTER(ctypes.c_void_p))]
 
 
 class StoreTotals(ctypes.Structure):
@@ -96,6 +111,14 @@ _SIGS = {
     "cpg_ep_workspace_bytes": (_sz, [_vp, _vp, _i]),
     "cpg_moe_ep": (_i, [_vp, _vp, _vp, _i, _vp, _vp, _vp, _vp, _sz, _vp]),
     "cpg_moe_ep_check": (_i, [_vp, _vp]),
+    "cpg_qwen3_create": (_i, [ctypes.POINTER(Qwen3Desc), ctypes.POINTER(_vp)]),
+    "cpg_qwen3_destroy": (None, [_vp]),
+    "cpg_qwen3_prefill": (_i, [_vp, _vp, _i, ctypes.POINTER(_i)]),
+    "cpg_qwen3_step": (_i, [_vp, _i, ctypes.POINTER(_i)]),
+    "cpg_qwen3_generate": (_i, [_vp, _vp, _i, _i, _vp]),
+    "cpg_qwen3_logits": (_vp, [_vp]),
+    "cpg_qwen3_stream": (_vp, [_vp]),
+    "cpg_qwen3_position": (_i, [_vp]),
     "cpg_ctx_x": (_vp, [_vp]),
     "cpg_ctx_topk": (_vp, [_vp]),
     "cpg_ctx_profile": (_i, [_vp, _i]),

@@ -15,7 +15,7 @@ from dataclasses import dataclass
 import numpy as np
 
 from . import _lib
-from ._lib import ENC_F32, ENC_Q4, ENC_Q8, GROUP_BYTES, MoeDesc, Tensor, check, lib
+from ._lib import ENC_F32, ENC_Q4, ENC_Q8, GROUP_BYTES, MoeDesc, Qwen3Attn, Qwen3Desc, Tensor, check, lib
 
 
 def row_bytes(enc: int, n_in: int) -> int:
@@ -278,6 +278,69 @@ class ExpertParallel:
     def close(self) -> None:
         if self.handle is not None and self.handle.value:
             lib().cpg_ep_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class Qwen3Model:
+    """cpg_qwen3: the whole model on one device (embed_rows, run_layers, apply_head and the greedy
+    loop of cp_chat, engine/api/cachepotato.c:108-166, 315-378).
+
+    attn: per layer a dict of device tensors ln1, q_norm, k_norm (f32) and wq, wk, wv, wo
+    (uint8 blocks in attn_enc); moe: per layer a MoELayer; embed / lm_head: device blocks in
+    their encodings; final_norm f32."""
+
+    def __init__(self, *, d_model, n_heads, n_kv, head_dim, vocab, max_ctx, attn, moe, attn_enc,
+                 embed, embed_enc, lm_head, head_enc, final_norm, rope_theta=1e6, rms_eps=1e-6):
+        L = len(attn)
+        tab = (Qwen3Attn * L)()
+        for i, a in enumerate(attn):
+            tab[i] = Qwen3Attn(a["ln1"].data_ptr(), a["q_norm"].data_ptr(), a["k_norm"].data_ptr(),
+                               Tensor(a["wq"].data_ptr(), attn_enc), Tensor(a["wk"].data_ptr(), attn_enc),
+                               Tensor(a["wv"].data_ptr(), attn_enc), Tensor(a["wo"].data_ptr(), attn_enc))
+        moes = (ctypes.c_void_p * L)(*[m.handle.value for m in moe])
+        desc = Qwen3Desc(d_model, n_heads, n_kv, head_dim, vocab, L, max_ctx, rope_theta, rms_eps,
+                         Tensor(embed.data_ptr(), embed_enc), Tensor(lm_head.data_ptr(), head_enc),
+                         final_norm.data_ptr(), tab, moes)
+        h = ctypes.c_void_p()
+        check(lib().cpg_qwen3_create(ctypes.byref(desc), ctypes.byref(h)))
+        self.handle, self.vocab = h, vocab
+        self._keep = (attn, moe, embed, lm_head, final_norm, tab, moes)
+
+    def prefill(self, ids) -> int:
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        nxt = ctypes.c_int()
+        check(lib().cpg_qwen3_prefill(self.handle, ids.ctypes.data, len(ids), ctypes.byref(nxt)))
+        return nxt.value
+
+    def step(self, token: int) -> int:
+        nxt = ctypes.c_int()
+        check(lib().cpg_qwen3_step(self.handle, int(token), ctypes.byref(nxt)))
+        return nxt.value
+
+    def generate(self, prompt, n_new: int) -> np.ndarray:
+        prompt = np.ascontiguousarray(prompt, dtype=np.int32)
+        out = np.zeros(n_new + 1, np.int32)
+        check(lib().cpg_qwen3_generate(self.handle, prompt.ctypes.data, len(prompt), n_new, out.ctypes.data))
+        return out
+
+    def logits(self):
+        """The last position's logits as a device tensor (a view; valid until the next call)."""
+        torch = _torch()
+        from .workload import device_view
+        return device_view(torch, int(lib().cpg_qwen3_logits(self.handle)), self.vocab * 4, "f4")
+
+    def stream_ptr(self) -> int:
+        return int(lib().cpg_qwen3_stream(self.handle) or 0)
+
+    def close(self) -> None:
+        if self.handle is not None and self.handle.value:
+            lib().cpg_qwen3_destroy(self.handle)
             self.handle = None
 
     def __del__(self):

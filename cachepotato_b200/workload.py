@@ -78,3 +78,18 @@ def load_stats(topk: np.ndarray, E: int) -> dict:
 def rmsnorm_rows(x: np.ndarray, eps: float = 1e-6) -> np.ndarray:
     x = x.astype(np.float32)
     return x / np.sqrt((x * x).mean(-1, keepdims=True) + np.float32(eps))
+
+
+class _DevRange:
+    """A raw device range with __cuda_array_interface__, for viewing library-owned buffers."""
+
+    def __init__(self, ptr: int, nbytes: int, typestr: str):
+        item = int(typestr[-1])
+        self.__cuda_array_interface__ = {"shape": (nbytes // item,), "typestr": typestr,
+                                         "data": (ptr, False), "version": 2, "strides": None}
+
+
+def device_view(torch, ptr: int, nbytes: int, dtype: str = "f4"):
+    """A torch view of nbytes of device memory at ptr (no copy)."""
+    ts = {"f4": "<f4", "u1": "|u1", "i4": "<i4"}[dtype]
+    return torch.as_tensor(_DevRange(ptr, nbytes, ts), device="cuda")

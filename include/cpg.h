@@ -193,6 +193,37 @@ int cpg_moe_ep(cpg_ep *ep, const cpg_moe_layer *local_layer, const float *xn, in
    zero). */
 int cpg_moe_ep_check(const void *ws, void *stream);
 
+/* ============================================================== the whole model (config 3)
+ * A Qwen3-MoE model on one device: embed_rows, run_layers (attention half of qwen3_layer_kv,
+ * qwen3_moe.c:110-167, then the MoE half through cpg_moe_forward), apply_head and the greedy
+ * argmax of cp_chat (engine/api/cachepotato.c:108-166, 315-378). Tensors are device pointers;
+ * head_dim must be 128. The model owns an f32 KV cache of max_ctx positions per layer. */
+typedef struct {
+    const float *ln1, *q_norm, *k_norm;      /* (d_model), (head_dim), (head_dim) */
+    cpg_tensor wq, wk, wv, wo;               /* (n_heads·hd, d), (n_kv·hd, d) ×2, (d, n_heads·hd) */
+} cpg_qwen3_attn;
+typedef struct {
+    int d_model, n_heads, n_kv, head_dim, vocab, n_layers, max_ctx;
+    float rope_theta, rms_eps;
+    cpg_tensor embed, lm_head;               /* (vocab, d_model), Q8_0 or Q4_0 / any encoding */
+    const float *final_norm;
+    const cpg_qwen3_attn *attn;              /* n_layers */
+    cpg_moe_layer *const *moe;               /* n_layers */
+} cpg_qwen3_desc;
+typedef struct cpg_qwen3 cpg_qwen3;
+int cpg_qwen3_create(const cpg_qwen3_desc *d, cpg_qwen3 **out);
+void cpg_qwen3_destroy(cpg_qwen3 *m);
+/* The prompt (host ids) in one pass at position 0 (the cache restarts); *next_id = argmax of
+   the last position's logits (first maximum wins). */
+int cpg_qwen3_prefill(cpg_qwen3 *m, const int *ids, int T, int *next_id);
+/* One token at the next position. */
+int cpg_qwen3_step(cpg_qwen3 *m, int id, int *next_id);
+/* Prefill, then n_new steps each feeding the previous argmax; out_ids gets n_new + 1 ids. */
+int cpg_qwen3_generate(cpg_qwen3 *m, const int *prompt, int n_prompt, int n_new, int *out_ids);
+const float *cpg_qwen3_logits(const cpg_qwen3 *m);   /* device (vocab) f32, last position */
+void *cpg_qwen3_stream(const cpg_qwen3 *m);
+int cpg_qwen3_position(const cpg_qwen3 *m);
+
 /* ============================================================== decode loop (host buffers)
  * A context owns a stream, a workspace and device activation buffers on one device. */
 typedef struct cpg_ctx cpg_ctx;

@@ -168,6 +168,11 @@ class Reference:
         L.refh_moe_apply.restype = ctypes.c_int
         L.refh_moe_apply.argtypes = [_vpp, ctypes.c_int, ctypes.c_int, ctypes.c_int, _f32p,
                                      ctypes.c_int, ctypes.c_int, _i32p, _f32p, _f32p]
+        L.refh_qwen3_generate.restype = ctypes.c_int
+        L.refh_qwen3_generate.argtypes = ([ctypes.c_int] * 9 + [ctypes.c_float] * 2 +
+                                          [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_int, _f32p] +
+                                          [_vpp] * 8 + [ctypes.c_int, _vpp, _vpp, ctypes.c_int] +
+                                          [_i32p, ctypes.c_int, ctypes.c_int, _i32p, _f32p])
         for n in ("matmul_wx_q4", "matmul_wx_q8"):
             getattr(L, n).argtypes = [_f32p, _f32p, _u8p, ctypes.c_int, ctypes.c_int]
         L.matmul_wx.argtypes = [_f32p, _f32p, _f32p, ctypes.c_int, ctypes.c_int]
@@ -210,6 +215,34 @@ class Reference:
         assert rc == 0, rc
         return dict(mlp=mlp, router=router, topk_idx=idx)
 
+    def qwen3_generate(self, model: "SynthModel", prompt, n_new: int):
+        """The reference engine over a whole model: the prompt in one pass, then n_new greedy
+        steps. Returns (ids of the n_new + 1 argmaxes, logits of the last step)."""
+        m = model
+        prompt = np.ascontiguousarray(prompt, dtype=np.int32)
+        ids = np.zeros(n_new + 1, np.int32)
+        logits = np.zeros(m.vocab, np.float32)
+
+        def arr(xs):
+            a = (ctypes.c_void_p * len(xs))(*[x.ctypes.data for x in xs])
+            keep.append(a)
+            return ctypes.cast(a, _vpp)
+        keep = []
+        exp = (ctypes.c_void_p * (m.n_layers * m.n_experts * 3))()
+        for l, ly in enumerate(m.layers):
+            for e in range(m.n_experts):
+                for k in range(3):
+                    exp[(l * m.n_experts + e) * 3 + k] = ly.blob.ctypes.data + e * ly.region_bytes + k * ly.mat_bytes
+        rc = self.L.refh_qwen3_generate(
+            m.d_model, m.n_heads, m.n_kv, m.head_dim, m.d_exp, m.n_experts, m.topk, m.vocab, m.n_layers,
+            m.rope_theta, m.eps, m.embed.ctypes.data, m.embed_enc, m.lm_head.ctypes.data, m.head_enc,
+            _ptr(m.final_norm, _f32p), arr(m.ln1), arr([ly.ln2 for ly in m.layers]), arr(m.q_norm), arr(m.k_norm),
+            arr(m.wq), arr(m.wk), arr(m.wv), arr(m.wo), m.attn_enc, arr([ly.wgate for ly in m.layers]),
+            ctypes.cast(exp, _vpp), m.layers[0].enc, _ptr(prompt, _i32p), len(prompt), n_new,
+            _ptr(ids, _i32p), _ptr(logits, _f32p))
+        assert rc == 0
+        return ids, logits
+
     def moe_apply(self, layer: "SynthLayer", xn: np.ndarray, idx: np.ndarray, wt: np.ndarray):
         xn = np.ascontiguousarray(xn, dtype=np.float32)
         idx = np.ascontiguousarray(idx, dtype=np.int32)
@@ -225,6 +258,49 @@ class Reference:
 
 def reference_available() -> bool:
     return os.path.exists(REF_SO) or os.path.isdir(os.path.join(REF_TREE, "engine"))
+
+
+class SynthModel:
+    """A whole Qwen3-MoE model in host memory (SURVEY config 3 shape or smaller): per layer an
+    attention half (ln1, Wq/Wk/Wv/Wo in attn_enc, q_norm/k_norm) and a SynthLayer MoE half, plus
+    embed and lm_head (head_enc) and the final norm. Norm gains are 1 + norm_jitter·N(0,1)."""
+
+    def __init__(self, d_model, n_heads, n_kv, head_dim, d_exp, n_experts, topk, vocab, n_layers, seed,
+                 attn_enc=ENC_Q4, exp_enc=ENC_Q4, head_enc=ENC_Q8, rope_theta=1e6, eps=1e-6, norm_jitter=0.0,
+                 oracle: Oracle | None = None, std: float = 0.02):
+        orc = oracle or Oracle()
+        self.d_model, self.n_heads, self.n_kv, self.head_dim = d_model, n_heads, n_kv, head_dim
+        self.d_exp, self.n_experts, self.topk, self.vocab, self.n_layers = d_exp, n_experts, topk, vocab, n_layers
+        self.rope_theta, self.eps = rope_theta, eps
+        self.attn_enc, self.head_enc, self.embed_enc = attn_enc, head_enc, head_enc
+        qd, kd = n_heads * head_dim, n_kv * head_dim
+
+        def gain(n, s):
+            g = np.ones(n, np.float32)
+            if norm_jitter:
+                g += norm_jitter * orc.normal(n, s, 1.0)
+            return np.ascontiguousarray(g, dtype=np.float32)
+
+        def mat(rows, cols, s, enc):
+            w = orc.normal(rows * cols, s, std)
+            return w if enc == ENC_F32 else orc.quantize(w, enc)
+        self.layers, self.ln1, self.q_norm, self.k_norm = [], [], [], []
+        self.wq, self.wk, self.wv, self.wo = [], [], [], []
+        for l in range(n_layers):
+            b = seed * 1000 + 20 * l
+            ly = SynthLayer(d_model, d_exp, n_experts, topk, exp_enc, seed=b + 1, oracle=orc, std=std)
+            ly.ln2 = gain(d_model, b + 2)
+            self.layers.append(ly)
+            self.ln1.append(gain(d_model, b + 3))
+            self.q_norm.append(gain(head_dim, b + 4))
+            self.k_norm.append(gain(head_dim, b + 5))
+            self.wq.append(mat(qd, d_model, b + 6, attn_enc))
+            self.wk.append(mat(kd, d_model, b + 7, attn_enc))
+            self.wv.append(mat(kd, d_model, b + 8, attn_enc))
+            self.wo.append(mat(d_model, qd, b + 9, attn_enc))
+        self.embed = mat(vocab, d_model, seed * 1000 + 991, head_enc)
+        self.lm_head = mat(vocab, d_model, seed * 1000 + 992, head_enc)
+        self.final_norm = gain(d_model, seed * 1000 + 993)
 
 
 class SynthLayer:

@@ -96,3 +96,82 @@ int refh_moe_apply(const void *const *exp, int exp_enc, int D, int F, const floa
     free(gu); free(hh);
     return 0;
 }
+
+/* A whole model, prompt then greedy decode, with the engine's own functions in the order cp_chat
+   uses them (engine/api/cachepotato.c:315-378): embed_rows (108-133: q8/q4_dequant_row of the
+   token's row), run_layers (149-166: qwen3_layer_kv per layer, then x += attn + mlp), apply_head
+   (135-147: rmsnorm of the last position, lm_head through qwen3_mm), argmax with the first
+   maximum winning (353-356). The prompt runs in one pass at position 0; then n_new single-token
+   steps, each feeding the previous argmax. out_ids receives n_new + 1 ids (the argmax after the
+   prompt and after every step); out_logits the logits of the last step. Per-layer tensors come
+   as arrays of L pointers; exp holds L * E * 3 expert pointers. */
+static void refh_embed(const void *embed, int enc, int id, float *x, int D) {
+    if (enc == QW3_ENC_Q8) q8_dequant_row((const uint8_t *)embed + (size_t)id * (size_t)(D / 32) * 34, x, D);
+    else if (enc == QW3_ENC_Q4) q4_dequant_row((const uint8_t *)embed + (size_t)id * (size_t)(D / 32) * 18, x, D);
+    else memcpy(x, (const float *)embed + (size_t)id * D, sizeof(float) * (size_t)D);
+}
+
+static int refh_argmax(const float *v, int n) {
+    int best = 0;
+    for (int j = 1; j < n; j++) if (v[j] > v[best]) best = j;
+    return best;
+}
+
+int refh_qwen3_generate(int D, int H, int KV, int HD, int F, int E, int K, int V, int L, float theta, float eps,
+                        const void *embed, int embed_enc, const void *lm_head, int head_enc, const float *final_norm,
+                        const void *const *ln1, const void *const *ln2, const void *const *qn, const void *const *kn,
+                        const void *const *wq, const void *const *wk, const void *const *wv, const void *const *wo,
+                        int attn_enc, const void *const *wgate, const void *const *exp, int exp_enc,
+                        const int *prompt, int n_prompt, int n_new, int *out_ids, float *out_logits) {
+    const int cap = n_prompt + n_new;
+    QW3Layer *ls = calloc((size_t)L, sizeof(QW3Layer));
+    QW3KV *kv = calloc((size_t)L, sizeof(QW3KV));
+    QW3T *tab = calloc((size_t)L * E * 3, sizeof(QW3T));
+    float *x = malloc(sizeof(float) * (size_t)n_prompt * D);
+    float *logits = malloc(sizeof(float) * (size_t)V);
+    int rc = -2;
+    if (!ls || !kv || !tab || !x || !logits) goto out;
+    for (int l = 0; l < L; l++) {
+        QW3Layer *m = &ls[l];
+        m->d_model = D; m->n_heads = H; m->n_kv = KV; m->head_dim = HD;
+        m->d_exp = F; m->n_experts = E; m->topk = K; m->vocab = V;
+        m->rope_theta = theta; m->rms_eps = eps;
+        m->ln1 = ln1[l]; m->ln2 = ln2[l]; m->q_norm = qn[l]; m->k_norm = kn[l];
+        m->Wq.p = wq[l]; m->Wk.p = wk[l]; m->Wv.p = wv[l]; m->Wo.p = wo[l];
+        m->Wq.enc = m->Wk.enc = m->Wv.enc = m->Wo.enc = attn_enc;
+        m->Wgate.p = wgate[l]; m->Wgate.enc = QW3_ENC_F32;
+        for (int i = 0; i < E * 3; i++) {
+            tab[(size_t)l * E * 3 + i].p = exp[(size_t)l * E * 3 + i];
+            tab[(size_t)l * E * 3 + i].enc = exp_enc;
+        }
+        m->exp = tab + (size_t)l * E * 3;
+        if (qwen3_kv_alloc(&kv[l], m, cap)) goto out;
+    }
+    QW3T head = { lm_head, head_enc };
+    int pos = 0, T = n_prompt;
+    const int *ids = prompt;
+    int cur = 0;
+    for (int step = 0; step <= n_new; step++) {
+        for (int t = 0; t < T; t++) refh_embed(embed, embed_enc, step == 0 ? ids[t] : cur, x + (size_t)t * D, D);
+        for (int l = 0; l < L; l++) {
+            QW3Out o;
+            if (qwen3_layer_alloc(&o, &ls[l], T)) goto out;
+            if (qwen3_layer_kv(&ls[l], x, T, pos, &kv[l], &o)) { qwen3_layer_free(&o); goto out; }
+            for (size_t i = 0; i < (size_t)T * D; i++) x[i] += o.attn[i] + o.mlp[i];
+            qwen3_layer_free(&o);
+        }
+        float *xl = x + (size_t)(T - 1) * D;
+        rmsnorm(xl, xl, final_norm, D, eps);
+        qwen3_mm(&head, logits, xl, D, V);
+        cur = refh_argmax(logits, V);
+        out_ids[step] = cur;
+        pos += T;
+        T = 1;
+    }
+    if (out_logits) memcpy(out_logits, logits, sizeof(float) * (size_t)V);
+    rc = 0;
+out:
+    if (kv) for (int l = 0; l < L; l++) qwen3_kv_free(&kv[l]);
+    free(ls); free(kv); free(tab); free(x); free(logits);
+    return rc;
+}

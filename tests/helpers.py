@@ -39,3 +39,20 @@ def check_topk(got_idx, want_idx, want_logits, K):
         if not close:
             bad.append(t)
     return bad
+
+
+def device_model(model, max_ctx, torch=None):
+    """cachepotato_b200 Qwen3Model over a copy of oracle SynthModel `model` in device memory."""
+    import torch as _t
+    from cachepotato_b200.qwen3 import Qwen3Model
+    torch = torch or _t
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    attn = [dict(ln1=dev(model.ln1[l]), q_norm=dev(model.q_norm[l]), k_norm=dev(model.k_norm[l]),
+                 wq=dev(model.wq[l]), wk=dev(model.wk[l]), wv=dev(model.wv[l]), wo=dev(model.wo[l]))
+            for l in range(model.n_layers)]
+    moe = [device_layer(ly) for ly in model.layers]
+    return Qwen3Model(d_model=model.d_model, n_heads=model.n_heads, n_kv=model.n_kv, head_dim=model.head_dim,
+                      vocab=model.vocab, max_ctx=max_ctx, attn=attn, moe=moe, attn_enc=model.attn_enc,
+                      embed=dev(model.embed), embed_enc=model.embed_enc, lm_head=dev(model.lm_head),
+                      head_enc=model.head_enc, final_norm=dev(model.final_norm), rope_theta=model.rope_theta,
+                      rms_eps=model.eps)
