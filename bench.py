@@ -19,6 +19,9 @@ layers (router, experts, combine, residual), weights resident in HBM.
   expert_parallel  configs[4]: 2048 tokens (2048/N per rank) through the 48 stacked layers with
           the 128 experts sharded 128/N per GPU (cpg_moe_ep: NCCL dispatch and combine), uniform
           top-8 routing; tok/s, ms per layer, and the binding roof (HBM, tensor or NVLink)
+  full_model  configs[2]: the whole 48-layer model (attention + MoE, vocab 151936, Q4_0 attention
+          and experts, Q8_0 embed and lm_head): 512-token prompt, then 128 greedy decode steps;
+          decode tok/s and HBM GB/s of the bytes a token must read
   prefill   configs[3]: 4096 Zipf(1.2)-routed tokens through one Q4_0 MoE block per step on the
           tcgen05 grouped GEMM (cpg_moe_apply), tok/s and TFLOP/s, roofline of the gate/up GEMM
           against the measured tensor peak
@@ -67,6 +70,9 @@ def parse():
     ap.add_argument("--prefill-tokens", type=int, default=4096, help="0 skips the prefill section")
     ap.add_argument("--no-q8", action="store_true", help="skip the Q8 batch-1 section")
     ap.add_argument("--ep-tokens", type=int, default=2048, help="0 skips the expert-parallel section")
+    ap.add_argument("--no-full-model", action="store_true", help="skip the whole-model section")
+    ap.add_argument("--full-prompt", type=int, default=512)
+    ap.add_argument("--full-new", type=int, default=128)
     return ap.parse_args()
 
 
@@ -281,6 +287,10 @@ def run_ours(args, rank, world, torch, dist):
     q8 = None if args.no_q8 else q8_batch1_bench(args, torch, lib, Q, barrier)
     ms_q8 = q8.pop("_ms") if q8 else 0.0
 
+    # ---- the whole model, prompt + greedy decode
+    fm = None if args.no_full_model else full_model_bench(args, layers, torch, lib, Q, barrier)
+    ms_fm = fm.pop("_ms") if fm else 0.0
+
     # ---- expert parallelism across the ranks (a collective: every rank takes part)
     ep = ep_bench(args, layers, torch, lib, Q, dist, rank, world, barrier) if args.ep_tokens > 0 else None
     ms_ep = ep.pop("_ms") if ep else 0.0
@@ -290,10 +300,10 @@ def run_ours(args, rank, world, torch, dist):
     ms_pf = pf.pop("_ms") if pf else 0.0
 
     # max over ranks
-    t = torch.tensor([ms, ms_e2e, ms_b1, ms_pf, ms_q8, ms_ep], dtype=torch.float64, device="cuda")
+    t = torch.tensor([ms, ms_e2e, ms_b1, ms_pf, ms_q8, ms_ep, ms_fm], dtype=torch.float64, device="cuda")
     if dist is not None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms, ms_e2e, ms_b1, ms_pf, ms_q8, ms_ep = (float(v) for v in t.tolist())
+    ms, ms_e2e, ms_b1, ms_pf, ms_q8, ms_ep, ms_fm = (float(v) for v in t.tolist())
     if rank != 0:
         return None
 
@@ -343,6 +353,13 @@ def run_ours(args, rank, world, torch, dist):
         q8["hbm_gbs"] = round(q8["bytes_per_step"] / (per * 1e-3) / 1e9, 1)
         q8["frac"] = round(q8["hbm_gbs"] / hbm, 4)
         res["decode_q8_batch1"] = q8
+    if fm:
+        per_tok = ms_fm / args.full_new
+        fm["value"] = round(world * args.full_new / (ms_fm * 1e-3), 1)
+        fm["ms_per_token"] = round(per_tok, 4)
+        fm["hbm_gbs"] = round(fm["bytes_per_token"] / (per_tok * 1e-3) / 1e9, 1)
+        fm["frac"] = round(fm["hbm_gbs"] / hbm, 4)
+        res["full_model"] = fm
     if ep:
         per_layer = ms_ep / args.steps / L
         ep["value"] = round(args.ep_tokens * args.steps / (ms_ep * 1e-3), 1)
@@ -405,6 +422,66 @@ def q8_batch1_bench(args, torch, lib, Q, barrier):
             "bytes_per_step": L * (LN_BYTES + ROUTER_BYTES + K * 3 * MAT_BYTES_Q8 + 2 * D * 4),
             "config": {"workload": f"configs[0]: decode batch 1 through {L} stacked Q8_0 MoE layers "
                                    "(plain N(0,0.02) f32 router)", "expert_encoding": "Q8_0"}}
+
+
+def full_model_bench(args, layers, torch, lib, Q, barrier):
+    """the whole Qwen3-30B-A3B-shaped model (48 layers, hidden 2048, 32 query / 4 KV
+    heads of 128, QK-RMSNorm, RoPE theta 1e6, 128 experts top-8 of width 768, vocab 151936) with
+    random weights N(0,0.02): attention and experts Q4_0, embed and lm_head Q8_0, norms 1, f32
+    routers (not Zipf-scaled: the experts are the region store's, the routers are fresh). A prompt
+    of args.full_prompt uniform ids in one pass, then args.full_new greedy steps through
+    cpg_qwen3_generate (each step embeds the previous argmax on the device and reads its id back)."""
+    L, V, H, KVH, HD = len(layers), 151936, 32, 4, 128
+    QD, KD = H * HD, KVH * HD
+    g = torch.Generator(device="cuda")
+
+    def q4(rows, cols, seed, enc=ENC_Q4):
+        gb = 18 if enc == ENC_Q4 else 34
+        out = torch.empty(rows * cols // 32 * gb, dtype=torch.uint8, device="cuda")
+        w = torch.randn(rows * cols, generator=g.manual_seed(seed), device="cuda").mul_(0.02)
+        Q.check(lib.cpg_quantize(out.data_ptr(), w.data_ptr(), enc, w.numel(), None))
+        return out
+    ones_d, ones_h = torch.ones(2048, device="cuda"), torch.ones(HD, device="cuda")
+    attn, moe = [], []
+    for l, ly in enumerate(layers):
+        b = args.seed * 5000 + 10 * l
+        attn.append(dict(ln1=ones_d, q_norm=ones_h, k_norm=ones_h, wq=q4(QD, D, b + 1), wk=q4(KD, D, b + 2),
+                         wv=q4(KD, D, b + 3), wo=q4(D, QD, b + 4)))
+        wg = torch.randn((E, D), generator=g.manual_seed(b + 5), device="cuda") * 0.02
+        moe.append(Q.MoELayer(ones_d, wg, ENC_Q4, D, F, E, K, blob=None, expert_ptrs=ly.ptr_list))
+    embed = q4(V, D, args.seed * 5000 + 901, ENC_Q8)
+    head = q4(V, D, args.seed * 5000 + 902, ENC_Q8)
+    prompt = np.random.default_rng(args.seed + 3).integers(0, V, args.full_prompt).astype(np.int32)
+    max_ctx = args.full_prompt + args.full_new + 1
+    m = Q.Qwen3Model(d_model=D, n_heads=H, n_kv=KVH, head_dim=HD, vocab=V, max_ctx=max_ctx, attn=attn, moe=moe,
+                     attn_enc=ENC_Q4, embed=embed, embed_enc=ENC_Q8, lm_head=head, head_enc=ENC_Q8,
+                     final_norm=ones_d)
+    s = torch.cuda.ExternalStream(m.stream_ptr())
+    m.generate(prompt[:8], 4)                           # warm-up (small)
+    barrier()
+    e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+    e0.record(s)
+    nxt = m.prefill(prompt)
+    e1.record(s)
+    ids = [nxt]
+    for _ in range(args.full_new):
+        nxt = m.step(nxt)
+        ids.append(nxt)
+    e2.record(s)
+    barrier()
+    ms_prefill, ms_decode = e0.elapsed_time(e1), e1.elapsed_time(e2)
+    m.close()
+    avg_pos = args.full_prompt + args.full_new / 2
+    per_layer = (2 * QD * D + 2 * KD * D) // 32 * 18 + ROUTER_BYTES + K * REGION_BYTES + 2 * D * 4 + 2 * HD * 4
+    bytes_tok = L * (per_layer + 2 * KD * 4 * avg_pos) + V * D // 32 * 34 + D // 32 * 34 + D * 4
+    return {"_ms": ms_decode, "unit": "tok/s", "bytes_per_token": int(bytes_tok),
+            "prefill_ms": round(ms_prefill, 3), "prefill_tok_s": round(args.full_prompt / (ms_prefill * 1e-3), 1),
+            "tokens_head": [int(v) for v in ids[:8]],
+            "config": {"workload": f"configs[2]: whole model, {L} layers, vocab {V}, prompt {args.full_prompt} uniform "
+                                   f"ids, {args.full_new} greedy steps (host reads each argmax)",
+                       "attention": "32 query / 4 KV heads x 128, QK-RMSNorm, RoPE theta 1e6, f32 KV cache",
+                       "bytes_per_token": "48 x (attention 10.6 MB + router 1 MiB + 8 experts 21.2 MB + KV reads "
+                                          "at the mean position) + lm_head 330.6 MB + embed row"}}
 
 
 def ep_bench(args, layers, torch, lib, Q, dist, rank, world, barrier):

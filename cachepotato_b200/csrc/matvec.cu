@@ -112,6 +112,137 @@ __device__ __forceinline__ void row_partial(const uint8_t *__restrict__ row, int
     }
 }
 
+// ---------------------------------------------------------------- streaming GEMV (T ≤ 4)
+// For decode-sized T the weight rows are the only traffic: 16 consecutive rows at a time arrive
+// in shared memory by one 1D bulk copy (a 4-deep ring filled by one producer thread), and each
+// lane decodes whole 64-value group pairs from there (word stride 9 or 17, odd: no bank
+// conflicts), with the same exact (float)q·d and fp32 FMA as the row-per-warp kernel above.
+constexpr int GV_ROWS = 16;
+constexpr int GV_CONS = 8;                      // consumer warps, two rows each per stage
+constexpr int GV_MAXT = 4;
+
+template <int ENC, int NT>
+__device__ __forceinline__ void gemv_pair(const uint32_t *__restrict__ wp, const float *__restrict__ xp, int np,
+                                          int n_in, float (&acc)[NT]) {
+    constexpr int GB = ENC == CPG_ENC_Q4 ? 18 : 34;
+    constexpr int NW = GB / 2;
+    uint32_t w[NW];
+#pragma unroll
+    for (int i = 0; i < NW; ++i) w[i] = wp[i];
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+        const int b0 = half * GB;
+        const float d = f16_bits_to_f32((w[b0 / 4] >> ((b0 % 4) * 8)) & 0xFFFFu);
+        const float *xh = xp + (half * 32) * np;
+        if (ENC == CPG_ENC_Q4) {
+#pragma unroll
+            for (int k = 0; k < 16; ++k) {
+                const int bo = b0 + 2 + k;
+                const uint32_t byte = (w[bo / 4] >> ((bo % 4) * 8)) & 0xFFu;
+                const float lo = __fmul_rn((float)sext4(byte), d);
+                const float hi = __fmul_rn((float)sext4(byte >> 4), d);
+#pragma unroll
+                for (int t = 0; t < NT; ++t) {
+                    acc[t] = fmaf(lo, xh[t * n_in + k * np], acc[t]);
+                    acc[t] = fmaf(hi, xh[t * n_in + (k + 16) * np], acc[t]);
+                }
+            }
+        } else {
+#pragma unroll
+            for (int k = 0; k < 32; ++k) {
+                const int bo = b0 + 2 + k;
+                const float v = __fmul_rn((float)(int)(int8_t)((w[bo / 4] >> ((bo % 4) * 8)) & 0xFFu), d);
+#pragma unroll
+                for (int t = 0; t < NT; ++t) acc[t] = fmaf(v, xh[t * n_in + k * np], acc[t]);
+            }
+        }
+    }
+}
+
+template <int ENC, int NT>
+__global__ void __launch_bounds__((GV_CONS + 1) * 32)
+k_gemv(float *__restrict__ out, const float *__restrict__ x, const uint8_t *__restrict__ w, int n_in, int n_out,
+       long rowbytes, int stages) {
+    extern __shared__ __align__(16) uint8_t gsm[];
+    float *xs = reinterpret_cast<float *>(gsm);                           // (NT, n_in) pair-permuted
+    uint8_t *ring = gsm + (size_t)NT * n_in * sizeof(float);
+    __shared__ uint64_t full[8], empty[8];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int np = n_in / 64;
+    const int ntiles = (n_out + GV_ROWS - 1) / GV_ROWS;
+    const size_t stage_bytes = (size_t)GV_ROWS * rowbytes;
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < stages; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], GV_CONS);
+        }
+        fence_mbar_init();
+    }
+    for (int i = threadIdx.x; i < NT * n_in; i += blockDim.x) {
+        const int t = i / n_in, e = i - t * n_in;
+        xs[t * n_in + (e % 64) * np + e / 64] = x[i];
+    }
+    __syncthreads();
+    if (warp == GV_CONS) {
+        if (lane != 0) return;
+        int it = 0;
+        for (int tl = blockIdx.x; tl < ntiles; tl += gridDim.x, ++it) {
+            const int st = it % stages;
+            if (it >= stages && !mbar_wait(&empty[st], (uint32_t)(it / stages - 1) & 1u)) break;
+            const int r0 = tl * GV_ROWS, nr = min(GV_ROWS, n_out - r0);
+            mbar_arrive_expect_tx(&full[st], (uint32_t)(nr * rowbytes));
+            bulk_g2s(ring + st * stage_bytes, w + (size_t)r0 * rowbytes, (uint32_t)(nr * rowbytes), &full[st]);
+        }
+        for (int q = it > stages ? it - stages : 0; q < it; ++q) mbar_wait(&full[q % stages], (uint32_t)(q / stages) & 1u);
+        return;
+    }
+    int it = 0;
+    for (int tl = blockIdx.x; tl < ntiles; tl += gridDim.x, ++it) {
+        const int st = it % stages;
+        if (!mbar_wait(&full[st], (uint32_t)(it / stages) & 1u)) break;
+        const int r0 = tl * GV_ROWS, nr = min(GV_ROWS, n_out - r0);
+#pragma unroll
+        for (int rr = 0; rr < 2; ++rr) {
+            const int r = warp * 2 + rr;
+            if (r >= nr) break;
+            const uint32_t *row = reinterpret_cast<const uint32_t *>(ring + st * stage_bytes + (size_t)r * rowbytes);
+            float acc[NT];
+#pragma unroll
+            for (int t = 0; t < NT; ++t) acc[t] = 0.0f;
+            for (int p = lane; p < np; p += 32) gemv_pair<ENC, NT>(row + p * (ENC == CPG_ENC_Q4 ? 9 : 17), xs + p, np, n_in, acc);
+#pragma unroll
+            for (int t = 0; t < NT; ++t) {
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) acc[t] += __shfl_xor_sync(0xffffffffu, acc[t], o);
+            }
+            if (lane == 0) {
+#pragma unroll
+                for (int t = 0; t < NT; ++t) out[(size_t)t * n_out + r0 + r] = acc[t];
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[st]);
+    }
+}
+
+template <int ENC, int NT>
+static int gemv_launch(float *out, const float *x, const uint8_t *w, int n_in, int n_out, long rb, cudaStream_t s) {
+    auto *k = k_gemv<ENC, NT>;
+    const size_t xbytes = (size_t)NT * n_in * sizeof(float);
+    const size_t stage = (size_t)GV_ROWS * rb;
+    const int avail = smem_optin() - 2048;
+    int stages = (int)((avail - (long)xbytes) / (long)stage);
+    if (stages > 4) stages = 4;
+    if (stages < 2) return 1;                                 // too wide: the row kernel takes it
+    const size_t smem = xbytes + stages * stage;
+    CPG_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    const int ntiles = (n_out + GV_ROWS - 1) / GV_ROWS;
+    const int grid = ntiles < sm_count() ? ntiles : sm_count();
+    k<<<grid, (GV_CONS + 1) * 32, smem, s>>>(out, x, w, n_in, n_out, rb, stages);
+    CPG_CUDA(cudaGetLastError());
+    return CPG_OK;
+}
+
 template <int ENC>
 __global__ void __launch_bounds__(MV_WARPS * 32)
 k_matvec(float *__restrict__ out, const float *__restrict__ x, const uint8_t *__restrict__ w,
@@ -163,6 +294,25 @@ int matvec_launch(float *out, const float *x, cpg_tensor w, int n_in, int n_out,
     if (w.enc == CPG_ENC_F32)
         CPG_REQUIRE(((uintptr_t)w.p & 15) == 0, "cpg_matvec: f32 weights must be 16-byte aligned");
     const long rb = row_bytes(w.enc, n_in);
+    // decode-sized batches of quantised rows: the streaming kernel (rows 16-byte multiples,
+    // 4-byte aligned base, whole group pairs)
+    if (w.enc != CPG_ENC_F32 && T <= GV_MAXT && n_in % 64 == 0 && rb % 16 == 0 && ((uintptr_t)w.p & 15) == 0 &&
+        ((uintptr_t)x & 15) == 0) {
+        const uint8_t *wp = (const uint8_t *)w.p;
+        int r = 1;
+        if (w.enc == CPG_ENC_Q4) {
+            r = T == 1 ? gemv_launch<CPG_ENC_Q4, 1>(out, x, wp, n_in, n_out, rb, s)
+              : T == 2 ? gemv_launch<CPG_ENC_Q4, 2>(out, x, wp, n_in, n_out, rb, s)
+              : T == 3 ? gemv_launch<CPG_ENC_Q4, 3>(out, x, wp, n_in, n_out, rb, s)
+                       : gemv_launch<CPG_ENC_Q4, 4>(out, x, wp, n_in, n_out, rb, s);
+        } else {
+            r = T == 1 ? gemv_launch<CPG_ENC_Q8, 1>(out, x, wp, n_in, n_out, rb, s)
+              : T == 2 ? gemv_launch<CPG_ENC_Q8, 2>(out, x, wp, n_in, n_out, rb, s)
+              : T == 3 ? gemv_launch<CPG_ENC_Q8, 3>(out, x, wp, n_in, n_out, rb, s)
+                       : gemv_launch<CPG_ENC_Q8, 4>(out, x, wp, n_in, n_out, rb, s);
+        }
+        if (r != 1) return r;
+    }
     // tokens per CTA: as many as fit 96 KB of staged x
     int tpc = (int)((96 * 1024) / ((long)n_in * 4));
     CPG_REQUIRE(tpc >= 1, "cpg_matvec: n_in=%d too large to stage", n_in);

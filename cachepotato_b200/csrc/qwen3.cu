@@ -73,22 +73,33 @@ __global__ void __launch_bounds__(256) k_rmsnorm(const float *__restrict__ x, co
 }
 
 // One warp per (token, head) of q (heads 0..H-1) and k (heads H..H+KV-1): head RMSNorm, then
-// RoPE at position pos0 + t. Lane l holds elements l, l+32 (first half) and l+64, l+96 (their
+// RoPE at position pos0 + t (pos0 read from the device, so a captured step serves every
+// position). q is updated in place; k and v go from their staging rows (T, KV·hd) into the
+// cache at position pos0 + t. Lane l holds elements l, l+32 (first half) and l+64, l+96 (their
 // rotation partners). Products and sums are rounded one at a time, as the reference's ISO C.
-__global__ void __launch_bounds__(256) k_qk_norm_rope(float *__restrict__ q, float *__restrict__ kc, int T, int pos0,
+__global__ void __launch_bounds__(256) k_qk_norm_rope(float *__restrict__ q, const float *__restrict__ kst,
+                                                       const float *__restrict__ vst, float *__restrict__ kc,
+                                                       float *__restrict__ vc, int T, const int *__restrict__ d_pos,
                                                        int H, int KV, const float *__restrict__ qn,
                                                        const float *__restrict__ kn, float theta, float eps) {
     const int lane = threadIdx.x & 31;
     const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int nh = H + KV;
     if (w >= T * nh) return;
+    const int pos0 = *d_pos;
     const int t = w / nh, h = w - t * nh;
     const bool isq = h < H;
-    float *v = isq ? q + ((size_t)t * H + h) * QW_HD : kc + ((size_t)(pos0 + t) * KV + (h - H)) * QW_HD;
+    const size_t krow = ((size_t)t * KV + (h - H)) * QW_HD, kdst = ((size_t)(pos0 + t) * KV + (h - H)) * QW_HD;
+    const float *src = isq ? q + ((size_t)t * H + h) * QW_HD : kst + krow;
+    float *v = isq ? q + ((size_t)t * H + h) * QW_HD : kc + kdst;
     const float *g = isq ? qn : kn;
     float e[4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) e[i] = v[lane + 32 * i];
+    for (int i = 0; i < 4; ++i) e[i] = src[lane + 32 * i];
+    if (!isq) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) vc[kdst + lane + 32 * i] = vst[krow + lane + 32 * i];
+    }
     float ss = 0.0f;
 #pragma unroll
     for (int i = 0; i < 4; ++i) ss = fmaf(e[i], e[i], ss);
@@ -112,42 +123,58 @@ __global__ void __launch_bounds__(256) k_qk_norm_rope(float *__restrict__ q, flo
     for (int i = 0; i < 4; ++i) v[lane + 32 * i] = e[i];
 }
 
-// Causal GQA attention (qwen3_moe.c:135-155), one block per (query token i, head h): scores over
-// the n = pos0 + i + 1 cached positions, softmax (max, expf, sum, divide), then each thread one
-// output element with the weighted sum over positions in order.
-__global__ void __launch_bounds__(QW_HD) k_attention(const float *__restrict__ q, const float *__restrict__ kc,
-                                                      const float *__restrict__ vc, int pos0, int H, int KV,
-                                                      float *__restrict__ ao) {
+// Causal GQA attention (qwen3_moe.c:135-155), one block of 256 threads per (query token i,
+// head h) over the n = pos0 + i + 1 cached positions:
+//   scores   one thread per position: s = Σ_e q[e]·k[e] in element order with one rounding per
+//            product and per sum (the reference's loop, ISO C without contraction), then / √hd
+//   softmax  max, expf(s - max), sum, divide (block reductions: the sum's order differs)
+//   output   warp w takes positions [w·n/8, (w+1)·n/8), lane l elements 4l..4l+3 (float4 rows),
+//            the eight partial sums added in warp order
+constexpr int AT_THREADS = 256;
+constexpr int AT_WARPS = AT_THREADS / 32;
+__global__ void __launch_bounds__(AT_THREADS) k_attention(const float *__restrict__ q, const float *__restrict__ kc,
+                                                           const float *__restrict__ vc, const int *__restrict__ d_pos,
+                                                           int H, int KV, float *__restrict__ ao) {
+    const int pos0 = *d_pos;
     extern __shared__ float sc[];                        // (n) scores
-    __shared__ float s_red[4];
-    __shared__ float s_q[QW_HD];
+    __shared__ float s_red[AT_WARPS];
+    __shared__ __align__(16) float s_q[QW_HD];
+    __shared__ __align__(16) float s_out[AT_WARPS][QW_HD];
     const int h = blockIdx.x, i = blockIdx.y;
     const int kh = h / (H / KV);
     const int n = pos0 + i + 1;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    s_q[threadIdx.x] = q[((size_t)i * H + h) * QW_HD + threadIdx.x];
+    if (threadIdx.x < QW_HD) s_q[threadIdx.x] = q[((size_t)i * H + h) * QW_HD + threadIdx.x];
     __syncthreads();
     const float scale = __fsqrt_rn((float)QW_HD);
-    for (int j = warp; j < n; j += 4) {
-        const float *kj = kc + ((size_t)j * KV + kh) * QW_HD;
+    const size_t ks = (size_t)KV * QW_HD;
+    for (int j = threadIdx.x; j < n; j += AT_THREADS) {
+        const float4 *kj = reinterpret_cast<const float4 *>(kc + (size_t)j * ks + (size_t)kh * QW_HD);
+        const float4 *q4 = reinterpret_cast<const float4 *>(s_q);
         float s = 0.0f;
-#pragma unroll
-        for (int e = 0; e < 4; ++e) s = fmaf(s_q[lane + 32 * e], kj[lane + 32 * e], s);
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-        if (lane == 0) sc[j] = __fdiv_rn(s, scale);
+#pragma unroll 8
+        for (int e = 0; e < QW_HD / 4; ++e) {
+            const float4 kv = __ldg(kj + e), qv = q4[e];
+            s = __fadd_rn(s, __fmul_rn(qv.x, kv.x));
+            s = __fadd_rn(s, __fmul_rn(qv.y, kv.y));
+            s = __fadd_rn(s, __fmul_rn(qv.z, kv.z));
+            s = __fadd_rn(s, __fmul_rn(qv.w, kv.w));
+        }
+        sc[j] = __fdiv_rn(s, scale);
     }
     __syncthreads();
     float mx = -INFINITY;
-    for (int j = threadIdx.x; j < n; j += blockDim.x) mx = fmaxf(mx, sc[j]);
+    for (int j = threadIdx.x; j < n; j += AT_THREADS) mx = fmaxf(mx, sc[j]);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     if (lane == 0) s_red[warp] = mx;
     __syncthreads();
-    mx = fmaxf(fmaxf(s_red[0], s_red[1]), fmaxf(s_red[2], s_red[3]));
+    mx = s_red[0];
+#pragma unroll
+    for (int w = 1; w < AT_WARPS; ++w) mx = fmaxf(mx, s_red[w]);
     __syncthreads();
     float sum = 0.0f;
-    for (int j = threadIdx.x; j < n; j += blockDim.x) {
+    for (int j = threadIdx.x; j < n; j += AT_THREADS) {
         const float ex = expf(__fsub_rn(sc[j], mx));
         sc[j] = ex;
         sum += ex;
@@ -156,25 +183,54 @@ __global__ void __launch_bounds__(QW_HD) k_attention(const float *__restrict__ q
     for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
     if (lane == 0) s_red[warp] = sum;
     __syncthreads();
-    sum = (s_red[0] + s_red[1]) + (s_red[2] + s_red[3]);
-    for (int j = threadIdx.x; j < n; j += blockDim.x) sc[j] = __fdiv_rn(sc[j], sum);
+    sum = 0.0f;
+#pragma unroll
+    for (int w = 0; w < AT_WARPS; ++w) sum += s_red[w];
+    for (int j = threadIdx.x; j < n; j += AT_THREADS) sc[j] = __fdiv_rn(sc[j], sum);
     __syncthreads();
-    float acc = 0.0f;
-    const float *vp = vc + (size_t)kh * QW_HD + threadIdx.x;
-    for (int j = 0; j < n; ++j) acc = __fadd_rn(acc, __fmul_rn(sc[j], vp[(size_t)j * KV * QW_HD]));
-    ao[((size_t)i * H + h) * QW_HD + threadIdx.x] = acc;
+    const int per = (n + AT_WARPS - 1) / AT_WARPS;
+    const int j0 = warp * per, j1 = min(n, j0 + per);
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    const float *vb = vc + (size_t)kh * QW_HD + lane * 4;
+    int j = j0;
+    for (; j + 4 <= j1; j += 4) {                        // four rows in flight
+        float4 vv[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) vv[u] = __ldg(reinterpret_cast<const float4 *>(vb + (size_t)(j + u) * ks));
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const float p = sc[j + u];
+            acc.x = __fadd_rn(acc.x, __fmul_rn(p, vv[u].x));
+            acc.y = __fadd_rn(acc.y, __fmul_rn(p, vv[u].y));
+            acc.z = __fadd_rn(acc.z, __fmul_rn(p, vv[u].z));
+            acc.w = __fadd_rn(acc.w, __fmul_rn(p, vv[u].w));
+        }
+    }
+    for (; j < j1; ++j) {
+        const float4 v = __ldg(reinterpret_cast<const float4 *>(vb + (size_t)j * ks));
+        const float p = sc[j];
+        acc.x = __fadd_rn(acc.x, __fmul_rn(p, v.x));
+        acc.y = __fadd_rn(acc.y, __fmul_rn(p, v.y));
+        acc.z = __fadd_rn(acc.z, __fmul_rn(p, v.z));
+        acc.w = __fadd_rn(acc.w, __fmul_rn(p, v.w));
+    }
+    *reinterpret_cast<float4 *>(&s_out[warp][lane * 4]) = acc;
+    __syncthreads();
+    if (threadIdx.x < QW_HD) {
+        float o = 0.0f;
+#pragma unroll
+        for (int w = 0; w < AT_WARPS; ++w) o = __fadd_rn(o, s_out[w][threadIdx.x]);
+        ao[((size_t)i * H + h) * QW_HD + threadIdx.x] = o;
+    }
 }
 
-// argmax with the first maximum winning (cachepotato.c:353-356): one block, NaN-free logits.
-__global__ void __launch_bounds__(1024) k_argmax(const float *__restrict__ v, int n, int *out) {
+// argmax with the first maximum winning (cachepotato.c:353-356), NaN-free logits: each block
+// takes one contiguous chunk (partial results), then one block combines them; ties go to the
+// smaller index at every level.
+constexpr int AM_BLOCKS = 148;
+__device__ __forceinline__ void argmax_block(float best, int bi, float *out_v, int *out_i) {
     __shared__ float s_v[32];
     __shared__ int s_i[32];
-    float best = -INFINITY;
-    int bi = 0x7fffffff;
-    for (int j = threadIdx.x; j < n; j += blockDim.x) {
-        const float x = v[j];
-        if (x > best) { best = x; bi = j; }                 // j ascends: ties keep the first
-    }
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
@@ -187,8 +243,45 @@ __global__ void __launch_bounds__(1024) k_argmax(const float *__restrict__ v, in
     if (threadIdx.x == 0) {
         for (int w = 1; w < (int)(blockDim.x >> 5); ++w)
             if (s_v[w] > best || (s_v[w] == best && s_i[w] < bi)) { best = s_v[w]; bi = s_i[w]; }
-        *out = bi;
+        *out_v = best;
+        *out_i = bi;
     }
+}
+
+__global__ void __launch_bounds__(512) k_argmax_part(const float *__restrict__ v, int n, float *part_v, int *part_i) {
+    const int chunk = (n + gridDim.x - 1) / gridDim.x;
+    const int lo = blockIdx.x * chunk, hi = min(n, lo + chunk);
+    float best = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int j = lo + threadIdx.x; j < hi; j += blockDim.x) {
+        const float x = v[j];
+        if (x > best) { best = x; bi = j; }                 // j ascends: ties keep the first
+    }
+    argmax_block(best, bi, part_v + blockIdx.x, part_i + blockIdx.x);
+}
+
+__global__ void __launch_bounds__(256) k_argmax_final(const float *__restrict__ part_v, const int *__restrict__ part_i,
+                                                       int nparts, int *out) {
+    __shared__ float s_best;
+    float best = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int j = threadIdx.x; j < nparts; j += blockDim.x) {
+        const float x = part_v[j];
+        const int i = part_i[j];
+        if (x > best || (x == best && i < bi)) { best = x; bi = i; }
+    }
+    argmax_block(best, bi, &s_best, out);
+}
+
+// After a step: the argmax becomes the next step's input id, the position advances, and the id
+// is recorded at out[*d_pos - base] when out is given.
+__global__ void k_advance(const int *__restrict__ next, int *__restrict__ ids, int *__restrict__ d_pos, int T,
+                          int *__restrict__ out, int base) {
+    const int id = *next;
+    const int p = *d_pos + T;
+    *d_pos = p;
+    ids[0] = id;
+    if (out) out[p - base] = id;
 }
 
 int matvec_launch(float *out, const float *x, cpg_tensor w, int n_in, int n_out, int T, cudaStream_t s);
@@ -204,7 +297,11 @@ struct cpg_qwen3 {
     std::vector<cpg_qwen3_attn> attn;
     std::vector<const cpg_moe_layer *> moe;
     float *x = nullptr, *xn = nullptr, *q = nullptr, *ao = nullptr, *at = nullptr, *kv = nullptr, *logits = nullptr;
-    int *d_ids = nullptr, *d_next = nullptr, *h_next = nullptr;
+    float *kst = nullptr, *vst = nullptr;          // (max_ctx, KV·hd) k and v before the cache
+    float *am_v = nullptr;                         // argmax partials
+    int *am_i = nullptr;
+    int *d_ids = nullptr, *d_next = nullptr, *h_next = nullptr, *d_pos = nullptr, *d_out = nullptr;
+    cudaGraphExec_t step_graph = nullptr;          // one decode step, T = 1, any position
     void *ws = nullptr;
     size_t ws_bytes = 0;
     int pos = 0;
@@ -216,6 +313,9 @@ using namespace cpg;
 static void qwen3_free(cpg_qwen3 *m) {
     cudaFree(m->x); cudaFree(m->xn); cudaFree(m->q); cudaFree(m->ao); cudaFree(m->at); cudaFree(m->kv);
     cudaFree(m->logits); cudaFree(m->d_ids); cudaFree(m->d_next); cudaFree(m->ws);
+    cudaFree(m->kst); cudaFree(m->vst); cudaFree(m->d_pos); cudaFree(m->d_out);
+    cudaFree(m->am_v); cudaFree(m->am_i);
+    if (m->step_graph) cudaGraphExecDestroy(m->step_graph);
     if (m->h_next) cudaFreeHost(m->h_next);
     if (m->s) cudaStreamDestroy(m->s);
     delete m;
@@ -257,11 +357,29 @@ extern "C" int cpg_qwen3_create(const cpg_qwen3_desc *d, cpg_qwen3 **out) {
     if (ce == cudaSuccess) ce = cudaMalloc(&m->logits, (size_t)d->vocab * 4);
     if (ce == cudaSuccess) ce = cudaMalloc(&m->d_ids, C * 4);
     if (ce == cudaSuccess) ce = cudaMalloc(&m->d_next, 4);
+    if (ce == cudaSuccess) ce = cudaMalloc(&m->kst, C * KD * 4);
+    if (ce == cudaSuccess) ce = cudaMalloc(&m->vst, C * KD * 4);
+    if (ce == cudaSuccess) ce = cudaMalloc(&m->d_pos, 4);
+    if (ce == cudaSuccess) ce = cudaMalloc(&m->am_v, AM_BLOCKS * 4);
+    if (ce == cudaSuccess) ce = cudaMalloc(&m->am_i, AM_BLOCKS * 4);
+    if (ce == cudaSuccess) ce = cudaMalloc(&m->d_out, (C + 1) * 4);
     if (ce == cudaSuccess) ce = cudaMallocHost(&m->h_next, 4);
     if (ce == cudaSuccess) ce = cudaMalloc(&m->ws, m->ws_bytes);
     if (ce != cudaSuccess) {
         qwen3_free(m);
         return cuda_fail(ce, "cpg_qwen3_create: allocation");
+    }
+    const size_t asmem = C * sizeof(float);            // attention scores of every position
+    if (asmem > 32 * 1024) {                           // beyond the default with the static arrays
+        if (asmem > 200 * 1024) {
+            qwen3_free(m);
+            CPG_REQUIRE(false, "cpg_qwen3_create: max_ctx %d too long for the attention kernel", d->max_ctx);
+        }
+        ce = cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)asmem);
+        if (ce != cudaSuccess) {
+            qwen3_free(m);
+            return cuda_fail(ce, "cpg_qwen3_create: attention shared memory");
+        }
     }
     *out = m;
     return CPG_OK;
@@ -271,12 +389,10 @@ extern "C" void cpg_qwen3_destroy(cpg_qwen3 *m) {
     if (m) qwen3_free(m);
 }
 
-// T tokens (ids already in m->d_ids[0..T)) at positions m->pos.. through embed, the layers and the
-// head; the argmax lands in m->d_next.
-static int qwen3_forward(cpg_qwen3 *m, int T) {
-    CPG_REQUIRE(T > 0 && m->pos + T <= m->max_ctx, "cpg_qwen3: %d tokens at position %d exceed max_ctx %d", T, m->pos,
-                m->max_ctx);
-    cudaStream_t s = m->s;
+// Enqueue T tokens (ids in m->d_ids[0..T)) at the device position *d_pos through embed, the
+// layers and the head; the argmax lands in m->d_next. Nothing here depends on the position on
+// the host, so the T = 1 sequence is captured once and replayed for every decode step.
+static int qwen3_enqueue(cpg_qwen3 *m, int T, cudaStream_t s) {
     const int D = m->D, H = m->H, KV = m->KV, QD = H * QW_HD, KD = KV * QW_HD;
     const size_t C = (size_t)m->max_ctx;
     k_embed<<<T, 256, 0, s>>>((const uint8_t *)m->embed.p, m->embed.enc, m->d_ids, D, m->x);
@@ -287,18 +403,15 @@ static int qwen3_forward(cpg_qwen3 *m, int T) {
         k_rmsnorm<<<T, 256, 0, s>>>(m->x, A.ln1, D, m->eps, m->xn);
         CPG_CUDA(cudaGetLastError());
         int rc = matvec_launch(m->q, m->xn, A.wq, D, QD, T, s);
-        if (!rc) rc = matvec_launch(kc + (size_t)m->pos * KD, m->xn, A.wk, D, KD, T, s);
-        if (!rc) rc = matvec_launch(vc + (size_t)m->pos * KD, m->xn, A.wv, D, KD, T, s);
+        if (!rc) rc = matvec_launch(m->kst, m->xn, A.wk, D, KD, T, s);
+        if (!rc) rc = matvec_launch(m->vst, m->xn, A.wv, D, KD, T, s);
         if (rc) return rc;
         const int warps = T * (H + KV);
-        k_qk_norm_rope<<<(warps + 7) / 8, 256, 0, s>>>(m->q, kc, T, m->pos, H, KV, A.q_norm, A.k_norm, m->theta,
-                                                       m->eps);
+        k_qk_norm_rope<<<(warps + 7) / 8, 256, 0, s>>>(m->q, m->kst, m->vst, kc, vc, T, m->d_pos, H, KV, A.q_norm,
+                                                       A.k_norm, m->theta, m->eps);
         CPG_CUDA(cudaGetLastError());
-        const size_t asmem = (size_t)(m->pos + T) * sizeof(float);
-        CPG_REQUIRE(asmem <= 160 * 1024, "cpg_qwen3: context %d too long for the attention kernel", m->pos + T);
-        if (asmem > 48 * 1024)
-            CPG_CUDA(cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)asmem));
-        k_attention<<<dim3(H, T), QW_HD, asmem, s>>>(m->q, kc, vc, m->pos, H, KV, m->ao);
+        const size_t asmem = (size_t)m->max_ctx * sizeof(float);     // scores of every cached position
+        k_attention<<<dim3(H, T), AT_THREADS, asmem, s>>>(m->q, kc, vc, m->d_pos, H, KV, m->ao);
         CPG_CUDA(cudaGetLastError());
         rc = matvec_launch(m->at, m->ao, A.wo, QD, D, T, s);
         if (rc) return rc;
@@ -310,9 +423,33 @@ static int qwen3_forward(cpg_qwen3 *m, int T) {
     CPG_CUDA(cudaGetLastError());
     int rc = matvec_launch(m->logits, m->xn, m->lm_head, D, m->V, 1, s);
     if (rc) return rc;
-    k_argmax<<<1, 1024, 0, s>>>(m->logits, m->V, m->d_next);
+    k_argmax_part<<<AM_BLOCKS, 512, 0, s>>>(m->logits, m->V, m->am_v, m->am_i);
+    k_argmax_final<<<1, 256, 0, s>>>(m->am_v, m->am_i, AM_BLOCKS, m->d_next);
     CPG_CUDA(cudaGetLastError());
-    m->pos += T;
+    return CPG_OK;
+}
+
+// One token at the current device position: the captured step graph (built on first use).
+static int qwen3_step_device(cpg_qwen3 *m, int *out, int base) {
+    CPG_REQUIRE(m->pos + 1 <= m->max_ctx, "cpg_qwen3: position %d reached max_ctx %d", m->pos, m->max_ctx);
+    if (!m->step_graph) {
+        cudaGraph_t g = nullptr;
+        CPG_CUDA(cudaStreamBeginCapture(m->s, cudaStreamCaptureModeThreadLocal));
+        int rc = qwen3_enqueue(m, 1, m->s);
+        const cudaError_t ce = cudaStreamEndCapture(m->s, &g);
+        if (rc) {
+            if (g) cudaGraphDestroy(g);
+            return rc;
+        }
+        if (ce != cudaSuccess) return cuda_fail(ce, "cpg_qwen3: step capture");
+        const cudaError_t ie = cudaGraphInstantiate(&m->step_graph, g, 0);
+        cudaGraphDestroy(g);
+        if (ie != cudaSuccess) return cuda_fail(ie, "cpg_qwen3: step instantiate");
+    }
+    CPG_CUDA(cudaGraphLaunch(m->step_graph, m->s));
+    k_advance<<<1, 1, 0, m->s>>>(m->d_next, m->d_ids, m->d_pos, 1, out, base);
+    CPG_CUDA(cudaGetLastError());
+    m->pos += 1;
     return CPG_OK;
 }
 
@@ -328,16 +465,21 @@ extern "C" int cpg_qwen3_prefill(cpg_qwen3 *m, const int *ids, int T, int *next_
     CPG_REQUIRE(T <= m->max_ctx, "cpg_qwen3_prefill: %d tokens > max_ctx %d", T, m->max_ctx);
     for (int t = 0; t < T; ++t) CPG_REQUIRE(ids[t] >= 0 && ids[t] < m->V, "cpg_qwen3_prefill: id %d out of range", ids[t]);
     m->pos = 0;
+    CPG_CUDA(cudaMemsetAsync(m->d_pos, 0, 4, m->s));
     CPG_CUDA(cudaMemcpyAsync(m->d_ids, ids, sizeof(int) * (size_t)T, cudaMemcpyHostToDevice, m->s));
-    const int rc = qwen3_forward(m, T);
+    const int rc = qwen3_enqueue(m, T, m->s);
     if (rc) return rc;
+    k_advance<<<1, 1, 0, m->s>>>(m->d_next, m->d_ids, m->d_pos, T, nullptr, 0);
+    CPG_CUDA(cudaGetLastError());
+    m->pos = T;
     return qwen3_read_next(m, next_id);
 }
 
 extern "C" int cpg_qwen3_step(cpg_qwen3 *m, int id, int *next_id) {
     CPG_REQUIRE(m && id >= 0 && id < m->V, "cpg_qwen3_step: bad argument");
-    CPG_CUDA(cudaMemcpyAsync(m->d_ids, &id, sizeof(int), cudaMemcpyHostToDevice, m->s));
-    const int rc = qwen3_forward(m, 1);
+    *m->h_next = id;
+    CPG_CUDA(cudaMemcpyAsync(m->d_ids, m->h_next, sizeof(int), cudaMemcpyHostToDevice, m->s));
+    const int rc = qwen3_step_device(m, nullptr, 0);
     if (rc) return rc;
     return qwen3_read_next(m, next_id);
 }
@@ -348,14 +490,15 @@ extern "C" int cpg_qwen3_generate(cpg_qwen3 *m, const int *prompt, int n_prompt,
     int rc = cpg_qwen3_prefill(m, prompt, n_prompt, &next);
     if (rc) return rc;
     out_ids[0] = next;
+    // the argmax stays on the device: each step embeds the previous one and records it at
+    // d_out[position - prompt]; the ids come back once at the end
     for (int i = 1; i <= n_new; ++i) {
-        // the argmax stays on the device: the next step embeds it directly
-        CPG_CUDA(cudaMemcpyAsync(m->d_ids, m->d_next, 4, cudaMemcpyDeviceToDevice, m->s));
-        rc = qwen3_forward(m, 1);
+        rc = qwen3_step_device(m, m->d_out, n_prompt);
         if (rc) return rc;
-        rc = qwen3_read_next(m, &next);
-        if (rc) return rc;
-        out_ids[i] = next;
+    }
+    if (n_new > 0) {
+        CPG_CUDA(cudaMemcpyAsync(out_ids + 1, m->d_out + 1, sizeof(int) * (size_t)n_new, cudaMemcpyDeviceToHost, m->s));
+        CPG_CUDA(cudaStreamSynchronize(m->s));
     }
     return CPG_OK;
 }
