@@ -260,19 +260,35 @@ __global__ void __launch_bounds__(R_THREADS) k_router(RouterArgs a) {
     }
     __syncthreads();
 
-    // hh = x + attn (qwen3_moe.c:178)
+    // hh = x + attn (qwen3_moe.c:178). The loads are issued 16 at a time per thread before any
+    // store, so the tile costs about one memory round trip (the kernel is latency-bound).
     {
         const float4 *x4 = reinterpret_cast<const float4 *>(a.x + (size_t)t0 * D);
         const float4 *a4 = a.attn ? reinterpret_cast<const float4 *>(a.attn + (size_t)t0 * D) : nullptr;
         float4 *s4 = reinterpret_cast<float4 *>(xs);
-#pragma unroll 8
-        for (int i = tid; i < nt * D / 4; i += R_THREADS) {
-            float4 v = x4[i];
-            if (a4) {
-                const float4 b = a4[i];
-                v.x += b.x; v.y += b.y; v.z += b.z; v.w += b.w;
+        const int n4 = nt * D / 4;
+        for (int i0 = tid; i0 < n4; i0 += 16 * R_THREADS) {
+            float4 v[16];
+#pragma unroll
+            for (int u = 0; u < 16; ++u) {
+                const int i = i0 + u * R_THREADS;
+                if (i < n4) v[u] = __ldg(x4 + i);
             }
-            s4[i] = v;
+            if (a4) {
+#pragma unroll
+                for (int u = 0; u < 16; ++u) {
+                    const int i = i0 + u * R_THREADS;
+                    if (i < n4) {
+                        const float4 b = __ldg(a4 + i);
+                        v[u].x += b.x; v[u].y += b.y; v[u].z += b.z; v[u].w += b.w;
+                    }
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < 16; ++u) {
+                const int i = i0 + u * R_THREADS;
+                if (i < n4) s4[i] = v[u];
+            }
         }
     }
     __syncthreads();
@@ -284,8 +300,26 @@ __global__ void __launch_bounds__(R_THREADS) k_router(RouterArgs a) {
         for (int k = lane; k < D; k += 32) ss = fmaf(row[k], row[k], ss);
         ss = warp_sum(ss);
         const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fdiv_rn(ss, (float)D) + a.eps));
-#pragma unroll 8
-        for (int k = lane; k < D; k += 32) row[k] = __fmul_rn(__fmul_rn(row[k], inv), __ldg(a.ln2 + k));
+        const float4 *g4 = reinterpret_cast<const float4 *>(a.ln2);
+        float4 *r4 = reinterpret_cast<float4 *>(row);
+        for (int c0 = lane; c0 < D / 4; c0 += 16 * 32) {
+            float4 gv[16];
+#pragma unroll
+            for (int u = 0; u < 16; ++u)
+                if (c0 + u * 32 < D / 4) gv[u] = __ldg(g4 + c0 + u * 32);
+#pragma unroll
+            for (int u = 0; u < 16; ++u) {
+                const int c = c0 + u * 32;
+                if (c < D / 4) {
+                    float4 v = r4[c];
+                    v.x = __fmul_rn(__fmul_rn(v.x, inv), gv[u].x);
+                    v.y = __fmul_rn(__fmul_rn(v.y, inv), gv[u].y);
+                    v.z = __fmul_rn(__fmul_rn(v.z, inv), gv[u].z);
+                    v.w = __fmul_rn(__fmul_rn(v.w, inv), gv[u].w);
+                    r4[c] = v;
+                }
+            }
+        }
         __syncwarp();
         if (blockIdx.x == 0) {
             // fp16 copy of xn in the expert kernels' K order
@@ -303,17 +337,27 @@ __global__ void __launch_bounds__(R_THREADS) k_router(RouterArgs a) {
 #pragma unroll
         for (int t = 0; t < R_TB; ++t) acc[t] = 0.0f;
         const float4 *w4 = reinterpret_cast<const float4 *>(a.wgate + (size_t)e * D);
-#pragma unroll 4
-        for (int k = lane * 4; k < D; k += 128) {
-            const float4 w = __ldg(w4 + k / 4);
+        // the row's loads (16 float4 per lane for D = 2048) are all in flight before the FMAs;
+        // per lane the sum still runs over k ascending
+        for (int c0 = 0; c0 < D / 128; c0 += 16) {
+            float4 w[16];
 #pragma unroll
-            for (int t = 0; t < R_TB; ++t) {
-                if (t < nt) {
-                    const float4 v = *reinterpret_cast<const float4 *>(xs + t * D + k);
-                    acc[t] = fmaf(w.x, v.x, acc[t]);
-                    acc[t] = fmaf(w.y, v.y, acc[t]);
-                    acc[t] = fmaf(w.z, v.z, acc[t]);
-                    acc[t] = fmaf(w.w, v.w, acc[t]);
+            for (int c = 0; c < 16; ++c)
+                if (c0 + c < D / 128) w[c] = __ldg(w4 + (c0 + c) * 32 + lane);
+#pragma unroll
+            for (int c = 0; c < 16; ++c) {
+                if (c0 + c < D / 128) {
+                    const int k = ((c0 + c) * 32 + lane) * 4;
+#pragma unroll
+                    for (int t = 0; t < R_TB; ++t) {
+                        if (t < nt) {
+                            const float4 v = *reinterpret_cast<const float4 *>(xs + t * D + k);
+                            acc[t] = fmaf(w[c].x, v.x, acc[t]);
+                            acc[t] = fmaf(w[c].y, v.y, acc[t]);
+                            acc[t] = fmaf(w[c].z, v.z, acc[t]);
+                            acc[t] = fmaf(w[c].w, v.w, acc[t]);
+                        }
+                    }
                 }
             }
         }
@@ -944,7 +988,7 @@ int cpg::moe_forward_impl(const cpg_moe_layer *L, const float *x, const float *a
     ra.act_ptr = (const uint8_t **)(w + W.act_ptr);
     ra.pairs = (int *)(w + W.pairs);
     // few tokens: spread the 1 MiB router over more CTAs; many: normalise each token fewer times
-    ra.eb = T <= R_TB ? 4 : 16;
+    ra.eb = T <= R_TB ? 4 : 8;                 // one expert row per warp: 128 CTAs at T = 64
     const dim3 rgrid((L->E + ra.eb - 1) / ra.eb, (T + R_TB - 1) / R_TB);
     CPG_CUDA(launch_pdl(k_router, rgrid, dim3(R_THREADS), (size_t)R_TB * L->D * sizeof(float), s, ra));
     CPG_CUDA(launch_pdl(k_route, dim3((T + RT_THREADS / 32 - 1) / (RT_THREADS / 32)), dim3(RT_THREADS), 0, s, ra));
