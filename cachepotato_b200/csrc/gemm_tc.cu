@@ -470,28 +470,34 @@ static EncodeTiledFn encode_tiled() {
     return fn;
 }
 
-int gemm_tc_build_weight_maps(const uint8_t *const *h_ptrs, int E, int D, int F, void **d_maps) {
+int build_row_maps(const uint8_t *const *h_ptrs, int E, int D, int F, int wenc, int rows_gu, int rows_dn,
+                   void **d_maps) {
     EncodeTiledFn enc = encode_tiled();
     if (!enc) {
-        set_error("grouped GEMM: cuTensorMapEncodeTiled is unavailable from the driver");
+        set_error("cuTensorMapEncodeTiled is unavailable from the driver");
         return CPG_ECUDA;
     }
+    const int gb = wenc == CPG_ENC_Q4 ? 18 : 34;
+    // a box is 256 K values of each row: 8 groups (144 B for Q4_0 as bytes, 272 B for Q8_0 as
+    // 16-bit elements, since a box dimension holds at most 256 elements)
+    const int esz = wenc == CPG_ENC_Q4 ? 1 : 2;
     CUtensorMap *h = (CUtensorMap *)malloc(sizeof(CUtensorMap) * 3 * (size_t)E);
     CPG_REQUIRE(h != nullptr, "host allocation failed");
     for (int i = 0; i < 3 * E; ++i) {
         const int kind = i % 3;                               // 0 gate, 1 up: (F, D); 2 down: (D, F)
         const int n_in = kind == 2 ? F : D, n_out = kind == 2 ? D : F;
-        const cuuint64_t rb = (cuuint64_t)(n_in / 32) * 18;
-        const cuuint64_t dims[2] = {rb, (cuuint64_t)n_out};
+        const cuuint64_t rb = (cuuint64_t)(n_in / 32) * gb;
+        const cuuint64_t dims[2] = {rb / esz, (cuuint64_t)n_out};
         const cuuint64_t strides[1] = {rb};
-        const cuuint32_t box[2] = {TC_RAW_ROW, TC_BM};
+        const cuuint32_t box[2] = {(cuuint32_t)(8 * gb / esz), (cuuint32_t)(kind == 2 ? rows_dn : rows_gu)};
         const cuuint32_t estr[2] = {1, 1};
-        const CUresult r = enc(&h[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t *>(h_ptrs[i]), dims, strides,
-                               box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+        const CUresult r = enc(&h[i], esz == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_UINT16, 2,
+                               const_cast<uint8_t *>(h_ptrs[i]), dims, strides, box, estr,
+                               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
                                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
         if (r != CUDA_SUCCESS) {
             free(h);
-            set_error("grouped GEMM: tensor map of expert %d kind %d failed (%d)", i / 3, kind, (int)r);
+            set_error("tensor map of expert %d kind %d failed (%d)", i / 3, kind, (int)r);
             return CPG_ECUDA;
         }
     }
@@ -501,10 +507,14 @@ int gemm_tc_build_weight_maps(const uint8_t *const *h_ptrs, int E, int D, int F,
     free(h);
     if (ce != cudaSuccess) {
         cudaFree(d);
-        return cuda_fail(ce, "grouped GEMM: tensor map upload");
+        return cuda_fail(ce, "tensor map upload");
     }
     *d_maps = d;
     return CPG_OK;
+}
+
+int gemm_tc_build_weight_maps(const uint8_t *const *h_ptrs, int E, int D, int F, void **d_maps) {
+    return build_row_maps(h_ptrs, E, D, F, CPG_ENC_Q4, TC_BM, TC_BM, d_maps);
 }
 
 int gemm_tc_launch(int kind, const TcArgs &a, const __half *b, int b_rows, int max_tiles, cudaStream_t s) {

@@ -402,20 +402,25 @@ struct ExpertArgs {
     int *status;
     int *item_ctr;               // dynamic work counter (zeroed with the header)
     int stages;
-    int rs;                      // shared-memory row stride (bytes)
+    const void *maps;            // (E, 3) TMA tensor maps over the expert matrices (256-value K slices)
 };
 
+// An item is one row block of one active expert for one chunk of its tokens; it streams through
+// the stage ring in K slices of 256 values (eight groups per row: 144 B of Q4_0, 272 B of Q8_0).
+// GATEUP: 64 gate rows + the same 64 up rows, warp w holds matrix w & 1, 16-row tile w >> 1.
+// DOWN: 128 rows of Wd, warp w holds tile w. Every warp keeps its rows over the whole K.
+constexpr int EX_KSL = 256;
 template <int ENC, int KIND>
 struct ExCfg {
     static constexpr int GB = ENC == CPG_ENC_Q4 ? 18 : 34;
+    static constexpr int SLB = 8 * GB;                        // bytes of one row's K slice
     static constexpr int MATS = KIND == KIND_GATEUP ? 2 : 1;
-    static constexpr int MT = KIND == KIND_GATEUP ? 1 : 4;   // 16-row tiles per matrix per item
-    static constexpr int COMBOS = MATS * MT;                  // 16-row tiles per item
-    static constexpr int KS = EX_NW / COMBOS;                 // K split across warps
-    static constexpr int ROWS = 16 * MT;                      // output rows per item per matrix
+    static constexpr int RB = KIND == KIND_GATEUP ? 64 : 128; // rows per matrix per item
+    static constexpr int STAGE = MATS * RB * SLB;
+    static constexpr int WPAIR = GB / 2;                       // 32-bit words per group pair
 };
 
-struct StageMeta { int item, m, off, cnt; };     // off/cnt: this item's token chunk
+struct StageMeta { int item, m, off, cnt, s, pad; };   // off/cnt: the item's token chunk; s: K slice
 
 template <int ENC>
 __device__ __forceinline__ void load_pair_words(const uint32_t *row, int P, int t, uint32_t &w1,
@@ -530,45 +535,49 @@ __device__ __forceinline__ void group_pair_mma(const uint32_t *rowg, const uint3
     }
 }
 
-// This warp's share of the K split (group pairs kp, kp+KS, ...), operands loaded one group pair
-// ahead into two alternating buffers.
-template <int ENC, int KS, int NTL>
-__device__ __forceinline__ void expert_item_loop(const uint32_t *rowg, const uint32_t *rowg8,
-                                                 const __half *const (&brow)[EX_NCH], int NP, int kp, int t,
-                                                 float (&acc)[EX_NCH][4]) {
+// Group pairs p0..p0+3 of one K slice (pair index in the slice: 0..3), B loaded one pair ahead.
+template <int ENC, int NTL>
+__device__ __forceinline__ void slice_mma(const uint32_t *rowg, const uint32_t *rowg8, const __half *const (&brow)[EX_NCH],
+                                          int P0, int t, float (&acc)[EX_NCH][4]) {
     uint4 b0[EX_NCH][2], b1[EX_NCH][2];
-    load_b<NTL>(brow, kp, b0);
-    for (int P = kp; P < NP; P += 2 * KS) {
-        const int P1 = P + KS;
-        load_b<NTL>(brow, P1 < NP ? P1 : P, b1);
-        group_pair_mma<ENC, NTL>(rowg, rowg8, P, t, b0, acc);
-        if (P1 >= NP) break;
-        const int P2 = P1 + KS;
-        load_b<NTL>(brow, P2 < NP ? P2 : P1, b0);
-        group_pair_mma<ENC, NTL>(rowg, rowg8, P1, t, b1, acc);
-    }
+    load_b<NTL>(brow, P0, b0);
+    load_b<NTL>(brow, P0 + 1, b1);
+    group_pair_mma<ENC, NTL>(rowg, rowg8, 0, t, b0, acc);
+    load_b<NTL>(brow, P0 + 2, b0);
+    group_pair_mma<ENC, NTL>(rowg, rowg8, 1, t, b1, acc);
+    load_b<NTL>(brow, P0 + 3, b1);
+    group_pair_mma<ENC, NTL>(rowg, rowg8, 2, t, b0, acc);
+    group_pair_mma<ENC, NTL>(rowg, rowg8, 3, t, b1, acc);
+}
+
+__device__ __forceinline__ void tma_load_2d_map(void *dst, const void *map, int x, int y, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+        ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
 }
 
 template <int ENC, int KIND>
 __global__ void __launch_bounds__((1 + EX_NW) * 32, 2) k_experts(ExpertArgs a) {
     using C = ExCfg<ENC, KIND>;
-    extern __shared__ __align__(128) uint8_t smem[];
+    // Dynamic shared memory starts after the static arrays, 16-byte aligned only; the stages
+    // (2D tensor TMA destinations) need 128 bytes, so the base moves up (the launch adds the
+    // slack). Layout: stages | gate-sum exchange | barriers | stage metadata.
+    extern __shared__ __align__(16) uint8_t smem_raw[];
+    uint8_t *const smem = smem_raw + ((128u - (smem_u32(smem_raw) & 127u)) & 127u);
     __shared__ Perm64 s_perm;
     __shared__ int s_abort;
     __shared__ int4 s_act[MAX_E + 1];
-    __shared__ const uint8_t *s_ptr[MAX_E][C::MATS];
-    const int S = a.stages, RS = a.rs;
+    const int S = a.stages;
     const int K_in = KIND == KIND_GATEUP ? a.D : a.F;
     const int n_rows = KIND == KIND_GATEUP ? a.F : a.D;
-    const int RB = (K_in / 32) * C::GB;
-    const int NP = K_in / 64;
-    const int stage_bytes = C::COMBOS * 16 * RS;
-    float *red = reinterpret_cast<float *>(smem + (size_t)S * stage_bytes);     // (NW, NCH, 32, 4)
-    StageMeta *meta = reinterpret_cast<StageMeta *>(red + EX_NW * EX_NCH * 128);
-    uint64_t *full = reinterpret_cast<uint64_t *>(meta + S);
+    const int NS = K_in / EX_KSL;                              // K slices per item
+    float *xbuf = reinterpret_cast<float *>(smem + (size_t)S * C::STAGE);      // (4 tiles, NCH, 32, 4) gate sums
+    uint64_t *full = reinterpret_cast<uint64_t *>(xbuf + 4 * EX_NCH * 128);
     uint64_t *empty = full + S;
+    StageMeta *meta = reinterpret_cast<StageMeta *>(empty + S);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int tiles = n_rows / C::ROWS;
+    const int tiles = n_rows / C::RB;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
@@ -586,152 +595,145 @@ __global__ void __launch_bounds__((1 + EX_NW) * 32, 2) k_experts(ExpertArgs a) {
     pdl_wait();                                  // routing table from k_route / h from gate-up
     pdl_launch_dependents();
     const int U = *a.n_active;
-    for (int u = threadIdx.x; u <= U; u += blockDim.x) {
-        s_act[u] = a.act[u];
-        if (u < U) {
-#pragma unroll
-            for (int mat = 0; mat < C::MATS; ++mat)
-                s_ptr[u][mat] = a.act_ptr[3 * u + (KIND == KIND_GATEUP ? mat : 2)];
-        }
-    }
+    for (int u = threadIdx.x; u <= U; u += blockDim.x) s_act[u] = a.act[u];
     __syncthreads();
     const int total = tiles * s_act[U].w;
 
     if (warp == 0) {
-        // ---------------- producer: one thread streams weight rows into the stage ring
+        // ---------------- producer: one thread, one 2D tensor box per matrix and K slice
         if (lane != 0) return;
+        const uint8_t *maps = reinterpret_cast<const uint8_t *>(a.maps);
+        constexpr int MAPB = 128;                              // sizeof(CUtensorMap)
+        constexpr int XSTEP = ENC == CPG_ENC_Q4 ? C::SLB : C::SLB / 2;   // box x step in elements
         int it = 0;
-        bool ok = true;
-        for (;; ++it) {
-            const int st = it % S;
-            const uint32_t ph = (uint32_t)(it / S) & 1u;
-            if (it >= S && !mbar_wait(&empty[st], ph ^ 1u)) {
-                atomicCAS(a.status + WS_STATUS, ST_OK, ST_TIMEOUT_EMPTY);
-                ok = false;
-                break;
-            }
+        bool ok = true, done = false;
+        while (!done) {
             const int item = atomicAdd(a.item_ctr, 1);
-            if (item >= total) {
-                meta[st].item = -1;
-                mbar_arrive(&full[st]);
-                ++it;
-                break;
-            }
-            int u, m, c;
-            decode_item(s_act, U, tiles, item, u, m, c);
+            int u = 0, m = 0, c = 0;
+            if (item < total) decode_item(s_act, U, tiles, item, u, m, c);
             const int4 ex = s_act[u];
             const int c0 = c * EX_NCHUNK;
-            meta[st] = StageMeta{item, m, ex.y + c0, min(EX_NCHUNK, ex.z - c0)};
-            mbar_arrive_expect_tx(&full[st], (uint32_t)(C::COMBOS * 16 * RB));
-            uint8_t *dst = smem + (size_t)st * stage_bytes;
-#pragma unroll
-            for (int cb = 0; cb < C::COMBOS; ++cb) {
-                const int mat = KIND == KIND_GATEUP ? cb : 0;         // gate, up / down
-                const int r0 = m * C::ROWS + (KIND == KIND_GATEUP ? 0 : cb * 16);
-                const uint8_t *src = s_ptr[u][mat] + (size_t)r0 * RB;
-                uint8_t *d = dst + cb * 16 * RS;
-                if (RS == RB) {
-                    bulk_g2s(d, src, 16 * RB, &full[st]);
+            for (int sl = 0; sl < (item < total ? NS : 1); ++sl, ++it) {
+                const int st = it % S;
+                if (it >= S && !mbar_wait(&empty[st], (uint32_t)(it / S - 1) & 1u)) {
+                    atomicCAS(a.status + WS_STATUS, ST_OK, ST_TIMEOUT_EMPTY);
+                    ok = false;
+                    break;
+                }
+                if (item >= total) {                           // sentinel: no more items
+                    meta[st].item = -1;
+                    mbar_arrive(&full[st]);
+                    done = true;
+                    ++it;
+                    break;
+                }
+                meta[st] = StageMeta{item, m, ex.y + c0, min(EX_NCHUNK, ex.z - c0), sl};
+                mbar_arrive_expect_tx(&full[st], (uint32_t)C::STAGE);
+                uint8_t *dst = smem + (size_t)st * C::STAGE;
+                const int e = ex.x;
+                if (KIND == KIND_GATEUP) {
+                    tma_load_2d_map(dst, maps + (size_t)(3 * e + 0) * MAPB, sl * XSTEP, m * C::RB, &full[st]);
+                    tma_load_2d_map(dst + C::RB * C::SLB, maps + (size_t)(3 * e + 1) * MAPB, sl * XSTEP, m * C::RB, &full[st]);
                 } else {
-                    for (int r = 0; r < 16; ++r) bulk_g2s(d + r * RS, src + (size_t)r * RB, RB, &full[st]);
+                    tma_load_2d_map(dst, maps + (size_t)(3 * e + 2) * MAPB, sl * XSTEP, m * C::RB, &full[st]);
                 }
             }
+            if (!ok) break;
         }
-        // keep the CTA alive until every issued copy has landed (also on the timeout path)
-        if (!ok) {
-            for (int k = 1; k <= S && it - k >= 0; ++k) {
-                const int j = it - k;
-                mbar_wait(&full[j % S], (uint32_t)(j / S) & 1u);
-            }
+        // keep the CTA alive until every issued copy has landed (bounded)
+        for (int k = 1; k <= S && it - k >= 0; ++k) {
+            const int j = it - k;
+            mbar_wait(&full[j % S], (uint32_t)(j / S) & 1u);
         }
         return;
     }
 
-    // ---------------- consumers
+    // ---------------- consumers: warp cw owns 16 rows of one matrix over the whole K
     const int cw = warp - 1;
-    const int combo = cw % C::COMBOS, kp = cw / C::COMBOS;
+    const int mat = KIND == KIND_GATEUP ? (cw & 1) : 0;
+    const int tile = KIND == KIND_GATEUP ? (cw >> 1) : cw;
     const int g = lane >> 2, t = lane & 3;
+    const __half *brow[EX_NCH];
+    float acc[EX_NCH][4];
+    bool two = false;
     for (int it = 0;; ++it) {
         const int st = it % S;
-        const uint32_t ph = (uint32_t)(it / S) & 1u;
-        // every consumer warp reaches the barrier (the wait is bounded), so a timeout seen by
-        // any warp ends the loop for all of them at the same point
-        if (!mbar_wait(&full[st], ph) && lane == 0) {
-            s_abort = 1;
-            atomicCAS(a.status + WS_STATUS, ST_OK, ST_TIMEOUT_FULL);
+        if (!mbar_wait(&full[st], (uint32_t)(it / S) & 1u)) {
+            if (lane == 0) atomicCAS(a.status + WS_STATUS, ST_OK, ST_TIMEOUT_FULL);
+            break;
         }
-        named_bar_sync(1, EX_NW * 32);
-        if (s_abort) break;
         const StageMeta md = meta[st];
         if (md.item < 0) break;
-        const uint32_t *rows = reinterpret_cast<const uint32_t *>(smem + (size_t)st * stage_bytes + combo * 16 * RS);
-        const uint32_t *rowg = rows + (g * RS) / 4;
-        const uint32_t *rowg8 = rows + ((g + 8) * RS) / 4;
-        const bool two = md.cnt > 8;                 // second 8-token MMA tile in use
-        // operand rows for column g of both 8-token tiles (the zero row pads short chunks)
-        const __half *brow[EX_NCH];
+        if (md.s == 0) {                                   // a new item: its token columns
+            two = md.cnt > 8;
 #pragma unroll
-        for (int nt = 0; nt < EX_NCH; ++nt) {
-            const int col = nt * 8 + g;
-            brow[nt] = a.zero_row;
-            if (col < md.cnt) {
-                const int p = md.off + col;
-                brow[nt] = KIND == KIND_GATEUP ? a.bsrc + (size_t)(a.pairs[p] / a.K) * a.D : a.bsrc + (size_t)p * a.F;
+            for (int nt = 0; nt < EX_NCH; ++nt) {
+                const int col = nt * 8 + g;
+                brow[nt] = a.zero_row;
+                if (col < md.cnt) {
+                    const int p = md.off + col;
+                    brow[nt] = KIND == KIND_GATEUP ? a.bsrc + (size_t)(a.pairs[p] / a.K) * a.D : a.bsrc + (size_t)p * a.F;
+                }
+                brow[nt] += t * 16;
+#pragma unroll
+                for (int c = 0; c < 4; ++c) acc[nt][c] = 0.0f;
             }
-            brow[nt] += t * 16;
         }
-        float acc[EX_NCH][4];
-#pragma unroll
-        for (int nt = 0; nt < EX_NCH; ++nt)
-#pragma unroll
-            for (int c = 0; c < 4; ++c) acc[nt][c] = 0.0f;
-        if (two) expert_item_loop<ENC, C::KS, 2>(rowg, rowg8, brow, NP, kp, t, acc);
-        else expert_item_loop<ENC, C::KS, 1>(rowg, rowg8, brow, NP, kp, t, acc);
+        const uint32_t *rows = reinterpret_cast<const uint32_t *>(smem + (size_t)st * C::STAGE +
+                                                                   (size_t)(mat * C::RB + tile * 16) * C::SLB);
+        const uint32_t *rowg = rows + (g * C::SLB) / 4;
+        const uint32_t *rowg8 = rows + ((g + 8) * C::SLB) / 4;
+        if (two) slice_mma<ENC, 2>(rowg, rowg8, brow, md.s * 4, t, acc);
+        else slice_mma<ENC, 1>(rowg, rowg8, brow, md.s * 4, t, acc);
         __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[st]);     // this warp is done with the stage
-        // cross-warp reduction of the K split, then the epilogue
+        if (lane == 0) mbar_arrive(&empty[st]);           // this warp is done with the stage
+        if (md.s != NS - 1) continue;
+        // ---------------- epilogue of the item
         const int ntl = two ? 2 : 1;
-#pragma unroll
-        for (int nt = 0; nt < EX_NCH; ++nt)
-            if (nt < ntl)
-                *reinterpret_cast<float4 *>(red + ((cw * EX_NCH + nt) * 32 + lane) * 4) =
-                    make_float4(acc[nt][0], acc[nt][1], acc[nt][2], acc[nt][3]);
-        named_bar_sync(1, EX_NW * 32);
-        const int ctid = threadIdx.x - 32;
         if (KIND == KIND_GATEUP) {
-            // element (nt, l, c): gate = combo 0, up = combo 1; K parts at warps combo + 2*kp
-            for (int i = ctid; i < ntl * 128; i += EX_NW * 32) {
-                const int nt = i >> 7, l = (i >> 2) & 31, c = i & 3;
-                float gsum = 0.0f, usum = 0.0f;
+            float *xb = xbuf + (size_t)tile * EX_NCH * 128;
+            if (mat == 0) {
 #pragma unroll
-                for (int k = 0; k < C::KS; ++k) {
-                    gsum += red[(((0 + 2 * k) * EX_NCH + nt) * 32 + l) * 4 + c];
-                    usum += red[(((1 + 2 * k) * EX_NCH + nt) * 32 + l) * 4 + c];
-                }
-                const int col = nt * 8 + 2 * (l & 3) + (c & 1);
-                if (col < md.cnt) {
-                    const int row = md.m * 16 + (l >> 2) + 8 * (c >> 1);          // feature in [0, F)
-                    const float silu = gsum / (1.0f + expf(-gsum));             // kernels.c:416
-                    const float h = silu * usum;                                 // qwen3_moe.c:219
-                    const int pos = (row & ~63) + s_perm.elem_to_pos[row & 63];
-                    a.h_out[(size_t)(md.off + col) * a.F + pos] = __float2half_rn(h);
+                for (int nt = 0; nt < EX_NCH; ++nt)
+                    if (nt < ntl)
+                        *reinterpret_cast<float4 *>(xb + (nt * 32 + lane) * 4) =
+                            make_float4(acc[nt][0], acc[nt][1], acc[nt][2], acc[nt][3]);
+            }
+            named_bar_sync(1, EX_NW * 32);
+            if (mat == 1) {
+#pragma unroll
+                for (int nt = 0; nt < EX_NCH; ++nt) {
+                    if (nt >= ntl) continue;
+                    const float4 gv = *reinterpret_cast<const float4 *>(xb + (nt * 32 + lane) * 4);
+                    const float gs[4] = {gv.x, gv.y, gv.z, gv.w};
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        const int col = nt * 8 + 2 * t + (c & 1);
+                        if (col < md.cnt) {
+                            const int row = md.m * C::RB + tile * 16 + g + 8 * (c >> 1);       // feature in [0, F)
+                            const float silu = gs[c] / (1.0f + expf(-gs[c]));                 // kernels.c:416
+                            const float h = silu * acc[nt][c];                                // qwen3_moe.c:219
+                            const int pos = (row & ~63) + s_perm.elem_to_pos[row & 63];
+                            a.h_out[(size_t)(md.off + col) * a.F + pos] = __float2half_rn(h);
+                        }
+                    }
                 }
             }
+            named_bar_sync(1, EX_NW * 32);                 // the exchange buffer is free again
         } else {
-            for (int i = ctid; i < C::COMBOS * ntl * 128; i += EX_NW * 32) {
-                const int cbx = i / (ntl * 128), r = i - cbx * ntl * 128;
-                const int nt = r >> 7, l = (r >> 2) & 31, c = r & 3;
-                float v = 0.0f;
 #pragma unroll
-                for (int k = 0; k < C::KS; ++k) v += red[(((cbx + C::COMBOS * k) * EX_NCH + nt) * 32 + l) * 4 + c];
-                const int col = nt * 8 + 2 * (l & 3) + (c & 1);
-                if (col < md.cnt) {
-                    const int row = md.m * C::ROWS + cbx * 16 + (l >> 2) + 8 * (c >> 1);   // in [0, D)
-                    a.y_out[(size_t)a.pairs[md.off + col] * a.D + row] = v;
+            for (int nt = 0; nt < EX_NCH; ++nt) {
+                if (nt >= ntl) continue;
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    const int col = nt * 8 + 2 * t + (c & 1);
+                    if (col < md.cnt) {
+                        const int row = md.m * C::RB + tile * 16 + g + 8 * (c >> 1);           // in [0, D)
+                        a.y_out[(size_t)a.pairs[md.off + col] * a.D + row] = acc[nt][c];
+                    }
                 }
             }
         }
-        named_bar_sync(1, EX_NW * 32);
     }
 }
 
@@ -778,7 +780,7 @@ __global__ void k_combine(const float *__restrict__ x, const float *__restrict__
 
 // ------------------------------------------------------------------ host side
 struct KernelPlan {
-    int stages = 0, rs = 0, ctas = 0;
+    int stages = 0, ctas = 0;
     size_t smem = 0;
 };
 
@@ -794,33 +796,32 @@ struct cpg_moe_layer {
     std::vector<const uint8_t *> h_ptrs;   // host copy of the same table
     void *d_wmaps = nullptr;       // device (E, 3) TMA tensor maps of the expert matrices, built
                                    // on the first tcgen05 call (cpg_moe_apply)
+    void *d_dmaps = nullptr;       // device (E, 3) maps for the decode expert kernels (K slices of
+                                   // 256 values, 64-row gate/up and 128-row down boxes), built here
     std::mutex wmaps_mu;
     cpg::KernelPlan gateup, down;
 };
 
 namespace cpg {
 
-static int smem_row_stride(int rb) { return (rb / 16) % 2 == 0 ? rb + 16 : rb; }
-
 template <int ENC, int KIND>
-static int plan_kernel(int K_in, KernelPlan &p) {
+static int plan_kernel(KernelPlan &p) {
     using C = ExCfg<ENC, KIND>;
     auto *k = k_experts<ENC, KIND>;
-    const int rb = (K_in / 32) * C::GB;
-    p.rs = smem_row_stride(rb);
-    const int stage = C::COMBOS * 16 * p.rs;
-    const size_t fixed = sizeof(float) * EX_NW * EX_NCH * 128 + 8 * (sizeof(StageMeta) + 16) + 128;
+    const size_t fixed = sizeof(float) * 4 * EX_NCH * 128 + 8 * (sizeof(StageMeta) + 16) + 256;
     cudaFuncAttributes fa;
     CPG_CUDA(cudaFuncGetAttributes(&fa, k));
     const size_t limit = (size_t)smem_optin() - fa.sharedSizeBytes;
     // two CTAs per SM (latency hiding comes from warps); stages fill about 100 KB per CTA
-    int S = (int)((100 * 1024 - fixed) / stage);
+    int S = (int)((100 * 1024 - fixed) / C::STAGE);
     if (S < 2) S = 2;
     if (S > 8) S = 8;
-    while (S > 1 && fixed + (size_t)S * stage > limit) --S;
-    CPG_REQUIRE(fixed + (size_t)S * stage <= limit, "expert kernel: a %d-byte stage does not fit in shared memory", stage);
+    while (S > 1 && fixed + (size_t)S * C::STAGE > limit) --S;
+    CPG_REQUIRE(fixed + (size_t)S * C::STAGE <= limit, "expert kernel: a %d-byte stage does not fit in shared memory",
+                C::STAGE);
     p.stages = S;
-    p.smem = (size_t)S * stage + sizeof(float) * EX_NW * EX_NCH * 128 + S * sizeof(StageMeta) + 2 * S * sizeof(uint64_t);
+    p.smem = (size_t)S * C::STAGE + sizeof(float) * 4 * EX_NCH * 128 + S * sizeof(StageMeta) + 2 * S * sizeof(uint64_t) +
+             128;                                           // alignment slack
     int rc = allow_max_smem((const void *)k);
     if (rc) return rc;
     int per_sm = 0;
@@ -835,7 +836,7 @@ static int launch_experts(const cpg_moe_layer *L, int KIND, const ExpertArgs &a,
     const int grid = max_items < p.ctas ? (max_items > 0 ? max_items : 1) : p.ctas;
     ExpertArgs b = a;
     b.stages = p.stages;
-    b.rs = p.rs;
+    b.maps = L->d_dmaps;
     const dim3 block((1 + EX_NW) * 32);
     auto *k = L->enc == CPG_ENC_Q4 ? (KIND == KIND_GATEUP ? k_experts<CPG_ENC_Q4, KIND_GATEUP> : k_experts<CPG_ENC_Q4, KIND_DOWN>)
                                    : (KIND == KIND_GATEUP ? k_experts<CPG_ENC_Q8, KIND_GATEUP> : k_experts<CPG_ENC_Q8, KIND_DOWN>);
@@ -858,6 +859,8 @@ int layer_ptrs(const cpg_moe_layer *L, const uint8_t *const **ptrs, int *enc) {
     return CPG_OK;
 }
 int gemm_tc_build_weight_maps(const uint8_t *const *h_ptrs, int E, int D, int F, void **d_maps);
+int build_row_maps(const uint8_t *const *h_ptrs, int E, int D, int F, int wenc, int rows_gu, int rows_dn,
+                   void **d_maps);
 int layer_weight_maps(const cpg_moe_layer *Lc, const void **maps) {
     CPG_REQUIRE(Lc, "null layer");
     cpg_moe_layer *L = const_cast<cpg_moe_layer *>(Lc);
@@ -909,11 +912,15 @@ extern "C" int cpg_moe_layer_create(const cpg_moe_desc *d, cpg_moe_layer **out) 
     }
     int rc;
     if (enc == CPG_ENC_Q4) {
-        rc = plan_kernel<CPG_ENC_Q4, KIND_GATEUP>(L->D, L->gateup);
-        if (rc == CPG_OK) rc = plan_kernel<CPG_ENC_Q4, KIND_DOWN>(L->F, L->down);
+        rc = plan_kernel<CPG_ENC_Q4, KIND_GATEUP>(L->gateup);
+        if (rc == CPG_OK) rc = plan_kernel<CPG_ENC_Q4, KIND_DOWN>(L->down);
     } else {
-        rc = plan_kernel<CPG_ENC_Q8, KIND_GATEUP>(L->D, L->gateup);
-        if (rc == CPG_OK) rc = plan_kernel<CPG_ENC_Q8, KIND_DOWN>(L->F, L->down);
+        rc = plan_kernel<CPG_ENC_Q8, KIND_GATEUP>(L->gateup);
+        if (rc == CPG_OK) rc = plan_kernel<CPG_ENC_Q8, KIND_DOWN>(L->down);
+    }
+    if (rc == CPG_OK) {
+        // decode tensor maps: every expert matrix of the layer, 256-value K slices
+        rc = build_row_maps(L->h_ptrs.data(), E, L->D, L->F, enc, 64, 128, &L->d_dmaps);
     }
     if (rc == CPG_OK) {
         const int rsmem = R_TB * L->D * (int)sizeof(float);
@@ -926,6 +933,7 @@ extern "C" int cpg_moe_layer_create(const cpg_moe_desc *d, cpg_moe_layer **out) 
     }
     if (rc != CPG_OK) {
         cudaFree(L->d_ptrs);
+        if (L->d_dmaps) cudaFree(L->d_dmaps);
         delete L;
         return rc;
     }
@@ -936,6 +944,7 @@ extern "C" int cpg_moe_layer_create(const cpg_moe_desc *d, cpg_moe_layer **out) 
 extern "C" void cpg_moe_layer_destroy(cpg_moe_layer *L) {
     if (!L) return;
     cudaFree(L->d_ptrs);
+    if (L->d_dmaps) cudaFree(L->d_dmaps);
     if (L->d_wmaps) cudaFree(L->d_wmaps);
     delete L;
 }
@@ -1005,14 +1014,14 @@ int cpg::moe_forward_impl(const cpg_moe_layer *L, const float *x, const float *a
     ea.h_out = (__half *)(w + W.h);
     ea.item_ctr = hdr + WS_ITEMS_GATEUP;
     if (ev) CPG_CUDA(cudaEventRecordWithFlags(ev[1], s, cudaEventRecordExternal));
-    int rc = launch_experts(L, KIND_GATEUP, ea, max_chunks * (L->F / 16), s);
+    int rc = launch_experts(L, KIND_GATEUP, ea, max_chunks * (L->F / 64), s);
     if (rc) return rc;
 
     ea.bsrc = (const __half *)(w + W.h);
     ea.y_out = (float *)(w + W.y);
     ea.item_ctr = hdr + WS_ITEMS_DOWN;
     if (ev) CPG_CUDA(cudaEventRecordWithFlags(ev[2], s, cudaEventRecordExternal));
-    rc = launch_experts(L, KIND_DOWN, ea, max_chunks * (L->D / 64), s);
+    rc = launch_experts(L, KIND_DOWN, ea, max_chunks * (L->D / 128), s);
     if (rc) return rc;
 
     const int n4 = T * L->D / 4;
