@@ -416,7 +416,9 @@ struct ExCfg {
     static constexpr int SLB = 8 * GB;                        // bytes of one row's K slice
     static constexpr int MATS = KIND == KIND_GATEUP ? 2 : 1;
     static constexpr int RB = KIND == KIND_GATEUP ? 64 : 128; // rows per matrix per item
-    static constexpr int STAGE = MATS * RB * SLB;
+    static constexpr int WBYTES = MATS * RB * SLB;             // weight boxes of a stage
+    static constexpr int BROW = EX_KSL * 2 + 16;               // token row slice, fp16, padded (odd 16 B)
+    static constexpr int STAGE = WBYTES + EX_NCHUNK * BROW;    // + the chunk's token rows
     static constexpr int WPAIR = GB / 2;                       // 32-bit words per group pair
 };
 
@@ -535,17 +537,29 @@ __device__ __forceinline__ void group_pair_mma(const uint32_t *rowg, const uint3
     }
 }
 
-// Group pairs p0..p0+3 of one K slice (pair index in the slice: 0..3), B loaded one pair ahead.
+// Operand fragments of pair p of the K slice for the NTL token tiles, from the stage's token
+// rows in shared memory (bs[nt] = this thread's row, already offset by t·32 bytes).
+template <int NTL>
+__device__ __forceinline__ void load_b_smem(const uint8_t *const (&bs)[EX_NCH], int p, uint4 (&b)[EX_NCH][2]) {
+#pragma unroll
+    for (int nt = 0; nt < NTL; ++nt) {
+        const uint4 *bp = reinterpret_cast<const uint4 *>(bs[nt] + p * 128);
+        b[nt][0] = bp[0];
+        b[nt][1] = bp[1];
+    }
+}
+
+// The four group pairs of one K slice.
 template <int ENC, int NTL>
-__device__ __forceinline__ void slice_mma(const uint32_t *rowg, const uint32_t *rowg8, const __half *const (&brow)[EX_NCH],
-                                          int P0, int t, float (&acc)[EX_NCH][4]) {
+__device__ __forceinline__ void slice_mma(const uint32_t *rowg, const uint32_t *rowg8, const uint8_t *const (&bs)[EX_NCH],
+                                          int t, float (&acc)[EX_NCH][4]) {
     uint4 b0[EX_NCH][2], b1[EX_NCH][2];
-    load_b<NTL>(brow, P0, b0);
-    load_b<NTL>(brow, P0 + 1, b1);
+    load_b_smem<NTL>(bs, 0, b0);
+    load_b_smem<NTL>(bs, 1, b1);
     group_pair_mma<ENC, NTL>(rowg, rowg8, 0, t, b0, acc);
-    load_b<NTL>(brow, P0 + 2, b0);
+    load_b_smem<NTL>(bs, 2, b0);
     group_pair_mma<ENC, NTL>(rowg, rowg8, 1, t, b1, acc);
-    load_b<NTL>(brow, P0 + 3, b1);
+    load_b_smem<NTL>(bs, 3, b1);
     group_pair_mma<ENC, NTL>(rowg, rowg8, 2, t, b0, acc);
     group_pair_mma<ENC, NTL>(rowg, rowg8, 3, t, b1, acc);
 }
@@ -613,6 +627,12 @@ __global__ void __launch_bounds__((1 + EX_NW) * 32, 2) k_experts(ExpertArgs a) {
             if (item < total) decode_item(s_act, U, tiles, item, u, m, c);
             const int4 ex = s_act[u];
             const int c0 = c * EX_NCHUNK;
+            const int cnt = item < total ? min(EX_NCHUNK, ex.z - c0) : 0;
+            const __half *trow[EX_NCHUNK];                     // the chunk's token rows (fp16, permuted K)
+            for (int j = 0; j < cnt; ++j) {
+                const int p = ex.y + c0 + j;
+                trow[j] = KIND == KIND_GATEUP ? a.bsrc + (size_t)(a.pairs[p] / a.K) * a.D : a.bsrc + (size_t)p * a.F;
+            }
             for (int sl = 0; sl < (item < total ? NS : 1); ++sl, ++it) {
                 const int st = it % S;
                 if (it >= S && !mbar_wait(&empty[st], (uint32_t)(it / S - 1) & 1u)) {
@@ -627,9 +647,12 @@ __global__ void __launch_bounds__((1 + EX_NW) * 32, 2) k_experts(ExpertArgs a) {
                     ++it;
                     break;
                 }
-                meta[st] = StageMeta{item, m, ex.y + c0, min(EX_NCHUNK, ex.z - c0), sl};
-                mbar_arrive_expect_tx(&full[st], (uint32_t)C::STAGE);
+                meta[st] = StageMeta{item, m, ex.y + c0, cnt, sl, 0};
+                mbar_arrive_expect_tx(&full[st], (uint32_t)(C::WBYTES + cnt * EX_KSL * 2));
                 uint8_t *dst = smem + (size_t)st * C::STAGE;
+                for (int j = 0; j < cnt; ++j)                  // columns past cnt keep stale rows: their
+                    bulk_g2s(dst + C::WBYTES + j * C::BROW,    // results are never stored
+                             trow[j] + (size_t)sl * EX_KSL, EX_KSL * 2, &full[st]);
                 const int e = ex.x;
                 if (KIND == KIND_GATEUP) {
                     tma_load_2d_map(dst, maps + (size_t)(3 * e + 0) * MAPB, sl * XSTEP, m * C::RB, &full[st]);
@@ -653,7 +676,6 @@ __global__ void __launch_bounds__((1 + EX_NW) * 32, 2) k_experts(ExpertArgs a) {
     const int mat = KIND == KIND_GATEUP ? (cw & 1) : 0;
     const int tile = KIND == KIND_GATEUP ? (cw >> 1) : cw;
     const int g = lane >> 2, t = lane & 3;
-    const __half *brow[EX_NCH];
     float acc[EX_NCH][4];
     bool two = false;
     for (int it = 0;; ++it) {
@@ -664,27 +686,23 @@ __global__ void __launch_bounds__((1 + EX_NW) * 32, 2) k_experts(ExpertArgs a) {
         }
         const StageMeta md = meta[st];
         if (md.item < 0) break;
-        if (md.s == 0) {                                   // a new item: its token columns
+        if (md.s == 0) {                                   // a new item
             two = md.cnt > 8;
 #pragma unroll
-            for (int nt = 0; nt < EX_NCH; ++nt) {
-                const int col = nt * 8 + g;
-                brow[nt] = a.zero_row;
-                if (col < md.cnt) {
-                    const int p = md.off + col;
-                    brow[nt] = KIND == KIND_GATEUP ? a.bsrc + (size_t)(a.pairs[p] / a.K) * a.D : a.bsrc + (size_t)p * a.F;
-                }
-                brow[nt] += t * 16;
+            for (int nt = 0; nt < EX_NCH; ++nt)
 #pragma unroll
                 for (int c = 0; c < 4; ++c) acc[nt][c] = 0.0f;
-            }
         }
+        const uint8_t *bs[EX_NCH];
+#pragma unroll
+        for (int nt = 0; nt < EX_NCH; ++nt)
+            bs[nt] = smem + (size_t)st * C::STAGE + C::WBYTES + (nt * 8 + g) * C::BROW + t * 32;
         const uint32_t *rows = reinterpret_cast<const uint32_t *>(smem + (size_t)st * C::STAGE +
                                                                    (size_t)(mat * C::RB + tile * 16) * C::SLB);
         const uint32_t *rowg = rows + (g * C::SLB) / 4;
         const uint32_t *rowg8 = rows + ((g + 8) * C::SLB) / 4;
-        if (two) slice_mma<ENC, 2>(rowg, rowg8, brow, md.s * 4, t, acc);
-        else slice_mma<ENC, 1>(rowg, rowg8, brow, md.s * 4, t, acc);
+        if (two) slice_mma<ENC, 2>(rowg, rowg8, bs, t, acc);
+        else slice_mma<ENC, 1>(rowg, rowg8, bs, t, acc);
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[st]);           // this warp is done with the stage
         if (md.s != NS - 1) continue;
