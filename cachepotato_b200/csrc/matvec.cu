@@ -159,18 +159,41 @@ __device__ __forceinline__ void gemv_pair(const uint32_t *__restrict__ wp, const
     }
 }
 
+// Up to three matrices of the same width and encoding read the same vectors (the attention
+// projections Wq, Wk, Wv); their 16-row tiles are numbered one after the other. With `norm`
+// set, x is first RMS-normalised per vector with that gain (kernels.c:408-413: inv = 1/sqrt(Σx²/n
+// + eps), xn = (x·inv)·g), so the layer's first RMSNorm needs no launch of its own.
+struct GemvSeg {
+    const uint8_t *w;
+    float *out;
+    int n_out;
+};
+struct GemvArgs {
+    GemvSeg seg[3];
+    int nseg;
+    const float *x;
+    const float *norm;
+    float eps;
+    int n_in;
+    long rowbytes;
+    int stages;
+};
+
 template <int ENC, int NT>
-__global__ void __launch_bounds__((GV_CONS + 1) * 32)
-k_gemv(float *__restrict__ out, const float *__restrict__ x, const uint8_t *__restrict__ w, int n_in, int n_out,
-       long rowbytes, int stages) {
+__global__ void __launch_bounds__((GV_CONS + 1) * 32) k_gemv(const GemvArgs a) {
     extern __shared__ __align__(16) uint8_t gsm[];
+    const int n_in = a.n_in;
     float *xs = reinterpret_cast<float *>(gsm);                           // (NT, n_in) pair-permuted
     uint8_t *ring = gsm + (size_t)NT * n_in * sizeof(float);
     __shared__ uint64_t full[8], empty[8];
+    __shared__ float s_red[GV_CONS + 1][NT];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int np = n_in / 64;
-    const int ntiles = (n_out + GV_ROWS - 1) / GV_ROWS;
-    const size_t stage_bytes = (size_t)GV_ROWS * rowbytes;
+    int t0[4] = {0, 0, 0, 0};
+    for (int i = 0; i < a.nseg; ++i) t0[i + 1] = t0[i] + (a.seg[i].n_out + GV_ROWS - 1) / GV_ROWS;
+    const int ntiles = t0[a.nseg];
+    const size_t stage_bytes = (size_t)GV_ROWS * a.rowbytes;
+    const int stages = a.stages;
     if (threadIdx.x == 0) {
         for (int i = 0; i < stages; ++i) {
             mbar_init(&full[i], 1);
@@ -178,34 +201,72 @@ k_gemv(float *__restrict__ out, const float *__restrict__ x, const uint8_t *__re
         }
         fence_mbar_init();
     }
-    for (int i = threadIdx.x; i < NT * n_in; i += blockDim.x) {
-        const int t = i / n_in, e = i - t * n_in;
-        xs[t * n_in + (e % 64) * np + e / 64] = x[i];
-    }
     __syncthreads();
+    pdl_launch_dependents();
     if (warp == GV_CONS) {
+        // weights do not depend on the previous kernel: the ring fills while it finishes
         if (lane != 0) return;
         int it = 0;
         for (int tl = blockIdx.x; tl < ntiles; tl += gridDim.x, ++it) {
             const int st = it % stages;
             if (it >= stages && !mbar_wait(&empty[st], (uint32_t)(it / stages - 1) & 1u)) break;
-            const int r0 = tl * GV_ROWS, nr = min(GV_ROWS, n_out - r0);
-            mbar_arrive_expect_tx(&full[st], (uint32_t)(nr * rowbytes));
-            bulk_g2s(ring + st * stage_bytes, w + (size_t)r0 * rowbytes, (uint32_t)(nr * rowbytes), &full[st]);
+            int sg = 0;
+            while (tl >= t0[sg + 1]) ++sg;
+            const int r0 = (tl - t0[sg]) * GV_ROWS, nr = min(GV_ROWS, a.seg[sg].n_out - r0);
+            mbar_arrive_expect_tx(&full[st], (uint32_t)(nr * a.rowbytes));
+            bulk_g2s(ring + st * stage_bytes, a.seg[sg].w + (size_t)r0 * a.rowbytes, (uint32_t)(nr * a.rowbytes), &full[st]);
         }
         for (int q = it > stages ? it - stages : 0; q < it; ++q) mbar_wait(&full[q % stages], (uint32_t)(q / stages) & 1u);
         return;
     }
+    pdl_wait();                                        // x comes from the previous kernel
+    float inv[NT];
+#pragma unroll
+    for (int t = 0; t < NT; ++t) inv[t] = 1.0f;
+    if (a.norm) {
+        float ss[NT];
+#pragma unroll
+        for (int t = 0; t < NT; ++t) ss[t] = 0.0f;
+        for (int i = threadIdx.x; i < n_in; i += GV_CONS * 32) {
+#pragma unroll
+            for (int t = 0; t < NT; ++t) {
+                const float v = a.x[(size_t)t * n_in + i];
+                ss[t] = fmaf(v, v, ss[t]);
+            }
+        }
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) ss[t] += __shfl_xor_sync(0xffffffffu, ss[t], o);
+            if (lane == 0) s_red[warp][t] = ss[t];
+        }
+        named_bar_sync(1, GV_CONS * 32);
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+            float tot = 0.0f;
+            for (int w = 0; w < GV_CONS; ++w) tot += s_red[w][t];
+            inv[t] = __fdiv_rn(1.0f, __fsqrt_rn(__fdiv_rn(tot, (float)n_in) + a.eps));
+        }
+    }
+    for (int i = threadIdx.x; i < NT * n_in; i += GV_CONS * 32) {
+        const int t = i / n_in, e = i - t * n_in;
+        float v = a.x[i];
+        if (a.norm) v = __fmul_rn(__fmul_rn(v, inv[t]), a.norm[e]);
+        xs[t * n_in + (e % 64) * np + e / 64] = v;
+    }
+    named_bar_sync(1, GV_CONS * 32);
     int it = 0;
     for (int tl = blockIdx.x; tl < ntiles; tl += gridDim.x, ++it) {
         const int st = it % stages;
         if (!mbar_wait(&full[st], (uint32_t)(it / stages) & 1u)) break;
-        const int r0 = tl * GV_ROWS, nr = min(GV_ROWS, n_out - r0);
+        int sg = 0;
+        while (tl >= t0[sg + 1]) ++sg;
+        const int r0 = (tl - t0[sg]) * GV_ROWS, n_out = a.seg[sg].n_out, nr = min(GV_ROWS, n_out - r0);
 #pragma unroll
         for (int rr = 0; rr < 2; ++rr) {
             const int r = warp * 2 + rr;
             if (r >= nr) break;
-            const uint32_t *row = reinterpret_cast<const uint32_t *>(ring + st * stage_bytes + (size_t)r * rowbytes);
+            const uint32_t *row = reinterpret_cast<const uint32_t *>(ring + st * stage_bytes + (size_t)r * a.rowbytes);
             float acc[NT];
 #pragma unroll
             for (int t = 0; t < NT; ++t) acc[t] = 0.0f;
@@ -217,7 +278,7 @@ k_gemv(float *__restrict__ out, const float *__restrict__ x, const uint8_t *__re
             }
             if (lane == 0) {
 #pragma unroll
-                for (int t = 0; t < NT; ++t) out[(size_t)t * n_out + r0 + r] = acc[t];
+                for (int t = 0; t < NT; ++t) a.seg[sg].out[(size_t)t * n_out + r0 + r] = acc[t];
             }
         }
         __syncwarp();
@@ -226,21 +287,43 @@ k_gemv(float *__restrict__ out, const float *__restrict__ x, const uint8_t *__re
 }
 
 template <int ENC, int NT>
-static int gemv_launch(float *out, const float *x, const uint8_t *w, int n_in, int n_out, long rb, cudaStream_t s) {
+static int gemv_launch(const GemvArgs &ga, cudaStream_t s) {
     auto *k = k_gemv<ENC, NT>;
-    const size_t xbytes = (size_t)NT * n_in * sizeof(float);
-    const size_t stage = (size_t)GV_ROWS * rb;
-    const int avail = smem_optin() - 2048;
+    const size_t xbytes = (size_t)NT * ga.n_in * sizeof(float);
+    const size_t stage = (size_t)GV_ROWS * ga.rowbytes;
+    const int avail = smem_optin() - 4096;
     int stages = (int)((avail - (long)xbytes) / (long)stage);
     if (stages > 4) stages = 4;
     if (stages < 2) return 1;                                 // too wide: the row kernel takes it
+    GemvArgs a = ga;
+    a.stages = stages;
     const size_t smem = xbytes + stages * stage;
     CPG_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    const int ntiles = (n_out + GV_ROWS - 1) / GV_ROWS;
+    int ntiles = 0;
+    for (int i = 0; i < a.nseg; ++i) ntiles += (a.seg[i].n_out + GV_ROWS - 1) / GV_ROWS;
     const int grid = ntiles < sm_count() ? ntiles : sm_count();
-    k<<<grid, (GV_CONS + 1) * 32, smem, s>>>(out, x, w, n_in, n_out, rb, stages);
-    CPG_CUDA(cudaGetLastError());
+    CPG_CUDA(launch_pdl(k, dim3(grid), dim3((GV_CONS + 1) * 32), smem, s, a));
     return CPG_OK;
+}
+
+// Streaming GEMV over up to three matrices of one width (nseg ≤ 3), optional RMSNorm of x first.
+// Returns 1 when the shape does not suit the streaming kernel (the caller falls back).
+int gemv_multi(const GemvSeg *segs, int nseg, const float *x, int T, const float *norm, float eps, int n_in, int enc,
+               cudaStream_t s) {
+    const long rb = row_bytes(enc, n_in);
+    if (enc == CPG_ENC_F32 || T < 1 || T > GV_MAXT || nseg < 1 || nseg > 3 || n_in % 64 || rb % 16 || ((uintptr_t)x & 15))
+        return 1;
+    GemvArgs a{};
+    for (int i = 0; i < nseg; ++i) {
+        if ((uintptr_t)segs[i].w & 15) return 1;
+        a.seg[i] = segs[i];
+    }
+    a.nseg = nseg; a.x = x; a.norm = norm; a.eps = eps; a.n_in = n_in; a.rowbytes = rb;
+    if (enc == CPG_ENC_Q4)
+        return T == 1 ? gemv_launch<CPG_ENC_Q4, 1>(a, s) : T == 2 ? gemv_launch<CPG_ENC_Q4, 2>(a, s)
+             : T == 3 ? gemv_launch<CPG_ENC_Q4, 3>(a, s) : gemv_launch<CPG_ENC_Q4, 4>(a, s);
+    return T == 1 ? gemv_launch<CPG_ENC_Q8, 1>(a, s) : T == 2 ? gemv_launch<CPG_ENC_Q8, 2>(a, s)
+         : T == 3 ? gemv_launch<CPG_ENC_Q8, 3>(a, s) : gemv_launch<CPG_ENC_Q8, 4>(a, s);
 }
 
 template <int ENC>
@@ -294,23 +377,10 @@ int matvec_launch(float *out, const float *x, cpg_tensor w, int n_in, int n_out,
     if (w.enc == CPG_ENC_F32)
         CPG_REQUIRE(((uintptr_t)w.p & 15) == 0, "cpg_matvec: f32 weights must be 16-byte aligned");
     const long rb = row_bytes(w.enc, n_in);
-    // decode-sized batches of quantised rows: the streaming kernel (rows 16-byte multiples,
-    // 4-byte aligned base, whole group pairs)
-    if (w.enc != CPG_ENC_F32 && T <= GV_MAXT && n_in % 64 == 0 && rb % 16 == 0 && ((uintptr_t)w.p & 15) == 0 &&
-        ((uintptr_t)x & 15) == 0) {
-        const uint8_t *wp = (const uint8_t *)w.p;
-        int r = 1;
-        if (w.enc == CPG_ENC_Q4) {
-            r = T == 1 ? gemv_launch<CPG_ENC_Q4, 1>(out, x, wp, n_in, n_out, rb, s)
-              : T == 2 ? gemv_launch<CPG_ENC_Q4, 2>(out, x, wp, n_in, n_out, rb, s)
-              : T == 3 ? gemv_launch<CPG_ENC_Q4, 3>(out, x, wp, n_in, n_out, rb, s)
-                       : gemv_launch<CPG_ENC_Q4, 4>(out, x, wp, n_in, n_out, rb, s);
-        } else {
-            r = T == 1 ? gemv_launch<CPG_ENC_Q8, 1>(out, x, wp, n_in, n_out, rb, s)
-              : T == 2 ? gemv_launch<CPG_ENC_Q8, 2>(out, x, wp, n_in, n_out, rb, s)
-              : T == 3 ? gemv_launch<CPG_ENC_Q8, 3>(out, x, wp, n_in, n_out, rb, s)
-                       : gemv_launch<CPG_ENC_Q8, 4>(out, x, wp, n_in, n_out, rb, s);
-        }
+    // decode-sized batches of quantised rows: the streaming kernel
+    {
+        const GemvSeg seg{(const uint8_t *)w.p, out, n_out};
+        const int r = gemv_multi(&seg, 1, x, T, nullptr, 0.0f, n_in, w.enc, s);
         if (r != 1) return r;
     }
     // tokens per CTA: as many as fit 96 KB of staged x

@@ -38,6 +38,8 @@ __device__ __forceinline__ float block_sum(float v, float *s_red) {
 // embed_rows (cachepotato.c:108-133): row ids[t] of the Q8_0/Q4_0 table, q·d exact in fp32.
 __global__ void __launch_bounds__(256) k_embed(const uint8_t *__restrict__ tab, int enc, const int *__restrict__ ids,
                                                 int D, float *__restrict__ x) {
+    pdl_wait();
+    pdl_launch_dependents();
     const int t = blockIdx.x;
     const int gb = enc == CPG_ENC_Q4 ? 18 : 34;
     const uint8_t *row = tab + (size_t)ids[t] * (size_t)(D / 32) * gb;
@@ -62,6 +64,8 @@ __global__ void __launch_bounds__(256) k_embed(const uint8_t *__restrict__ tab, 
 // rmsnorm (kernels.c:408-413): inv = 1/sqrt(Σx²/n + eps), out = (x·inv)·g; one block per row.
 __global__ void __launch_bounds__(256) k_rmsnorm(const float *__restrict__ x, const float *__restrict__ g, int D,
                                                   float eps, float *__restrict__ out) {
+    pdl_wait();
+    pdl_launch_dependents();
     __shared__ float s_red[8];
     const float *xr = x + (size_t)blockIdx.x * D;
     float ss = 0.0f;
@@ -82,6 +86,8 @@ __global__ void __launch_bounds__(256) k_qk_norm_rope(float *__restrict__ q, con
                                                        float *__restrict__ vc, int T, const int *__restrict__ d_pos,
                                                        int H, int KV, const float *__restrict__ qn,
                                                        const float *__restrict__ kn, float theta, float eps) {
+    pdl_wait();
+    pdl_launch_dependents();
     const int lane = threadIdx.x & 31;
     const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int nh = H + KV;
@@ -135,6 +141,8 @@ constexpr int AT_WARPS = AT_THREADS / 32;
 __global__ void __launch_bounds__(AT_THREADS) k_attention(const float *__restrict__ q, const float *__restrict__ kc,
                                                            const float *__restrict__ vc, const int *__restrict__ d_pos,
                                                            int H, int KV, float *__restrict__ ao) {
+    pdl_wait();
+    pdl_launch_dependents();
     const int pos0 = *d_pos;
     extern __shared__ float sc[];                        // (n) scores
     __shared__ float s_red[AT_WARPS];
@@ -249,6 +257,8 @@ __device__ __forceinline__ void argmax_block(float best, int bi, float *out_v, i
 }
 
 __global__ void __launch_bounds__(512) k_argmax_part(const float *__restrict__ v, int n, float *part_v, int *part_i) {
+    pdl_wait();
+    pdl_launch_dependents();
     const int chunk = (n + gridDim.x - 1) / gridDim.x;
     const int lo = blockIdx.x * chunk, hi = min(n, lo + chunk);
     float best = -INFINITY;
@@ -262,6 +272,8 @@ __global__ void __launch_bounds__(512) k_argmax_part(const float *__restrict__ v
 
 __global__ void __launch_bounds__(256) k_argmax_final(const float *__restrict__ part_v, const int *__restrict__ part_i,
                                                        int nparts, int *out) {
+    pdl_wait();
+    pdl_launch_dependents();
     __shared__ float s_best;
     float best = -INFINITY;
     int bi = 0x7fffffff;
@@ -277,6 +289,8 @@ __global__ void __launch_bounds__(256) k_argmax_final(const float *__restrict__ 
 // is recorded at out[*d_pos - base] when out is given.
 __global__ void k_advance(const int *__restrict__ next, int *__restrict__ ids, int *__restrict__ d_pos, int T,
                           int *__restrict__ out, int base) {
+    pdl_wait();
+    pdl_launch_dependents();
     const int id = *next;
     const int p = *d_pos + T;
     *d_pos = p;
@@ -285,6 +299,13 @@ __global__ void k_advance(const int *__restrict__ next, int *__restrict__ ids, i
 }
 
 int matvec_launch(float *out, const float *x, cpg_tensor w, int n_in, int n_out, int T, cudaStream_t s);
+struct GemvSeg {
+    const uint8_t *w;
+    float *out;
+    int n_out;
+};
+int gemv_multi(const GemvSeg *segs, int nseg, const float *x, int T, const float *norm, float eps, int n_in, int enc,
+               cudaStream_t s);
 int layer_dims(const cpg_moe_layer *L, int *D, int *F, int *E, int *K);
 
 }  // namespace cpg
@@ -395,37 +416,52 @@ extern "C" void cpg_qwen3_destroy(cpg_qwen3 *m) {
 static int qwen3_enqueue(cpg_qwen3 *m, int T, cudaStream_t s) {
     const int D = m->D, H = m->H, KV = m->KV, QD = H * QW_HD, KD = KV * QW_HD;
     const size_t C = (size_t)m->max_ctx;
-    k_embed<<<T, 256, 0, s>>>((const uint8_t *)m->embed.p, m->embed.enc, m->d_ids, D, m->x);
-    CPG_CUDA(cudaGetLastError());
+    CPG_CUDA(launch_pdl(k_embed, dim3(T), dim3(256), 0, s, (const uint8_t *)m->embed.p, m->embed.enc,
+                        (const int *)m->d_ids, D, m->x));
     for (int l = 0; l < m->L; ++l) {
         const cpg_qwen3_attn &A = m->attn[l];
         float *kc = m->kv + (size_t)l * 2 * C * KD, *vc = kc + C * KD;
-        k_rmsnorm<<<T, 256, 0, s>>>(m->x, A.ln1, D, m->eps, m->xn);
-        CPG_CUDA(cudaGetLastError());
-        int rc = matvec_launch(m->q, m->xn, A.wq, D, QD, T, s);
-        if (!rc) rc = matvec_launch(m->kst, m->xn, A.wk, D, KD, T, s);
-        if (!rc) rc = matvec_launch(m->vst, m->xn, A.wv, D, KD, T, s);
+        // RMSNorm(x, ln1) and q, k, v in one streaming launch (decode-sized T), else separately
+        const int enc = A.wq.enc;
+        int rc = 1;
+        if (A.wk.enc == enc && A.wv.enc == enc) {
+            const GemvSeg seg[3] = {{(const uint8_t *)A.wq.p, m->q, QD}, {(const uint8_t *)A.wk.p, m->kst, KD},
+                                    {(const uint8_t *)A.wv.p, m->vst, KD}};
+            rc = gemv_multi(seg, 3, m->x, T, A.ln1, m->eps, D, enc, s);
+        }
+        if (rc == 1) {
+            k_rmsnorm<<<T, 256, 0, s>>>(m->x, A.ln1, D, m->eps, m->xn);
+            CPG_CUDA(cudaGetLastError());
+            rc = matvec_launch(m->q, m->xn, A.wq, D, QD, T, s);
+            if (!rc) rc = matvec_launch(m->kst, m->xn, A.wk, D, KD, T, s);
+            if (!rc) rc = matvec_launch(m->vst, m->xn, A.wv, D, KD, T, s);
+        }
         if (rc) return rc;
         const int warps = T * (H + KV);
-        k_qk_norm_rope<<<(warps + 7) / 8, 256, 0, s>>>(m->q, m->kst, m->vst, kc, vc, T, m->d_pos, H, KV, A.q_norm,
-                                                       A.k_norm, m->theta, m->eps);
-        CPG_CUDA(cudaGetLastError());
+        CPG_CUDA(launch_pdl(k_qk_norm_rope, dim3((warps + 7) / 8), dim3(256), 0, s, m->q, (const float *)m->kst,
+                            (const float *)m->vst, kc, vc, T, (const int *)m->d_pos, H, KV, A.q_norm, A.k_norm,
+                            m->theta, m->eps));
         const size_t asmem = (size_t)m->max_ctx * sizeof(float);     // scores of every cached position
-        k_attention<<<dim3(H, T), AT_THREADS, asmem, s>>>(m->q, kc, vc, m->d_pos, H, KV, m->ao);
-        CPG_CUDA(cudaGetLastError());
+        CPG_CUDA(launch_pdl(k_attention, dim3(H, T), dim3(AT_THREADS), asmem, s, (const float *)m->q,
+                            (const float *)kc, (const float *)vc, (const int *)m->d_pos, H, KV, m->ao));
         rc = matvec_launch(m->at, m->ao, A.wo, QD, D, T, s);
         if (rc) return rc;
         rc = cpg_moe_forward(m->moe[l], m->x, m->at, T, nullptr, m->x, nullptr, nullptr, nullptr, m->ws, m->ws_bytes, s);
         if (rc) return rc;
     }
-    float *xl = m->x + (size_t)(T - 1) * D;
-    k_rmsnorm<<<1, 256, 0, s>>>(xl, m->final_norm, D, m->eps, m->xn);
-    CPG_CUDA(cudaGetLastError());
-    int rc = matvec_launch(m->logits, m->xn, m->lm_head, D, m->V, 1, s);
+    // head: RMSNorm of the last position with final_norm fused into the lm_head GEMV
+    const float *xl = m->x + (size_t)(T - 1) * D;
+    const GemvSeg hseg{(const uint8_t *)m->lm_head.p, m->logits, m->V};
+    int rc = m->lm_head.enc == CPG_ENC_F32 ? 1 : gemv_multi(&hseg, 1, xl, 1, m->final_norm, m->eps, D, m->lm_head.enc, s);
+    if (rc == 1) {
+        k_rmsnorm<<<1, 256, 0, s>>>(xl, m->final_norm, D, m->eps, m->xn);
+        CPG_CUDA(cudaGetLastError());
+        rc = matvec_launch(m->logits, m->xn, m->lm_head, D, m->V, 1, s);
+    }
     if (rc) return rc;
-    k_argmax_part<<<AM_BLOCKS, 512, 0, s>>>(m->logits, m->V, m->am_v, m->am_i);
-    k_argmax_final<<<1, 256, 0, s>>>(m->am_v, m->am_i, AM_BLOCKS, m->d_next);
-    CPG_CUDA(cudaGetLastError());
+    CPG_CUDA(launch_pdl(k_argmax_part, dim3(AM_BLOCKS), dim3(512), 0, s, (const float *)m->logits, m->V, m->am_v, m->am_i));
+    CPG_CUDA(launch_pdl(k_argmax_final, dim3(1), dim3(256), 0, s, (const float *)m->am_v, (const int *)m->am_i,
+                        AM_BLOCKS, m->d_next));
     return CPG_OK;
 }
 
