@@ -11,11 +11,13 @@
 //   warp 1      one thread issues tcgen05.mma (M=128, N≤256, K=16, fp16 × fp16 → fp32 in TMEM),
 //               twice per K step (one per 128-row half), and commits each stage to the mbarrier
 //               that frees it
-//   warp 2      one thread loads the token tile of each stage with a 2D tensor TMA (64-byte
-//               swizzle, a 128- or 256-row box) from the expert-sorted fp16 activation rows
-//   warps 3-10  decode each raw row from shared memory into fp16 (q·d rounded once) in the
-//               K-major no-swizzle canonical layout, one Q4_0 group pair per two stages, then run
-//               the epilogue from TMEM:
+//   warps 2, 3  one thread each loads the token tile of every other stage with a 2D tensor TMA
+//               (64-byte swizzle, a 128- or 256-row box) from the expert-sorted fp16 activation
+//               rows (one issuing warp's copies are served one after another, ~500 cycles each)
+//   warps 4-19  decode the raw rows from shared memory into fp16 (q·d rounded once) in the
+//               K-major no-swizzle canonical layout, two threads per row (one takes quant bytes
+//               0-7 of each group = K chunks 0 and 2, the other bytes 8-15 = chunks 1 and 3, so
+//               both write the same stage), then run the epilogue from TMEM:
 //                 gate/up: h = silu(g)·u (engine/blocks/qwen3_moe.c:217-219), fp16 per pair
 //                 down:    y per (token, slot) in fp32, combined in selection order by k_combine
 // Every mbarrier wait is bounded; a timeout records a status code, all roles leave together, and
@@ -44,8 +46,9 @@ constexpr int TC_B_BYTES = TC_BN * TC_BK * 2;                       // 16 KB
 constexpr int TC_STAGE_BYTES = TC_A_BYTES + TC_B_BYTES;
 constexpr int TC_STAGE0 = TC_RAW_SLOTS * TC_RAW_BYTES;              // operand stages follow the raw ring
 constexpr int TC_SMEM = TC_STAGE0 + TC_STAGES * TC_STAGE_BYTES;     // 200 KB (+1 KB alignment slack)
-constexpr int TC_MATH_WARPS = 8;
-constexpr int TC_FIRST_MATH = 3;
+constexpr int TC_MATH_WARPS = 16;               // two threads per weight row
+constexpr int TC_B_WARPS = 2;                   // token-tile producers: warps 2, 3
+constexpr int TC_FIRST_MATH = 2 + TC_B_WARPS;
 constexpr int TC_THREADS = (TC_FIRST_MATH + TC_MATH_WARPS) * 32;
 constexpr int TC_SBO = (TC_BK / 8) * 128;   // no-swizzle A: bytes between 8-row core-matrix groups
 constexpr int TC_LBO = 128;                 // no-swizzle A: bytes between 8-column core matrices
@@ -165,6 +168,32 @@ __device__ __forceinline__ void q4_pair_to_f16(const uint32_t *w, uint4 (&out)[8
         out[grp * 4 + 2] = make_uint4(v[8], v[9], v[10], v[11]);
         out[grp * 4 + 3] = make_uint4(v[12], v[13], v[14], v[15]);
     }
+}
+
+// Eight quant bytes of one Q4_0 group (u0 = bytes 0..3, u1 = bytes 4..7 of the caller's half) and
+// its fp16 scale (duplicated in both halves of sc) -> the low-nibble values (8 consecutive K) and
+// the high-nibble values (the 8 values 16 further on), each as one 16-byte chunk of q·d in fp16.
+__device__ __forceinline__ void q4_half_group(uint32_t u0, uint32_t u1, uint32_t sc, uint4 &lo_chunk, uint4 &hi_chunk) {
+    const uint32_t k1032 = 0x64086408u, k1_16 = 0x2C002C00u, km72 = 0xD480D480u;
+    const uint32_t q[2] = {u0, u1};
+    uint32_t lo[4], hi[4];
+#pragma unroll
+    for (int wi = 0; wi < 2; ++wi) {
+        const uint32_t x = __byte_perm(q[wi], 0, 0x3120);              // [b0, b2, b1, b3]
+        const uint32_t x2 = x >> 8;
+        lo[2 * wi] = hsub2_u32(lop3_and_xor(x, 0x000F000Fu, 0x64086408u), k1032);
+        lo[2 * wi + 1] = hsub2_u32(lop3_and_xor(x2, 0x000F000Fu, 0x64086408u), k1032);
+        hi[2 * wi] = hfma2_u32(lop3_and_xor(x, 0x00F000F0u, 0x64806480u), k1_16, km72);
+        hi[2 * wi + 1] = hfma2_u32(lop3_and_xor(x2, 0x00F000F0u, 0x64806480u), k1_16, km72);
+    }
+    uint32_t v[8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(v[i]) : "r"(lo[i]), "r"(sc));
+        asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(v[4 + i]) : "r"(hi[i]), "r"(sc));
+    }
+    lo_chunk = make_uint4(v[0], v[1], v[2], v[3]);
+    hi_chunk = make_uint4(v[4], v[5], v[6], v[7]);
 }
 
 // canonical K-major no-swizzle offset of the 16-byte chunk (row r, chunk c) in a 128-row half
@@ -321,9 +350,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const TcArgs a, const
             umma_commit(&drain_bar);
             mbar_wait(&drain_bar, 0);
         }
-    } else if (warp == 2) {
-        // ---------------- token-tile producer (one thread): 2D tensor TMA per stage
+    } else if (warp < TC_FIRST_MATH) {
+        // ---------------- token-tile producers (one thread per warp): 2D tensor TMA per stage,
+        // stages dealt round-robin over TC_B_WARPS warps (a warp's copies are served one at a
+        // time, ~500 cycles each on B200 whatever their size, so one warp cannot feed a stage
+        // per MMA stage time)
         if (lane == 0) {
+            const int bw = warp - 2;
             int it = 0;
             bool ok = true;
             for (int tile = blockIdx.x; ok && tile < total; tile += gridDim.x) {
@@ -334,6 +367,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const TcArgs a, const
                 const CUtensorMap *bmap = small ? &tmap_b_small : &tmap_b;
                 const uint32_t bbytes = small ? TC_B_BYTES / 2 : TC_B_BYTES;
                 for (int ks = 0; ks < KST; ++ks, ++it) {
+                    if (it % TC_B_WARPS != bw) continue;
                     const int st = it % TC_STAGES;
                     if (it >= TC_STAGES &&
                         !tc_wait(&empty_bar[st], (uint32_t)(it / TC_STAGES - 1) & 1u, abort_flag, a.status, ST_TIMEOUT_EMPTY)) {
@@ -345,14 +379,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const TcArgs a, const
                 }
             }
             for (int q = it > TC_STAGES ? it - TC_STAGES : 0; q < it; ++q)
-                mbar_wait(&b_full[q % TC_STAGES], (uint32_t)(q / TC_STAGES) & 1u);
+                if (q % TC_B_WARPS == bw) mbar_wait(&b_full[q % TC_STAGES], (uint32_t)(q / TC_STAGES) & 1u);
         }
     } else {
         // ---------------- math warps: decode weights into the A operand, epilogue
-        const int mt = threadIdx.x - TC_FIRST_MATH * 32;   // weight row of the tile, 0..255
+        // a warp decodes 16 rows: lanes 0-15 the byte half 0 of each, lanes 16-31 half 1, so each
+        // 8-lane phase of a 16-byte store covers 8 consecutive rows (conflict-free)
+        const int wrow = ((warp - TC_FIRST_MATH) << 4) | (lane & 15);   // weight row of the tile
+        const int hb = lane >> 4;                          // quant bytes 0-7 or 8-15 of each group
         const int quad = warp & 3;                         // TMEM lane quadrant this warp may access
-        const int colhalf = (warp - TC_FIRST_MATH) >> 2;   // epilogue columns [128*colhalf, +128)
-        const int hr = mt >> 7, rr = mt & 127;             // half, row within half
+        const int colq = (warp - TC_FIRST_MATH) >> 2;      // epilogue columns [64*colq, +64)
+        const int hr = wrow >> 7, rr = wrow & 127;         // half, row within half
         int it = 0, git = 0, ti = 0;
         for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++ti) {
             int u, m, n;
@@ -367,12 +404,18 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const TcArgs a, const
                     ok = false;
                     break;
                 }
-                uint32_t w[36];
-                const uint4 *src = reinterpret_cast<const uint4 *>(smem + slot * TC_RAW_BYTES + mt * TC_RAW_ROW);
+                // per group pair: scales (words 0, 4), and this half's quant words
+                uint32_t w[TC_GRP / 2][6];
+                const uint32_t *src = reinterpret_cast<const uint32_t *>(smem + slot * TC_RAW_BYTES + wrow * TC_RAW_ROW);
 #pragma unroll
-                for (int i = 0; i < 9; ++i) {
-                    const uint4 v = src[i];
-                    w[4 * i] = v.x; w[4 * i + 1] = v.y; w[4 * i + 2] = v.z; w[4 * i + 3] = v.w;
+                for (int j = 0; j < TC_GRP / 2; ++j) {
+                    const uint32_t *pw = src + 9 * j;
+                    w[j][0] = pw[0];
+                    w[j][1] = pw[2];
+                    w[j][2] = pw[4];
+                    w[j][3] = pw[1 + 2 * hb];
+                    w[j][4] = pw[5 + 2 * hb];
+                    w[j][5] = pw[6 + 2 * hb];
                 }
 #pragma unroll
                 for (int j = 0; j < TC_GRP / 2; ++j) {     // group pair j -> stages it+2j, it+2j+1
@@ -384,15 +427,21 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const TcArgs a, const
                         ok = false;
                         break;
                     }
-                    uint4 v[8];
-                    q4_pair_to_f16(&w[9 * j], v);
+                    const uint32_t w0 = w[j][0], w2 = w[j][1], w4 = w[j][2];
+                    const uint32_t d0 = w0 & 0xFFFFu, d1 = w4 >> 16;
+                    // group 0: bytes 0..7 (half 0) are w0[2..3], w1, w2[0..1]; bytes 8..15 (half 1)
+                    // are w2[2..3], w3, w4[0..1]; group 1: words 5,6 (half 0) or 7,8 (half 1)
+                    const uint32_t u0 = hb ? __byte_perm(w2, w[j][3], 0x5432) : __byte_perm(w0, w[j][3], 0x5432);
+                    const uint32_t u1 = hb ? __byte_perm(w[j][3], w4, 0x5432) : __byte_perm(w[j][3], w2, 0x5432);
+                    uint4 l0, h0, l1, h1;
+                    q4_half_group(u0, u1, d0 | (d0 << 16), l0, h0);
+                    q4_half_group(w[j][4], w[j][5], d1 | (d1 << 16), l1, h1);
                     uint8_t *sa0 = smem + TC_STAGE0 + st0 * TC_STAGE_BYTES + hr * (TC_BM / 8) * TC_SBO;
                     uint8_t *sa1 = smem + TC_STAGE0 + st1 * TC_STAGE_BYTES + hr * (TC_BM / 8) * TC_SBO;
-#pragma unroll
-                    for (int c = 0; c < 4; ++c) {
-                        *reinterpret_cast<uint4 *>(sa0 + canon_off(rr, c)) = v[c];
-                        *reinterpret_cast<uint4 *>(sa1 + canon_off(rr, c)) = v[4 + c];
-                    }
+                    *reinterpret_cast<uint4 *>(sa0 + canon_off(rr, hb)) = l0;
+                    *reinterpret_cast<uint4 *>(sa0 + canon_off(rr, 2 + hb)) = h0;
+                    *reinterpret_cast<uint4 *>(sa1 + canon_off(rr, hb)) = l1;
+                    *reinterpret_cast<uint4 *>(sa1 + canon_off(rr, 2 + hb)) = h1;
                     fence_async_smem();                    // generic-proxy writes -> tensor core
                     mbar_arrive(&a_full[st0]);
                     mbar_arrive(&a_full[st1]);
@@ -410,7 +459,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const TcArgs a, const
             if (!__all_sync(0xffffffffu, got)) break;
             tc_fence_after();
             const int row = quad * 32 + lane;              // accumulator row (TMEM lane)
-            for (int c0 = colhalf * (TC_BN / 2); c0 < colhalf * (TC_BN / 2) + TC_BN / 2 && c0 < cnt; c0 += 32) {
+            for (int c0 = colq * (TC_BN / 4); c0 < colq * (TC_BN / 4) + TC_BN / 4 && c0 < cnt; c0 += 32) {
                 float g[32], w2[32];
                 tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + c0, g);
                 tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + TC_BN + c0, w2);

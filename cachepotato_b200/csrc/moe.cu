@@ -4,17 +4,18 @@
 //   k_router   RMSNorm(x + attn), f32 router GEMV, softmax over experts, strict-'>' top-k,
 //              renormalisation (qwen3_moe.c:178-197); the last CTA of each token tile routes
 //              its tokens and the last tile groups the (token, slot) pairs by expert.
-//   k_experts<GATEUP>  per (expert, 16-row tile): gate and up GEMMs over that expert's tokens,
+//   k_experts<GATEUP>  per (expert, 64-row tile, chunk of up to 16 tokens): gate and up GEMMs,
 //              h = silu(g)·u (qwen3_moe.c:217-219)
-//   k_experts<DOWN>    per (expert, 32-row tile): y = Wd·h (qwen3_moe.c:220)
+//   k_experts<DOWN>    per (expert, 128-row tile, token chunk): y = Wd·h (qwen3_moe.c:220)
 //   k_combine  mlp += sum_j wt_j·y_j in selection order (qwen3_moe.c:221) and the residual
 //              x + (attn + mlp) of run_layers (engine/api/cachepotato.c:157-159)
 //
-// Expert kernels: a producer warp streams weight rows from HBM into shared memory with 1D
-// TMA bulk copies (no multicast) through an mbarrier ring; four consumer warps decode Q4_0 /
-// Q8_0 groups in registers (exact integers in fp16) and feed mma.m16n8k16 with fp32
-// accumulators; the group scale is applied in fp32 after each group's MMAs. Tokens are the
-// N dimension (8 per MMA tile), weights are read exactly once per layer.
+// Expert kernels: two producer warps fill an mbarrier ring of stages. One deals the work items
+// and streams the weight rows from HBM as 2D tensor TMA boxes (one 256-value K slice of the
+// item's rows, no multicast); the other copies the same K slice of the item's token rows. Eight
+// consumer warps decode Q4_0 / Q8_0 groups in registers (exact integers in fp16) and feed
+// mma.m16n8k16 with fp32 accumulators; the group scale is applied in fp32 after each group's
+// MMAs. Tokens are the N dimension (8 per MMA tile), weights are read exactly once per layer.
 #include <math.h>
 
 #include <mutex>
@@ -34,6 +35,8 @@ constexpr int MAX_K = 32;
 constexpr int KIND_GATEUP = 0;
 constexpr int KIND_DOWN = 1;
 constexpr int EX_NW = 8;         // consumer warps per CTA
+constexpr int EX_NP = 2;         // producer warps: weight boxes, token rows (one issuing warp's
+                                 // copies are served one after another on B200)
 constexpr int EX_NCH = 2;        // 8-column MMA tiles per item
 constexpr int EX_NCHUNK = 8 * EX_NCH;   // tokens per item (an expert with more is split)
 
@@ -572,7 +575,7 @@ __device__ __forceinline__ void tma_load_2d_map(void *dst, const void *map, int 
 }
 
 template <int ENC, int KIND>
-__global__ void __launch_bounds__((1 + EX_NW) * 32, 2) k_experts(ExpertArgs a) {
+__global__ void __launch_bounds__((EX_NP + EX_NW) * 32, 2) k_experts(ExpertArgs a) {
     using C = ExCfg<ENC, KIND>;
     // Dynamic shared memory starts after the static arrays, 16-byte aligned only; the stages
     // (2D tensor TMA destinations) need 128 bytes, so the base moves up (the launch adds the
@@ -589,14 +592,16 @@ __global__ void __launch_bounds__((1 + EX_NW) * 32, 2) k_experts(ExpertArgs a) {
     float *xbuf = reinterpret_cast<float *>(smem + (size_t)S * C::STAGE);      // (4 tiles, NCH, 32, 4) gate sums
     uint64_t *full = reinterpret_cast<uint64_t *>(xbuf + 4 * EX_NCH * 128);
     uint64_t *empty = full + S;
-    StageMeta *meta = reinterpret_cast<StageMeta *>(empty + S);
+    uint64_t *mready = empty + S;                              // stage metadata written
+    StageMeta *meta = reinterpret_cast<StageMeta *>(mready + S);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int tiles = n_rows / C::RB;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
-            mbar_init(&full[s], 1);
+            mbar_init(&full[s], EX_NP);
             mbar_init(&empty[s], EX_NW);
+            mbar_init(&mready[s], 1);
         }
         fence_mbar_init();
         s_abort = 0;
@@ -613,8 +618,39 @@ __global__ void __launch_bounds__((1 + EX_NW) * 32, 2) k_experts(ExpertArgs a) {
     __syncthreads();
     const int total = tiles * s_act[U].w;
 
+    if (warp == 1) {
+        // ---------------- token-row producer: one thread, the chunk's rows of each K slice
+        if (lane != 0) return;
+        const __half *trow[EX_NCHUNK];
+        int cur = -1;
+        for (int it = 0;; ++it) {
+            const int st = it % S;
+            if (!mbar_wait(&mready[st], (uint32_t)(it / S) & 1u)) {
+                atomicCAS(a.status + WS_STATUS, ST_OK, ST_TIMEOUT_FULL);
+                return;
+            }
+            const StageMeta md = meta[st];
+            if (md.item < 0) {                                 // sentinel
+                mbar_arrive(&full[st]);
+                return;
+            }
+            if (md.item != cur) {                              // the chunk's token rows (fp16, permuted K)
+                cur = md.item;
+                for (int j = 0; j < md.cnt; ++j) {
+                    const int p = md.off + j;
+                    trow[j] = KIND == KIND_GATEUP ? a.bsrc + (size_t)(a.pairs[p] / a.K) * a.D : a.bsrc + (size_t)p * a.F;
+                }
+            }
+            mbar_arrive_expect_tx(&full[st], (uint32_t)(md.cnt * EX_KSL * 2));
+            uint8_t *dst = smem + (size_t)st * C::STAGE + C::WBYTES;
+            for (int j = 0; j < md.cnt; ++j)                   // columns past cnt keep stale rows: their
+                bulk_g2s(dst + j * C::BROW,                    // results are never stored
+                         trow[j] + (size_t)md.s * EX_KSL, EX_KSL * 2, &full[st]);
+        }
+    }
     if (warp == 0) {
-        // ---------------- producer: one thread, one 2D tensor box per matrix and K slice
+        // ---------------- weight producer: one thread, one 2D tensor box per matrix and K slice;
+        // it deals the items and publishes each stage's metadata to the token-row producer
         if (lane != 0) return;
         const uint8_t *maps = reinterpret_cast<const uint8_t *>(a.maps);
         constexpr int MAPB = 128;                              // sizeof(CUtensorMap)
@@ -628,11 +664,6 @@ __global__ void __launch_bounds__((1 + EX_NW) * 32, 2) k_experts(ExpertArgs a) {
             const int4 ex = s_act[u];
             const int c0 = c * EX_NCHUNK;
             const int cnt = item < total ? min(EX_NCHUNK, ex.z - c0) : 0;
-            const __half *trow[EX_NCHUNK];                     // the chunk's token rows (fp16, permuted K)
-            for (int j = 0; j < cnt; ++j) {
-                const int p = ex.y + c0 + j;
-                trow[j] = KIND == KIND_GATEUP ? a.bsrc + (size_t)(a.pairs[p] / a.K) * a.D : a.bsrc + (size_t)p * a.F;
-            }
             for (int sl = 0; sl < (item < total ? NS : 1); ++sl, ++it) {
                 const int st = it % S;
                 if (it >= S && !mbar_wait(&empty[st], (uint32_t)(it / S - 1) & 1u)) {
@@ -642,17 +673,16 @@ __global__ void __launch_bounds__((1 + EX_NW) * 32, 2) k_experts(ExpertArgs a) {
                 }
                 if (item >= total) {                           // sentinel: no more items
                     meta[st].item = -1;
+                    mbar_arrive(&mready[st]);
                     mbar_arrive(&full[st]);
                     done = true;
                     ++it;
                     break;
                 }
                 meta[st] = StageMeta{item, m, ex.y + c0, cnt, sl, 0};
-                mbar_arrive_expect_tx(&full[st], (uint32_t)(C::WBYTES + cnt * EX_KSL * 2));
+                mbar_arrive(&mready[st]);                      // release: the metadata is visible
+                mbar_arrive_expect_tx(&full[st], (uint32_t)C::WBYTES);
                 uint8_t *dst = smem + (size_t)st * C::STAGE;
-                for (int j = 0; j < cnt; ++j)                  // columns past cnt keep stale rows: their
-                    bulk_g2s(dst + C::WBYTES + j * C::BROW,    // results are never stored
-                             trow[j] + (size_t)sl * EX_KSL, EX_KSL * 2, &full[st]);
                 const int e = ex.x;
                 if (KIND == KIND_GATEUP) {
                     tma_load_2d_map(dst, maps + (size_t)(3 * e + 0) * MAPB, sl * XSTEP, m * C::RB, &full[st]);
@@ -672,7 +702,7 @@ __global__ void __launch_bounds__((1 + EX_NW) * 32, 2) k_experts(ExpertArgs a) {
     }
 
     // ---------------- consumers: warp cw owns 16 rows of one matrix over the whole K
-    const int cw = warp - 1;
+    const int cw = warp - EX_NP;
     const int mat = KIND == KIND_GATEUP ? (cw & 1) : 0;
     const int tile = KIND == KIND_GATEUP ? (cw >> 1) : cw;
     const int g = lane >> 2, t = lane & 3;
@@ -826,7 +856,7 @@ template <int ENC, int KIND>
 static int plan_kernel(KernelPlan &p) {
     using C = ExCfg<ENC, KIND>;
     auto *k = k_experts<ENC, KIND>;
-    const size_t fixed = sizeof(float) * 4 * EX_NCH * 128 + 8 * (sizeof(StageMeta) + 16) + 256;
+    const size_t fixed = sizeof(float) * 4 * EX_NCH * 128 + 8 * (sizeof(StageMeta) + 24) + 256;
     cudaFuncAttributes fa;
     CPG_CUDA(cudaFuncGetAttributes(&fa, k));
     const size_t limit = (size_t)smem_optin() - fa.sharedSizeBytes;
@@ -838,12 +868,12 @@ static int plan_kernel(KernelPlan &p) {
     CPG_REQUIRE(fixed + (size_t)S * C::STAGE <= limit, "expert kernel: a %d-byte stage does not fit in shared memory",
                 C::STAGE);
     p.stages = S;
-    p.smem = (size_t)S * C::STAGE + sizeof(float) * 4 * EX_NCH * 128 + S * sizeof(StageMeta) + 2 * S * sizeof(uint64_t) +
+    p.smem = (size_t)S * C::STAGE + sizeof(float) * 4 * EX_NCH * 128 + S * sizeof(StageMeta) + 3 * S * sizeof(uint64_t) +
              128;                                           // alignment slack
     int rc = allow_max_smem((const void *)k);
     if (rc) return rc;
     int per_sm = 0;
-    CPG_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, (1 + EX_NW) * 32, p.smem));
+    CPG_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, (EX_NP + EX_NW) * 32, p.smem));
     CPG_REQUIRE(per_sm >= 1, "expert kernel: no CTA fits on an SM");
     p.ctas = per_sm * sm_count();
     return CPG_OK;
@@ -855,7 +885,7 @@ static int launch_experts(const cpg_moe_layer *L, int KIND, const ExpertArgs &a,
     ExpertArgs b = a;
     b.stages = p.stages;
     b.maps = L->d_dmaps;
-    const dim3 block((1 + EX_NW) * 32);
+    const dim3 block((EX_NP + EX_NW) * 32);
     auto *k = L->enc == CPG_ENC_Q4 ? (KIND == KIND_GATEUP ? k_experts<CPG_ENC_Q4, KIND_GATEUP> : k_experts<CPG_ENC_Q4, KIND_DOWN>)
                                    : (KIND == KIND_GATEUP ? k_experts<CPG_ENC_Q8, KIND_GATEUP> : k_experts<CPG_ENC_Q8, KIND_DOWN>);
     CPG_CUDA(launch_pdl(k, dim3(grid), block, p.smem, s, b));
