@@ -2,10 +2,13 @@
 //
 // Four launches per layer, all enqueued on one stream and free of host syncs:
 //   k_router   RMSNorm(x + attn), f32 router GEMV, softmax over experts, strict-'>' top-k,
-//              renormalisation (qwen3_moe.c:178-197); the last CTA of each token tile routes
-//              its tokens and the last tile groups the (token, slot) pairs by expert.
+//              renormalisation (qwen3_moe.c:178-197). The CTAs of one token tile form a thread-
+//              block cluster (each holds a slice of the experts); after a cluster barrier, CTA r
+//              routes token r of the tile.
 //   k_experts<GATEUP>  per (expert, 64-row tile, chunk of up to 16 tokens): gate and up GEMMs,
-//              h = silu(g)·u (qwen3_moe.c:217-219)
+//              h = silu(g)·u (qwen3_moe.c:217-219). Each CTA first groups the (token, slot)
+//              pairs by expert in its own shared memory (CTA 0 publishes the table for the
+//              later kernels); batches over EX_GROUP_MAX pairs are grouped by k_group instead.
 //   k_experts<DOWN>    per (expert, 128-row tile, token chunk): y = Wd·h (qwen3_moe.c:220)
 //   k_combine  mlp += sum_j wt_j·y_j in selection order (qwen3_moe.c:221) and the residual
 //              x + (attn + mlp) of run_layers (engine/api/cachepotato.c:157-159)
@@ -39,12 +42,14 @@ constexpr int EX_NP = 2;         // producer warps: weight boxes, token rows (on
                                  // copies are served one after another on B200)
 constexpr int EX_NCH = 2;        // 8-column MMA tiles per item
 constexpr int EX_NCHUNK = 8 * EX_NCH;   // tokens per item (an expert with more is split)
+constexpr int EX_GROUP_MAX = 1024;       // pairs the gate/up kernel groups itself (T ≤ 128)
+constexpr int R_CLUSTER_MAX = 16;        // router CTAs per token tile (one cluster)
 
 // workspace words
-enum { WS_STATUS = 0, WS_DONE_TILES = 1, WS_ITEMS_GATEUP = 2, WS_ITEMS_DOWN = 3, WS_HDR_INTS = 16 };
+enum { WS_STATUS = 0, WS_ITEMS_GATEUP = 2, WS_ITEMS_DOWN = 3, WS_HDR_INTS = 16 };
 
 struct WsLayout {
-    size_t zero_row, n_active, act, act_ptr, pairs, topk, wt, logits, xn, h, y, total;
+    size_t zero_row, n_active, act, pairs, topk, wt, logits, xn, h, y, total;
 };
 
 static size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
@@ -58,7 +63,6 @@ static WsLayout ws_layout(int D, int F, int E, int K, int T) {
     L.n_active = o; o += sizeof(int);
     o = align_up(o, 256);
     L.act = o; o = align_up(o + sizeof(int4) * (size_t)(E + 1), 256);
-    L.act_ptr = o; o = align_up(o + sizeof(void *) * 3 * (size_t)E, 256);
     L.pairs = o; o = align_up(o + sizeof(int) * (size_t)T * K, 256);
     L.topk = o; o = align_up(o + sizeof(int) * (size_t)T * K, 256);
     L.wt = o; o = align_up(o + sizeof(float) * (size_t)T * K, 256);
@@ -87,10 +91,8 @@ struct RouterArgs {
     __half *xn_perm;
     int *status;                 // workspace header (status word, counters)
     __half *zero_row;
-    const uint8_t *const *ptrs;  // (E, 3) expert matrix pointers
     int *n_active, *pairs;
     int4 *act;                   // active experts ascending: (e, pair offset, tokens, token chunks before)
-    const uint8_t **act_ptr;     // (U, 3) their gate/up/down pointers
 };
 
 __device__ __forceinline__ float warp_sum(float v) {
@@ -208,14 +210,9 @@ __device__ void group_pairs(const RouterArgs &a) {
         }
     }
     __syncthreads();
-    for (int e = tid; e < a.E; e += blockDim.x) {     // one thread per expert: loads in parallel
+    for (int e = tid; e < a.E; e += blockDim.x) {
         const int u = s_uidx[e];
-        if (u >= 0) {
-            a.act[u] = make_int4(e, s_off[e], s_cnt[e], s_chp[e]);
-            a.act_ptr[3 * u + 0] = a.ptrs[3 * e + 0];
-            a.act_ptr[3 * u + 1] = a.ptrs[3 * e + 1];
-            a.act_ptr[3 * u + 2] = a.ptrs[3 * e + 2];
-        }
+        if (u >= 0) a.act[u] = make_int4(e, s_off[e], s_cnt[e], s_chp[e]);
     }
     (void)s_tot;
     for (int c0 = 0; c0 < a.T; c0 += 32) {
@@ -244,7 +241,66 @@ __device__ void group_pairs(const RouterArgs &a) {
     }
 }
 
-__global__ void __launch_bounds__(R_THREADS) k_router(RouterArgs a) {
+// The grouping of group_pairs inside one CTA, into shared memory: s_act[0..U) = (expert, first
+// pair, pairs, token chunks before), s_act[U] = (-1, T·K, 0, all chunks); s_pairs = the pair
+// indices t·K + j, experts ascending, tokens ascending within an expert (the same order).
+// scratch: (4·E + E·ceil(T/32) + T·K + 1) ints of shared memory. Every thread calls it; it
+// returns U after a barrier.
+__device__ int group_cta(const int *topk, int T, int K, int E, int4 *s_act, int *s_pairs, int *scratch) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int TK = T * K, W = (T + 31) >> 5;
+    int *s_cnt = scratch, *s_off = s_cnt + E, *s_chp = s_off + E, *s_uidx = s_chp + E;
+    uint32_t *s_mask = reinterpret_cast<uint32_t *>(s_uidx + E);     // (E, W): tokens of expert e
+    int *s_tk = reinterpret_cast<int *>(s_mask + E * W);
+    int *s_u = s_tk + TK;
+    for (int e = tid; e < E; e += blockDim.x) s_cnt[e] = 0;
+    for (int i = tid; i < E * W; i += blockDim.x) s_mask[i] = 0u;
+    for (int i = tid; i < TK; i += blockDim.x) s_tk[i] = __ldcg(topk + i);
+    __syncthreads();
+    for (int i = tid; i < TK; i += blockDim.x) {      // a token's experts are distinct
+        const int e = s_tk[i], t = i / K;
+        atomicAdd(&s_cnt[e], 1);
+        atomicOr(&s_mask[e * W + (t >> 5)], 1u << (t & 31));
+    }
+    __syncthreads();
+    if (warp == 0) {                                  // exclusive scans over experts, 32 at a time
+        int o = 0, u = 0, chp = 0;
+        for (int e0 = 0; e0 < E; e0 += 32) {
+            const int e = e0 + lane;
+            const int c = e < E ? s_cnt[e] : 0;
+            const int ch = (c + EX_NCHUNK - 1) / EX_NCHUNK, act = c > 0;
+            const int ic = warp_incl_scan(c), ich = warp_incl_scan(ch), ia = warp_incl_scan(act);
+            if (e < E) {
+                s_off[e] = o + ic - c;
+                s_chp[e] = chp + ich - ch;
+                s_uidx[e] = act ? u + ia - 1 : -1;
+            }
+            o += __shfl_sync(0xffffffffu, ic, 31);
+            chp += __shfl_sync(0xffffffffu, ich, 31);
+            u += __shfl_sync(0xffffffffu, ia, 31);
+        }
+        if (lane == 0) {
+            s_act[u] = make_int4(-1, o, 0, chp);
+            *s_u = u;
+        }
+    }
+    __syncthreads();
+    for (int e = tid; e < E; e += blockDim.x) {
+        const int u = s_uidx[e];
+        if (u >= 0) s_act[u] = make_int4(e, s_off[e], s_cnt[e], s_chp[e]);
+    }
+    for (int i = tid; i < TK; i += blockDim.x) {      // rank = tokens before t that chose e
+        const int e = s_tk[i], t = i / K;
+        const uint32_t *m = s_mask + e * W;
+        int r = __popc(m[t >> 5] & ((1u << (t & 31)) - 1u));
+        for (int w = 0; w < (t >> 5); ++w) r += __popc(m[w]);
+        s_pairs[s_off[e] + r] = i;
+    }
+    __syncthreads();
+    return *s_u;
+}
+
+__global__ void __launch_bounds__(R_THREADS, 2) k_router(RouterArgs a) {
     extern __shared__ float xs[];                         // (R_TB, D): hh, then xn
     __shared__ int s_last;
     __shared__ uint8_t s_p2e[64];
@@ -370,24 +426,21 @@ __global__ void __launch_bounds__(R_THREADS) k_router(RouterArgs a) {
             if (lane == 0 && t < nt) a.logits[(size_t)(t0 + t) * a.E + e] = v;
         }
     }
+    // every logit of the tile is written once the cluster (all CTAs of this token tile) has
+    // passed the barrier; CTA r then routes tokens r, r + cluster size, ... of the tile
+    __threadfence();
+    cluster_sync();
+    const int rank = cluster_ctarank(), csz = cluster_nctarank();
+    for (int r = rank, i = 0; r < nt; r += csz, ++i)
+        if (warp == i) route_token(a, t0 + r);
 }
 
-// Softmax, top-k and renormalisation for a tile of tokens (one warp per token); the last CTA
-// to finish groups all (token, slot) pairs by expert.
+// Batches of more than EX_GROUP_MAX pairs: one CTA groups the (token, slot) pairs by expert
+// into the workspace (smaller batches are grouped by the gate/up kernel itself).
 constexpr int RT_THREADS = 512;
-__global__ void __launch_bounds__(RT_THREADS) k_route(RouterArgs a) {
-    __shared__ int s_last;
-    pdl_wait();                                           // logits from k_router
+__global__ void __launch_bounds__(RT_THREADS) k_group(RouterArgs a) {
+    pdl_wait();                                           // top-k from k_router
     pdl_launch_dependents();
-    const int warp = threadIdx.x >> 5;
-    const int t = blockIdx.x * (RT_THREADS / 32) + warp;
-    if (t < a.T) route_token(a, t);
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) s_last = atomicAdd(a.status + WS_DONE_TILES, 1) == (int)gridDim.x - 1;
-    __syncthreads();
-    if (!s_last) return;
-    __threadfence();
     group_pairs(a);
 }
 
@@ -395,8 +448,13 @@ __global__ void __launch_bounds__(RT_THREADS) k_route(RouterArgs a) {
 struct ExpertArgs {
     int D, F, K;
     const int *n_active, *pairs;
-    const int4 *act;             // active-expert table from the router (see RouterArgs)
-    const uint8_t *const *act_ptr;
+    const int4 *act;             // active-expert table (see RouterArgs)
+    // GATEUP with topk set: group topk (T, K) over E experts in each CTA, CTA 0 writing the
+    // table to the three pointers below for the later kernels; otherwise read it from above
+    const int *topk;
+    int T, E;
+    int *g_n_active, *g_pairs;
+    int4 *g_act;
     const __half *bsrc;          // GATEUP: xn_perm (T, D); DOWN: h_perm (pairs, F)
     __half *h_out;               // GATEUP output (pairs, F), permuted for Wd
     float *y_out;                // DOWN output (T*K, D), row = t*K + j
@@ -585,6 +643,7 @@ __global__ void __launch_bounds__((EX_NP + EX_NW) * 32, 2) k_experts(ExpertArgs 
     __shared__ Perm64 s_perm;
     __shared__ int s_abort;
     __shared__ int4 s_act[MAX_E + 1];
+    __shared__ int s_pairs[KIND == KIND_GATEUP ? EX_GROUP_MAX : 1];
     const int S = a.stages;
     const int K_in = KIND == KIND_GATEUP ? a.D : a.F;
     const int n_rows = KIND == KIND_GATEUP ? a.F : a.D;
@@ -611,12 +670,25 @@ __global__ void __launch_bounds__((EX_NP + EX_NW) * 32, 2) k_experts(ExpertArgs 
         s_perm.pos_to_elem[threadIdx.x] = pm.pos_to_elem[threadIdx.x];
         s_perm.elem_to_pos[threadIdx.x] = pm.elem_to_pos[threadIdx.x];
     }
-    pdl_wait();                                  // routing table from k_route / h from gate-up
+    pdl_wait();                                  // top-k from k_router / table and h from gate-up
     pdl_launch_dependents();
-    const int U = *a.n_active;
-    for (int u = threadIdx.x; u <= U; u += blockDim.x) s_act[u] = a.act[u];
-    __syncthreads();
+    const bool self_group = KIND == KIND_GATEUP && a.topk != nullptr;
+    int U;
+    if (self_group) {
+        // the stage ring is not in use yet: it holds the grouping scratch
+        U = group_cta(a.topk, a.T, a.K, a.E, s_act, s_pairs, reinterpret_cast<int *>(smem));
+        if (blockIdx.x == 0) {                   // the table for the down and combine kernels
+            for (int u = threadIdx.x; u <= U; u += blockDim.x) a.g_act[u] = s_act[u];
+            for (int i = threadIdx.x; i < a.T * a.K; i += blockDim.x) a.g_pairs[i] = s_pairs[i];
+            if (threadIdx.x == 0) *a.g_n_active = U;
+        }
+    } else {
+        U = *a.n_active;
+        for (int u = threadIdx.x; u <= U; u += blockDim.x) s_act[u] = a.act[u];
+        __syncthreads();
+    }
     const int total = tiles * s_act[U].w;
+    const int *pairs = self_group ? s_pairs : a.pairs;
 
     if (warp == 1) {
         // ---------------- token-row producer: one thread, the chunk's rows of each K slice
@@ -638,7 +710,7 @@ __global__ void __launch_bounds__((EX_NP + EX_NW) * 32, 2) k_experts(ExpertArgs 
                 cur = md.item;
                 for (int j = 0; j < md.cnt; ++j) {
                     const int p = md.off + j;
-                    trow[j] = KIND == KIND_GATEUP ? a.bsrc + (size_t)(a.pairs[p] / a.K) * a.D : a.bsrc + (size_t)p * a.F;
+                    trow[j] = KIND == KIND_GATEUP ? a.bsrc + (size_t)(pairs[p] / a.K) * a.D : a.bsrc + (size_t)p * a.F;
                 }
             }
             mbar_arrive_expect_tx(&full[st], (uint32_t)(md.cnt * EX_KSL * 2));
@@ -924,6 +996,11 @@ int layer_weight_maps(const cpg_moe_layer *Lc, const void **maps) {
 
 using namespace cpg;
 
+namespace cpg {
+int router_cluster(int E, int *eb);
+int router_cluster_check(int E, int rsmem);
+}  // namespace cpg
+
 extern "C" int cpg_moe_layer_create(const cpg_moe_desc *d, cpg_moe_layer **out) {
     CPG_REQUIRE(d && out, "cpg_moe_layer_create: null argument");
     *out = nullptr;
@@ -977,6 +1054,7 @@ extern "C" int cpg_moe_layer_create(const cpg_moe_desc *d, cpg_moe_layer **out) 
             rc = CPG_EINVAL;
         } else {
             rc = allow_max_smem((const void *)k_router);
+            if (rc == CPG_OK) rc = router_cluster_check(E, rsmem);
         }
     }
     if (rc != CPG_OK) {
@@ -988,6 +1066,37 @@ extern "C" int cpg_moe_layer_create(const cpg_moe_desc *d, cpg_moe_layer **out) 
     *out = L;
     return CPG_OK;
 }
+
+namespace cpg {
+// CTAs per router cluster for E experts (experts per CTA: at least one per warp).
+int router_cluster(int E, int *eb) {
+    const int min_eb = (E + R_CLUSTER_MAX - 1) / R_CLUSTER_MAX;
+    *eb = min_eb > R_THREADS / 32 ? min_eb : R_THREADS / 32;
+    return (E + *eb - 1) / *eb;
+}
+
+// The router's clusters must fit on this device (checked once per layer).
+int router_cluster_check(int E, int rsmem) {
+    int eb = 0;
+    const int csz = router_cluster(E, &eb);
+    CPG_CUDA(cudaFuncSetAttribute(k_router, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(csz, 1);
+    cfg.blockDim = dim3(R_THREADS);
+    cfg.dynamicSmemBytes = (size_t)rsmem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)csz;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    CPG_CUDA(cudaOccupancyMaxActiveClusters(&n, k_router, &cfg));
+    CPG_REQUIRE(n >= 1, "router kernel: a cluster of %d CTAs does not fit on this device", csz);
+    return CPG_OK;
+}
+}  // namespace cpg
 
 extern "C" void cpg_moe_layer_destroy(cpg_moe_layer *L) {
     if (!L) return;
@@ -1039,20 +1148,23 @@ int cpg::moe_forward_impl(const cpg_moe_layer *L, const float *x, const float *a
     ra.xn_perm = (__half *)(w + W.xn);
     ra.status = hdr;
     ra.zero_row = (__half *)(w + W.zero_row);
-    ra.ptrs = L->d_ptrs;
     ra.n_active = (int *)(w + W.n_active);
     ra.act = (int4 *)(w + W.act);
-    ra.act_ptr = (const uint8_t **)(w + W.act_ptr);
     ra.pairs = (int *)(w + W.pairs);
-    // few tokens: spread the 1 MiB router over more CTAs; many: normalise each token fewer times
-    ra.eb = T <= R_TB ? 4 : 8;                 // one expert row per warp: 128 CTAs at T = 64
-    const dim3 rgrid((L->E + ra.eb - 1) / ra.eb, (T + R_TB - 1) / R_TB);
-    CPG_CUDA(launch_pdl(k_router, rgrid, dim3(R_THREADS), (size_t)R_TB * L->D * sizeof(float), s, ra));
-    CPG_CUDA(launch_pdl(k_route, dim3((T + RT_THREADS / 32 - 1) / (RT_THREADS / 32)), dim3(RT_THREADS), 0, s, ra));
+    // one cluster of at most R_CLUSTER_MAX CTAs per token tile, one expert row per warp when
+    // E ≤ 8 · R_CLUSTER_MAX (16 CTAs, 128 per 64 tokens for Qwen3-30B-A3B)
+    const int csz = router_cluster(L->E, &ra.eb);
+    const dim3 rgrid(csz, (T + R_TB - 1) / R_TB);
+    CPG_CUDA(launch_pdl_cluster(k_router, rgrid, dim3(R_THREADS), (size_t)R_TB * L->D * sizeof(float), s, csz, ra));
+    // the gate/up kernel groups small batches itself; its scratch (group_cta) must fit in two
+    // stages of the smallest stage ring (Q4 gate/up: 2 × 26,880 bytes)
+    const size_t group_scratch = sizeof(int) * (4 * (size_t)L->E + (size_t)L->E * ((T + 31) / 32) + (size_t)T * L->K + 1);
+    const bool self_group = T * L->K <= EX_GROUP_MAX && group_scratch <= 40960;
+    if (!self_group) CPG_CUDA(launch_pdl(k_group, dim3(1), dim3(RT_THREADS), 0, s, ra));
 
     ExpertArgs ea{};
     ea.D = L->D; ea.F = L->F; ea.K = L->K;
-    ea.n_active = ra.n_active; ea.act = ra.act; ea.act_ptr = ra.act_ptr;
+    ea.n_active = ra.n_active; ea.act = ra.act;
     ea.zero_row = ra.zero_row;
     ea.pairs = ra.pairs; ea.h_enc = L->enc; ea.status = hdr;
     const int max_active = T * L->K < L->E ? T * L->K : L->E;
@@ -1061,6 +1173,10 @@ int cpg::moe_forward_impl(const cpg_moe_layer *L, const float *x, const float *a
     ea.bsrc = ra.xn_perm;
     ea.h_out = (__half *)(w + W.h);
     ea.item_ctr = hdr + WS_ITEMS_GATEUP;
+    if (self_group) {
+        ea.topk = ra.topk; ea.T = T; ea.E = L->E;
+        ea.g_n_active = ra.n_active; ea.g_act = ra.act; ea.g_pairs = ra.pairs;
+    }
     if (ev) CPG_CUDA(cudaEventRecordWithFlags(ev[1], s, cudaEventRecordExternal));
     int rc = launch_experts(L, KIND_GATEUP, ea, max_chunks * (L->F / 64), s);
     if (rc) return rc;
@@ -1068,6 +1184,7 @@ int cpg::moe_forward_impl(const cpg_moe_layer *L, const float *x, const float *a
     ea.bsrc = (const __half *)(w + W.h);
     ea.y_out = (float *)(w + W.y);
     ea.item_ctr = hdr + WS_ITEMS_DOWN;
+    ea.topk = nullptr;
     if (ev) CPG_CUDA(cudaEventRecordWithFlags(ev[2], s, cudaEventRecordExternal));
     rc = launch_experts(L, KIND_DOWN, ea, max_chunks * (L->D / 128), s);
     if (rc) return rc;

@@ -60,8 +60,10 @@ def test_block_vs_reference_engine(orc, golden, layers, case):
 
 
 @pytest.mark.parametrize("enc", [O.ENC_Q4, O.ENC_Q8])
-@pytest.mark.parametrize("T", [1, 3, 8, 17, 64])
+@pytest.mark.parametrize("T", [1, 3, 8, 17, 64, 200, 300])
 def test_block_vs_oracle_small(orc, layers, enc, T):
+    # T·K ≤ 1024 pairs are grouped by the gate/up kernel itself (T = 200: 7 mask words per
+    # expert), larger batches (T = 300) by the separate grouping kernel
     D, F, E, K = 256, 256, 16, 4
     L, dl = layers(D, F, E, K, enc, 100 + enc)
     x = orc.normal(T * D, 1000 + T, 1.0).reshape(T, D)
