@@ -26,6 +26,7 @@
 #include <math.h>
 
 #include <mutex>
+#include <vector>
 
 #include "gemm_tc.cuh"
 
@@ -173,7 +174,10 @@ __device__ __forceinline__ void q4_pair_to_f16(const uint32_t *w, uint4 (&out)[8
 // Eight quant bytes of one Q4_0 group (u0 = bytes 0..3, u1 = bytes 4..7 of the caller's half) and
 // its fp16 scale (duplicated in both halves of sc) -> the low-nibble values (8 consecutive K) and
 // the high-nibble values (the 8 values 16 further on), each as one 16-byte chunk of q·d in fp16.
-__device__ __forceinline__ void q4_half_group(uint32_t u0, uint32_t u1, uint32_t sc, uint4 &lo_chunk, uint4 &hi_chunk) {
+// low: the residual q·d − fp16(q·d) instead (one fused multiply-add, exact in fp16 while it is
+// not below the subnormal range), the second half of a weight split into two fp16 terms.
+__device__ __forceinline__ void q4_half_group(uint32_t u0, uint32_t u1, uint32_t sc, uint4 &lo_chunk, uint4 &hi_chunk,
+                                              bool low = false) {
     const uint32_t k1032 = 0x64086408u, k1_16 = 0x2C002C00u, km72 = 0xD480D480u;
     const uint32_t q[2] = {u0, u1};
     uint32_t lo[4], hi[4];
@@ -191,6 +195,13 @@ __device__ __forceinline__ void q4_half_group(uint32_t u0, uint32_t u1, uint32_t
     for (int i = 0; i < 4; ++i) {
         asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(v[i]) : "r"(lo[i]), "r"(sc));
         asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(v[4 + i]) : "r"(hi[i]), "r"(sc));
+    }
+    if (low) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(v[i]) : "r"(lo[i]), "r"(sc), "r"(v[i] ^ 0x80008000u));
+            asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(v[4 + i]) : "r"(hi[i]), "r"(sc), "r"(v[4 + i] ^ 0x80008000u));
+        }
     }
     lo_chunk = make_uint4(v[0], v[1], v[2], v[3]);
     hi_chunk = make_uint4(v[4], v[5], v[6], v[7]);
@@ -220,7 +231,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const TcArgs a, const
     const int K_in = KIND == 0 ? a.D : a.F;
     const int n_rows = KIND == 0 ? a.F : a.D;
     const int MT = KIND == 0 ? n_rows / TC_BM : n_rows / TC_ROWS;   // row tiles per expert
-    const int KST = K_in / TC_BK;                                   // K stages per tile
+    // KIND 2 (dense projections) runs K three times: W_hi·x_hi, W_hi·x_lo, W_lo·x_hi, where
+    // x = x_hi + x_lo (the token rows hold [x_hi | x_lo]) and W_hi + W_lo = q·d exactly
+    const int KST1 = K_in / TC_BK;                                  // K stages of one pass
+    const int NG1 = KST1 / TC_GRP;
+    const int KST = KIND == 2 ? 3 * KST1 : KST1;                    // K stages per tile
     const int NG = KST / TC_GRP;                                    // raw groups per tile
     constexpr int NMATH = TC_MATH_WARPS * 32;
 
@@ -302,8 +317,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const TcArgs a, const
                     }
                     uint8_t *dst = smem + slot * TC_RAW_BYTES;
                     mbar_arrive_expect_tx(&raw_full[slot], TC_RAW_BYTES);
-                    tma_load_2d(dst, m0, g * TC_RAW_ROW, y0, &raw_full[slot]);
-                    tma_load_2d(dst + TC_BM * TC_RAW_ROW, m1, g * TC_RAW_ROW, y1, &raw_full[slot]);
+                    const int gx = (KIND == 2 ? g % NG1 : g) * TC_RAW_ROW;   // each pass re-reads W
+                    tma_load_2d(dst, m0, gx, y0, &raw_full[slot]);
+                    tma_load_2d(dst + TC_BM * TC_RAW_ROW, m1, gx, y1, &raw_full[slot]);
                 }
             }
             // the last groups' copies must land before the CTA may exit (bounded)
@@ -375,7 +391,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const TcArgs a, const
                         break;
                     }
                     mbar_arrive_expect_tx(&b_full[st], bbytes);
-                    tma_load_2d(smem + TC_STAGE0 + st * TC_STAGE_BYTES + TC_A_BYTES, bmap, ks * TC_BK, row0, &b_full[st]);
+                    // KIND 2: x_hi in passes 0 and 2, x_lo (columns K_in..2K_in) in pass 1
+                    const int bx = KIND == 2 ? (ks % KST1) * TC_BK + (ks / KST1 == 1 ? K_in : 0) : ks * TC_BK;
+                    tma_load_2d(smem + TC_STAGE0 + st * TC_STAGE_BYTES + TC_A_BYTES, bmap, bx, row0, &b_full[st]);
                 }
             }
             for (int q = it > TC_STAGES ? it - TC_STAGES : 0; q < it; ++q)
@@ -434,8 +452,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const TcArgs a, const
                     const uint32_t u0 = hb ? __byte_perm(w2, w[j][3], 0x5432) : __byte_perm(w0, w[j][3], 0x5432);
                     const uint32_t u1 = hb ? __byte_perm(w[j][3], w4, 0x5432) : __byte_perm(w[j][3], w2, 0x5432);
                     uint4 l0, h0, l1, h1;
-                    q4_half_group(u0, u1, d0 | (d0 << 16), l0, h0);
-                    q4_half_group(w[j][4], w[j][5], d1 | (d1 << 16), l1, h1);
+                    const bool low = KIND == 2 && g >= 2 * NG1;   // W_lo in the third pass
+                    q4_half_group(u0, u1, d0 | (d0 << 16), l0, h0, low);
+                    q4_half_group(w[j][4], w[j][5], d1 | (d1 << 16), l1, h1, low);
                     uint8_t *sa0 = smem + TC_STAGE0 + st0 * TC_STAGE_BYTES + hr * (TC_BM / 8) * TC_SBO;
                     uint8_t *sa1 = smem + TC_STAGE0 + st1 * TC_STAGE_BYTES + hr * (TC_BM / 8) * TC_SBO;
                     *reinterpret_cast<uint4 *>(sa0 + canon_off(rr, hb)) = l0;
@@ -566,8 +585,59 @@ int gemm_tc_build_weight_maps(const uint8_t *const *h_ptrs, int E, int D, int F,
     return build_row_maps(h_ptrs, E, D, F, CPG_ENC_Q4, TC_BM, TC_BM, d_maps);
 }
 
+int gemm_tc_dense_maps(const uint8_t *const *w, const int *rows, const int *k, int n, void **d_maps) {
+    EncodeTiledFn enc = encode_tiled();
+    if (!enc) {
+        set_error("cuTensorMapEncodeTiled is unavailable from the driver");
+        return CPG_ECUDA;
+    }
+    std::vector<CUtensorMap> h((size_t)3 * n);
+    for (int i = 0; i < n; ++i) {
+        CPG_REQUIRE(rows[i] % TC_ROWS == 0 && k[i] % (TC_BK * TC_GRP) == 0,
+                    "dense GEMM: a %d x %d matrix is not a multiple of %d x %d", rows[i], k[i], TC_ROWS, TC_BK * TC_GRP);
+        const cuuint64_t rb = (cuuint64_t)(k[i] / 32) * 18;              // Q4_0 row bytes
+        const cuuint64_t dims[2] = {rb, (cuuint64_t)rows[i]};
+        const cuuint64_t strides[1] = {rb};
+        const cuuint32_t box[2] = {(cuuint32_t)TC_RAW_ROW, (cuuint32_t)TC_BM};
+        const cuuint32_t estr[2] = {1, 1};
+        const CUresult r = enc(&h[(size_t)3 * i + 2], CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t *>(w[i]), dims,
+                               strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) {
+            set_error("dense GEMM: tensor map of matrix %d failed (%d)", i, (int)r);
+            return CPG_ECUDA;
+        }
+        h[(size_t)3 * i] = h[(size_t)3 * i + 1] = h[(size_t)3 * i + 2];   // only entry 3i+2 is read
+    }
+    void *d = nullptr;
+    cudaError_t ce = cudaMalloc(&d, sizeof(CUtensorMap) * h.size());
+    if (ce == cudaSuccess) ce = cudaMemcpy(d, h.data(), sizeof(CUtensorMap) * h.size(), cudaMemcpyHostToDevice);
+    if (ce != cudaSuccess) {
+        cudaFree(d);
+        return cuda_fail(ce, "dense GEMM: tensor map upload");
+    }
+    *d_maps = d;
+    return CPG_OK;
+}
+
+int gemm_tc_dense(const void *maps, const int4 *tab, const int *n_active, const int *iota, const __half *x16, int T,
+                  int rows, int k, float *y, int *status, cudaStream_t s) {
+    TcArgs a{};
+    a.n_active = n_active;
+    a.act = tab;
+    a.wmaps = maps;
+    a.pairs = iota;
+    a.D = rows;
+    a.F = k;
+    a.K = 1;
+    a.y_out = y;
+    a.status = status;
+    return gemm_tc_launch(2, a, x16, T, (rows / TC_ROWS) * ((T + TC_BN - 1) / TC_BN), s);
+}
+
 int gemm_tc_launch(int kind, const TcArgs &a, const __half *b, int b_rows, int max_tiles, cudaStream_t s) {
     const int kdim = kind == 0 ? a.D : a.F;
+    const int bdim = kind == 2 ? 2 * kdim : kdim;                   // [x_hi | x_lo] for kind 2
     CPG_REQUIRE(kdim % (TC_BK * TC_GRP) == 0, "grouped GEMM: K=%d must be a multiple of %d", kdim, TC_BK * TC_GRP);
     CPG_REQUIRE(((uintptr_t)b & 15) == 0, "grouped GEMM: token rows must be 16-byte aligned");
     EncodeTiledFn enc = encode_tiled();
@@ -576,8 +646,8 @@ int gemm_tc_launch(int kind, const TcArgs &a, const __half *b, int b_rows, int m
         return CPG_ECUDA;
     }
     CUtensorMap map[2];
-    const cuuint64_t dims[2] = {(cuuint64_t)kdim, (cuuint64_t)b_rows};
-    const cuuint64_t strides[1] = {(cuuint64_t)kdim * 2};
+    const cuuint64_t dims[2] = {(cuuint64_t)bdim, (cuuint64_t)b_rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)bdim * 2};
     const cuuint32_t estr[2] = {1, 1};
     for (int i = 0; i < 2; ++i) {
         const cuuint32_t box[2] = {TC_BK, (cuuint32_t)(i == 0 ? TC_BN : TC_BN_SMALL)};
@@ -589,7 +659,7 @@ int gemm_tc_launch(int kind, const TcArgs &a, const __half *b, int b_rows, int m
             return CPG_ECUDA;
         }
     }
-    auto *k = kind == 0 ? k_gemm_tc<0> : k_gemm_tc<1>;
+    auto *k = kind == 0 ? k_gemm_tc<0> : kind == 1 ? k_gemm_tc<1> : k_gemm_tc<2>;
     const size_t smem = (size_t)TC_SMEM + 1024;
     CPG_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     int grid = sm_count();

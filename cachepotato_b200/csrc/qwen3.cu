@@ -6,6 +6,10 @@
 // Per layer, for T new tokens at positions pos0..pos0+T-1:
 //   k_rmsnorm       xn = RMSNorm(x, ln1)                                   kernels.c:408-413
 //   cpg_matvec ×3   q = Wq·xn, k = Wk·xn, v = Wv·xn (k, v straight into the f32 KV cache)
+//                   (T ≤ 4: one streaming GEMV launch with the RMSNorm fused; a prompt of
+//                   QW_DENSE_MIN_T tokens or more with Q4_0 projections: the tcgen05 GEMM of
+//                   gemm_tc.cu, operands split into two fp16 terms each, three passes, which
+//                   keeps the result within f32 rounding of the GEMV's)
 //   k_qk_norm_rope  per-head RMSNorm of q and k (head_rmsnorm, qwen3_moe.c:44-49), then RoPE at
 //                   each token's position (rope_apply_from, kernels.c:425-447)
 //   k_attention     causal GQA: s = q·k / sqrt(hd), softmax, Σ s·v (qwen3_moe.c:135-155)
@@ -18,10 +22,12 @@
 #include <vector>
 
 #include "common.cuh"
+#include "gemm_tc.cuh"
 
 namespace cpg {
 
 constexpr int QW_HD = 128;
+constexpr int QW_DENSE_MIN_T = 32;     // prompt length from which projections run on tcgen05
 
 __device__ __forceinline__ float block_sum(float v, float *s_red) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
@@ -74,6 +80,51 @@ __global__ void __launch_bounds__(256) k_rmsnorm(const float *__restrict__ x, co
     const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fdiv_rn(ss, (float)D) + eps));
     float *o = out + (size_t)blockIdx.x * D;
     for (int k = threadIdx.x; k < D; k += blockDim.x) o[k] = __fmul_rn(__fmul_rn(xr[k], inv), g[k]);
+}
+
+// hi = fp16(v), lo = fp16(v − hi): v to about 22 bits in two fp16 terms.
+__device__ __forceinline__ void split_f16(float v, __half &hi, __half &lo) {
+    hi = __float2half_rn(v);
+    lo = __float2half_rn(v - __half2float(hi));
+}
+
+// k_rmsnorm as the operand of the tensor-core projections: row t of out (2·D halves) holds
+// [hi(xn_t) | lo(xn_t)].
+__global__ void __launch_bounds__(256) k_rmsnorm_f16(const float *__restrict__ x, const float *__restrict__ g, int D,
+                                                      float eps, __half *__restrict__ out) {
+    __shared__ float s_red[8];
+    const float *xr = x + (size_t)blockIdx.x * D;
+    float ss = 0.0f;
+    for (int k = threadIdx.x; k < D; k += blockDim.x) ss = fmaf(xr[k], xr[k], ss);
+    ss = block_sum(ss, s_red);
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fdiv_rn(ss, (float)D) + eps));
+    __half *o = out + (size_t)blockIdx.x * 2 * D;
+    for (int k = threadIdx.x; k < D; k += blockDim.x)
+        split_f16(__fmul_rn(__fmul_rn(xr[k], inv), g[k]), o[k], o[D + k]);
+}
+
+// (T, n) f32 rows -> (T, 2n) [hi | lo] fp16 rows.
+__global__ void k_split_f16(const float *__restrict__ x, int T, int n, __half *__restrict__ out) {
+    const size_t total = (size_t)T * n;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        const size_t t = i / n, c = i - t * n;
+        split_f16(x[i], out[t * 2 * n + c], out[t * 2 * n + n + c]);
+    }
+}
+
+// The single-group tables of the dense projections: group p (0..3 = q, k, v, o) holds all T
+// tokens in order.
+__global__ void k_dense_tab(int4 *tab, int *n_active, int T) {
+    const int p = threadIdx.x;
+    if (p < 4) {
+        tab[2 * p] = make_int4(p, 0, T, 0);
+        tab[2 * p + 1] = make_int4(-1, T, 0, 0);
+    }
+    if (p == 0) *n_active = 1;
+}
+
+__global__ void k_iota(int *v, int n) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) v[i] = i;
 }
 
 // One warp per (token, head) of q (heads 0..H-1) and k (heads H..H+KV-1): head RMSNorm, then
@@ -323,6 +374,12 @@ struct cpg_qwen3 {
     int *am_i = nullptr;
     int *d_ids = nullptr, *d_next = nullptr, *h_next = nullptr, *d_pos = nullptr, *d_out = nullptr;
     cudaGraphExec_t step_graph = nullptr;          // one decode step, T = 1, any position
+    // prompts on the tensor cores (Q4_0 projections): per layer 12 tensor maps (entry 3p+2 over
+    // Wq, Wk, Wv, Wo), the four single-group tables, t -> t, the fp16 operand rows, a status word
+    void *dmaps = nullptr;
+    int4 *dtab = nullptr;
+    int *dn_active = nullptr, *iota = nullptr, *d_status = nullptr;
+    __half *x16 = nullptr;
     void *ws = nullptr;
     size_t ws_bytes = 0;
     int pos = 0;
@@ -336,6 +393,8 @@ static void qwen3_free(cpg_qwen3 *m) {
     cudaFree(m->logits); cudaFree(m->d_ids); cudaFree(m->d_next); cudaFree(m->ws);
     cudaFree(m->kst); cudaFree(m->vst); cudaFree(m->d_pos); cudaFree(m->d_out);
     cudaFree(m->am_v); cudaFree(m->am_i);
+    cudaFree(m->dmaps); cudaFree(m->dtab); cudaFree(m->dn_active); cudaFree(m->iota); cudaFree(m->d_status);
+    cudaFree(m->x16);
     if (m->step_graph) cudaGraphExecDestroy(m->step_graph);
     if (m->h_next) cudaFreeHost(m->h_next);
     if (m->s) cudaStreamDestroy(m->s);
@@ -402,6 +461,45 @@ extern "C" int cpg_qwen3_create(const cpg_qwen3_desc *d, cpg_qwen3 **out) {
             return cuda_fail(ce, "cpg_qwen3_create: attention shared memory");
         }
     }
+    // tensor-core projections for prompts, when every projection is Q4_0 of a usable shape
+    bool dense = D % 256 == 0 && QD % 256 == 0 && KD % 256 == 0;
+    for (int l = 0; l < d->n_layers && dense; ++l) {
+        const cpg_qwen3_attn &A = d->attn[l];
+        dense = A.wq.enc == CPG_ENC_Q4 && A.wk.enc == CPG_ENC_Q4 && A.wv.enc == CPG_ENC_Q4 && A.wo.enc == CPG_ENC_Q4;
+    }
+    if (dense) {
+        std::vector<const uint8_t *> w;
+        std::vector<int> rows, k;
+        for (int l = 0; l < d->n_layers; ++l) {
+            const cpg_qwen3_attn &A = d->attn[l];
+            const uint8_t *p[4] = {(const uint8_t *)A.wq.p, (const uint8_t *)A.wk.p, (const uint8_t *)A.wv.p,
+                                   (const uint8_t *)A.wo.p};
+            const int r[4] = {(int)QD, (int)KD, (int)KD, (int)D}, kk[4] = {(int)D, (int)D, (int)D, (int)QD};
+            for (int i = 0; i < 4; ++i) {
+                w.push_back(p[i]); rows.push_back(r[i]); k.push_back(kk[i]);
+            }
+        }
+        int rc = gemm_tc_dense_maps(w.data(), rows.data(), k.data(), (int)w.size(), &m->dmaps);
+        if (rc) {
+            qwen3_free(m);
+            return rc;
+        }
+        ce = cudaMalloc(&m->dtab, 8 * sizeof(int4));
+        if (ce == cudaSuccess) ce = cudaMalloc(&m->dn_active, sizeof(int));
+        if (ce == cudaSuccess) ce = cudaMalloc(&m->iota, C * sizeof(int));
+        if (ce == cudaSuccess) ce = cudaMalloc(&m->d_status, sizeof(int));
+        if (ce == cudaSuccess) ce = cudaMalloc(&m->x16, C * 2 * (QD > D ? QD : D) * sizeof(__half));
+        if (ce == cudaSuccess) ce = cudaMemsetAsync(m->d_status, 0, sizeof(int), m->s);
+        if (ce == cudaSuccess) {
+            k_iota<<<(int)((C + 255) / 256), 256, 0, m->s>>>(m->iota, (int)C);
+            ce = cudaGetLastError();
+        }
+        if (ce == cudaSuccess) ce = cudaStreamSynchronize(m->s);
+        if (ce != cudaSuccess) {
+            qwen3_free(m);
+            return cuda_fail(ce, "cpg_qwen3_create: dense projection tables");
+        }
+    }
     *out = m;
     return CPG_OK;
 }
@@ -418,13 +516,27 @@ static int qwen3_enqueue(cpg_qwen3 *m, int T, cudaStream_t s) {
     const size_t C = (size_t)m->max_ctx;
     CPG_CUDA(launch_pdl(k_embed, dim3(T), dim3(256), 0, s, (const uint8_t *)m->embed.p, m->embed.enc,
                         (const int *)m->d_ids, D, m->x));
+    const bool dense = m->dmaps && T >= QW_DENSE_MIN_T;
+    if (dense) {
+        k_dense_tab<<<1, 32, 0, s>>>(m->dtab, m->dn_active, T);
+        CPG_CUDA(cudaGetLastError());
+    }
     for (int l = 0; l < m->L; ++l) {
         const cpg_qwen3_attn &A = m->attn[l];
         float *kc = m->kv + (size_t)l * 2 * C * KD, *vc = kc + C * KD;
-        // RMSNorm(x, ln1) and q, k, v in one streaming launch (decode-sized T), else separately
+        const void *maps = dense ? (const void *)((const uint8_t *)m->dmaps + (size_t)l * 12 * 128) : nullptr;
+        // RMSNorm(x, ln1) and q, k, v: prompts on the tensor cores; decode-sized T in one
+        // streaming launch; otherwise separately
         const int enc = A.wq.enc;
         int rc = 1;
-        if (A.wk.enc == enc && A.wv.enc == enc) {
+        if (dense) {
+            k_rmsnorm_f16<<<T, 256, 0, s>>>(m->x, A.ln1, D, m->eps, m->x16);
+            CPG_CUDA(cudaGetLastError());
+            rc = gemm_tc_dense(maps, m->dtab + 0, m->dn_active, m->iota, m->x16, T, QD, D, m->q, m->d_status, s);
+            if (!rc) rc = gemm_tc_dense(maps, m->dtab + 2, m->dn_active, m->iota, m->x16, T, KD, D, m->kst, m->d_status, s);
+            if (!rc) rc = gemm_tc_dense(maps, m->dtab + 4, m->dn_active, m->iota, m->x16, T, KD, D, m->vst, m->d_status, s);
+            if (rc) return rc;
+        } else if (A.wk.enc == enc && A.wv.enc == enc) {
             const GemvSeg seg[3] = {{(const uint8_t *)A.wq.p, m->q, QD}, {(const uint8_t *)A.wk.p, m->kst, KD},
                                     {(const uint8_t *)A.wv.p, m->vst, KD}};
             rc = gemv_multi(seg, 3, m->x, T, A.ln1, m->eps, D, enc, s);
@@ -444,7 +556,14 @@ static int qwen3_enqueue(cpg_qwen3 *m, int T, cudaStream_t s) {
         const size_t asmem = (size_t)m->max_ctx * sizeof(float);     // scores of every cached position
         CPG_CUDA(launch_pdl(k_attention, dim3(H, T), dim3(AT_THREADS), asmem, s, (const float *)m->q,
                             (const float *)kc, (const float *)vc, (const int *)m->d_pos, H, KV, m->ao));
-        rc = matvec_launch(m->at, m->ao, A.wo, QD, D, T, s);
+        if (dense) {
+            const size_t n = (size_t)T * QD;
+            k_split_f16<<<(int)((n + 255) / 256 < 1184 ? (n + 255) / 256 : 1184), 256, 0, s>>>(m->ao, T, QD, m->x16);
+            CPG_CUDA(cudaGetLastError());
+            rc = gemm_tc_dense(maps, m->dtab + 6, m->dn_active, m->iota, m->x16, T, D, QD, m->at, m->d_status, s);
+        } else {
+            rc = matvec_launch(m->at, m->ao, A.wo, QD, D, T, s);
+        }
         if (rc) return rc;
         rc = cpg_moe_forward(m->moe[l], m->x, m->at, T, nullptr, m->x, nullptr, nullptr, nullptr, m->ws, m->ws_bytes, s);
         if (rc) return rc;
@@ -505,10 +624,19 @@ extern "C" int cpg_qwen3_prefill(cpg_qwen3 *m, const int *ids, int T, int *next_
     CPG_CUDA(cudaMemcpyAsync(m->d_ids, ids, sizeof(int) * (size_t)T, cudaMemcpyHostToDevice, m->s));
     const int rc = qwen3_enqueue(m, T, m->s);
     if (rc) return rc;
+    int rc2 = 0;
     k_advance<<<1, 1, 0, m->s>>>(m->d_next, m->d_ids, m->d_pos, T, nullptr, 0);
     CPG_CUDA(cudaGetLastError());
     m->pos = T;
-    return qwen3_read_next(m, next_id);
+    rc2 = qwen3_read_next(m, next_id);
+    if (rc2 || !m->d_status) return rc2;
+    int st = 0;
+    CPG_CUDA(cudaMemcpy(&st, m->d_status, sizeof(int), cudaMemcpyDeviceToHost));
+    if (st != ST_OK) {
+        set_error("cpg_qwen3_prefill: a bounded wait in the projection GEMM timed out (status %d)", st);
+        return CPG_ETIMEOUT;
+    }
+    return CPG_OK;
 }
 
 extern "C" int cpg_qwen3_step(cpg_qwen3 *m, int id, int *next_id) {

@@ -50,6 +50,22 @@ def test_qwen3_shape_two_layers(orc, ref):
     assert max_rel(got_logits, want_logits) <= BLOCK_TOL
 
 
+def test_qwen3_shape_prompt_on_tensor_cores(orc, ref):
+    """A 64-token prompt at Qwen3-30B-A3B widths: the prompt pass runs the attention projections
+    on the tcgen05 GEMM (fp16 operands, fp32 accumulation); same ids, logits within the bar."""
+    m = O.SynthModel(2048, 32, 4, 128, 768, 128, 8, 4096, 2, seed=11, norm_jitter=0.05, oracle=orc)
+    prompt = np.random.default_rng(4).integers(0, m.vocab, 64).astype(np.int32)
+    want_ids, want_logits = ref.qwen3_generate(m, prompt, 3)
+    gm = device_model(m, max_ctx=80)
+    try:
+        got_ids = gm.generate(prompt, 3)
+        got_logits = gm.logits().cpu().numpy()
+    finally:
+        gm.close()
+    assert got_ids.tolist() == want_ids.tolist()
+    assert max_rel(got_logits, want_logits) <= BLOCK_TOL
+
+
 def test_step_matches_generate(orc):
     m = O.SynthModel(256, 4, 2, 128, 256, 16, 4, 512, 2, seed=6, oracle=orc)
     prompt = np.array([5, 100, 7], np.int32)
