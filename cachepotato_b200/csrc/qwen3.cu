@@ -283,6 +283,130 @@ __global__ void __launch_bounds__(AT_THREADS) k_attention(const float *__restric
     }
 }
 
+// The same attention for a prompt (T ≥ QW_DENSE_MIN_T new tokens): one block per (head h,
+// AP_QT consecutive queries), so each key and value row read from the cache serves AP_QT queries.
+//   scores   key tiles of AP_KT rows in shared memory; a thread holds 4 queries × 2 keys, each
+//            score a sequential f32 sum over the 128 elements (fused multiply-adds), then / √hd
+//   softmax  one warp per query row: max, expf(s - max), sum, divide (rows past the causal end
+//            are zero)
+//   output   value tiles in shared memory; warp w holds queries 4w..4w+3, lane l elements
+//            4l..4l+3, summed over positions in order
+// Shared memory: the (AP_QT, n_cap) score rows, one key/value tile, the query rows.
+constexpr int AP_QT = 32, AP_KT = 64, AP_KS = QW_HD + 4;        // row stride: conflict-free float4
+__global__ void __launch_bounds__(256) k_attention_prompt(const float *__restrict__ q, const float *__restrict__ kc,
+                                                          const float *__restrict__ vc, const int *__restrict__ d_pos,
+                                                          int T, int H, int KV, int n_cap, float *__restrict__ ao) {
+    extern __shared__ __align__(16) float smp[];
+    const int ss = (n_cap + 3) & ~3;                          // score row stride (16-byte rows)
+    float *sS = smp;                                          // (AP_QT, ss)
+    float *sK = sS + (size_t)AP_QT * ss;                      // (AP_KT, AP_KS) keys, then values
+    float *sQ = sK + AP_KT * AP_KS;                           // (AP_QT, hd)
+    const int h = blockIdx.x, q0 = blockIdx.y * AP_QT;
+    const int kh = h / (H / KV);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int pos0 = *d_pos;
+    const int nq = min(AP_QT, T - q0);
+    const int nmax = min(n_cap, pos0 + q0 + nq);              // keys the last query of the tile sees
+    const size_t ks = (size_t)KV * QW_HD;
+    for (int i = tid; i < AP_QT * QW_HD / 4; i += 256) {
+        const int qi = i / (QW_HD / 4), d4 = i % (QW_HD / 4);
+        const float4 v = qi < nq ? *reinterpret_cast<const float4 *>(q + ((size_t)(q0 + qi) * H + h) * QW_HD + 4 * d4)
+                                 : make_float4(0.f, 0.f, 0.f, 0.f);
+        *reinterpret_cast<float4 *>(sQ + qi * QW_HD + 4 * d4) = v;
+    }
+    const float scale = __fsqrt_rn((float)QW_HD);
+    const int qg = warp, kg = lane;                           // queries 4qg..4qg+3, keys kg, kg+32
+    for (int kt0 = 0; kt0 < nmax; kt0 += AP_KT) {
+        __syncthreads();
+        for (int i = tid; i < AP_KT * QW_HD / 4; i += 256) {
+            const int r = i / (QW_HD / 4), d4 = i % (QW_HD / 4);
+            const float4 v = kt0 + r < nmax ? *reinterpret_cast<const float4 *>(kc + (size_t)(kt0 + r) * ks + (size_t)kh * QW_HD + 4 * d4)
+                                            : make_float4(0.f, 0.f, 0.f, 0.f);
+            *reinterpret_cast<float4 *>(sK + r * AP_KS + 4 * d4) = v;
+        }
+        __syncthreads();
+        float acc[4][2] = {};
+#pragma unroll 4
+        for (int d4 = 0; d4 < QW_HD / 4; ++d4) {
+            float4 qv[4], kv[2];
+#pragma unroll
+            for (int a = 0; a < 4; ++a) qv[a] = *reinterpret_cast<const float4 *>(sQ + (4 * qg + a) * QW_HD + 4 * d4);
+#pragma unroll
+            for (int b = 0; b < 2; ++b) kv[b] = *reinterpret_cast<const float4 *>(sK + (kg + 32 * b) * AP_KS + 4 * d4);
+#pragma unroll
+            for (int a = 0; a < 4; ++a)
+#pragma unroll
+                for (int b = 0; b < 2; ++b) {
+                    float t = acc[a][b];
+                    t = fmaf(qv[a].x, kv[b].x, t);
+                    t = fmaf(qv[a].y, kv[b].y, t);
+                    t = fmaf(qv[a].z, kv[b].z, t);
+                    t = fmaf(qv[a].w, kv[b].w, t);
+                    acc[a][b] = t;
+                }
+        }
+#pragma unroll
+        for (int a = 0; a < 4; ++a)
+#pragma unroll
+            for (int b = 0; b < 2; ++b) {
+                const int j = kt0 + kg + 32 * b;
+                if (j < nmax) sS[(size_t)(4 * qg + a) * ss + j] = __fdiv_rn(acc[a][b], scale);
+            }
+    }
+    __syncthreads();
+    for (int qi = warp; qi < AP_QT; qi += 8) {                // softmax per row, zeros past the end
+        float *row = sS + (size_t)qi * ss;
+        const int n = qi < nq ? min(nmax, pos0 + q0 + qi + 1) : 0;
+        float mx = -INFINITY;
+        for (int j = lane; j < n; j += 32) mx = fmaxf(mx, row[j]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        float sum = 0.0f;
+        for (int j = lane; j < n; j += 32) {
+            const float ex = expf(__fsub_rn(row[j], mx));
+            row[j] = ex;
+            sum += ex;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        for (int j = lane; j < nmax; j += 32) row[j] = j < n ? __fdiv_rn(row[j], sum) : 0.0f;
+    }
+    float4 out[4];
+#pragma unroll
+    for (int a = 0; a < 4; ++a) out[a] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int vt0 = 0; vt0 < nmax; vt0 += AP_KT) {
+        __syncthreads();
+        for (int i = tid; i < AP_KT * QW_HD / 4; i += 256) {
+            const int r = i / (QW_HD / 4), d4 = i % (QW_HD / 4);
+            const float4 v = vt0 + r < nmax ? *reinterpret_cast<const float4 *>(vc + (size_t)(vt0 + r) * ks + (size_t)kh * QW_HD + 4 * d4)
+                                            : make_float4(0.f, 0.f, 0.f, 0.f);
+            *reinterpret_cast<float4 *>(sK + r * AP_KS + 4 * d4) = v;
+        }
+        __syncthreads();
+        const int jn = min(AP_KT, nmax - vt0);
+        for (int j = 0; j < jn; ++j) {
+            const float4 v = *reinterpret_cast<const float4 *>(sK + j * AP_KS + 4 * lane);
+#pragma unroll
+            for (int a = 0; a < 4; ++a) {
+                const float p = sS[(size_t)(4 * warp + a) * ss + vt0 + j];
+                out[a].x = fmaf(p, v.x, out[a].x);
+                out[a].y = fmaf(p, v.y, out[a].y);
+                out[a].z = fmaf(p, v.z, out[a].z);
+                out[a].w = fmaf(p, v.w, out[a].w);
+            }
+        }
+    }
+#pragma unroll
+    for (int a = 0; a < 4; ++a) {
+        const int qi = 4 * warp + a;
+        if (qi < nq) *reinterpret_cast<float4 *>(ao + ((size_t)(q0 + qi) * H + h) * QW_HD + 4 * lane) = out[a];
+    }
+}
+
+static size_t attention_prompt_smem(int n_cap) {
+    return sizeof(float) * ((size_t)AP_QT * ((n_cap + 3) & ~3) + AP_KT * AP_KS + AP_QT * QW_HD);
+}
+
 // argmax with the first maximum winning (cachepotato.c:353-356), NaN-free logits: each block
 // takes one contiguous chunk (partial results), then one block combines them; ties go to the
 // smaller index at every level.
@@ -380,6 +504,7 @@ struct cpg_qwen3 {
     int4 *dtab = nullptr;
     int *dn_active = nullptr, *iota = nullptr, *d_status = nullptr;
     __half *x16 = nullptr;
+    size_t ap_smem = 0;                            // shared memory k_attention_prompt may use
     void *ws = nullptr;
     size_t ws_bytes = 0;
     int pos = 0;
@@ -500,6 +625,16 @@ extern "C" int cpg_qwen3_create(const cpg_qwen3_desc *d, cpg_qwen3 **out) {
             return cuda_fail(ce, "cpg_qwen3_create: dense projection tables");
         }
     }
+    // prompt attention: the score rows of the whole context when they fit in shared memory
+    const size_t ap = attention_prompt_smem(d->max_ctx);
+    if (ap <= (size_t)smem_optin()) {
+        ce = cudaFuncSetAttribute(k_attention_prompt, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ap);
+        if (ce != cudaSuccess) {
+            qwen3_free(m);
+            return cuda_fail(ce, "cpg_qwen3_create: prompt attention shared memory");
+        }
+        m->ap_smem = ap;
+    }
     *out = m;
     return CPG_OK;
 }
@@ -553,9 +688,16 @@ static int qwen3_enqueue(cpg_qwen3 *m, int T, cudaStream_t s) {
         CPG_CUDA(launch_pdl(k_qk_norm_rope, dim3((warps + 7) / 8), dim3(256), 0, s, m->q, (const float *)m->kst,
                             (const float *)m->vst, kc, vc, T, (const int *)m->d_pos, H, KV, A.q_norm, A.k_norm,
                             m->theta, m->eps));
-        const size_t asmem = (size_t)m->max_ctx * sizeof(float);     // scores of every cached position
-        CPG_CUDA(launch_pdl(k_attention, dim3(H, T), dim3(AT_THREADS), asmem, s, (const float *)m->q,
-                            (const float *)kc, (const float *)vc, (const int *)m->d_pos, H, KV, m->ao));
+        const int n_cap = m->pos + T;                                // prompt: positions known here
+        if (T >= QW_DENSE_MIN_T && attention_prompt_smem(n_cap) <= m->ap_smem) {
+            k_attention_prompt<<<dim3(H, (T + AP_QT - 1) / AP_QT), 256, attention_prompt_smem(n_cap), s>>>(
+                (const float *)m->q, (const float *)kc, (const float *)vc, (const int *)m->d_pos, T, H, KV, n_cap, m->ao);
+            CPG_CUDA(cudaGetLastError());
+        } else {
+            const size_t asmem = (size_t)m->max_ctx * sizeof(float);     // scores of every cached position
+            CPG_CUDA(launch_pdl(k_attention, dim3(H, T), dim3(AT_THREADS), asmem, s, (const float *)m->q,
+                                (const float *)kc, (const float *)vc, (const int *)m->d_pos, H, KV, m->ao));
+        }
         if (dense) {
             const size_t n = (size_t)T * QD;
             k_split_f16<<<(int)((n + 255) / 256 < 1184 ? (n + 255) / 256 : 1184), 256, 0, s>>>(m->ao, T, QD, m->x16);
