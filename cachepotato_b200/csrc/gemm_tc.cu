@@ -231,11 +231,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const TcArgs a, const
     const int K_in = KIND == 0 ? a.D : a.F;
     const int n_rows = KIND == 0 ? a.F : a.D;
     const int MT = KIND == 0 ? n_rows / TC_BM : n_rows / TC_ROWS;   // row tiles per expert
-    // KIND 2 (dense projections) runs K three times: W_hi·x_hi, W_hi·x_lo, W_lo·x_hi, where
-    // x = x_hi + x_lo (the token rows hold [x_hi | x_lo]) and W_hi + W_lo = q·d exactly
-    const int KST1 = K_in / TC_BK;                                  // K stages of one pass
-    const int NG1 = KST1 / TC_GRP;
-    const int KST = KIND == 2 ? 3 * KST1 : KST1;                    // K stages per tile
+    // KIND 2 (dense projections): three passes, each its own tiles and output plane,
+    // W_hi·x_hi, W_hi·x_lo, W_lo·x_hi, where x = x_hi + x_lo (the token rows hold [x_hi | x_lo])
+    // and W_hi + W_lo = q·d exactly; 128-token tiles, for more CTAs on short prompts
+    constexpr int NPASS = KIND == 2 ? 3 : 1;
+    constexpr int BN = KIND == 2 ? TC_BN_SMALL : TC_BN;             // tokens per tile
+    const int KST = K_in / TC_BK;                                   // K stages per tile
     const int NG = KST / TC_GRP;                                    // raw groups per tile
     constexpr int NMATH = TC_MATH_WARPS * 32;
 
@@ -267,7 +268,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const TcArgs a, const
         int acc = 0;
         for (int u = 0; u < U; ++u) {
             s_tpre[u] = acc;
-            acc += (s_act[u].z + TC_BN - 1) / TC_BN;
+            acc += (s_act[u].z + BN - 1) / BN;
         }
         s_tpre[U] = acc;
     }
@@ -275,13 +276,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const TcArgs a, const
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = s_tmem;
-    const int total = MT * s_tpre[U];
+    const int per_pass = MT * s_tpre[U];
+    const int total = per_pass * NPASS;
     volatile int *abort_flag = &s_abort;
     const uint32_t sbase = smem_u32(smem);
 
     // tile -> (active expert u, row tile m, token tile n); token tiles innermost so the tiles of
     // one weight block run back to back and its later reads hit L2
-    auto decode = [&](int tile, int &u, int &m, int &n) {
+    auto decode = [&](int tile, int &u, int &m, int &n, int &pass) {
+        pass = NPASS > 1 ? tile / per_pass : 0;
+        tile -= pass * per_pass;
         int lo = 0, hi = U;
         while (hi - lo > 1) {
             const int mid = (lo + hi) >> 1;
@@ -301,8 +305,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const TcArgs a, const
             int git = 0;
             bool ok = true;
             for (int tile = blockIdx.x; ok && tile < total; tile += gridDim.x) {
-                int u, m, n;
-                decode(tile, u, m, n);
+                int u, m, n, pass;
+                decode(tile, u, m, n, pass);
                 const int e = s_act[u].x;
                 const CUtensorMap *m0 = maps + 3 * e + (KIND == 0 ? 0 : 2);
                 const CUtensorMap *m1 = KIND == 0 ? maps + 3 * e + 1 : m0;
@@ -317,9 +321,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const TcArgs a, const
                     }
                     uint8_t *dst = smem + slot * TC_RAW_BYTES;
                     mbar_arrive_expect_tx(&raw_full[slot], TC_RAW_BYTES);
-                    const int gx = (KIND == 2 ? g % NG1 : g) * TC_RAW_ROW;   // each pass re-reads W
-                    tma_load_2d(dst, m0, gx, y0, &raw_full[slot]);
-                    tma_load_2d(dst + TC_BM * TC_RAW_ROW, m1, gx, y1, &raw_full[slot]);
+                    tma_load_2d(dst, m0, g * TC_RAW_ROW, y0, &raw_full[slot]);
+                    tma_load_2d(dst + TC_BM * TC_RAW_ROW, m1, g * TC_RAW_ROW, y1, &raw_full[slot]);
                 }
             }
             // the last groups' copies must land before the CTA may exit (bounded)
@@ -331,9 +334,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const TcArgs a, const
         if (lane == 0) {
             int it = 0, ti = 0;
             for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++ti) {
-                int u, m, n;
-                decode(tile, u, m, n);
-                const int cnt = min(TC_BN, s_act[u].z - n * TC_BN);
+                int u, m, n, pass;
+                decode(tile, u, m, n, pass);
+                const int cnt = min(BN, s_act[u].z - n * BN);
                 const uint32_t idesc = umma_idesc_f16(TC_BM, (cnt + 15) & ~15);
                 if (ti > 0 && !tc_wait(&acc_empty, (uint32_t)(ti - 1) & 1u, abort_flag, a.status, ST_TIMEOUT_EMPTY)) break;
                 tc_fence_after();
@@ -376,10 +379,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const TcArgs a, const
             int it = 0;
             bool ok = true;
             for (int tile = blockIdx.x; ok && tile < total; tile += gridDim.x) {
-                int u, m, n;
-                decode(tile, u, m, n);
-                const int row0 = s_act[u].y + n * TC_BN;
-                const bool small = s_act[u].z - n * TC_BN <= TC_BN_SMALL;
+                int u, m, n, pass;
+                decode(tile, u, m, n, pass);
+                const int row0 = s_act[u].y + n * BN;
+                const bool small = s_act[u].z - n * BN <= TC_BN_SMALL;
                 const CUtensorMap *bmap = small ? &tmap_b_small : &tmap_b;
                 const uint32_t bbytes = small ? TC_B_BYTES / 2 : TC_B_BYTES;
                 for (int ks = 0; ks < KST; ++ks, ++it) {
@@ -392,7 +395,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const TcArgs a, const
                     }
                     mbar_arrive_expect_tx(&b_full[st], bbytes);
                     // KIND 2: x_hi in passes 0 and 2, x_lo (columns K_in..2K_in) in pass 1
-                    const int bx = KIND == 2 ? (ks % KST1) * TC_BK + (ks / KST1 == 1 ? K_in : 0) : ks * TC_BK;
+                    const int bx = ks * TC_BK + (KIND == 2 && pass == 1 ? K_in : 0);
                     tma_load_2d(smem + TC_STAGE0 + st * TC_STAGE_BYTES + TC_A_BYTES, bmap, bx, row0, &b_full[st]);
                 }
             }
@@ -410,11 +413,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const TcArgs a, const
         const int hr = wrow >> 7, rr = wrow & 127;         // half, row within half
         int it = 0, git = 0, ti = 0;
         for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++ti) {
-            int u, m, n;
-            decode(tile, u, m, n);
+            int u, m, n, pass;
+            decode(tile, u, m, n, pass);
             const int4 ex = s_act[u];
-            const int off = ex.y + n * TC_BN;
-            const int cnt = min(TC_BN, ex.z - n * TC_BN);
+            const int off = ex.y + n * BN;
+            const int cnt = min(BN, ex.z - n * BN);
             bool ok = true;
             for (int g = 0; g < NG && ok; ++g, ++git) {
                 const int slot = git & 1;
@@ -452,7 +455,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const TcArgs a, const
                     const uint32_t u0 = hb ? __byte_perm(w2, w[j][3], 0x5432) : __byte_perm(w0, w[j][3], 0x5432);
                     const uint32_t u1 = hb ? __byte_perm(w[j][3], w4, 0x5432) : __byte_perm(w[j][3], w2, 0x5432);
                     uint4 l0, h0, l1, h1;
-                    const bool low = KIND == 2 && g >= 2 * NG1;   // W_lo in the third pass
+                    const bool low = KIND == 2 && pass == 2;      // W_lo in the third pass
                     q4_half_group(u0, u1, d0 | (d0 << 16), l0, h0, low);
                     q4_half_group(w[j][4], w[j][5], d1 | (d1 << 16), l1, h1, low);
                     uint8_t *sa0 = smem + TC_STAGE0 + st0 * TC_STAGE_BYTES + hr * (TC_BM / 8) * TC_SBO;
@@ -478,7 +481,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const TcArgs a, const
             if (!__all_sync(0xffffffffu, got)) break;
             tc_fence_after();
             const int row = quad * 32 + lane;              // accumulator row (TMEM lane)
-            for (int c0 = colq * (TC_BN / 4); c0 < colq * (TC_BN / 4) + TC_BN / 4 && c0 < cnt; c0 += 32) {
+            for (int c0 = colq * (BN / 4); c0 < colq * (BN / 4) + BN / 4 && c0 < cnt; c0 += 32) {
                 float g[32], w2[32];
                 tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + c0, g);
                 tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + TC_BN + c0, w2);
@@ -500,7 +503,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const TcArgs a, const
                     for (int j = 0; j < 32; ++j) {
                         const int col = c0 + j;
                         if (col < cnt) {
-                            float *yr = a.y_out + (size_t)a.pairs[off + col] * a.D + m * TC_ROWS;
+                            float *yr = a.y_out + (KIND == 2 ? pass * a.pass_stride : 0) +
+                                        (size_t)a.pairs[off + col] * a.D + m * TC_ROWS;
                             yr[row] = g[j];
                             yr[TC_BM + row] = w2[j];
                         }
@@ -620,8 +624,16 @@ int gemm_tc_dense_maps(const uint8_t *const *w, const int *rows, const int *k, i
     return CPG_OK;
 }
 
+// y = p0 + p1 + p2 over the three planes of the passes, in that order.
+__global__ void k_sum3(const float4 *__restrict__ p, size_t n4, float4 *__restrict__ y) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
+        const float4 a = p[i], b = p[n4 + i], c = p[2 * n4 + i];
+        y[i] = make_float4((a.x + b.x) + c.x, (a.y + b.y) + c.y, (a.z + b.z) + c.z, (a.w + b.w) + c.w);
+    }
+}
+
 int gemm_tc_dense(const void *maps, const int4 *tab, const int *n_active, const int *iota, const __half *x16, int T,
-                  int rows, int k, float *y, int *status, cudaStream_t s) {
+                  int rows, int k, float *y, float *planes, int *status, cudaStream_t s) {
     TcArgs a{};
     a.n_active = n_active;
     a.act = tab;
@@ -630,9 +642,15 @@ int gemm_tc_dense(const void *maps, const int4 *tab, const int *n_active, const 
     a.D = rows;
     a.F = k;
     a.K = 1;
-    a.y_out = y;
+    a.y_out = planes;
+    a.pass_stride = (size_t)T * rows;
     a.status = status;
-    return gemm_tc_launch(2, a, x16, T, (rows / TC_ROWS) * ((T + TC_BN - 1) / TC_BN), s);
+    const int rc = gemm_tc_launch(2, a, x16, T, 3 * (rows / TC_ROWS) * ((T + TC_BN_SMALL - 1) / TC_BN_SMALL), s);
+    if (rc) return rc;
+    const size_t n4 = (size_t)T * rows / 4;
+    k_sum3<<<(int)(n4 / 256 + 1 < 1184 ? n4 / 256 + 1 : 1184), 256, 0, s>>>((const float4 *)planes, n4, (float4 *)y);
+    CPG_CUDA(cudaGetLastError());
+    return CPG_OK;
 }
 
 int gemm_tc_launch(int kind, const TcArgs &a, const __half *b, int b_rows, int max_tiles, cudaStream_t s) {

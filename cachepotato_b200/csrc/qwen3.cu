@@ -504,6 +504,7 @@ struct cpg_qwen3 {
     int4 *dtab = nullptr;
     int *dn_active = nullptr, *iota = nullptr, *d_status = nullptr;
     __half *x16 = nullptr;
+    float *planes = nullptr;                       // the projection GEMM's three pass planes
     size_t ap_smem = 0;                            // shared memory k_attention_prompt may use
     void *ws = nullptr;
     size_t ws_bytes = 0;
@@ -519,7 +520,7 @@ static void qwen3_free(cpg_qwen3 *m) {
     cudaFree(m->kst); cudaFree(m->vst); cudaFree(m->d_pos); cudaFree(m->d_out);
     cudaFree(m->am_v); cudaFree(m->am_i);
     cudaFree(m->dmaps); cudaFree(m->dtab); cudaFree(m->dn_active); cudaFree(m->iota); cudaFree(m->d_status);
-    cudaFree(m->x16);
+    cudaFree(m->x16); cudaFree(m->planes);
     if (m->step_graph) cudaGraphExecDestroy(m->step_graph);
     if (m->h_next) cudaFreeHost(m->h_next);
     if (m->s) cudaStreamDestroy(m->s);
@@ -614,6 +615,7 @@ extern "C" int cpg_qwen3_create(const cpg_qwen3_desc *d, cpg_qwen3 **out) {
         if (ce == cudaSuccess) ce = cudaMalloc(&m->iota, C * sizeof(int));
         if (ce == cudaSuccess) ce = cudaMalloc(&m->d_status, sizeof(int));
         if (ce == cudaSuccess) ce = cudaMalloc(&m->x16, C * 2 * (QD > D ? QD : D) * sizeof(__half));
+        if (ce == cudaSuccess) ce = cudaMalloc(&m->planes, C * 3 * (QD > D ? QD : D) * sizeof(float));
         if (ce == cudaSuccess) ce = cudaMemsetAsync(m->d_status, 0, sizeof(int), m->s);
         if (ce == cudaSuccess) {
             k_iota<<<(int)((C + 255) / 256), 256, 0, m->s>>>(m->iota, (int)C);
@@ -667,9 +669,9 @@ static int qwen3_enqueue(cpg_qwen3 *m, int T, cudaStream_t s) {
         if (dense) {
             k_rmsnorm_f16<<<T, 256, 0, s>>>(m->x, A.ln1, D, m->eps, m->x16);
             CPG_CUDA(cudaGetLastError());
-            rc = gemm_tc_dense(maps, m->dtab + 0, m->dn_active, m->iota, m->x16, T, QD, D, m->q, m->d_status, s);
-            if (!rc) rc = gemm_tc_dense(maps, m->dtab + 2, m->dn_active, m->iota, m->x16, T, KD, D, m->kst, m->d_status, s);
-            if (!rc) rc = gemm_tc_dense(maps, m->dtab + 4, m->dn_active, m->iota, m->x16, T, KD, D, m->vst, m->d_status, s);
+            rc = gemm_tc_dense(maps, m->dtab + 0, m->dn_active, m->iota, m->x16, T, QD, D, m->q, m->planes, m->d_status, s);
+            if (!rc) rc = gemm_tc_dense(maps, m->dtab + 2, m->dn_active, m->iota, m->x16, T, KD, D, m->kst, m->planes, m->d_status, s);
+            if (!rc) rc = gemm_tc_dense(maps, m->dtab + 4, m->dn_active, m->iota, m->x16, T, KD, D, m->vst, m->planes, m->d_status, s);
             if (rc) return rc;
         } else if (A.wk.enc == enc && A.wv.enc == enc) {
             const GemvSeg seg[3] = {{(const uint8_t *)A.wq.p, m->q, QD}, {(const uint8_t *)A.wk.p, m->kst, KD},
@@ -702,7 +704,7 @@ static int qwen3_enqueue(cpg_qwen3 *m, int T, cudaStream_t s) {
             const size_t n = (size_t)T * QD;
             k_split_f16<<<(int)((n + 255) / 256 < 1184 ? (n + 255) / 256 : 1184), 256, 0, s>>>(m->ao, T, QD, m->x16);
             CPG_CUDA(cudaGetLastError());
-            rc = gemm_tc_dense(maps, m->dtab + 6, m->dn_active, m->iota, m->x16, T, D, QD, m->at, m->d_status, s);
+            rc = gemm_tc_dense(maps, m->dtab + 6, m->dn_active, m->iota, m->x16, T, D, QD, m->at, m->planes, m->d_status, s);
         } else {
             rc = matvec_launch(m->at, m->ao, A.wo, QD, D, T, s);
         }
