@@ -403,6 +403,115 @@ __global__ void __launch_bounds__(256) k_attention_prompt(const float *__restric
     }
 }
 
+// Decode-sized T: the positions of each (query, head) are split into AS_SPLIT ranges, one block
+// each, so that a step's attention spreads over H·AS_SPLIT blocks whatever the context:
+//   block    scores of its range (warp per position, lane l elements 4l..4l+3, shuffle sum),
+//            local max m and sum l of expf(s - m), o = Σ expf(s - m)·v (positions in order per
+//            warp, warps added in order); (m, l, o) to part
+//   last     the block that finishes last for (query, head) (a counter per pair, reset by that
+//            block) merges the ranges: M = max m, out = Σ o·e^(m-M) / Σ l·e^(m-M)
+// The range length follows the device position, so a captured step serves every position.
+constexpr int AS_SPLIT = 16, AS_THREADS = 256;
+__global__ void __launch_bounds__(AS_THREADS) k_attention_split(const float *__restrict__ q, const float *__restrict__ kc,
+                                                                const float *__restrict__ vc, const int *__restrict__ d_pos,
+                                                                int H, int KV, float *__restrict__ part, int *__restrict__ cnt,
+                                                                float *__restrict__ ao) {
+    pdl_wait();
+    pdl_launch_dependents();
+    extern __shared__ float s_sc[];                               // the range's scores
+    __shared__ float s_red[AS_THREADS / 32];
+    __shared__ __align__(16) float s_o[AS_THREADS / 32][QW_HD];
+    __shared__ int s_last;
+    const int h = blockIdx.x, b = blockIdx.y, i = blockIdx.z;
+    const int kh = h / (H / KV);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int n = *d_pos + i + 1;
+    const int chunk = (n + AS_SPLIT - 1) / AS_SPLIT;
+    const int j0 = b * chunk, len = max(0, min(n, j0 + chunk) - j0);
+    const size_t ks = (size_t)KV * QW_HD;
+    const float4 qv = *reinterpret_cast<const float4 *>(q + ((size_t)i * H + h) * QW_HD + 4 * lane);
+    const float scale = __fsqrt_rn((float)QW_HD);
+    const float *kb = kc + (size_t)kh * QW_HD + 4 * lane, *vb = vc + (size_t)kh * QW_HD + 4 * lane;
+    for (int jj = warp; jj < len; jj += AS_THREADS / 32) {
+        const float4 kv = __ldg(reinterpret_cast<const float4 *>(kb + (size_t)(j0 + jj) * ks));
+        float sv = fmaf(qv.x, kv.x, fmaf(qv.y, kv.y, fmaf(qv.z, kv.z, __fmul_rn(qv.w, kv.w))));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) sv += __shfl_xor_sync(0xffffffffu, sv, o);
+        if (lane == 0) s_sc[jj] = __fdiv_rn(sv, scale);
+    }
+    __syncthreads();
+    float mx = -INFINITY;
+    for (int jj = tid; jj < len; jj += AS_THREADS) mx = fmaxf(mx, s_sc[jj]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (lane == 0) s_red[warp] = mx;
+    __syncthreads();
+    mx = s_red[0];
+#pragma unroll
+    for (int w = 1; w < AS_THREADS / 32; ++w) mx = fmaxf(mx, s_red[w]);
+    __syncthreads();
+    float sum = 0.0f;
+    for (int jj = tid; jj < len; jj += AS_THREADS) {
+        const float ex = expf(__fsub_rn(s_sc[jj], mx));
+        s_sc[jj] = ex;
+        sum += ex;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    if (lane == 0) s_red[warp] = sum;
+    __syncthreads();
+    sum = 0.0f;
+#pragma unroll
+    for (int w = 0; w < AS_THREADS / 32; ++w) sum += s_red[w];
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int jj = warp; jj < len; jj += AS_THREADS / 32) {
+        const float4 v = __ldg(reinterpret_cast<const float4 *>(vb + (size_t)(j0 + jj) * ks));
+        const float p = s_sc[jj];
+        acc.x = fmaf(p, v.x, acc.x);
+        acc.y = fmaf(p, v.y, acc.y);
+        acc.z = fmaf(p, v.z, acc.z);
+        acc.w = fmaf(p, v.w, acc.w);
+    }
+    *reinterpret_cast<float4 *>(&s_o[warp][4 * lane]) = acc;
+    __syncthreads();
+    float *pp = part + (((size_t)i * H + h) * AS_SPLIT + b) * (QW_HD + 2);
+    if (tid < QW_HD) {
+        float o = 0.0f;
+#pragma unroll
+        for (int w = 0; w < AS_THREADS / 32; ++w) o += s_o[w][tid];
+        pp[2 + tid] = o;
+    }
+    if (tid == 0) {
+        pp[0] = mx;
+        pp[1] = sum;
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) s_last = atomicAdd(&cnt[i * H + h], 1) == AS_SPLIT - 1;
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    if (tid < QW_HD) {
+        const float *p0 = part + ((size_t)i * H + h) * AS_SPLIT * (QW_HD + 2);
+        float M = -INFINITY;
+        for (int r = 0; r < AS_SPLIT; ++r) {
+            const float l = __ldcg(p0 + r * (QW_HD + 2) + 1);
+            if (l > 0.0f) M = fmaxf(M, __ldcg(p0 + r * (QW_HD + 2)));
+        }
+        float L = 0.0f, o = 0.0f;
+        for (int r = 0; r < AS_SPLIT; ++r) {
+            const float l = __ldcg(p0 + r * (QW_HD + 2) + 1);
+            if (l > 0.0f) {
+                const float e = expf(__fsub_rn(__ldcg(p0 + r * (QW_HD + 2)), M));
+                L = fmaf(l, e, L);
+                o = fmaf(__ldcg(p0 + r * (QW_HD + 2) + 2 + tid), e, o);
+            }
+        }
+        ao[((size_t)i * H + h) * QW_HD + tid] = __fdiv_rn(o, L);
+    }
+    if (tid == 0) cnt[i * H + h] = 0;                             // ready for the next launch
+}
+
 static size_t attention_prompt_smem(int n_cap) {
     return sizeof(float) * ((size_t)AP_QT * ((n_cap + 3) & ~3) + AP_KT * AP_KS + AP_QT * QW_HD);
 }
@@ -505,6 +614,8 @@ struct cpg_qwen3 {
     int *dn_active = nullptr, *iota = nullptr, *d_status = nullptr;
     __half *x16 = nullptr;
     float *planes = nullptr;                       // the projection GEMM's three pass planes
+    float *as_part = nullptr;                      // split attention: (T < QW_DENSE_MIN_T, H, AS_SPLIT, 2 + hd)
+    int *as_cnt = nullptr;                         // and a counter per (query, head), zero between launches
     size_t ap_smem = 0;                            // shared memory k_attention_prompt may use
     void *ws = nullptr;
     size_t ws_bytes = 0;
@@ -520,7 +631,7 @@ static void qwen3_free(cpg_qwen3 *m) {
     cudaFree(m->kst); cudaFree(m->vst); cudaFree(m->d_pos); cudaFree(m->d_out);
     cudaFree(m->am_v); cudaFree(m->am_i);
     cudaFree(m->dmaps); cudaFree(m->dtab); cudaFree(m->dn_active); cudaFree(m->iota); cudaFree(m->d_status);
-    cudaFree(m->x16); cudaFree(m->planes);
+    cudaFree(m->x16); cudaFree(m->planes); cudaFree(m->as_part); cudaFree(m->as_cnt);
     if (m->step_graph) cudaGraphExecDestroy(m->step_graph);
     if (m->h_next) cudaFreeHost(m->h_next);
     if (m->s) cudaStreamDestroy(m->s);
@@ -571,6 +682,10 @@ extern "C" int cpg_qwen3_create(const cpg_qwen3_desc *d, cpg_qwen3 **out) {
     if (ce == cudaSuccess) ce = cudaMalloc(&m->d_out, (C + 1) * 4);
     if (ce == cudaSuccess) ce = cudaMallocHost(&m->h_next, 4);
     if (ce == cudaSuccess) ce = cudaMalloc(&m->ws, m->ws_bytes);
+    if (ce == cudaSuccess)
+        ce = cudaMalloc(&m->as_part, (size_t)QW_DENSE_MIN_T * d->n_heads * AS_SPLIT * (QW_HD + 2) * sizeof(float));
+    if (ce == cudaSuccess) ce = cudaMalloc(&m->as_cnt, (size_t)QW_DENSE_MIN_T * d->n_heads * sizeof(int));
+    if (ce == cudaSuccess) ce = cudaMemset(m->as_cnt, 0, (size_t)QW_DENSE_MIN_T * d->n_heads * sizeof(int));
     if (ce != cudaSuccess) {
         qwen3_free(m);
         return cuda_fail(ce, "cpg_qwen3_create: allocation");
@@ -695,6 +810,11 @@ static int qwen3_enqueue(cpg_qwen3 *m, int T, cudaStream_t s) {
             k_attention_prompt<<<dim3(H, (T + AP_QT - 1) / AP_QT), 256, attention_prompt_smem(n_cap), s>>>(
                 (const float *)m->q, (const float *)kc, (const float *)vc, (const int *)m->d_pos, T, H, KV, n_cap, m->ao);
             CPG_CUDA(cudaGetLastError());
+        } else if (T < QW_DENSE_MIN_T) {
+            const size_t ssmem = (size_t)((m->max_ctx + AS_SPLIT - 1) / AS_SPLIT) * sizeof(float);
+            CPG_CUDA(launch_pdl(k_attention_split, dim3(H, AS_SPLIT, T), dim3(AS_THREADS), ssmem, s, (const float *)m->q,
+                                (const float *)kc, (const float *)vc, (const int *)m->d_pos, H, KV, m->as_part,
+                                m->as_cnt, m->ao));
         } else {
             const size_t asmem = (size_t)m->max_ctx * sizeof(float);     // scores of every cached position
             CPG_CUDA(launch_pdl(k_attention, dim3(H, T), dim3(AT_THREADS), asmem, s, (const float *)m->q,
