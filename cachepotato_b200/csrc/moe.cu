@@ -309,6 +309,14 @@ __global__ void __launch_bounds__(R_THREADS, 2) k_router(RouterArgs a) {
     if (tid < 64) s_p2e[tid] = perm_of(a.xn_enc).pos_to_elem[tid];
     const int e0 = blockIdx.x * a.eb;
     const int D = a.D;
+    {   // the router rows and the gain do not depend on the previous kernel: into L2 meanwhile
+        const char *wb = reinterpret_cast<const char *>(a.wgate + (size_t)e0 * D);
+        const size_t wbytes = (size_t)max(0, min(a.eb, a.E - e0)) * D * sizeof(float);
+        for (size_t o = (size_t)tid * 128; o < wbytes; o += (size_t)R_THREADS * 128)
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(wb + o));
+        for (int o = tid * 128; o < D * (int)sizeof(float); o += R_THREADS * 128)
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<const char *>(a.ln2) + o));
+    }
     pdl_wait();                                           // x comes from the previous kernel
     pdl_launch_dependents();
     if (blockIdx.x == 0 && blockIdx.y == 0) {
