@@ -387,15 +387,23 @@ __global__ void __launch_bounds__(R_THREADS, 2) k_router(RouterArgs a) {
                 }
             }
         }
-        __syncwarp();
-        if (blockIdx.x == 0) {
-            // fp16 copy of xn in the expert kernels' K order
-            __half *dst = a.xn_perm + (size_t)(t0 + warp) * D;
-            for (int pos = lane; pos < D; pos += 32)
-                dst[pos] = __float2half_rn(row[(pos & ~63) + s_p2e[pos & 63]]);
-        }
     }
     __syncthreads();
+    // fp16 copy of xn in the expert kernels' K order: CTA x of the cluster writes token x of the
+    // tile, eight values (one 16-byte store) per thread
+    for (int t = blockIdx.x; t < nt; t += gridDim.x) {
+        const float *row = xs + t * D;
+        for (int p0 = tid * 8; p0 < D; p0 += R_THREADS * 8) {
+            uint32_t h[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int q0 = p0 + 2 * k, q1 = q0 + 1;
+                const __half2 v = __floats2half2_rn(row[(q0 & ~63) + s_p2e[q0 & 63]], row[(q1 & ~63) + s_p2e[q1 & 63]]);
+                h[k] = *reinterpret_cast<const uint32_t *>(&v);
+            }
+            *reinterpret_cast<uint4 *>(a.xn_perm + (size_t)(t0 + t) * D + p0) = make_uint4(h[0], h[1], h[2], h[3]);
+        }
+    }
     // logits = Wgate·xn (matmul_wx, kernels.c:84-95): warp w owns experts e0 + w, e0 + w + 8, ...
     for (int el = warp; el < a.eb; el += R_THREADS / 32) {
         const int e = e0 + el;
@@ -435,8 +443,8 @@ __global__ void __launch_bounds__(R_THREADS, 2) k_router(RouterArgs a) {
         }
     }
     // every logit of the tile is written once the cluster (all CTAs of this token tile) has
-    // passed the barrier; CTA r then routes tokens r, r + cluster size, ... of the tile
-    __threadfence();
+    // passed the barrier (release/acquire at cluster scope); CTA r then routes tokens r,
+    // r + cluster size, ... of the tile
     cluster_sync();
     const int rank = cluster_ctarank(), csz = cluster_nctarank();
     for (int r = rank, i = 0; r < nt; r += csz, ++i)
