@@ -442,8 +442,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const TcArgs a, const
                 for (int j = 0; j < TC_GRP / 2; ++j) {     // group pair j -> stages it+2j, it+2j+1
                     const int i0 = it + 2 * j, i1 = i0 + 1;
                     const int st0 = i0 % TC_STAGES, st1 = i1 % TC_STAGES;
-                    if (i0 >= TC_STAGES &&
-                        (!tc_wait(&empty_bar[st0], (uint32_t)(i0 / TC_STAGES - 1) & 1u, abort_flag, a.status, ST_TIMEOUT_EMPTY) ||
+                    // each stage waits for its own previous use (a pair of stages straddles the
+                    // first pass through the ring if the stage count is odd)
+                    if ((i0 >= TC_STAGES &&
+                         !tc_wait(&empty_bar[st0], (uint32_t)(i0 / TC_STAGES - 1) & 1u, abort_flag, a.status, ST_TIMEOUT_EMPTY)) ||
+                        (i1 >= TC_STAGES &&
                          !tc_wait(&empty_bar[st1], (uint32_t)(i1 / TC_STAGES - 1) & 1u, abort_flag, a.status, ST_TIMEOUT_EMPTY))) {
                         ok = false;
                         break;
