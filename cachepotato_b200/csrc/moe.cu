@@ -935,21 +935,24 @@ struct cpg_moe_layer {
     void *d_dmaps = nullptr;       // device (E, 3) maps for the decode expert kernels (K slices of
                                    // 256 values, 64-row gate/up and 128-row down boxes), built here
     std::mutex wmaps_mu;
-    cpg::KernelPlan gateup, down;
+    cpg::KernelPlan gateup, down;            // two CTAs per SM, ~100 KB of stages each
+    cpg::KernelPlan gateup_deep, down_deep;  // one CTA per SM with all the shared memory in stages:
+                                             // for launches with at most one item per SM
 };
 
 namespace cpg {
 
 template <int ENC, int KIND>
-static int plan_kernel(KernelPlan &p) {
+static int plan_kernel(KernelPlan &p, bool deep) {
     using C = ExCfg<ENC, KIND>;
     auto *k = k_experts<ENC, KIND>;
     const size_t fixed = sizeof(float) * 4 * EX_NCH * 128 + 8 * (sizeof(StageMeta) + 24) + 256;
     cudaFuncAttributes fa;
     CPG_CUDA(cudaFuncGetAttributes(&fa, k));
     const size_t limit = (size_t)smem_optin() - fa.sharedSizeBytes;
-    // two CTAs per SM (latency hiding comes from warps); stages fill about 100 KB per CTA
-    int S = (int)((100 * 1024 - fixed) / C::STAGE);
+    // two CTAs per SM (latency hiding comes from warps); stages fill about 100 KB per CTA. Deep:
+    // one CTA per SM, as many stages as fit (up to 8 = every K slice of a gate/up item in flight)
+    int S = (int)(((deep ? limit : 100 * 1024) - fixed) / C::STAGE);
     if (S < 2) S = 2;
     if (S > 8) S = 8;
     while (S > 1 && fixed + (size_t)S * C::STAGE > limit) --S;
@@ -968,7 +971,9 @@ static int plan_kernel(KernelPlan &p) {
 }
 
 static int launch_experts(const cpg_moe_layer *L, int KIND, const ExpertArgs &a, int max_items, cudaStream_t s) {
-    const KernelPlan &p = KIND == KIND_GATEUP ? L->gateup : L->down;
+    // few items (one token: 8 experts): one CTA per SM with the whole item's slices in flight
+    const bool deep = max_items <= sm_count();
+    const KernelPlan &p = KIND == KIND_GATEUP ? (deep ? L->gateup_deep : L->gateup) : (deep ? L->down_deep : L->down);
     const int grid = max_items < p.ctas ? (max_items > 0 ? max_items : 1) : p.ctas;
     ExpertArgs b = a;
     b.stages = p.stages;
@@ -1053,11 +1058,15 @@ extern "C" int cpg_moe_layer_create(const cpg_moe_desc *d, cpg_moe_layer **out) 
     }
     int rc;
     if (enc == CPG_ENC_Q4) {
-        rc = plan_kernel<CPG_ENC_Q4, KIND_GATEUP>(L->gateup);
-        if (rc == CPG_OK) rc = plan_kernel<CPG_ENC_Q4, KIND_DOWN>(L->down);
+        rc = plan_kernel<CPG_ENC_Q4, KIND_GATEUP>(L->gateup, false);
+        if (rc == CPG_OK) rc = plan_kernel<CPG_ENC_Q4, KIND_DOWN>(L->down, false);
+        if (rc == CPG_OK) rc = plan_kernel<CPG_ENC_Q4, KIND_GATEUP>(L->gateup_deep, true);
+        if (rc == CPG_OK) rc = plan_kernel<CPG_ENC_Q4, KIND_DOWN>(L->down_deep, true);
     } else {
-        rc = plan_kernel<CPG_ENC_Q8, KIND_GATEUP>(L->gateup);
-        if (rc == CPG_OK) rc = plan_kernel<CPG_ENC_Q8, KIND_DOWN>(L->down);
+        rc = plan_kernel<CPG_ENC_Q8, KIND_GATEUP>(L->gateup, false);
+        if (rc == CPG_OK) rc = plan_kernel<CPG_ENC_Q8, KIND_DOWN>(L->down, false);
+        if (rc == CPG_OK) rc = plan_kernel<CPG_ENC_Q8, KIND_GATEUP>(L->gateup_deep, true);
+        if (rc == CPG_OK) rc = plan_kernel<CPG_ENC_Q8, KIND_DOWN>(L->down_deep, true);
     }
     if (rc == CPG_OK) {
         // decode tensor maps: every expert matrix of the layer, 256-value K slices
