@@ -127,11 +127,41 @@ __global__ void k_iota(int *v, int n) {
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) v[i] = i;
 }
 
-// One warp per (token, head) of q (heads 0..H-1) and k (heads H..H+KV-1): head RMSNorm, then
-// RoPE at position pos0 + t (pos0 read from the device, so a captured step serves every
-// position). q is updated in place; k and v go from their staging rows (T, KV·hd) into the
-// cache at position pos0 + t. Lane l holds elements l, l+32 (first half) and l+64, l+96 (their
-// rotation partners). Products and sums are rounded one at a time, as the reference's ISO C.
+// One warp: head RMSNorm with gain g (head_rmsnorm, qwen3_moe.c:44-49), then RoPE at `pos`
+// (rope_apply_from, kernels.c:425-447), of the 128 values at src into dst (may alias). Lane l
+// holds elements l, l+32 (first half) and l+64, l+96 (their rotation partners). Products and
+// sums are rounded one at a time, as the reference's ISO C.
+__device__ __forceinline__ void head_norm_rope(const float *src, const float *__restrict__ g, float pos, float theta,
+                                               float eps, float *dst) {
+    const int lane = threadIdx.x & 31;
+    float e[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) e[i] = src[lane + 32 * i];
+    float ss = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) ss = fmaf(e[i], e[i], ss);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fdiv_rn(ss, (float)QW_HD) + eps));
+#pragma unroll
+    for (int i = 0; i < 4; ++i) e[i] = __fmul_rn(__fmul_rn(e[i], inv), g[lane + 32 * i]);
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const int fi = lane + 32 * i;                               // frequency index in [0, 64)
+        const float invf = powf(theta, __fdiv_rn(-2.0f * (float)fi, (float)QW_HD));
+        const float ang = __fmul_rn(pos, invf);
+        const float c = cosf(ang), s = sinf(ang);
+        const float a = e[i], b = e[i + 2];
+        e[i] = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
+        e[i + 2] = __fadd_rn(__fmul_rn(b, c), __fmul_rn(a, s));
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) dst[lane + 32 * i] = e[i];
+}
+
+// One warp per (token, head) of q (heads 0..H-1) and k (heads H..H+KV-1): head_norm_rope at
+// position pos0 + t (pos0 read from the device, so a captured step serves every position). q is
+// updated in place; k and v go from their staging rows (T, KV·hd) into the cache at pos0 + t.
 __global__ void __launch_bounds__(256) k_qk_norm_rope(float *__restrict__ q, const float *__restrict__ kst,
                                                        const float *__restrict__ vst, float *__restrict__ kc,
                                                        float *__restrict__ vc, int T, const int *__restrict__ d_pos,
@@ -150,34 +180,11 @@ __global__ void __launch_bounds__(256) k_qk_norm_rope(float *__restrict__ q, con
     const float *src = isq ? q + ((size_t)t * H + h) * QW_HD : kst + krow;
     float *v = isq ? q + ((size_t)t * H + h) * QW_HD : kc + kdst;
     const float *g = isq ? qn : kn;
-    float e[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) e[i] = src[lane + 32 * i];
     if (!isq) {
 #pragma unroll
         for (int i = 0; i < 4; ++i) vc[kdst + lane + 32 * i] = vst[krow + lane + 32 * i];
     }
-    float ss = 0.0f;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) ss = fmaf(e[i], e[i], ss);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fdiv_rn(ss, (float)QW_HD) + eps));
-#pragma unroll
-    for (int i = 0; i < 4; ++i) e[i] = __fmul_rn(__fmul_rn(e[i], inv), g[lane + 32 * i]);
-    const float pos = (float)(pos0 + t);
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-        const int fi = lane + 32 * i;                               // frequency index in [0, 64)
-        const float invf = powf(theta, __fdiv_rn(-2.0f * (float)fi, (float)QW_HD));
-        const float ang = __fmul_rn(pos, invf);
-        const float c = cosf(ang), s = sinf(ang);
-        const float a = e[i], b = e[i + 2];
-        e[i] = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
-        e[i + 2] = __fadd_rn(__fmul_rn(b, c), __fmul_rn(a, s));
-    }
-#pragma unroll
-    for (int i = 0; i < 4; ++i) v[lane + 32 * i] = e[i];
+    head_norm_rope(src, g, (float)(pos0 + t), theta, eps, v);
 }
 
 // Causal GQA attention (qwen3_moe.c:135-155), one block of 256 threads per (query token i,
@@ -411,29 +418,54 @@ __global__ void __launch_bounds__(256) k_attention_prompt(const float *__restric
 //   last     the block that finishes last for (query, head) (a counter per pair, reset by that
 //            block) merges the ranges: M = max m, out = Σ o·e^(m-M) / Σ l·e^(m-M)
 // The range length follows the device position, so a captured step serves every position.
+// With `nr` set (one new token, a decode step), the head norm and RoPE of k_qk_norm_rope happen
+// here: every block normalises its q row, the block whose range holds the new position pos0
+// normalises the new key itself (and takes the new value from the staging row), and of the
+// heads sharing a KV head the first writes both into the cache for the later steps.
+struct AttnNorm {
+    const float *kst, *vst, *qn, *kn;
+    float theta, eps;
+    int on;
+};
 constexpr int AS_SPLIT = 16, AS_THREADS = 256;
-__global__ void __launch_bounds__(AS_THREADS) k_attention_split(const float *__restrict__ q, const float *__restrict__ kc,
-                                                                const float *__restrict__ vc, const int *__restrict__ d_pos,
+__global__ void __launch_bounds__(AS_THREADS) k_attention_split(const float *__restrict__ q, float *__restrict__ kc,
+                                                                float *__restrict__ vc, const int *__restrict__ d_pos,
                                                                 int H, int KV, float *__restrict__ part, int *__restrict__ cnt,
-                                                                float *__restrict__ ao) {
+                                                                float *__restrict__ ao, const AttnNorm nr) {
     pdl_wait();
     pdl_launch_dependents();
     extern __shared__ float s_sc[];                               // the range's scores
     __shared__ float s_red[AS_THREADS / 32];
     __shared__ __align__(16) float s_o[AS_THREADS / 32][QW_HD];
+    __shared__ __align__(16) float s_qk[3][QW_HD];               // normalised q, new k, new v
     __shared__ int s_last;
     const int h = blockIdx.x, b = blockIdx.y, i = blockIdx.z;
     const int kh = h / (H / KV);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int n = *d_pos + i + 1;
+    const int pos0 = *d_pos;
+    const int n = pos0 + i + 1;
     const int chunk = (n + AS_SPLIT - 1) / AS_SPLIT;
     const int j0 = b * chunk, len = max(0, min(n, j0 + chunk) - j0);
     const size_t ks = (size_t)KV * QW_HD;
-    const float4 qv = *reinterpret_cast<const float4 *>(q + ((size_t)i * H + h) * QW_HD + 4 * lane);
+    const bool holds_new = nr.on && pos0 >= j0 && pos0 < j0 + len;   // this range ends at the new key
+    if (nr.on) {
+        if (warp == 0) head_norm_rope(q + (size_t)h * QW_HD, nr.qn, (float)pos0, nr.theta, nr.eps, s_qk[0]);
+        if (holds_new && warp == 1) head_norm_rope(nr.kst + (size_t)kh * QW_HD, nr.kn, (float)pos0, nr.theta, nr.eps, s_qk[1]);
+        if (holds_new && warp == 2)
+            for (int e = lane; e < QW_HD; e += 32) s_qk[2][e] = nr.vst[(size_t)kh * QW_HD + e];
+        __syncthreads();
+        if (holds_new && h % (H / KV) == 0 && tid < 2 * QW_HD) {  // the cache row for later steps
+            float *dst = (tid < QW_HD ? kc : vc) + (size_t)pos0 * ks + (size_t)kh * QW_HD;
+            dst[tid % QW_HD] = s_qk[1 + tid / QW_HD][tid % QW_HD];
+        }
+    }
+    const float4 qv = nr.on ? *reinterpret_cast<const float4 *>(&s_qk[0][4 * lane])
+                            : *reinterpret_cast<const float4 *>(q + ((size_t)i * H + h) * QW_HD + 4 * lane);
     const float scale = __fsqrt_rn((float)QW_HD);
     const float *kb = kc + (size_t)kh * QW_HD + 4 * lane, *vb = vc + (size_t)kh * QW_HD + 4 * lane;
     for (int jj = warp; jj < len; jj += AS_THREADS / 32) {
-        const float4 kv = __ldg(reinterpret_cast<const float4 *>(kb + (size_t)(j0 + jj) * ks));
+        const float4 kv = holds_new && j0 + jj == pos0 ? *reinterpret_cast<const float4 *>(&s_qk[1][4 * lane])
+                                                       : *reinterpret_cast<const float4 *>(kb + (size_t)(j0 + jj) * ks);
         float sv = fmaf(qv.x, kv.x, fmaf(qv.y, kv.y, fmaf(qv.z, kv.z, __fmul_rn(qv.w, kv.w))));
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) sv += __shfl_xor_sync(0xffffffffu, sv, o);
@@ -465,7 +497,8 @@ __global__ void __launch_bounds__(AS_THREADS) k_attention_split(const float *__r
     for (int w = 0; w < AS_THREADS / 32; ++w) sum += s_red[w];
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int jj = warp; jj < len; jj += AS_THREADS / 32) {
-        const float4 v = __ldg(reinterpret_cast<const float4 *>(vb + (size_t)(j0 + jj) * ks));
+        const float4 v = holds_new && j0 + jj == pos0 ? *reinterpret_cast<const float4 *>(&s_qk[2][4 * lane])
+                                                      : *reinterpret_cast<const float4 *>(vb + (size_t)(j0 + jj) * ks);
         const float p = s_sc[jj];
         acc.x = fmaf(p, v.x, acc.x);
         acc.y = fmaf(p, v.y, acc.y);
@@ -802,9 +835,12 @@ static int qwen3_enqueue(cpg_qwen3 *m, int T, cudaStream_t s) {
         }
         if (rc) return rc;
         const int warps = T * (H + KV);
-        CPG_CUDA(launch_pdl(k_qk_norm_rope, dim3((warps + 7) / 8), dim3(256), 0, s, m->q, (const float *)m->kst,
-                            (const float *)m->vst, kc, vc, T, (const int *)m->d_pos, H, KV, A.q_norm, A.k_norm,
-                            m->theta, m->eps));
+        AttnNorm nr{};                                               // T = 1: fused into the attention
+        if (T == 1) nr = AttnNorm{m->kst, m->vst, A.q_norm, A.k_norm, m->theta, m->eps, 1};
+        else
+            CPG_CUDA(launch_pdl(k_qk_norm_rope, dim3((warps + 7) / 8), dim3(256), 0, s, m->q, (const float *)m->kst,
+                                (const float *)m->vst, kc, vc, T, (const int *)m->d_pos, H, KV, A.q_norm, A.k_norm,
+                                m->theta, m->eps));
         const int n_cap = m->pos + T;                                // prompt: positions known here
         if (T >= QW_DENSE_MIN_T && attention_prompt_smem(n_cap) <= m->ap_smem) {
             k_attention_prompt<<<dim3(H, (T + AP_QT - 1) / AP_QT), 256, attention_prompt_smem(n_cap), s>>>(
@@ -813,8 +849,7 @@ static int qwen3_enqueue(cpg_qwen3 *m, int T, cudaStream_t s) {
         } else if (T < QW_DENSE_MIN_T) {
             const size_t ssmem = (size_t)((m->max_ctx + AS_SPLIT - 1) / AS_SPLIT) * sizeof(float);
             CPG_CUDA(launch_pdl(k_attention_split, dim3(H, AS_SPLIT, T), dim3(AS_THREADS), ssmem, s, (const float *)m->q,
-                                (const float *)kc, (const float *)vc, (const int *)m->d_pos, H, KV, m->as_part,
-                                m->as_cnt, m->ao));
+                                kc, vc, (const int *)m->d_pos, H, KV, m->as_part, m->as_cnt, m->ao, nr));
         } else {
             const size_t asmem = (size_t)m->max_ctx * sizeof(float);     // scores of every cached position
             CPG_CUDA(launch_pdl(k_attention, dim3(H, T), dim3(AT_THREADS), asmem, s, (const float *)m->q,
