@@ -1,7 +1,7 @@
 #!/usr/bin/env python3
 """Benchmark: Qwen3-30B-A3B-shaped MoE decode (Q4_0 experts) on B200.
 
-Workload: decode batch of 64 tokens through a stack of 48 distinct
+Workload (benchmark configs[1]): decode batch of 64 tokens through a stack of 48 distinct
 MoE layers (hidden 2048, 128 experts, top-8, intermediate 768, Q4_0 experts, f32 router whose
 rows are scaled so the expert load follows Zipf(1.1)). One step = one batch through all 48
 layers (router, experts, combine, residual), weights resident in HBM.
@@ -323,7 +323,7 @@ def run_ours(args, rank, world, torch, dist):
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "q4_0 x f16 -> f32 (fp16 tensor-core MMA, fp32 accumulate)", "data": "synthetic",
         "config": {"workload": "Qwen3-30B-A3B MoE decode: 64-token batch through 48 stacked MoE layers "
-                               "(BASELINE configs[1], Q4_0 experts, Zipf(1.1)-calibrated f32 router)",
+                               "(configs[1], Q4_0 experts, Zipf(1.1)-calibrated f32 router)",
                    "tokens_per_step_per_gpu": T, "layers": L, "d_model": D, "d_exp": F, "experts": E,
                    "topk": K, "expert_encoding": "Q4_0", "parallelism": f"replicas x{world}",
                    "l2": "inputs larger than L2: each step streams ~13 GB of distinct expert weights"},
@@ -654,7 +654,7 @@ def run_reference(args, rank):
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "q4_0 x f32 (AVX2 FMA)",
         "data": "synthetic",
         "config": {"workload": "Qwen3-30B-A3B MoE decode: 64-token batch through 48 stacked MoE layers "
-                               "(BASELINE configs[1], Q4_0 experts, Zipf(1.1)-calibrated f32 router)",
+                               "(configs[1], Q4_0 experts, Zipf(1.1)-calibrated f32 router)",
                    "tokens_per_step_per_gpu": T, "layers": L, "parallelism": "reference engine, 1 process"},
         "cpu_baseline": {"value": round(tok_s, 3), "unit": "tok/s", "cores": threads, "kind": "reference",
                          "sample": f"{args.cpu_sample_layers} of {L} layers per step, T={T}; "

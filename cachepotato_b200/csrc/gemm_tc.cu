@@ -20,6 +20,9 @@
 //               both write the same stage), then run the epilogue from TMEM:
 //                 gate/up: h = silu(g)·u (engine/blocks/qwen3_moe.c:217-219), fp16 per pair
 //                 down:    y per (token, slot) in fp32, combined in selection order by k_combine
+// Kind 2 (dense) serves the whole model's attention projections on a prompt: one group of all
+// tokens in 128-token tiles, each tile one of three passes (W_hi·x_hi, W_hi·x_lo, W_lo·x_hi, with
+// both operands split exactly into two fp16 terms), each pass writing its own f32 plane.
 // Every mbarrier wait is bounded; a timeout records a status code, all roles leave together, and
 // the copy engines' last transfers are waited for (bounded) before the CTA exits.
 #include <cuda.h>

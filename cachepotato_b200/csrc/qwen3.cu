@@ -1,4 +1,4 @@
-// qwen3.cu — the whole Qwen3-MoE model on the device (SURVEY config 3): the attention half of
+// qwen3.cu — the whole Qwen3-MoE model on the device (the whole-model benchmark): the attention half of
 // qwen3_layer_kv (engine/blocks/qwen3_moe.c:110-167), the MoE half through cpg_moe_forward, and the
 // model loop of cp_chat (engine/api/cachepotato.c:108-166, 315-378): embed_rows, run_layers,
 // apply_head, greedy argmax.
@@ -11,8 +11,11 @@
 //                   gemm_tc.cu, operands split into two fp16 terms each, three passes, which
 //                   keeps the result within f32 rounding of the GEMV's)
 //   k_qk_norm_rope  per-head RMSNorm of q and k (head_rmsnorm, qwen3_moe.c:44-49), then RoPE at
-//                   each token's position (rope_apply_from, kernels.c:425-447)
-//   k_attention     causal GQA: s = q·k / sqrt(hd), softmax, Σ s·v (qwen3_moe.c:135-155)
+//                   each token's position (rope_apply_from, kernels.c:425-447); a one-token step
+//                   does this inside the attention kernel
+//   attention       causal GQA: s = q·k / sqrt(hd), softmax, Σ s·v (qwen3_moe.c:135-155):
+//                   k_attention_split (decode-sized T: position ranges per head, merged),
+//                   k_attention_prompt (prompts: 32 queries per block), k_attention (fallback)
 //   cpg_matvec      attn = Wo·ao
 //   cpg_moe_forward RMSNorm(x + attn, ln2) → router → experts → x += attn + mlp (fused residual)
 // Head: RMSNorm of the last position with final_norm, lm_head GEMV, k_argmax (first maximum wins).

@@ -261,7 +261,7 @@ def reference_available() -> bool:
 
 
 class SynthModel:
-    """A whole Qwen3-MoE model in host memory (SURVEY config 3 shape or smaller): per layer an
+    """A whole Qwen3-MoE model in host memory (the whole-model benchmark shape or smaller): per layer an
     attention half (ln1, Wq/Wk/Wv/Wo in attn_enc, q_norm/k_norm) and a SynthLayer MoE half, plus
     embed and lm_head (head_enc) and the final norm. Norm gains are 1 + norm_jitter·N(0,1)."""
 

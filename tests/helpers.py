@@ -2,7 +2,7 @@
 agreement rule (expert ids identical except where the top-k margin is below 1e-6)."""
 import numpy as np
 
-TOPK_MARGIN = 1e-6     # BASELINE north_star: ids may differ only where the margin is below this
+TOPK_MARGIN = 1e-6     # routing agreement: ids may differ only where the margin is below this
 BLOCK_TOL = 1e-3       # max|d| / max|ref| for block outputs (fp16 tensor-core operands)
 KERNEL_TOL = 1e-5      # fp32 matvec kernels (tools/verify_q8_kernels.py tolerance)
 
