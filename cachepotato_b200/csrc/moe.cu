@@ -360,8 +360,31 @@ __global__ void __launch_bounds__(R_THREADS, 2) k_router(RouterArgs a) {
     }
     __syncthreads();
     // rmsnorm (kernels.c:408-413): inv = 1 / sqrt(sum(x^2)/n + eps); xn = x * inv * g.
-    // One warp per token throughout, so no index division is needed.
-    if (warp < nt) {
+    // One warp per token throughout, so no index division is needed; a lone token (a decode step
+    // of batch 1) is normalised by the whole CTA instead.
+    if (nt == 1) {
+        __shared__ float s_rs[R_THREADS / 32];
+        float ss = 0.0f;
+        for (int k = tid; k < D; k += R_THREADS) ss = fmaf(xs[k], xs[k], ss);
+        ss = warp_sum(ss);
+        if (lane == 0) s_rs[warp] = ss;
+        __syncthreads();
+        float tot = 0.0f;
+#pragma unroll
+        for (int w = 0; w < R_THREADS / 32; ++w) tot += s_rs[w];
+        const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fdiv_rn(tot, (float)D) + a.eps));
+        const float4 *g4 = reinterpret_cast<const float4 *>(a.ln2);
+        float4 *r4 = reinterpret_cast<float4 *>(xs);
+        for (int c = tid; c < D / 4; c += R_THREADS) {
+            const float4 gv = __ldg(g4 + c);
+            float4 v = r4[c];
+            v.x = __fmul_rn(__fmul_rn(v.x, inv), gv.x);
+            v.y = __fmul_rn(__fmul_rn(v.y, inv), gv.y);
+            v.z = __fmul_rn(__fmul_rn(v.z, inv), gv.z);
+            v.w = __fmul_rn(__fmul_rn(v.w, inv), gv.w);
+            r4[c] = v;
+        }
+    } else if (warp < nt) {
         float *row = xs + warp * D;
         float ss = 0.0f;
         for (int k = lane; k < D; k += 32) ss = fmaf(row[k], row[k], ss);
