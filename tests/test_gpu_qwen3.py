@@ -66,6 +66,22 @@ def test_qwen3_shape_prompt_on_tensor_cores(orc, ref):
     assert max_rel(got_logits, want_logits) <= BLOCK_TOL
 
 
+def test_long_context_attention_fallback(orc, ref):
+    """max_ctx 2048: the prompt attention's score rows no longer fit in shared memory, so a
+    40-token prompt takes the one-query-per-block kernel; decode steps keep the split kernel."""
+    m = O.SynthModel(256, 4, 2, 128, 256, 16, 4, 512, 2, seed=7, norm_jitter=0.1, oracle=orc)
+    prompt = np.random.default_rng(40).integers(0, m.vocab, 40).astype(np.int32)
+    want_ids, want_logits = ref.qwen3_generate(m, prompt, 3)
+    gm = device_model(m, max_ctx=2048)
+    try:
+        got_ids = gm.generate(prompt, 3)
+        got_logits = gm.logits().cpu().numpy()
+    finally:
+        gm.close()
+    assert got_ids.tolist() == want_ids.tolist()
+    assert max_rel(got_logits, want_logits) <= BLOCK_TOL
+
+
 def test_step_matches_generate(orc):
     m = O.SynthModel(256, 4, 2, 128, 256, 16, 4, 512, 2, seed=6, oracle=orc)
     prompt = np.array([5, 100, 7], np.int32)
