@@ -301,7 +301,12 @@ static int gemv_launch(const GemvArgs &ga, cudaStream_t s) {
     CPG_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     int ntiles = 0;
     for (int i = 0; i < a.nseg; ++i) ntiles += (a.seg[i].n_out + GV_ROWS - 1) / GV_ROWS;
-    const int grid = ntiles < sm_count() ? ntiles : sm_count();
+    // as many CTAs as fit (two per SM for the attention projections' 18 KB tiles): more tiles in
+    // flight and fewer tiles per CTA, which is what bounds a small matrix
+    int per_sm = 1;
+    CPG_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, (GV_CONS + 1) * 32, smem));
+    if (per_sm < 1) per_sm = 1;
+    const int grid = ntiles < per_sm * sm_count() ? ntiles : per_sm * sm_count();
     CPG_CUDA(launch_pdl(k, dim3(grid), dim3((GV_CONS + 1) * 32), smem, s, a));
     return CPG_OK;
 }
