@@ -30,7 +30,7 @@
 namespace cpg {
 
 // ------------------------------------------------------------------ constants and layouts
-constexpr int R_TB = 8;          // router: tokens per CTA (one warp per token)
+constexpr int R_TB = 8;          // router: tokens per CTA (one warp per token); 1-2 for tiny batches
 constexpr int R_THREADS = 256;
 constexpr int MAX_E = 256;
 constexpr int MAX_K = 32;
@@ -176,11 +176,11 @@ __device__ __forceinline__ int warp_incl_scan(int v) {
 __device__ void group_pairs(const RouterArgs &a) {
     __shared__ int s_cnt[MAX_E], s_off[MAX_E], s_base[MAX_E], s_uidx[MAX_E], s_chp[MAX_E];
     __shared__ uint32_t s_mask[MAX_E];
-    __shared__ int s_tk[R_TB * 8 * MAX_K];
+    __shared__ int s_tk[8 * 8 * MAX_K];
     __shared__ int s_tot[3];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int TK = a.T * a.K;
-    const bool staged = TK <= R_TB * 8 * MAX_K;
+    const bool staged = TK <= 8 * 8 * MAX_K;
     for (int e = tid; e < a.E; e += blockDim.x) { s_cnt[e] = 0; s_base[e] = 0; }
     if (staged)
         for (int i = tid; i < TK; i += blockDim.x) s_tk[i] = __ldcg(a.topk + i);
@@ -300,12 +300,15 @@ __device__ int group_cta(const int *topk, int T, int K, int E, int4 *s_act, int 
     return *s_u;
 }
 
+// TB tokens per CTA: 8, or the batch itself for one or two tokens (a tile of 8 costs a lone token
+// the larger staging and the unrolled token loops).
+template <int TB>
 __global__ void __launch_bounds__(R_THREADS, 2) k_router(RouterArgs a) {
-    extern __shared__ float xs[];                         // (R_TB, D): hh, then xn
+    extern __shared__ float xs[];                         // (TB, D): hh, then xn
     __shared__ int s_last;
     __shared__ uint8_t s_p2e[64];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int t0 = blockIdx.y * R_TB, nt = min(R_TB, a.T - t0);
+    const int t0 = blockIdx.y * TB, nt = min(TB, a.T - t0);
     if (tid < 64) s_p2e[tid] = perm_of(a.xn_enc).pos_to_elem[tid];
     const int e0 = blockIdx.x * a.eb;
     const int D = a.D;
@@ -431,9 +434,9 @@ __global__ void __launch_bounds__(R_THREADS, 2) k_router(RouterArgs a) {
     for (int el = warp; el < a.eb; el += R_THREADS / 32) {
         const int e = e0 + el;
         if (e >= a.E) break;
-        float acc[R_TB];
+        float acc[TB];
 #pragma unroll
-        for (int t = 0; t < R_TB; ++t) acc[t] = 0.0f;
+        for (int t = 0; t < TB; ++t) acc[t] = 0.0f;
         const float4 *w4 = reinterpret_cast<const float4 *>(a.wgate + (size_t)e * D);
         // the row's loads (16 float4 per lane for D = 2048) are all in flight before the FMAs;
         // per lane the sum still runs over k ascending
@@ -447,7 +450,7 @@ __global__ void __launch_bounds__(R_THREADS, 2) k_router(RouterArgs a) {
                 if (c0 + c < D / 128) {
                     const int k = ((c0 + c) * 32 + lane) * 4;
 #pragma unroll
-                    for (int t = 0; t < R_TB; ++t) {
+                    for (int t = 0; t < TB; ++t) {
                         if (t < nt) {
                             const float4 v = *reinterpret_cast<const float4 *>(xs + t * D + k);
                             acc[t] = fmaf(w[c].x, v.x, acc[t]);
@@ -460,7 +463,7 @@ __global__ void __launch_bounds__(R_THREADS, 2) k_router(RouterArgs a) {
             }
         }
 #pragma unroll
-        for (int t = 0; t < R_TB; ++t) {
+        for (int t = 0; t < TB; ++t) {
             const float v = warp_sum(acc[t]);
             if (lane == 0 && t < nt) a.logits[(size_t)(t0 + t) * a.E + e] = v;
         }
@@ -1101,7 +1104,9 @@ extern "C" int cpg_moe_layer_create(const cpg_moe_desc *d, cpg_moe_layer **out) 
             set_error("d_model=%d too large for the router kernel", L->D);
             rc = CPG_EINVAL;
         } else {
-            rc = allow_max_smem((const void *)k_router);
+            rc = allow_max_smem((const void *)k_router<1>);
+            if (rc == CPG_OK) rc = allow_max_smem((const void *)k_router<2>);
+            if (rc == CPG_OK) rc = allow_max_smem((const void *)k_router<R_TB>);
             if (rc == CPG_OK) rc = router_cluster_check(E, rsmem);
         }
     }
@@ -1127,7 +1132,9 @@ int router_cluster(int E, int *eb) {
 int router_cluster_check(int E, int rsmem) {
     int eb = 0;
     const int csz = router_cluster(E, &eb);
-    CPG_CUDA(cudaFuncSetAttribute(k_router, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+    CPG_CUDA(cudaFuncSetAttribute(k_router<1>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+    CPG_CUDA(cudaFuncSetAttribute(k_router<2>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+    CPG_CUDA(cudaFuncSetAttribute(k_router<R_TB>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(csz, 1);
     cfg.blockDim = dim3(R_THREADS);
@@ -1140,7 +1147,7 @@ int router_cluster_check(int E, int rsmem) {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     int n = 0;
-    CPG_CUDA(cudaOccupancyMaxActiveClusters(&n, k_router, &cfg));
+    CPG_CUDA(cudaOccupancyMaxActiveClusters(&n, k_router<R_TB>, &cfg));
     CPG_REQUIRE(n >= 1, "router kernel: a cluster of %d CTAs does not fit on this device", csz);
     return CPG_OK;
 }
@@ -1202,8 +1209,10 @@ int cpg::moe_forward_impl(const cpg_moe_layer *L, const float *x, const float *a
     // one cluster of at most R_CLUSTER_MAX CTAs per token tile, one expert row per warp when
     // E ≤ 8 · R_CLUSTER_MAX (16 CTAs, 128 per 64 tokens for Qwen3-30B-A3B)
     const int csz = router_cluster(L->E, &ra.eb);
-    const dim3 rgrid(csz, (T + R_TB - 1) / R_TB);
-    CPG_CUDA(launch_pdl_cluster(k_router, rgrid, dim3(R_THREADS), (size_t)R_TB * L->D * sizeof(float), s, csz, ra));
+    const int tb = T <= 2 ? T : R_TB;
+    const dim3 rgrid(csz, (T + tb - 1) / tb);
+    auto *rk = tb == 1 ? k_router<1> : tb == 2 ? k_router<2> : k_router<R_TB>;
+    CPG_CUDA(launch_pdl_cluster(rk, rgrid, dim3(R_THREADS), (size_t)tb * L->D * sizeof(float), s, csz, ra));
     // the gate/up kernel groups small batches itself; its scratch (group_cta) must fit in two
     // stages of the smallest stage ring (Q4 gate/up: 2 × 26,880 bytes)
     const size_t group_scratch = sizeof(int) * (4 * (size_t)L->E + (size_t)L->E * ((T + 31) / 32) + (size_t)T * L->K + 1);
