@@ -700,7 +700,7 @@ __global__ void __launch_bounds__((EX_NP + EX_NW) * 32, 2) k_experts(ExpertArgs 
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
-            mbar_init(&full[s], EX_NP);
+            mbar_init(&full[s], 1 + 32);           // weight producer + the 32 token-row lanes
             mbar_init(&empty[s], EX_NW);
             mbar_init(&mready[s], 1);
         }
@@ -733,34 +733,41 @@ __global__ void __launch_bounds__((EX_NP + EX_NW) * 32, 2) k_experts(ExpertArgs 
     const int *pairs = self_group ? s_pairs : a.pairs;
 
     if (warp == 1) {
-        // ---------------- token-row producer: one thread, the chunk's rows of each K slice
-        if (lane != 0) return;
+        // ---------------- token-row producer: the whole warp, the chunk's rows of each K slice by
+        // 16-byte asynchronous copies (lane l copies bytes [16l, 16l + 16) of every row's slice;
+        // the copies of one warp instruction read 512 contiguous bytes). A bulk copy per row would
+        // queue up to 16 copies per stage behind one issuing thread. Each lane's copies count as
+        // one arrival on the stage's full barrier once they have landed.
         const __half *trow[EX_NCHUNK];
         int cur = -1;
         for (int it = 0;; ++it) {
             const int st = it % S;
             if (!mbar_wait(&mready[st], (uint32_t)(it / S) & 1u)) {
-                atomicCAS(a.status + WS_STATUS, ST_OK, ST_TIMEOUT_FULL);
-                return;
+                if (lane == 0) atomicCAS(a.status + WS_STATUS, ST_OK, ST_TIMEOUT_FULL);
+                break;
             }
             const StageMeta md = meta[st];
             if (md.item < 0) {                                 // sentinel
                 mbar_arrive(&full[st]);
-                return;
+                break;
             }
             if (md.item != cur) {                              // the chunk's token rows (fp16, permuted K)
                 cur = md.item;
-                for (int j = 0; j < md.cnt; ++j) {
-                    const int p = md.off + j;
+#pragma unroll
+                for (int j = 0; j < EX_NCHUNK; ++j) {
+                    const int p = md.off + min(j, md.cnt - 1);
                     trow[j] = KIND == KIND_GATEUP ? a.bsrc + (size_t)(pairs[p] / a.K) * a.D : a.bsrc + (size_t)p * a.F;
                 }
             }
-            mbar_arrive_expect_tx(&full[st], (uint32_t)(md.cnt * EX_KSL * 2));
-            uint8_t *dst = smem + (size_t)st * C::STAGE + C::WBYTES;
-            for (int j = 0; j < md.cnt; ++j)                   // columns past cnt keep stale rows: their
-                bulk_g2s(dst + j * C::BROW,                    // results are never stored
-                         trow[j] + (size_t)md.s * EX_KSL, EX_KSL * 2, &full[st]);
+            uint8_t *dst = smem + (size_t)st * C::STAGE + C::WBYTES + lane * 16;
+#pragma unroll
+            for (int j = 0; j < EX_NCHUNK; ++j)                // columns past cnt keep stale rows: their
+                if (j < md.cnt)                                // results are never stored
+                    cp_async16(dst + j * C::BROW, trow[j] + (size_t)md.s * EX_KSL + lane * 8);
+            cp_async_mbar_arrive(&full[st]);
         }
+        cp_async_wait_all();                                   // nothing in flight when the warp leaves
+        return;
     }
     if (warp == 0) {
         // ---------------- weight producer: one thread, one 2D tensor box per matrix and K slice;
