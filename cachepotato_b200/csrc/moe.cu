@@ -21,6 +21,7 @@
 // MMAs. Tokens are the N dimension (8 per MMA tile), weights are read exactly once per layer.
 #include <math.h>
 
+#include <algorithm>
 #include <mutex>
 #include <vector>
 
@@ -505,7 +506,7 @@ struct ExpertArgs {
     int *status;
     int *item_ctr;               // dynamic work counter (zeroed with the header)
     int stages;
-    const void *maps;            // (E, 3) TMA tensor maps over the expert matrices (256-value K slices)
+    const uint8_t *tiles;        // the layer's expert matrices in the decode tile layout, (E, 3)
 };
 
 // An item is one row block of one active expert for one chunk of its tokens; it streams through
@@ -585,45 +586,31 @@ __device__ __forceinline__ void decode_item(const int4 *act, int U, int tiles, i
 }
 
 
-// Operand fragments of group pair P for the NTL token tiles (32 contiguous bytes per thread).
-template <int NTL>
-__device__ __forceinline__ void load_b(const __half *const (&brow)[EX_NCH], int P, uint4 (&b)[EX_NCH][2]) {
-#pragma unroll
-    for (int nt = 0; nt < NTL; ++nt) {
-        const uint4 *bp = reinterpret_cast<const uint4 *>(brow[nt] + P * 64);
-        b[nt][0] = __ldg(bp);
-        b[nt][1] = __ldg(bp + 1);
-    }
-}
+// Decode tile layout of one expert matrix (R rows, Kd values), built once per layer: tile (s, rt)
+// covers rows [16rt, 16rt + 16) and values [256s, 256s + 256) and sits at byte (s·R/16 + rt)·TB,
+// TB = 16 rows × 8 groups × group bytes, so the row tiles of one K slice are contiguous (one bulk
+// copy per matrix and stage). Inside a tile, for group pair P and lane l = 4g + t of the warp that
+// consumes it:
+//   Q4: 16 B at (32P + l)·16 = row g's two words for this lane, then row g+8's two words;
+//   Q8: 16 B at (32P + l)·16 = row g's four words; row g+8's at 2048 + (32P + l)·16;
+// then the scales: row g's eight fp16 group scales at DB + 32g, row g+8's at DB + 32g + 16
+// (DB = 2048 for Q4, 4096 for Q8). The words are the raw group bytes (load_pair_words), regrouped
+// so that a lane's share of a pair is one aligned 16-byte load; the bytes per tile are unchanged.
+template <int ENC>
+struct ExTile {
+    static constexpr int GB = ENC == CPG_ENC_Q4 ? 18 : 34;
+    static constexpr int TB = 16 * 8 * GB;                    // bytes per tile
+    static constexpr int DB = ENC == CPG_ENC_Q4 ? 2048 : 4096; // scale block offset
+};
 
-// One group pair (64 K values) of rows g and g+8: decode, then 4 MMAs per token tile and the
-// fp32 group-scale accumulation.
-template <int ENC, int NTL>
-__device__ __forceinline__ void group_pair_mma(const uint32_t *rowg, const uint32_t *rowg8, int P, int t,
-                                               const uint4 (&b)[EX_NCH][2], float (&acc)[EX_NCH][4]) {
-    uint32_t fr[4][4];       // [k16 step][a0..a3]
-    float dj[2], dj1[2];     // scales: group j / j+1, rows g / g+8
-    uint32_t w1, w2, w3, w4;
-    load_pair_words<ENC>(rowg, P, t, w1, w2, w3, w4, dj[0], dj1[0]);
-    if (ENC == CPG_ENC_Q4) {
-        q4_word(w1, fr[0][0], fr[0][2], fr[1][0], fr[1][2]);
-        q4_word(w2, fr[2][0], fr[2][2], fr[3][0], fr[3][2]);
-    } else {
-        q8_word(w1, fr[0][0], fr[0][2]);
-        q8_word(w2, fr[1][0], fr[1][2]);
-        q8_word(w3, fr[2][0], fr[2][2]);
-        q8_word(w4, fr[3][0], fr[3][2]);
-    }
-    load_pair_words<ENC>(rowg8, P, t, w1, w2, w3, w4, dj[1], dj1[1]);
-    if (ENC == CPG_ENC_Q4) {
-        q4_word(w1, fr[0][1], fr[0][3], fr[1][1], fr[1][3]);
-        q4_word(w2, fr[2][1], fr[2][3], fr[3][1], fr[3][3]);
-    } else {
-        q8_word(w1, fr[0][1], fr[0][3]);
-        q8_word(w2, fr[1][1], fr[1][3]);
-        q8_word(w3, fr[2][1], fr[2][3]);
-        q8_word(w4, fr[3][1], fr[3][3]);
-    }
+// One group pair of rows g and g+8 from the fragments: 4 MMAs per token tile and the fp32
+// group-scale accumulation (dg/d8: the pair's two scales of row g / g+8 as one fp16 pair).
+template <int NTL>
+__device__ __forceinline__ void pair_mma(const uint32_t (&fr)[4][4], uint32_t dg, uint32_t d8,
+                                         const uint4 (&b)[EX_NCH][2], float (&acc)[EX_NCH][4]) {
+    const float2 fg = __half22float2(*reinterpret_cast<const __half2 *>(&dg));
+    const float2 f8 = __half22float2(*reinterpret_cast<const __half2 *>(&d8));
+    const float dj[2] = {fg.x, f8.x}, dj1[2] = {fg.y, f8.y};   // group 2P / 2P+1, rows g / g+8
 #pragma unroll
     for (int nt = 0; nt < NTL; ++nt) {
         const float z[4] = {0.0f, 0.0f, 0.0f, 0.0f};
@@ -640,6 +627,28 @@ __device__ __forceinline__ void group_pair_mma(const uint32_t *rowg, const uint3
     }
 }
 
+// Decoded fragments of pair P of a tile for this lane.
+template <int ENC>
+__device__ __forceinline__ void tile_frags(const uint8_t *tp, int P, int lane, uint32_t (&fr)[4][4]) {
+    const uint4 w = *reinterpret_cast<const uint4 *>(tp + (P * 32 + lane) * 16);
+    if (ENC == CPG_ENC_Q4) {
+        q4_word(w.x, fr[0][0], fr[0][2], fr[1][0], fr[1][2]);
+        q4_word(w.y, fr[2][0], fr[2][2], fr[3][0], fr[3][2]);
+        q4_word(w.z, fr[0][1], fr[0][3], fr[1][1], fr[1][3]);
+        q4_word(w.w, fr[2][1], fr[2][3], fr[3][1], fr[3][3]);
+    } else {
+        const uint4 v = *reinterpret_cast<const uint4 *>(tp + 2048 + (P * 32 + lane) * 16);
+        q8_word(w.x, fr[0][0], fr[0][2]);
+        q8_word(w.y, fr[1][0], fr[1][2]);
+        q8_word(w.z, fr[2][0], fr[2][2]);
+        q8_word(w.w, fr[3][0], fr[3][2]);
+        q8_word(v.x, fr[0][1], fr[0][3]);
+        q8_word(v.y, fr[1][1], fr[1][3]);
+        q8_word(v.z, fr[2][1], fr[2][3]);
+        q8_word(v.w, fr[3][1], fr[3][3]);
+    }
+}
+
 // Operand fragments of pair p of the K slice for the NTL token tiles, from the stage's token
 // rows in shared memory (bs[nt] = this thread's row, already offset by t·32 bytes).
 template <int NTL>
@@ -652,26 +661,73 @@ __device__ __forceinline__ void load_b_smem(const uint8_t *const (&bs)[EX_NCH], 
     }
 }
 
-// The four group pairs of one K slice.
+// The four group pairs of one K slice of a tile.
 template <int ENC, int NTL>
-__device__ __forceinline__ void slice_mma(const uint32_t *rowg, const uint32_t *rowg8, const uint8_t *const (&bs)[EX_NCH],
-                                          int t, float (&acc)[EX_NCH][4]) {
+__device__ __forceinline__ void slice_mma(const uint8_t *tp, int lane, const uint8_t *const (&bs)[EX_NCH],
+                                          float (&acc)[EX_NCH][4]) {
+    using X = ExTile<ENC>;
+    const uint2 *sc = reinterpret_cast<const uint2 *>(tp + X::DB + (lane >> 2) * 32);   // scales, 2 pairs a load
     uint4 b0[EX_NCH][2], b1[EX_NCH][2];
+    uint32_t fr[4][4];
     load_b_smem<NTL>(bs, 0, b0);
     load_b_smem<NTL>(bs, 1, b1);
-    group_pair_mma<ENC, NTL>(rowg, rowg8, 0, t, b0, acc);
+    uint2 sg = sc[0], s8 = sc[2];
+    tile_frags<ENC>(tp, 0, lane, fr);
+    pair_mma<NTL>(fr, sg.x, s8.x, b0, acc);
     load_b_smem<NTL>(bs, 2, b0);
-    group_pair_mma<ENC, NTL>(rowg, rowg8, 1, t, b1, acc);
+    tile_frags<ENC>(tp, 1, lane, fr);
+    pair_mma<NTL>(fr, sg.y, s8.y, b1, acc);
     load_b_smem<NTL>(bs, 3, b1);
-    group_pair_mma<ENC, NTL>(rowg, rowg8, 2, t, b0, acc);
-    group_pair_mma<ENC, NTL>(rowg, rowg8, 3, t, b1, acc);
+    sg = sc[1];
+    s8 = sc[3];
+    tile_frags<ENC>(tp, 2, lane, fr);
+    pair_mma<NTL>(fr, sg.x, s8.x, b0, acc);
+    tile_frags<ENC>(tp, 3, lane, fr);
+    pair_mma<NTL>(fr, sg.y, s8.y, b1, acc);
 }
 
-__device__ __forceinline__ void tma_load_2d_map(void *dst, const void *map, int x, int y, uint64_t *bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
-        ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
-        : "memory");
+// Builds the decode tiles of every expert matrix of a layer from the raw Q4_0/Q8_0 rows: one
+// thread per (matrix, tile, lane). mats: device table (E·3) of matrix pointers, [3e + kind].
+template <int ENC>
+__global__ void k_tile_experts(const uint8_t *const *mats, uint8_t *out, int E, int D, int F) {
+    using X = ExTile<ENC>;
+    const size_t MB = (size_t)F * D / 32 * X::GB;             // bytes per matrix, every kind
+    const int ntile = (F / 16) * (D / EX_KSL);                 // tiles per matrix, every kind
+    const long n = (long)E * 3 * ntile * 32;
+    for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
+        const int lane = (int)(i & 31);
+        const long q = i >> 5;
+        const int tile = (int)(q % ntile), mat = (int)(q / ntile);
+        const bool down = mat % 3 == 2;
+        const int RT = (down ? D : F) / 16;
+        const int s = tile / RT, rt = tile - s * RT;
+        const size_t rowb = (size_t)(down ? F : D) / 32 * X::GB;
+        const uint8_t *src = mats[mat] + (size_t)rt * 16 * rowb + (size_t)s * 8 * X::GB;
+        uint8_t *dst = out + (size_t)mat * MB + (size_t)tile * X::TB;
+        const int g = lane >> 2, t = lane & 3;
+        const uint32_t *rg = reinterpret_cast<const uint32_t *>(src + g * rowb);
+        const uint32_t *r8 = reinterpret_cast<const uint32_t *>(src + (g + 8) * rowb);
+        for (int P = 0; P < 4; ++P) {
+            uint32_t a1, a2, a3, a4, b1, b2, b3, b4;
+            float d0, d1;
+            load_pair_words<ENC>(rg, P, t, a1, a2, a3, a4, d0, d1);
+            load_pair_words<ENC>(r8, P, t, b1, b2, b3, b4, d0, d1);
+            if (ENC == CPG_ENC_Q4) {
+                *reinterpret_cast<uint4 *>(dst + (P * 32 + lane) * 16) = make_uint4(a1, a2, b1, b2);
+            } else {
+                *reinterpret_cast<uint4 *>(dst + (P * 32 + lane) * 16) = make_uint4(a1, a2, a3, a4);
+                *reinterpret_cast<uint4 *>(dst + 2048 + (P * 32 + lane) * 16) = make_uint4(b1, b2, b3, b4);
+            }
+        }
+        if (t < 2) {                                           // lane t = 0: row g, t = 1: row g + 8
+            const uint8_t *row = src + (g + 8 * t) * rowb;
+            uint32_t w[4];
+            for (int j = 0; j < 4; ++j)
+                w[j] = (uint32_t)*reinterpret_cast<const uint16_t *>(row + 2 * j * X::GB) |
+                       ((uint32_t)*reinterpret_cast<const uint16_t *>(row + (2 * j + 1) * X::GB) << 16);
+            *reinterpret_cast<uint4 *>(dst + X::DB + g * 32 + t * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+    }
 }
 
 template <int ENC, int KIND>
@@ -770,12 +826,12 @@ __global__ void __launch_bounds__((EX_NP + EX_NW) * 32, 2) k_experts(ExpertArgs 
         return;
     }
     if (warp == 0) {
-        // ---------------- weight producer: one thread, one 2D tensor box per matrix and K slice;
+        // ---------------- weight producer: one thread, one bulk copy per matrix and K slice;
         // it deals the items and publishes each stage's metadata to the token-row producer
         if (lane != 0) return;
-        const uint8_t *maps = reinterpret_cast<const uint8_t *>(a.maps);
-        constexpr int MAPB = 128;                              // sizeof(CUtensorMap)
-        constexpr int XSTEP = ENC == CPG_ENC_Q4 ? C::SLB : C::SLB / 2;   // box x step in elements
+        using X = ExTile<ENC>;
+        const size_t MB = (size_t)a.D * a.F / 32 * X::GB;     // bytes per matrix
+        constexpr int TPI = C::RB / 16;                        // row tiles per matrix and item
         int it = 0;
         bool ok = true, done = false;
         while (!done) {
@@ -804,12 +860,14 @@ __global__ void __launch_bounds__((EX_NP + EX_NW) * 32, 2) k_experts(ExpertArgs 
                 mbar_arrive(&mready[st]);                      // release: the metadata is visible
                 mbar_arrive_expect_tx(&full[st], (uint32_t)C::WBYTES);
                 uint8_t *dst = smem + (size_t)st * C::STAGE;
-                const int e = ex.x;
+                // the item's row tiles of K slice sl: contiguous in the tile layout
+                const size_t toff = ((size_t)sl * (n_rows / 16) + (size_t)m * TPI) * X::TB;
+                const uint8_t *tm = a.tiles + (size_t)(3 * ex.x) * MB + toff;
                 if (KIND == KIND_GATEUP) {
-                    tma_load_2d_map(dst, maps + (size_t)(3 * e + 0) * MAPB, sl * XSTEP, m * C::RB, &full[st]);
-                    tma_load_2d_map(dst + C::RB * C::SLB, maps + (size_t)(3 * e + 1) * MAPB, sl * XSTEP, m * C::RB, &full[st]);
+                    bulk_g2s(dst, tm, TPI * X::TB, &full[st]);
+                    bulk_g2s(dst + TPI * X::TB, tm + MB, TPI * X::TB, &full[st]);
                 } else {
-                    tma_load_2d_map(dst, maps + (size_t)(3 * e + 2) * MAPB, sl * XSTEP, m * C::RB, &full[st]);
+                    bulk_g2s(dst, tm + 2 * MB, TPI * X::TB, &full[st]);
                 }
             }
             if (!ok) break;
@@ -848,12 +906,9 @@ __global__ void __launch_bounds__((EX_NP + EX_NW) * 32, 2) k_experts(ExpertArgs 
 #pragma unroll
         for (int nt = 0; nt < EX_NCH; ++nt)
             bs[nt] = smem + (size_t)st * C::STAGE + C::WBYTES + (nt * 8 + g) * C::BROW + t * 32;
-        const uint32_t *rows = reinterpret_cast<const uint32_t *>(smem + (size_t)st * C::STAGE +
-                                                                   (size_t)(mat * C::RB + tile * 16) * C::SLB);
-        const uint32_t *rowg = rows + (g * C::SLB) / 4;
-        const uint32_t *rowg8 = rows + ((g + 8) * C::SLB) / 4;
-        if (two) slice_mma<ENC, 2>(rowg, rowg8, bs, t, acc);
-        else slice_mma<ENC, 1>(rowg, rowg8, bs, t, acc);
+        const uint8_t *tp = smem + (size_t)st * C::STAGE + (size_t)(mat * (C::RB / 16) + tile) * ExTile<ENC>::TB;
+        if (two) slice_mma<ENC, 2>(tp, lane, bs, acc);
+        else slice_mma<ENC, 1>(tp, lane, bs, acc);
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[st]);           // this warp is done with the stage
         if (md.s != NS - 1) continue;
@@ -965,8 +1020,8 @@ struct cpg_moe_layer {
     std::vector<const uint8_t *> h_ptrs;   // host copy of the same table
     void *d_wmaps = nullptr;       // device (E, 3) TMA tensor maps of the expert matrices, built
                                    // on the first tcgen05 call (cpg_moe_apply)
-    void *d_dmaps = nullptr;       // device (E, 3) maps for the decode expert kernels (K slices of
-                                   // 256 values, 64-row gate/up and 128-row down boxes), built here
+    uint8_t *d_tiles = nullptr;    // device copy of the expert matrices in the decode tile layout
+                                   // (k_tile_experts), built here
     std::mutex wmaps_mu;
     cpg::KernelPlan gateup, down;            // two CTAs per SM, ~100 KB of stages each
     cpg::KernelPlan gateup_deep, down_deep;  // one CTA per SM with all the shared memory in stages:
@@ -1010,7 +1065,7 @@ static int launch_experts(const cpg_moe_layer *L, int KIND, const ExpertArgs &a,
     const int grid = max_items < p.ctas ? (max_items > 0 ? max_items : 1) : p.ctas;
     ExpertArgs b = a;
     b.stages = p.stages;
-    b.maps = L->d_dmaps;
+    b.tiles = L->d_tiles;
     const dim3 block((EX_NP + EX_NW) * 32);
     auto *k = L->enc == CPG_ENC_Q4 ? (KIND == KIND_GATEUP ? k_experts<CPG_ENC_Q4, KIND_GATEUP> : k_experts<CPG_ENC_Q4, KIND_DOWN>)
                                    : (KIND == KIND_GATEUP ? k_experts<CPG_ENC_Q8, KIND_GATEUP> : k_experts<CPG_ENC_Q8, KIND_DOWN>);
@@ -1033,8 +1088,6 @@ int layer_ptrs(const cpg_moe_layer *L, const uint8_t *const **ptrs, int *enc) {
     return CPG_OK;
 }
 int gemm_tc_build_weight_maps(const uint8_t *const *h_ptrs, int E, int D, int F, void **d_maps);
-int build_row_maps(const uint8_t *const *h_ptrs, int E, int D, int F, int wenc, int rows_gu, int rows_dn,
-                   void **d_maps);
 int layer_weight_maps(const cpg_moe_layer *Lc, const void **maps) {
     CPG_REQUIRE(Lc, "null layer");
     cpg_moe_layer *L = const_cast<cpg_moe_layer *>(Lc);
@@ -1052,6 +1105,24 @@ using namespace cpg;
 
 namespace cpg {
 int router_cluster(int E, int *eb);
+
+// The decode kernels' copy of the layer's expert matrices (k_tile_experts), made from the
+// matrices as they are now: the caller's weights must hold their final values.
+static int build_tiles(cpg_moe_layer *L) {
+    const size_t gb = L->enc == CPG_ENC_Q4 ? 18 : 34;
+    const size_t bytes = (size_t)3 * L->E * L->F * L->D / 32 * gb;
+    CPG_CUDA(cudaDeviceSynchronize());              // the weights' writers, on any stream
+    CPG_CUDA(cudaMalloc((void **)&L->d_tiles, bytes));
+    const long threads = (long)L->E * 3 * (L->F / 16) * (L->D / EX_KSL) * 32;
+    const int grid = (int)std::min<long>((threads + 255) / 256, (long)sm_count() * 8);
+    if (L->enc == CPG_ENC_Q4)
+        k_tile_experts<CPG_ENC_Q4><<<grid, 256>>>(L->d_ptrs, L->d_tiles, L->E, L->D, L->F);
+    else
+        k_tile_experts<CPG_ENC_Q8><<<grid, 256>>>(L->d_ptrs, L->d_tiles, L->E, L->D, L->F);
+    CPG_CUDA(cudaGetLastError());
+    CPG_CUDA(cudaDeviceSynchronize());
+    return CPG_OK;
+}
 int router_cluster_check(int E, int rsmem);
 }  // namespace cpg
 
@@ -1101,10 +1172,7 @@ extern "C" int cpg_moe_layer_create(const cpg_moe_desc *d, cpg_moe_layer **out) 
         if (rc == CPG_OK) rc = plan_kernel<CPG_ENC_Q8, KIND_GATEUP>(L->gateup_deep, true);
         if (rc == CPG_OK) rc = plan_kernel<CPG_ENC_Q8, KIND_DOWN>(L->down_deep, true);
     }
-    if (rc == CPG_OK) {
-        // decode tensor maps: every expert matrix of the layer, 256-value K slices
-        rc = build_row_maps(L->h_ptrs.data(), E, L->D, L->F, enc, 64, 128, &L->d_dmaps);
-    }
+    if (rc == CPG_OK) rc = build_tiles(L);
     if (rc == CPG_OK) {
         const int rsmem = R_TB * L->D * (int)sizeof(float);
         if (rsmem > smem_optin() - 8 * 1024) {
@@ -1119,7 +1187,7 @@ extern "C" int cpg_moe_layer_create(const cpg_moe_desc *d, cpg_moe_layer **out) 
     }
     if (rc != CPG_OK) {
         cudaFree(L->d_ptrs);
-        if (L->d_dmaps) cudaFree(L->d_dmaps);
+        if (L->d_tiles) cudaFree(L->d_tiles);
         delete L;
         return rc;
     }
@@ -1163,7 +1231,7 @@ int router_cluster_check(int E, int rsmem) {
 extern "C" void cpg_moe_layer_destroy(cpg_moe_layer *L) {
     if (!L) return;
     cudaFree(L->d_ptrs);
-    if (L->d_dmaps) cudaFree(L->d_dmaps);
+    if (L->d_tiles) cudaFree(L->d_tiles);
     if (L->d_wmaps) cudaFree(L->d_wmaps);
     delete L;
 }

@@ -109,7 +109,11 @@ typedef struct {
 
 typedef struct cpg_moe_layer cpg_moe_layer;
 
-/* Validate a layer and upload its expert table (qwen3_bind_layer, qwen3_moe.c:462-586). */
+/* Validate a layer and upload its expert table (qwen3_bind_layer, qwen3_moe.c:462-586).
+ * Also builds the small-batch expert kernels' copy of the expert matrices, regrouped into
+ * 16-row x 256-value tiles (same bytes per matrix, device memory owned by the layer): the
+ * matrices must hold their final values when the layer is created, as the reference's
+ * mapped model file does. Synchronises the device. */
 int cpg_moe_layer_create(const cpg_moe_desc *desc, cpg_moe_layer **out);
 void cpg_moe_layer_destroy(cpg_moe_layer *layer);
 /* Scratch bytes one forward of up to max_T tokens needs (the caller allocates it). */
