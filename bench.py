@@ -9,8 +9,9 @@ layers (router, experts, combine, residual), weights resident in HBM.
   value   tok/s with activations already on the device (CUDA graph of the 48 layers)
   e2e     tok/s through the host-buffer C entry point cpg_run_moe_layers: each step copies
           the batch from pinned host memory, runs the layers, copies the result back
-  roofline  the gate/up expert kernel (the dominant launch), algorithmic bytes / its measured
-          duration (CUDA events inside the decode graph), against MEASURED_PEAKS.json
+  roofline  the expert kernel (gate/up and down items in one launch, the dominant kernel),
+          algorithmic bytes / its measured duration (CUDA events inside the decode graph),
+          against MEASURED_PEAKS.json
   cpu_baseline  the reference engine (oracle/_ref: the reference's own C sources) on the host
           cores, a bounded sample of the same workload
   decode_q8_batch1  configs[0]: one token through 48 stacked layers with Q8_0 experts (plain
@@ -309,12 +310,13 @@ def run_ours(args, rank, world, torch, dist):
 
     U = [st["distinct_experts"] for st in stats]
     step_bytes = sum(LN_BYTES + ROUTER_BYTES + u * REGION_BYTES + 2 * T * D * 4 for u in U)
-    gateup_bytes = sum(u * 2 * MAT_BYTES + T * D * 2 + T * K * F * 2 for u in U)
+    # expert launch: the active experts' three matrices, xn read, h written and read back, y written
+    expert_bytes = sum(u * 3 * MAT_BYTES + T * D * 2 + 2 * T * K * F * 2 + T * K * D * 4 for u in U)
     ms_step = ms / args.steps
     hbm, kind = peaks()
-    gateup_ms_per_step = phase[1] / args.steps
+    expert_ms_per_step = (phase[1] + phase[2]) / args.steps
     b1_bytes = L * (LN_BYTES + ROUTER_BYTES + K * REGION_BYTES + 2 * D * 4)
-    achieved = gateup_bytes / (gateup_ms_per_step * 1e-3) / 1e9
+    achieved = expert_bytes / (expert_ms_per_step * 1e-3) / 1e9
     tok_s = world * T * args.steps / (ms * 1e-3)
     e2e_tok_s = world * T * args.steps / (ms_e2e * 1e-3)
     res = {
@@ -330,12 +332,14 @@ def run_ours(args, rank, world, torch, dist):
         "moe_layer_hbm_gbs": round(step_bytes / (ms_step * 1e-3) / 1e9, 1),
         "routing": {"distinct_experts_per_layer_mean": round(float(np.mean(U)), 1),
                     "max_expert_load_mean": round(float(np.mean([st["max_load"] for st in stats])), 1)},
-        "phase_ms_per_step": {"router": round(phase[0] / args.steps, 4), "gate_up": round(phase[1] / args.steps, 4),
-                              "down": round(phase[2] / args.steps, 4), "combine": round(phase[3] / args.steps, 4)},
-        "roofline": {"bound": "hbm", "kernel": "k_experts<Q4,GATEUP>", "achieved": round(achieved, 1),
+        "phase_ms_per_step": {"router": round(phase[0] / args.steps, 4),
+                              "experts": round((phase[1] + phase[2]) / args.steps, 4),
+                              "combine": round(phase[3] / args.steps, 4)},
+        "roofline": {"bound": "hbm", "kernel": "k_experts<Q4,BOTH> (gate/up then down items, one launch)",
+                     "achieved": round(achieved, 1),
                      "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),
                      "peak_kind": kind,
-                     "algorithmic_bytes_per_launch": int(gateup_bytes / L), "traffic": None},
+                     "algorithmic_bytes_per_launch": int(expert_bytes / L), "traffic": None},
         "e2e": {"value": round(e2e_tok_s, 1), "unit": "tok/s", "h2d_bytes_per_step": xbytes,
                 "d2h_bytes_per_step": xbytes},
         "decode_batch1": {"value": round(world * args.steps / (ms_b1 * 1e-3), 1), "unit": "tok/s",

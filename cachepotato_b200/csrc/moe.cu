@@ -38,6 +38,7 @@ constexpr int MAX_K = 32;
 
 constexpr int KIND_GATEUP = 0;
 constexpr int KIND_DOWN = 1;
+constexpr int KIND_BOTH = 2;     // gate/up then down items in one launch
 constexpr int EX_NW = 8;         // consumer warps per CTA
 constexpr int EX_NP = 2;         // producer warps: weight boxes, token rows (one issuing warp's
                                  // copies are served one after another on B200)
@@ -50,8 +51,14 @@ constexpr int R_CLUSTER_MAX = 16;        // router CTAs per token tile (one clus
 enum { WS_STATUS = 0, WS_ITEMS_GATEUP = 2, WS_ITEMS_DOWN = 3, WS_HDR_INTS = 16 };
 
 struct WsLayout {
-    size_t zero_row, n_active, act, pairs, topk, wt, logits, xn, h, y, total;
+    size_t zero_row, n_active, act, pairs, topk, wt, logits, xn, h, y, dep, total;
 };
+
+// Token chunks of a batch: at most one partial chunk per active expert plus the full ones.
+static int max_token_chunks(int E, int K, int T) {
+    const int max_active = T * K < E ? T * K : E;
+    return max_active + T * K / EX_NCHUNK;
+}
 
 static size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
@@ -71,6 +78,7 @@ static WsLayout ws_layout(int D, int F, int E, int K, int T) {
     L.xn = o; o = align_up(o + sizeof(__half) * (size_t)T * D, 256);
     L.h = o; o = align_up(o + sizeof(__half) * (size_t)T * K * F, 256);
     L.y = o; o = align_up(o + sizeof(float) * (size_t)T * K * D, 256);
+    L.dep = o; o = align_up(o + sizeof(int) * (size_t)max_token_chunks(E, K, T), 256);
     L.total = o;
     return L;
 }
@@ -94,6 +102,8 @@ struct RouterArgs {
     __half *zero_row;
     int *n_active, *pairs;
     int4 *act;                   // active experts ascending: (e, pair offset, tokens, token chunks before)
+    int *dep;                    // per token chunk counters of the one-launch expert kernel
+    int n_dep;
 };
 
 __device__ __forceinline__ float warp_sum(float v) {
@@ -326,6 +336,7 @@ __global__ void __launch_bounds__(R_THREADS, 2) k_router(RouterArgs a) {
     if (blockIdx.x == 0 && blockIdx.y == 0) {
         // per-forward state: status word and counters, the padding operand row
         if (tid < WS_HDR_INTS) a.status[tid] = 0;
+        for (int i = tid; i < a.n_dep; i += R_THREADS) a.dep[i] = 0;
         for (int i = tid; i < (D > a.F ? D : a.F) / 2; i += R_THREADS)
             reinterpret_cast<uint32_t *>(a.zero_row)[i] = 0u;
     }
@@ -505,6 +516,7 @@ struct ExpertArgs {
     const __half *zero_row;      // operand row for padded token columns (zeroed with the header)
     int *status;
     int *item_ctr;               // dynamic work counter (zeroed with the header)
+    int *dep;                    // KIND_BOTH: per token chunk, gate/up items whose h is stored (zeroed by the router)
     int stages;
     const uint8_t *tiles;        // the layer's expert matrices in the decode tile layout, (E, 3)
 };
@@ -526,7 +538,8 @@ struct ExCfg {
     static constexpr int WPAIR = GB / 2;                       // 32-bit words per group pair
 };
 
-struct StageMeta { int item, m, off, cnt, s, pad; };   // off/cnt: the item's token chunk; s: K slice
+struct StageMeta { int item, m, off, cnt, s, kind, chunk, pad; };   // off/cnt: the item's token chunk; s: K slice;
+                                                                      // chunk: its index over all experts
 
 template <int ENC>
 __device__ __forceinline__ void load_pair_words(const uint32_t *row, int P, int t, uint32_t &w1,
@@ -730,29 +743,51 @@ __global__ void k_tile_experts(const uint8_t *const *mats, uint8_t *out, int E, 
     }
 }
 
+// Bounded wait until *p >= need (gpu-scope acquire). Returns false after kWaitLimitNs.
+__device__ __forceinline__ bool wait_count_geq(const int *p, int need) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    if (v >= need) return true;
+    const uint64_t t0 = global_ns();
+    for (uint32_t i = 1;; ++i) {
+        __nanosleep(64);
+        asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+        if (v >= need) return true;
+        if ((i & 63u) == 0 && global_ns() - t0 > kWaitLimitNs) return false;
+    }
+}
+
+// KIND_GATEUP, KIND_DOWN: one matrix kind per launch. KIND_BOTH: one launch for the whole
+// block: the gate/up items first, then the down items, from one work counter. A down item needs
+// the h rows of its token chunk, which the chunk's F/64 gate/up items store: each of those bumps
+// the chunk's counter (release) after its stores, and the down item's token-row warp waits for
+// the count (acquire, bounded) before copying the rows. Items are claimed in order, so a down
+// item only ever waits for gate/up items that running CTAs have already claimed: no CTA needs
+// another to become resident, and the down items fill the SMs the gate/up tail leaves idle.
 template <int ENC, int KIND>
 __global__ void __launch_bounds__((EX_NP + EX_NW) * 32, 2) k_experts(ExpertArgs a) {
     using C = ExCfg<ENC, KIND>;
+    using X = ExTile<ENC>;
+    constexpr bool HAS_GU = KIND != KIND_DOWN, HAS_DN = KIND != KIND_GATEUP;
     // Dynamic shared memory starts after the static arrays, 16-byte aligned only; the stages
-    // (2D tensor TMA destinations) need 128 bytes, so the base moves up (the launch adds the
-    // slack). Layout: stages | gate-sum exchange | barriers | stage metadata.
+    // (bulk copy destinations) are placed on 128 bytes (the launch adds the slack).
+    // Layout: stages | gate-sum exchange | barriers | stage metadata.
     extern __shared__ __align__(16) uint8_t smem_raw[];
     uint8_t *const smem = smem_raw + ((128u - (smem_u32(smem_raw) & 127u)) & 127u);
     __shared__ Perm64 s_perm;
     __shared__ int s_abort;
     __shared__ int4 s_act[MAX_E + 1];
-    __shared__ int s_pairs[KIND == KIND_GATEUP ? EX_GROUP_MAX : 1];
+    __shared__ int s_pairs[HAS_GU ? EX_GROUP_MAX : 1];
     const int S = a.stages;
-    const int K_in = KIND == KIND_GATEUP ? a.D : a.F;
-    const int n_rows = KIND == KIND_GATEUP ? a.F : a.D;
-    const int NS = K_in / EX_KSL;                              // K slices per item
+    const int tiles_gu = a.F / 64, tiles_dn = a.D / 128;     // row blocks per matrix and chunk
+    const int ns_gu = a.D / EX_KSL, ns_dn = a.F / EX_KSL;     // K slices per item
     float *xbuf = reinterpret_cast<float *>(smem + (size_t)S * C::STAGE);      // (4 tiles, NCH, 32, 4) gate sums
     uint64_t *full = reinterpret_cast<uint64_t *>(xbuf + 4 * EX_NCH * 128);
     uint64_t *empty = full + S;
     uint64_t *mready = empty + S;                              // stage metadata written
     StageMeta *meta = reinterpret_cast<StageMeta *>(mready + S);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int tiles = n_rows / C::RB;
+    const size_t MB = (size_t)a.D * a.F / 32 * X::GB;          // bytes per expert matrix
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
@@ -770,7 +805,7 @@ __global__ void __launch_bounds__((EX_NP + EX_NW) * 32, 2) k_experts(ExpertArgs 
     }
     pdl_wait();                                  // top-k from k_router / table and h from gate-up
     pdl_launch_dependents();
-    const bool self_group = KIND == KIND_GATEUP && a.topk != nullptr;
+    const bool self_group = HAS_GU && a.topk != nullptr;
     int U;
     if (self_group) {
         // the stage ring is not in use yet: it holds the grouping scratch
@@ -785,7 +820,9 @@ __global__ void __launch_bounds__((EX_NP + EX_NW) * 32, 2) k_experts(ExpertArgs 
         for (int u = threadIdx.x; u <= U; u += blockDim.x) s_act[u] = a.act[u];
         __syncthreads();
     }
-    const int total = tiles * s_act[U].w;
+    const int chunks = s_act[U].w;
+    const int total_gu = HAS_GU ? tiles_gu * chunks : 0;
+    const int total = total_gu + (HAS_DN ? tiles_dn * chunks : 0);
     const int *pairs = self_group ? s_pairs : a.pairs;
 
     if (warp == 1) {
@@ -809,10 +846,17 @@ __global__ void __launch_bounds__((EX_NP + EX_NW) * 32, 2) k_experts(ExpertArgs 
             }
             if (md.item != cur) {                              // the chunk's token rows (fp16, permuted K)
                 cur = md.item;
+                const bool gu = md.kind == KIND_GATEUP;
+                if (KIND == KIND_BOTH && !gu) {                // h of this chunk stored by its gate/up items
+                    if (!wait_count_geq(a.dep + md.chunk, tiles_gu) && lane == 0)
+                        atomicCAS(a.status + WS_STATUS, ST_OK, ST_TIMEOUT_FULL);
+                    __threadfence();
+                }
+                const __half *src = KIND == KIND_BOTH && !gu ? a.h_out : a.bsrc;
 #pragma unroll
                 for (int j = 0; j < EX_NCHUNK; ++j) {
                     const int p = md.off + min(j, md.cnt - 1);
-                    trow[j] = KIND == KIND_GATEUP ? a.bsrc + (size_t)(pairs[p] / a.K) * a.D : a.bsrc + (size_t)p * a.F;
+                    trow[j] = gu ? src + (size_t)(pairs[p] / a.K) * a.D : src + (size_t)p * a.F;
                 }
             }
             uint8_t *dst = smem + (size_t)st * C::STAGE + C::WBYTES + lane * 16;
@@ -829,19 +873,20 @@ __global__ void __launch_bounds__((EX_NP + EX_NW) * 32, 2) k_experts(ExpertArgs 
         // ---------------- weight producer: one thread, one bulk copy per matrix and K slice;
         // it deals the items and publishes each stage's metadata to the token-row producer
         if (lane != 0) return;
-        using X = ExTile<ENC>;
-        const size_t MB = (size_t)a.D * a.F / 32 * X::GB;     // bytes per matrix
-        constexpr int TPI = C::RB / 16;                        // row tiles per matrix and item
         int it = 0;
         bool ok = true, done = false;
         while (!done) {
             const int item = atomicAdd(a.item_ctr, 1);
+            const bool gu = HAS_GU && item < total_gu;
+            const int kind = gu ? KIND_GATEUP : KIND_DOWN;
+            const int li = gu ? item : item - total_gu;
+            const int ns = gu ? ns_gu : ns_dn;
             int u = 0, m = 0, c = 0;
-            if (item < total) decode_item(s_act, U, tiles, item, u, m, c);
+            if (item < total) decode_item(s_act, U, gu ? tiles_gu : tiles_dn, li, u, m, c);
             const int4 ex = s_act[u];
             const int c0 = c * EX_NCHUNK;
             const int cnt = item < total ? min(EX_NCHUNK, ex.z - c0) : 0;
-            for (int sl = 0; sl < (item < total ? NS : 1); ++sl, ++it) {
+            for (int sl = 0; sl < (item < total ? ns : 1); ++sl, ++it) {
                 const int st = it % S;
                 if (it >= S && !mbar_wait(&empty[st], (uint32_t)(it / S - 1) & 1u)) {
                     atomicCAS(a.status + WS_STATUS, ST_OK, ST_TIMEOUT_EMPTY);
@@ -856,18 +901,19 @@ __global__ void __launch_bounds__((EX_NP + EX_NW) * 32, 2) k_experts(ExpertArgs 
                     ++it;
                     break;
                 }
-                meta[st] = StageMeta{item, m, ex.y + c0, cnt, sl, 0};
+                meta[st] = StageMeta{item, m, ex.y + c0, cnt, sl, kind, ex.w + c, 0};
                 mbar_arrive(&mready[st]);                      // release: the metadata is visible
                 mbar_arrive_expect_tx(&full[st], (uint32_t)C::WBYTES);
                 uint8_t *dst = smem + (size_t)st * C::STAGE;
                 // the item's row tiles of K slice sl: contiguous in the tile layout
-                const size_t toff = ((size_t)sl * (n_rows / 16) + (size_t)m * TPI) * X::TB;
-                const uint8_t *tm = a.tiles + (size_t)(3 * ex.x) * MB + toff;
-                if (KIND == KIND_GATEUP) {
-                    bulk_g2s(dst, tm, TPI * X::TB, &full[st]);
-                    bulk_g2s(dst + TPI * X::TB, tm + MB, TPI * X::TB, &full[st]);
+                const uint8_t *te = a.tiles + (size_t)(3 * ex.x) * MB;
+                if (gu) {
+                    const size_t toff = ((size_t)sl * (a.F / 16) + (size_t)m * 4) * X::TB;
+                    bulk_g2s(dst, te + toff, 4 * X::TB, &full[st]);
+                    bulk_g2s(dst + 4 * X::TB, te + MB + toff, 4 * X::TB, &full[st]);
                 } else {
-                    bulk_g2s(dst, tm + 2 * MB, TPI * X::TB, &full[st]);
+                    const size_t toff = ((size_t)sl * (a.D / 16) + (size_t)m * 8) * X::TB;
+                    bulk_g2s(dst, te + 2 * MB + toff, 8 * X::TB, &full[st]);
                 }
             }
             if (!ok) break;
@@ -880,10 +926,9 @@ __global__ void __launch_bounds__((EX_NP + EX_NW) * 32, 2) k_experts(ExpertArgs 
         return;
     }
 
-    // ---------------- consumers: warp cw owns 16 rows of one matrix over the whole K
+    // ---------------- consumers: gate/up items: warp cw owns 16 rows of matrix cw & 1 (tile
+    // cw >> 1 of the item's 64); down items: 16 rows (tile cw of the item's 128); over the whole K
     const int cw = warp - EX_NP;
-    const int mat = KIND == KIND_GATEUP ? (cw & 1) : 0;
-    const int tile = KIND == KIND_GATEUP ? (cw >> 1) : cw;
     const int g = lane >> 2, t = lane & 3;
     float acc[EX_NCH][4];
     bool two = false;
@@ -895,6 +940,7 @@ __global__ void __launch_bounds__((EX_NP + EX_NW) * 32, 2) k_experts(ExpertArgs 
         }
         const StageMeta md = meta[st];
         if (md.item < 0) break;
+        const bool gu = HAS_GU && (!HAS_DN || md.kind == KIND_GATEUP);
         if (md.s == 0) {                                   // a new item
             two = md.cnt > 8;
 #pragma unroll
@@ -906,15 +952,17 @@ __global__ void __launch_bounds__((EX_NP + EX_NW) * 32, 2) k_experts(ExpertArgs 
 #pragma unroll
         for (int nt = 0; nt < EX_NCH; ++nt)
             bs[nt] = smem + (size_t)st * C::STAGE + C::WBYTES + (nt * 8 + g) * C::BROW + t * 32;
-        const uint8_t *tp = smem + (size_t)st * C::STAGE + (size_t)(mat * (C::RB / 16) + tile) * ExTile<ENC>::TB;
+        const int tidx = gu ? (cw & 1) * 4 + (cw >> 1) : cw;
+        const uint8_t *tp = smem + (size_t)st * C::STAGE + (size_t)tidx * X::TB;
         if (two) slice_mma<ENC, 2>(tp, lane, bs, acc);
         else slice_mma<ENC, 1>(tp, lane, bs, acc);
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[st]);           // this warp is done with the stage
-        if (md.s != NS - 1) continue;
+        if (md.s != (gu ? ns_gu : ns_dn) - 1) continue;
         // ---------------- epilogue of the item
         const int ntl = two ? 2 : 1;
-        if (KIND == KIND_GATEUP) {
+        if (gu) {
+            const int mat = cw & 1, tile = cw >> 1;
             float *xb = xbuf + (size_t)tile * EX_NCH * 128;
             if (mat == 0) {
 #pragma unroll
@@ -934,7 +982,7 @@ __global__ void __launch_bounds__((EX_NP + EX_NW) * 32, 2) k_experts(ExpertArgs 
                     for (int c = 0; c < 4; ++c) {
                         const int col = nt * 8 + 2 * t + (c & 1);
                         if (col < md.cnt) {
-                            const int row = md.m * C::RB + tile * 16 + g + 8 * (c >> 1);       // feature in [0, F)
+                            const int row = md.m * 64 + tile * 16 + g + 8 * (c >> 1);         // feature in [0, F)
                             const float silu = gs[c] / (1.0f + expf(-gs[c]));                 // kernels.c:416
                             const float h = silu * acc[nt][c];                                // qwen3_moe.c:219
                             const int pos = (row & ~63) + s_perm.elem_to_pos[row & 63];
@@ -944,6 +992,10 @@ __global__ void __launch_bounds__((EX_NP + EX_NW) * 32, 2) k_experts(ExpertArgs 
                 }
             }
             named_bar_sync(1, EX_NW * 32);                 // the exchange buffer is free again
+            if (KIND == KIND_BOTH && cw == 0 && lane == 0) {
+                __threadfence();                           // the CTA's h stores before the count
+                atomicAdd(a.dep + md.chunk, 1);
+            }
         } else {
 #pragma unroll
             for (int nt = 0; nt < EX_NCH; ++nt) {
@@ -952,8 +1004,8 @@ __global__ void __launch_bounds__((EX_NP + EX_NW) * 32, 2) k_experts(ExpertArgs 
                 for (int c = 0; c < 4; ++c) {
                     const int col = nt * 8 + 2 * t + (c & 1);
                     if (col < md.cnt) {
-                        const int row = md.m * C::RB + tile * 16 + g + 8 * (c >> 1);           // in [0, D)
-                        a.y_out[(size_t)a.pairs[md.off + col] * a.D + row] = acc[nt][c];
+                        const int row = md.m * 128 + cw * 16 + g + 8 * (c >> 1);               // in [0, D)
+                        a.y_out[(size_t)pairs[md.off + col] * a.D + row] = acc[nt][c];
                     }
                 }
             }
@@ -1023,7 +1075,7 @@ struct cpg_moe_layer {
     uint8_t *d_tiles = nullptr;    // device copy of the expert matrices in the decode tile layout
                                    // (k_tile_experts), built here
     std::mutex wmaps_mu;
-    cpg::KernelPlan gateup, down;            // two CTAs per SM, ~100 KB of stages each
+    cpg::KernelPlan gateup, down, both;      // two CTAs per SM, ~100 KB of stages each
     cpg::KernelPlan gateup_deep, down_deep;  // one CTA per SM with all the shared memory in stages:
                                              // for launches with at most one item per SM
 };
@@ -1060,15 +1112,19 @@ static int plan_kernel(KernelPlan &p, bool deep) {
 
 static int launch_experts(const cpg_moe_layer *L, int KIND, const ExpertArgs &a, int max_items, cudaStream_t s) {
     // few items (one token: 8 experts): one CTA per SM with the whole item's slices in flight
-    const bool deep = max_items <= sm_count();
-    const KernelPlan &p = KIND == KIND_GATEUP ? (deep ? L->gateup_deep : L->gateup) : (deep ? L->down_deep : L->down);
+    const bool deep = KIND != KIND_BOTH && max_items <= sm_count();
+    const KernelPlan &p = KIND == KIND_BOTH ? L->both
+                          : KIND == KIND_GATEUP ? (deep ? L->gateup_deep : L->gateup) : (deep ? L->down_deep : L->down);
     const int grid = max_items < p.ctas ? (max_items > 0 ? max_items : 1) : p.ctas;
     ExpertArgs b = a;
     b.stages = p.stages;
     b.tiles = L->d_tiles;
     const dim3 block((EX_NP + EX_NW) * 32);
-    auto *k = L->enc == CPG_ENC_Q4 ? (KIND == KIND_GATEUP ? k_experts<CPG_ENC_Q4, KIND_GATEUP> : k_experts<CPG_ENC_Q4, KIND_DOWN>)
-                                   : (KIND == KIND_GATEUP ? k_experts<CPG_ENC_Q8, KIND_GATEUP> : k_experts<CPG_ENC_Q8, KIND_DOWN>);
+    auto *k = L->enc == CPG_ENC_Q4
+                  ? (KIND == KIND_BOTH ? k_experts<CPG_ENC_Q4, KIND_BOTH>
+                     : KIND == KIND_GATEUP ? k_experts<CPG_ENC_Q4, KIND_GATEUP> : k_experts<CPG_ENC_Q4, KIND_DOWN>)
+                  : (KIND == KIND_BOTH ? k_experts<CPG_ENC_Q8, KIND_BOTH>
+                     : KIND == KIND_GATEUP ? k_experts<CPG_ENC_Q8, KIND_GATEUP> : k_experts<CPG_ENC_Q8, KIND_DOWN>);
     CPG_CUDA(launch_pdl(k, dim3(grid), block, p.smem, s, b));
     return CPG_OK;
 }
@@ -1163,11 +1219,13 @@ extern "C" int cpg_moe_layer_create(const cpg_moe_desc *d, cpg_moe_layer **out) 
     int rc;
     if (enc == CPG_ENC_Q4) {
         rc = plan_kernel<CPG_ENC_Q4, KIND_GATEUP>(L->gateup, false);
+        if (rc == CPG_OK) rc = plan_kernel<CPG_ENC_Q4, KIND_BOTH>(L->both, false);
         if (rc == CPG_OK) rc = plan_kernel<CPG_ENC_Q4, KIND_DOWN>(L->down, false);
         if (rc == CPG_OK) rc = plan_kernel<CPG_ENC_Q4, KIND_GATEUP>(L->gateup_deep, true);
         if (rc == CPG_OK) rc = plan_kernel<CPG_ENC_Q4, KIND_DOWN>(L->down_deep, true);
     } else {
         rc = plan_kernel<CPG_ENC_Q8, KIND_GATEUP>(L->gateup, false);
+        if (rc == CPG_OK) rc = plan_kernel<CPG_ENC_Q8, KIND_BOTH>(L->both, false);
         if (rc == CPG_OK) rc = plan_kernel<CPG_ENC_Q8, KIND_DOWN>(L->down, false);
         if (rc == CPG_OK) rc = plan_kernel<CPG_ENC_Q8, KIND_GATEUP>(L->gateup_deep, true);
         if (rc == CPG_OK) rc = plan_kernel<CPG_ENC_Q8, KIND_DOWN>(L->down_deep, true);
@@ -1281,6 +1339,8 @@ int cpg::moe_forward_impl(const cpg_moe_layer *L, const float *x, const float *a
     ra.n_active = (int *)(w + W.n_active);
     ra.act = (int4 *)(w + W.act);
     ra.pairs = (int *)(w + W.pairs);
+    ra.dep = (int *)(w + W.dep);
+    ra.n_dep = max_token_chunks(L->E, L->K, T);
     // one cluster of at most R_CLUSTER_MAX CTAs per token tile, one expert row per warp when
     // E ≤ 8 · R_CLUSTER_MAX (16 CTAs, 128 per 64 tokens for Qwen3-30B-A3B)
     const int csz = router_cluster(L->E, &ra.eb);
@@ -1299,27 +1359,37 @@ int cpg::moe_forward_impl(const cpg_moe_layer *L, const float *x, const float *a
     ea.n_active = ra.n_active; ea.act = ra.act;
     ea.zero_row = ra.zero_row;
     ea.pairs = ra.pairs; ea.h_enc = L->enc; ea.status = hdr;
-    const int max_active = T * L->K < L->E ? T * L->K : L->E;
-    const int max_chunks = max_active + T * L->K / EX_NCHUNK;
+    const int max_chunks = ra.n_dep;
+    const int gu_items = max_chunks * (L->F / 64), dn_items = max_chunks * (L->D / 128);
 
     ea.bsrc = ra.xn_perm;
     ea.h_out = (__half *)(w + W.h);
+    ea.y_out = (float *)(w + W.y);
+    ea.dep = ra.dep;
     ea.item_ctr = hdr + WS_ITEMS_GATEUP;
     if (self_group) {
         ea.topk = ra.topk; ea.T = T; ea.E = L->E;
         ea.g_n_active = ra.n_active; ea.g_act = ra.act; ea.g_pairs = ra.pairs;
     }
     if (ev) CPG_CUDA(cudaEventRecordWithFlags(ev[1], s, cudaEventRecordExternal));
-    int rc = launch_experts(L, KIND_GATEUP, ea, max_chunks * (L->F / 64), s);
-    if (rc) return rc;
-
-    ea.bsrc = (const __half *)(w + W.h);
-    ea.y_out = (float *)(w + W.y);
-    ea.item_ctr = hdr + WS_ITEMS_DOWN;
-    ea.topk = nullptr;
-    if (ev) CPG_CUDA(cudaEventRecordWithFlags(ev[2], s, cudaEventRecordExternal));
-    rc = launch_experts(L, KIND_DOWN, ea, max_chunks * (L->D / 128), s);
-    if (rc) return rc;
+    int rc;
+    if (gu_items > sm_count()) {
+        // more items than SMs: gate/up and down in one launch (the down items fill the gate/up tail)
+        rc = launch_experts(L, KIND_BOTH, ea, gu_items + dn_items, s);
+        if (rc) return rc;
+        if (ev) CPG_CUDA(cudaEventRecordWithFlags(ev[2], s, cudaEventRecordExternal));
+    } else {
+        // a few items (one token: 8 experts): each kind on one CTA per SM with all its K slices
+        // in flight
+        rc = launch_experts(L, KIND_GATEUP, ea, gu_items, s);
+        if (rc) return rc;
+        ea.bsrc = (const __half *)(w + W.h);
+        ea.item_ctr = hdr + WS_ITEMS_DOWN;
+        ea.topk = nullptr;
+        if (ev) CPG_CUDA(cudaEventRecordWithFlags(ev[2], s, cudaEventRecordExternal));
+        rc = launch_experts(L, KIND_DOWN, ea, dn_items, s);
+        if (rc) return rc;
+    }
 
     const int n4 = T * L->D / 4;
     int cgrid = (n4 + 255) / 256;

@@ -249,7 +249,9 @@ float *cpg_ctx_x(cpg_ctx *ctx);
 int *cpg_ctx_topk(cpg_ctx *ctx);
 /* Phase timing: when enabled, the decode graph records CUDA events around the router,
  * gate/up, down and combine launches of every layer; cpg_ctx_phase_ms sums each phase over
- * the layers of the last run (synchronises the stream). */
+ * the layers of the last run (synchronises the stream). Batches whose gate/up items outnumber
+ * the SMs run gate/up and down in one launch: its time is the gate/up phase and the down
+ * phase is then ~0. */
 int cpg_ctx_profile(cpg_ctx *ctx, int enable);
 int cpg_ctx_phase_ms(cpg_ctx *ctx, float *ms4);
 

@@ -138,4 +138,5 @@ def test_phase_profile(orc, layers):
     xh = orc.normal(T * D, 5, 1.0).reshape(T, D)
     ctx.run([l, l], xh)
     ms = ctx.phase_ms()
-    assert all(m > 0 for m in ms) and ms[1] > ms[3]
+    # T=64: gate/up and down items share one launch (timed as the gate/up phase)
+    assert ms[0] > 0 and ms[1] > 0 and ms[2] >= 0 and ms[3] > 0 and ms[1] > ms[3]
