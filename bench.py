@@ -149,6 +149,17 @@ class DevPtr:
                                          "data": (ptr, False), "version": 2, "strides": None}
 
 
+def moe_launches_per_layer(T: int) -> int:
+    """Kernels one cpg_moe_forward enqueues (moe.cu): the router, k_group when the T*K pairs are
+    too many for the expert kernel to group itself (> 1024), the expert kernel(s) (one launch
+    when the gate/up items (token chunks x d_exp/64) outnumber the SMs, else gate/up and down),
+    and the combine."""
+    import torch
+    chunks = min(T * K, E) + T * K // 16
+    experts = 1 if chunks * (F // 64) > torch.cuda.get_device_properties(0).multi_processor_count else 2
+    return 1 + (1 if T * K > 1024 else 0) + experts + 1
+
+
 def view(torch, ptr, nbytes, dtype="f4"):
     ts = {"f4": "<f4", "u1": "|u1"}[dtype]
     return torch.as_tensor(DevPtr(ptr, nbytes, ts), device="cuda")
@@ -347,7 +358,7 @@ def run_ours(args, rank, world, torch, dist):
                           "hbm_gbs": round(b1_bytes / (ms_b1 / args.steps * 1e-3) / 1e9, 1),
                           "frac": round(b1_bytes / (ms_b1 / args.steps * 1e-3) / 1e9 / hbm, 4),
                           "bytes_per_step": b1_bytes},
-        "gpu_launches": 4 * L * args.steps,
+        "gpu_launches": moe_launches_per_layer(T) * L * args.steps,
         "clocks": clk,
     }
     if q8:
