@@ -1,6 +1,6 @@
 // moe.cu — the Qwen3-MoE block (engine/blocks/qwen3_moe.c:169-223) on B200.
 //
-// Four launches per layer, all enqueued on one stream and free of host syncs:
+// Three or four launches per layer, all enqueued on one stream and free of host syncs:
 //   k_router   RMSNorm(x + attn), f32 router GEMV, softmax over experts, strict-'>' top-k,
 //              renormalisation (qwen3_moe.c:178-197). The CTAs of one token tile form a thread-
 //              block cluster (each holds a slice of the experts); after a cluster barrier, CTA r
@@ -10,12 +10,16 @@
 //              pairs by expert in its own shared memory (CTA 0 publishes the table for the
 //              later kernels); batches over EX_GROUP_MAX pairs are grouped by k_group instead.
 //   k_experts<DOWN>    per (expert, 128-row tile, token chunk): y = Wd·h (qwen3_moe.c:220)
+//   k_experts<BOTH>    the two above in one launch when the gate/up items outnumber the SMs
+//              (every batch of two or more tokens): gate/up items first, then down items, each
+//              down item waiting (bounded) for its token chunk's h
 //   k_combine  mlp += sum_j wt_j·y_j in selection order (qwen3_moe.c:221) and the residual
 //              x + (attn + mlp) of run_layers (engine/api/cachepotato.c:157-159)
 //
-// Expert kernels: two producer warps fill an mbarrier ring of stages. One deals the work items
-// and streams the weight rows from HBM as 2D tensor TMA boxes (one 256-value K slice of the
-// item's rows, no multicast); the other copies the same K slice of the item's token rows. Eight
+// Expert kernels: two producer warps fill an mbarrier ring of stages. One thread deals the work
+// items and streams the weight rows from the layer's decode tile copy (k_tile_experts) by one
+// bulk copy per matrix and stage (one 256-value K slice of the item's rows, no multicast); the
+// other warp copies the same K slice of the item's token rows by 16-byte cp.async. Eight
 // consumer warps decode Q4_0 / Q8_0 groups in registers (exact integers in fp16) and feed
 // mma.m16n8k16 with fp32 accumulators; the group scale is applied in fp32 after each group's
 // MMAs. Tokens are the N dimension (8 per MMA tile), weights are read exactly once per layer.
