@@ -210,6 +210,43 @@ extern "C" int cpg_store_totals(cpg_store_totals_t *out) {
     return CPG_OK;
 }
 
+namespace cpg {
+int crc32_regions(const std::vector<const uint8_t *> &base, const std::vector<unsigned long long> &len,
+                  uint32_t *out, cudaStream_t s);
+}
+
+// The v4 loader's digest check (format/v4_writer.py:235-250 writes zlib.crc32 of each region's
+// bytes as a u64; the loader compares at open): every region's CRC-32 computed in HBM.
+extern "C" int cpg_store_verify(const uint64_t *digests, int n, int *first_bad) {
+    CPG_REQUIRE(digests || n == 0, "cpg_store_verify: null digests");
+    if (first_bad) *first_bad = -1;
+    std::lock_guard<std::mutex> lk(g_store.mu);
+    if (!g_store.dev) {
+        set_error("cpg_store_verify: store not open");
+        return CPG_ESTATE;
+    }
+    CPG_REQUIRE(n == (int)g_store.regions.size(), "cpg_store_verify: %d digests for %zu regions", n,
+                g_store.regions.size());
+    std::vector<const uint8_t *> b(n);
+    std::vector<unsigned long long> l(n);
+    for (int i = 0; i < n; ++i) {
+        b[i] = g_store.dev + g_store.regions[i].off;
+        l[i] = g_store.regions[i].len;
+    }
+    std::vector<uint32_t> crc(n > 0 ? n : 1);
+    const int rc = crc32_regions(b, l, crc.data(), nullptr);
+    if (rc != CPG_OK) return rc;
+    for (int i = 0; i < n; ++i) {
+        if ((uint64_t)crc[i] != digests[i]) {
+            if (first_bad) *first_bad = i;
+            set_error("cpg_store_verify: region %d: CRC-32 %08x, file digest %016llx", i, crc[i],
+                      (unsigned long long)digests[i]);
+            return CPG_EINVAL;
+        }
+    }
+    return CPG_OK;
+}
+
 extern "C" void cpg_store_close(void) {
     std::lock_guard<std::mutex> lk(g_store.mu);
     if (g_store.dev) cudaFree(g_store.dev);

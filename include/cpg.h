@@ -83,6 +83,13 @@ size_t cpg_store_bytes(void);
 typedef struct { long regions, expert_regions; long resident_bytes; long h2d_bytes; } cpg_store_totals_t;
 int cpg_store_totals(cpg_store_totals_t *out);                                         /* pager_totals */
 void cpg_store_close(void);
+/* The loader's region digest check, on the device: region i's CRC-32 (IEEE, zlib.crc32, the
+ * digest format/v4_writer.py:235-250 stores as a u64 in the region table) against digests[i],
+ * for all n regions added (n must equal their count). CPG_OK, or CPG_EINVAL with *first_bad =
+ * the lowest mismatching region id (-1 otherwise; first_bad may be NULL). Synchronous. */
+int cpg_store_verify(const uint64_t *digests, int n, int *first_bad);
+/* CRC-32 (IEEE, zlib.crc32) of n bytes of device memory; synchronous on `stream`. */
+int cpg_crc32(const void *dev, size_t n, uint32_t *out, void *stream);
 
 /* ============================================================== MoE block
  * The MoE half of qwen3_layer_kv (engine/blocks/qwen3_moe.c:169-223) plus the residual add of

@@ -37,6 +37,10 @@ def test_errors_without_a_gpu_are_reported_not_crashes():
     assert "multiple of 32" in _lib.last_error()
     assert L.cpg_store_add_region(0, 16, 1) == _lib.CPG_ESTATE
     assert L.cpg_store_region_get(0) is None
+    assert L.cpg_store_verify(None, 0, None) == _lib.CPG_ESTATE          # no store open
+    out = ctypes.c_uint32(5)
+    assert L.cpg_crc32(None, 0, ctypes.byref(out), None) == 0 and out.value == 0   # zlib.crc32(b"")
+    assert L.cpg_crc32(None, 5, ctypes.byref(out), None) == _lib.CPG_EINVAL
 
 
 def test_router_calibration_is_deterministic_and_skewed():
