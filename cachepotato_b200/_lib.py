@@ -21,7 +21,7 @@ EXPORTS = [
     "cpg_dequant", "cpg_quantize", "cpg_matvec",
     "cpg_store_open_v4", "cpg_store_open", "cpg_store_add_region", "cpg_store_region_get",
     "cpg_store_translate", "cpg_store_base", "cpg_store_bytes", "cpg_store_totals", "cpg_store_close",
-    "cpg_store_verify", "cpg_crc32",
+    "cpg_store_verify", "cpg_crc32", "cpg_route_check",
     "cpg_moe_layer_create", "cpg_moe_layer_destroy", "cpg_moe_workspace_bytes", "cpg_moe_forward",
     "cpg_moe_check", "cpg_moe_forward_noalloc",
     "cpg_ctx_create", "cpg_ctx_destroy", "cpg_ctx_stream", "cpg_run_moe_layers",
@@ -92,6 +92,7 @@ _SIGS = {
     "cpg_store_close": (None, []),
     "cpg_store_verify": (_i, [_vp, _i, ctypes.POINTER(_i)]),
     "cpg_crc32": (_i, [_vp, _sz, ctypes.POINTER(ctypes.c_uint32), _vp]),
+    "cpg_route_check": (_i, [_vp, _vp, _vp, _i, _i, _i, ctypes.POINTER(_i), ctypes.POINTER(ctypes.c_double), _vp]),
     "cpg_moe_layer_create": (_i, [ctypes.POINTER(MoeDesc), ctypes.POINTER(_vp)]),
     "cpg_moe_layer_destroy": (None, [_vp]),
     "cpg_moe_workspace_bytes": (_sz, [_vp, _i]),

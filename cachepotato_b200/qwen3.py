@@ -109,6 +109,23 @@ def qwen3_mm(w, enc: int, x, n_in: int, n_out: int, stream=None):
     return out
 
 
+def route_check(logits, topk, wt, stream=None) -> dict:
+    """Routing agreement under ties on the device (cpg_route_check): the rule of
+    tools/check_qwen3_baseline.py:39-72 for one layer's tokens. logits (T, E), topk (T, K) and
+    wt (T, K) on the device. Returns the invalid-token count, the tie count, the first invalid
+    token (-1 if none) and the two weight errors."""
+    torch = _torch()
+    logits = logits.contiguous().float()
+    topk = topk.contiguous().to(torch.int32)
+    wt = wt.contiguous().float()
+    T, E = logits.shape
+    K = topk.shape[1]
+    stats, errs = (ctypes.c_int * 3)(), (ctypes.c_double * 2)()
+    check(lib().cpg_route_check(logits.data_ptr(), topk.data_ptr(), wt.data_ptr(), T, E, K, stats, errs,
+                                _stream_ptr(stream)))
+    return {"bad": stats[0], "ties": stats[1], "first_bad": stats[2], "sum_err": errs[0], "w_err": errs[1]}
+
+
 @dataclass
 class MoEOutputs:
     mlp: object

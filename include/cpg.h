@@ -116,6 +116,16 @@ typedef struct {
 
 typedef struct cpg_moe_layer cpg_moe_layer;
 
+/* Routing agreement under ties, on the device: the rule of tools/check_qwen3_baseline.py:39-72
+ * (models/qwen3-30b-a3b/MODEL.md section 6). logits (T, E) f32, topk (T, K) int ids, wt (T, K)
+ * f32, all device; E <= 256, K <= 32. p = softmax(logits) in float64, thr = its K-th largest;
+ * a token's ids (as a set) are a valid top-K if every chosen p >= thr - 1e-12 and exactly the
+ * experts with p > thr + 1e-12 are chosen among those above it. Writes stats[3] = {invalid
+ * tokens, valid tokens resolved by a tie, first invalid token or -1} and errs[2] = {max
+ * |sum(w) - 1|, max |w - p[ids] / sum(p[ids])|}. Synchronous on `stream`. */
+int cpg_route_check(const float *logits, const int *topk, const float *wt, int T, int E, int K,
+                    int *stats, double *errs, void *stream);
+
 /* Validate a layer and upload its expert table (qwen3_bind_layer, qwen3_moe.c:462-586).
  * Also builds the small-batch expert kernels' copy of the expert matrices, regrouped into
  * 16-row x 256-value tiles (same bytes per matrix, device memory owned by the layer): the

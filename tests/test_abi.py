@@ -41,6 +41,9 @@ def test_errors_without_a_gpu_are_reported_not_crashes():
     out = ctypes.c_uint32(5)
     assert L.cpg_crc32(None, 0, ctypes.byref(out), None) == 0 and out.value == 0   # zlib.crc32(b"")
     assert L.cpg_crc32(None, 5, ctypes.byref(out), None) == _lib.CPG_EINVAL
+    st, er = (ctypes.c_int * 3)(), (ctypes.c_double * 2)()
+    assert L.cpg_route_check(None, None, None, 0, 128, 8, st, er, None) == 0 and st[2] == -1
+    assert L.cpg_route_check(None, None, None, 4, 300, 8, st, er, None) == _lib.CPG_EINVAL
 
 
 def test_router_calibration_is_deterministic_and_skewed():

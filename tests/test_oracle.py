@@ -103,3 +103,24 @@ def test_topk_tie_rule(orc):
                     wt.ctypes.data_as(f))
     assert list(idx) == [3, 5, 9, 12]
     assert abs(float(wt.sum()) - 1.0) < 1e-6
+
+
+def test_route_check_oracle_matches_reference_verdicts(golden):
+    """The tie-aware agreement oracle against the reference's own checker
+    (tools/check_qwen3_baseline.py run on the same trace: tests/golden/make_route_golden.py)."""
+    import route_check as RC
+    g = golden("route_check.npz")
+    L = int(g["n_layers"])
+    mismatch, ties, sum_err, w_err = [], 0, 0.0, 0.0
+    for i in range(L):
+        r = RC.route_check(g[f"logits{i}"], g[f"topk{i}"], g[f"wt{i}"])
+        if r["bad"]:
+            mismatch.append(i)
+            ties += int(r["tie"][:r["first_bad"]].sum())     # the reference stops a layer there
+        else:
+            ties += r["ties"]
+        sum_err, w_err = max(sum_err, r["sum_err"]), max(w_err, r["w_err"])
+    assert mismatch == g["ref_mismatch"].tolist() == [3, 4]
+    assert ties == int(g["ref_ties"]) and ties > 0
+    assert abs(w_err - float(g["ref_w_err"])) <= 0.01 * float(g["ref_w_err"])   # printed to 3 digits
+    assert sum_err <= 1e-6 and float(g["ref_sum_err"]) <= 1e-6                 # float32 weights
