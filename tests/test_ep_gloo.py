@@ -65,11 +65,13 @@ def _worker(rank, G, port, seed, skew, out_path):
 
 
 @pytest.mark.parametrize("skew", [False, True])
-def test_ep_protocol_two_ranks(tmp_path, orc, skew):
+def test_ep_protocol_two_ranks(orc, skew):
     import oracle as O
     import torch.multiprocessing as mp
     G, seed = 2, 77
-    out = str(tmp_path / "mlp.npy")
+    out_dir = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_build")   # git-ignored
+    os.makedirs(out_dir, exist_ok=True)
+    out = os.path.join(out_dir, f"ep_gloo_mlp_{int(skew)}.npy")
     mp.start_processes(_worker, args=(G, _free_port(), seed, skew, out), nprocs=G, join=True, start_method="spawn")
     got = np.load(out)
     L = O.SynthLayer(D, F, E, K, O.ENC_Q4, seed=seed, oracle=orc)
