@@ -44,7 +44,7 @@ constexpr int KIND_GATEUP = 0;
 constexpr int KIND_DOWN = 1;
 constexpr int KIND_BOTH = 2;     // gate/up then down items in one launch
 constexpr int EX_NW = 8;         // consumer warps per CTA
-constexpr int EX_NP = 2;         // producer warps: weight boxes, token rows (one issuing warp's
+constexpr int EX_NP = 2;         // producer warps: weight tiles, token rows (one issuing warp's
                                  // copies are served one after another on B200)
 constexpr int EX_NCH = 2;        // 8-column MMA tiles per item
 constexpr int EX_NCHUNK = 8 * EX_NCH;   // tokens per item (an expert with more is split)
@@ -536,7 +536,7 @@ struct ExCfg {
     static constexpr int SLB = 8 * GB;                        // bytes of one row's K slice
     static constexpr int MATS = KIND == KIND_GATEUP ? 2 : 1;
     static constexpr int RB = KIND == KIND_GATEUP ? 64 : 128; // rows per matrix per item
-    static constexpr int WBYTES = MATS * RB * SLB;             // weight boxes of a stage
+    static constexpr int WBYTES = MATS * RB * SLB;             // weight tiles of a stage
     static constexpr int BROW = EX_KSL * 2 + 16;               // token row slice, fp16, padded (odd 16 B)
     static constexpr int STAGE = WBYTES + EX_NCHUNK * BROW;    // + the chunk's token rows
     static constexpr int WPAIR = GB / 2;                       // 32-bit words per group pair
