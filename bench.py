@@ -334,7 +334,8 @@ def run_ours(args, rank, world, torch, dist):
         "metric": METRIC, "value": round(tok_s, 1), "unit": "tok/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "q4_0 x f16 -> f32 (fp16 tensor-core MMA, fp32 accumulate)", "data": "synthetic",
+        "dtype": "q4_0 x f32 (f32 activations as fp16 hi + lo halves, exact q on mma.sync, fp32 accumulate)",
+        "data": "synthetic",
         "config": {"workload": "Qwen3-30B-A3B MoE decode: 64-token batch through 48 stacked MoE layers "
                                "(configs[1], Q4_0 experts, Zipf(1.1)-calibrated f32 router)",
                    "tokens_per_step_per_gpu": T, "layers": L, "d_model": D, "d_exp": F, "experts": E,

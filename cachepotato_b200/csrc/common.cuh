@@ -220,6 +220,21 @@ __device__ __forceinline__ void mma_16816(float d[4], const uint32_t a[4], uint3
           "f"(c[0]), "f"(c[1]), "f"(c[2]), "f"(c[3]));
 }
 
+// Two f32 values as fp16 hi and lo halves (hi = fp16(v), lo = fp16(v - hi); v - hi is exact in
+// f32), packed as half2 words {a, b}: hi + lo keeps about 22 significant bits of v for |v| in
+// fp16's normal range (the lo half's absolute error is at most 2^-25 below it).
+__device__ __forceinline__ void split_half2(float a, float b, uint32_t &hi, uint32_t &lo) {
+    const __half2 h = __floats2half2_rn(a, b);
+    const float2 hf = __half22float2(h);
+    const __half2 l = __floats2half2_rn(a - hf.x, b - hf.y);
+    hi = *reinterpret_cast<const uint32_t *>(&h);
+    lo = *reinterpret_cast<const uint32_t *>(&l);
+}
+__device__ __forceinline__ void split_half(float v, __half &hi, __half &lo) {
+    hi = __float2half_rn(v);
+    lo = __float2half_rn(v - __half2float(hi));
+}
+
 // (a & b) ^ c in one LOP3.
 __device__ __forceinline__ uint32_t lop3_and_xor(uint32_t a, uint32_t b, uint32_t c) {
     uint32_t r;

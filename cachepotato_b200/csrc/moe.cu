@@ -22,7 +22,15 @@
 // other warp copies the same K slice of the item's token rows by 16-byte cp.async. Eight
 // consumer warps decode Q4_0 / Q8_0 groups in registers (exact integers in fp16) and feed
 // mma.m16n8k16 with fp32 accumulators; the group scale is applied in fp32 after each group's
-// MMAs. Tokens are the N dimension (8 per MMA tile), weights are read exactly once per layer.
+// MMAs. Weights are read exactly once per layer.
+//
+// Activations keep f32 accuracy on fp16 tensor cores: every f32 operand value v (xn, h) is
+// stored as two fp16 halves, hi = fp16(v) and lo = fp16(v - hi), so hi + lo carries about 22
+// significant bits. The halves are neighbouring N columns of the MMA (token j of an item ->
+// columns 2j and 2j+1), so a column pair's two partial sums land in one thread's accumulator
+// pair and add up in fp32 after the K loop; the Q4/Q8 integers are exact in fp16. One 8-column
+// MMA tile therefore carries four tokens, and an item of at most four tokens (a one-token decode
+// step, most experts of a 64-token batch) issues no more MMAs than a single fp16 operand would.
 #include <math.h>
 
 #include <algorithm>
@@ -46,8 +54,8 @@ constexpr int KIND_BOTH = 2;     // gate/up then down items in one launch
 constexpr int EX_NW = 8;         // consumer warps per CTA
 constexpr int EX_NP = 2;         // producer warps: weight tiles, token rows (one issuing warp's
                                  // copies are served one after another on B200)
-constexpr int EX_NCH = 2;        // 8-column MMA tiles per item
-constexpr int EX_NCHUNK = 8 * EX_NCH;   // tokens per item (an expert with more is split)
+constexpr int EX_NCH = 4;        // 8-column MMA tiles per item (four tokens each: hi and lo columns)
+constexpr int EX_NCHUNK = 4 * EX_NCH;   // tokens per item (an expert with more is split)
 constexpr int EX_GROUP_MAX = 1024;       // pairs the gate/up kernel groups itself (T ≤ 128)
 constexpr int R_CLUSTER_MAX = 16;        // router CTAs per token tile (one cluster)
 
@@ -79,8 +87,8 @@ static WsLayout ws_layout(int D, int F, int E, int K, int T) {
     L.topk = o; o = align_up(o + sizeof(int) * (size_t)T * K, 256);
     L.wt = o; o = align_up(o + sizeof(float) * (size_t)T * K, 256);
     L.logits = o; o = align_up(o + sizeof(float) * (size_t)T * E, 256);
-    L.xn = o; o = align_up(o + sizeof(__half) * (size_t)T * D, 256);
-    L.h = o; o = align_up(o + sizeof(__half) * (size_t)T * K * F, 256);
+    L.xn = o; o = align_up(o + sizeof(__half) * 2 * (size_t)T * D, 256);       // per token: hi | lo
+    L.h = o; o = align_up(o + sizeof(__half) * 2 * (size_t)T * K * F, 256);    // per pair: hi | lo
     L.y = o; o = align_up(o + sizeof(float) * (size_t)T * K * D, 256);
     L.dep = o; o = align_up(o + sizeof(int) * (size_t)max_token_chunks(E, K, T), 256);
     L.total = o;
@@ -431,19 +439,20 @@ __global__ void __launch_bounds__(R_THREADS, 2) k_router(RouterArgs a) {
         }
     }
     __syncthreads();
-    // fp16 copy of xn in the expert kernels' K order: CTA x of the cluster writes token x of the
-    // tile, eight values (one 16-byte store) per thread
+    // xn for the expert kernels as fp16 hi | lo halves (row of 2·D), in their K order: CTA x of
+    // the cluster writes token x of the tile, eight values (two 16-byte stores) per thread
     for (int t = blockIdx.x; t < nt; t += gridDim.x) {
         const float *row = xs + t * D;
+        __half *dst = a.xn_perm + (size_t)(t0 + t) * 2 * D;
         for (int p0 = tid * 8; p0 < D; p0 += R_THREADS * 8) {
-            uint32_t h[4];
+            uint32_t hi[4], lo[4];
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
                 const int q0 = p0 + 2 * k, q1 = q0 + 1;
-                const __half2 v = __floats2half2_rn(row[(q0 & ~63) + s_p2e[q0 & 63]], row[(q1 & ~63) + s_p2e[q1 & 63]]);
-                h[k] = *reinterpret_cast<const uint32_t *>(&v);
+                split_half2(row[(q0 & ~63) + s_p2e[q0 & 63]], row[(q1 & ~63) + s_p2e[q1 & 63]], hi[k], lo[k]);
             }
-            *reinterpret_cast<uint4 *>(a.xn_perm + (size_t)(t0 + t) * D + p0) = make_uint4(h[0], h[1], h[2], h[3]);
+            *reinterpret_cast<uint4 *>(dst + p0) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+            *reinterpret_cast<uint4 *>(dst + D + p0) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
         }
     }
     // logits = Wgate·xn (matmul_wx, kernels.c:84-95): warp w owns experts e0 + w, e0 + w + 8, ...
@@ -537,7 +546,11 @@ struct ExCfg {
     static constexpr int MATS = KIND == KIND_GATEUP ? 2 : 1;
     static constexpr int RB = KIND == KIND_GATEUP ? 64 : 128; // rows per matrix per item
     static constexpr int WBYTES = MATS * RB * SLB;             // weight tiles of a stage
-    static constexpr int BROW = EX_KSL * 2 + 16;               // token row slice, fp16, padded (odd 16 B)
+    // one token's row slice in shared memory: hi half (512 B), 16 B gap, lo half, 16 B gap. The
+    // gap puts a row's hi and lo reads on different banks (lanes 2i and 2i+1 of a quarter warp
+    // read the two halves of one token).
+    static constexpr int LOFF = EX_KSL * 2 + 16;
+    static constexpr int BROW = 2 * LOFF;
     static constexpr int STAGE = WBYTES + EX_NCHUNK * BROW;    // + the chunk's token rows
     static constexpr int WPAIR = GB / 2;                       // 32-bit words per group pair
 };
@@ -666,35 +679,80 @@ __device__ __forceinline__ void tile_frags(const uint8_t *tp, int P, int lane, u
     }
 }
 
+// The fragments of one group (hf = 0: group 2P, 1: group 2P + 1) of pair P: fr[0..1] or fr[2..3]
+// of tile_frags.
+template <int ENC>
+__device__ __forceinline__ void group_frags(const uint8_t *tp, int P, int hf, int lane, uint32_t (&fh)[2][4]) {
+    const uint4 w = *reinterpret_cast<const uint4 *>(tp + (P * 32 + lane) * 16);
+    if (ENC == CPG_ENC_Q4) {
+        q4_word(hf ? w.y : w.x, fh[0][0], fh[0][2], fh[1][0], fh[1][2]);
+        q4_word(hf ? w.w : w.z, fh[0][1], fh[0][3], fh[1][1], fh[1][3]);
+    } else {
+        const uint4 v = *reinterpret_cast<const uint4 *>(tp + 2048 + (P * 32 + lane) * 16);
+        q8_word(hf ? w.z : w.x, fh[0][0], fh[0][2]);
+        q8_word(hf ? w.w : w.y, fh[1][0], fh[1][2]);
+        q8_word(hf ? v.z : v.x, fh[0][1], fh[0][3]);
+        q8_word(hf ? v.w : v.y, fh[1][1], fh[1][3]);
+    }
+}
+
 // Operand fragments of pair p of the K slice for the NTL token tiles, from the stage's token
-// rows in shared memory (bs[nt] = this thread's row, already offset by t·32 bytes).
-template <int NTL>
-__device__ __forceinline__ void load_b_smem(const uint8_t *const (&bs)[EX_NCH], int p, uint4 (&b)[EX_NCH][2]) {
+// rows in shared memory (bs = this thread's row in tile 0, already offset by t·32 bytes; tile nt
+// starts `tstride` bytes further per tile).
+template <int NTL, int TSTRIDE>
+__device__ __forceinline__ void load_b_smem(const uint8_t *bs, int p, uint4 (&b)[EX_NCH][2]) {
 #pragma unroll
     for (int nt = 0; nt < NTL; ++nt) {
-        const uint4 *bp = reinterpret_cast<const uint4 *>(bs[nt] + p * 128);
+        const uint4 *bp = reinterpret_cast<const uint4 *>(bs + nt * TSTRIDE + p * 128);
         b[nt][0] = bp[0];
         b[nt][1] = bp[1];
     }
 }
 
 // The four group pairs of one K slice of a tile.
-template <int ENC, int NTL>
-__device__ __forceinline__ void slice_mma(const uint8_t *tp, int lane, const uint8_t *const (&bs)[EX_NCH],
-                                          float (&acc)[EX_NCH][4]) {
+template <int ENC, int NTL, int TSTRIDE>
+__device__ __forceinline__ void slice_mma(const uint8_t *tp, int lane, const uint8_t *bs, float (&acc)[EX_NCH][4]) {
     using X = ExTile<ENC>;
     const uint2 *sc = reinterpret_cast<const uint2 *>(tp + X::DB + (lane >> 2) * 32);   // scales, 2 pairs a load
-    uint4 b0[EX_NCH][2], b1[EX_NCH][2];
     uint32_t fr[4][4];
-    load_b_smem<NTL>(bs, 0, b0);
-    load_b_smem<NTL>(bs, 1, b1);
+    if (NTL > 2) {
+        // three or four tiles: one group (half a pair) decoded and applied at a time, which keeps
+        // the live fragments to 8 registers; per tile the accumulation order is the same
+#pragma unroll
+        for (int P = 0; P < 4; ++P) {
+            const uint2 sg = sc[(P >> 1)], s8 = sc[2 + (P >> 1)];
+            const uint32_t dg = P & 1 ? sg.y : sg.x, d8 = P & 1 ? s8.y : s8.x;
+            const float2 fg = __half22float2(*reinterpret_cast<const __half2 *>(&dg));
+            const float2 f8 = __half22float2(*reinterpret_cast<const __half2 *>(&d8));
+#pragma unroll
+            for (int hf = 0; hf < 2; ++hf) {                 // group 2P + hf
+                uint32_t fh[2][4];
+                group_frags<ENC>(tp, P, hf, lane, fh);
+                const float d0 = hf ? fg.y : fg.x, d1 = hf ? f8.y : f8.x;   // rows g / g + 8
+#pragma unroll
+                for (int nt = 0; nt < NTL; ++nt) {
+                    const uint4 bq = *reinterpret_cast<const uint4 *>(bs + nt * TSTRIDE + P * 128 + hf * 16);
+                    const float z[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                    float sj[4];
+                    mma_16816(sj, fh[0], bq.x, bq.y, z);
+                    mma_16816(sj, fh[1], bq.z, bq.w, sj);
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) acc[nt][c] = fmaf(c >> 1 ? d1 : d0, sj[c], acc[nt][c]);
+                }
+            }
+        }
+        return;
+    }
+    uint4 b0[EX_NCH][2], b1[EX_NCH][2];
+    load_b_smem<NTL, TSTRIDE>(bs, 0, b0);
+    load_b_smem<NTL, TSTRIDE>(bs, 1, b1);
     uint2 sg = sc[0], s8 = sc[2];
     tile_frags<ENC>(tp, 0, lane, fr);
     pair_mma<NTL>(fr, sg.x, s8.x, b0, acc);
-    load_b_smem<NTL>(bs, 2, b0);
+    load_b_smem<NTL, TSTRIDE>(bs, 2, b0);
     tile_frags<ENC>(tp, 1, lane, fr);
     pair_mma<NTL>(fr, sg.y, s8.y, b1, acc);
-    load_b_smem<NTL>(bs, 3, b1);
+    load_b_smem<NTL, TSTRIDE>(bs, 3, b1);
     sg = sc[1];
     s8 = sc[3];
     tile_frags<ENC>(tp, 2, lane, fr);
@@ -785,8 +843,8 @@ __global__ void __launch_bounds__((EX_NP + EX_NW) * 32, 2) k_experts(ExpertArgs 
     const int S = a.stages;
     const int tiles_gu = a.F / 64, tiles_dn = a.D / 128;     // row blocks per matrix and chunk
     const int ns_gu = a.D / EX_KSL, ns_dn = a.F / EX_KSL;     // K slices per item
-    float *xbuf = reinterpret_cast<float *>(smem + (size_t)S * C::STAGE);      // (4 tiles, NCH, 32, 4) gate sums
-    uint64_t *full = reinterpret_cast<uint64_t *>(xbuf + 4 * EX_NCH * 128);
+    float *xbuf = reinterpret_cast<float *>(smem + (size_t)S * C::STAGE);      // (4 tiles, NCH, 32, 2) gate sums
+    uint64_t *full = reinterpret_cast<uint64_t *>(xbuf + 4 * EX_NCH * 64);
     uint64_t *empty = full + S;
     uint64_t *mready = empty + S;                              // stage metadata written
     StageMeta *meta = reinterpret_cast<StageMeta *>(mready + S);
@@ -835,8 +893,9 @@ __global__ void __launch_bounds__((EX_NP + EX_NW) * 32, 2) k_experts(ExpertArgs 
         // the copies of one warp instruction read 512 contiguous bytes). A bulk copy per row would
         // queue up to 16 copies per stage behind one issuing thread. Each lane's copies count as
         // one arrival on the stage's full barrier once they have landed.
-        const __half *trow[EX_NCHUNK];
-        int cur = -1;
+        int trow[EX_NCHUNK];                                    // source row of each token column
+        const __half *src = a.bsrc;
+        int cur = -1, rlen = 0;
         for (int it = 0;; ++it) {
             const int st = it % S;
             if (!mbar_wait(&mready[st], (uint32_t)(it / S) & 1u)) {
@@ -856,18 +915,24 @@ __global__ void __launch_bounds__((EX_NP + EX_NW) * 32, 2) k_experts(ExpertArgs 
                         atomicCAS(a.status + WS_STATUS, ST_OK, ST_TIMEOUT_FULL);
                     __threadfence();
                 }
-                const __half *src = KIND == KIND_BOTH && !gu ? a.h_out : a.bsrc;
+                src = KIND == KIND_BOTH && !gu ? a.h_out : a.bsrc;
+                rlen = gu ? a.D : a.F;                         // a source row is hi | lo, rlen each
 #pragma unroll
                 for (int j = 0; j < EX_NCHUNK; ++j) {
                     const int p = md.off + min(j, md.cnt - 1);
-                    trow[j] = gu ? src + (size_t)(pairs[p] / a.K) * a.D : src + (size_t)p * a.F;
+                    trow[j] = gu ? pairs[p] / a.K : p;
                 }
             }
             uint8_t *dst = smem + (size_t)st * C::STAGE + C::WBYTES + lane * 16;
+            const __half *sl = src + (size_t)md.s * EX_KSL + lane * 8;
 #pragma unroll
-            for (int j = 0; j < EX_NCHUNK; ++j)                // columns past cnt keep stale rows: their
-                if (j < md.cnt)                                // results are never stored
-                    cp_async16(dst + j * C::BROW, trow[j] + (size_t)md.s * EX_KSL + lane * 8);
+            for (int j = 0; j < EX_NCHUNK; ++j) {              // columns past cnt keep stale rows: their
+                if (j < md.cnt) {                              // results are never stored
+                    const __half *r = sl + (size_t)trow[j] * 2 * rlen;
+                    cp_async16(dst + j * C::BROW, r);
+                    cp_async16(dst + j * C::BROW + C::LOFF, r + rlen);
+                }
+            }
             cp_async_mbar_arrive(&full[st]);
         }
         cp_async_wait_all();                                   // nothing in flight when the warp leaves
@@ -934,8 +999,11 @@ __global__ void __launch_bounds__((EX_NP + EX_NW) * 32, 2) k_experts(ExpertArgs 
     // cw >> 1 of the item's 64); down items: 16 rows (tile cw of the item's 128); over the whole K
     const int cw = warp - EX_NP;
     const int g = lane >> 2, t = lane & 3;
+    // MMA column 8·nt + c holds token 4·nt + c/2 of the item, its hi half for even c, lo for
+    // odd c. This lane feeds column g of every tile and receives columns 2t, 2t+1: accumulator
+    // acc[nt][0] + acc[nt][1] is token 4·nt + t at row g, acc[nt][2] + acc[nt][3] at row g + 8.
     float acc[EX_NCH][4];
-    bool two = false;
+    int ntl = 1;                                           // 8-column tiles in use: ceil(cnt / 4)
     for (int it = 0;; ++it) {
         const int st = it % S;
         if (!mbar_wait(&full[st], (uint32_t)(it / S) & 1u)) {
@@ -946,53 +1014,52 @@ __global__ void __launch_bounds__((EX_NP + EX_NW) * 32, 2) k_experts(ExpertArgs 
         if (md.item < 0) break;
         const bool gu = HAS_GU && (!HAS_DN || md.kind == KIND_GATEUP);
         if (md.s == 0) {                                   // a new item
-            two = md.cnt > 8;
+            ntl = (md.cnt + 3) >> 2;
 #pragma unroll
             for (int nt = 0; nt < EX_NCH; ++nt)
 #pragma unroll
                 for (int c = 0; c < 4; ++c) acc[nt][c] = 0.0f;
         }
-        const uint8_t *bs[EX_NCH];
-#pragma unroll
-        for (int nt = 0; nt < EX_NCH; ++nt)
-            bs[nt] = smem + (size_t)st * C::STAGE + C::WBYTES + (nt * 8 + g) * C::BROW + t * 32;
+        constexpr int TS = 4 * C::BROW;                    // bytes from one 8-column tile's rows to the next
+        const uint8_t *bs = smem + (size_t)st * C::STAGE + C::WBYTES + (g >> 1) * C::BROW + (g & 1) * C::LOFF + t * 32;
         const int tidx = gu ? (cw & 1) * 4 + (cw >> 1) : cw;
         const uint8_t *tp = smem + (size_t)st * C::STAGE + (size_t)tidx * X::TB;
-        if (two) slice_mma<ENC, 2>(tp, lane, bs, acc);
-        else slice_mma<ENC, 1>(tp, lane, bs, acc);
+        switch (ntl) {
+            case 1: slice_mma<ENC, 1, TS>(tp, lane, bs, acc); break;
+            case 2: slice_mma<ENC, 2, TS>(tp, lane, bs, acc); break;
+            case 3: slice_mma<ENC, 3, TS>(tp, lane, bs, acc); break;
+            default: slice_mma<ENC, 4, TS>(tp, lane, bs, acc); break;
+        }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[st]);           // this warp is done with the stage
         if (md.s != (gu ? ns_gu : ns_dn) - 1) continue;
-        // ---------------- epilogue of the item
-        const int ntl = two ? 2 : 1;
+        // ---------------- epilogue of the item: hi and lo partial sums added in fp32
         if (gu) {
             const int mat = cw & 1, tile = cw >> 1;
-            float *xb = xbuf + (size_t)tile * EX_NCH * 128;
+            float *xb = xbuf + (size_t)tile * EX_NCH * 64;
             if (mat == 0) {
 #pragma unroll
                 for (int nt = 0; nt < EX_NCH; ++nt)
                     if (nt < ntl)
-                        *reinterpret_cast<float4 *>(xb + (nt * 32 + lane) * 4) =
-                            make_float4(acc[nt][0], acc[nt][1], acc[nt][2], acc[nt][3]);
+                        *reinterpret_cast<float2 *>(xb + (nt * 32 + lane) * 2) =
+                            make_float2(acc[nt][0] + acc[nt][1], acc[nt][2] + acc[nt][3]);
             }
             named_bar_sync(1, EX_NW * 32);
             if (mat == 1) {
+                const int fr = md.m * 64 + tile * 16 + g;                                     // features fr, fr + 8
+                const int pos0 = (fr & ~63) + s_perm.elem_to_pos[fr & 63];
+                const int pos1 = ((fr + 8) & ~63) + s_perm.elem_to_pos[(fr + 8) & 63];
 #pragma unroll
                 for (int nt = 0; nt < EX_NCH; ++nt) {
-                    if (nt >= ntl) continue;
-                    const float4 gv = *reinterpret_cast<const float4 *>(xb + (nt * 32 + lane) * 4);
-                    const float gs[4] = {gv.x, gv.y, gv.z, gv.w};
-#pragma unroll
-                    for (int c = 0; c < 4; ++c) {
-                        const int col = nt * 8 + 2 * t + (c & 1);
-                        if (col < md.cnt) {
-                            const int row = md.m * 64 + tile * 16 + g + 8 * (c >> 1);         // feature in [0, F)
-                            const float silu = gs[c] / (1.0f + expf(-gs[c]));                 // kernels.c:416
-                            const float h = silu * acc[nt][c];                                // qwen3_moe.c:219
-                            const int pos = (row & ~63) + s_perm.elem_to_pos[row & 63];
-                            a.h_out[(size_t)(md.off + col) * a.F + pos] = __float2half_rn(h);
-                        }
-                    }
+                    const int col = nt * 4 + t;                                               // token of the item
+                    if (nt >= ntl || col >= md.cnt) continue;
+                    const float2 gv = *reinterpret_cast<const float2 *>(xb + (nt * 32 + lane) * 2);
+                    const float u0 = acc[nt][0] + acc[nt][1], u1 = acc[nt][2] + acc[nt][3];
+                    const float h0 = gv.x / (1.0f + expf(-gv.x)) * u0;                        // kernels.c:416,
+                    const float h1 = gv.y / (1.0f + expf(-gv.y)) * u1;                        // qwen3_moe.c:219
+                    __half *hr = a.h_out + (size_t)(md.off + col) * 2 * a.F;                  // hi | lo
+                    split_half(h0, hr[pos0], hr[a.F + pos0]);
+                    split_half(h1, hr[pos1], hr[a.F + pos1]);
                 }
             }
             named_bar_sync(1, EX_NW * 32);                 // the exchange buffer is free again
@@ -1001,17 +1068,14 @@ __global__ void __launch_bounds__((EX_NP + EX_NW) * 32, 2) k_experts(ExpertArgs 
                 atomicAdd(a.dep + md.chunk, 1);
             }
         } else {
+            const int row = md.m * 128 + cw * 16 + g;                                         // rows row, row + 8
 #pragma unroll
             for (int nt = 0; nt < EX_NCH; ++nt) {
-                if (nt >= ntl) continue;
-#pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    const int col = nt * 8 + 2 * t + (c & 1);
-                    if (col < md.cnt) {
-                        const int row = md.m * 128 + cw * 16 + g + 8 * (c >> 1);               // in [0, D)
-                        a.y_out[(size_t)pairs[md.off + col] * a.D + row] = acc[nt][c];
-                    }
-                }
+                const int col = nt * 4 + t;
+                if (nt >= ntl || col >= md.cnt) continue;
+                float *yr = a.y_out + (size_t)pairs[md.off + col] * a.D;
+                yr[row] = acc[nt][0] + acc[nt][1];
+                yr[row + 8] = acc[nt][2] + acc[nt][3];
             }
         }
     }
@@ -1079,7 +1143,7 @@ struct cpg_moe_layer {
     uint8_t *d_tiles = nullptr;    // device copy of the expert matrices in the decode tile layout
                                    // (k_tile_experts), built here
     std::mutex wmaps_mu;
-    cpg::KernelPlan gateup, down, both;      // two CTAs per SM, ~100 KB of stages each
+    cpg::KernelPlan gateup, down, both;      // two CTAs per SM (Q4_0), ~100 KB of stages each
     cpg::KernelPlan gateup_deep, down_deep;  // one CTA per SM with all the shared memory in stages:
                                              // for launches with at most one item per SM
 };
@@ -1090,12 +1154,13 @@ template <int ENC, int KIND>
 static int plan_kernel(KernelPlan &p, bool deep) {
     using C = ExCfg<ENC, KIND>;
     auto *k = k_experts<ENC, KIND>;
-    const size_t fixed = sizeof(float) * 4 * EX_NCH * 128 + 8 * (sizeof(StageMeta) + 24) + 256;
+    const size_t fixed = sizeof(float) * 4 * EX_NCH * 64 + 8 * (sizeof(StageMeta) + 24) + 256;
     cudaFuncAttributes fa;
     CPG_CUDA(cudaFuncGetAttributes(&fa, k));
     const size_t limit = (size_t)smem_optin() - fa.sharedSizeBytes;
-    // two CTAs per SM (latency hiding comes from warps); stages fill about 100 KB per CTA. Deep:
-    // one CTA per SM, as many stages as fit (up to 8 = every K slice of a gate/up item in flight)
+    // two CTAs per SM (latency hiding comes from warps); stages fill about 100 KB per CTA (two
+    // 35 KB Q4_0 stages; Q8_0's 51 KB stages leave room for one CTA per SM). Deep: one CTA per
+    // SM, as many stages as fit (up to 8 = every K slice of a gate/up item in flight)
     int S = (int)(((deep ? limit : 100 * 1024) - fixed) / C::STAGE);
     if (S < 2) S = 2;
     if (S > 8) S = 8;
@@ -1103,7 +1168,7 @@ static int plan_kernel(KernelPlan &p, bool deep) {
     CPG_REQUIRE(fixed + (size_t)S * C::STAGE <= limit, "expert kernel: a %d-byte stage does not fit in shared memory",
                 C::STAGE);
     p.stages = S;
-    p.smem = (size_t)S * C::STAGE + sizeof(float) * 4 * EX_NCH * 128 + S * sizeof(StageMeta) + 3 * S * sizeof(uint64_t) +
+    p.smem = (size_t)S * C::STAGE + sizeof(float) * 4 * EX_NCH * 64 + S * sizeof(StageMeta) + 3 * S * sizeof(uint64_t) +
              128;                                           // alignment slack
     int rc = allow_max_smem((const void *)k);
     if (rc) return rc;

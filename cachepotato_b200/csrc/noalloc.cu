@@ -6,7 +6,7 @@
 // of the library's own device image: nothing is allocated per call.
 //
 // The array is fixed in size (kStaticScratchBytes, 8 MiB: 64 tokens of a Qwen3-30B-A3B layer
-// need about 5.1 MB), every GPU that loads the library holds it until the process exits, and all
+// need about 6.3 MB), every GPU that loads the library holds it until the process exits, and all
 // calls share it.
 #include <mutex>
 

@@ -3,7 +3,10 @@ agreement rule (expert ids identical except where the top-k margin is below 1e-6
 import numpy as np
 
 TOPK_MARGIN = 1e-6     # routing agreement: ids may differ only where the margin is below this
-BLOCK_TOL = 1e-3       # max|d| / max|ref| for block outputs (fp16 tensor-core operands)
+BLOCK_TOL = 1e-3       # max|d| / max|ref| for block outputs on fp16 operand rows (the tcgen05
+                       # prefill and expert-parallel paths: the benchmark's bf16-class config)
+DECODE_TOL = 1e-5      # max|d| / max|ref| for the decode MoE block (f32 activations carried as
+                       # fp16 hi + lo halves; the kernel gate of tools/verify_q8_kernels.py)
 KERNEL_TOL = 1e-5      # fp32 matvec kernels (tools/verify_q8_kernels.py tolerance)
 
 
@@ -26,17 +29,20 @@ def probs_from_logits(logits):
 
 
 def check_topk(got_idx, want_idx, want_logits, K):
-    """Per token: same ordered ids, or a difference explained by a sub-1e-6 probability margin
-    (the reference's top-k picks by strict '>' in descending order, qwen3_moe.c:184-194)."""
+    """Per token: same ordered ids, or every differing slot explained by a sub-1e-6 probability
+    margin between the two experts that swapped there (the reference's top-k picks by strict '>'
+    in descending order, qwen3_moe.c:184-194, so only near-equal probabilities can trade places,
+    within the top k or across the k-th / (k+1)-th boundary)."""
     p = probs_from_logits(want_logits)
     bad = []
     for t in range(got_idx.shape[0]):
-        if np.array_equal(got_idx[t], want_idx[t]):
+        g, w = np.asarray(got_idx[t]), np.asarray(want_idx[t])
+        if np.array_equal(g, w):
             continue
-        ps = np.sort(p[t])[::-1]
-        # any swap needs two probabilities within the margin among the top K+1
-        close = np.min(np.abs(np.diff(ps[:K + 1]))) < TOPK_MARGIN
-        if not close:
+        diff = np.nonzero(g != w)[0]
+        ok = len(set(g.tolist())) == len(g) and all(
+            0 <= g[j] < p.shape[1] and abs(p[t, g[j]] - p[t, w[j]]) < TOPK_MARGIN for j in diff)
+        if not ok:
             bad.append(t)
     return bad
 

@@ -3,15 +3,15 @@
 
 Bars: router logits rel 1e-5 (fp32 GEMV, different summation order); expert ids identical
 except where the top-k probability margin is below 1e-6; routing weights rel 1e-5; block
-output max|d|/max|ref| <= 1e-3 (experts run on fp16 tensor-core operands: exact Q4/Q8
-integers, fp16-rounded activations, fp32 accumulation)."""
+output max|d|/max|ref| <= 1e-5 (the experts run on fp16 tensor cores with exact Q4/Q8 integers
+and f32 activations carried as fp16 hi + lo halves, fp32 accumulation)."""
 import numpy as np
 import pytest
 
 import oracle as O
 import make_golden as MG
 from conftest import max_rel
-from helpers import BLOCK_TOL, check_topk, device_layer
+from helpers import DECODE_TOL, check_topk, device_layer
 
 pytestmark = pytest.mark.gpu
 torch = pytest.importorskip("torch")
@@ -41,7 +41,7 @@ def _compare(got, want, K, logits_tol=1e-5):
     if "wt" in want:
         assert max_rel(got.wt.cpu().numpy()[ok], want["wt"][ok]) <= 1e-5
     err = max_rel(got.mlp.cpu().numpy()[ok], want["mlp"][ok])
-    assert err <= BLOCK_TOL, err
+    assert err <= DECODE_TOL, err
     return err
 
 
@@ -95,7 +95,7 @@ def test_attn_input_and_mlp_accumulation(orc, layers):
     got = dl.forward(torch.from_numpy(x).cuda(), torch.from_numpy(attn).cuda(),
                      mlp=torch.from_numpy(mlp0.copy()).cuda())
     want = orc.qwen3_moe(L, x, attn)                       # oracle mlp starts at zero
-    assert max_rel(got.mlp.cpu().numpy() - mlp0, want["mlp"]) <= BLOCK_TOL
+    assert max_rel(got.mlp.cpu().numpy() - mlp0, want["mlp"]) <= DECODE_TOL
     assert np.array_equal(got.topk_idx.cpu().numpy(), want["topk_idx"])
     xo = got.x_out.cpu().numpy()
     assert np.array_equal(xo, (x + (attn + got.mlp.cpu().numpy())).astype(np.float32))

@@ -124,3 +124,26 @@ def test_route_check_oracle_matches_reference_verdicts(golden):
     assert ties == int(g["ref_ties"]) and ties > 0
     assert abs(w_err - float(g["ref_w_err"])) <= 0.01 * float(g["ref_w_err"])   # printed to 3 digits
     assert sum_err <= 1e-6 and float(g["ref_sum_err"]) <= 1e-6                 # float32 weights
+
+
+def test_routing_agreement_excuses_only_near_tied_swaps():
+    """The parity helper accepts an id difference only where the two experts that traded places
+    have reference probabilities within 1e-6 (a planted near-tie elsewhere excuses nothing)."""
+    from helpers import check_topk
+    E, K = 16, 4
+    logits = np.zeros((1, E), np.float32)
+    logits[0, :6] = [5.0, 4.0, 3.0, 2.0, 2.0, 1.0]          # experts 3 and 4 tie exactly
+    logits[0, 10] = 3.0 + 1e-3                                # a clear 3rd place, not a tie with 2
+    want = np.array([[0, 1, 10, 2]], np.int32)
+    assert check_topk(want, want, logits, K) == []
+    # 2nd/3rd swapped: probabilities differ by far more than 1e-6
+    assert check_topk(np.array([[0, 10, 1, 2]], np.int32), want, logits, K) == [0]
+    # the 4th slot taken by a non-tied expert, although a tie exists among 3 / 4
+    assert check_topk(np.array([[0, 1, 10, 3]], np.int32), want, logits, K) == [0]
+    logits2 = logits.copy()
+    logits2[0, 10] = 0.0
+    want2 = np.array([[0, 1, 2, 3]], np.int32)
+    # the boundary tie 3 / 4 may go either way
+    assert check_topk(np.array([[0, 1, 2, 4]], np.int32), want2, logits2, K) == []
+    # a repeated id is never accepted
+    assert check_topk(np.array([[0, 1, 2, 2]], np.int32), want2, logits2, K) == [0]
