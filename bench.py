@@ -66,7 +66,7 @@ def parse():
     ap.add_argument("--layers", type=int, default=48)
     ap.add_argument("--zipf", type=float, default=1.1)
     ap.add_argument("--seed", type=int, default=1234)
-    ap.add_argument("--cpu-sample-layers", type=int, default=2)
+    ap.add_argument("--cpu-sample-layers", type=int, default=4)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--prefill-tokens", type=int, default=4096, help="0 skips the prefill section")
     ap.add_argument("--no-q8", action="store_true", help="skip the Q8 batch-1 section")
@@ -75,6 +75,53 @@ def parse():
     ap.add_argument("--full-prompt", type=int, default=512)
     ap.add_argument("--full-new", type=int, default=128)
     return ap.parse_args()
+
+
+def physical_cores() -> int:
+    """Distinct (physical id, core id) pairs among the CPUs this process may run on: hyper-threads
+    share a core (the reference's cp_physical_cores, engine/api/cachepotato.c:59-80, restated; it
+    also falls back to the online CPU count)."""
+    allowed = os.sched_getaffinity(0) if hasattr(os, "sched_getaffinity") else None
+    seen, proc, pkg = set(), None, 0
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                k, _, v = line.partition(":")
+                k, v = k.strip(), v.strip()
+                if k == "processor":
+                    proc = int(v)
+                elif k == "physical id":
+                    pkg = int(v)
+                elif k == "core id" and (allowed is None or proc in allowed):
+                    seen.add((pkg, int(v)))
+    except (OSError, ValueError):
+        seen = set()
+    if seen:
+        return len(seen)
+    return len(allowed) if allowed else (os.cpu_count() or 1)
+
+
+def headline_config(args) -> dict:
+    """The headline workload, identical in both arms' JSON lines."""
+    return {"workload": "Qwen3-30B-A3B MoE decode: 64-token batch through 48 stacked MoE layers "
+                        "(configs[1], Q4_0 experts, Zipf(1.1)-calibrated f32 router)",
+            "tokens_per_step_per_gpu": args.tokens, "layers": args.layers, "d_model": D, "d_exp": F, "experts": E,
+            "topk": K, "expert_encoding": "Q4_0",
+            "l2": "inputs larger than L2: each step streams ~13 GB of distinct expert weights"}
+
+
+def profiled_traffic():
+    """DRAM bytes of one captured launch of the headline expert kernel and the algorithmic bytes of
+    that same launch, from the committed ncu summary (profiles/k_experts_q4_decode_T64.md)."""
+    import re
+    path = os.path.join(ROOT, "profiles", "k_experts_q4_decode_T64.md")
+    try:
+        txt = open(path).read()
+    except OSError:
+        return None, None
+    t = re.search(r"traffic_bytes_per_launch:\s*(\d+)", txt)
+    a = re.search(r"algorithmic_bytes_same_launch:\s*(\d+)", txt)
+    return (int(t.group(1)) if t else None), (int(a.group(1)) if a else None)
 
 
 def peaks():
@@ -166,6 +213,49 @@ def view(torch, ptr, nbytes, dtype="f4"):
 
 
 # ------------------------------------------------------------------ our implementation
+def expert_blob(torch, lib, Q, seed, l, out_ptr=None):
+    """Layer l's 128 experts as the benchmark's stack holds them: Wg | Wu | Wd per expert,
+    N(0, 0.02) from a seeded device generator, quantised to Q4_0 on the device. Written to
+    out_ptr, or returned as a new device tensor."""
+    out = None
+    if out_ptr is None:
+        out = torch.empty(E * REGION_BYTES, dtype=torch.uint8, device="cuda")
+        out_ptr = out.data_ptr()
+    g = torch.Generator(device="cuda")
+    w32 = torch.randn(E * 3 * F * D, generator=g.manual_seed(seed * 1000 + 2 * l + 2), device="cuda")
+    w32.mul_(0.02)
+    Q.check(lib.cpg_quantize(out_ptr, w32.data_ptr(), ENC_Q4, w32.numel(), None))
+    del w32
+    return out
+
+
+def full_model_parts(torch, lib, Q, seed, L, V=151936, n_prompt=512):
+    """configs[2]'s weights besides the experts (attention Q4_0, fresh f32 routers, Q8_0 embed and
+    lm_head, unit norms) and its prompt, from the benchmark's seeds."""
+    H, KVH, HD = 32, 4, 128
+    QD, KD = H * HD, KVH * HD
+    g = torch.Generator(device="cuda")
+
+    def quant(rows, cols, s, enc=ENC_Q4):
+        gb = 18 if enc == ENC_Q4 else 34
+        out = torch.empty(rows * cols // 32 * gb, dtype=torch.uint8, device="cuda")
+        w = torch.randn(rows * cols, generator=g.manual_seed(s), device="cuda").mul_(0.02)
+        Q.check(lib.cpg_quantize(out.data_ptr(), w.data_ptr(), enc, w.numel(), None))
+        return out
+    ones_d, ones_h = torch.ones(D, device="cuda"), torch.ones(HD, device="cuda")
+    attn, routers = [], []
+    for l in range(L):
+        b = seed * 5000 + 10 * l
+        attn.append(dict(ln1=ones_d, q_norm=ones_h, k_norm=ones_h, wq=quant(QD, D, b + 1), wk=quant(KD, D, b + 2),
+                         wv=quant(KD, D, b + 3), wo=quant(D, QD, b + 4)))
+        routers.append(torch.randn((E, D), generator=g.manual_seed(b + 5), device="cuda") * 0.02)
+    embed = quant(V, D, seed * 5000 + 901, ENC_Q8)
+    head = quant(V, D, seed * 5000 + 902, ENC_Q8)
+    prompt = np.random.default_rng(seed + 3).integers(0, V, n_prompt).astype(np.int32)
+    return dict(attn=attn, routers=routers, embed=embed, head=head, final_norm=ones_d, ln2=ones_d,
+                prompt=prompt, V=V, H=H, KVH=KVH, HD=HD)
+
+
 def build_stack(torch, L, T, zipf, seed, lib, Q):
     """48 layers in the HBM region store, routers calibrated on the chained activations."""
     from cachepotato_b200.workload import calibrate_router_scales, load_stats
@@ -187,10 +277,7 @@ def build_stack(torch, L, T, zipf, seed, lib, Q):
         ln2.fill_(1.0)
         wg = view(torch, lib.cpg_store_region_get(r_wg), ROUTER_BYTES).view(E, D)
         wg.copy_(torch.randn((E, D), generator=g.manual_seed(seed * 1000 + 2 * l + 1), device="cuda") * 0.02)
-        w32 = torch.randn(E * 3 * F * D, generator=g.manual_seed(seed * 1000 + 2 * l + 2), device="cuda")
-        w32.mul_(0.02)
-        Q.check(lib.cpg_quantize(lib.cpg_store_region_get(r_ex[0]), w32.data_ptr(), ENC_Q4, w32.numel(), None))
-        del w32
+        expert_blob(torch, lib, Q, seed, l, lib.cpg_store_region_get(r_ex[0]))
         # Zipf calibration on this layer's actual input
         xn = x * torch.rsqrt((x * x).mean(-1, keepdim=True) + 1e-6)
         z = (xn @ wg.T).double().cpu().numpy()
@@ -312,22 +399,30 @@ def run_ours(args, rank, world, torch, dist):
     ms_pf = pf.pop("_ms") if pf else 0.0
 
     # max over ranks
-    t = torch.tensor([ms, ms_e2e, ms_b1, ms_pf, ms_q8, ms_ep, ms_fm], dtype=torch.float64, device="cuda")
+    ep_par = ep.pop("_parity") if ep else 0.0
+    t = torch.tensor([ms, ms_e2e, ms_b1, ms_pf, ms_q8, ms_ep, ms_fm, ep_par], dtype=torch.float64, device="cuda")
     if dist is not None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms, ms_e2e, ms_b1, ms_pf, ms_q8, ms_ep, ms_fm = (float(v) for v in t.tolist())
+    ms, ms_e2e, ms_b1, ms_pf, ms_q8, ms_ep, ms_fm, ep_par = (float(v) for v in t.tolist())
+    if ep is not None:
+        ep["parity"] = {"max_rel_vs_single_gpu_apply": ep_par, "tolerance": 1e-3, "ranks": world,
+                        "layers": "0 and last", "reference": "cpg_moe_apply of the whole layer on each rank's GPU"}
+        if ep_par > 1e-3:
+            raise SystemExit(f"expert-parallel parity failed: max_rel {ep_par:.3e} > 1e-3")
     if rank != 0:
         return None
 
     U = [st["distinct_experts"] for st in stats]
     step_bytes = sum(LN_BYTES + ROUTER_BYTES + u * REGION_BYTES + 2 * T * D * 4 for u in U)
-    # expert launch: the active experts' three matrices, xn read, h written and read back, y written
-    expert_bytes = sum(u * 3 * MAT_BYTES + T * D * 2 + 2 * T * K * F * 2 + T * K * D * 4 for u in U)
+    # expert launch: the active experts' three matrices, xn read (fp16 hi + lo: 4 B a value), h
+    # written and read back (4 B a value each way), y written (f32)
+    expert_bytes = sum(u * 3 * MAT_BYTES + T * D * 4 + 2 * T * K * F * 4 + T * K * D * 4 for u in U)
     ms_step = ms / args.steps
     hbm, kind = peaks()
     expert_ms_per_step = (phase[1] + phase[2]) / args.steps
     b1_bytes = L * (LN_BYTES + ROUTER_BYTES + K * REGION_BYTES + 2 * D * 4)
     achieved = expert_bytes / (expert_ms_per_step * 1e-3) / 1e9
+    traffic, traffic_alg = profiled_traffic()
     tok_s = world * T * args.steps / (ms * 1e-3)
     e2e_tok_s = world * T * args.steps / (ms_e2e * 1e-3)
     res = {
@@ -336,11 +431,7 @@ def run_ours(args, rank, world, torch, dist):
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "q4_0 x f32 (f32 activations as fp16 hi + lo halves, exact q on mma.sync, fp32 accumulate)",
         "data": "synthetic",
-        "config": {"workload": "Qwen3-30B-A3B MoE decode: 64-token batch through 48 stacked MoE layers "
-                               "(configs[1], Q4_0 experts, Zipf(1.1)-calibrated f32 router)",
-                   "tokens_per_step_per_gpu": T, "layers": L, "d_model": D, "d_exp": F, "experts": E,
-                   "topk": K, "expert_encoding": "Q4_0", "parallelism": f"replicas x{world}",
-                   "l2": "inputs larger than L2: each step streams ~13 GB of distinct expert weights"},
+        "config": headline_config(args), "parallelism": f"replicas x{world}",
         "moe_layer_hbm_gbs": round(step_bytes / (ms_step * 1e-3) / 1e9, 1),
         "routing": {"distinct_experts_per_layer_mean": round(float(np.mean(U)), 1),
                     "max_expert_load_mean": round(float(np.mean([st["max_load"] for st in stats])), 1)},
@@ -351,7 +442,11 @@ def run_ours(args, rank, world, torch, dist):
                      "achieved": round(achieved, 1),
                      "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),
                      "peak_kind": kind,
-                     "algorithmic_bytes_per_launch": int(expert_bytes / L), "traffic": None},
+                     "algorithmic_bytes_per_launch": int(expert_bytes / L),
+                     "traffic": traffic,
+                     "traffic_source": ("ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch of this "
+                                        "kernel (profiles/k_experts_q4_decode_T64.md); its algorithmic bytes: "
+                                        f"{traffic_alg}") if traffic else None},
         "e2e": {"value": round(e2e_tok_s, 1), "unit": "tok/s", "h2d_bytes_per_step": xbytes,
                 "d2h_bytes_per_step": xbytes},
         "decode_batch1": {"value": round(world * args.steps / (ms_b1 * 1e-3), 1), "unit": "tok/s",
@@ -447,31 +542,16 @@ def full_model_bench(args, layers, torch, lib, Q, barrier):
     routers (not Zipf-scaled: the experts are the region store's, the routers are fresh). A prompt
     of args.full_prompt uniform ids in one pass, then args.full_new greedy steps through
     cpg_qwen3_generate (each step embeds the previous argmax on the device and reads its id back)."""
-    L, V, H, KVH, HD = len(layers), 151936, 32, 4, 128
+    L = len(layers)
+    P = full_model_parts(torch, lib, Q, args.seed, L, n_prompt=args.full_prompt)
+    V, H, KVH, HD, prompt = P["V"], P["H"], P["KVH"], P["HD"], P["prompt"]
     QD, KD = H * HD, KVH * HD
-    g = torch.Generator(device="cuda")
-
-    def q4(rows, cols, seed, enc=ENC_Q4):
-        gb = 18 if enc == ENC_Q4 else 34
-        out = torch.empty(rows * cols // 32 * gb, dtype=torch.uint8, device="cuda")
-        w = torch.randn(rows * cols, generator=g.manual_seed(seed), device="cuda").mul_(0.02)
-        Q.check(lib.cpg_quantize(out.data_ptr(), w.data_ptr(), enc, w.numel(), None))
-        return out
-    ones_d, ones_h = torch.ones(2048, device="cuda"), torch.ones(HD, device="cuda")
-    attn, moe = [], []
-    for l, ly in enumerate(layers):
-        b = args.seed * 5000 + 10 * l
-        attn.append(dict(ln1=ones_d, q_norm=ones_h, k_norm=ones_h, wq=q4(QD, D, b + 1), wk=q4(KD, D, b + 2),
-                         wv=q4(KD, D, b + 3), wo=q4(D, QD, b + 4)))
-        wg = torch.randn((E, D), generator=g.manual_seed(b + 5), device="cuda") * 0.02
-        moe.append(Q.MoELayer(ones_d, wg, ENC_Q4, D, F, E, K, blob=None, expert_ptrs=ly.ptr_list))
-    embed = q4(V, D, args.seed * 5000 + 901, ENC_Q8)
-    head = q4(V, D, args.seed * 5000 + 902, ENC_Q8)
-    prompt = np.random.default_rng(args.seed + 3).integers(0, V, args.full_prompt).astype(np.int32)
+    moe = [Q.MoELayer(P["ln2"], P["routers"][l], ENC_Q4, D, F, E, K, blob=None, expert_ptrs=ly.ptr_list)
+           for l, ly in enumerate(layers)]
     max_ctx = args.full_prompt + args.full_new + 1
-    m = Q.Qwen3Model(d_model=D, n_heads=H, n_kv=KVH, head_dim=HD, vocab=V, max_ctx=max_ctx, attn=attn, moe=moe,
-                     attn_enc=ENC_Q4, embed=embed, embed_enc=ENC_Q8, lm_head=head, head_enc=ENC_Q8,
-                     final_norm=ones_d)
+    m = Q.Qwen3Model(d_model=D, n_heads=H, n_kv=KVH, head_dim=HD, vocab=V, max_ctx=max_ctx, attn=P["attn"],
+                     moe=moe, attn_enc=ENC_Q4, embed=P["embed"], embed_enc=ENC_Q8, lm_head=P["head"],
+                     head_enc=ENC_Q8, final_norm=P["final_norm"])
     s = torch.cuda.ExternalStream(m.stream_ptr())
     m.generate(prompt[:8], 4)                           # warm-up (small)
     barrier()
@@ -540,6 +620,7 @@ def ep_bench(args, layers, torch, lib, Q, dist, rank, world, barrier):
 
     for _ in range(max(3, args.warmup)):
         step()
+    ep.wait()
     Q.check(lib.cpg_moe_ep_check(ws.data_ptr(), None))
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -549,14 +630,33 @@ def ep_bench(args, layers, torch, lib, Q, dist, rank, world, barrier):
     e1.record()
     barrier()
     ms = e0.elapsed_time(e1)
+    ep.wait()
     Q.check(lib.cpg_moe_ep_check(ws.data_ptr(), None))
+    # per-phase device times (events inside cpg_moe_ep; every rank takes the same calls)
+    n_ph = min(L, 8)
+    phase = np.zeros(5)
+    x.copy_(x0)
+    for l in range(n_ph):
+        ph = [0.0] * 5
+        ep.forward(local[l], x, idx_l[l], wt_l[l], mlp=x, ws=ws, check_status=False, phase_ms=ph)
+        phase += np.array(ph)
+    phase /= n_ph
+    # parity: this rank's tokens through layers 0 and L-1 by expert parallelism against the whole
+    # layer applied on this GPU alone (cpg_moe_apply, all 128 experts), same rows and routing
+    parity = 0.0
+    for l in sorted({0, L - 1}):
+        got = ep.forward(local[l], x0, idx_l[l], wt_l[l], ws=ws)
+        want = Q.moe_apply(layers[l], x0, idx_l[l], wt_l[l])
+        parity = max(parity, float((got - want).abs().max() / want.abs().max()))
     ep.close()
     pairs = args.ep_tokens * K / G                      # per GPU, uniform routing
     link_bytes = remote_rows / L * D * (2 + 4)          # per layer: fp16 rows out, f32 rows back
     roof = {"hbm": E_l * REGION_BYTES / (peaks()[0] * 1e9) * 1e3,
             "tensor": pairs * 3 * 2 * F * D / (tensor_peak()[0] * 1e12) * 1e3,
             "nvlink": link_bytes / 770e9 * 1e3}
-    return {"_ms": ms, "_roof_ms": roof, "unit": "tok/s",
+    return {"_ms": ms, "_roof_ms": roof, "_parity": parity, "unit": "tok/s",
+            "phase_ms_per_layer_rank": {k: round(float(v), 5) for k, v in
+                                        zip(("plan_pack", "dispatch", "owner_experts", "return", "combine"), phase)},
             "config": {"workload": f"configs[4]: {args.ep_tokens} tokens x {L} stacked Q4_0 MoE layers, experts "
                                    f"sharded {E_l} per GPU over {G} GPU(s), uniform top-8 routing",
                        "tokens_per_rank": T, "experts_per_rank": E_l, "scaling": "strong",
@@ -625,14 +725,28 @@ def prefill_bench(args, layers, torch, lib, Q, s, barrier):
 
 
 # ------------------------------------------------------------------ reference (CPU)
+_REF = {}
+
+
+def reference_engine():
+    """The reference engine (oracle/_ref), its thread pool on the host's physical cores (the pool
+    is process-global: the first initialisation fixes it, engine/kernels/parallel.c:126-132)."""
+    if "ref" not in _REF:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle as O
+        _REF["O"] = O
+        _REF["ref"] = O.Reference(threads=physical_cores())
+        _REF["orc"] = O.Oracle()
+    return _REF["O"], _REF["ref"], _REF["orc"]
+
+
 def reference_sample(n_layers: int, T: int, zipf, seed: int, steps: int, warmup: int, enc: int = ENC_Q4):
-    """The reference engine (oracle/_ref) on n_layers distinct layers, T tokens per pass; routers
-    Zipf-calibrated on the chained activations unless zipf is None."""
-    sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    import oracle as O
+    """The reference engine on n_layers distinct layers, T tokens per pass (one sampled step =
+    those layers in sequence, x += mlp after each, as run_layers does); routers Zipf-calibrated on
+    the chained activations unless zipf is None. Returns (per-step seconds of the timed steps,
+    threads)."""
+    O, ref, orc = reference_engine()
     from cachepotato_b200.workload import calibrate_router_scales, rmsnorm_rows
-    ref = O.Reference(threads=os.cpu_count() or 1)
-    orc = O.Oracle()
     x = orc.normal(T * D, seed, 1.0).reshape(T, D)
     layers = []
     xi = x
@@ -653,28 +767,32 @@ def reference_sample(n_layers: int, T: int, zipf, seed: int, steps: int, warmup:
         dt = time.perf_counter() - t0
         if i >= warmup:
             times.append(dt)
-    per_layer = float(np.sum(times)) / (len(times) * n_layers)
-    return per_layer, ref.threads
+    return times, ref.threads
+
+
+def reference_line(args, times, threads, n_layers):
+    """tok/s of the 48-layer step from the sampled steps (per-layer time x 48)."""
+    per_layer = float(np.mean(times)) / n_layers
+    return args.tokens / (per_layer * args.layers), per_layer
 
 
 def run_reference(args, rank):
     if rank != 0:
         return None
-    T, L = args.tokens, args.layers
-    per_layer, threads = reference_sample(args.cpu_sample_layers, T, args.zipf, args.seed,
-                                          args.steps, args.warmup)
-    tok_s = T / (per_layer * L)
+    T, L, n = args.tokens, args.layers, args.cpu_sample_layers
+    times, threads = reference_sample(n, T, args.zipf, args.seed, args.steps, args.warmup)
+    tok_s, per_layer = reference_line(args, times, threads, n)
+    sample = (f"{n} of {L} distinct layers per timed step (T={T}); ms_per_step is that sampled step, value "
+              f"scales its per-layer time to the {L}-layer step; {threads} threads = physical cores")
     return {
         "metric": METRIC, "impl": "reference", "value": round(tok_s, 3), "unit": "tok/s", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per_layer * L * 1e3, 2),
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(float(np.mean(times)) * 1e3, 2),
+        "layers_timed": n, "ms_per_layer": round(per_layer * 1e3, 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "q4_0 x f32 (AVX2 FMA)",
-        "data": "synthetic",
-        "config": {"workload": "Qwen3-30B-A3B MoE decode: 64-token batch through 48 stacked MoE layers "
-                               "(configs[1], Q4_0 experts, Zipf(1.1)-calibrated f32 router)",
-                   "tokens_per_step_per_gpu": T, "layers": L, "parallelism": "reference engine, 1 process"},
+        "data": "synthetic", "config": headline_config(args),
+        "parallelism": f"reference engine, 1 process, {threads} threads",
         "cpu_baseline": {"value": round(tok_s, 3), "unit": "tok/s", "cores": threads, "kind": "reference",
-                         "sample": f"{args.cpu_sample_layers} of {L} layers per step, T={T}; "
-                                   f"per-layer time x {L}"},
+                         "sample": sample},
         "e2e": {"value": round(tok_s, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
 
@@ -701,17 +819,19 @@ def main():
         torch.cuda.set_device(0)
     res = run_ours(args, rank, world, torch, dist)
     if rank == 0 and not args.no_cpu_baseline and world == 1:
-        per_layer, threads = reference_sample(args.cpu_sample_layers, args.tokens, args.zipf,
-                                              args.seed, 2, 1)
-        res["cpu_baseline"] = {"value": round(args.tokens / (per_layer * args.layers), 3), "unit": "tok/s",
-                               "cores": threads, "kind": "reference",
-                               "sample": f"reference engine, {args.cpu_sample_layers} layers x 2 reps, "
-                                         f"T={args.tokens}, per-layer time x {args.layers}"}
+        n = args.cpu_sample_layers
+        times, threads = reference_sample(n, args.tokens, args.zipf, args.seed, 5, 1)
+        tok_s, per_layer = reference_line(args, times, threads, n)
+        res["cpu_baseline"] = {"value": round(tok_s, 3), "unit": "tok/s", "cores": threads, "kind": "reference",
+                               "sample": f"reference engine, {n} of {args.layers} distinct layers x 5 timed reps, "
+                                         f"T={args.tokens}, per-layer time x {args.layers}; threads = physical cores",
+                               "ms_per_layer": round(per_layer * 1e3, 3)}
         if "decode_q8_batch1" in res:
-            pl8, th8 = reference_sample(args.cpu_sample_layers, 1, None, args.seed + 5, 3, 1, ENC_Q8)
+            t8, th8 = reference_sample(n, 1, None, args.seed + 5, 5, 1, ENC_Q8)
+            pl8 = float(np.mean(t8)) / n
             res["decode_q8_batch1"]["cpu_baseline"] = {
                 "value": round(1.0 / (pl8 * args.layers), 3), "unit": "tok/s", "cores": th8, "kind": "reference",
-                "sample": f"reference engine, Q8_0 experts, {args.cpu_sample_layers} layers x 3 reps, T=1, "
+                "sample": f"reference engine, Q8_0 experts, {n} layers x 5 timed reps, T=1, "
                           f"per-layer time x {args.layers}"}
     if res is not None:
         print(json.dumps(res), flush=True)

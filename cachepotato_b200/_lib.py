@@ -28,7 +28,7 @@ EXPORTS = [
     "cpg_ctx_run", "cpg_ctx_x", "cpg_ctx_topk", "cpg_ctx_profile", "cpg_ctx_phase_ms",
     "cpg_moe_apply_workspace_bytes", "cpg_moe_apply", "cpg_moe_apply_check", "cpg_moe_apply_profile",
     "cpg_moe_apply_rows", "cpg_ep_unique_id", "cpg_ep_create", "cpg_ep_destroy", "cpg_ep_workspace_bytes",
-    "cpg_moe_ep", "cpg_moe_ep_check",
+    "cpg_moe_ep", "cpg_moe_ep_check", "cpg_moe_ep_profile", "cpg_ep_set_timeout", "cpg_ep_abort", "cpg_ep_wait",
     "cpg_qwen3_create", "cpg_qwen3_destroy", "cpg_qwen3_prefill", "cpg_qwen3_step", "cpg_qwen3_generate",
     "cpg_qwen3_logits", "cpg_qwen3_stream", "cpg_qwen3_position",
 ]
@@ -115,6 +115,10 @@ _SIGS = {
     "cpg_ep_workspace_bytes": (_sz, [_vp, _vp, _i]),
     "cpg_moe_ep": (_i, [_vp, _vp, _vp, _i, _vp, _vp, _vp, _vp, _sz, _vp]),
     "cpg_moe_ep_check": (_i, [_vp, _vp]),
+    "cpg_moe_ep_profile": (_i, [_vp, _vp, _vp, _i, _vp, _vp, _vp, _vp, _sz, _vp, ctypes.POINTER(ctypes.c_float)]),
+    "cpg_ep_set_timeout": (_i, [_vp, _i]),
+    "cpg_ep_abort": (_i, [_vp]),
+    "cpg_ep_wait": (_i, [_vp, _vp]),
     "cpg_qwen3_create": (_i, [ctypes.POINTER(Qwen3Desc), ctypes.POINTER(_vp)]),
     "cpg_qwen3_destroy": (None, [_vp]),
     "cpg_qwen3_prefill": (_i, [_vp, _vp, _i, ctypes.POINTER(_i)]),

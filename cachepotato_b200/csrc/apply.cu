@@ -14,6 +14,9 @@
 
 namespace cpg {
 
+int apply_validate(const cpg_moe_layer *layer, int T, size_t ws_bytes);
+int apply_rows_impl(const cpg_moe_layer *layer, const void *rows_f16, int R, const int *slot_expert,
+                    const float *slot_wt, float *out, void *ws, size_t ws_bytes, cudaStream_t s);
 int layer_dims(const cpg_moe_layer *L, int *D, int *F, int *E, int *K);
 int layer_ptrs(const cpg_moe_layer *L, const uint8_t *const **ptrs, int *enc);
 int layer_weight_maps(const cpg_moe_layer *L, const void **maps);
@@ -45,13 +48,13 @@ static ApplyWs apply_layout(int D, int F, int E, int K, int T) {
     return w;
 }
 
-// per-block expert counts, id validation (negative ids are empty slots when empty_ok)
+// per-block expert counts, id validation (negative ids are empty slots when empty_ok). The
+// status words are cleared on the stream before this launch, so a bad id any block records stays.
 __global__ void __launch_bounds__(AP_BLOCK) k_apply_prep(int T, int E, int K, const int *__restrict__ idx,
                                                           int *__restrict__ blk_cnt, int *status, int empty_ok) {
     __shared__ int s_cnt[AP_MAX_E];
     const int b = blockIdx.x, t0 = b * AP_BLOCK;
     for (int e = threadIdx.x; e < E; e += blockDim.x) s_cnt[e] = 0;
-    if (b == 0 && threadIdx.x < 16) status[threadIdx.x] = 0;
     __syncthreads();
     const int nt = min(AP_BLOCK, T - t0);
     for (int i = threadIdx.x; i < nt * K; i += blockDim.x) {
@@ -192,13 +195,11 @@ extern "C" size_t cpg_moe_apply_workspace_bytes(const cpg_moe_layer *layer, int 
     return apply_layout(D, F, E, K, max_T).total;
 }
 
-// Input rows: xn (f32) or xh (fp16). empty_ok: negative ids are empty slots, not errors.
-// accumulate: mlp += the block output, else mlp = it. ev: null, or 5 events recorded around the
-// sort, gate/up, down and combine phases.
-static int apply_impl(const cpg_moe_layer *layer, const float *xn, const __half *xh, int T, const int *topk_idx,
-                      const float *wt, float *mlp, int accumulate, int empty_ok, void *ws, size_t ws_bytes,
-                      cudaStream_t s, cudaEvent_t *ev) {
-    CPG_REQUIRE(layer && (xn || xh) && topk_idx && wt && mlp && ws, "cpg_moe_apply: null argument");
+// Everything apply_impl rejects before it launches anything, and the layer's tensor maps built:
+// the expert-parallel path calls this before its first collective, so a bad argument can never
+// leave the peers waiting in a collective this rank does not join.
+int cpg::apply_validate(const cpg_moe_layer *layer, int T, size_t ws_bytes) {
+    CPG_REQUIRE(layer, "cpg_moe_apply: null layer");
     CPG_REQUIRE(T > 0, "cpg_moe_apply: T=%d", T);
     int D, F, E, K, enc;
     const uint8_t *const *ptrs;
@@ -210,12 +211,31 @@ static int apply_impl(const cpg_moe_layer *layer, const float *xn, const __half 
     CPG_REQUIRE(F % 256 == 0 && D % 256 == 0, "cpg_moe_apply: d_exp %% 256 and d_model %% 256 must be 0");
     const ApplyWs W = apply_layout(D, F, E, K, T);
     CPG_REQUIRE(ws_bytes >= W.total, "cpg_moe_apply: workspace %zu < %zu bytes for T=%d", ws_bytes, W.total, T);
+    const void *maps = nullptr;
+    return layer_weight_maps(layer, &maps);
+}
+
+// Input rows: xn (f32) or xh (fp16). empty_ok: negative ids are empty slots, not errors.
+// accumulate: mlp += the block output, else mlp = it. ev: null, or 5 events recorded around the
+// sort, gate/up, down and combine phases.
+static int apply_impl(const cpg_moe_layer *layer, const float *xn, const __half *xh, int T, const int *topk_idx,
+                      const float *wt, float *mlp, int accumulate, int empty_ok, void *ws, size_t ws_bytes,
+                      cudaStream_t s, cudaEvent_t *ev) {
+    CPG_REQUIRE(layer && (xn || xh) && topk_idx && wt && mlp && ws, "cpg_moe_apply: null argument");
+    int rc = apply_validate(layer, T, ws_bytes);
+    if (rc) return rc;
+    int D, F, E, K, enc;
+    const uint8_t *const *ptrs;
+    layer_dims(layer, &D, &F, &E, &K);
+    layer_ptrs(layer, &ptrs, &enc);
+    const ApplyWs W = apply_layout(D, F, E, K, T);
     CPG_REQUIRE((((uintptr_t)xn | (uintptr_t)xh | (uintptr_t)mlp | (uintptr_t)ws) & 15) == 0,
                 "cpg_moe_apply: 16-byte alignment");
     uint8_t *w = (uint8_t *)ws;
     int *status = (int *)(w + W.status);
     const int nblk = (T + AP_BLOCK - 1) / AP_BLOCK;
     if (ev) CPG_CUDA(cudaEventRecord(ev[0], s));
+    CPG_CUDA(cudaMemsetAsync(status, 0, 16 * sizeof(int), s));
     k_apply_prep<<<nblk, AP_BLOCK, 0, s>>>(T, E, K, topk_idx, (int *)(w + W.blk_cnt), status, empty_ok);
     CPG_CUDA(cudaGetLastError());
     k_apply_group<<<nblk, AP_BLOCK, 0, s>>>(T, E, K, topk_idx, (const int *)(w + W.blk_cnt), nblk, ptrs,
@@ -260,6 +280,13 @@ static int apply_impl(const cpg_moe_layer *layer, const float *xn, const __half 
 extern "C" int cpg_moe_apply(const cpg_moe_layer *layer, const float *xn, int T, const int *topk_idx,
                              const float *wt, float *mlp, void *ws, size_t ws_bytes, void *stream) {
     return apply_impl(layer, xn, nullptr, T, topk_idx, wt, mlp, 1, 0, ws, ws_bytes, (cudaStream_t)stream, nullptr);
+}
+
+int cpg::apply_rows_impl(const cpg_moe_layer *layer, const void *rows_f16, int R, const int *slot_expert,
+                         const float *slot_wt, float *out, void *ws, size_t ws_bytes, cudaStream_t s) {
+    CPG_REQUIRE(rows_f16, "cpg_moe_apply_rows: null rows");
+    return apply_impl(layer, nullptr, (const __half *)rows_f16, R, slot_expert, slot_wt, out, 0, 1, ws, ws_bytes, s,
+                      nullptr);
 }
 
 extern "C" int cpg_moe_apply_rows(const cpg_moe_layer *layer, const void *rows_f16, int R, const int *slot_expert,

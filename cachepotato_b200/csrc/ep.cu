@@ -17,6 +17,9 @@
 // resolved at run time, so the library itself links no NCCL.
 #include <dlfcn.h>
 #include <nccl.h>
+#include <stdlib.h>
+#include <string.h>
+#include <time.h>
 
 #include <mutex>
 
@@ -29,6 +32,10 @@ int layer_dims(const cpg_moe_layer *L, int *D, int *F, int *E, int *K);
 struct NcclApi {
     decltype(&ncclGetUniqueId) get_unique_id = nullptr;
     decltype(&ncclCommInitRank) init_rank = nullptr;
+    decltype(&ncclCommInitRankConfig) init_rank_config = nullptr;   // optional: non-blocking init
+    decltype(&ncclCommGetAsyncError) async_error = nullptr;          // optional
+    decltype(&ncclCommAbort) abort = nullptr;                        // optional
+    decltype(&ncclCommFinalize) finalize = nullptr;                  // optional
     decltype(&ncclCommDestroy) destroy = nullptr;
     decltype(&ncclGroupStart) group_start = nullptr;
     decltype(&ncclGroupEnd) group_end = nullptr;
@@ -47,6 +54,10 @@ static const NcclApi &nccl() {
         if (!h) return;
         api.get_unique_id = (decltype(api.get_unique_id))dlsym(h, "ncclGetUniqueId");
         api.init_rank = (decltype(api.init_rank))dlsym(h, "ncclCommInitRank");
+        api.init_rank_config = (decltype(api.init_rank_config))dlsym(h, "ncclCommInitRankConfig");
+        api.async_error = (decltype(api.async_error))dlsym(h, "ncclCommGetAsyncError");
+        api.abort = (decltype(api.abort))dlsym(h, "ncclCommAbort");
+        api.finalize = (decltype(api.finalize))dlsym(h, "ncclCommFinalize");
         api.destroy = (decltype(api.destroy))dlsym(h, "ncclCommDestroy");
         api.group_start = (decltype(api.group_start))dlsym(h, "ncclGroupStart");
         api.group_end = (decltype(api.group_end))dlsym(h, "ncclGroupEnd");
@@ -62,7 +73,7 @@ static const NcclApi &nccl() {
 #define CPG_NCCL(call)                                                                            \
     do {                                                                                          \
         const ncclResult_t r_ = (call);                                                           \
-        if (r_ != ncclSuccess) {                                                                  \
+        if (r_ != ncclSuccess && r_ != ncclInProgress) {                                          \
             ::cpg::set_error("%s: %s", #call, nccl().err_str(r_));                                \
             return CPG_ENCCL;                                                                     \
         }                                                                                         \
@@ -212,9 +223,87 @@ __global__ void __launch_bounds__(256) k_ep_combine(int T, int D, int G, const i
 struct cpg_ep {
     int G, rank, device;
     ncclComm_t comm;
+    bool nonblocking;      // communicator created with config.blocking = 0
+    bool aborted;          // ncclCommAbort was called: every later call fails with CPG_ENCCL
+    int timeout_ms;        // host deadline for NCCL's asynchronous steps (init, group launch, wait)
 };
 
 using namespace cpg;
+
+namespace cpg {
+
+// Monotonic milliseconds.
+static double now_ms() {
+    timespec ts;
+    clock_gettime(CLOCK_MONOTONIC, &ts);
+    return ts.tv_sec * 1e3 + ts.tv_nsec * 1e-6;
+}
+
+// Abort the communicator (NCCL stops its kernels in flight and frees the communicator); every
+// later call on this handle returns CPG_ENCCL. Peers blocked on this rank see their own
+// collectives fail or time out instead of waiting for ever.
+static void ep_abort(cpg_ep *ep) {
+    if (ep->aborted) return;
+    ep->aborted = true;
+    if (nccl().abort) nccl().abort(ep->comm);
+}
+
+// A non-blocking communicator finishes init and group launches in the background: poll its
+// state until it leaves ncclInProgress, giving up (and aborting) at the host deadline.
+static int ep_settle(cpg_ep *ep, const char *what) {
+    if (!ep->nonblocking || !nccl().async_error) return CPG_OK;
+    const double t0 = now_ms();
+    for (;;) {
+        ncclResult_t st = ncclSuccess;
+        const ncclResult_t r = nccl().async_error(ep->comm, &st);
+        if (r != ncclSuccess) st = r;
+        if (st == ncclSuccess) return CPG_OK;
+        if (st != ncclInProgress) {
+            set_error("%s: %s", what, nccl().err_str(st));
+            ep_abort(ep);
+            return CPG_ENCCL;
+        }
+        if (now_ms() - t0 > ep->timeout_ms) {
+            set_error("%s: not complete after %d ms (communicator aborted)", what, ep->timeout_ms);
+            ep_abort(ep);
+            return CPG_ETIMEOUT;
+        }
+        const timespec ns = {0, 20000};
+        nanosleep(&ns, nullptr);
+    }
+}
+
+// One grouped send/recv round. On any failure the group is still closed (a group left open
+// would swallow the caller's next NCCL calls) and the communicator is aborted, so no peer keeps
+// waiting on a transfer this rank will never post.
+struct P2P { void *buf; size_t count; ncclDataType_t type; int peer; bool send; };
+static int ep_group(cpg_ep *ep, const P2P *ops, int n, cudaStream_t s, const char *what) {
+    const NcclApi &api = nccl();
+    ncclResult_t r = api.group_start();
+    int failed = -1;
+    if (r == ncclSuccess || r == ncclInProgress) {
+        for (int i = 0; i < n; ++i) {
+            r = ops[i].send ? api.send(ops[i].buf, ops[i].count, ops[i].type, ops[i].peer, ep->comm, s)
+                            : api.recv(ops[i].buf, ops[i].count, ops[i].type, ops[i].peer, ep->comm, s);
+            if (r != ncclSuccess && r != ncclInProgress) { failed = i; break; }
+        }
+    }
+    const ncclResult_t re = api.group_end();
+    if (failed >= 0 || (r != ncclSuccess && r != ncclInProgress) || (re != ncclSuccess && re != ncclInProgress)) {
+        set_error("%s: %s", what, api.err_str(failed >= 0 || (r != ncclSuccess && r != ncclInProgress) ? r : re));
+        ep_abort(ep);
+        return CPG_ENCCL;
+    }
+    return ep_settle(ep, what);
+}
+
+static int ep_timeout_default() {
+    const char *e = getenv("CPG_EP_TIMEOUT_MS");
+    const int v = e ? atoi(e) : 0;
+    return v > 0 ? v : 120000;
+}
+
+}  // namespace cpg
 
 extern "C" int cpg_ep_unique_id(void *out) {
     CPG_REQUIRE(out, "cpg_ep_unique_id: null output");
@@ -241,12 +330,28 @@ extern "C" int cpg_ep_create(int nranks, int rank, const void *unique_id, cpg_ep
     cpg_ep *ep = new cpg_ep();
     ep->G = nranks;
     ep->rank = rank;
+    ep->timeout_ms = ep_timeout_default();
     cudaGetDevice(&ep->device);
-    const ncclResult_t r = nccl().init_rank(&ep->comm, nranks, id, rank);
-    if (r != ncclSuccess) {
+    ncclResult_t r;
+    if (nccl().init_rank_config && nccl().async_error && nccl().abort) {
+        // non-blocking: a peer that never joins ends in CPG_ETIMEOUT here, not a hung process
+        ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+        cfg.blocking = 0;
+        r = nccl().init_rank_config(&ep->comm, nranks, id, rank, &cfg);
+        ep->nonblocking = true;
+    } else {
+        r = nccl().init_rank(&ep->comm, nranks, id, rank);
+    }
+    if (r != ncclSuccess && r != ncclInProgress) {
         set_error("ncclCommInitRank: %s", nccl().err_str(r));
+        if (ep->nonblocking && ep->comm) nccl().abort(ep->comm);
         delete ep;
         return CPG_ENCCL;
+    }
+    const int rc = ep_settle(ep, "ncclCommInitRankConfig");
+    if (rc) {
+        delete ep;          // ep_settle aborted (and freed) the communicator
+        return rc;
     }
     *out = ep;
     return CPG_OK;
@@ -254,8 +359,65 @@ extern "C" int cpg_ep_create(int nranks, int rank, const void *unique_id, cpg_ep
 
 extern "C" void cpg_ep_destroy(cpg_ep *ep) {
     if (!ep) return;
-    nccl().destroy(ep->comm);
+    if (!ep->aborted) {
+        if (ep->nonblocking) {
+            // finish outstanding work first (bounded), then free; a stuck peer ends in an abort
+            bool ok = ep_settle(ep, "cpg_ep_destroy") == CPG_OK;
+            if (ok && nccl().finalize) {
+                const ncclResult_t r = nccl().finalize(ep->comm);
+                ok = (r == ncclSuccess || r == ncclInProgress) && ep_settle(ep, "ncclCommFinalize") == CPG_OK;
+                if (!ok) ep_abort(ep);
+            }
+            if (ok) nccl().destroy(ep->comm);
+        } else {
+            nccl().destroy(ep->comm);
+        }
+    }
     delete ep;
+}
+
+extern "C" int cpg_ep_abort(cpg_ep *ep) {
+    CPG_REQUIRE(ep, "cpg_ep_abort: null handle");
+    ep_abort(ep);
+    return CPG_OK;
+}
+
+extern "C" int cpg_ep_set_timeout(cpg_ep *ep, int timeout_ms) {
+    CPG_REQUIRE(ep && timeout_ms > 0, "cpg_ep_set_timeout: null handle or timeout %d ms", timeout_ms);
+    ep->timeout_ms = timeout_ms;
+    return CPG_OK;
+}
+
+extern "C" int cpg_ep_wait(cpg_ep *ep, void *stream) {
+    CPG_REQUIRE(ep, "cpg_ep_wait: null handle");
+    if (ep->aborted) {
+        set_error("cpg_ep_wait: the communicator was aborted");
+        return CPG_ENCCL;
+    }
+    cudaStream_t s = (cudaStream_t)stream;
+    const double t0 = now_ms();
+    for (;;) {
+        const cudaError_t ce = cudaStreamQuery(s);
+        if (ce == cudaSuccess) return ep_settle(ep, "cpg_ep_wait");
+        if (ce != cudaErrorNotReady) return cuda_fail(ce, "cpg_ep_wait: stream");
+        if (nccl().async_error) {
+            ncclResult_t st = ncclSuccess;
+            nccl().async_error(ep->comm, &st);
+            if (st != ncclSuccess && st != ncclInProgress) {
+                set_error("cpg_ep_wait: %s (communicator aborted)", nccl().err_str(st));
+                ep_abort(ep);
+                return CPG_ENCCL;
+            }
+        }
+        if (now_ms() - t0 > ep->timeout_ms) {
+            // a peer stopped taking part: abort, which ends this rank's NCCL kernels in flight
+            set_error("cpg_ep_wait: stream not done after %d ms (communicator aborted)", ep->timeout_ms);
+            ep_abort(ep);
+            return CPG_ETIMEOUT;
+        }
+        const timespec ns = {0, 50000};
+        nanosleep(&ns, nullptr);
+    }
 }
 
 extern "C" size_t cpg_ep_workspace_bytes(const cpg_ep *ep, const cpg_moe_layer *local_layer, int T) {
@@ -264,22 +426,36 @@ extern "C" size_t cpg_ep_workspace_bytes(const cpg_ep *ep, const cpg_moe_layer *
     return ep_layout(ep->G, T, D, K, cpg_moe_apply_workspace_bytes(local_layer, ep->G * T)).total;
 }
 
-extern "C" int cpg_moe_ep(cpg_ep *ep, const cpg_moe_layer *local_layer, const float *xn, int T, const int *topk_idx,
-                          const float *wt, float *mlp, void *ws, size_t ws_bytes, void *stream) {
+namespace cpg {
+int apply_validate(const cpg_moe_layer *layer, int T, size_t ws_bytes);
+int apply_rows_impl(const cpg_moe_layer *layer, const void *rows_f16, int R, const int *slot_expert,
+                    const float *slot_wt, float *out, void *ws, size_t ws_bytes, cudaStream_t s);
+
+// ev: null, or 6 events recorded before plan/pack, dispatch, owner experts, return, combine and
+// after the combine.
+static int ep_impl(cpg_ep *ep, const cpg_moe_layer *local_layer, const float *xn, int T, const int *topk_idx,
+                   const float *wt, float *mlp, void *ws, size_t ws_bytes, cudaStream_t s, cudaEvent_t *ev) {
     CPG_REQUIRE(ep && local_layer && xn && topk_idx && wt && mlp && ws, "cpg_moe_ep: null argument");
     CPG_REQUIRE(T > 0, "cpg_moe_ep: T=%d", T);
+    if (ep->aborted) {
+        set_error("cpg_moe_ep: the communicator was aborted");
+        return CPG_ENCCL;
+    }
     int D, F, E_l, K;
     int rc = layer_dims(local_layer, &D, &F, &E_l, &K);
     if (rc) return rc;
     CPG_REQUIRE(K <= EP_MAX_K, "cpg_moe_ep: topk %d > %d", K, EP_MAX_K);
-    const int G = ep->G;
+    const int G = ep->G, me = ep->rank;
     const size_t apply_bytes = cpg_moe_apply_workspace_bytes(local_layer, G * T);
     const EpWs W = ep_layout(G, T, D, K, apply_bytes);
     CPG_REQUIRE(ws_bytes >= W.total, "cpg_moe_ep: workspace %zu < %zu bytes", ws_bytes, W.total);
     CPG_REQUIRE((((uintptr_t)xn | (uintptr_t)mlp | (uintptr_t)ws) & 15) == 0, "cpg_moe_ep: 16-byte alignment");
-    cudaStream_t s = (cudaStream_t)stream;
+    // everything the owner step can reject, checked before the first collective
+    rc = apply_validate(local_layer, G * T, apply_bytes);
+    if (rc) return rc;
     uint8_t *w = (uint8_t *)ws;
     int *status = (int *)(w + W.status);
+    if (ev) CPG_CUDA(cudaEventRecord(ev[0], s));
     CPG_CUDA(cudaMemsetAsync(status, 0, 16 * sizeof(int), s));
     int *pos = (int *)(w + W.pos);
     k_ep_plan<<<G, EP_PLAN_THREADS, 0, s>>>(T, K, G, E_l, topk_idx, wt, pos, (int *)(w + W.send_ide),
@@ -290,49 +466,112 @@ extern "C" int cpg_moe_ep(cpg_ep *ep, const cpg_moe_layer *local_layer, const fl
     k_ep_pack_rows<<<pgrid, 256, 0, s>>>(T, D, G, xn, pos, (__half *)(w + W.send_rows));
     CPG_CUDA(cudaGetLastError());
 
-    // dispatch: rows + metadata to every owner (this rank's own share goes through NCCL too)
+    // dispatch: rows + metadata to every other owner through NCCL; this rank's own share is a
+    // device copy
     const size_t row_b = (size_t)T * D * sizeof(__half), meta_n = (size_t)T * K;
-    const NcclApi &n = nccl();
-    CPG_NCCL(n.group_start());
-    for (int p = 0; p < G; ++p) {
-        CPG_NCCL(n.send(w + W.send_rows + p * row_b, row_b, ncclUint8, p, ep->comm, s));
-        CPG_NCCL(n.send((int *)(w + W.send_ide) + p * meta_n, meta_n, ncclInt32, p, ep->comm, s));
-        CPG_NCCL(n.send((float *)(w + W.send_wt) + p * meta_n, meta_n, ncclFloat32, p, ep->comm, s));
-        CPG_NCCL(n.recv(w + W.recv_rows + p * row_b, row_b, ncclUint8, p, ep->comm, s));
-        CPG_NCCL(n.recv((int *)(w + W.recv_ide) + p * meta_n, meta_n, ncclInt32, p, ep->comm, s));
-        CPG_NCCL(n.recv((float *)(w + W.recv_wt) + p * meta_n, meta_n, ncclFloat32, p, ep->comm, s));
+    if (ev) CPG_CUDA(cudaEventRecord(ev[1], s));
+    CPG_CUDA(cudaMemcpyAsync(w + W.recv_rows + me * row_b, w + W.send_rows + me * row_b, row_b,
+                             cudaMemcpyDeviceToDevice, s));
+    CPG_CUDA(cudaMemcpyAsync((int *)(w + W.recv_ide) + me * meta_n, (int *)(w + W.send_ide) + me * meta_n,
+                             meta_n * sizeof(int), cudaMemcpyDeviceToDevice, s));
+    CPG_CUDA(cudaMemcpyAsync((float *)(w + W.recv_wt) + me * meta_n, (float *)(w + W.send_wt) + me * meta_n,
+                             meta_n * sizeof(float), cudaMemcpyDeviceToDevice, s));
+    if (G > 1) {
+        P2P ops[6 * 64];
+        int n = 0;
+        for (int p = 0; p < G && n + 6 <= 6 * 64; ++p) {
+            if (p == me) continue;
+            ops[n++] = {w + W.send_rows + p * row_b, row_b, ncclUint8, p, true};
+            ops[n++] = {(int *)(w + W.send_ide) + p * meta_n, meta_n, ncclInt32, p, true};
+            ops[n++] = {(float *)(w + W.send_wt) + p * meta_n, meta_n, ncclFloat32, p, true};
+            ops[n++] = {w + W.recv_rows + p * row_b, row_b, ncclUint8, p, false};
+            ops[n++] = {(int *)(w + W.recv_ide) + p * meta_n, meta_n, ncclInt32, p, false};
+            ops[n++] = {(float *)(w + W.recv_wt) + p * meta_n, meta_n, ncclFloat32, p, false};
+        }
+        CPG_REQUIRE(G <= 64, "cpg_moe_ep: at most 64 ranks");
+        rc = ep_group(ep, ops, n, s, "cpg_moe_ep dispatch");
+        if (rc) return rc;
     }
-    CPG_NCCL(n.group_end());
 
-    // the owner's experts over every received row (empty slots are -1)
-    rc = cpg_moe_apply_rows(local_layer, w + W.recv_rows, G * T, (const int *)(w + W.recv_ide),
-                            (const float *)(w + W.recv_wt), (float *)(w + W.out_rows), w + W.apply, apply_bytes, s);
-    if (rc) return rc;
+    // the owner's experts over every received row (empty slots are -1); arguments were checked
+    // above, so only a CUDA launch failure can end it here: the communicator is aborted then,
+    // which fails the peers' return exchange instead of leaving it waiting
+    if (ev) CPG_CUDA(cudaEventRecord(ev[2], s));
+    rc = apply_rows_impl(local_layer, w + W.recv_rows, G * T, (const int *)(w + W.recv_ide),
+                         (const float *)(w + W.recv_wt), (float *)(w + W.out_rows), w + W.apply, apply_bytes, s);
+    if (rc) {
+        ep_abort(ep);
+        return rc;
+    }
+    // the owner step's status word (bounded device waits) next to this call's own
+    CPG_CUDA(cudaMemcpyAsync(status + 1, w + W.apply, sizeof(int), cudaMemcpyDeviceToDevice, s));
 
-    // return: one partial row per (token, owner)
+    // return: one partial row per (token, owner); this rank's own rows by a device copy
     const size_t out_n = (size_t)T * D;
-    CPG_NCCL(n.group_start());
-    for (int p = 0; p < G; ++p) {
-        CPG_NCCL(n.send((float *)(w + W.out_rows) + p * out_n, out_n, ncclFloat32, p, ep->comm, s));
-        CPG_NCCL(n.recv((float *)(w + W.back) + p * out_n, out_n, ncclFloat32, p, ep->comm, s));
+    if (ev) CPG_CUDA(cudaEventRecord(ev[3], s));
+    CPG_CUDA(cudaMemcpyAsync((float *)(w + W.back) + me * out_n, (float *)(w + W.out_rows) + me * out_n,
+                             out_n * sizeof(float), cudaMemcpyDeviceToDevice, s));
+    if (G > 1) {
+        P2P ops[2 * 64];
+        int n = 0;
+        for (int p = 0; p < G; ++p) {
+            if (p == me) continue;
+            ops[n++] = {(float *)(w + W.out_rows) + p * out_n, out_n, ncclFloat32, p, true};
+            ops[n++] = {(float *)(w + W.back) + p * out_n, out_n, ncclFloat32, p, false};
+        }
+        rc = ep_group(ep, ops, n, s, "cpg_moe_ep return");
+        if (rc) return rc;
     }
-    CPG_NCCL(n.group_end());
 
+    if (ev) CPG_CUDA(cudaEventRecord(ev[4], s));
     int cgrid = (T * D / 4 + 255) / 256;
     if (cgrid > sm_count() * 8) cgrid = sm_count() * 8;
     k_ep_combine<<<cgrid, 256, 0, s>>>(T, D, G, pos, (const float *)(w + W.back), mlp);
     CPG_CUDA(cudaGetLastError());
+    if (ev) CPG_CUDA(cudaEventRecord(ev[5], s));
     return CPG_OK;
+}
+}  // namespace cpg
+
+extern "C" int cpg_moe_ep(cpg_ep *ep, const cpg_moe_layer *local_layer, const float *xn, int T, const int *topk_idx,
+                          const float *wt, float *mlp, void *ws, size_t ws_bytes, void *stream) {
+    return ep_impl(ep, local_layer, xn, T, topk_idx, wt, mlp, ws, ws_bytes, (cudaStream_t)stream, nullptr);
+}
+
+extern "C" int cpg_moe_ep_profile(cpg_ep *ep, const cpg_moe_layer *local_layer, const float *xn, int T,
+                                  const int *topk_idx, const float *wt, float *mlp, void *ws, size_t ws_bytes,
+                                  void *stream, float *phase_ms) {
+    CPG_REQUIRE(phase_ms, "cpg_moe_ep_profile: null phase_ms");
+    cudaEvent_t ev[6] = {};
+    for (int i = 0; i < 6; ++i) {
+        const cudaError_t ce = cudaEventCreate(&ev[i]);
+        if (ce != cudaSuccess) {
+            for (int j = 0; j < i; ++j) cudaEventDestroy(ev[j]);
+            return cuda_fail(ce, "cpg_moe_ep_profile: event");
+        }
+    }
+    int rc = ep_impl(ep, local_layer, xn, T, topk_idx, wt, mlp, ws, ws_bytes, (cudaStream_t)stream, ev);
+    if (rc == CPG_OK) rc = cpg_ep_wait(ep, stream);
+    for (int i = 0; rc == CPG_OK && i < 5; ++i) {
+        const cudaError_t e2 = cudaEventElapsedTime(&phase_ms[i], ev[i], ev[i + 1]);
+        if (e2 != cudaSuccess) rc = cuda_fail(e2, "cpg_moe_ep_profile: elapsed time");
+    }
+    for (int i = 0; i < 6; ++i) cudaEventDestroy(ev[i]);
+    return rc;
 }
 
 extern "C" int cpg_moe_ep_check(const void *ws, void *stream) {
     CPG_REQUIRE(ws, "cpg_moe_ep_check: null workspace");
-    int st = 0;
+    int st[2] = {0, 0};
     CPG_CUDA(cudaStreamSynchronize((cudaStream_t)stream));
-    CPG_CUDA(cudaMemcpy(&st, ws, sizeof(int), cudaMemcpyDeviceToHost));
-    if (st == ST_BAD_ITEM) {
+    CPG_CUDA(cudaMemcpy(st, ws, sizeof(st), cudaMemcpyDeviceToHost));
+    if (st[0] == ST_BAD_ITEM) {
         set_error("cpg_moe_ep: expert id outside [0, n_ranks * local experts) (those slots contributed zero)");
         return CPG_EINVAL;
+    }
+    if (st[1] != ST_OK) {
+        set_error("cpg_moe_ep: a bounded device wait in the owner's expert GEMMs gave up (status %d)", st[1]);
+        return CPG_ETIMEOUT;
     }
     return CPG_OK;
 }

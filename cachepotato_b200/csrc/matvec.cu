@@ -6,6 +6,8 @@
 // kernel-gate tolerance (rel 1e-5, tools/verify_q8_kernels.py). One warp per output row;
 // lanes take 64-value group pairs (36 B for Q4, 68 B for Q8, 4-byte aligned), x is staged in
 // shared memory, up to 8 vectors share each weight load.
+#include <algorithm>
+
 #include "common.cuh"
 
 namespace cpg {
@@ -371,16 +373,37 @@ k_matvec(float *__restrict__ out, const float *__restrict__ x, const uint8_t *__
     }
 }
 
+// f32 W·x of any shape and alignment (matmul_wx takes any n_in, kernels.c:84-95): one warp per
+// (token, output row), lane-strided scalar loads, fp32 FMA, a warp reduction.
+__global__ void __launch_bounds__(256) k_matvec_f32_any(float *__restrict__ out, const float *__restrict__ x,
+                                                        const float *__restrict__ w, int n_in, int n_out, int T) {
+    const int lane = threadIdx.x & 31;
+    const long nw = (long)gridDim.x * (blockDim.x >> 5);
+    for (long i = (long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); i < (long)T * n_out; i += nw) {
+        const int t = (int)(i / n_out), r = (int)(i - (long)t * n_out);
+        const float *row = w + (size_t)r * n_in, *xt = x + (size_t)t * n_in;
+        float acc = 0.0f;
+        for (int k = lane; k < n_in; k += 32) acc = fmaf(__ldg(row + k), __ldg(xt + k), acc);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+        if (lane == 0) out[(size_t)t * n_out + r] = acc;
+    }
+}
+
 int matvec_launch(float *out, const float *x, cpg_tensor w, int n_in, int n_out, int T,
                   cudaStream_t s) {
     CPG_REQUIRE(out && x && w.p, "cpg_matvec: null pointer");
     CPG_REQUIRE(n_in > 0 && n_out > 0 && T > 0, "cpg_matvec: empty shape (%d, %d, T=%d)", n_in, n_out, T);
     CPG_REQUIRE(w.enc == CPG_ENC_F32 || w.enc == CPG_ENC_Q4 || w.enc == CPG_ENC_Q8,
                 "cpg_matvec: unknown encoding %d", w.enc);
-    CPG_REQUIRE(w.enc == CPG_ENC_F32 ? n_in % 4 == 0 : n_in % 32 == 0,
-                "cpg_matvec: n_in=%d not a multiple of the group size", n_in);
-    if (w.enc == CPG_ENC_F32)
-        CPG_REQUIRE(((uintptr_t)w.p & 15) == 0, "cpg_matvec: f32 weights must be 16-byte aligned");
+    CPG_REQUIRE(w.enc == CPG_ENC_F32 || n_in % 32 == 0, "cpg_matvec: n_in=%d not a multiple of 32", n_in);
+    if (w.enc == CPG_ENC_F32 && (n_in % 4 != 0 || ((uintptr_t)w.p & 15) != 0)) {
+        long warps = (long)T * n_out;
+        int grid = (int)std::min<long>((warps + 7) / 8, (long)sm_count() * 16);
+        k_matvec_f32_any<<<grid, 256, 0, s>>>(out, x, (const float *)w.p, n_in, n_out, T);
+        CPG_CUDA(cudaGetLastError());
+        return CPG_OK;
+    }
     const long rb = row_bytes(w.enc, n_in);
     // decode-sized batches of quantised rows: the streaming kernel
     {

@@ -54,7 +54,9 @@ constexpr int KIND_BOTH = 2;     // gate/up then down items in one launch
 constexpr int EX_NW = 8;         // consumer warps per CTA
 constexpr int EX_NP = 2;         // producer warps: weight tiles, token rows (one issuing warp's
                                  // copies are served one after another on B200)
-constexpr int EX_NCH = 4;        // 8-column MMA tiles per item (four tokens each: hi and lo columns)
+constexpr int EX_NCH = 3;        // 8-column MMA tiles per item (four tokens each: hi and lo columns);
+                                 // 12 tokens per item measured ahead of 8 and 16 (two 35 KB or
+                                 // three 26 KB stages per CTA against three 31 KB ones)
 constexpr int EX_NCHUNK = 4 * EX_NCH;   // tokens per item (an expert with more is split)
 constexpr int EX_GROUP_MAX = 1024;       // pairs the gate/up kernel groups itself (T ≤ 128)
 constexpr int R_CLUSTER_MAX = 16;        // router CTAs per token tile (one cluster)
@@ -1027,8 +1029,7 @@ __global__ void __launch_bounds__((EX_NP + EX_NW) * 32, 2) k_experts(ExpertArgs 
         switch (ntl) {
             case 1: slice_mma<ENC, 1, TS>(tp, lane, bs, acc); break;
             case 2: slice_mma<ENC, 2, TS>(tp, lane, bs, acc); break;
-            case 3: slice_mma<ENC, 3, TS>(tp, lane, bs, acc); break;
-            default: slice_mma<ENC, 4, TS>(tp, lane, bs, acc); break;
+            default: slice_mma<ENC, 3, TS>(tp, lane, bs, acc); break;
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[st]);           // this warp is done with the stage
@@ -1158,8 +1159,8 @@ static int plan_kernel(KernelPlan &p, bool deep) {
     cudaFuncAttributes fa;
     CPG_CUDA(cudaFuncGetAttributes(&fa, k));
     const size_t limit = (size_t)smem_optin() - fa.sharedSizeBytes;
-    // two CTAs per SM (latency hiding comes from warps); stages fill about 100 KB per CTA (two
-    // 35 KB Q4_0 stages; Q8_0's 51 KB stages leave room for one CTA per SM). Deep: one CTA per
+    // two CTAs per SM (latency hiding comes from warps); stages fill about 100 KB per CTA (three
+    // 31 KB Q4_0 stages; Q8_0's 48 KB stages leave room for one CTA per SM). Deep: one CTA per
     // SM, as many stages as fit (up to 8 = every K slice of a gate/up item in flight)
     int S = (int)(((deep ? limit : 100 * 1024) - fixed) / C::STAGE);
     if (S < 2) S = 2;

@@ -252,6 +252,54 @@ def moe_apply_rows(layer: "MoELayer", rows_f16, slot_expert, slot_wt, *, ws=None
     return out
 
 
+class PeerLost(RuntimeError):
+    """A rank of the expert-parallel group left or stopped answering its heartbeat."""
+
+
+class EpHeartbeat:
+    """Host-side liveness of an expert-parallel group, over a key-value store every rank reaches
+    (torch.distributed.TCPStore / FileStore or anything with set(key, value) and check(keys)).
+
+    Before each step (e.g. each batch through the stacked layers) every rank calls step(): it
+    publishes that it reached the step and waits, up to `timeout_s`, until every peer has too.
+    A peer that called leave() is noticed at once, one that died is noticed at the deadline;
+    either way step() raises PeerLost BEFORE this rank enqueues the step's collectives, so no
+    NCCL transfer is ever posted towards a peer that is gone (the caller then aborts its
+    communicator with ExpertParallel.abort()). The reference engine is single-process and has
+    no counterpart; its error contract (NULL + message or rc < 0, never a hang,
+    engine/api/cachepotato.h:44-69) is the model."""
+
+    def __init__(self, store, rank: int, nranks: int, timeout_s: float = 30.0, prefix: str = "cpg_ep"):
+        self.store, self.rank, self.nranks = store, rank, nranks
+        self.timeout_s, self.prefix, self.n = float(timeout_s), prefix, 0
+
+    def _key(self, what: str, r: int) -> str:
+        return f"{self.prefix}/{what}/{r}"
+
+    def step(self) -> int:
+        import time
+        n = self.n
+        self.store.set(self._key(f"step{n}", self.rank), "1")
+        peers = [p for p in range(self.nranks) if p != self.rank]
+        want = [self._key(f"step{n}", p) for p in peers]
+        t0 = time.monotonic()
+        while True:
+            if not want or self.store.check(want):
+                self.n += 1
+                return n
+            gone = [p for p in peers if self.store.check([self._key("left", p)])]
+            if gone:
+                raise PeerLost(f"rank(s) {gone} left the expert-parallel group before step {n}")
+            if time.monotonic() - t0 > self.timeout_s:
+                late = [p for p in peers if not self.store.check([self._key(f"step{n}", p)])]
+                raise PeerLost(f"rank(s) {late} did not reach step {n} within {self.timeout_s:.1f} s")
+            time.sleep(0.001)
+
+    def leave(self) -> None:
+        """Announce that this rank takes no further steps (call between steps)."""
+        self.store.set(self._key("left", self.rank), "1")
+
+
 class ExpertParallel:
     """cpg_ep: one rank of an expert-parallel group (one process per GPU). Rank r's local layer
     holds experts [r*E_l, (r+1)*E_l) of the full layer; every rank passes the same T."""
@@ -262,11 +310,13 @@ class ExpertParallel:
         check(lib().cpg_ep_unique_id(buf))
         return buf.raw
 
-    def __init__(self, nranks: int, rank: int, uid: bytes):
+    def __init__(self, nranks: int, rank: int, uid: bytes, timeout_ms: int | None = None):
         assert len(uid) == 128
         h = ctypes.c_void_p()
         check(lib().cpg_ep_create(nranks, rank, ctypes.create_string_buffer(uid, 128), ctypes.byref(h)))
         self.handle, self.nranks, self.rank = h, nranks, rank
+        if timeout_ms is not None:
+            check(lib().cpg_ep_set_timeout(self.handle, int(timeout_ms)))
 
     def workspace(self, local_layer: "MoELayer", T: int):
         torch = _torch()
@@ -274,8 +324,10 @@ class ExpertParallel:
                            device="cuda")
 
     def forward(self, local_layer: "MoELayer", xn, topk_idx, wt, *, mlp=None, ws=None, stream=None,
-                check_status=True):
-        """mlp += the MoE block over this rank's T tokens (global expert ids in topk_idx)."""
+                check_status=True, phase_ms=None):
+        """mlp += the MoE block over this rank's T tokens (global expert ids in topk_idx).
+        phase_ms: a list to receive the five phase times (plan + pack, dispatch, owner experts,
+        return, combine; synchronising)."""
         torch = _torch()
         xn = xn.contiguous()
         T = xn.shape[0]
@@ -286,11 +338,27 @@ class ExpertParallel:
         if mlp is None:
             mlp = torch.zeros((T, local_layer.d_model), dtype=torch.float32, device=xn.device)
         sp = _stream_ptr(stream)
-        check(lib().cpg_moe_ep(self.handle, local_layer.handle, xn.data_ptr(), T, idx.data_ptr(), wt.data_ptr(),
-                               mlp.data_ptr(), ws.data_ptr(), ws.numel(), sp))
+        if phase_ms is not None:
+            ph = (ctypes.c_float * 5)()
+            check(lib().cpg_moe_ep_profile(self.handle, local_layer.handle, xn.data_ptr(), T, idx.data_ptr(),
+                                           wt.data_ptr(), mlp.data_ptr(), ws.data_ptr(), ws.numel(), sp, ph))
+            phase_ms[:] = list(ph)
+        else:
+            check(lib().cpg_moe_ep(self.handle, local_layer.handle, xn.data_ptr(), T, idx.data_ptr(), wt.data_ptr(),
+                                   mlp.data_ptr(), ws.data_ptr(), ws.numel(), sp))
         if check_status:
+            self.wait(stream)
             check(lib().cpg_moe_ep_check(ws.data_ptr(), sp))
         return mlp
+
+    def wait(self, stream=None) -> None:
+        """Bounded wait for this rank's enqueued EP work (aborts the communicator at the deadline)."""
+        check(lib().cpg_ep_wait(self.handle, _stream_ptr(stream)))
+
+    def abort(self) -> None:
+        """ncclCommAbort: for a rank that learned (EpHeartbeat) that a peer is gone."""
+        if self.handle is not None and self.handle.value:
+            check(lib().cpg_ep_abort(self.handle))
 
     def close(self) -> None:
         if self.handle is not None and self.handle.value:

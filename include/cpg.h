@@ -200,18 +200,40 @@ int cpg_moe_apply_rows(const cpg_moe_layer *layer, const void *rows_f16, int R, 
  * cpg_ep_create on every rank with the device current. */
 typedef struct cpg_ep cpg_ep;
 int cpg_ep_unique_id(void *out128);
+/* Creates the communicator non-blocking where NCCL offers it (ncclCommInitRankConfig with
+   blocking = 0): a peer that never joins ends in CPG_ETIMEOUT after the rank's deadline (120 s,
+   or CPG_EP_TIMEOUT_MS from the environment), with the communicator aborted, not in a hang. */
 int cpg_ep_create(int nranks, int rank, const void *unique_id128, cpg_ep **out);
+/* Frees the communicator after its outstanding work (bounded by the deadline, then aborted). */
 void cpg_ep_destroy(cpg_ep *ep);
+/* The host deadline (milliseconds) for this rank's asynchronous NCCL steps and cpg_ep_wait. */
+int cpg_ep_set_timeout(cpg_ep *ep, int timeout_ms);
+/* ncclCommAbort: NCCL ends this rank's collectives in flight and frees the communicator; every
+   later call on `ep` returns CPG_ENCCL (destroy still frees the handle). For a caller that
+   learned on the host that a peer is gone (a heartbeat or store), before its next launch. */
+int cpg_ep_abort(cpg_ep *ep);
+/* Wait (polling, bounded by the deadline) until `stream` has finished this rank's EP work.
+   CPG_OK; CPG_ENCCL if NCCL reported an asynchronous error; CPG_ETIMEOUT if the stream was not
+   done by the deadline (a peer stopped taking part). Both abort the communicator first, so
+   the stream drains. */
+int cpg_ep_wait(cpg_ep *ep, void *stream);
 size_t cpg_ep_workspace_bytes(const cpg_ep *ep, const cpg_moe_layer *local_layer, int T);
 /* mlp[t] += sum_j wt[t,j] · expert_{topk_idx[t,j]}(xn[t]) with global expert ids, the experts
  * computed on their owners: each token's row travels once per owner (fp16), each owner returns
  * one f32 row per token combining that token's slots on it in slot order, and the source adds
  * the owners' rows in ascending rank. Collective: every rank calls it in the same order.
- * Returns CPG_ENCCL on an NCCL error. */
+ * Every argument is checked before the first collective (a rejected call posts no transfer).
+ * Returns CPG_ENCCL on an NCCL error, after which the communicator is aborted (no open group,
+ * no peer left waiting on a transfer this rank will not post). */
 int cpg_moe_ep(cpg_ep *ep, const cpg_moe_layer *local_layer, const float *xn, int T, const int *topk_idx,
                const float *wt, float *mlp, void *ws, size_t ws_bytes, void *stream);
+/* cpg_moe_ep with CUDA events around its phases; waits (cpg_ep_wait) and writes phase_ms[5]:
+   plan + pack, dispatch, owner experts, return, combine (milliseconds). */
+int cpg_moe_ep_profile(cpg_ep *ep, const cpg_moe_layer *local_layer, const float *xn, int T,
+                       const int *topk_idx, const float *wt, float *mlp, void *ws, size_t ws_bytes,
+                       void *stream, float *phase_ms);
 /* Synchronise; CPG_EINVAL if an expert id was outside [0, nranks·E_l) (those slots contributed
-   zero). */
+   zero); CPG_ETIMEOUT if a bounded device wait in the owner's expert GEMMs gave up. */
 int cpg_moe_ep_check(const void *ws, void *stream);
 
 /* ============================================================== the whole model (config 3)

@@ -19,7 +19,11 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_SO = os.path.join(HERE, "_build", "libcpg_oracle.so")
 REF_SO = os.path.join(HERE, "_ref", "libcpref.so")
-REF_TREE = os.environ.get("CPG_REFERENCE_TREE", "/root/reference")
+REF_GPU_SO = os.path.join(HERE, "_ref", "libcpref_gpu.so")
+# The reference source tree: CPG_REFERENCE_TREE, else a `reference` checkout beside this
+# repository (where the build environment keeps it). Absent on machines that only run the
+# prebuilt checkers.
+REF_TREE = os.environ.get("CPG_REFERENCE_TREE") or os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference")
 
 ENC_F32, ENC_Q8, ENC_Q4 = 0, 8, 4
 GROUP_BYTES = {ENC_Q4: 18, ENC_Q8: 34}
@@ -31,10 +35,13 @@ _vpp = ctypes.POINTER(ctypes.c_void_p)
 
 
 def build(ref: bool = True) -> None:
-    """Compile the checkers (the restatement always; the reference when its tree is here)."""
+    """Compile the checkers (the restatement always; the reference when its tree is here, and
+    its drop-in build linked to libcpg_b200.so when that library exists)."""
     targets = ["oracle"]
     if ref and os.path.isdir(os.path.join(REF_TREE, "engine")):
         targets.append("ref")
+        if os.path.exists(os.path.join(os.path.dirname(HERE), "cachepotato_b200", "_build", "libcpg_b200.so")):
+            targets.append("ref_gpu")
     subprocess.run(["make", "-s", "-C", HERE, f"REF={REF_TREE}", *targets], check=True)
 
 

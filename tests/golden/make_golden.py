@@ -10,6 +10,8 @@ and its compiled engine exist; the GPU box only reads the .npz files).
                     on seeded synthetic inputs
   moe_ref.npz       the reference engine's qwen3_layer_kv (engine/blocks/qwen3_moe.c:87-229)
                     on seeded synthetic layers: router logits, top-k ids, MoE output
+  moe_zipf_ref.npz  the same for the 64-token headline batch (Zipf(1.1)-calibrated router, its
+                    per-expert router scales stored with the outputs)
   apply_ref.npz     the reference's expert loop on externally drawn routing
 
 Synthetic weights and activations come from the oracle's counter-based generator
@@ -55,6 +57,21 @@ MATVEC_CASES = [
     ("f32_router", O.ENC_F32, 2048, 128, 38),
 ]
 APPLY_CASE = ("apply_q4", 256, 256, 16, 4, O.ENC_Q4, 40, 41)
+# the headline decode batch: 64 tokens, full shape, Q4_0, router rows scaled so the top-8 load
+# follows Zipf(1.1) (scales computed here and stored, so the GPU test rebuilds the same layer)
+ZIPF_CASE = ("zipf_q4_t64", 2048, 768, 128, 8, O.ENC_Q4, 64, 77)
+
+
+def zipf_case_layer(orc, scale=None):
+    """The ZIPF_CASE layer and its input x; with scale None the scales are calibrated here."""
+    sys.path.insert(0, ROOT)
+    from cachepotato_b200.workload import calibrate_router_scales, rmsnorm_rows
+    name, D, F, E, K, enc, T, seed = ZIPF_CASE
+    x = orc.normal(T * D, 4242, 1.0).reshape(T, D)
+    if scale is None:
+        L0 = O.SynthLayer(D, F, E, K, enc, seed=seed, oracle=orc)
+        scale = calibrate_router_scales(rmsnorm_rows(x) @ L0.wgate.T, K, 1.1, seed=5)
+    return O.SynthLayer(D, F, E, K, enc, seed=seed, oracle=orc, router_scale=scale), x, scale
 
 
 def moe_inputs(d_model, T, seed, orc):
@@ -139,6 +156,11 @@ def main():
         for k, v in r.items():
             moe[f"{name}_{k}"] = v
     np.savez_compressed(os.path.join(HERE, "moe_ref.npz"), **moe)
+
+    layer, x, scale = zipf_case_layer(orc)
+    r = ref.qwen3_moe(layer, x)
+    np.savez_compressed(os.path.join(HERE, "moe_zipf_ref.npz"), threads=np.array(ref.threads),
+                        router_scale=scale.astype(np.float32), **r)
 
     name, D, F, E, K, enc, T, seed = APPLY_CASE
     layer = O.SynthLayer(D, F, E, K, enc, seed=seed, oracle=orc)

@@ -21,6 +21,8 @@ import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 OUT = os.path.join(HERE, "route_check.npz")
+sys.path.insert(0, os.path.join(os.path.dirname(os.path.dirname(HERE)), "oracle"))
+import oracle as O  # noqa: E402  (only for the reference tree's location)
 
 
 def bf16(x: np.ndarray) -> np.ndarray:
@@ -64,7 +66,7 @@ def make_layers(seed: int = 5, L: int = 6, T: int = 40, E: int = 128, K: int = 8
 
 
 def main():
-    ref = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    ref = sys.argv[1] if len(sys.argv) > 1 else O.REF_TREE
     layers = make_layers()
     arrays = {"meta": json.dumps({"layers": len(layers), "dtype": "bf16"})}
     for i, (lg, top, w) in enumerate(layers):

@@ -91,3 +91,77 @@ def test_ep_plan_layout():
     assert ide[0, 0].tolist() == [0, -1, -1, 1] and ide[1, 0].tolist() == [-1, 1, 2, -1]
     assert ide[1, 1].tolist() == [0, 1, 2, 3] and ide[0, 1].tolist() == [0, 1, 2, 3]
     assert (ide[0, 2] == -1).all() and (w[0, 2] == 0).all()
+
+
+# ------------------------------------------------------------------ a rank that leaves
+def _leaver(rank, G, port, sport, mode, out_path):
+    """Steps of the EP protocol, each gated by the host heartbeat; rank 1 stops after step 1
+    (mode 'leave': announces it; mode 'die': exits silently). Rank 0 must raise PeerLost at
+    step 2 without entering that step's collective."""
+    import sys
+    import time
+    here = os.path.dirname(os.path.abspath(__file__))
+    sys.path[:0] = [os.path.dirname(here), os.path.join(os.path.dirname(here), "oracle"), here]
+    import torch.distributed as dist
+    import oracle as O
+    import ep_model
+    from cachepotato_b200.qwen3 import EpHeartbeat, PeerLost
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=G)
+    store = dist.TCPStore("127.0.0.1", sport, G, rank == 0)
+    hb = EpHeartbeat(store, rank, G, timeout_s=3.0, prefix=f"t_{mode}")
+    orc = O.Oracle()
+    L = O.SynthLayer(D, F, E, K, O.ENC_Q4, seed=5, oracle=orc)
+    xn = orc.normal(T * D, 6 + rank, 1.0).reshape(T, D)
+    idx, wt = _routing(G, 7, False)
+    sl = slice(rank * T, (rank + 1) * T)
+
+    def exchange(parts):
+        send = torch.from_numpy(np.ascontiguousarray(np.stack(parts)))
+        recv = torch.empty_like(send)
+        dist.all_to_all_single(recv, send)
+        return list(recv.numpy())
+
+    steps_done = 0
+    for step in range(4):
+        if rank == 1 and step == 2:
+            if mode == "leave":
+                hb.leave()
+            os._exit(0)                      # between steps: nothing of this rank in flight
+        t0 = time.monotonic()
+        try:
+            hb.step()
+        except PeerLost as e:
+            with open(out_path, "w") as f:
+                f.write(f"{steps_done} {time.monotonic() - t0:.3f} {e}")
+            os._exit(0)                      # the collective of this step was never entered
+        ep_model.run_rank(orc, L.shard(rank, G), xn, idx[sl], wt[sl], G, exchange)
+        steps_done += 1
+    with open(out_path, "w") as f:
+        f.write(f"{steps_done} 0 no PeerLost")
+    os._exit(0)
+
+
+@pytest.mark.parametrize("mode", ["leave", "die"])
+def test_ep_peer_lost_between_steps_is_reported_not_hung(mode):
+    import time
+    import torch.multiprocessing as mp
+    out_dir = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_build")
+    os.makedirs(out_dir, exist_ok=True)
+    out = os.path.join(out_dir, f"ep_peer_lost_{mode}.txt")
+    if os.path.exists(out):
+        os.unlink(out)
+    ctx = mp.start_processes(_leaver, args=(2, _free_port(), _free_port(), mode, out), nprocs=2, join=False,
+                             start_method="spawn")
+    deadline = time.monotonic() + 120
+    while not ctx.join(timeout=1):
+        if time.monotonic() > deadline:
+            for p in ctx.processes:
+                if p.is_alive():
+                    p.terminate()
+            pytest.fail("ranks did not finish: the survivor hung")
+    done, waited, msg = open(out).read().split(" ", 2)
+    assert int(done) == 2, msg                       # steps 0 and 1 ran on both ranks
+    assert "PeerLost" not in msg and ("left" in msg if mode == "leave" else "did not reach" in msg), msg
+    # a rank that announced its departure is noticed at once, a silent one at the deadline
+    assert float(waited) < (1.5 if mode == "leave" else 10.0), waited

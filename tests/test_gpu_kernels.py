@@ -155,3 +155,16 @@ def test_region_store_translates_host_mapping(q, orc):
         assert np.array_equal(out_dev.cpu().numpy().view(np.uint32), want.view(np.uint32))
     finally:
         L.cpg_store_close()
+
+
+@pytest.mark.parametrize("n_in,n_out,shift", [(2, 2048, 0), (37, 19, 1), (2048, 2, 3)])
+def test_f32_matvec_any_shape(q, orc, n_in, n_out, shift):
+    """matmul_wx takes any n_in and any row alignment (kernels.c:84-95; the reference's own
+    attention uses (D, 2) f32 tensors): odd widths and weights shifted off 16 bytes."""
+    ref = O.Reference(threads=8)
+    buf = orc.normal(n_in * n_out + shift, 70 + n_in, 0.02)
+    w = buf[shift:]                                   # shift floats: 4-byte aligned only
+    x = orc.normal(n_in, 71 + n_in, 1.0)
+    out = np.empty(n_out, np.float32)
+    q.matmul_wx(out, x, w, n_in, n_out)
+    assert max_rel(out, ref.mm(np.ascontiguousarray(w), O.ENC_F32, x, n_in, n_out)) <= KERNEL_TOL

@@ -140,3 +140,15 @@ def test_phase_profile(orc, layers):
     ms = ctx.phase_ms()
     # T=64: gate/up and down items share one launch (timed as the gate/up phase)
     assert ms[0] > 0 and ms[1] > 0 and ms[2] >= 0 and ms[3] > 0 and ms[1] > ms[3]
+
+
+def test_block_zipf_t64_vs_reference_engine(orc, golden):
+    """The headline batch (64 tokens, Zipf(1.1)-calibrated router, full shape, Q4_0) against the
+    reference engine's own qwen3_layer_kv output (tests/golden/moe_zipf_ref.npz)."""
+    g = golden("moe_zipf_ref.npz")
+    L, x, _ = MG.zipf_case_layer(orc, scale=g["router_scale"])
+    got = device_layer(L).forward(torch.from_numpy(x).cuda())
+    want = {k: g[k] for k in ("router", "topk_idx", "mlp")}
+    err = _compare(got, want, L.topk)
+    counts = np.bincount(want["topk_idx"].ravel(), minlength=L.n_experts)
+    assert counts.max() > 32 and err <= DECODE_TOL     # experts spanning several token chunks

@@ -83,3 +83,27 @@ def test_apply_rejects_bad_expert_ids(orc):
     with pytest.raises(CpgError):
         moe_apply(device_layer(L), torch.from_numpy(xn).cuda(), torch.from_numpy(idx).cuda(),
                   torch.from_numpy(wt).cuda())
+
+
+def test_apply_bench_config_T4096_sampled():
+    """The prefill benchmark's own batch: 4096 tokens routed by zipf_assignment(4096, 128, 8, 1.2,
+    20.0, seed 1234 + 77) (groups of about 90-890 tokens, up to four 256-token tiles per expert),
+    checked on 320 tokens against the reference engine's expert loop (qwen3_moe.c:199-222 with
+    the routing given): every token of the largest group's last token tile, and random others."""
+    ref = O.Reference(threads=16)
+    orc = O.Oracle()
+    D, F, E, K, T = 2048, 768, 128, 8, 4096
+    L = O.SynthLayer(D, F, E, K, O.ENC_Q4, seed=1277, oracle=orc)
+    xn = orc.normal(T * D, 1278, 1.0).reshape(T, D)
+    idx, wt = zipf_assignment(T, E, K, 1.2, 20.0, 1234 + 77)
+    got = _apply(device_layer(L), xn, idx, wt)
+    counts = np.bincount(idx.ravel(), minlength=E)
+    big = int(counts.argmax())
+    members = np.nonzero((idx == big).any(1))[0]               # tokens ascending, as the sort keeps them
+    last_tile = members[(len(members) - 1) // 256 * 256:]
+    assert counts.max() > 768 and len(last_tile) > 0           # a fourth token tile exists
+    rest = np.setdiff1d(np.arange(T), last_tile)
+    sample = np.sort(np.concatenate([last_tile, np.random.default_rng(6).choice(rest, 320 - len(last_tile),
+                                                                                 replace=False)]))
+    want = ref.moe_apply(L, xn[sample], idx[sample], wt[sample])
+    assert max_rel(got[sample], want) <= BLOCK_TOL

@@ -147,3 +147,13 @@ def test_routing_agreement_excuses_only_near_tied_swaps():
     assert check_topk(np.array([[0, 1, 2, 4]], np.int32), want2, logits2, K) == []
     # a repeated id is never accepted
     assert check_topk(np.array([[0, 1, 2, 2]], np.int32), want2, logits2, K) == [0]
+
+
+def test_oracle_zipf_t64_vs_reference_engine(orc, golden):
+    """The C restatement on the headline 64-token Zipf batch against the reference engine."""
+    import make_golden as MG
+    g = golden("moe_zipf_ref.npz")
+    L, x, _ = MG.zipf_case_layer(orc, scale=g["router_scale"])
+    r = orc.qwen3_moe(L, x)
+    assert np.array_equal(r["topk_idx"], g["topk_idx"])
+    assert np.abs(r["mlp"] - g["mlp"]).max() / np.abs(g["mlp"]).max() <= 1e-5
