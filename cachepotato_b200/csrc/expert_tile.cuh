@@ -1,0 +1,162 @@
+// expert_tile.cuh — the decode tile layout of expert matrices and its register decoders,
+// shared by the expert kernels (moe.cu) and the one-token layer kernel (moe_one.cu).
+#pragma once
+#include "common.cuh"
+#include "layout.cuh"
+
+namespace cpg {
+
+constexpr int EX_KSL = 256;       // values per K slice of a decode tile (eight 32-value groups)
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// The reference's top-k scan (engine/blocks/qwen3_moe.c:184-194) by one warp over probabilities
+// held PL per lane (expert lane + 32 i): for each slot j the scan starts from the lowest-id
+// expert not yet taken and moves only to a strictly larger probability, so ties keep the lower
+// id, a NaN never wins, and a NaN first candidate stays selected. Returns the ids and their
+// probabilities in selection order (valid on every lane).
+template <int PL, int MAXK>
+__device__ __forceinline__ void warp_topk(const float (&p)[PL], int E, int K, int (&sel_e)[MAXK],
+                                          float (&sel_p)[MAXK]) {
+    const int lane = threadIdx.x & 31;
+    uint32_t taken = 0;                       // bit i: expert lane + 32 i already selected
+    for (int j = 0; j < K && j < MAXK; ++j) {
+        float bv = -1.0f;                     // probabilities are >= 0 (or NaN)
+        int be = 0x7fffffff, first = 0x7fffffff;
+#pragma unroll
+        for (int i = 0; i < PL; ++i) {
+            const int e = lane + 32 * i;
+            if (e < E && !((taken >> i) & 1u)) {
+                if (e < first) first = e;
+                if (p[i] > bv) { bv = p[i]; be = e; }
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {     // larger probability wins, equal: lower id
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oe = __shfl_xor_sync(0xffffffffu, be, o);
+            const int of = __shfl_xor_sync(0xffffffffu, first, o);
+            if (ov > bv || (ov == bv && oe < be)) { bv = ov; be = oe; }
+            if (of < first) first = of;
+        }
+        // the scan's starting point keeps the slot if its probability is NaN (nothing compares
+        // larger) or if no number beat it
+        float mine = 0.0f;                    // this lane's value in the first candidate's column
+#pragma unroll
+        for (int i = 0; i < PL; ++i)
+            if (i == (first >> 5)) mine = p[i];
+        const float pf = __shfl_sync(0xffffffffu, mine, first & 31);
+        if (first < E && (isnan(pf) || be >= E)) { be = first; bv = pf; }
+        if ((be & 31) == lane && be < E) taken |= 1u << (be >> 5);
+        sel_p[j] = bv;
+        sel_e[j] = be;
+    }
+}
+
+template <int ENC>
+__device__ __forceinline__ void load_pair_words(const uint32_t *row, int P, int t, uint32_t &w1,
+                                                uint32_t &w2, uint32_t &w3, uint32_t &w4, float &d0,
+                                                float &d1) {
+    if (ENC == CPG_ENC_Q4) {
+        const uint32_t *s = row + P * 9;
+        const uint32_t wa = s[1 + t], w0 = s[0], wq = s[4], wb = s[5 + t];
+        w1 = t == 3 ? __byte_perm(w0, wq, 0x5432) : wa;
+        w2 = wb;
+        w3 = 0; w4 = 0;
+        d0 = __half2float(__ushort_as_half((unsigned short)(w0 & 0xFFFFu)));
+        d1 = __half2float(__ushort_as_half((unsigned short)(wq >> 16)));
+    } else {
+        const uint32_t *s = row + P * 17;
+        const uint32_t wa = s[1 + t], wb = s[5 + t], w0 = s[0], w8 = s[8], wc = s[9 + t], wd = s[13 + t];
+        w1 = wa;
+        w2 = t == 3 ? __byte_perm(w0, w8, 0x5432) : wb;
+        w3 = wc;
+        w4 = wd;
+        d0 = __half2float(__ushort_as_half((unsigned short)(w0 & 0xFFFFu)));
+        d1 = __half2float(__ushort_as_half((unsigned short)(w8 >> 16)));
+    }
+}
+
+// Q4 word -> two k16 steps of one row: {lo(b0),lo(b2)}, {hi(b0),hi(b2)}, {lo(b1),lo(b3)}, {hi(b1),hi(b3)}
+__device__ __forceinline__ void q4_word(uint32_t w, uint32_t &sA0, uint32_t &sA2, uint32_t &sB0, uint32_t &sB2) {
+    const uint32_t k1032 = 0x64086408u, k1_16 = 0x2C002C00u, km72 = 0xD480D480u;
+    const uint32_t w2 = w >> 8;
+    sA0 = hsub2_u32(lop3_and_xor(w, 0x000F000Fu, 0x64086408u), k1032);
+    sA2 = hfma2_u32(lop3_and_xor(w, 0x00F000F0u, 0x64806480u), k1_16, km72);
+    sB0 = hsub2_u32(lop3_and_xor(w2, 0x000F000Fu, 0x64086408u), k1032);
+    sB2 = hfma2_u32(lop3_and_xor(w2, 0x00F000F0u, 0x64806480u), k1_16, km72);
+}
+
+// Q8 word -> one k16 step of one row: {b0,b1}, {b2,b3}
+__device__ __forceinline__ void q8_word(uint32_t w, uint32_t &s0, uint32_t &s2) {
+    const uint32_t x = w ^ 0x80808080u, k1152 = 0x64806480u;
+    s0 = hsub2_u32(__byte_perm(x, 0x64646464u, 0x4140), k1152);
+    s2 = hsub2_u32(__byte_perm(x, 0x64646464u, 0x4342), k1152);
+}
+
+// Decode tile layout of one expert matrix (R rows, Kd values), built once per layer: tile (s, rt)
+// covers rows [16rt, 16rt + 16) and values [256s, 256s + 256) and sits at byte (s·R/16 + rt)·TB,
+// TB = 16 rows × 8 groups × group bytes, so the row tiles of one K slice are contiguous (one bulk
+// copy per matrix and stage). Inside a tile, for group pair P and lane l = 4g + t of the warp that
+// consumes it:
+//   Q4: 16 B at (32P + l)·16 = row g's two words for this lane, then row g+8's two words;
+//   Q8: 16 B at (32P + l)·16 = row g's four words; row g+8's at 2048 + (32P + l)·16;
+// then the scales: row g's eight fp16 group scales at DB + 32g, row g+8's at DB + 32g + 16
+// (DB = 2048 for Q4, 4096 for Q8). The words are the raw group bytes (load_pair_words), regrouped
+// so that a lane's share of a pair is one aligned 16-byte load; the bytes per tile are unchanged.
+template <int ENC>
+struct ExTile {
+    static constexpr int GB = ENC == CPG_ENC_Q4 ? 18 : 34;
+    static constexpr int TB = 16 * 8 * GB;                    // bytes per tile
+    static constexpr int DB = ENC == CPG_ENC_Q4 ? 2048 : 4096; // scale block offset
+};
+
+// Decoded fragments of pair P of a tile for this lane.
+template <int ENC>
+__device__ __forceinline__ void tile_frags(const uint8_t *tp, int P, int lane, uint32_t (&fr)[4][4]) {
+    const uint4 w = *reinterpret_cast<const uint4 *>(tp + (P * 32 + lane) * 16);
+    if (ENC == CPG_ENC_Q4) {
+        q4_word(w.x, fr[0][0], fr[0][2], fr[1][0], fr[1][2]);
+        q4_word(w.y, fr[2][0], fr[2][2], fr[3][0], fr[3][2]);
+        q4_word(w.z, fr[0][1], fr[0][3], fr[1][1], fr[1][3]);
+        q4_word(w.w, fr[2][1], fr[2][3], fr[3][1], fr[3][3]);
+    } else {
+        const uint4 v = *reinterpret_cast<const uint4 *>(tp + 2048 + (P * 32 + lane) * 16);
+        q8_word(w.x, fr[0][0], fr[0][2]);
+        q8_word(w.y, fr[1][0], fr[1][2]);
+        q8_word(w.z, fr[2][0], fr[2][2]);
+        q8_word(w.w, fr[3][0], fr[3][2]);
+        q8_word(v.x, fr[0][1], fr[0][3]);
+        q8_word(v.y, fr[1][1], fr[1][3]);
+        q8_word(v.z, fr[2][1], fr[2][3]);
+        q8_word(v.w, fr[3][1], fr[3][3]);
+    }
+}
+
+// The fragments of one group (hf = 0: group 2P, 1: group 2P + 1) of pair P: fr[0..1] or fr[2..3]
+// of tile_frags.
+template <int ENC>
+__device__ __forceinline__ void group_frags(const uint8_t *tp, int P, int hf, int lane, uint32_t (&fh)[2][4]) {
+    const uint4 w = *reinterpret_cast<const uint4 *>(tp + (P * 32 + lane) * 16);
+    if (ENC == CPG_ENC_Q4) {
+        q4_word(hf ? w.y : w.x, fh[0][0], fh[0][2], fh[1][0], fh[1][2]);
+        q4_word(hf ? w.w : w.z, fh[0][1], fh[0][3], fh[1][1], fh[1][3]);
+    } else {
+        const uint4 v = *reinterpret_cast<const uint4 *>(tp + 2048 + (P * 32 + lane) * 16);
+        q8_word(hf ? w.z : w.x, fh[0][0], fh[0][2]);
+        q8_word(hf ? w.w : w.y, fh[1][0], fh[1][2]);
+        q8_word(hf ? v.z : v.x, fh[0][1], fh[0][3]);
+        q8_word(hf ? v.w : v.y, fh[1][1], fh[1][3]);
+    }
+}
+
+}  // namespace cpg

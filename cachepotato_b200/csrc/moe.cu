@@ -38,7 +38,9 @@
 #include <vector>
 
 #include "common.cuh"
+#include "expert_tile.cuh"
 #include "layout.cuh"
+#include "moe_one.cuh"
 
 namespace cpg {
 
@@ -120,17 +122,6 @@ struct RouterArgs {
     int n_dep;
 };
 
-__device__ __forceinline__ float warp_sum(float v) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    return v;
-}
-__device__ __forceinline__ float warp_max(float v) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-    return v;
-}
-
 // softmax + top-k + renormalisation for one token, one warp (qwen3_moe.c:181-197)
 __device__ void route_token(const RouterArgs &a, int t) {
     const int lane = threadIdx.x & 31;
@@ -154,26 +145,9 @@ __device__ void route_token(const RouterArgs &a, int t) {
     sum = warp_sum(sum);
 #pragma unroll
     for (int i = 0; i < PL; ++i) p[i] = __fdiv_rn(p[i], sum);
-    uint32_t taken = 0;                       // bit i: expert lane + 32 i already selected
     float sel_p[MAX_K];
     int sel_e[MAX_K];
-    for (int j = 0; j < a.K; ++j) {
-        float bv = -1.0f;
-        int be = 0x7fffffff;
-#pragma unroll
-        for (int i = 0; i < PL; ++i) {
-            const int e = lane + 32 * i;
-            if (e < a.E && !((taken >> i) & 1u) && p[i] > bv) { bv = p[i]; be = e; }
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {     // larger prob wins, equal prob: lower id (strict '>')
-            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-            const int oe = __shfl_xor_sync(0xffffffffu, be, o);
-            if (ov > bv || (ov == bv && oe < be)) { bv = ov; be = oe; }
-        }
-        if ((be & 31) == lane) taken |= 1u << (be >> 5);
-        if (j < MAX_K) { sel_p[j] = bv; sel_e[j] = be; }
-    }
+    warp_topk<PL, MAX_K>(p, a.E, a.K, sel_e, sel_p);
     if (lane == 0) {
         float s = 0.0f;
         for (int j = 0; j < a.K; ++j) s += sel_p[j];
@@ -540,7 +514,6 @@ struct ExpertArgs {
 // the stage ring in K slices of 256 values (eight groups per row: 144 B of Q4_0, 272 B of Q8_0).
 // GATEUP: 64 gate rows + the same 64 up rows, warp w holds matrix w & 1, 16-row tile w >> 1.
 // DOWN: 128 rows of Wd, warp w holds tile w. Every warp keeps its rows over the whole K.
-constexpr int EX_KSL = 256;
 template <int ENC, int KIND>
 struct ExCfg {
     static constexpr int GB = ENC == CPG_ENC_Q4 ? 18 : 34;
@@ -560,47 +533,6 @@ struct ExCfg {
 struct StageMeta { int item, m, off, cnt, s, kind, chunk, pad; };   // off/cnt: the item's token chunk; s: K slice;
                                                                       // chunk: its index over all experts
 
-template <int ENC>
-__device__ __forceinline__ void load_pair_words(const uint32_t *row, int P, int t, uint32_t &w1,
-                                                uint32_t &w2, uint32_t &w3, uint32_t &w4, float &d0,
-                                                float &d1) {
-    if (ENC == CPG_ENC_Q4) {
-        const uint32_t *s = row + P * 9;
-        const uint32_t wa = s[1 + t], w0 = s[0], wq = s[4], wb = s[5 + t];
-        w1 = t == 3 ? __byte_perm(w0, wq, 0x5432) : wa;
-        w2 = wb;
-        w3 = 0; w4 = 0;
-        d0 = __half2float(__ushort_as_half((unsigned short)(w0 & 0xFFFFu)));
-        d1 = __half2float(__ushort_as_half((unsigned short)(wq >> 16)));
-    } else {
-        const uint32_t *s = row + P * 17;
-        const uint32_t wa = s[1 + t], wb = s[5 + t], w0 = s[0], w8 = s[8], wc = s[9 + t], wd = s[13 + t];
-        w1 = wa;
-        w2 = t == 3 ? __byte_perm(w0, w8, 0x5432) : wb;
-        w3 = wc;
-        w4 = wd;
-        d0 = __half2float(__ushort_as_half((unsigned short)(w0 & 0xFFFFu)));
-        d1 = __half2float(__ushort_as_half((unsigned short)(w8 >> 16)));
-    }
-}
-
-// Q4 word -> two k16 steps of one row: {lo(b0),lo(b2)}, {hi(b0),hi(b2)}, {lo(b1),lo(b3)}, {hi(b1),hi(b3)}
-__device__ __forceinline__ void q4_word(uint32_t w, uint32_t &sA0, uint32_t &sA2, uint32_t &sB0, uint32_t &sB2) {
-    const uint32_t k1032 = 0x64086408u, k1_16 = 0x2C002C00u, km72 = 0xD480D480u;
-    const uint32_t w2 = w >> 8;
-    sA0 = hsub2_u32(lop3_and_xor(w, 0x000F000Fu, 0x64086408u), k1032);
-    sA2 = hfma2_u32(lop3_and_xor(w, 0x00F000F0u, 0x64806480u), k1_16, km72);
-    sB0 = hsub2_u32(lop3_and_xor(w2, 0x000F000Fu, 0x64086408u), k1032);
-    sB2 = hfma2_u32(lop3_and_xor(w2, 0x00F000F0u, 0x64806480u), k1_16, km72);
-}
-
-// Q8 word -> one k16 step of one row: {b0,b1}, {b2,b3}
-__device__ __forceinline__ void q8_word(uint32_t w, uint32_t &s0, uint32_t &s2) {
-    const uint32_t x = w ^ 0x80808080u, k1152 = 0x64806480u;
-    s0 = hsub2_u32(__byte_perm(x, 0x64646464u, 0x4140), k1152);
-    s2 = hsub2_u32(__byte_perm(x, 0x64646464u, 0x4342), k1152);
-}
-
 // Item -> (active expert u, row tile m, token chunk c). Items run expert-major, then row tile,
 // then chunk, so the chunks of one weight tile are fetched back to back (the later fetches hit
 // L2). items_before(u) = tiles * chunks_before(u), from the router's table in shared memory.
@@ -617,23 +549,6 @@ __device__ __forceinline__ void decode_item(const int4 *act, int U, int tiles, i
     c = local - m * nch;
 }
 
-
-// Decode tile layout of one expert matrix (R rows, Kd values), built once per layer: tile (s, rt)
-// covers rows [16rt, 16rt + 16) and values [256s, 256s + 256) and sits at byte (s·R/16 + rt)·TB,
-// TB = 16 rows × 8 groups × group bytes, so the row tiles of one K slice are contiguous (one bulk
-// copy per matrix and stage). Inside a tile, for group pair P and lane l = 4g + t of the warp that
-// consumes it:
-//   Q4: 16 B at (32P + l)·16 = row g's two words for this lane, then row g+8's two words;
-//   Q8: 16 B at (32P + l)·16 = row g's four words; row g+8's at 2048 + (32P + l)·16;
-// then the scales: row g's eight fp16 group scales at DB + 32g, row g+8's at DB + 32g + 16
-// (DB = 2048 for Q4, 4096 for Q8). The words are the raw group bytes (load_pair_words), regrouped
-// so that a lane's share of a pair is one aligned 16-byte load; the bytes per tile are unchanged.
-template <int ENC>
-struct ExTile {
-    static constexpr int GB = ENC == CPG_ENC_Q4 ? 18 : 34;
-    static constexpr int TB = 16 * 8 * GB;                    // bytes per tile
-    static constexpr int DB = ENC == CPG_ENC_Q4 ? 2048 : 4096; // scale block offset
-};
 
 // One group pair of rows g and g+8 from the fragments: 4 MMAs per token tile and the fp32
 // group-scale accumulation (dg/d8: the pair's two scales of row g / g+8 as one fp16 pair).
@@ -656,45 +571,6 @@ __device__ __forceinline__ void pair_mma(const uint32_t (&fr)[4][4], uint32_t dg
             acc[nt][c] = fmaf(dj[c >> 1], sj[c], acc[nt][c]);
             acc[nt][c] = fmaf(dj1[c >> 1], sj1[c], acc[nt][c]);
         }
-    }
-}
-
-// Decoded fragments of pair P of a tile for this lane.
-template <int ENC>
-__device__ __forceinline__ void tile_frags(const uint8_t *tp, int P, int lane, uint32_t (&fr)[4][4]) {
-    const uint4 w = *reinterpret_cast<const uint4 *>(tp + (P * 32 + lane) * 16);
-    if (ENC == CPG_ENC_Q4) {
-        q4_word(w.x, fr[0][0], fr[0][2], fr[1][0], fr[1][2]);
-        q4_word(w.y, fr[2][0], fr[2][2], fr[3][0], fr[3][2]);
-        q4_word(w.z, fr[0][1], fr[0][3], fr[1][1], fr[1][3]);
-        q4_word(w.w, fr[2][1], fr[2][3], fr[3][1], fr[3][3]);
-    } else {
-        const uint4 v = *reinterpret_cast<const uint4 *>(tp + 2048 + (P * 32 + lane) * 16);
-        q8_word(w.x, fr[0][0], fr[0][2]);
-        q8_word(w.y, fr[1][0], fr[1][2]);
-        q8_word(w.z, fr[2][0], fr[2][2]);
-        q8_word(w.w, fr[3][0], fr[3][2]);
-        q8_word(v.x, fr[0][1], fr[0][3]);
-        q8_word(v.y, fr[1][1], fr[1][3]);
-        q8_word(v.z, fr[2][1], fr[2][3]);
-        q8_word(v.w, fr[3][1], fr[3][3]);
-    }
-}
-
-// The fragments of one group (hf = 0: group 2P, 1: group 2P + 1) of pair P: fr[0..1] or fr[2..3]
-// of tile_frags.
-template <int ENC>
-__device__ __forceinline__ void group_frags(const uint8_t *tp, int P, int hf, int lane, uint32_t (&fh)[2][4]) {
-    const uint4 w = *reinterpret_cast<const uint4 *>(tp + (P * 32 + lane) * 16);
-    if (ENC == CPG_ENC_Q4) {
-        q4_word(hf ? w.y : w.x, fh[0][0], fh[0][2], fh[1][0], fh[1][2]);
-        q4_word(hf ? w.w : w.z, fh[0][1], fh[0][3], fh[1][1], fh[1][3]);
-    } else {
-        const uint4 v = *reinterpret_cast<const uint4 *>(tp + 2048 + (P * 32 + lane) * 16);
-        q8_word(hf ? w.z : w.x, fh[0][0], fh[0][2]);
-        q8_word(hf ? w.w : w.y, fh[1][0], fh[1][2]);
-        q8_word(hf ? v.z : v.x, fh[0][1], fh[0][3]);
-        q8_word(hf ? v.w : v.y, fh[1][1], fh[1][3]);
     }
 }
 
@@ -1129,6 +1005,7 @@ struct KernelPlan {
     size_t smem = 0;
 };
 
+
 }  // namespace cpg
 
 struct cpg_moe_layer {
@@ -1147,6 +1024,8 @@ struct cpg_moe_layer {
     cpg::KernelPlan gateup, down, both;      // two CTAs per SM (Q4_0), ~100 KB of stages each
     cpg::KernelPlan gateup_deep, down_deep;  // one CTA per SM with all the shared memory in stages:
                                              // for launches with at most one item per SM
+    cpg::OnePlan one;                        // the one-token layer kernel (moe_one.cu), if it fits
+    unsigned *d_one_bar = nullptr;           // its grid-barrier counters (zeroed at creation)
 };
 
 namespace cpg {
@@ -1213,6 +1092,13 @@ int layer_ptrs(const cpg_moe_layer *L, const uint8_t *const **ptrs, int *enc) {
     *enc = L->enc;
     return CPG_OK;
 }
+int layer_one_info(const cpg_moe_layer *L, int *D, int *F, int *E, int *K, int *enc, const float **ln2,
+                   const float **wgate, const uint8_t **tiles, float *eps) {
+    CPG_REQUIRE(L, "null layer");
+    *D = L->D; *F = L->F; *E = L->E; *K = L->K; *enc = L->enc;
+    *ln2 = L->ln2; *wgate = L->wgate; *tiles = L->d_tiles; *eps = L->eps;
+    return CPG_OK;
+}
 int gemm_tc_build_weight_maps(const uint8_t *const *h_ptrs, int E, int D, int F, void **d_maps);
 int layer_weight_maps(const cpg_moe_layer *Lc, const void **maps) {
     CPG_REQUIRE(Lc, "null layer");
@@ -1262,6 +1148,7 @@ extern "C" int cpg_moe_layer_create(const cpg_moe_desc *d, cpg_moe_layer **out) 
     CPG_REQUIRE(d->ln2 && d->wgate.p && d->experts, "cpg_moe_layer_create: null tensor");
     CPG_REQUIRE(d->wgate.enc == CPG_ENC_F32, "router weights must be f32 (the reference keeps Wgate f32)");
     CPG_REQUIRE(((uintptr_t)d->wgate.p & 15) == 0, "router weights must be 16-byte aligned");
+    CPG_REQUIRE(((uintptr_t)d->ln2 & 15) == 0, "ln2 must be 16-byte aligned");
     const int enc = d->experts[0].enc;
     CPG_REQUIRE(enc == CPG_ENC_Q4 || enc == CPG_ENC_Q8, "expert encoding %d is not Q4_0/Q8_0", enc);
     const int E = d->n_experts;
@@ -1301,6 +1188,12 @@ extern "C" int cpg_moe_layer_create(const cpg_moe_desc *d, cpg_moe_layer **out) 
         if (rc == CPG_OK) rc = plan_kernel<CPG_ENC_Q8, KIND_DOWN>(L->down_deep, true);
     }
     if (rc == CPG_OK) rc = build_tiles(L);
+    if (rc == CPG_OK) rc = one_plan(L, &L->one);
+    if (rc == CPG_OK && L->one.ok) {
+        cudaError_t ce = cudaMalloc((void **)&L->d_one_bar, 2 * sizeof(unsigned));
+        if (ce == cudaSuccess) ce = cudaMemset(L->d_one_bar, 0, 2 * sizeof(unsigned));
+        if (ce != cudaSuccess) rc = cuda_fail(ce, "cpg_moe_layer_create: barrier counters");
+    }
     if (rc == CPG_OK) {
         const int rsmem = R_TB * L->D * (int)sizeof(float);
         if (rsmem > smem_optin() - 8 * 1024) {
@@ -1316,6 +1209,7 @@ extern "C" int cpg_moe_layer_create(const cpg_moe_desc *d, cpg_moe_layer **out) 
     if (rc != CPG_OK) {
         cudaFree(L->d_ptrs);
         if (L->d_tiles) cudaFree(L->d_tiles);
+        if (L->d_one_bar) cudaFree(L->d_one_bar);
         delete L;
         return rc;
     }
@@ -1361,6 +1255,7 @@ extern "C" void cpg_moe_layer_destroy(cpg_moe_layer *L) {
     cudaFree(L->d_ptrs);
     if (L->d_tiles) cudaFree(L->d_tiles);
     if (L->d_wmaps) cudaFree(L->d_wmaps);
+    if (L->d_one_bar) cudaFree(L->d_one_bar);
     delete L;
 }
 
@@ -1396,6 +1291,17 @@ int cpg::moe_forward_impl(const cpg_moe_layer *L, const float *x, const float *a
     uint8_t *w = (uint8_t *)ws;
     int *hdr = (int *)w;
     if (ev) CPG_CUDA(cudaEventRecordWithFlags(ev[0], s, cudaEventRecordExternal));
+    if (T == 1 && L->one.ok) {
+        // one token: the whole block in one cooperative launch (moe_one.cu); its time is the
+        // router phase of the phase events
+        const int rc = one_launch(L, L->one, x, attn, mlp, x_out, topk_idx ? topk_idx : (int *)(w + W.topk),
+                                  wt ? wt : (float *)(w + W.wt), router ? router : (float *)(w + W.logits), hdr,
+                                  (float *)(w + W.h), L->d_one_bar, s);
+        if (rc) return rc;
+        if (ev)
+            for (int i = 1; i < 5; ++i) CPG_CUDA(cudaEventRecordWithFlags(ev[i], s, cudaEventRecordExternal));
+        return CPG_OK;
+    }
 
     RouterArgs ra{};
     ra.x = x; ra.attn = attn; ra.ln2 = L->ln2; ra.wgate = L->wgate;

@@ -143,7 +143,9 @@ size_t cpg_moe_workspace_bytes(const cpg_moe_layer *layer, int max_T);
  *     residual of run_layers); may alias x;
  *   topk_idx (T,topk) int, wt (T,topk), router (T,n_experts) logits: optional outputs.
  * The status word in the workspace records device-side timeouts; read it with
- * cpg_moe_check(). */
+ * cpg_moe_check(). A one-token forward (T = 1) runs the whole block in one cooperative launch
+ * (one CTA per SM, grid-wide barriers through two counters the layer owns): one-token forwards
+ * of the same layer must not overlap on the GPU (serialise them on one stream, or with events). */
 int cpg_moe_forward(const cpg_moe_layer *layer, const float *x, const float *attn, int T,
                     float *mlp, float *x_out, int *topk_idx, float *wt, float *router,
                     void *ws, size_t ws_bytes, void *stream);

@@ -152,3 +152,25 @@ def test_block_zipf_t64_vs_reference_engine(orc, golden):
     err = _compare(got, want, L.topk)
     counts = np.bincount(want["topk_idx"].ravel(), minlength=L.n_experts)
     assert counts.max() > 32 and err <= DECODE_TOL     # experts spanning several token chunks
+
+
+@pytest.mark.parametrize("T,bad", [(1, 0), (3, 2)])
+def test_nan_token_routes_like_the_reference(orc, layers, T, bad):
+    """A token whose activations hold a NaN has NaN logits: the reference's scan
+    (qwen3_moe.c:184-194) then keeps its starting candidate, the lowest untaken id, in every
+    slot. The device routes it the same way (one-token and batched paths) and the tokens before
+    it are unaffected (in the reference harness later tokens see the NaN token's keys through
+    its zero attention, 0 * NaN = NaN, so only earlier tokens are compared)."""
+    ref = O.Reference(threads=8)
+    D, F, E, K = 256, 256, 16, 4
+    L, dl = layers(D, F, E, K, O.ENC_Q4, 310)
+    x = orc.normal(T * D, 311, 1.0).reshape(T, D)
+    x[bad, 17] = np.nan
+    want = ref.qwen3_moe(L, x)
+    got = dl.forward(torch.from_numpy(x).cuda())
+    idx = got.topk_idx.cpu().numpy()
+    assert idx[bad].tolist() == want["topk_idx"][bad].tolist() == list(range(K))
+    good = list(range(bad))
+    if good:
+        assert np.array_equal(idx[good], want["topk_idx"][good])
+        assert max_rel(got.mlp.cpu().numpy()[good], want["mlp"][good]) <= DECODE_TOL
