@@ -434,6 +434,7 @@ def run_ours(args, rank, world, torch, dist):
         "config": headline_config(args), "parallelism": f"replicas x{world}",
         "moe_layer_hbm_gbs": round(step_bytes / (ms_step * 1e-3) / 1e9, 1),
         "routing": {"distinct_experts_per_layer_mean": round(float(np.mean(U)), 1),
+                    "distinct_experts_per_layer": [int(u) for u in U],
                     "max_expert_load_mean": round(float(np.mean([st["max_load"] for st in stats])), 1)},
         "phase_ms_per_step": {"router": round(phase[0] / args.steps, 4),
                               "experts": round((phase[1] + phase[2]) / args.steps, 4),

@@ -180,6 +180,9 @@ class Reference:
                                           [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_int, _f32p] +
                                           [_vpp] * 8 + [ctypes.c_int, _vpp, _vpp, ctypes.c_int] +
                                           [_i32p, ctypes.c_int, ctypes.c_int, _i32p, _f32p])
+        if hasattr(L, "refh_v4_generate"):
+            L.refh_v4_generate.restype = ctypes.c_int
+            L.refh_v4_generate.argtypes = [ctypes.c_char_p, _i32p, ctypes.c_int, ctypes.c_int, _i32p, _f32p, _i32p]
         for n in ("matmul_wx_q4", "matmul_wx_q8"):
             getattr(L, n).argtypes = [_f32p, _f32p, _u8p, ctypes.c_int, ctypes.c_int]
         L.matmul_wx.argtypes = [_f32p, _f32p, _f32p, ctypes.c_int, ctypes.c_int]
@@ -249,6 +252,19 @@ class Reference:
             _ptr(ids, _i32p), _ptr(logits, _f32p))
         assert rc == 0
         return ids, logits
+
+    def v4_generate(self, path: str, prompt, n_new: int):
+        """A CPW1 v4 file through the reference's own loader and generate loop. Returns (ids of
+        the n_new + 1 argmaxes, the last step's logits, [layers, d_model, vocab, experts, topk,
+        d_exp])."""
+        prompt = np.ascontiguousarray(prompt, dtype=np.int32)
+        ids = np.zeros(n_new + 1, np.int32)
+        meta = np.zeros(6, np.int32)
+        logits = np.zeros(151936 * 2, np.float32)          # the loader's vocabulary (qwen3_moe.c:401), with room
+        rc = self.L.refh_v4_generate(path.encode(), _ptr(prompt, _i32p), len(prompt), n_new, _ptr(ids, _i32p),
+                                     _ptr(logits, _f32p), _ptr(meta, _i32p))
+        assert rc == 0, rc
+        return ids, logits[:meta[2]].copy(), meta
 
     def moe_apply(self, layer: "SynthLayer", xn: np.ndarray, idx: np.ndarray, wt: np.ndarray):
         xn = np.ascontiguousarray(xn, dtype=np.float32)

@@ -175,3 +175,81 @@ out:
     free(ls); free(kv); free(tab); free(x); free(logits);
     return rc;
 }
+
+/* A CPW1 v4 file through the reference's OWN loader: qwen3_map_ex with no pager (the weights
+   are read from the mapping, engine/blocks/qwen3_moe.c:318-459) and qwen3_bind_layer per layer,
+   as cp_open binds them (engine/api/cachepotato.c:262-283), then the generate loop above with
+   embed_rows' chunked-table lookup (cachepotato.c:108-133). out_ids gets n_new + 1 ids, out_meta
+   {n_layers, d_model, vocab, n_experts, topk, d_exp}. */
+int refh_v4_generate(const char *path, const int *prompt, int n_prompt, int n_new, int *out_ids,
+                     float *out_logits, int *out_meta) {
+    QW3Layer base;
+    if (qwen3_map_ex(&base, path, QW3_BUDGET_NONE)) return -1;
+    if (qwen3_bind_layer(&base, 0)) return -2;
+    const int L = base.n_layers, D = base.d_model, V = base.vocab, E = base.n_experts;
+    const int cap = n_prompt + n_new;
+    QW3Layer *ls = calloc((size_t)L, sizeof(QW3Layer));
+    QW3KV *kv = calloc((size_t)L, sizeof(QW3KV));
+    float *x = malloc(sizeof(float) * (size_t)n_prompt * D);
+    float *logits = malloc(sizeof(float) * (size_t)V);
+    int rc = -3;
+    if (!ls || !kv || !x || !logits) goto out;
+    for (int l = 0; l < L; l++) {
+        ls[l] = base;                                   /* tables of 128 experts, as qwen3_map_ex
+                                                           allocates them: qwen3_bind_layer clears 128 */
+        ls[l].exp = calloc((size_t)(E > 128 ? E : 128) * 3, sizeof(QW3T));
+        ls[l].exp_owned = 0;
+        ls[l].reg_exp = calloc((size_t)(E > 128 ? E : 128), sizeof(int));
+        if (!ls[l].exp || !ls[l].reg_exp || qwen3_bind_layer(&ls[l], l)) goto out;
+        if (qwen3_kv_alloc(&kv[l], &ls[l], cap)) goto out;
+    }
+    if (out_meta) {
+        out_meta[0] = L; out_meta[1] = D; out_meta[2] = V;
+        out_meta[3] = E; out_meta[4] = base.topk; out_meta[5] = ls[0].d_exp;
+    }
+    {
+        const size_t q8_row = (size_t)(D / 32) * 34, q4_row = (size_t)(D / 32) * 18;
+        int pos = 0, T = n_prompt, cur = 0;
+        for (int step = 0; step <= n_new; step++) {
+            for (int t = 0; t < T; t++) {
+                int row = step == 0 ? prompt[t] : cur;
+                const void *eb = base.embed.p;
+                if (base.embed_chunks > 0 && base.embed_rows > 0) {
+                    int c = row / base.embed_rows, r = row - c * base.embed_rows;
+                    if (c >= base.embed_chunks) { c = base.embed_chunks - 1; r = row - c * base.embed_rows; }
+                    eb = base.embed_chunk_ptr[c];
+                    row = r;
+                }
+                float *xt = x + (size_t)t * D;
+                if (base.embed.enc == QW3_ENC_Q8) q8_dequant_row((const uint8_t *)eb + (size_t)row * q8_row, xt, D);
+                else if (base.embed.enc == QW3_ENC_Q4) q4_dequant_row((const uint8_t *)eb + (size_t)row * q4_row, xt, D);
+                else memcpy(xt, (const float *)eb + (size_t)row * D, sizeof(float) * (size_t)D);
+            }
+            for (int l = 0; l < L; l++) {
+                QW3Out o;
+                if (qwen3_layer_alloc(&o, &ls[l], T)) goto out;
+                if (qwen3_layer_kv(&ls[l], x, T, pos, &kv[l], &o)) { qwen3_layer_free(&o); goto out; }
+                for (size_t i = 0; i < (size_t)T * D; i++) x[i] += o.attn[i] + o.mlp[i];
+                qwen3_layer_free(&o);
+            }
+            float *xl = x + (size_t)(T - 1) * D;
+            rmsnorm(xl, xl, base.final_norm, D, base.rms_eps);
+            qwen3_mm(&base.lm_head, logits, xl, D, V);
+            cur = refh_argmax(logits, V);
+            out_ids[step] = cur;
+            pos += T;
+            T = 1;
+        }
+    }
+    if (out_logits) memcpy(out_logits, logits, sizeof(float) * (size_t)V);
+    rc = 0;
+out:
+    if (ls)
+        for (int l = 0; l < L; l++) {
+            free(ls[l].exp);
+            free(ls[l].reg_exp);
+            if (kv) qwen3_kv_free(&kv[l]);
+        }
+    free(ls); free(kv); free(x); free(logits);
+    return rc;
+}
