@@ -122,42 +122,6 @@ struct RouterArgs {
     int n_dep;
 };
 
-// softmax + top-k + renormalisation for one token, one warp (qwen3_moe.c:181-197)
-__device__ void route_token(const RouterArgs &a, int t) {
-    const int lane = threadIdx.x & 31;
-    constexpr int PL = MAX_E / 32;
-    float p[PL];
-    float mx = -INFINITY;
-#pragma unroll
-    for (int i = 0; i < PL; ++i) {
-        const int e = lane + 32 * i;
-        p[i] = e < a.E ? __ldcg(a.logits + (size_t)t * a.E + e) : -INFINITY;
-        mx = fmaxf(mx, p[i]);
-    }
-    mx = warp_max(mx);
-    float sum = 0.0f;
-#pragma unroll
-    for (int i = 0; i < PL; ++i) {
-        const int e = lane + 32 * i;
-        p[i] = e < a.E ? expf(p[i] - mx) : 0.0f;
-        sum += p[i];
-    }
-    sum = warp_sum(sum);
-#pragma unroll
-    for (int i = 0; i < PL; ++i) p[i] = __fdiv_rn(p[i], sum);
-    float sel_p[MAX_K];
-    int sel_e[MAX_K];
-    warp_topk<PL, MAX_K>(p, a.E, a.K, sel_e, sel_p);
-    if (lane == 0) {
-        float s = 0.0f;
-        for (int j = 0; j < a.K; ++j) s += sel_p[j];
-        for (int j = 0; j < a.K; ++j) {
-            a.topk[(size_t)t * a.K + j] = sel_e[j];
-            a.wt[(size_t)t * a.K + j] = __fdiv_rn(sel_p[j], s);
-        }
-    }
-}
-
 // group (token, slot) pairs by expert, tokens ascending inside an expert; one CTA
 __device__ __forceinline__ int warp_incl_scan(int v) {
     const int lane = threadIdx.x & 31;
@@ -471,11 +435,21 @@ __global__ void __launch_bounds__(R_THREADS, 2) k_router(RouterArgs a) {
     }
     // every logit of the tile is written once the cluster (all CTAs of this token tile) has
     // passed the barrier (release/acquire at cluster scope); CTA r then routes tokens r,
-    // r + cluster size, ... of the tile
+    // r + cluster size, ... of the tile, each with the whole CTA
     cluster_sync();
     const int rank = cluster_ctarank(), csz = cluster_nctarank();
-    for (int r = rank, i = 0; r < nt; r += csz, ++i)
-        if (warp == i) route_token(a, t0 + r);
+    __shared__ float s_p[MAX_E + MAX_K];
+    __shared__ int s_e[MAX_K];
+    __shared__ float s_w[MAX_K];
+    for (int r = rank; r < nt; r += csz) {
+        const int t = t0 + r;
+        select_topk<MAX_E, MAX_K>(a.logits + (size_t)t * a.E, a.E, a.K, s_e, s_w, s_p);
+        if (tid < a.K) {
+            a.topk[(size_t)t * a.K + tid] = s_e[tid];
+            a.wt[(size_t)t * a.K + tid] = s_w[tid];
+        }
+        __syncthreads();
+    }
 }
 
 // Batches of more than EX_GROUP_MAX pairs: one CTA groups the (token, slot) pairs by expert

@@ -114,84 +114,6 @@ __device__ __forceinline__ void tile_one(const uint8_t *tp, const uint8_t *b, in
     }
 }
 
-// Softmax over the E logits, strict-'>' top-k (larger probability first, lower id on ties) and
-// renormalisation (qwen3_moe.c:181-197; softmax kernels.c:20-26), by the whole CTA. Warp 0
-// computes the probabilities into shared memory; thread e then counts the rank of expert e,
-// #{e' : p' > p, or p' == p and e' < e}, and the experts of rank < K fill the K slots in rank
-// order: the reference scan's result without its K sequential passes (the loops stay short:
-// this code runs once per launch, so its instruction fetch is part of the latency). A NaN
-// probability makes ranks meaningless; warp 0 then runs the scan itself (warp_topk, which
-// reproduces the reference's NaN behaviour).
-__device__ void select_topk(const float *logits, int E, int K, int *sel_e, float *sel_w, float *s_p) {
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    constexpr int PL = O_MAXE / 32;
-    __shared__ int s_nan;
-    if (warp == 0) {
-        float p[PL];
-        float mx = -INFINITY;
-#pragma unroll
-        for (int i = 0; i < PL; ++i) {
-            const int e = lane + 32 * i;
-            p[i] = e < E ? __ldcg(logits + e) : -INFINITY;
-            mx = fmaxf(mx, p[i]);
-        }
-        mx = warp_max(mx);
-        float sum = 0.0f;
-#pragma unroll 1
-        for (int i = 0; i < PL; ++i) {
-            const int e = lane + 32 * i;
-            p[i] = e < E ? expf(p[i] - mx) : 0.0f;
-            sum += p[i];
-        }
-        sum = warp_sum(sum);
-        bool nan = false;
-#pragma unroll 1
-        for (int i = 0; i < PL; ++i) {
-            const int e = lane + 32 * i;
-            p[i] = __fdiv_rn(p[i], sum);
-            if (e < E) {
-                s_p[e] = p[i];
-                nan |= isnan(p[i]);
-            }
-        }
-        nan = __any_sync(0xffffffffu, nan);
-        if (lane == 0) s_nan = nan;
-        if (nan) {
-            float sp[O_MAXK];
-            int se[O_MAXK];
-            warp_topk<PL, O_MAXK>(p, E, K, se, sp);
-            if (lane == 0)
-                for (int j = 0; j < K; ++j) {
-                    sel_e[j] = se[j];
-                    s_p[O_MAXE + j] = sp[j];
-                }
-        }
-    }
-    __syncthreads();
-    if (!s_nan) {
-        for (int e = tid; e < E; e += blockDim.x) {
-            const float pe = s_p[e];
-            int r = 0;
-#pragma unroll 4
-            for (int f = 0; f < E; ++f) {
-                const float pf = s_p[f];
-                r += (pf > pe || (pf == pe && f < e)) ? 1 : 0;
-            }
-            if (r < K) {
-                sel_e[r] = e;
-                s_p[O_MAXE + r] = pe;
-            }
-        }
-        __syncthreads();
-    }
-    if (tid == 0) {                                      // qwen3_moe.c:195-197, selection order
-        float s = 0.0f;
-        for (int j = 0; j < K; ++j) s += s_p[O_MAXE + j];
-        for (int j = 0; j < K; ++j) sel_w[j] = __fdiv_rn(s_p[O_MAXE + j], s);
-    }
-    __syncthreads();
-}
-
 // Vector loads a thread keeps in flight: D <= O_XV * 4 * O_THREADS values in phase R,
 // K * F <= O_HV * 4 * O_THREADS in phase D (every load of a phase is issued before any is used).
 constexpr int O_XV = 4;
@@ -339,7 +261,7 @@ __global__ void __launch_bounds__(O_THREADS, 1) k_moe_one(OneArgs a) {
     // ---------------- phase S: routing; this CTA's gate/up bands are a consecutive range
     {
         __shared__ float s_p[O_MAXE + O_MAXK];           // probabilities, then the selected ones
-        select_topk(a.logits, E, K, s_sel_e, s_sel_w, s_p);
+        select_topk<O_MAXE, O_MAXK>(a.logits, E, K, s_sel_e, s_sel_w, s_p);
     }
     if (c == 0 && tid < K) {
         a.topk[tid] = s_sel_e[tid];
