@@ -23,6 +23,9 @@ layers (router, experts, combine, residual), weights resident in HBM.
   full_model  configs[2]: the whole 48-layer model (attention + MoE, vocab 151936, Q4_0 attention
           and experts, Q8_0 embed and lm_head): 512-token prompt, then 128 greedy decode steps;
           decode tok/s and HBM GB/s of the bytes a token must read
+  batched_decode  64 sequences of the same model decoded together (cpg_qwen3_batch, continuous
+          batching), each with its own prompt and KV cache: tok/s over all sequences, and two of
+          them checked against the single-sequence path
   prefill   configs[3]: 4096 Zipf(1.2)-routed tokens through one Q4_0 MoE block per step on the
           tcgen05 grouped GEMM (cpg_moe_apply), tok/s and TFLOP/s, roofline of the gate/up GEMM
           against the measured tensor peak
@@ -74,6 +77,9 @@ def parse():
     ap.add_argument("--no-full-model", action="store_true", help="skip the whole-model section")
     ap.add_argument("--full-prompt", type=int, default=512)
     ap.add_argument("--full-new", type=int, default=128)
+    ap.add_argument("--batch-seqs", type=int, default=64, help="0 skips the several-sequence decode section")
+    ap.add_argument("--batch-prompt", type=int, default=32)
+    ap.add_argument("--batch-new", type=int, default=32)
     return ap.parse_args()
 
 
@@ -389,6 +395,8 @@ def run_ours(args, rank, world, torch, dist):
     # ---- the whole model, prompt + greedy decode
     fm = None if args.no_full_model else full_model_bench(args, layers, torch, lib, Q, barrier)
     ms_fm = fm.pop("_ms") if fm else 0.0
+    bt = fm.pop("_batched") if fm else None
+    ms_bt = bt.pop("_ms") if bt else 0.0
 
     # ---- expert parallelism across the ranks (a collective: every rank takes part)
     ep = ep_bench(args, layers, torch, lib, Q, dist, rank, world, barrier) if args.ep_tokens > 0 else None
@@ -472,6 +480,10 @@ def run_ours(args, rank, world, torch, dist):
         fm["hbm_gbs"] = round(fm["bytes_per_token"] / (per_tok * 1e-3) / 1e9, 1)
         fm["frac"] = round(fm["hbm_gbs"] / hbm, 4)
         res["full_model"] = fm
+    if bt:
+        bt["value"] = round(world * bt["sequences"] * bt["steps"] / (ms_bt * 1e-3), 1)
+        bt["vs_one_sequence"] = round(bt["value"] / fm["value"], 2)
+        res["batched_decode"] = bt
     if ep:
         per_layer = ms_ep / args.steps / L
         ep["value"] = round(args.ep_tokens * args.steps / (ms_ep * 1e-3), 1)
@@ -567,11 +579,12 @@ def full_model_bench(args, layers, torch, lib, Q, barrier):
     e2.record(s)
     barrier()
     ms_prefill, ms_decode = e0.elapsed_time(e1), e1.elapsed_time(e2)
+    bt = batched_decode_bench(args, m, V, torch, Q, barrier) if args.batch_seqs > 0 else None
     m.close()
     avg_pos = args.full_prompt + args.full_new / 2
     per_layer = (2 * QD * D + 2 * KD * D) // 32 * 18 + ROUTER_BYTES + K * REGION_BYTES + 2 * D * 4 + 2 * HD * 4
     bytes_tok = L * (per_layer + 2 * KD * 4 * avg_pos) + V * D // 32 * 34 + D // 32 * 34 + D * 4
-    return {"_ms": ms_decode, "unit": "tok/s", "bytes_per_token": int(bytes_tok),
+    return {"_ms": ms_decode, "_batched": bt, "unit": "tok/s", "bytes_per_token": int(bytes_tok),
             "prefill_ms": round(ms_prefill, 3), "prefill_tok_s": round(args.full_prompt / (ms_prefill * 1e-3), 1),
             "tokens_head": [int(v) for v in ids[:8]],
             "config": {"workload": f"configs[2]: whole model, {L} layers, vocab {V}, prompt {args.full_prompt} uniform "
@@ -579,6 +592,40 @@ def full_model_bench(args, layers, torch, lib, Q, barrier):
                        "attention": "32 query / 4 KV heads x 128, QK-RMSNorm, RoPE theta 1e6, f32 KV cache",
                        "bytes_per_token": "48 x (attention 10.6 MB + router 1 MiB + 8 experts 21.2 MB + KV reads "
                                           "at the mean position) + lm_head 330.6 MB + embed row"}}
+
+
+def batched_decode_bench(args, m, V, torch, Q, barrier):
+    """Several sequences through the same whole model at once (cpg_qwen3_batch; the reference
+    decodes one sequence at a time). args.batch_seqs sequences, each with its own prompt of
+    args.batch_prompt uniform ids and its own KV cache, are prefilled one by one; then
+    args.batch_new steps advance all of them together (one new token per sequence per step, each
+    argmax fed back on the device, the ids read back at the end). The first and last sequences
+    are checked against the single-sequence path (cpg_qwen3_generate on the same prompt)."""
+    S, n_p, n_new = args.batch_seqs, args.batch_prompt, args.batch_new
+    rng = np.random.default_rng(args.seed + 5)
+    prompts = [rng.integers(0, V, n_p).astype(np.int32) for _ in range(S)]
+    b = Q.Qwen3Batch(m, S, n_p + n_new + 2)
+    s = torch.cuda.ExternalStream(m.stream_ptr())
+    first = [b.prefill(j, p) for j, p in enumerate(prompts)]
+    slots = np.arange(S, dtype=np.int32)
+    warm = b.generate(slots, first, 1)[0]               # warm-up step (captures the step of S sequences)
+    barrier()
+    e0, e1 = (torch.cuda.Event(enable_timing=True) for _ in range(2))
+    e0.record(s)
+    out = b.generate(slots, warm, n_new)
+    e1.record(s)
+    barrier()
+    ms = e0.elapsed_time(e1)
+    b.close()
+    match = []
+    for j in (0, S - 1):
+        want = m.generate(prompts[j], n_new + 1)
+        match.append([first[j], int(warm[j])] + out[:, j].tolist() == want.tolist())
+    return {"_ms": ms, "unit": "tok/s", "sequences": S, "steps": n_new,
+            "ms_per_step": round(ms / n_new, 4), "ids_match_single_sequence": match,
+            "config": {"workload": f"{S} sequences of the configs[2] model, each its own {n_p}-id uniform prompt "
+                                   f"and KV cache, then {n_new} steps of all {S} together (greedy, ids fed back "
+                                   "on the device)"}}
 
 
 def ep_bench(args, layers, torch, lib, Q, dist, rank, world, barrier):

@@ -31,6 +31,8 @@ EXPORTS = [
     "cpg_moe_ep", "cpg_moe_ep_check", "cpg_moe_ep_profile", "cpg_ep_set_timeout", "cpg_ep_abort", "cpg_ep_wait",
     "cpg_qwen3_create", "cpg_qwen3_destroy", "cpg_qwen3_prefill", "cpg_qwen3_step", "cpg_qwen3_generate",
     "cpg_qwen3_logits", "cpg_qwen3_stream", "cpg_qwen3_position",
+    "cpg_qwen3_batch_create", "cpg_qwen3_batch_destroy", "cpg_qwen3_batch_prefill", "cpg_qwen3_batch_step",
+    "cpg_qwen3_batch_generate", "cpg_qwen3_batch_position", "cpg_qwen3_batch_logits",
 ]
 
 
@@ -127,6 +129,13 @@ _SIGS = {
     "cpg_qwen3_logits": (_vp, [_vp]),
     "cpg_qwen3_stream": (_vp, [_vp]),
     "cpg_qwen3_position": (_i, [_vp]),
+    "cpg_qwen3_batch_create": (_i, [_vp, _i, _i, ctypes.POINTER(_vp)]),
+    "cpg_qwen3_batch_destroy": (None, [_vp]),
+    "cpg_qwen3_batch_prefill": (_i, [_vp, _i, _vp, _i, ctypes.POINTER(_i)]),
+    "cpg_qwen3_batch_step": (_i, [_vp, _vp, _vp, _i, _vp]),
+    "cpg_qwen3_batch_generate": (_i, [_vp, _vp, _vp, _i, _i, _vp]),
+    "cpg_qwen3_batch_position": (_i, [_vp, _i]),
+    "cpg_qwen3_batch_logits": (_vp, [_vp, ctypes.POINTER(_i)]),
     "cpg_ctx_x": (_vp, [_vp]),
     "cpg_ctx_topk": (_vp, [_vp]),
     "cpg_ctx_profile": (_i, [_vp, _i]),

@@ -22,6 +22,8 @@
 // Head dimension 128 (one warp per head, four values per lane).
 #include <math.h>
 
+#include <algorithm>
+
 #include <vector>
 
 #include "common.cuh"
@@ -413,28 +415,36 @@ __global__ void __launch_bounds__(256) k_attention_prompt(const float *__restric
     }
 }
 
-// Decode-sized T: the positions of each (query, head) are split into AS_SPLIT ranges, one block
-// each, so that a step's attention spreads over H·AS_SPLIT blocks whatever the context:
+// Decode-sized T: the positions of each (query, head) are split into gridDim.y ≤ AS_SPLIT ranges,
+// one block each, so that a step's attention spreads over enough blocks whatever the context
+// (as_splits: 16 for one query, one range once the T·H pairs alone fill the GPU):
 //   block    scores of its range (warp per position, lane l elements 4l..4l+3, shuffle sum),
 //            local max m and sum l of expf(s - m), o = Σ expf(s - m)·v (positions in order per
 //            warp, warps added in order); (m, l, o) to part
 //   last     the block that finishes last for (query, head) (a counter per pair, reset by that
 //            block) merges the ranges: M = max m, out = Σ o·e^(m-M) / Σ l·e^(m-M)
 // The range length follows the device position, so a captured step serves every position.
-// With `nr` set (one new token, a decode step), the head norm and RoPE of k_qk_norm_rope happen
-// here: every block normalises its q row, the block whose range holds the new position pos0
-// normalises the new key itself (and takes the new value from the staging row), and of the
-// heads sharing a KV head the first writes both into the cache for the later steps.
+// With `nr` set (each query a new token: a decode step), the head norm and RoPE of
+// k_qk_norm_rope happen here: every block normalises its q row, the block whose range holds the
+// new position normalises the new key itself (and takes the new value from the staging row), and
+// of the heads sharing a KV head the first writes both into the cache for the later steps.
+// With `seq.tok_pos` set (a step of several sequences), query i is the new token of its own
+// sequence: position tok_pos[i], cache rows at kc/vc + tok_slot[i]·slot_elems; otherwise the T
+// queries are consecutive tokens of one sequence at positions *d_pos + i.
 struct AttnNorm {
     const float *kst, *vst, *qn, *kn;
     float theta, eps;
     int on;
 };
+struct AttnSeqs {
+    const int *tok_slot, *tok_pos;
+    size_t slot_elems;
+};
 constexpr int AS_SPLIT = 16, AS_THREADS = 256;
 __global__ void __launch_bounds__(AS_THREADS) k_attention_split(const float *__restrict__ q, float *__restrict__ kc,
                                                                 float *__restrict__ vc, const int *__restrict__ d_pos,
                                                                 int H, int KV, float *__restrict__ part, int *__restrict__ cnt,
-                                                                float *__restrict__ ao, const AttnNorm nr) {
+                                                                float *__restrict__ ao, const AttnNorm nr, const AttnSeqs seq) {
     pdl_wait();
     pdl_launch_dependents();
     extern __shared__ float s_sc[];                               // the range's scores
@@ -445,20 +455,30 @@ __global__ void __launch_bounds__(AS_THREADS) k_attention_split(const float *__r
     const int h = blockIdx.x, b = blockIdx.y, i = blockIdx.z;
     const int kh = h / (H / KV);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int pos0 = *d_pos;
-    const int n = pos0 + i + 1;
-    const int chunk = (n + AS_SPLIT - 1) / AS_SPLIT;
+    int pnew;                                                     // this query's position
+    if (seq.tok_pos) {
+        pnew = seq.tok_pos[i];
+        const size_t off = (size_t)seq.tok_slot[i] * seq.slot_elems;
+        kc += off;
+        vc += off;
+    } else {
+        pnew = *d_pos + i;
+    }
+    const int n = pnew + 1;
+    const int ns = gridDim.y;
+    const int chunk = (n + ns - 1) / ns;
     const int j0 = b * chunk, len = max(0, min(n, j0 + chunk) - j0);
     const size_t ks = (size_t)KV * QW_HD;
-    const bool holds_new = nr.on && pos0 >= j0 && pos0 < j0 + len;   // this range ends at the new key
+    const bool holds_new = nr.on && pnew >= j0 && pnew < j0 + len;   // this range ends at the new key
     if (nr.on) {
-        if (warp == 0) head_norm_rope(q + (size_t)h * QW_HD, nr.qn, (float)pos0, nr.theta, nr.eps, s_qk[0]);
-        if (holds_new && warp == 1) head_norm_rope(nr.kst + (size_t)kh * QW_HD, nr.kn, (float)pos0, nr.theta, nr.eps, s_qk[1]);
+        const size_t krow = ((size_t)i * KV + kh) * QW_HD;
+        if (warp == 0) head_norm_rope(q + ((size_t)i * H + h) * QW_HD, nr.qn, (float)pnew, nr.theta, nr.eps, s_qk[0]);
+        if (holds_new && warp == 1) head_norm_rope(nr.kst + krow, nr.kn, (float)pnew, nr.theta, nr.eps, s_qk[1]);
         if (holds_new && warp == 2)
-            for (int e = lane; e < QW_HD; e += 32) s_qk[2][e] = nr.vst[(size_t)kh * QW_HD + e];
+            for (int e = lane; e < QW_HD; e += 32) s_qk[2][e] = nr.vst[krow + e];
         __syncthreads();
         if (holds_new && h % (H / KV) == 0 && tid < 2 * QW_HD) {  // the cache row for later steps
-            float *dst = (tid < QW_HD ? kc : vc) + (size_t)pos0 * ks + (size_t)kh * QW_HD;
+            float *dst = (tid < QW_HD ? kc : vc) + (size_t)pnew * ks + (size_t)kh * QW_HD;
             dst[tid % QW_HD] = s_qk[1 + tid / QW_HD][tid % QW_HD];
         }
     }
@@ -467,7 +487,7 @@ __global__ void __launch_bounds__(AS_THREADS) k_attention_split(const float *__r
     const float scale = __fsqrt_rn((float)QW_HD);
     const float *kb = kc + (size_t)kh * QW_HD + 4 * lane, *vb = vc + (size_t)kh * QW_HD + 4 * lane;
     for (int jj = warp; jj < len; jj += AS_THREADS / 32) {
-        const float4 kv = holds_new && j0 + jj == pos0 ? *reinterpret_cast<const float4 *>(&s_qk[1][4 * lane])
+        const float4 kv = holds_new && j0 + jj == pnew ? *reinterpret_cast<const float4 *>(&s_qk[1][4 * lane])
                                                        : *reinterpret_cast<const float4 *>(kb + (size_t)(j0 + jj) * ks);
         float sv = fmaf(qv.x, kv.x, fmaf(qv.y, kv.y, fmaf(qv.z, kv.z, __fmul_rn(qv.w, kv.w))));
 #pragma unroll
@@ -500,7 +520,7 @@ __global__ void __launch_bounds__(AS_THREADS) k_attention_split(const float *__r
     for (int w = 0; w < AS_THREADS / 32; ++w) sum += s_red[w];
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int jj = warp; jj < len; jj += AS_THREADS / 32) {
-        const float4 v = holds_new && j0 + jj == pos0 ? *reinterpret_cast<const float4 *>(&s_qk[2][4 * lane])
+        const float4 v = holds_new && j0 + jj == pnew ? *reinterpret_cast<const float4 *>(&s_qk[2][4 * lane])
                                                       : *reinterpret_cast<const float4 *>(vb + (size_t)(j0 + jj) * ks);
         const float p = s_sc[jj];
         acc.x = fmaf(p, v.x, acc.x);
@@ -510,7 +530,7 @@ __global__ void __launch_bounds__(AS_THREADS) k_attention_split(const float *__r
     }
     *reinterpret_cast<float4 *>(&s_o[warp][4 * lane]) = acc;
     __syncthreads();
-    float *pp = part + (((size_t)i * H + h) * AS_SPLIT + b) * (QW_HD + 2);
+    float *pp = part + (((size_t)i * H + h) * ns + b) * (QW_HD + 2);
     if (tid < QW_HD) {
         float o = 0.0f;
 #pragma unroll
@@ -523,19 +543,19 @@ __global__ void __launch_bounds__(AS_THREADS) k_attention_split(const float *__r
     }
     __threadfence();
     __syncthreads();
-    if (tid == 0) s_last = atomicAdd(&cnt[i * H + h], 1) == AS_SPLIT - 1;
+    if (tid == 0) s_last = atomicAdd(&cnt[i * H + h], 1) == ns - 1;
     __syncthreads();
     if (!s_last) return;
     __threadfence();
     if (tid < QW_HD) {
-        const float *p0 = part + ((size_t)i * H + h) * AS_SPLIT * (QW_HD + 2);
+        const float *p0 = part + ((size_t)i * H + h) * ns * (QW_HD + 2);
         float M = -INFINITY;
-        for (int r = 0; r < AS_SPLIT; ++r) {
+        for (int r = 0; r < ns; ++r) {
             const float l = __ldcg(p0 + r * (QW_HD + 2) + 1);
             if (l > 0.0f) M = fmaxf(M, __ldcg(p0 + r * (QW_HD + 2)));
         }
         float L = 0.0f, o = 0.0f;
-        for (int r = 0; r < AS_SPLIT; ++r) {
+        for (int r = 0; r < ns; ++r) {
             const float l = __ldcg(p0 + r * (QW_HD + 2) + 1);
             if (l > 0.0f) {
                 const float e = expf(__fsub_rn(__ldcg(p0 + r * (QW_HD + 2)), M));
@@ -546,6 +566,12 @@ __global__ void __launch_bounds__(AS_THREADS) k_attention_split(const float *__r
         ao[((size_t)i * H + h) * QW_HD + tid] = __fdiv_rn(o, L);
     }
     if (tid == 0) cnt[i * H + h] = 0;                             // ready for the next launch
+}
+
+// Ranges per (query, head) for T queries of H heads: enough blocks for four waves of 148 SMs.
+static int as_splits(int T, int H) {
+    const int pairs = T * H, want = 4 * 148;
+    return pairs >= want ? 1 : std::min(AS_SPLIT, (want + pairs - 1) / pairs);
 }
 
 static size_t attention_prompt_smem(int n_cap) {
@@ -576,9 +602,13 @@ __device__ __forceinline__ void argmax_block(float best, int bi, float *out_v, i
     }
 }
 
+// Row r = blockIdx.y of (rows, n) logits; its partials at part + r·gridDim.x.
 __global__ void __launch_bounds__(512) k_argmax_part(const float *__restrict__ v, int n, float *part_v, int *part_i) {
     pdl_wait();
     pdl_launch_dependents();
+    v += (size_t)blockIdx.y * n;
+    part_v += (size_t)blockIdx.y * gridDim.x;
+    part_i += (size_t)blockIdx.y * gridDim.x;
     const int chunk = (n + gridDim.x - 1) / gridDim.x;
     const int lo = blockIdx.x * chunk, hi = min(n, lo + chunk);
     float best = -INFINITY;
@@ -590,10 +620,14 @@ __global__ void __launch_bounds__(512) k_argmax_part(const float *__restrict__ v
     argmax_block(best, bi, part_v + blockIdx.x, part_i + blockIdx.x);
 }
 
+// Row r = blockIdx.x: its nparts partials, the id to out[r].
 __global__ void __launch_bounds__(256) k_argmax_final(const float *__restrict__ part_v, const int *__restrict__ part_i,
                                                        int nparts, int *out) {
     pdl_wait();
     pdl_launch_dependents();
+    part_v += (size_t)blockIdx.x * nparts;
+    part_i += (size_t)blockIdx.x * nparts;
+    out += blockIdx.x;
     __shared__ float s_best;
     float best = -INFINITY;
     int bi = 0x7fffffff;
@@ -616,6 +650,32 @@ __global__ void k_advance(const int *__restrict__ next, int *__restrict__ ids, i
     *d_pos = p;
     ids[0] = id;
     if (out) out[p - base] = id;
+}
+
+// A step of several sequences: token t is the new token of slot tok_slot[t], at that slot's
+// position.
+__global__ void k_batch_begin(const int *__restrict__ tok_slot, const int *__restrict__ slot_pos,
+                              int *__restrict__ tok_pos, int n) {
+    pdl_wait();
+    pdl_launch_dependents();
+    for (int t = threadIdx.x; t < n; t += blockDim.x) tok_pos[t] = slot_pos[tok_slot[t]];
+}
+
+// After such a step: every slot of the step advances by one position, its argmax becomes its
+// next input id and is recorded at out[step·n + t], step = *d_step, which then advances.
+__global__ void k_batch_advance(const int *__restrict__ next, int *__restrict__ ids, const int *__restrict__ tok_slot,
+                                int *__restrict__ slot_pos, int n, int *__restrict__ out, int *__restrict__ d_step) {
+    pdl_wait();
+    pdl_launch_dependents();
+    const int step = *d_step;
+    __syncthreads();
+    for (int t = threadIdx.x; t < n; t += blockDim.x) {
+        const int id = next[t];
+        slot_pos[tok_slot[t]] += 1;
+        ids[t] = id;
+        out[(size_t)step * n + t] = id;
+    }
+    if (threadIdx.x == 0) *d_step = step + 1;
 }
 
 int matvec_launch(float *out, const float *x, cpg_tensor w, int n_in, int n_out, int T, cudaStream_t s);
@@ -733,6 +793,8 @@ extern "C" int cpg_qwen3_create(const cpg_qwen3_desc *d, cpg_qwen3 **out) {
             CPG_REQUIRE(false, "cpg_qwen3_create: max_ctx %d too long for the attention kernel", d->max_ctx);
         }
         ce = cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)asmem);
+        if (ce == cudaSuccess)       // one range per (query, head): the scores of every position
+            ce = cudaFuncSetAttribute(k_attention_split, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)asmem);
         if (ce != cudaSuccess) {
             qwen3_free(m);
             return cuda_fail(ce, "cpg_qwen3_create: attention shared memory");
@@ -796,12 +858,32 @@ extern "C" void cpg_qwen3_destroy(cpg_qwen3 *m) {
     if (m) qwen3_free(m);
 }
 
-// Enqueue T tokens (ids in m->d_ids[0..T)) at the device position *d_pos through embed, the
-// layers and the head; the argmax lands in m->d_next. Nothing here depends on the position on
-// the host, so the T = 1 sequence is captured once and replayed for every decode step.
-static int qwen3_enqueue(cpg_qwen3 *m, int T, cudaStream_t s) {
+// Where the T tokens of one enqueue belong. The KV cache holds S slots of C positions per layer:
+// layer l's keys of slot j at kv + ((2l)·S + j)·C·KD, its values at kv + ((2l + 1)·S + j)·C·KD
+// (S = 1: the model's own sequence). Either the T tokens are consecutive tokens of slot `slot`
+// from the device position *d_pos (a prompt, or the model's own decode step), or (slot < 0)
+// token t is the new token of slot tok_slot[t] at position tok_pos[t] (a step of several
+// sequences). The head runs on the last row (one sequence) or on every row (several), into
+// logits (rows, V) and the argmax into d_next[row].
+struct QwSeq {
+    float *kv;
+    int S, C;
+    const int *d_pos;
+    int slot;
+    const int *tok_slot, *tok_pos;
+    int n_cap;                      // one sequence: its length after these T tokens
+    float *as_part;
+    int *as_cnt;
+    float *logits, *am_v;
+    int *am_i, *d_next;
+};
+
+// Enqueue T tokens (ids in m->d_ids[0..T)) through embed, the layers and the head. Nothing here
+// reads a position on the host, so a decode step is captured once and replayed at every position.
+static int qwen3_enqueue(cpg_qwen3 *m, const QwSeq &sq, int T, cudaStream_t s) {
     const int D = m->D, H = m->H, KV = m->KV, QD = H * QW_HD, KD = KV * QW_HD;
-    const size_t C = (size_t)m->max_ctx;
+    const size_t C = (size_t)sq.C, S = (size_t)sq.S;
+    const bool multi = sq.slot < 0;
     CPG_CUDA(launch_pdl(k_embed, dim3(T), dim3(256), 0, s, (const uint8_t *)m->embed.p, m->embed.enc,
                         (const int *)m->d_ids, D, m->x));
     const bool dense = m->dmaps && T >= QW_DENSE_MIN_T;
@@ -809,9 +891,14 @@ static int qwen3_enqueue(cpg_qwen3 *m, int T, cudaStream_t s) {
         k_dense_tab<<<1, 32, 0, s>>>(m->dtab, m->dn_active, T);
         CPG_CUDA(cudaGetLastError());
     }
+    const AttnSeqs aseq{multi ? sq.tok_slot : nullptr, multi ? sq.tok_pos : nullptr, C * KD};
     for (int l = 0; l < m->L; ++l) {
         const cpg_qwen3_attn &A = m->attn[l];
-        float *kc = m->kv + (size_t)l * 2 * C * KD, *vc = kc + C * KD;
+        float *kc = sq.kv + (size_t)(2 * l) * S * C * KD, *vc = kc + S * C * KD;
+        if (!multi) {
+            kc += (size_t)sq.slot * C * KD;
+            vc += (size_t)sq.slot * C * KD;
+        }
         const void *maps = dense ? (const void *)((const uint8_t *)m->dmaps + (size_t)l * 12 * 128) : nullptr;
         // RMSNorm(x, ln1) and q, k, v: prompts on the tensor cores; decode-sized T in one
         // streaming launch; otherwise separately
@@ -838,25 +925,26 @@ static int qwen3_enqueue(cpg_qwen3 *m, int T, cudaStream_t s) {
         }
         if (rc) return rc;
         const int warps = T * (H + KV);
-        AttnNorm nr{};                                               // T = 1: fused into the attention
-        if (T == 1) nr = AttnNorm{m->kst, m->vst, A.q_norm, A.k_norm, m->theta, m->eps, 1};
+        AttnNorm nr{};                               // new tokens, one per sequence: fused into the attention
+        if (T == 1 || multi) nr = AttnNorm{m->kst, m->vst, A.q_norm, A.k_norm, m->theta, m->eps, 1};
         else
             CPG_CUDA(launch_pdl(k_qk_norm_rope, dim3((warps + 7) / 8), dim3(256), 0, s, m->q, (const float *)m->kst,
-                                (const float *)m->vst, kc, vc, T, (const int *)m->d_pos, H, KV, A.q_norm, A.k_norm,
+                                (const float *)m->vst, kc, vc, T, sq.d_pos, H, KV, A.q_norm, A.k_norm,
                                 m->theta, m->eps));
-        const int n_cap = m->pos + T;                                // prompt: positions known here
-        if (T >= QW_DENSE_MIN_T && attention_prompt_smem(n_cap) <= m->ap_smem) {
+        const int n_cap = sq.n_cap;                                  // prompt: positions known here
+        if (!multi && T >= QW_DENSE_MIN_T && attention_prompt_smem(n_cap) <= m->ap_smem) {
             k_attention_prompt<<<dim3(H, (T + AP_QT - 1) / AP_QT), 256, attention_prompt_smem(n_cap), s>>>(
-                (const float *)m->q, (const float *)kc, (const float *)vc, (const int *)m->d_pos, T, H, KV, n_cap, m->ao);
+                (const float *)m->q, (const float *)kc, (const float *)vc, sq.d_pos, T, H, KV, n_cap, m->ao);
             CPG_CUDA(cudaGetLastError());
-        } else if (T < QW_DENSE_MIN_T) {
-            const size_t ssmem = (size_t)((m->max_ctx + AS_SPLIT - 1) / AS_SPLIT) * sizeof(float);
-            CPG_CUDA(launch_pdl(k_attention_split, dim3(H, AS_SPLIT, T), dim3(AS_THREADS), ssmem, s, (const float *)m->q,
-                                kc, vc, (const int *)m->d_pos, H, KV, m->as_part, m->as_cnt, m->ao, nr));
+        } else if (multi || T < QW_DENSE_MIN_T) {
+            const int ns = as_splits(T, H);
+            const size_t ssmem = (size_t)((sq.C + ns - 1) / ns) * sizeof(float);
+            CPG_CUDA(launch_pdl(k_attention_split, dim3(H, ns, T), dim3(AS_THREADS), ssmem, s, (const float *)m->q,
+                                kc, vc, sq.d_pos, H, KV, sq.as_part, sq.as_cnt, m->ao, nr, aseq));
         } else {
-            const size_t asmem = (size_t)m->max_ctx * sizeof(float);     // scores of every cached position
+            const size_t asmem = (size_t)sq.C * sizeof(float);          // scores of every cached position
             CPG_CUDA(launch_pdl(k_attention, dim3(H, T), dim3(AT_THREADS), asmem, s, (const float *)m->q,
-                                (const float *)kc, (const float *)vc, (const int *)m->d_pos, H, KV, m->ao));
+                                (const float *)kc, (const float *)vc, sq.d_pos, H, KV, m->ao));
         }
         if (dense) {
             const size_t n = (size_t)T * QD;
@@ -870,20 +958,29 @@ static int qwen3_enqueue(cpg_qwen3 *m, int T, cudaStream_t s) {
         rc = cpg_moe_forward(m->moe[l], m->x, m->at, T, nullptr, m->x, nullptr, nullptr, nullptr, m->ws, m->ws_bytes, s);
         if (rc) return rc;
     }
-    // head: RMSNorm of the last position with final_norm fused into the lm_head GEMV
-    const float *xl = m->x + (size_t)(T - 1) * D;
-    const GemvSeg hseg{(const uint8_t *)m->lm_head.p, m->logits, m->V};
-    int rc = m->lm_head.enc == CPG_ENC_F32 ? 1 : gemv_multi(&hseg, 1, xl, 1, m->final_norm, m->eps, D, m->lm_head.enc, s);
+    // head: RMSNorm with final_norm fused into the lm_head GEMV, of the last position (one
+    // sequence) or of every row (one new token per sequence)
+    const int hr = multi ? T : 1;
+    const float *xl = m->x + (size_t)(T - hr) * D;
+    const GemvSeg hseg{(const uint8_t *)m->lm_head.p, sq.logits, m->V};
+    int rc = m->lm_head.enc == CPG_ENC_F32 ? 1 : gemv_multi(&hseg, 1, xl, hr, m->final_norm, m->eps, D, m->lm_head.enc, s);
     if (rc == 1) {
-        k_rmsnorm<<<1, 256, 0, s>>>(xl, m->final_norm, D, m->eps, m->xn);
+        k_rmsnorm<<<hr, 256, 0, s>>>(xl, m->final_norm, D, m->eps, m->xn);
         CPG_CUDA(cudaGetLastError());
-        rc = matvec_launch(m->logits, m->xn, m->lm_head, D, m->V, 1, s);
+        rc = matvec_launch(sq.logits, m->xn, m->lm_head, D, m->V, hr, s);
     }
     if (rc) return rc;
-    CPG_CUDA(launch_pdl(k_argmax_part, dim3(AM_BLOCKS), dim3(512), 0, s, (const float *)m->logits, m->V, m->am_v, m->am_i));
-    CPG_CUDA(launch_pdl(k_argmax_final, dim3(1), dim3(256), 0, s, (const float *)m->am_v, (const int *)m->am_i,
-                        AM_BLOCKS, m->d_next));
+    CPG_CUDA(launch_pdl(k_argmax_part, dim3(AM_BLOCKS, hr), dim3(512), 0, s, (const float *)sq.logits, m->V, sq.am_v,
+                        sq.am_i));
+    CPG_CUDA(launch_pdl(k_argmax_final, dim3(hr), dim3(256), 0, s, (const float *)sq.am_v, (const int *)sq.am_i,
+                        AM_BLOCKS, sq.d_next));
     return CPG_OK;
+}
+
+// The model's own sequence: slot 0 of its own cache.
+static QwSeq own_seq(cpg_qwen3 *m, int T) {
+    return QwSeq{m->kv, 1, m->max_ctx, m->d_pos, 0, nullptr, nullptr, m->pos + T, m->as_part, m->as_cnt,
+                 m->logits, m->am_v, m->am_i, m->d_next};
 }
 
 // One token at the current device position: the captured step graph (built on first use).
@@ -892,7 +989,7 @@ static int qwen3_step_device(cpg_qwen3 *m, int *out, int base) {
     if (!m->step_graph) {
         cudaGraph_t g = nullptr;
         CPG_CUDA(cudaStreamBeginCapture(m->s, cudaStreamCaptureModeThreadLocal));
-        int rc = qwen3_enqueue(m, 1, m->s);
+        int rc = qwen3_enqueue(m, own_seq(m, 1), 1, m->s);
         const cudaError_t ce = cudaStreamEndCapture(m->s, &g);
         if (rc) {
             if (g) cudaGraphDestroy(g);
@@ -924,7 +1021,7 @@ extern "C" int cpg_qwen3_prefill(cpg_qwen3 *m, const int *ids, int T, int *next_
     m->pos = 0;
     CPG_CUDA(cudaMemsetAsync(m->d_pos, 0, 4, m->s));
     CPG_CUDA(cudaMemcpyAsync(m->d_ids, ids, sizeof(int) * (size_t)T, cudaMemcpyHostToDevice, m->s));
-    const int rc = qwen3_enqueue(m, T, m->s);
+    const int rc = qwen3_enqueue(m, own_seq(m, T), T, m->s);
     if (rc) return rc;
     int rc2 = 0;
     k_advance<<<1, 1, 0, m->s>>>(m->d_next, m->d_ids, m->d_pos, T, nullptr, 0);
@@ -972,3 +1069,209 @@ extern "C" int cpg_qwen3_generate(cpg_qwen3 *m, const int *prompt, int n_prompt,
 extern "C" const float *cpg_qwen3_logits(const cpg_qwen3 *m) { return m ? m->logits : nullptr; }
 extern "C" void *cpg_qwen3_stream(const cpg_qwen3 *m) { return m ? (void *)m->s : nullptr; }
 extern "C" int cpg_qwen3_position(const cpg_qwen3 *m) { return m ? m->pos : -1; }
+
+// ---------------------------------------------------------------------------------------------
+// Several sequences at once (continuous batching). The reference engine decodes one sequence
+// (engine/api/cachepotato.h:12-16); here n_slots sequences share the model's weights, each with
+// its own KV cache and position, and a step embeds one new token per named slot and runs them
+// through every layer as one batch: the projections and the MoE block see T = n tokens (the
+// batched expert kernel reads each routed expert once for all of them), the attention of token t
+// reads only its own slot's cache. Per sequence this is the greedy loop of cp_chat
+// (cachepotato.c:315-378). Everything runs on the model's stream and scratch rows, so a batch
+// and the model's own sequence never run at the same time.
+struct cpg_qwen3_batch {
+    cpg_qwen3 *m = nullptr;
+    int S = 0, C = 0;
+    float *kv = nullptr;                 // L × 2 × S × C × KD
+    int *slot_pos = nullptr;             // (S) device positions
+    std::vector<int> pos;                // host copies
+    int *tok_slot = nullptr, *tok_pos = nullptr, *d_next = nullptr, *d_step = nullptr;
+    int *d_out = nullptr;                // (C, S) ids of a generate call, step-major
+    int *h_buf = nullptr;                // pinned staging: 2S ints
+    float *logits = nullptr, *am_v = nullptr, *as_part = nullptr;
+    int *am_i = nullptr, *as_cnt = nullptr;
+    int last_rows = 0;
+    std::vector<cudaGraphExec_t> graphs; // one step of n sequences, by n
+};
+
+// The projection GEMM's bounded waits (prompts and steps of QW_DENSE_MIN_T tokens or more).
+static int qwen3_status(cpg_qwen3 *m, const char *fn) {
+    if (!m->d_status) return CPG_OK;
+    int st = 0;
+    CPG_CUDA(cudaMemcpy(&st, m->d_status, sizeof(int), cudaMemcpyDeviceToHost));
+    if (st != ST_OK) {
+        set_error("%s: a bounded wait in the projection GEMM timed out (status %d)", fn, st);
+        return CPG_ETIMEOUT;
+    }
+    return CPG_OK;
+}
+
+static void batch_free(cpg_qwen3_batch *b) {
+    for (cudaGraphExec_t g : b->graphs)
+        if (g) cudaGraphExecDestroy(g);
+    cudaFree(b->kv); cudaFree(b->slot_pos); cudaFree(b->tok_slot); cudaFree(b->tok_pos);
+    cudaFree(b->d_next); cudaFree(b->d_step); cudaFree(b->d_out); cudaFree(b->logits); cudaFree(b->am_v);
+    cudaFree(b->am_i); cudaFree(b->as_part); cudaFree(b->as_cnt);
+    if (b->h_buf) cudaFreeHost(b->h_buf);
+    delete b;
+}
+
+extern "C" int cpg_qwen3_batch_create(cpg_qwen3 *m, int n_slots, int max_ctx, cpg_qwen3_batch **out) {
+    CPG_REQUIRE(m && out, "cpg_qwen3_batch_create: null argument");
+    *out = nullptr;
+    CPG_REQUIRE(n_slots >= 1 && n_slots <= m->max_ctx,
+                "cpg_qwen3_batch_create: n_slots %d (1..the model's max_ctx %d)", n_slots, m->max_ctx);
+    CPG_REQUIRE(max_ctx >= 1 && max_ctx <= m->max_ctx,
+                "cpg_qwen3_batch_create: max_ctx %d (1..the model's max_ctx %d)", max_ctx, m->max_ctx);
+    cpg_qwen3_batch *b = new cpg_qwen3_batch();
+    b->m = m;
+    b->S = n_slots;
+    b->C = max_ctx;
+    b->pos.assign(n_slots, -1);
+    b->graphs.assign(n_slots + 1, nullptr);
+    const size_t S = n_slots, C = max_ctx, KD = (size_t)m->KV * QW_HD;
+    cudaError_t ce = cudaMalloc(&b->kv, (size_t)m->L * 2 * S * C * KD * sizeof(float));
+    if (ce == cudaSuccess) ce = cudaMalloc(&b->slot_pos, S * sizeof(int));
+    if (ce == cudaSuccess) ce = cudaMalloc(&b->tok_slot, S * sizeof(int));
+    if (ce == cudaSuccess) ce = cudaMalloc(&b->tok_pos, S * sizeof(int));
+    if (ce == cudaSuccess) ce = cudaMalloc(&b->d_next, S * sizeof(int));
+    if (ce == cudaSuccess) ce = cudaMalloc(&b->d_step, sizeof(int));
+    if (ce == cudaSuccess) ce = cudaMalloc(&b->d_out, C * S * sizeof(int));
+    if (ce == cudaSuccess) ce = cudaMallocHost(&b->h_buf, 2 * S * sizeof(int));
+    if (ce == cudaSuccess) ce = cudaMalloc(&b->logits, S * (size_t)m->V * sizeof(float));
+    if (ce == cudaSuccess) ce = cudaMalloc(&b->am_v, S * AM_BLOCKS * sizeof(float));
+    if (ce == cudaSuccess) ce = cudaMalloc(&b->am_i, S * AM_BLOCKS * sizeof(int));
+    if (ce == cudaSuccess) ce = cudaMalloc(&b->as_part, S * m->H * AS_SPLIT * (QW_HD + 2) * sizeof(float));
+    if (ce == cudaSuccess) ce = cudaMalloc(&b->as_cnt, S * m->H * sizeof(int));
+    if (ce == cudaSuccess) ce = cudaMemsetAsync(b->as_cnt, 0, S * m->H * sizeof(int), m->s);
+    if (ce == cudaSuccess) ce = cudaMemsetAsync(b->slot_pos, 0, S * sizeof(int), m->s);
+    if (ce == cudaSuccess) ce = cudaStreamSynchronize(m->s);
+    if (ce != cudaSuccess) {
+        batch_free(b);
+        return cuda_fail(ce, "cpg_qwen3_batch_create: allocation");
+    }
+    *out = b;
+    return CPG_OK;
+}
+
+extern "C" void cpg_qwen3_batch_destroy(cpg_qwen3_batch *b) {
+    if (b) {
+        if (b->m) cudaStreamSynchronize(b->m->s);
+        batch_free(b);
+    }
+}
+
+extern "C" int cpg_qwen3_batch_prefill(cpg_qwen3_batch *b, int slot, const int *ids, int n, int *next_id) {
+    CPG_REQUIRE(b && ids && n > 0, "cpg_qwen3_batch_prefill: bad argument");
+    cpg_qwen3 *m = b->m;
+    CPG_REQUIRE(slot >= 0 && slot < b->S, "cpg_qwen3_batch_prefill: slot %d of %d", slot, b->S);
+    CPG_REQUIRE(n < b->C, "cpg_qwen3_batch_prefill: %d tokens leave no room in max_ctx %d", n, b->C);
+    for (int t = 0; t < n; ++t)
+        CPG_REQUIRE(ids[t] >= 0 && ids[t] < m->V, "cpg_qwen3_batch_prefill: id %d out of range", ids[t]);
+    CPG_CUDA(cudaMemsetAsync(b->slot_pos + slot, 0, sizeof(int), m->s));
+    CPG_CUDA(cudaMemcpyAsync(m->d_ids, ids, sizeof(int) * (size_t)n, cudaMemcpyHostToDevice, m->s));
+    const QwSeq sq{b->kv, b->S, b->C, b->slot_pos + slot, slot, nullptr, nullptr, n, m->as_part, m->as_cnt,
+                   b->logits, b->am_v, b->am_i, b->d_next};
+    int rc = qwen3_enqueue(m, sq, n, m->s);
+    if (rc) return rc;
+    b->h_buf[0] = n;
+    CPG_CUDA(cudaMemcpyAsync(b->slot_pos + slot, b->h_buf, sizeof(int), cudaMemcpyHostToDevice, m->s));
+    CPG_CUDA(cudaMemcpyAsync(b->h_buf + 1, b->d_next, sizeof(int), cudaMemcpyDeviceToHost, m->s));
+    CPG_CUDA(cudaStreamSynchronize(m->s));
+    b->pos[slot] = n;
+    b->last_rows = 1;
+    if (next_id) *next_id = b->h_buf[1];
+    return qwen3_status(m, "cpg_qwen3_batch_prefill");
+}
+
+// The slots of a step: distinct, prefilled, room for n_steps more positions each.
+static int batch_check(cpg_qwen3_batch *b, const int *slots, int n, int n_steps, const char *fn) {
+    CPG_REQUIRE(slots && n >= 1 && n <= b->S, "%s: %d sequences (1..%d)", fn, n, b->S);
+    std::vector<char> seen(b->S, 0);
+    for (int t = 0; t < n; ++t) {
+        const int j = slots[t];
+        CPG_REQUIRE(j >= 0 && j < b->S, "%s: slot %d of %d", fn, j, b->S);
+        CPG_REQUIRE(!seen[j], "%s: slot %d named twice", fn, j);
+        seen[j] = 1;
+        CPG_REQUIRE(b->pos[j] >= 1, "%s: slot %d holds no sequence (prefill it first)", fn, j);
+        CPG_REQUIRE(b->pos[j] + n_steps <= b->C, "%s: slot %d at position %d: %d more steps pass max_ctx %d", fn, j,
+                    b->pos[j], n_steps, b->C);
+    }
+    return CPG_OK;
+}
+
+// n_steps steps of the named slots from ids (host, one per slot); each step's argmax is the
+// next step's input. The step of n sequences is captured once (positions live on the device).
+static int batch_run(cpg_qwen3_batch *b, const int *slots, const int *ids, int n, int n_steps) {
+    cpg_qwen3 *m = b->m;
+    for (int t = 0; t < n; ++t) {
+        b->h_buf[t] = slots[t];
+        b->h_buf[n + t] = ids[t];
+    }
+    CPG_CUDA(cudaMemcpyAsync(b->tok_slot, b->h_buf, sizeof(int) * n, cudaMemcpyHostToDevice, m->s));
+    CPG_CUDA(cudaMemcpyAsync(m->d_ids, b->h_buf + n, sizeof(int) * n, cudaMemcpyHostToDevice, m->s));
+    CPG_CUDA(cudaMemsetAsync(b->d_step, 0, sizeof(int), m->s));
+    if (!b->graphs[n]) {
+        const QwSeq sq{b->kv, b->S, b->C, nullptr, -1, b->tok_slot, b->tok_pos, 0, b->as_part, b->as_cnt,
+                       b->logits, b->am_v, b->am_i, b->d_next};
+        cudaGraph_t g = nullptr;
+        CPG_CUDA(cudaStreamBeginCapture(m->s, cudaStreamCaptureModeThreadLocal));
+        int rc = 0;
+        k_batch_begin<<<1, 256, 0, m->s>>>(b->tok_slot, b->slot_pos, b->tok_pos, n);
+        cudaError_t le = cudaGetLastError();
+        if (le != cudaSuccess) rc = cuda_fail(le, "cpg_qwen3_batch: step launch");
+        if (!rc) rc = qwen3_enqueue(m, sq, n, m->s);
+        if (!rc) {
+            k_batch_advance<<<1, 256, 0, m->s>>>(b->d_next, m->d_ids, b->tok_slot, b->slot_pos, n, b->d_out, b->d_step);
+            le = cudaGetLastError();
+            if (le != cudaSuccess) rc = cuda_fail(le, "cpg_qwen3_batch: step launch");
+        }
+        const cudaError_t ce = cudaStreamEndCapture(m->s, &g);
+        if (rc) {
+            if (g) cudaGraphDestroy(g);
+            return rc;
+        }
+        if (ce != cudaSuccess) return cuda_fail(ce, "cpg_qwen3_batch: step capture");
+        const cudaError_t ie = cudaGraphInstantiate(&b->graphs[n], g, 0);
+        cudaGraphDestroy(g);
+        if (ie != cudaSuccess) return cuda_fail(ie, "cpg_qwen3_batch: step instantiate");
+    }
+    for (int i = 0; i < n_steps; ++i) CPG_CUDA(cudaGraphLaunch(b->graphs[n], m->s));
+    for (int t = 0; t < n; ++t) b->pos[slots[t]] += n_steps;
+    b->last_rows = n;
+    return CPG_OK;
+}
+
+extern "C" int cpg_qwen3_batch_step(cpg_qwen3_batch *b, const int *slots, const int *ids, int n, int *next_ids) {
+    CPG_REQUIRE(b && ids && next_ids, "cpg_qwen3_batch_step: null argument");
+    int rc = batch_check(b, slots, n, 1, "cpg_qwen3_batch_step");
+    for (int t = 0; !rc && t < n; ++t)
+        CPG_REQUIRE(ids[t] >= 0 && ids[t] < b->m->V, "cpg_qwen3_batch_step: id %d out of range", ids[t]);
+    if (!rc) rc = batch_run(b, slots, ids, n, 1);
+    if (rc) return rc;
+    CPG_CUDA(cudaMemcpyAsync(next_ids, b->d_out, sizeof(int) * n, cudaMemcpyDeviceToHost, b->m->s));
+    CPG_CUDA(cudaStreamSynchronize(b->m->s));
+    return qwen3_status(b->m, "cpg_qwen3_batch_step");
+}
+
+extern "C" int cpg_qwen3_batch_generate(cpg_qwen3_batch *b, const int *slots, const int *ids, int n, int n_steps,
+                                        int *out_ids) {
+    CPG_REQUIRE(b && ids && out_ids && n_steps >= 1, "cpg_qwen3_batch_generate: bad argument");
+    int rc = batch_check(b, slots, n, n_steps, "cpg_qwen3_batch_generate");
+    for (int t = 0; !rc && t < n; ++t)
+        CPG_REQUIRE(ids[t] >= 0 && ids[t] < b->m->V, "cpg_qwen3_batch_generate: id %d out of range", ids[t]);
+    if (!rc) rc = batch_run(b, slots, ids, n, n_steps);
+    if (rc) return rc;
+    CPG_CUDA(cudaMemcpyAsync(out_ids, b->d_out, sizeof(int) * (size_t)n * n_steps, cudaMemcpyDeviceToHost, b->m->s));
+    CPG_CUDA(cudaStreamSynchronize(b->m->s));
+    return qwen3_status(b->m, "cpg_qwen3_batch_generate");
+}
+
+extern "C" int cpg_qwen3_batch_position(const cpg_qwen3_batch *b, int slot) {
+    return b && slot >= 0 && slot < b->S ? b->pos[slot] : -1;
+}
+
+extern "C" const float *cpg_qwen3_batch_logits(const cpg_qwen3_batch *b, int *rows) {
+    if (rows) *rows = b ? b->last_rows : 0;
+    return b ? b->logits : nullptr;
+}

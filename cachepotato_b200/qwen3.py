@@ -435,6 +435,64 @@ class Qwen3Model:
             pass
 
 
+class Qwen3Batch:
+    """cpg_qwen3_batch: n_slots sequences over one Qwen3Model's weights (continuous batching).
+    Each slot has its own KV cache and position; prefill(slot, prompt) starts a sequence in a
+    slot, step(slots, ids) advances the named slots by one token each, generate(slots, ids, n)
+    runs n such steps feeding each argmax back on the device."""
+
+    def __init__(self, model: Qwen3Model, n_slots: int, max_ctx: int):
+        h = ctypes.c_void_p()
+        check(lib().cpg_qwen3_batch_create(model.handle, n_slots, max_ctx, ctypes.byref(h)))
+        self.handle, self.model, self.vocab, self.n_slots = h, model, model.vocab, n_slots
+
+    def prefill(self, slot: int, ids) -> int:
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        nxt = ctypes.c_int()
+        check(lib().cpg_qwen3_batch_prefill(self.handle, int(slot), ids.ctypes.data, len(ids), ctypes.byref(nxt)))
+        return nxt.value
+
+    def step(self, slots, ids) -> np.ndarray:
+        slots = np.ascontiguousarray(slots, dtype=np.int32)
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        assert len(slots) == len(ids)
+        out = np.zeros(len(slots), np.int32)
+        check(lib().cpg_qwen3_batch_step(self.handle, slots.ctypes.data, ids.ctypes.data, len(slots), out.ctypes.data))
+        return out
+
+    def generate(self, slots, ids, n_steps: int) -> np.ndarray:
+        """(n_steps, len(slots)) ids: row s = the ids step s produced."""
+        slots = np.ascontiguousarray(slots, dtype=np.int32)
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        assert len(slots) == len(ids)
+        out = np.zeros((n_steps, len(slots)), np.int32)
+        check(lib().cpg_qwen3_batch_generate(self.handle, slots.ctypes.data, ids.ctypes.data, len(slots), n_steps,
+                                             out.ctypes.data))
+        return out
+
+    def position(self, slot: int) -> int:
+        return int(lib().cpg_qwen3_batch_position(self.handle, int(slot)))
+
+    def logits(self):
+        """The last call's logits as a (rows, vocab) device tensor (a view; valid until the next call)."""
+        torch = _torch()
+        from .workload import device_view
+        rows = ctypes.c_int()
+        p = int(lib().cpg_qwen3_batch_logits(self.handle, ctypes.byref(rows)))
+        return device_view(torch, p, rows.value * self.vocab * 4, "f4").view(rows.value, self.vocab)
+
+    def close(self) -> None:
+        if self.handle is not None and self.handle.value:
+            lib().cpg_qwen3_batch_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 class DecodeContext:
     """cpg_ctx: the host-buffer decode loop (run_layers' MoE half, cachepotato.c:149-166)."""
 

@@ -269,6 +269,33 @@ const float *cpg_qwen3_logits(const cpg_qwen3 *m);   /* device (vocab) f32, last
 void *cpg_qwen3_stream(const cpg_qwen3 *m);
 int cpg_qwen3_position(const cpg_qwen3 *m);
 
+/* ------------------------------------------- several sequences at once (continuous batching)
+ * The reference decodes one sequence per engine (engine/api/cachepotato.h:12-16). A batch holds
+ * n_slots sequences over one model's weights, each with its own f32 KV cache of max_ctx
+ * positions (≤ the model's max_ctx; n_slots ≤ the model's max_ctx). A sequence enters a slot
+ * with cpg_qwen3_batch_prefill (its prompt from position 0, replacing what the slot held); a
+ * step then takes one new token for each slot it names, so sequences join and leave between
+ * steps. Per sequence the ids are those of cpg_qwen3_generate on the same prompt (the greedy
+ * loop of cp_chat, cachepotato.c:315-378). Runs on the model's stream and scratch: do not use
+ * the model's own sequence (cpg_qwen3_prefill/step) concurrently from another thread; its KV
+ * cache and position are left untouched. */
+typedef struct cpg_qwen3_batch cpg_qwen3_batch;
+int cpg_qwen3_batch_create(cpg_qwen3 *m, int n_slots, int max_ctx, cpg_qwen3_batch **out);
+void cpg_qwen3_batch_destroy(cpg_qwen3_batch *b);
+/* n < max_ctx prompt ids into `slot`; *next_id = argmax of the last position's logits. */
+int cpg_qwen3_batch_prefill(cpg_qwen3_batch *b, int slot, const int *ids, int n, int *next_id);
+/* One step: slots[0..n) distinct prefilled slots, ids[t] the new token of slots[t];
+   next_ids[t] its argmax. */
+int cpg_qwen3_batch_step(cpg_qwen3_batch *b, const int *slots, const int *ids, int n, int *next_ids);
+/* n_steps steps of the same slots, each feeding the previous argmax; out_ids (n_steps, n),
+   step-major. */
+int cpg_qwen3_batch_generate(cpg_qwen3_batch *b, const int *slots, const int *ids, int n, int n_steps,
+                             int *out_ids);
+int cpg_qwen3_batch_position(const cpg_qwen3_batch *b, int slot);   /* -1: empty slot */
+/* Device logits of the last call, *rows rows of vocab f32: a step's rows in its slot order; a
+   prefill's one row. */
+const float *cpg_qwen3_batch_logits(const cpg_qwen3_batch *b, int *rows);
+
 /* ============================================================== decode loop (host buffers)
  * A context owns a stream, a workspace and device activation buffers on one device. */
 typedef struct cpg_ctx cpg_ctx;
