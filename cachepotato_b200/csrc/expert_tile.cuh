@@ -200,6 +200,37 @@ struct ExTile {
     static constexpr int DB = ENC == CPG_ENC_Q4 ? 2048 : 4096; // scale block offset
 };
 
+// Lane `lane`'s share of building one decode tile from raw rows: src = the tile's first row at
+// its K slice (row stride rowb bytes), dst = the tile. Every lane of a warp writes its words of
+// the four group pairs; lanes t = 0, 1 of each quad also write the scales of rows g, g + 8.
+template <int ENC>
+__device__ __forceinline__ void tile_build_lane(const uint8_t *src, size_t rowb, uint8_t *dst, int lane) {
+    using X = ExTile<ENC>;
+    const int g = lane >> 2, t = lane & 3;
+    const uint32_t *rg = reinterpret_cast<const uint32_t *>(src + g * rowb);
+    const uint32_t *r8 = reinterpret_cast<const uint32_t *>(src + (g + 8) * rowb);
+    for (int P = 0; P < 4; ++P) {
+        uint32_t a1, a2, a3, a4, b1, b2, b3, b4;
+        float d0, d1;
+        load_pair_words<ENC>(rg, P, t, a1, a2, a3, a4, d0, d1);
+        load_pair_words<ENC>(r8, P, t, b1, b2, b3, b4, d0, d1);
+        if (ENC == CPG_ENC_Q4) {
+            *reinterpret_cast<uint4 *>(dst + (P * 32 + lane) * 16) = make_uint4(a1, a2, b1, b2);
+        } else {
+            *reinterpret_cast<uint4 *>(dst + (P * 32 + lane) * 16) = make_uint4(a1, a2, a3, a4);
+            *reinterpret_cast<uint4 *>(dst + 2048 + (P * 32 + lane) * 16) = make_uint4(b1, b2, b3, b4);
+        }
+    }
+    if (t < 2) {                                               // lane t = 0: row g, t = 1: row g + 8
+        const uint8_t *row = src + (g + 8 * t) * rowb;
+        uint32_t w[4];
+        for (int j = 0; j < 4; ++j)
+            w[j] = (uint32_t)*reinterpret_cast<const uint16_t *>(row + 2 * j * X::GB) |
+                   ((uint32_t)*reinterpret_cast<const uint16_t *>(row + (2 * j + 1) * X::GB) << 16);
+        *reinterpret_cast<uint4 *>(dst + X::DB + g * 32 + t * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+}
+
 // Decoded fragments of pair P of a tile for this lane.
 template <int ENC>
 __device__ __forceinline__ void tile_frags(const uint8_t *tp, int P, int lane, uint32_t (&fr)[4][4]) {

@@ -630,30 +630,7 @@ __global__ void k_tile_experts(const uint8_t *const *mats, uint8_t *out, int E, 
         const int s = tile / RT, rt = tile - s * RT;
         const size_t rowb = (size_t)(down ? F : D) / 32 * X::GB;
         const uint8_t *src = mats[mat] + (size_t)rt * 16 * rowb + (size_t)s * 8 * X::GB;
-        uint8_t *dst = out + (size_t)mat * MB + (size_t)tile * X::TB;
-        const int g = lane >> 2, t = lane & 3;
-        const uint32_t *rg = reinterpret_cast<const uint32_t *>(src + g * rowb);
-        const uint32_t *r8 = reinterpret_cast<const uint32_t *>(src + (g + 8) * rowb);
-        for (int P = 0; P < 4; ++P) {
-            uint32_t a1, a2, a3, a4, b1, b2, b3, b4;
-            float d0, d1;
-            load_pair_words<ENC>(rg, P, t, a1, a2, a3, a4, d0, d1);
-            load_pair_words<ENC>(r8, P, t, b1, b2, b3, b4, d0, d1);
-            if (ENC == CPG_ENC_Q4) {
-                *reinterpret_cast<uint4 *>(dst + (P * 32 + lane) * 16) = make_uint4(a1, a2, b1, b2);
-            } else {
-                *reinterpret_cast<uint4 *>(dst + (P * 32 + lane) * 16) = make_uint4(a1, a2, a3, a4);
-                *reinterpret_cast<uint4 *>(dst + 2048 + (P * 32 + lane) * 16) = make_uint4(b1, b2, b3, b4);
-            }
-        }
-        if (t < 2) {                                           // lane t = 0: row g, t = 1: row g + 8
-            const uint8_t *row = src + (g + 8 * t) * rowb;
-            uint32_t w[4];
-            for (int j = 0; j < 4; ++j)
-                w[j] = (uint32_t)*reinterpret_cast<const uint16_t *>(row + 2 * j * X::GB) |
-                       ((uint32_t)*reinterpret_cast<const uint16_t *>(row + (2 * j + 1) * X::GB) << 16);
-            *reinterpret_cast<uint4 *>(dst + X::DB + g * 32 + t * 16) = make_uint4(w[0], w[1], w[2], w[3]);
-        }
+        tile_build_lane<ENC>(src, rowb, out + (size_t)mat * MB + (size_t)tile * X::TB, lane);
     }
 }
 

@@ -27,6 +27,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "expert_tile.cuh"
 #include "gemm_tc.cuh"
 
 namespace cpg {
@@ -568,6 +569,104 @@ __global__ void __launch_bounds__(AS_THREADS) k_attention_split(const float *__r
     if (tid == 0) cnt[i * H + h] = 0;                             // ready for the next launch
 }
 
+// A step of several sequences, one block per (KV head, token): the H/KV query heads sharing the
+// KV head are the block's warps, so each cached key and value row is read once for all of them
+// (qwen3_moe.c:135-155 per head). The head norm and RoPE of q and of the new key happen here (as
+// in k_attention_split with `nr`), and the new key and value go into the token's slot at its
+// position. Positions are taken in chunks of AG_CHUNK rows staged in shared memory (rows padded
+// to AG_RS floats, so lane j reads row j without bank conflicts); per warp:
+//   scores   lane j: s_j = Σ_e q[e]·k_j[e] (fused multiply-adds in element order) / √hd
+//   softmax  online over the chunks: running max m, sum l and output o rescaled by e^(m - m')
+//            when a chunk raises the max
+//   output   lane l holds elements 4l..4l+3: o += e^(s_j - m)·v_j, positions in order; o / l
+constexpr int AG_CHUNK = 64, AG_RS = QW_HD + 4;
+static size_t attention_group_smem() { return (size_t)2 * AG_CHUNK * AG_RS * sizeof(float); }
+__global__ void __launch_bounds__(256) k_attention_group(const float *__restrict__ q, float *__restrict__ kc,
+                                                         float *__restrict__ vc, int H, int KV, const AttnNorm nr,
+                                                         const AttnSeqs seq, float *__restrict__ ao) {
+    pdl_wait();
+    pdl_launch_dependents();
+    extern __shared__ __align__(16) float ag[];
+    float *sK = ag, *sV = ag + AG_CHUNK * AG_RS;
+    __shared__ __align__(16) float s_q[8][QW_HD];
+    __shared__ __align__(16) float s_new[2][QW_HD];
+    const int kh = blockIdx.x, i = blockIdx.y, G = H / KV;
+    const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+    const int h = kh * G + w;
+    const int pos = seq.tok_pos[i], n = pos + 1;
+    const size_t off = (size_t)seq.tok_slot[i] * seq.slot_elems, ks = (size_t)KV * QW_HD;
+    kc += off;
+    vc += off;
+    const size_t krow = ((size_t)i * KV + kh) * QW_HD;
+    if (w < G) head_norm_rope(q + ((size_t)i * H + h) * QW_HD, nr.qn, (float)pos, nr.theta, nr.eps, s_q[w]);
+    if (w == 0) head_norm_rope(nr.kst + krow, nr.kn, (float)pos, nr.theta, nr.eps, s_new[0]);
+    if (w == 1)
+        for (int e = lane; e < QW_HD; e += 32) s_new[1][e] = nr.vst[krow + e];
+    __syncthreads();
+    for (int e = tid; e < 2 * QW_HD; e += blockDim.x)            // the cache rows for later steps
+        ((e < QW_HD ? kc : vc) + (size_t)pos * ks + (size_t)kh * QW_HD)[e % QW_HD] = s_new[e / QW_HD][e % QW_HD];
+    const float scale = __fsqrt_rn((float)QW_HD);
+    float m = -INFINITY, l = 0.0f;
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int c0 = 0; c0 < n; c0 += AG_CHUNK) {
+        const int cn = min(AG_CHUNK, n - c0);
+        __syncthreads();                                          // the previous chunk is consumed
+        for (int idx = tid; idx < cn * (QW_HD / 4); idx += blockDim.x) {
+            const int r = idx / (QW_HD / 4), c4 = idx % (QW_HD / 4), j = c0 + r;
+            float4 kv, vv;
+            if (j == pos) {
+                kv = *reinterpret_cast<const float4 *>(&s_new[0][4 * c4]);
+                vv = *reinterpret_cast<const float4 *>(&s_new[1][4 * c4]);
+            } else {
+                kv = __ldg(reinterpret_cast<const float4 *>(kc + (size_t)j * ks + (size_t)kh * QW_HD) + c4);
+                vv = __ldg(reinterpret_cast<const float4 *>(vc + (size_t)j * ks + (size_t)kh * QW_HD) + c4);
+            }
+            *reinterpret_cast<float4 *>(sK + r * AG_RS + 4 * c4) = kv;
+            *reinterpret_cast<float4 *>(sV + r * AG_RS + 4 * c4) = vv;
+        }
+        __syncthreads();
+        if (w >= G) continue;
+        float sc[2];
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            const int r = lane + 32 * u;
+            if (r < cn) {
+                const float4 *kr = reinterpret_cast<const float4 *>(sK + r * AG_RS);
+                const float4 *qr = reinterpret_cast<const float4 *>(s_q[w]);
+                float acc = 0.0f;
+#pragma unroll 8
+                for (int c = 0; c < QW_HD / 4; ++c) {
+                    const float4 kv = kr[c], qv = qr[c];
+                    acc = fmaf(qv.x, kv.x, acc);
+                    acc = fmaf(qv.y, kv.y, acc);
+                    acc = fmaf(qv.z, kv.z, acc);
+                    acc = fmaf(qv.w, kv.w, acc);
+                }
+                sc[u] = __fdiv_rn(acc, scale);
+            } else {
+                sc[u] = -INFINITY;
+            }
+        }
+        const float mn = fmaxf(m, warp_max(fmaxf(sc[0], sc[1])));
+        const float rs = expf(__fsub_rn(m, mn));                  // 0 on the first chunk
+        const float p0 = expf(__fsub_rn(sc[0], mn)), p1 = expf(__fsub_rn(sc[1], mn));
+        l = fmaf(l, rs, warp_sum(p0 + p1));
+        o.x *= rs; o.y *= rs; o.z *= rs; o.w *= rs;
+        for (int r = 0; r < cn; ++r) {
+            const float p = __shfl_sync(0xffffffffu, r < 32 ? p0 : p1, r & 31);
+            const float4 v = *reinterpret_cast<const float4 *>(sV + r * AG_RS + 4 * lane);
+            o.x = fmaf(p, v.x, o.x);
+            o.y = fmaf(p, v.y, o.y);
+            o.z = fmaf(p, v.z, o.z);
+            o.w = fmaf(p, v.w, o.w);
+        }
+        m = mn;
+    }
+    if (w < G)
+        *reinterpret_cast<float4 *>(ao + ((size_t)i * H + h) * QW_HD + 4 * lane) =
+            make_float4(__fdiv_rn(o.x, l), __fdiv_rn(o.y, l), __fdiv_rn(o.z, l), __fdiv_rn(o.w, l));
+}
+
 // Ranges per (query, head) for T queries of H heads: enough blocks for four waves of 148 SMs.
 static int as_splits(int T, int H) {
     const int pairs = T * H, want = 4 * 148;
@@ -687,6 +786,27 @@ struct GemvSeg {
 int gemv_multi(const GemvSeg *segs, int nseg, const float *x, int T, const float *norm, float eps, int n_in, int enc,
                cudaStream_t s);
 int layer_dims(const cpg_moe_layer *L, int *D, int *F, int *E, int *K);
+bool dense_ok(int enc, int rows, int k);
+size_t dense_act_bytes(int T, int K);
+int dense_build(const void *w, int enc, int rows, int k, uint8_t **tiles, cudaStream_t s);
+int dense_prep(const float *x, int T, int K, const float *gain, float eps, int enc, uint8_t *xh, cudaStream_t s);
+int dense_run(const uint8_t *const *tiles, const int *rows, float *const *outs, int nseg, int enc, int K,
+              const uint8_t *xh, int T, float *planes, size_t planes_floats, int *counters, int n_counters,
+              int *status, cudaStream_t s);
+constexpr int QW_DENSE_DEC_MIN_T = 5, QW_DENSE_DEC_MAX_T = 64;   // steps of several sequences on dense.cu
+
+// Decode tile copies of the attention projections and the lm_head (dense.cu), for steps of
+// QW_DENSE_DEC_MIN_T .. QW_DENSE_DEC_MAX_T sequences, with their operand and split-K buffers.
+struct QwDense {
+    std::vector<uint8_t *> attn;                   // 4 per layer: Wq, Wk, Wv, Wo
+    uint8_t *head = nullptr;
+    uint8_t *xh = nullptr;
+    float *planes = nullptr;
+    size_t planes_floats = 0;
+    int *counters = nullptr;                       // split K, one per band
+    int *status = nullptr;
+};
+constexpr int QW_DENSE_COUNTERS = 1024;
 
 }  // namespace cpg
 
@@ -876,6 +996,7 @@ struct QwSeq {
     int *as_cnt;
     float *logits, *am_v;
     int *am_i, *d_next;
+    const QwDense *dn;              // several sequences: the dense.cu path, or null
 };
 
 // Enqueue T tokens (ids in m->d_ids[0..T)) through embed, the layers and the head. Nothing here
@@ -904,7 +1025,16 @@ static int qwen3_enqueue(cpg_qwen3 *m, const QwSeq &sq, int T, cudaStream_t s) {
         // streaming launch; otherwise separately
         const int enc = A.wq.enc;
         int rc = 1;
-        if (dense) {
+        const bool ddec = sq.dn && T >= QW_DENSE_DEC_MIN_T && T <= QW_DENSE_DEC_MAX_T;
+        if (ddec) {
+            const uint8_t *tl[3] = {sq.dn->attn[4 * l], sq.dn->attn[4 * l + 1], sq.dn->attn[4 * l + 2]};
+            const int rows[3] = {QD, KD, KD};
+            float *const outs[3] = {m->q, m->kst, m->vst};
+            rc = dense_prep(m->x, T, D, A.ln1, m->eps, enc, sq.dn->xh, s);
+            if (!rc) rc = dense_run(tl, rows, outs, 3, enc, D, sq.dn->xh, T, sq.dn->planes, sq.dn->planes_floats,
+                                    sq.dn->counters, QW_DENSE_COUNTERS, sq.dn->status, s);
+            if (rc) return rc;
+        } else if (dense) {
             k_rmsnorm_f16<<<T, 256, 0, s>>>(m->x, A.ln1, D, m->eps, m->x16);
             CPG_CUDA(cudaGetLastError());
             rc = gemm_tc_dense(maps, m->dtab + 0, m->dn_active, m->iota, m->x16, T, QD, D, m->q, m->planes, m->d_status, s);
@@ -936,6 +1066,9 @@ static int qwen3_enqueue(cpg_qwen3 *m, const QwSeq &sq, int T, cudaStream_t s) {
             k_attention_prompt<<<dim3(H, (T + AP_QT - 1) / AP_QT), 256, attention_prompt_smem(n_cap), s>>>(
                 (const float *)m->q, (const float *)kc, (const float *)vc, sq.d_pos, T, H, KV, n_cap, m->ao);
             CPG_CUDA(cudaGetLastError());
+        } else if (multi && T * KV >= 148 && H / KV <= 8) {
+            CPG_CUDA(launch_pdl(k_attention_group, dim3(KV, T), dim3(32 * (H / KV)), attention_group_smem(), s,
+                                (const float *)m->q, kc, vc, H, KV, nr, aseq, m->ao));
         } else if (multi || T < QW_DENSE_MIN_T) {
             const int ns = as_splits(T, H);
             const size_t ssmem = (size_t)((sq.C + ns - 1) / ns) * sizeof(float);
@@ -946,7 +1079,14 @@ static int qwen3_enqueue(cpg_qwen3 *m, const QwSeq &sq, int T, cudaStream_t s) {
             CPG_CUDA(launch_pdl(k_attention, dim3(H, T), dim3(AT_THREADS), asmem, s, (const float *)m->q,
                                 (const float *)kc, (const float *)vc, sq.d_pos, H, KV, m->ao));
         }
-        if (dense) {
+        if (ddec) {
+            const uint8_t *tl[1] = {sq.dn->attn[4 * l + 3]};
+            const int rows[1] = {D};
+            float *const outs[1] = {m->at};
+            rc = dense_prep(m->ao, T, QD, nullptr, 0.0f, A.wo.enc, sq.dn->xh, s);
+            if (!rc) rc = dense_run(tl, rows, outs, 1, A.wo.enc, QD, sq.dn->xh, T, sq.dn->planes, sq.dn->planes_floats,
+                                    sq.dn->counters, QW_DENSE_COUNTERS, sq.dn->status, s);
+        } else if (dense) {
             const size_t n = (size_t)T * QD;
             k_split_f16<<<(int)((n + 255) / 256 < 1184 ? (n + 255) / 256 : 1184), 256, 0, s>>>(m->ao, T, QD, m->x16);
             CPG_CUDA(cudaGetLastError());
@@ -963,24 +1103,36 @@ static int qwen3_enqueue(cpg_qwen3 *m, const QwSeq &sq, int T, cudaStream_t s) {
     const int hr = multi ? T : 1;
     const float *xl = m->x + (size_t)(T - hr) * D;
     const GemvSeg hseg{(const uint8_t *)m->lm_head.p, sq.logits, m->V};
-    int rc = m->lm_head.enc == CPG_ENC_F32 ? 1 : gemv_multi(&hseg, 1, xl, hr, m->final_norm, m->eps, D, m->lm_head.enc, s);
+    int rc = 1;
+    if (multi && sq.dn && sq.dn->head && hr >= QW_DENSE_DEC_MIN_T && hr <= QW_DENSE_DEC_MAX_T) {
+        const uint8_t *tl[1] = {sq.dn->head};
+        const int rows[1] = {m->V};
+        float *const outs[1] = {sq.logits};
+        rc = dense_prep(xl, hr, D, m->final_norm, m->eps, m->lm_head.enc, sq.dn->xh, s);
+        if (!rc) rc = dense_run(tl, rows, outs, 1, m->lm_head.enc, D, sq.dn->xh, hr, sq.dn->planes,
+                                sq.dn->planes_floats, sq.dn->counters, QW_DENSE_COUNTERS, sq.dn->status, s);
+        if (rc) return rc;
+    } else if (m->lm_head.enc != CPG_ENC_F32) {
+        rc = gemv_multi(&hseg, 1, xl, hr, m->final_norm, m->eps, D, m->lm_head.enc, s);
+    }
     if (rc == 1) {
         k_rmsnorm<<<hr, 256, 0, s>>>(xl, m->final_norm, D, m->eps, m->xn);
         CPG_CUDA(cudaGetLastError());
         rc = matvec_launch(sq.logits, m->xn, m->lm_head, D, m->V, hr, s);
     }
     if (rc) return rc;
-    CPG_CUDA(launch_pdl(k_argmax_part, dim3(AM_BLOCKS, hr), dim3(512), 0, s, (const float *)sq.logits, m->V, sq.am_v,
+    const int parts = std::min(AM_BLOCKS, std::max(4, (2 * AM_BLOCKS + hr - 1) / hr));   // chunks per row
+    CPG_CUDA(launch_pdl(k_argmax_part, dim3(parts, hr), dim3(512), 0, s, (const float *)sq.logits, m->V, sq.am_v,
                         sq.am_i));
     CPG_CUDA(launch_pdl(k_argmax_final, dim3(hr), dim3(256), 0, s, (const float *)sq.am_v, (const int *)sq.am_i,
-                        AM_BLOCKS, sq.d_next));
+                        parts, sq.d_next));
     return CPG_OK;
 }
 
 // The model's own sequence: slot 0 of its own cache.
 static QwSeq own_seq(cpg_qwen3 *m, int T) {
     return QwSeq{m->kv, 1, m->max_ctx, m->d_pos, 0, nullptr, nullptr, m->pos + T, m->as_part, m->as_cnt,
-                 m->logits, m->am_v, m->am_i, m->d_next};
+                 m->logits, m->am_v, m->am_i, m->d_next, nullptr};
 }
 
 // One token at the current device position: the captured step graph (built on first use).
@@ -1092,16 +1244,20 @@ struct cpg_qwen3_batch {
     int *am_i = nullptr, *as_cnt = nullptr;
     int last_rows = 0;
     std::vector<cudaGraphExec_t> graphs; // one step of n sequences, by n
+    QwDense dn;                          // the dense.cu projections and head, when the shapes allow
 };
 
 // The projection GEMM's bounded waits (prompts and steps of QW_DENSE_MIN_T tokens or more).
-static int qwen3_status(cpg_qwen3 *m, const char *fn) {
-    if (!m->d_status) return CPG_OK;
-    int st = 0;
-    CPG_CUDA(cudaMemcpy(&st, m->d_status, sizeof(int), cudaMemcpyDeviceToHost));
-    if (st != ST_OK) {
-        set_error("%s: a bounded wait in the projection GEMM timed out (status %d)", fn, st);
-        return CPG_ETIMEOUT;
+static int qwen3_status(cpg_qwen3 *m, const char *fn, const int *extra = nullptr) {
+    const int *words[2] = {m->d_status, extra};
+    for (const int *w : words) {
+        if (!w) continue;
+        int st = 0;
+        CPG_CUDA(cudaMemcpy(&st, w, sizeof(int), cudaMemcpyDeviceToHost));
+        if (st != ST_OK) {
+            set_error("%s: a bounded wait in a projection kernel timed out (status %d)", fn, st);
+            return CPG_ETIMEOUT;
+        }
     }
     return CPG_OK;
 }
@@ -1112,6 +1268,8 @@ static void batch_free(cpg_qwen3_batch *b) {
     cudaFree(b->kv); cudaFree(b->slot_pos); cudaFree(b->tok_slot); cudaFree(b->tok_pos);
     cudaFree(b->d_next); cudaFree(b->d_step); cudaFree(b->d_out); cudaFree(b->logits); cudaFree(b->am_v);
     cudaFree(b->am_i); cudaFree(b->as_part); cudaFree(b->as_cnt);
+    for (uint8_t *p : b->dn.attn) cudaFree(p);
+    cudaFree(b->dn.head); cudaFree(b->dn.xh); cudaFree(b->dn.planes); cudaFree(b->dn.status); cudaFree(b->dn.counters);
     if (b->h_buf) cudaFreeHost(b->h_buf);
     delete b;
 }
@@ -1145,10 +1303,50 @@ extern "C" int cpg_qwen3_batch_create(cpg_qwen3 *m, int n_slots, int max_ctx, cp
     if (ce == cudaSuccess) ce = cudaMalloc(&b->as_cnt, S * m->H * sizeof(int));
     if (ce == cudaSuccess) ce = cudaMemsetAsync(b->as_cnt, 0, S * m->H * sizeof(int), m->s);
     if (ce == cudaSuccess) ce = cudaMemsetAsync(b->slot_pos, 0, S * sizeof(int), m->s);
+    if (ce == cudaSuccess)
+        ce = cudaFuncSetAttribute(k_attention_group, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)attention_group_smem());
     if (ce == cudaSuccess) ce = cudaStreamSynchronize(m->s);
     if (ce != cudaSuccess) {
         batch_free(b);
         return cuda_fail(ce, "cpg_qwen3_batch_create: allocation");
+    }
+    // steps of QW_DENSE_DEC_MIN_T .. QW_DENSE_DEC_MAX_T sequences: decode tile copies of every
+    // projection and of the lm_head (dense.cu), when every matrix is Q4_0 / Q8_0 of a usable shape
+    const int QD = m->H * QW_HD, KDi = m->KV * QW_HD, D = m->D;
+    bool dn = n_slots >= QW_DENSE_DEC_MIN_T;
+    for (int l = 0; l < m->L && dn; ++l) {
+        const cpg_qwen3_attn &A = m->attn[l];
+        dn = A.wk.enc == A.wq.enc && A.wv.enc == A.wq.enc && dense_ok(A.wq.enc, QD, D) && dense_ok(A.wk.enc, KDi, D) &&
+             dense_ok(A.wo.enc, D, QD);
+    }
+    if (dn) {
+        int rc = CPG_OK;
+        for (int l = 0; l < m->L && !rc; ++l) {
+            const cpg_qwen3_attn &A = m->attn[l];
+            const cpg_tensor w[4] = {A.wq, A.wk, A.wv, A.wo};
+            const int rows[4] = {QD, KDi, KDi, D}, ks[4] = {D, D, D, QD};
+            for (int i = 0; i < 4 && !rc; ++i) {
+                uint8_t *t = nullptr;
+                rc = dense_build(w[i].p, w[i].enc, rows[i], ks[i], &t, m->s);
+                if (!rc) b->dn.attn.push_back(t);
+            }
+        }
+        if (!rc && dense_ok(m->lm_head.enc, m->V, D)) rc = dense_build(m->lm_head.p, m->lm_head.enc, m->V, D, &b->dn.head, m->s);
+        const int kmax = QD > D ? QD : D;
+        b->dn.planes_floats = (size_t)16 * QW_DENSE_DEC_MAX_T * (QD + 2 * KDi > D ? QD + 2 * KDi : D);
+        if (!rc) ce = cudaMalloc(&b->dn.xh, dense_act_bytes(QW_DENSE_DEC_MAX_T, kmax));
+        if (!rc && ce == cudaSuccess) ce = cudaMalloc(&b->dn.planes, b->dn.planes_floats * sizeof(float));
+        if (!rc && ce == cudaSuccess) ce = cudaMalloc(&b->dn.status, sizeof(int));
+        if (!rc && ce == cudaSuccess) ce = cudaMemsetAsync(b->dn.status, 0, sizeof(int), m->s);
+        if (!rc && ce == cudaSuccess) ce = cudaMalloc(&b->dn.counters, QW_DENSE_COUNTERS * sizeof(int));
+        if (!rc && ce == cudaSuccess) ce = cudaMemsetAsync(b->dn.counters, 0, QW_DENSE_COUNTERS * sizeof(int), m->s);
+        if (!rc && ce == cudaSuccess) ce = cudaStreamSynchronize(m->s);
+        if (!rc && ce != cudaSuccess) rc = cuda_fail(ce, "cpg_qwen3_batch_create: dense projections");
+        if (rc) {
+            batch_free(b);
+            return rc;
+        }
     }
     *out = b;
     return CPG_OK;
@@ -1171,7 +1369,7 @@ extern "C" int cpg_qwen3_batch_prefill(cpg_qwen3_batch *b, int slot, const int *
     CPG_CUDA(cudaMemsetAsync(b->slot_pos + slot, 0, sizeof(int), m->s));
     CPG_CUDA(cudaMemcpyAsync(m->d_ids, ids, sizeof(int) * (size_t)n, cudaMemcpyHostToDevice, m->s));
     const QwSeq sq{b->kv, b->S, b->C, b->slot_pos + slot, slot, nullptr, nullptr, n, m->as_part, m->as_cnt,
-                   b->logits, b->am_v, b->am_i, b->d_next};
+                   b->logits, b->am_v, b->am_i, b->d_next, nullptr};
     int rc = qwen3_enqueue(m, sq, n, m->s);
     if (rc) return rc;
     b->h_buf[0] = n;
@@ -1213,7 +1411,7 @@ static int batch_run(cpg_qwen3_batch *b, const int *slots, const int *ids, int n
     CPG_CUDA(cudaMemsetAsync(b->d_step, 0, sizeof(int), m->s));
     if (!b->graphs[n]) {
         const QwSeq sq{b->kv, b->S, b->C, nullptr, -1, b->tok_slot, b->tok_pos, 0, b->as_part, b->as_cnt,
-                       b->logits, b->am_v, b->am_i, b->d_next};
+                       b->logits, b->am_v, b->am_i, b->d_next, b->dn.attn.empty() ? nullptr : &b->dn};
         cudaGraph_t g = nullptr;
         CPG_CUDA(cudaStreamBeginCapture(m->s, cudaStreamCaptureModeThreadLocal));
         int rc = 0;
@@ -1251,7 +1449,7 @@ extern "C" int cpg_qwen3_batch_step(cpg_qwen3_batch *b, const int *slots, const 
     if (rc) return rc;
     CPG_CUDA(cudaMemcpyAsync(next_ids, b->d_out, sizeof(int) * n, cudaMemcpyDeviceToHost, b->m->s));
     CPG_CUDA(cudaStreamSynchronize(b->m->s));
-    return qwen3_status(b->m, "cpg_qwen3_batch_step");
+    return qwen3_status(b->m, "cpg_qwen3_batch_step", b->dn.status);
 }
 
 extern "C" int cpg_qwen3_batch_generate(cpg_qwen3_batch *b, const int *slots, const int *ids, int n, int n_steps,
@@ -1264,7 +1462,7 @@ extern "C" int cpg_qwen3_batch_generate(cpg_qwen3_batch *b, const int *slots, co
     if (rc) return rc;
     CPG_CUDA(cudaMemcpyAsync(out_ids, b->d_out, sizeof(int) * (size_t)n * n_steps, cudaMemcpyDeviceToHost, b->m->s));
     CPG_CUDA(cudaStreamSynchronize(b->m->s));
-    return qwen3_status(b->m, "cpg_qwen3_batch_generate");
+    return qwen3_status(b->m, "cpg_qwen3_batch_generate", b->dn.status);
 }
 
 extern "C" int cpg_qwen3_batch_position(const cpg_qwen3_batch *b, int slot) {

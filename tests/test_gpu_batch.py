@@ -52,6 +52,29 @@ def test_batch_matches_reference_per_sequence(orc, ref):
         gm.close()
 
 
+def test_batch_of_twelve_on_dense_kernel(orc, ref):
+    """12 sequences: the step's projections and lm_head run on the dense tensor-core kernel
+    (5 to 64 token rows: decode tile copies, fp16 hi + lo activations, f32 group scales)."""
+    from cachepotato_b200.qwen3 import Qwen3Batch
+    m = _small(orc, 41)
+    prompts = _prompts(m.vocab, list(range(1, 13)), 42)
+    n_new = 4
+    gm = device_model(m, max_ctx=32)
+    b = Qwen3Batch(gm, 12, 20)
+    try:
+        first = [b.prefill(j, p) for j, p in enumerate(prompts)]
+        slots = np.arange(12)[::-1].copy()                       # reversed slot order
+        out = b.generate(slots, [first[j] for j in slots], n_new)
+        lg = b.logits().cpu().numpy()
+        for r, j in enumerate(slots):
+            want_ids, want_logits = ref.qwen3_generate(m, prompts[j], n_new)
+            assert [first[j]] + out[:, r].tolist() == want_ids.tolist(), f"slot {j}"
+            assert max_rel(lg[r], want_logits) <= BLOCK_TOL
+    finally:
+        b.close()
+        gm.close()
+
+
 def test_continuous_batching_join_and_leave(orc, ref):
     """Sequences join (prefill into a free slot) and leave between steps, in changing orders; a
     finished sequence's slot is reused. Each sequence's ids equal the reference's for its prompt."""
