@@ -69,9 +69,10 @@ __device__ __forceinline__ void warp_topk(const float (&p)[PL], int E, int K, in
 // order: the reference scan's result without its K sequential passes (the loops stay short:
 // this code runs once per launch, so its instruction fetch is part of the latency). A NaN
 // probability makes ranks meaningless; warp 0 then runs the scan itself (warp_topk, which
-// reproduces the reference's NaN behaviour). s_p: shared memory for MAXE + MAXK floats; sel_e,
-// sel_w: K ids and weights, in shared or global memory. Every thread of the CTA calls it.
-template <int MAXE, int MAXK>
+// reproduces the reference's NaN behaviour). logits: global memory, or shared memory with
+// LOGITS_SMEM; s_p: shared memory for MAXE + MAXK floats; sel_e, sel_w: K ids and weights, in
+// shared or global memory. Every thread of the CTA calls it.
+template <int MAXE, int MAXK, bool LOGITS_SMEM = false>
 __device__ void select_topk(const float *logits, int E, int K, int *sel_e, float *sel_w, float *s_p) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     constexpr int PL = MAXE / 32;
@@ -82,7 +83,7 @@ __device__ void select_topk(const float *logits, int E, int K, int *sel_e, float
 #pragma unroll
         for (int i = 0; i < PL; ++i) {
             const int e = lane + 32 * i;
-            p[i] = e < E ? __ldcg(logits + e) : -INFINITY;
+            p[i] = e < E ? (LOGITS_SMEM ? logits[e] : __ldcg(logits + e)) : -INFINITY;
             mx = fmaxf(mx, p[i]);
         }
         mx = warp_max(mx);
@@ -134,10 +135,10 @@ __device__ void select_topk(const float *logits, int E, int K, int *sel_e, float
         }
         __syncthreads();
     }
-    if (tid == 0) {                                      // qwen3_moe.c:195-197, selection order
-        float s = 0.0f;
+    if (tid < K) {                                       // qwen3_moe.c:195-197: the sum in selection
+        float s = 0.0f;                                  // order (every thread the same), one division each
         for (int j = 0; j < K; ++j) s += s_p[MAXE + j];
-        for (int j = 0; j < K; ++j) sel_w[j] = __fdiv_rn(s_p[MAXE + j], s);
+        sel_w[tid] = __fdiv_rn(s_p[MAXE + tid], s);
     }
     __syncthreads();
 }

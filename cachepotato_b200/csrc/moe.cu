@@ -263,25 +263,56 @@ __device__ int group_cta(const int *topk, int T, int K, int E, int4 *s_act, int 
     return *s_u;
 }
 
+// Sum of each of the N values over the warp's 32 lanes: for N = 32 or 64 by halving exchanges
+// (N - 2 or N - 1 shuffles; lane L ends with the sums of values (N/32)·L + j in v[j]), else one
+// warp sum per value (every lane ends with all N sums).
+template <int N>
+__device__ __forceinline__ void warp_sums(float (&v)[N]) {
+    const int lane = threadIdx.x & 31;
+    if constexpr (N == 32 || N == 64) {
+#pragma unroll
+        for (int o = 16, n = N / 2; o >= 1; o >>= 1, n >>= 1) {
+            const bool up = lane & o;                   // keep the upper half of the current range
+#pragma unroll
+            for (int i = 0; i < n; ++i) {
+                const float send = up ? v[i] : v[n + i];
+                const float keep = up ? v[n + i] : v[i];
+                v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+            }
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < N; ++i) v[i] = warp_sum(v[i]);
+    }
+}
+
 // TB tokens per CTA: 8, or the batch itself for one or two tokens (a tile of 8 costs a lone token
-// the larger staging and the unrolled token loops).
+// the larger staging and the unrolled token loops). Dynamic shared memory: the tile's (TB, D)
+// rows and the gain (D), copied in at kernel entry (it does not depend on the previous kernel).
+// The router rows are read from L2 (prefetched at entry): staged in shared memory they make the
+// CTA too large to share an SM with the previous kernel's CTAs, and the clusters start late.
 template <int TB>
 __global__ void __launch_bounds__(R_THREADS, 2) k_router(RouterArgs a) {
-    extern __shared__ float xs[];                         // (TB, D): hh, then xn
-    __shared__ int s_last;
+    extern __shared__ __align__(16) float xs[];           // (TB, D): hh, then xn; then the gain
     __shared__ uint8_t s_p2e[64];
+    __shared__ float s_red[R_THREADS / 32][TB];
+    __shared__ float s_inv[TB];
+    __shared__ float s_part[R_THREADS / 32][TB * 4];
+    __shared__ float s_lg[TB][MAX_E];                     // logits of the tokens this CTA routes
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int t0 = blockIdx.y * TB, nt = min(TB, a.T - t0);
     if (tid < 64) s_p2e[tid] = perm_of(a.xn_enc).pos_to_elem[tid];
     const int e0 = blockIdx.x * a.eb;
-    const int D = a.D;
-    {   // the router rows and the gain do not depend on the previous kernel: into L2 meanwhile
+    const int ne = max(0, min(a.eb, a.E - e0));
+    const int D = a.D, D4 = D / 4;
+    float *gsm = xs + TB * D;
+    {   // the gain into shared memory, the router rows into L2
+        for (int i = tid; i < D4; i += R_THREADS)
+            cp_async16(reinterpret_cast<float4 *>(gsm) + i, reinterpret_cast<const float4 *>(a.ln2) + i);
         const char *wb = reinterpret_cast<const char *>(a.wgate + (size_t)e0 * D);
-        const size_t wbytes = (size_t)max(0, min(a.eb, a.E - e0)) * D * sizeof(float);
+        const size_t wbytes = (size_t)ne * D * sizeof(float);
         for (size_t o = (size_t)tid * 128; o < wbytes; o += (size_t)R_THREADS * 128)
             asm volatile("prefetch.global.L2 [%0];" ::"l"(wb + o));
-        for (int o = tid * 128; o < D * (int)sizeof(float); o += R_THREADS * 128)
-            asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<const char *>(a.ln2) + o));
     }
     pdl_wait();                                           // x comes from the previous kernel
     pdl_launch_dependents();
@@ -292,7 +323,6 @@ __global__ void __launch_bounds__(R_THREADS, 2) k_router(RouterArgs a) {
         for (int i = tid; i < (D > a.F ? D : a.F) / 2; i += R_THREADS)
             reinterpret_cast<uint32_t *>(a.zero_row)[i] = 0u;
     }
-    __syncthreads();
 
     // hh = x + attn (qwen3_moe.c:178). The loads are issued 16 at a time per thread before any
     // store, so the tile costs about one memory round trip (the kernel is latency-bound).
@@ -300,7 +330,7 @@ __global__ void __launch_bounds__(R_THREADS, 2) k_router(RouterArgs a) {
         const float4 *x4 = reinterpret_cast<const float4 *>(a.x + (size_t)t0 * D);
         const float4 *a4 = a.attn ? reinterpret_cast<const float4 *>(a.attn + (size_t)t0 * D) : nullptr;
         float4 *s4 = reinterpret_cast<float4 *>(xs);
-        const int n4 = nt * D / 4;
+        const int n4 = nt * D4;
         for (int i0 = tid; i0 < n4; i0 += 16 * R_THREADS) {
             float4 v[16];
 #pragma unroll
@@ -326,56 +356,50 @@ __global__ void __launch_bounds__(R_THREADS, 2) k_router(RouterArgs a) {
         }
     }
     __syncthreads();
-    // rmsnorm (kernels.c:408-413): inv = 1 / sqrt(sum(x^2)/n + eps); xn = x * inv * g.
-    // One warp per token throughout, so no index division is needed; a lone token (a decode step
-    // of batch 1) is normalised by the whole CTA instead.
-    if (nt == 1) {
-        __shared__ float s_rs[R_THREADS / 32];
-        float ss = 0.0f;
-        for (int k = tid; k < D; k += R_THREADS) ss = fmaf(xs[k], xs[k], ss);
-        ss = warp_sum(ss);
-        if (lane == 0) s_rs[warp] = ss;
-        __syncthreads();
-        float tot = 0.0f;
+    // rmsnorm (kernels.c:408-413): inv = 1 / sqrt(sum(x^2)/n + eps); xn = x * inv * g. The sums of
+    // squares of all the tile's tokens with the whole CTA (float4 reads, a warp reduction per
+    // token, warps added in order), then the scaling pass.
+    {
+        const float4 *s4 = reinterpret_cast<const float4 *>(xs);
+        float ss[TB];
 #pragma unroll
-        for (int w = 0; w < R_THREADS / 32; ++w) tot += s_rs[w];
-        const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fdiv_rn(tot, (float)D) + a.eps));
-        const float4 *g4 = reinterpret_cast<const float4 *>(a.ln2);
+        for (int t = 0; t < TB; ++t) {
+            ss[t] = 0.0f;
+            if (t < nt)
+                for (int c = tid; c < D4; c += R_THREADS) {
+                    const float4 v = s4[t * D4 + c];
+                    ss[t] = fmaf(v.x, v.x, ss[t]);
+                    ss[t] = fmaf(v.y, v.y, ss[t]);
+                    ss[t] = fmaf(v.z, v.z, ss[t]);
+                    ss[t] = fmaf(v.w, v.w, ss[t]);
+                }
+        }
+#pragma unroll
+        for (int t = 0; t < TB; ++t) ss[t] = warp_sum(ss[t]);
+        if (lane == 0)
+#pragma unroll
+            for (int t = 0; t < TB; ++t) s_red[warp][t] = ss[t];
+        cp_async_wait_all();                              // this thread's gain copies
+        __syncthreads();
+        if (tid < nt) {
+            float tot = 0.0f;
+#pragma unroll
+            for (int w = 0; w < R_THREADS / 32; ++w) tot += s_red[w][tid];
+            s_inv[tid] = __fdiv_rn(1.0f, __fsqrt_rn(__fdiv_rn(tot, (float)D) + a.eps));
+        }
+        __syncthreads();
+        const float4 *g4 = reinterpret_cast<const float4 *>(gsm);
         float4 *r4 = reinterpret_cast<float4 *>(xs);
-        for (int c = tid; c < D / 4; c += R_THREADS) {
-            const float4 gv = __ldg(g4 + c);
-            float4 v = r4[c];
+        for (int i = tid; i < nt * D4; i += R_THREADS) {
+            const int t = i / D4;
+            const float inv = s_inv[t];
+            const float4 gv = g4[i - t * D4];
+            float4 v = r4[i];
             v.x = __fmul_rn(__fmul_rn(v.x, inv), gv.x);
             v.y = __fmul_rn(__fmul_rn(v.y, inv), gv.y);
             v.z = __fmul_rn(__fmul_rn(v.z, inv), gv.z);
             v.w = __fmul_rn(__fmul_rn(v.w, inv), gv.w);
-            r4[c] = v;
-        }
-    } else if (warp < nt) {
-        float *row = xs + warp * D;
-        float ss = 0.0f;
-        for (int k = lane; k < D; k += 32) ss = fmaf(row[k], row[k], ss);
-        ss = warp_sum(ss);
-        const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fdiv_rn(ss, (float)D) + a.eps));
-        const float4 *g4 = reinterpret_cast<const float4 *>(a.ln2);
-        float4 *r4 = reinterpret_cast<float4 *>(row);
-        for (int c0 = lane; c0 < D / 4; c0 += 16 * 32) {
-            float4 gv[16];
-#pragma unroll
-            for (int u = 0; u < 16; ++u)
-                if (c0 + u * 32 < D / 4) gv[u] = __ldg(g4 + c0 + u * 32);
-#pragma unroll
-            for (int u = 0; u < 16; ++u) {
-                const int c = c0 + u * 32;
-                if (c < D / 4) {
-                    float4 v = r4[c];
-                    v.x = __fmul_rn(__fmul_rn(v.x, inv), gv[u].x);
-                    v.y = __fmul_rn(__fmul_rn(v.y, inv), gv[u].y);
-                    v.z = __fmul_rn(__fmul_rn(v.z, inv), gv[u].z);
-                    v.w = __fmul_rn(__fmul_rn(v.w, inv), gv[u].w);
-                    r4[c] = v;
-                }
-            }
+            r4[i] = v;
         }
     }
     __syncthreads();
@@ -395,55 +419,87 @@ __global__ void __launch_bounds__(R_THREADS, 2) k_router(RouterArgs a) {
             *reinterpret_cast<uint4 *>(dst + D + p0) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
         }
     }
-    // logits = Wgate·xn (matmul_wx, kernels.c:84-95): warp w owns experts e0 + w, e0 + w + 8, ...
-    for (int el = warp; el < a.eb; el += R_THREADS / 32) {
-        const int e = e0 + el;
-        if (e >= a.E) break;
-        float acc[TB];
+    // logits = Wgate·xn (matmul_wx, kernels.c:84-95), four experts of the CTA at a time: warp w
+    // takes the 128-value K chunks w, w + 8, ... of every (token, expert) pair (lane l: values
+    // 4l..4l+3 of the chunk; the router rows' loads of a group are all in flight before its
+    // FMAs), then the lanes' and the warps' partial sums are added (warps in order). Each logit
+    // goes to the logits output and into the shared memory of the cluster CTA that routes its
+    // token (rank t mod cluster size).
+    const int rank = cluster_ctarank(), csz = cluster_nctarank();
+    const float4 *xs4 = reinterpret_cast<const float4 *>(xs);
+    const float *wrow = a.wgate + (size_t)e0 * D;
+    constexpr int RC = 4;                                  // K chunks of a warp in registers at once
+    for (int eg = 0; eg < ne; eg += 4) {
+        float acc[TB * 4];
 #pragma unroll
-        for (int t = 0; t < TB; ++t) acc[t] = 0.0f;
-        const float4 *w4 = reinterpret_cast<const float4 *>(a.wgate + (size_t)e * D);
-        // the row's loads (16 float4 per lane for D = 2048) are all in flight before the FMAs;
-        // per lane the sum still runs over k ascending
-        for (int c0 = 0; c0 < D / 128; c0 += 16) {
-            float4 w[16];
+        for (int i = 0; i < TB * 4; ++i) acc[i] = 0.0f;
+        for (int c0 = warp; c0 < D / 128; c0 += RC * (R_THREADS / 32)) {
+            float4 w[RC][4];
 #pragma unroll
-            for (int c = 0; c < 16; ++c)
-                if (c0 + c < D / 128) w[c] = __ldg(w4 + (c0 + c) * 32 + lane);
+            for (int r = 0; r < RC; ++r) {
+                const int c = c0 + r * (R_THREADS / 32);
 #pragma unroll
-            for (int c = 0; c < 16; ++c) {
-                if (c0 + c < D / 128) {
-                    const int k = ((c0 + c) * 32 + lane) * 4;
+                for (int el = 0; el < 4; ++el)
+                    w[r][el] = c < D / 128 && eg + el < ne
+                                   ? __ldg(reinterpret_cast<const float4 *>(wrow + (size_t)(eg + el) * D) + c * 32 + lane)
+                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
 #pragma unroll
-                    for (int t = 0; t < TB; ++t) {
-                        if (t < nt) {
-                            const float4 v = *reinterpret_cast<const float4 *>(xs + t * D + k);
-                            acc[t] = fmaf(w[c].x, v.x, acc[t]);
-                            acc[t] = fmaf(w[c].y, v.y, acc[t]);
-                            acc[t] = fmaf(w[c].z, v.z, acc[t]);
-                            acc[t] = fmaf(w[c].w, v.w, acc[t]);
+            for (int r = 0; r < RC; ++r) {
+                const int c = c0 + r * (R_THREADS / 32);
+                if (c >= D / 128) break;
+#pragma unroll
+                for (int t = 0; t < TB; ++t) {
+                    if (t < nt) {
+                        const float4 xv = xs4[t * D4 + c * 32 + lane];
+#pragma unroll
+                        for (int el = 0; el < 4; ++el) {
+                            float v = acc[t * 4 + el];
+                            v = fmaf(w[r][el].x, xv.x, v);
+                            v = fmaf(w[r][el].y, xv.y, v);
+                            v = fmaf(w[r][el].z, xv.z, v);
+                            v = fmaf(w[r][el].w, xv.w, v);
+                            acc[t * 4 + el] = v;
                         }
                     }
                 }
             }
         }
+        warp_sums<TB * 4>(acc);
+        if constexpr (TB * 4 == 32) {
+            s_part[warp][lane] = acc[0];
+        } else {
+            if (lane == 0)
 #pragma unroll
-        for (int t = 0; t < TB; ++t) {
-            const float v = warp_sum(acc[t]);
-            if (lane == 0 && t < nt) a.logits[(size_t)(t0 + t) * a.E + e] = v;
+                for (int i = 0; i < TB * 4; ++i) s_part[warp][i] = acc[i];
         }
+        __syncthreads();
+        if (tid < TB * 4) {
+            const int t = tid >> 2, el = tid & 3;
+            if (t < nt && eg + el < ne) {
+                float v = 0.0f;
+#pragma unroll
+                for (int w2 = 0; w2 < R_THREADS / 32; ++w2) v += s_part[w2][tid];
+                const int e = e0 + eg + el;
+                a.logits[(size_t)(t0 + t) * a.E + e] = v;
+                const uint32_t dst = smem_u32(&s_lg[t / csz][e]);
+                uint32_t remote;
+                asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(dst), "r"(t % csz));
+                asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(remote), "f"(v) : "memory");
+            }
+        }
+        __syncthreads();
     }
-    // every logit of the tile is written once the cluster (all CTAs of this token tile) has
-    // passed the barrier (release/acquire at cluster scope); CTA r then routes tokens r,
-    // r + cluster size, ... of the tile, each with the whole CTA
+    // every logit of the tile is in its routing CTA's shared memory once the cluster (all CTAs of
+    // this token tile) has passed the barrier (release/acquire at cluster scope); CTA r then
+    // routes tokens r, r + cluster size, ... of the tile, each with the whole CTA
     cluster_sync();
-    const int rank = cluster_ctarank(), csz = cluster_nctarank();
     __shared__ float s_p[MAX_E + MAX_K];
     __shared__ int s_e[MAX_K];
     __shared__ float s_w[MAX_K];
-    for (int r = rank; r < nt; r += csz) {
+    for (int r = rank, j = 0; r < nt; r += csz, ++j) {
         const int t = t0 + r;
-        select_topk<MAX_E, MAX_K>(a.logits + (size_t)t * a.E, a.E, a.K, s_e, s_w, s_p);
+        select_topk<MAX_E, MAX_K, true>(s_lg[j], a.E, a.K, s_e, s_w, s_p);
         if (tid < a.K) {
             a.topk[(size_t)t * a.K + tid] = s_e[tid];
             a.wt[(size_t)t * a.K + tid] = s_w[tid];
@@ -1086,7 +1142,7 @@ static int build_tiles(cpg_moe_layer *L) {
     CPG_CUDA(cudaDeviceSynchronize());
     return CPG_OK;
 }
-int router_cluster_check(int E, int rsmem);
+int router_cluster_check(int E, int rsmem, int *n_active = nullptr);
 }  // namespace cpg
 
 extern "C" int cpg_moe_layer_create(const cpg_moe_desc *d, cpg_moe_layer **out) {
@@ -1146,8 +1202,10 @@ extern "C" int cpg_moe_layer_create(const cpg_moe_desc *d, cpg_moe_layer **out) 
         if (ce != cudaSuccess) rc = cuda_fail(ce, "cpg_moe_layer_create: barrier counters");
     }
     if (rc == CPG_OK) {
-        const int rsmem = R_TB * L->D * (int)sizeof(float);
-        if (rsmem > smem_optin() - 8 * 1024) {
+        // the token tile's rows, plus the CTA's router rows when they fit beside them (static
+        // shared memory of the kernel: about 12 KB)
+        const int rsmem = (R_TB + 1) * L->D * (int)sizeof(float);        // the tile's rows and the gain
+        if (rsmem > smem_optin() - 16 * 1024) {
             set_error("d_model=%d too large for the router kernel", L->D);
             rc = CPG_EINVAL;
         } else {
@@ -1177,7 +1235,7 @@ int router_cluster(int E, int *eb) {
 }
 
 // The router's clusters must fit on this device (checked once per layer).
-int router_cluster_check(int E, int rsmem) {
+int router_cluster_check(int E, int rsmem, int *n_active) {
     int eb = 0;
     const int csz = router_cluster(E, &eb);
     CPG_CUDA(cudaFuncSetAttribute(k_router<1>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
@@ -1196,6 +1254,7 @@ int router_cluster_check(int E, int rsmem) {
     cfg.numAttrs = 1;
     int n = 0;
     CPG_CUDA(cudaOccupancyMaxActiveClusters(&n, k_router<R_TB>, &cfg));
+    if (n_active) *n_active = n;
     CPG_REQUIRE(n >= 1, "router kernel: a cluster of %d CTAs does not fit on this device", csz);
     return CPG_OK;
 }
@@ -1274,7 +1333,8 @@ int cpg::moe_forward_impl(const cpg_moe_layer *L, const float *x, const float *a
     const int tb = T <= 2 ? T : R_TB;
     const dim3 rgrid(csz, (T + tb - 1) / tb);
     auto *rk = tb == 1 ? k_router<1> : tb == 2 ? k_router<2> : k_router<R_TB>;
-    CPG_CUDA(launch_pdl_cluster(rk, rgrid, dim3(R_THREADS), (size_t)tb * L->D * sizeof(float), s, csz, ra));
+    const size_t rsm = (size_t)(tb + 1) * L->D * sizeof(float);
+    CPG_CUDA(launch_pdl_cluster(rk, rgrid, dim3(R_THREADS), rsm, s, csz, ra));
     // the gate/up kernel groups small batches itself; its scratch (group_cta) must fit in two
     // stages of the smallest stage ring (Q4 gate/up: 2 × 26,880 bytes)
     const size_t group_scratch = sizeof(int) * (4 * (size_t)L->E + (size_t)L->E * ((T + 31) / 32) + (size_t)T * L->K + 1);
