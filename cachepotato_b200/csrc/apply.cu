@@ -15,8 +15,9 @@
 namespace cpg {
 
 int apply_validate(const cpg_moe_layer *layer, int T, size_t ws_bytes);
-int apply_rows_impl(const cpg_moe_layer *layer, const void *rows_f16, int R, const int *slot_expert,
-                    const float *slot_wt, float *out, void *ws, size_t ws_bytes, cudaStream_t s);
+// rows_f16: R fp16 rows xstride halves apart; row r's slot ids / weights at + r·istride.
+int apply_rows_impl(const cpg_moe_layer *layer, const void *rows_f16, int xstride, int R, const int *slot_expert,
+                    const float *slot_wt, int istride, float *out, void *ws, size_t ws_bytes, cudaStream_t s);
 int layer_dims(const cpg_moe_layer *L, int *D, int *F, int *E, int *K);
 int layer_ptrs(const cpg_moe_layer *L, const uint8_t *const **ptrs, int *enc);
 int layer_weight_maps(const cpg_moe_layer *L, const void **maps);
@@ -50,7 +51,7 @@ static ApplyWs apply_layout(int D, int F, int E, int K, int T) {
 
 // per-block expert counts, id validation (negative ids are empty slots when empty_ok). The
 // status words are cleared on the stream before this launch, so a bad id any block records stays.
-__global__ void __launch_bounds__(AP_BLOCK) k_apply_prep(int T, int E, int K, const int *__restrict__ idx,
+__global__ void __launch_bounds__(AP_BLOCK) k_apply_prep(int T, int E, int K, const int *__restrict__ idx, int istride,
                                                           int *__restrict__ blk_cnt, int *status, int empty_ok) {
     __shared__ int s_cnt[AP_MAX_E];
     const int b = blockIdx.x, t0 = b * AP_BLOCK;
@@ -58,7 +59,7 @@ __global__ void __launch_bounds__(AP_BLOCK) k_apply_prep(int T, int E, int K, co
     __syncthreads();
     const int nt = min(AP_BLOCK, T - t0);
     for (int i = threadIdx.x; i < nt * K; i += blockDim.x) {
-        const int e = idx[(size_t)t0 * K + i];
+        const int e = idx[(size_t)(t0 + i / K) * istride + i % K];
         if (e >= 0 && e < E) atomicAdd(&s_cnt[e], 1);
         else if (!(empty_ok && e < 0)) atomicExch(status, ST_BAD_ITEM);
     }
@@ -68,7 +69,7 @@ __global__ void __launch_bounds__(AP_BLOCK) k_apply_prep(int T, int E, int K, co
 
 // Deterministic counting sort of the (token, slot) pairs by expert. Block b places its pairs at
 // off[e] + (pairs of e in blocks < b) + (pairs of e from earlier tokens of block b).
-__global__ void __launch_bounds__(AP_BLOCK) k_apply_group(int T, int E, int K, const int *__restrict__ idx,
+__global__ void __launch_bounds__(AP_BLOCK) k_apply_group(int T, int E, int K, const int *__restrict__ idx, int istride,
                                                            const int *__restrict__ blk_cnt, int nblk,
                                                            const uint8_t *const *ptrs, int *pairs, int4 *act,
                                                            const uint8_t **act_ptr, int *n_active) {
@@ -112,7 +113,7 @@ __global__ void __launch_bounds__(AP_BLOCK) k_apply_group(int T, int E, int K, c
         for (int i = tid; i < 32 * K; i += blockDim.x) {
             const int tl = i / K, t = t0 + c0 + tl;
             if (c0 + tl < nt) {
-                const int e = idx[(size_t)t * K + i % K];
+                const int e = idx[(size_t)t * istride + i % K];
                 if (e >= 0 && e < E) atomicOr(&s_mask[e], 1u << tl);
             }
         }
@@ -121,7 +122,7 @@ __global__ void __launch_bounds__(AP_BLOCK) k_apply_group(int T, int E, int K, c
             const int tl = i / K, j = i % K, t = t0 + c0 + tl;
             if (c0 + tl < nt) {
                 const int slot = t * K + j;
-                const int e = idx[slot];
+                const int e = idx[(size_t)t * istride + j];
                 if (e >= 0 && e < E) {
                     const int r = s_base[e] + __popc(s_mask[e] & ((1u << tl) - 1u));
                     pairs[s_off[e] + r] = slot;
@@ -135,9 +136,9 @@ __global__ void __launch_bounds__(AP_BLOCK) k_apply_group(int T, int E, int K, c
 }
 
 // xs[p] = fp16(xn[token of pair p]) for the valid pairs (one warp per row, 8 values per lane
-// step); from fp16 rows xh instead when xn is null
+// step); from fp16 rows xh (xstride halves apart) instead when xn is null
 __global__ void __launch_bounds__(256) k_apply_gather(const float *__restrict__ xn, const __half *__restrict__ xh,
-                                                       int D, int K, const int *__restrict__ pairs,
+                                                       int D, int xstride, int K, const int *__restrict__ pairs,
                                                        const int4 *__restrict__ act, const int *__restrict__ n_active,
                                                        __half *__restrict__ xs, int max_pairs) {
     const int n_valid = act[*n_active].y;
@@ -147,7 +148,7 @@ __global__ void __launch_bounds__(256) k_apply_gather(const float *__restrict__ 
         const size_t row = (size_t)(pairs[p] / K) * D;
         uint4 *dst = reinterpret_cast<uint4 *>(xs + (size_t)p * D);
         if (!xn) {
-            const uint4 *src16 = reinterpret_cast<const uint4 *>(xh + row);
+            const uint4 *src16 = reinterpret_cast<const uint4 *>(xh + (size_t)(pairs[p] / K) * xstride);
             for (int i = lane; i < D / 8; i += 32) dst[i] = src16[i];
             continue;
         }
@@ -165,16 +166,16 @@ __global__ void __launch_bounds__(256) k_apply_gather(const float *__restrict__ 
 // out[t] (+)= sum_j wt[t,j]·y[t*K+j] over slots with a valid id, in selection order with one
 // rounding per product and per sum (qwen3_moe.c:221); accumulate = 0 starts from zero.
 __global__ void __launch_bounds__(256) k_apply_combine(int T, int D, int K, int E, const int *__restrict__ idx,
-                                                        const float *__restrict__ wt, const float *__restrict__ y,
-                                                        float *out, int accumulate) {
+                                                        const float *__restrict__ wt, int istride,
+                                                        const float *__restrict__ y, float *out, int accumulate) {
     const int n4 = T * D / 4;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += gridDim.x * blockDim.x) {
         const int t = (i * 4) / D, k = i * 4 - t * D;
         float4 acc = accumulate ? reinterpret_cast<const float4 *>(out)[i] : make_float4(0.f, 0.f, 0.f, 0.f);
         for (int j = 0; j < K; ++j) {
-            const int e = __ldg(idx + (size_t)t * K + j);
+            const int e = __ldg(idx + (size_t)t * istride + j);
             if (e < 0 || e >= E) continue;
-            const float w = __ldg(wt + (size_t)t * K + j);
+            const float w = __ldg(wt + (size_t)t * istride + j);
             const float4 v = __ldg(reinterpret_cast<const float4 *>(y + ((size_t)t * K + j) * D + k));
             acc.x = __fadd_rn(acc.x, __fmul_rn(w, v.x));
             acc.y = __fadd_rn(acc.y, __fmul_rn(w, v.y));
@@ -215,12 +216,13 @@ int cpg::apply_validate(const cpg_moe_layer *layer, int T, size_t ws_bytes) {
     return layer_weight_maps(layer, &maps);
 }
 
-// Input rows: xn (f32) or xh (fp16). empty_ok: negative ids are empty slots, not errors.
+// Input rows: xn (f32, D apart) or xh (fp16, xstride halves apart); row t's K slot ids and
+// weights at topk_idx / wt + t·istride. empty_ok: negative ids are empty slots, not errors.
 // accumulate: mlp += the block output, else mlp = it. ev: null, or 5 events recorded around the
 // sort, gate/up, down and combine phases.
-static int apply_impl(const cpg_moe_layer *layer, const float *xn, const __half *xh, int T, const int *topk_idx,
-                      const float *wt, float *mlp, int accumulate, int empty_ok, void *ws, size_t ws_bytes,
-                      cudaStream_t s, cudaEvent_t *ev) {
+static int apply_impl(const cpg_moe_layer *layer, const float *xn, const __half *xh, int xstride, int T,
+                      const int *topk_idx, const float *wt, int istride, float *mlp, int accumulate, int empty_ok,
+                      void *ws, size_t ws_bytes, cudaStream_t s, cudaEvent_t *ev) {
     CPG_REQUIRE(layer && (xn || xh) && topk_idx && wt && mlp && ws, "cpg_moe_apply: null argument");
     int rc = apply_validate(layer, T, ws_bytes);
     if (rc) return rc;
@@ -236,9 +238,9 @@ static int apply_impl(const cpg_moe_layer *layer, const float *xn, const __half 
     const int nblk = (T + AP_BLOCK - 1) / AP_BLOCK;
     if (ev) CPG_CUDA(cudaEventRecord(ev[0], s));
     CPG_CUDA(cudaMemsetAsync(status, 0, 16 * sizeof(int), s));
-    k_apply_prep<<<nblk, AP_BLOCK, 0, s>>>(T, E, K, topk_idx, (int *)(w + W.blk_cnt), status, empty_ok);
+    k_apply_prep<<<nblk, AP_BLOCK, 0, s>>>(T, E, K, topk_idx, istride, (int *)(w + W.blk_cnt), status, empty_ok);
     CPG_CUDA(cudaGetLastError());
-    k_apply_group<<<nblk, AP_BLOCK, 0, s>>>(T, E, K, topk_idx, (const int *)(w + W.blk_cnt), nblk, ptrs,
+    k_apply_group<<<nblk, AP_BLOCK, 0, s>>>(T, E, K, topk_idx, istride, (const int *)(w + W.blk_cnt), nblk, ptrs,
                                             (int *)(w + W.pairs), (int4 *)(w + W.act), (const uint8_t **)(w + W.act_ptr),
                                             (int *)(w + W.n_active));
     CPG_CUDA(cudaGetLastError());
@@ -246,7 +248,7 @@ static int apply_impl(const cpg_moe_layer *layer, const float *xn, const __half 
         const int P = T * K;
         int ggrid = (P + 7) / 8;
         if (ggrid > sm_count() * 8) ggrid = sm_count() * 8;
-        k_apply_gather<<<ggrid, 256, 0, s>>>(xn, xh, D, K, (const int *)(w + W.pairs), (const int4 *)(w + W.act),
+        k_apply_gather<<<ggrid, 256, 0, s>>>(xn, xh, D, xstride, K, (const int *)(w + W.pairs), (const int4 *)(w + W.act),
                                              (const int *)(w + W.n_active), (__half *)(w + W.xs), P);
         CPG_CUDA(cudaGetLastError());
     }
@@ -271,7 +273,7 @@ static int apply_impl(const cpg_moe_layer *layer, const float *xn, const __half 
     const int n4 = T * D / 4;
     int cgrid = (n4 + 255) / 256;
     if (cgrid > sm_count() * 8) cgrid = sm_count() * 8;
-    k_apply_combine<<<cgrid, 256, 0, s>>>(T, D, K, E, topk_idx, wt, (const float *)(w + W.y), mlp, accumulate);
+    k_apply_combine<<<cgrid, 256, 0, s>>>(T, D, K, E, topk_idx, wt, istride, (const float *)(w + W.y), mlp, accumulate);
     CPG_CUDA(cudaGetLastError());
     if (ev) CPG_CUDA(cudaEventRecord(ev[4], s));
     return CPG_OK;
@@ -279,20 +281,25 @@ static int apply_impl(const cpg_moe_layer *layer, const float *xn, const __half 
 
 extern "C" int cpg_moe_apply(const cpg_moe_layer *layer, const float *xn, int T, const int *topk_idx,
                              const float *wt, float *mlp, void *ws, size_t ws_bytes, void *stream) {
-    return apply_impl(layer, xn, nullptr, T, topk_idx, wt, mlp, 1, 0, ws, ws_bytes, (cudaStream_t)stream, nullptr);
+    int D = 0, F, E, K = 0;
+    if (layer) layer_dims(layer, &D, &F, &E, &K);
+    return apply_impl(layer, xn, nullptr, D, T, topk_idx, wt, K, mlp, 1, 0, ws, ws_bytes, (cudaStream_t)stream,
+                      nullptr);
 }
 
-int cpg::apply_rows_impl(const cpg_moe_layer *layer, const void *rows_f16, int R, const int *slot_expert,
-                         const float *slot_wt, float *out, void *ws, size_t ws_bytes, cudaStream_t s) {
+int cpg::apply_rows_impl(const cpg_moe_layer *layer, const void *rows_f16, int xstride, int R, const int *slot_expert,
+                         const float *slot_wt, int istride, float *out, void *ws, size_t ws_bytes, cudaStream_t s) {
     CPG_REQUIRE(rows_f16, "cpg_moe_apply_rows: null rows");
-    return apply_impl(layer, nullptr, (const __half *)rows_f16, R, slot_expert, slot_wt, out, 0, 1, ws, ws_bytes, s,
-                      nullptr);
+    return apply_impl(layer, nullptr, (const __half *)rows_f16, xstride, R, slot_expert, slot_wt, istride, out, 0, 1,
+                      ws, ws_bytes, s, nullptr);
 }
 
 extern "C" int cpg_moe_apply_rows(const cpg_moe_layer *layer, const void *rows_f16, int R, const int *slot_expert,
                                   const float *slot_wt, float *out, void *ws, size_t ws_bytes, void *stream) {
     CPG_REQUIRE(rows_f16, "cpg_moe_apply_rows: null rows");
-    return apply_impl(layer, nullptr, (const __half *)rows_f16, R, slot_expert, slot_wt, out, 0, 1, ws, ws_bytes,
+    int D = 0, F, E, K = 0;
+    if (layer) layer_dims(layer, &D, &F, &E, &K);
+    return apply_impl(layer, nullptr, (const __half *)rows_f16, D, R, slot_expert, slot_wt, K, out, 0, 1, ws, ws_bytes,
                       (cudaStream_t)stream, nullptr);
 }
 
@@ -308,7 +315,9 @@ extern "C" int cpg_moe_apply_profile(const cpg_moe_layer *layer, const float *xn
             return cuda_fail(ce, "cpg_moe_apply_profile: event");
         }
     }
-    int rc = apply_impl(layer, xn, nullptr, T, topk_idx, wt, mlp, 1, 0, ws, ws_bytes, (cudaStream_t)stream, ev);
+    int D = 0, F, E, K = 0;
+    if (layer) layer_dims(layer, &D, &F, &E, &K);
+    int rc = apply_impl(layer, xn, nullptr, D, T, topk_idx, wt, K, mlp, 1, 0, ws, ws_bytes, (cudaStream_t)stream, ev);
     if (rc == CPG_OK) {
         const cudaError_t ce = cudaEventSynchronize(ev[4]);
         if (ce != cudaSuccess) rc = cuda_fail(ce, "cpg_moe_apply_profile: synchronize");

@@ -82,8 +82,11 @@ static const NcclApi &nccl() {
 constexpr int EP_PLAN_THREADS = 1024;
 constexpr int EP_MAX_K = 32;
 
+// One message per peer and direction. Out: T records of RS bytes per owner, record q =
+// [fp16 row (D halves) | K local expert ids | K weights | padding to 16 B]; back: T f32 rows.
 struct EpWs {
-    size_t status, send_rows, send_ide, send_wt, recv_rows, recv_ide, recv_wt, pos, out_rows, back, apply, total;
+    size_t status, send, recv, pos, out_rows, back, apply, total;
+    size_t rs;                              // record bytes
 };
 
 static size_t al(size_t v) { return (v + 255) / 256 * 256; }
@@ -92,13 +95,10 @@ static EpWs ep_layout(int G, int T, int D, int K, size_t apply_bytes) {
     EpWs w{};
     size_t o = 0;
     const size_t R = (size_t)G * T;
+    w.rs = ((size_t)D * sizeof(__half) + (size_t)K * 8 + 15) / 16 * 16;
     w.status = o; o = al(o + 16 * sizeof(int));
-    w.send_rows = o; o = al(o + R * D * sizeof(__half));
-    w.send_ide = o; o = al(o + R * K * sizeof(int));
-    w.send_wt = o; o = al(o + R * K * sizeof(float));
-    w.recv_rows = o; o = al(o + R * D * sizeof(__half));
-    w.recv_ide = o; o = al(o + R * K * sizeof(int));
-    w.recv_wt = o; o = al(o + R * K * sizeof(float));
+    w.send = o; o = al(o + R * w.rs);
+    w.recv = o; o = al(o + R * w.rs);
     w.pos = o; o = al(o + (size_t)T * G * sizeof(int));
     w.out_rows = o; o = al(o + R * D * sizeof(float));
     w.back = o; o = al(o + R * D * sizeof(float));
@@ -133,11 +133,11 @@ __device__ __forceinline__ int block_excl_scan(int flag, int *s_warp, int *total
     return r;
 }
 
-// One block per owner rank p: send positions (tokens ascending) and per-slot metadata.
-__global__ void __launch_bounds__(EP_PLAN_THREADS) k_ep_plan(int T, int K, int G, int E_l, const int *__restrict__ idx,
+// One block per owner rank p: send positions (tokens ascending) and per-slot metadata into the
+// records' tails (record r of the out buffer at send + r·rs; ids at byte 2D, weights after them).
+__global__ void __launch_bounds__(EP_PLAN_THREADS) k_ep_plan(int T, int K, int G, int E_l, int D, const int *__restrict__ idx,
                                                               const float *__restrict__ wt, int *__restrict__ pos,
-                                                              int *__restrict__ send_ide, float *__restrict__ send_wt,
-                                                              int *status) {
+                                                              uint8_t *__restrict__ send, size_t rs, int *status) {
     __shared__ int s_warp[33];
     const int p = blockIdx.x;
     const int E_tot = E_l * G;
@@ -160,12 +160,14 @@ __global__ void __launch_bounds__(EP_PLAN_THREADS) k_ep_plan(int T, int K, int G
             const int q = base + r;
             pos[(size_t)t * G + p] = flag ? q : -1;
             if (flag) {
-                const size_t m = ((size_t)p * T + q) * K;
+                uint8_t *rec = send + ((size_t)p * T + q) * rs + (size_t)D * sizeof(__half);
+                int *ide = reinterpret_cast<int *>(rec);
+                float *w8 = reinterpret_cast<float *>(rec) + K;
                 for (int j = 0; j < K; ++j) {
                     const int e = idx[(size_t)t * K + j];
                     const bool mine = e >= 0 && e < E_tot && e / E_l == p;
-                    send_ide[m + j] = mine ? e - p * E_l : -1;
-                    send_wt[m + j] = mine ? wt[(size_t)t * K + j] : 0.0f;
+                    ide[j] = mine ? e - p * E_l : -1;
+                    w8[j] = mine ? wt[(size_t)t * K + j] : 0.0f;
                 }
             }
         }
@@ -173,14 +175,15 @@ __global__ void __launch_bounds__(EP_PLAN_THREADS) k_ep_plan(int T, int K, int G
     }
     // capacity rows past the last token carry no slots
     for (size_t i = (size_t)base * K + threadIdx.x; i < (size_t)T * K; i += blockDim.x) {
-        send_ide[(size_t)p * T * K + i] = -1;
-        send_wt[(size_t)p * T * K + i] = 0.0f;
+        uint8_t *rec = send + ((size_t)p * T + i / K) * rs + (size_t)D * sizeof(__half);
+        reinterpret_cast<int *>(rec)[i % K] = -1;
+        reinterpret_cast<float *>(rec)[K + i % K] = 0.0f;
     }
 }
 
-// One warp per token: its row as fp16 into the send buffer of every owner that needs it.
+// One warp per token: its row as fp16 into the record of every owner that needs it.
 __global__ void __launch_bounds__(256) k_ep_pack_rows(int T, int D, int G, const float *__restrict__ xn,
-                                                       const int *__restrict__ pos, __half *__restrict__ send_rows) {
+                                                       const int *__restrict__ pos, uint8_t *__restrict__ send, size_t rs) {
     const int lane = threadIdx.x & 31;
     for (int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; t < T; t += (gridDim.x * blockDim.x) >> 5) {
         const float4 *src = reinterpret_cast<const float4 *>(xn + (size_t)t * D);
@@ -192,7 +195,7 @@ __global__ void __launch_bounds__(256) k_ep_pack_rows(int T, int D, int G, const
                                        *reinterpret_cast<const uint32_t *>(&h2), *reinterpret_cast<const uint32_t *>(&h3));
             for (int p = 0; p < G; ++p) {
                 const int q = __ldg(pos + (size_t)t * G + p);
-                if (q >= 0) reinterpret_cast<uint4 *>(send_rows + ((size_t)p * T + q) * D)[i] = v;
+                if (q >= 0) reinterpret_cast<uint4 *>(send + ((size_t)p * T + q) * rs)[i] = v;
             }
         }
     }
@@ -428,8 +431,9 @@ extern "C" size_t cpg_ep_workspace_bytes(const cpg_ep *ep, const cpg_moe_layer *
 
 namespace cpg {
 int apply_validate(const cpg_moe_layer *layer, int T, size_t ws_bytes);
-int apply_rows_impl(const cpg_moe_layer *layer, const void *rows_f16, int R, const int *slot_expert,
-                    const float *slot_wt, float *out, void *ws, size_t ws_bytes, cudaStream_t s);
+// rows_f16: R fp16 rows xstride halves apart; row r's slot ids / weights at + r·istride.
+int apply_rows_impl(const cpg_moe_layer *layer, const void *rows_f16, int xstride, int R, const int *slot_expert,
+                    const float *slot_wt, int istride, float *out, void *ws, size_t ws_bytes, cudaStream_t s);
 
 // ev: null, or 6 events recorded before plan/pack, dispatch, owner experts, return, combine and
 // after the combine.
@@ -446,6 +450,7 @@ static int ep_impl(cpg_ep *ep, const cpg_moe_layer *local_layer, const float *xn
     if (rc) return rc;
     CPG_REQUIRE(K <= EP_MAX_K, "cpg_moe_ep: topk %d > %d", K, EP_MAX_K);
     const int G = ep->G, me = ep->rank;
+    CPG_REQUIRE(G <= 64, "cpg_moe_ep: at most 64 ranks");
     const size_t apply_bytes = cpg_moe_apply_workspace_bytes(local_layer, G * T);
     const EpWs W = ep_layout(G, T, D, K, apply_bytes);
     CPG_REQUIRE(ws_bytes >= W.total, "cpg_moe_ep: workspace %zu < %zu bytes", ws_bytes, W.total);
@@ -458,37 +463,26 @@ static int ep_impl(cpg_ep *ep, const cpg_moe_layer *local_layer, const float *xn
     if (ev) CPG_CUDA(cudaEventRecord(ev[0], s));
     CPG_CUDA(cudaMemsetAsync(status, 0, 16 * sizeof(int), s));
     int *pos = (int *)(w + W.pos);
-    k_ep_plan<<<G, EP_PLAN_THREADS, 0, s>>>(T, K, G, E_l, topk_idx, wt, pos, (int *)(w + W.send_ide),
-                                            (float *)(w + W.send_wt), status);
+    k_ep_plan<<<G, EP_PLAN_THREADS, 0, s>>>(T, K, G, E_l, D, topk_idx, wt, pos, w + W.send, W.rs, status);
     CPG_CUDA(cudaGetLastError());
     int pgrid = (T + 7) / 8;
     if (pgrid > sm_count() * 8) pgrid = sm_count() * 8;
-    k_ep_pack_rows<<<pgrid, 256, 0, s>>>(T, D, G, xn, pos, (__half *)(w + W.send_rows));
+    k_ep_pack_rows<<<pgrid, 256, 0, s>>>(T, D, G, xn, pos, w + W.send, W.rs);
     CPG_CUDA(cudaGetLastError());
 
-    // dispatch: rows + metadata to every other owner through NCCL; this rank's own share is a
-    // device copy
-    const size_t row_b = (size_t)T * D * sizeof(__half), meta_n = (size_t)T * K;
+    // dispatch: one message of T records to every other owner through NCCL; this rank's own
+    // share is a device copy
+    const size_t msg_b = (size_t)T * W.rs;
     if (ev) CPG_CUDA(cudaEventRecord(ev[1], s));
-    CPG_CUDA(cudaMemcpyAsync(w + W.recv_rows + me * row_b, w + W.send_rows + me * row_b, row_b,
-                             cudaMemcpyDeviceToDevice, s));
-    CPG_CUDA(cudaMemcpyAsync((int *)(w + W.recv_ide) + me * meta_n, (int *)(w + W.send_ide) + me * meta_n,
-                             meta_n * sizeof(int), cudaMemcpyDeviceToDevice, s));
-    CPG_CUDA(cudaMemcpyAsync((float *)(w + W.recv_wt) + me * meta_n, (float *)(w + W.send_wt) + me * meta_n,
-                             meta_n * sizeof(float), cudaMemcpyDeviceToDevice, s));
+    CPG_CUDA(cudaMemcpyAsync(w + W.recv + me * msg_b, w + W.send + me * msg_b, msg_b, cudaMemcpyDeviceToDevice, s));
     if (G > 1) {
-        P2P ops[6 * 64];
+        P2P ops[2 * 64];
         int n = 0;
-        for (int p = 0; p < G && n + 6 <= 6 * 64; ++p) {
+        for (int p = 0; p < G; ++p) {
             if (p == me) continue;
-            ops[n++] = {w + W.send_rows + p * row_b, row_b, ncclUint8, p, true};
-            ops[n++] = {(int *)(w + W.send_ide) + p * meta_n, meta_n, ncclInt32, p, true};
-            ops[n++] = {(float *)(w + W.send_wt) + p * meta_n, meta_n, ncclFloat32, p, true};
-            ops[n++] = {w + W.recv_rows + p * row_b, row_b, ncclUint8, p, false};
-            ops[n++] = {(int *)(w + W.recv_ide) + p * meta_n, meta_n, ncclInt32, p, false};
-            ops[n++] = {(float *)(w + W.recv_wt) + p * meta_n, meta_n, ncclFloat32, p, false};
+            ops[n++] = {w + W.send + p * msg_b, msg_b, ncclUint8, p, true};
+            ops[n++] = {w + W.recv + p * msg_b, msg_b, ncclUint8, p, false};
         }
-        CPG_REQUIRE(G <= 64, "cpg_moe_ep: at most 64 ranks");
         rc = ep_group(ep, ops, n, s, "cpg_moe_ep dispatch");
         if (rc) return rc;
     }
@@ -497,8 +491,10 @@ static int ep_impl(cpg_ep *ep, const cpg_moe_layer *local_layer, const float *xn
     // above, so only a CUDA launch failure can end it here: the communicator is aborted then,
     // which fails the peers' return exchange instead of leaving it waiting
     if (ev) CPG_CUDA(cudaEventRecord(ev[2], s));
-    rc = apply_rows_impl(local_layer, w + W.recv_rows, G * T, (const int *)(w + W.recv_ide),
-                         (const float *)(w + W.recv_wt), (float *)(w + W.out_rows), w + W.apply, apply_bytes, s);
+    const uint8_t *meta = w + W.recv + (size_t)D * sizeof(__half);
+    rc = apply_rows_impl(local_layer, w + W.recv, (int)(W.rs / sizeof(__half)), G * T, (const int *)meta,
+                         (const float *)meta + K, (int)(W.rs / sizeof(int)), (float *)(w + W.out_rows), w + W.apply,
+                         apply_bytes, s);
     if (rc) {
         ep_abort(ep);
         return rc;

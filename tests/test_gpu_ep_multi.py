@@ -63,3 +63,86 @@ def test_ep_multi_gpu(tmp_path, orc, shape_name):
     L, xn, idx, wt = _inputs(orc, O, SHAPES[shape_name], G, seed)
     want = orc.moe_apply(L, xn, idx, wt)
     assert np.abs(got - want).max() / np.abs(want).max() <= 1e-3
+
+
+# ------------------------------------------------------------------ a rank that leaves
+def _free_port():
+    import socket
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _leaver(rank, G, uid, sport, mode, out_path):
+    """EP steps on the GPU, each gated by the host heartbeat; rank 1 stops after step 1 with its
+    stream drained (mode 'leave': announces it; 'die': exits silently). Rank 0 must raise PeerLost
+    at step 2 before posting that step's collectives, abort its communicator and return."""
+    import sys
+    import time
+    os.environ["NCCL_NVLS_ENABLE"] = "0"            # no NVLink multicast objects in this test
+    here = os.path.dirname(os.path.abspath(__file__))
+    sys.path[:0] = [os.path.dirname(here), os.path.join(os.path.dirname(here), "oracle"), here]
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(rank)
+    import oracle as O
+    from helpers import device_layer
+    from cachepotato_b200.qwen3 import EpHeartbeat, ExpertParallel, PeerLost
+    store = dist.TCPStore("127.0.0.1", sport, G, rank == 0, timeout=__import__("datetime").timedelta(seconds=60))
+    hb = EpHeartbeat(store, rank, G, timeout_s=3.0, prefix=f"g_{mode}")
+    orc = O.Oracle()
+    shape = SHAPES["small"]
+    T = shape[4]
+    L, xn, idx, wt = _inputs(orc, O, shape, G, 850)
+    sl = slice(rank * T, (rank + 1) * T)
+    ep = ExpertParallel(G, rank, uid, timeout_ms=10000)
+    local = device_layer(L.shard(rank, G))
+    x, i, w = (torch.from_numpy(a[sl]).cuda() for a in (xn, idx, wt))
+    steps_done = 0
+    for step in range(4):
+        if rank == 1 and step == 2:
+            ep.wait()                                   # nothing of this rank in flight
+            if mode == "leave":
+                hb.leave()
+            os._exit(0)
+        t0 = time.monotonic()
+        try:
+            hb.step()
+        except PeerLost as e:
+            ep.abort()
+            with open(out_path, "w") as f:
+                f.write(f"{steps_done} {time.monotonic() - t0:.3f} {e}")
+            ep.close()
+            os._exit(0)
+        ep.forward(local, x, i, w)
+        ep.wait()
+        steps_done += 1
+    with open(out_path, "w") as f:
+        f.write(f"{steps_done} 0 no PeerLost")
+    ep.close()
+    os._exit(0)
+
+
+@pytest.mark.parametrize("mode", ["leave", "die"])
+def test_ep_peer_lost_between_steps_on_gpus(tmp_path, mode):
+    """The heartbeat protocol of the CPU test (tests/test_ep_gloo.py) with the real NCCL
+    communicator on two GPUs: the survivor reports the lost peer instead of hanging."""
+    import time
+    import torch.multiprocessing as mp
+    from cachepotato_b200.qwen3 import ExpertParallel
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs at least two GPUs")
+    out = str(tmp_path / f"ep_lost_{mode}.txt")
+    ctx = mp.start_processes(_leaver, args=(2, ExpertParallel.unique_id(), _free_port(), mode, out), nprocs=2,
+                             join=False, start_method="spawn")
+    deadline = time.monotonic() + 180
+    while not ctx.join(timeout=1):
+        if time.monotonic() > deadline:
+            for p in ctx.processes:
+                if p.is_alive():
+                    p.terminate()
+            pytest.fail("ranks did not finish: the survivor hung")
+    done, waited, msg = open(out).read().split(" ", 2)
+    assert int(done) == 2, msg                       # steps 0 and 1 ran on both GPUs
+    assert "left" in msg if mode == "leave" else "did not reach" in msg, msg
+    assert float(waited) < (1.5 if mode == "leave" else 10.0), waited
