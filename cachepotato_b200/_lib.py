@@ -30,6 +30,7 @@ EXPORTS = [
     "cpg_moe_apply_rows", "cpg_ep_unique_id", "cpg_ep_create", "cpg_ep_destroy", "cpg_ep_workspace_bytes",
     "cpg_moe_ep", "cpg_moe_ep_check", "cpg_moe_ep_profile", "cpg_ep_set_timeout", "cpg_ep_abort", "cpg_ep_wait",
     "cpg_qwen3_create", "cpg_qwen3_destroy", "cpg_qwen3_prefill", "cpg_qwen3_step", "cpg_qwen3_generate",
+    "cpg_qwen3_append", "cpg_qwen3_rewind",
     "cpg_qwen3_logits", "cpg_qwen3_stream", "cpg_qwen3_position",
     "cpg_qwen3_batch_create", "cpg_qwen3_batch_destroy", "cpg_qwen3_batch_prefill", "cpg_qwen3_batch_step",
     "cpg_qwen3_batch_generate", "cpg_qwen3_batch_position", "cpg_qwen3_batch_logits",
@@ -125,6 +126,8 @@ _SIGS = {
     "cpg_qwen3_destroy": (None, [_vp]),
     "cpg_qwen3_prefill": (_i, [_vp, _vp, _i, ctypes.POINTER(_i)]),
     "cpg_qwen3_step": (_i, [_vp, _i, ctypes.POINTER(_i)]),
+    "cpg_qwen3_append": (_i, [_vp, _vp, _i, ctypes.POINTER(_i)]),
+    "cpg_qwen3_rewind": (_i, [_vp, _i]),
     "cpg_qwen3_generate": (_i, [_vp, _vp, _i, _i, _vp]),
     "cpg_qwen3_logits": (_vp, [_vp]),
     "cpg_qwen3_stream": (_vp, [_vp]),

@@ -1166,6 +1166,21 @@ static int qwen3_read_next(cpg_qwen3 *m, int *next_id) {
     return CPG_OK;
 }
 
+// The projection GEMM's bounded waits (prompts and steps of QW_DENSE_MIN_T tokens or more).
+static int qwen3_status(cpg_qwen3 *m, const char *fn, const int *extra = nullptr) {
+    const int *words[2] = {m->d_status, extra};
+    for (const int *w : words) {
+        if (!w) continue;
+        int st = 0;
+        CPG_CUDA(cudaMemcpy(&st, w, sizeof(int), cudaMemcpyDeviceToHost));
+        if (st != ST_OK) {
+            set_error("%s: a bounded wait in a projection kernel timed out (status %d)", fn, st);
+            return CPG_ETIMEOUT;
+        }
+    }
+    return CPG_OK;
+}
+
 extern "C" int cpg_qwen3_prefill(cpg_qwen3 *m, const int *ids, int T, int *next_id) {
     CPG_REQUIRE(m && ids && T > 0, "cpg_qwen3_prefill: bad argument");
     CPG_REQUIRE(T <= m->max_ctx, "cpg_qwen3_prefill: %d tokens > max_ctx %d", T, m->max_ctx);
@@ -1180,13 +1195,30 @@ extern "C" int cpg_qwen3_prefill(cpg_qwen3 *m, const int *ids, int T, int *next_
     CPG_CUDA(cudaGetLastError());
     m->pos = T;
     rc2 = qwen3_read_next(m, next_id);
-    if (rc2 || !m->d_status) return rc2;
-    int st = 0;
-    CPG_CUDA(cudaMemcpy(&st, m->d_status, sizeof(int), cudaMemcpyDeviceToHost));
-    if (st != ST_OK) {
-        set_error("cpg_qwen3_prefill: a bounded wait in the projection GEMM timed out (status %d)", st);
-        return CPG_ETIMEOUT;
-    }
+    return rc2 ? rc2 : qwen3_status(m, "cpg_qwen3_prefill");
+}
+
+extern "C" int cpg_qwen3_append(cpg_qwen3 *m, const int *ids, int T, int *next_id) {
+    CPG_REQUIRE(m && ids && T > 0, "cpg_qwen3_append: bad argument");
+    CPG_REQUIRE(m->pos + T <= m->max_ctx, "cpg_qwen3_append: %d + %d tokens > max_ctx %d", m->pos, T, m->max_ctx);
+    for (int t = 0; t < T; ++t) CPG_REQUIRE(ids[t] >= 0 && ids[t] < m->V, "cpg_qwen3_append: id %d out of range", ids[t]);
+    CPG_CUDA(cudaMemcpyAsync(m->d_ids, ids, sizeof(int) * (size_t)T, cudaMemcpyHostToDevice, m->s));
+    const int rc = qwen3_enqueue(m, own_seq(m, T), T, m->s);
+    if (rc) return rc;
+    k_advance<<<1, 1, 0, m->s>>>(m->d_next, m->d_ids, m->d_pos, T, nullptr, 0);
+    CPG_CUDA(cudaGetLastError());
+    m->pos += T;
+    const int rc2 = qwen3_read_next(m, next_id);
+    return rc2 ? rc2 : qwen3_status(m, "cpg_qwen3_append");
+}
+
+extern "C" int cpg_qwen3_rewind(cpg_qwen3 *m, int pos) {
+    CPG_REQUIRE(m && pos >= 0 && pos <= m->pos, "cpg_qwen3_rewind: position %d (current %d)", pos, m ? m->pos : -1);
+    m->pos = pos;
+    int *h = m->h_next;                                  // pinned staging word
+    *h = pos;
+    CPG_CUDA(cudaMemcpyAsync(m->d_pos, h, sizeof(int), cudaMemcpyHostToDevice, m->s));
+    CPG_CUDA(cudaStreamSynchronize(m->s));
     return CPG_OK;
 }
 
@@ -1246,21 +1278,6 @@ struct cpg_qwen3_batch {
     std::vector<cudaGraphExec_t> graphs; // one step of n sequences, by n
     QwDense dn;                          // the dense.cu projections and head, when the shapes allow
 };
-
-// The projection GEMM's bounded waits (prompts and steps of QW_DENSE_MIN_T tokens or more).
-static int qwen3_status(cpg_qwen3 *m, const char *fn, const int *extra = nullptr) {
-    const int *words[2] = {m->d_status, extra};
-    for (const int *w : words) {
-        if (!w) continue;
-        int st = 0;
-        CPG_CUDA(cudaMemcpy(&st, w, sizeof(int), cudaMemcpyDeviceToHost));
-        if (st != ST_OK) {
-            set_error("%s: a bounded wait in a projection kernel timed out (status %d)", fn, st);
-            return CPG_ETIMEOUT;
-        }
-    }
-    return CPG_OK;
-}
 
 static void batch_free(cpg_qwen3_batch *b) {
     for (cudaGraphExec_t g : b->graphs)

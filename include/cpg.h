@@ -97,9 +97,9 @@ int cpg_crc32(const void *dev, size_t n, uint32_t *out, void *stream);
  *   hh = x + attn; xn = rmsnorm(hh, ln2, eps); logits = Wgate·xn; p = softmax(logits);
  *   top-k by strict '>' (lower id wins ties), wt = p[idx] / sum(p[idx]);
  *   for j in selection order: mlp += wt_j · Wd_e·(silu(Wg_e·xn) · (Wu_e·xn)).
- * Expert GEMVs run on tensor cores with fp16 operands (exact Q4/Q8 integers, fp16-rounded
- * activations) and fp32 accumulation; the block output matches the f32 reference within
- * max|d|/max|ref| <= 1e-3. */
+ * Expert GEMVs run on tensor cores with exact Q4/Q8 integers and the f32 activations carried
+ * as fp16 hi + lo halves, fp32 scales and accumulation; the block output matches the f32
+ * reference within max|d|/max|ref| <= 1e-5. */
 typedef struct {
     int d_model;              /* 2048 for Qwen3-30B-A3B; multiple of 256 */
     int d_exp;                /* 768; multiple of 256 */
@@ -263,6 +263,12 @@ void cpg_qwen3_destroy(cpg_qwen3 *m);
 int cpg_qwen3_prefill(cpg_qwen3 *m, const int *ids, int T, int *next_id);
 /* One token at the next position. */
 int cpg_qwen3_step(cpg_qwen3 *m, int id, int *next_id);
+/* T more prompt tokens (host ids) at the current position, in one pass, keeping what the cache
+   holds (a conversation's next turn, cachepotato.c:336-346); *next_id = argmax after the last. */
+int cpg_qwen3_append(cpg_qwen3 *m, const int *ids, int T, int *next_id);
+/* Move the position back to pos (<= the current one); later tokens overwrite the cache from
+   there (cp_reset / a restarted conversation). */
+int cpg_qwen3_rewind(cpg_qwen3 *m, int pos);
 /* Prefill, then n_new steps each feeding the previous argmax; out_ids gets n_new + 1 ids. */
 int cpg_qwen3_generate(cpg_qwen3 *m, const int *prompt, int n_prompt, int n_new, int *out_ids);
 const float *cpg_qwen3_logits(const cpg_qwen3 *m);   /* device (vocab) f32, last position */

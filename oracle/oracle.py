@@ -20,6 +20,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_SO = os.path.join(HERE, "_build", "libcpg_oracle.so")
 REF_SO = os.path.join(HERE, "_ref", "libcpref.so")
 REF_GPU_SO = os.path.join(HERE, "_ref", "libcpref_gpu.so")
+REF_API_SO = os.path.join(HERE, "_ref", "libcpref_api.so")    # the reference's cachepotato.h engine (CPU)
+REF_TOK_SO = os.path.join(HERE, "_ref", "libcpref_tok.so")    # its tokenizer module alone
 # The reference source tree: CPG_REFERENCE_TREE, else a `reference` checkout beside this
 # repository (where the build environment keeps it). Absent on machines that only run the
 # prebuilt checkers.
@@ -39,7 +41,7 @@ def build(ref: bool = True) -> None:
     its drop-in build linked to libcpg_b200.so when that library exists)."""
     targets = ["oracle"]
     if ref and os.path.isdir(os.path.join(REF_TREE, "engine")):
-        targets.append("ref")
+        targets += ["ref", "ref_api"]
         if os.path.exists(os.path.join(os.path.dirname(HERE), "cachepotato_b200", "_build", "libcpg_b200.so")):
             targets.append("ref_gpu")
     subprocess.run(["make", "-s", "-C", HERE, f"REF={REF_TREE}", *targets], check=True)

@@ -38,6 +38,9 @@ sys.path.insert(0, os.path.join(os.path.dirname(os.path.dirname(HERE)), "oracle"
 CFG = dict(hidden_size=256, num_attention_heads=2, num_key_value_heads=1, head_dim=128, num_experts=16,
            num_experts_per_tok=8, moe_intermediate_size=256, vocab_size=151936, rope_theta=1000000.0,
            rms_norm_eps=1e-6, num_hidden_layers=2)
+# the public-API tests' model: 128 experts, as the reference engine's cp_open expects (its
+# layer binding clears a 128-entry expert-region table, qwen3_moe.c:462-586)
+CHAT_CFG = dict(CFG, num_experts=128)
 SEED = 20261202
 EMBED_ROWS = 1024                       # the converter's default region granularity of the embed table
 
@@ -51,9 +54,9 @@ ENC_DESC = {"f32": (0, 0, 0, 4, 1, 0, 4, "f32"), "q8_0": (1, 3, 32, 34, 1, 3, 64
             "q4_0": (1, 4, 32, 18, 1, 3, 64, "Q4_0")}
 
 
-def hf_tensors():
+def hf_tensors(c=None):
     """(HF name, shape, kind) in a fixed order; kind: 'norm' (1 + 0.05 N(0,1)) or 'mat' (0.02 N)."""
-    c = CFG
+    c = c or CFG
     D, H, KV, HD, E, F, V = (c["hidden_size"], c["num_attention_heads"], c["num_key_value_heads"], c["head_dim"],
                              c["num_experts"], c["moe_intermediate_size"], c["vocab_size"])
     out = [("model.embed_tokens.weight", (V, D), "mat")]
@@ -91,9 +94,9 @@ def write_checkpoint(d):
         json.dump({"weight_map": {n: "model.safetensors" for n in tens}}, f)
 
 
-def _layout():
+def _layout(c=None):
     """The converter's tensors in registration order: (name, hf name, shape, role, encoding)."""
-    c = CFG
+    c = c or CFG
     D, H, KV, HD, E, F, V, L = (c["hidden_size"], c["num_attention_heads"], c["num_key_value_heads"], c["head_dim"],
                                 c["num_experts"], c["moe_intermediate_size"], c["vocab_size"], c["num_hidden_layers"])
     t = []
@@ -123,14 +126,15 @@ def _nbytes(shape, enc):
     return n // 32 * 34 if enc == "q8_0" else n // 32 * 18 if enc == "q4_0" else n * 4
 
 
-def write_v4(path):
-    """The CPW1 v4 file of the checkpoint, byte for byte as the reference converter writes it."""
+def write_v4(path, c=None):
+    """The CPW1 v4 file of the checkpoint, byte for byte as the reference converter writes it
+    (c: another configuration of the same family, CFG by default)."""
     import oracle as O
     orc = O.Oracle()
-    c = CFG
-    kinds = {n: k for n, _, k in hf_tensors()}
-    hf_shape = {n: s for n, s, _ in hf_tensors()}
-    tensors = _layout()
+    c = c or CFG
+    kinds = {n: k for n, _, k in hf_tensors(c)}
+    hf_shape = {n: s for n, s, _ in hf_tensors(c)}
+    tensors = _layout(c)
     cache = {}
 
     def payload(i):
