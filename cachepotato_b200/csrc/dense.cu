@@ -316,9 +316,11 @@ int dense_run(const uint8_t *const *tiles, const int *rows, float *const *outs, 
     a.band0[nseg] = bands;
     a.row0[nseg] = rall;
     a.rows_all = rall;
-    // split K until about two CTAs per SM, as far as the planes allow
-    const int NS = K / EX_KSL, want = 2 * sm_count();
-    int splits = bands >= want || bands > n_counters ? 1 : std::min(NS, (want + bands - 1) / bands);
+    // split K while the CTAs still fit one wave (a CTA's stages take most of an SM's shared
+    // memory: one CTA per SM), as far as the planes allow; measured at 64 tokens: 2-3 waves of
+    // short two-slice CTAs took 38 us for q, k, v of a Qwen3 layer
+    const int NS = K / EX_KSL, sms = sm_count();
+    int splits = bands >= sms || bands > n_counters ? 1 : std::max(1, std::min(NS, sms / bands));
     while (splits > 1 && (size_t)splits * T * rall > planes_floats) --splits;
     a.spc = (NS + splits - 1) / splits;
     splits = (NS + a.spc - 1) / a.spc;

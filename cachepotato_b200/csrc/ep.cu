@@ -266,13 +266,18 @@ static int ep_settle(cpg_ep *ep, const char *what) {
             ep_abort(ep);
             return CPG_ENCCL;
         }
-        if (now_ms() - t0 > ep->timeout_ms) {
+        const double waited = now_ms() - t0;
+        if (waited > ep->timeout_ms) {
             set_error("%s: not complete after %d ms (communicator aborted)", what, ep->timeout_ms);
             ep_abort(ep);
             return CPG_ETIMEOUT;
         }
-        const timespec ns = {0, 20000};
-        nanosleep(&ns, nullptr);
+        // the stream's next work waits for this: poll without sleeping for the first 2 ms (a
+        // sleep overshoots by tens of microseconds, which the GPU would idle), then back off
+        if (waited > 2.0) {
+            const timespec ns = {0, 20000};
+            nanosleep(&ns, nullptr);
+        }
     }
 }
 
