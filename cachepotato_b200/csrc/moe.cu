@@ -306,10 +306,29 @@ __global__ void __launch_bounds__(R_THREADS, 2) k_router(RouterArgs a) {
     const int ne = max(0, min(a.eb, a.E - e0));
     const int D = a.D, D4 = D / 4;
     float *gsm = xs + TB * D;
-    {   // the gain into shared memory, the router rows into L2
+    // the GEMV's router rows (below): a warp's K chunks of four experts at a time. When they fit
+    // one set of registers (d_model <= 2048) the first group is loaded here, before the wait on
+    // the previous kernel, and each next group while the current one is reduced.
+    constexpr int RC = 2;
+    const bool one_pass = D / 128 <= RC * (R_THREADS / 32);
+    const float *wrow = a.wgate + (size_t)e0 * D;
+    float4 w[RC][4];
+    auto load_w = [&](int eg, int c0) {
+#pragma unroll
+        for (int r = 0; r < RC; ++r) {
+            const int c = c0 + r * (R_THREADS / 32);
+#pragma unroll
+            for (int el = 0; el < 4; ++el)
+                w[r][el] = c < D / 128 && eg + el < ne
+                               ? __ldg(reinterpret_cast<const float4 *>(wrow + (size_t)(eg + el) * D) + c * 32 + lane)
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    };
+    if (one_pass) load_w(0, warp);
+    {   // the gain into shared memory, the remaining router rows into L2
         for (int i = tid; i < D4; i += R_THREADS)
             cp_async16(reinterpret_cast<float4 *>(gsm) + i, reinterpret_cast<const float4 *>(a.ln2) + i);
-        const char *wb = reinterpret_cast<const char *>(a.wgate + (size_t)e0 * D);
+        const char *wb = reinterpret_cast<const char *>(wrow);
         const size_t wbytes = (size_t)ne * D * sizeof(float);
         for (size_t o = (size_t)tid * 128; o < wbytes; o += (size_t)R_THREADS * 128)
             asm volatile("prefetch.global.L2 [%0];" ::"l"(wb + o));
@@ -324,42 +343,107 @@ __global__ void __launch_bounds__(R_THREADS, 2) k_router(RouterArgs a) {
             reinterpret_cast<uint32_t *>(a.zero_row)[i] = 0u;
     }
 
-    // hh = x + attn (qwen3_moe.c:178). The loads are issued 16 at a time per thread before any
-    // store, so the tile costs about one memory round trip (the kernel is latency-bound).
-    {
+    // hh = x + attn (qwen3_moe.c:178), then rmsnorm (kernels.c:408-413): inv = 1 / sqrt(sum(x^2)/n
+    // + eps); xn = x * inv * g. When a token row is exactly two float4 per thread (d_model 2048
+    // with 256 threads) the tile stays in registers from the loads to the normalised store: thread
+    // i holds float4 columns i and i + 256 of every token, its sums of squares per token are
+    // reduced over the warp and then over the warps in order. Otherwise the same steps run through
+    // shared memory. The loads are all in flight before any is used (the kernel is latency-bound).
+    if (TB == R_TB && D4 == 2 * R_THREADS) {
         const float4 *x4 = reinterpret_cast<const float4 *>(a.x + (size_t)t0 * D);
         const float4 *a4 = a.attn ? reinterpret_cast<const float4 *>(a.attn + (size_t)t0 * D) : nullptr;
-        float4 *s4 = reinterpret_cast<float4 *>(xs);
-        const int n4 = nt * D4;
-        for (int i0 = tid; i0 < n4; i0 += 16 * R_THREADS) {
-            float4 v[16];
+        float4 v[TB][2];
 #pragma unroll
-            for (int u = 0; u < 16; ++u) {
-                const int i = i0 + u * R_THREADS;
-                if (i < n4) v[u] = __ldg(x4 + i);
+        for (int t = 0; t < TB; ++t)
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+                v[t][h] = t < nt ? __ldg(x4 + t * D4 + h * R_THREADS + tid) : make_float4(0.f, 0.f, 0.f, 0.f);
+        if (a4) {
+#pragma unroll
+            for (int t = 0; t < TB; ++t)
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    if (t < nt) {
+                        const float4 b = __ldg(a4 + t * D4 + h * R_THREADS + tid);
+                        v[t][h].x += b.x; v[t][h].y += b.y; v[t][h].z += b.z; v[t][h].w += b.w;
+                    }
+                }
+        }
+        float ss[TB];
+#pragma unroll
+        for (int t = 0; t < TB; ++t) {
+            float q = 0.0f;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                q = fmaf(v[t][h].x, v[t][h].x, q);
+                q = fmaf(v[t][h].y, v[t][h].y, q);
+                q = fmaf(v[t][h].z, v[t][h].z, q);
+                q = fmaf(v[t][h].w, v[t][h].w, q);
             }
-            if (a4) {
+            ss[t] = warp_sum(q);
+        }
+        if (lane == 0)
+#pragma unroll
+            for (int t = 0; t < TB; ++t) s_red[warp][t] = ss[t];
+        cp_async_wait_all();                              // this thread's gain copies
+        __syncthreads();
+        if (tid < nt) {
+            float tot = 0.0f;
+#pragma unroll
+            for (int w = 0; w < R_THREADS / 32; ++w) tot += s_red[w][tid];
+            s_inv[tid] = __fdiv_rn(1.0f, __fsqrt_rn(__fdiv_rn(tot, (float)D) + a.eps));
+        }
+        __syncthreads();
+        const float4 *g4 = reinterpret_cast<const float4 *>(gsm);
+        const float4 g0 = g4[tid], g1 = g4[R_THREADS + tid];
+        float4 *s4 = reinterpret_cast<float4 *>(xs);
+#pragma unroll
+        for (int t = 0; t < TB; ++t) {
+            if (t < nt) {
+                const float inv = s_inv[t];
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const float4 gv = h ? g1 : g0;
+                    float4 o;
+                    o.x = __fmul_rn(__fmul_rn(v[t][h].x, inv), gv.x);
+                    o.y = __fmul_rn(__fmul_rn(v[t][h].y, inv), gv.y);
+                    o.z = __fmul_rn(__fmul_rn(v[t][h].z, inv), gv.z);
+                    o.w = __fmul_rn(__fmul_rn(v[t][h].w, inv), gv.w);
+                    s4[t * D4 + h * R_THREADS + tid] = o;
+                }
+            }
+        }
+    } else {
+        {
+            const float4 *x4 = reinterpret_cast<const float4 *>(a.x + (size_t)t0 * D);
+            const float4 *a4 = a.attn ? reinterpret_cast<const float4 *>(a.attn + (size_t)t0 * D) : nullptr;
+            float4 *s4 = reinterpret_cast<float4 *>(xs);
+            const int n4 = nt * D4;
+            for (int i0 = tid; i0 < n4; i0 += 16 * R_THREADS) {
+                float4 v[16];
 #pragma unroll
                 for (int u = 0; u < 16; ++u) {
                     const int i = i0 + u * R_THREADS;
-                    if (i < n4) {
-                        const float4 b = __ldg(a4 + i);
-                        v[u].x += b.x; v[u].y += b.y; v[u].z += b.z; v[u].w += b.w;
+                    if (i < n4) v[u] = __ldg(x4 + i);
+                }
+                if (a4) {
+#pragma unroll
+                    for (int u = 0; u < 16; ++u) {
+                        const int i = i0 + u * R_THREADS;
+                        if (i < n4) {
+                            const float4 b = __ldg(a4 + i);
+                            v[u].x += b.x; v[u].y += b.y; v[u].z += b.z; v[u].w += b.w;
+                        }
                     }
                 }
-            }
 #pragma unroll
-            for (int u = 0; u < 16; ++u) {
-                const int i = i0 + u * R_THREADS;
-                if (i < n4) s4[i] = v[u];
+                for (int u = 0; u < 16; ++u) {
+                    const int i = i0 + u * R_THREADS;
+                    if (i < n4) s4[i] = v[u];
+                }
             }
         }
-    }
-    __syncthreads();
-    // rmsnorm (kernels.c:408-413): inv = 1 / sqrt(sum(x^2)/n + eps); xn = x * inv * g. The sums of
-    // squares of all the tile's tokens with the whole CTA (float4 reads, a warp reduction per
-    // token, warps added in order), then the scaling pass.
-    {
+        __syncthreads();
         const float4 *s4 = reinterpret_cast<const float4 *>(xs);
         float ss[TB];
 #pragma unroll
@@ -427,23 +511,12 @@ __global__ void __launch_bounds__(R_THREADS, 2) k_router(RouterArgs a) {
     // token (rank t mod cluster size).
     const int rank = cluster_ctarank(), csz = cluster_nctarank();
     const float4 *xs4 = reinterpret_cast<const float4 *>(xs);
-    const float *wrow = a.wgate + (size_t)e0 * D;
-    constexpr int RC = 4;                                  // K chunks of a warp in registers at once
     for (int eg = 0; eg < ne; eg += 4) {
         float acc[TB * 4];
 #pragma unroll
         for (int i = 0; i < TB * 4; ++i) acc[i] = 0.0f;
         for (int c0 = warp; c0 < D / 128; c0 += RC * (R_THREADS / 32)) {
-            float4 w[RC][4];
-#pragma unroll
-            for (int r = 0; r < RC; ++r) {
-                const int c = c0 + r * (R_THREADS / 32);
-#pragma unroll
-                for (int el = 0; el < 4; ++el)
-                    w[r][el] = c < D / 128 && eg + el < ne
-                                   ? __ldg(reinterpret_cast<const float4 *>(wrow + (size_t)(eg + el) * D) + c * 32 + lane)
-                                   : make_float4(0.f, 0.f, 0.f, 0.f);
-            }
+            if (!one_pass) load_w(eg, c0);
 #pragma unroll
             for (int r = 0; r < RC; ++r) {
                 const int c = c0 + r * (R_THREADS / 32);
@@ -465,6 +538,7 @@ __global__ void __launch_bounds__(R_THREADS, 2) k_router(RouterArgs a) {
                 }
             }
         }
+        if (one_pass && eg + 4 < ne) load_w(eg + 4, warp);     // in flight during the reduction
         warp_sums<TB * 4>(acc);
         if constexpr (TB * 4 == 32) {
             s_part[warp][lane] = acc[0];
