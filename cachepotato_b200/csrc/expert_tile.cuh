@@ -70,8 +70,9 @@ __device__ __forceinline__ void warp_topk(const float (&p)[PL], int E, int K, in
 // this code runs once per launch, so its instruction fetch is part of the latency). A NaN
 // probability makes ranks meaningless; warp 0 then runs the scan itself (warp_topk, which
 // reproduces the reference's NaN behaviour). logits: global memory, or shared memory with
-// LOGITS_SMEM; s_p: shared memory for MAXE + MAXK floats; sel_e, sel_w: K ids and weights, in
-// shared or global memory. Every thread of the CTA calls it.
+// LOGITS_SMEM; s_p: 16-byte aligned shared memory for MAXE + MAXK floats (MAXE a multiple of
+// four); sel_e, sel_w: K ids and weights, in shared or global memory. Every thread of the CTA
+// calls it.
 template <int MAXE, int MAXK, bool LOGITS_SMEM = false>
 __device__ void select_topk(const float *logits, int E, int K, int *sel_e, float *sel_w, float *s_p) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -107,6 +108,7 @@ __device__ void select_topk(const float *logits, int E, int K, int *sel_e, float
         }
         nan = __any_sync(0xffffffffu, nan);
         if (lane == 0) s_nan = nan;
+        if (lane < ((E + 3) & ~3) - E) s_p[E + lane] = -INFINITY;     // the rank loop's padding
         if (nan) {
             float sp[MAXK];
             int se[MAXK];
@@ -120,13 +122,20 @@ __device__ void select_topk(const float *logits, int E, int K, int *sel_e, float
     }
     __syncthreads();
     if (!s_nan) {
+        // rank of expert e: the probabilities read four at a time (s_p is 16-byte aligned and
+        // padded with -inf up to a multiple of four, which never counts)
+        const int E4 = (E + 3) >> 2;
         for (int e = tid; e < E; e += blockDim.x) {
             const float pe = s_p[e];
             int r = 0;
 #pragma unroll 4
-            for (int f = 0; f < E; ++f) {
-                const float pf = s_p[f];
-                r += (pf > pe || (pf == pe && f < e)) ? 1 : 0;
+            for (int f4 = 0; f4 < E4; ++f4) {
+                const float4 q = reinterpret_cast<const float4 *>(s_p)[f4];
+                const int f = 4 * f4;
+                r += (q.x > pe || (q.x == pe && f < e)) ? 1 : 0;
+                r += (q.y > pe || (q.y == pe && f + 1 < e)) ? 1 : 0;
+                r += (q.z > pe || (q.z == pe && f + 2 < e)) ? 1 : 0;
+                r += (q.w > pe || (q.w == pe && f + 3 < e)) ? 1 : 0;
             }
             if (r < K) {
                 sel_e[r] = e;

@@ -568,7 +568,7 @@ __global__ void __launch_bounds__(R_THREADS, 2) k_router(RouterArgs a) {
     // this token tile) has passed the barrier (release/acquire at cluster scope); CTA r then
     // routes tokens r, r + cluster size, ... of the tile, each with the whole CTA
     cluster_sync();
-    __shared__ float s_p[MAX_E + MAX_K];
+    __shared__ __align__(16) float s_p[MAX_E + MAX_K];
     __shared__ int s_e[MAX_K];
     __shared__ float s_w[MAX_K];
     for (int r = rank, j = 0; r < nt; r += csz, ++j) {

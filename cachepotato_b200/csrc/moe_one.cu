@@ -260,7 +260,7 @@ __global__ void __launch_bounds__(O_THREADS, 1) k_moe_one(OneArgs a) {
 
     // ---------------- phase S: routing; this CTA's gate/up bands are a consecutive range
     {
-        __shared__ float s_p[O_MAXE + O_MAXK];           // probabilities, then the selected ones
+        __shared__ __align__(16) float s_p[O_MAXE + O_MAXK];   // probabilities, then the selected ones
         select_topk<O_MAXE, O_MAXK>(a.logits, E, K, s_sel_e, s_sel_w, s_p);
     }
     if (c == 0 && tid < K) {
