@@ -316,9 +316,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const TcArgs a, const
                 const int y0 = KIND == 0 ? m * TC_BM : m * TC_ROWS;
                 const int y1 = KIND == 0 ? m * TC_BM : m * TC_ROWS + TC_BM;
                 for (int g = 0; g < NG; ++g, ++git) {
-                    const int slot = git & 1;
+                    const int slot = git % TC_RAW_SLOTS;
                     if (git >= TC_RAW_SLOTS &&
-                        !tc_wait(&raw_empty[slot], (uint32_t)((git >> 1) - 1) & 1u, abort_flag, a.status, ST_TIMEOUT_EMPTY)) {
+                        !tc_wait(&raw_empty[slot], (uint32_t)(git / TC_RAW_SLOTS - 1) & 1u, abort_flag, a.status, ST_TIMEOUT_EMPTY)) {
                         ok = false;
                         break;
                     }
@@ -330,7 +330,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const TcArgs a, const
             }
             // the last groups' copies must land before the CTA may exit (bounded)
             for (int q = git > TC_RAW_SLOTS ? git - TC_RAW_SLOTS : 0; q < git; ++q)
-                mbar_wait(&raw_full[q & 1], (uint32_t)(q >> 1) & 1u);
+                mbar_wait(&raw_full[q % TC_RAW_SLOTS], (uint32_t)(q / TC_RAW_SLOTS) & 1u);
         }
     } else if (warp == 1) {
         // ---------------- MMA issuer (one thread)
@@ -423,8 +423,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const TcArgs a, const
             const int cnt = min(BN, ex.z - n * BN);
             bool ok = true;
             for (int g = 0; g < NG && ok; ++g, ++git) {
-                const int slot = git & 1;
-                if (!tc_wait(&raw_full[slot], (uint32_t)(git >> 1) & 1u, abort_flag, a.status, ST_TIMEOUT_FULL)) {
+                const int slot = git % TC_RAW_SLOTS;
+                if (!tc_wait(&raw_full[slot], (uint32_t)(git / TC_RAW_SLOTS) & 1u, abort_flag, a.status, ST_TIMEOUT_FULL)) {
                     ok = false;
                     break;
                 }
