@@ -9,7 +9,7 @@
 //     xh[s][t] = hi(x_t[256s .. 256s + 255]) (512 B), 16 B gap, lo(...) (512 B), 16 B gap
 // so that one bulk copy brings a K slice of every token. A CTA owns a band of 64 rows and one
 // range of K slices (split K when the bands alone leave SMs idle): one producer thread copies
-// the band's four tiles and the tokens' slice per stage (two stages), eight consumer warps
+// the band's four tiles and the tokens' slice per stage (2-8 stages, as many as fit), eight consumer warps
 // (four 16-row groups × two halves of the tokens) decode Q4_0 / Q8_0 in registers into
 // mma.sync.m16n8k16 with the tokens' hi and lo halves in neighbouring N columns, scale each
 // group's partial sums in fp32 and add hi + lo at the end, as the batched expert kernel does.
@@ -27,7 +27,7 @@ constexpr int DN_ROWS = 64;                       // rows per band
 constexpr int DN_MAXT = 64;                       // token rows per launch
 constexpr int DN_LOFF = EX_KSL * 2 + 16;          // a token slice's lo half
 constexpr int DN_BROW = 2 * DN_LOFF;              // one token's slice
-constexpr int DN_STAGES = 2;
+constexpr int DN_MAX_STAGES = 8;                  // ring depth: as many stages as fit, at most 8
 
 __constant__ Perm64 c_perm_dense[2] = {kPermQ4, kPermQ8};
 
@@ -46,6 +46,7 @@ struct DenseArgs {
     float *planes;                                // split K: (splits, T, rows_all)
     int *counters;                                // split K: one per band, zero between launches
     int *status;
+    int stages;                                   // ring depth (<= DN_MAX_STAGES)
 };
 
 // One K slice of one 16-row tile against ntw ≤ 8 eight-column tiles of tokens (bs: this lane's
@@ -90,7 +91,8 @@ __global__ void __launch_bounds__(DN_THREADS, 1) k_dense_dec(const DenseArgs a) 
     using X = ExTile<ENC>;
     extern __shared__ uint8_t dn_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(dn_raw) + 127) & ~uintptr_t(127));
-    __shared__ __align__(8) uint64_t full[DN_STAGES], empty[DN_STAGES];
+    __shared__ __align__(8) uint64_t full[DN_MAX_STAGES], empty[DN_MAX_STAGES];
+    const int NST = a.stages;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int band = blockIdx.x, kidx = blockIdx.y;
     int sg = 0;                                           // the segment (static indices only)
@@ -103,10 +105,12 @@ __global__ void __launch_bounds__(DN_THREADS, 1) k_dense_dec(const DenseArgs a) 
     const int R = seg.rows, T = a.T;
     const int NS = a.K / EX_KSL;
     const int s0 = kidx * a.spc, s1 = min(NS, s0 + a.spc);
+    // a stage holds the token slices rounded up to four (the B fragments of a column tile read
+    // four tokens whatever T is; the columns past T are never written out)
     const uint32_t wbytes = 4 * X::TB, abytes = (uint32_t)T * DN_BROW;
-    const size_t stage = ((size_t)wbytes + abytes + 127) & ~size_t(127);
+    const size_t stage = ((size_t)wbytes + (size_t)((T + 3) & ~3) * DN_BROW + 127) & ~size_t(127);
     if (tid == 0) {
-        for (int i = 0; i < DN_STAGES; ++i) {
+        for (int i = 0; i < NST; ++i) {
             mbar_init(&full[i], 1);
             mbar_init(&empty[i], DN_CW);
         }
@@ -120,8 +124,8 @@ __global__ void __launch_bounds__(DN_THREADS, 1) k_dense_dec(const DenseArgs a) 
         if (lane != 0) return;
         int issued = 0;
         for (int s = s0; s < s1; ++s, ++issued) {
-            const int i = s - s0, st = i % DN_STAGES;
-            if (i >= DN_STAGES && !mbar_wait(&empty[st], (uint32_t)(i / DN_STAGES - 1) & 1u)) {
+            const int i = s - s0, st = i % NST;
+            if (i >= NST && !mbar_wait(&empty[st], (uint32_t)(i / NST - 1) & 1u)) {
                 atomicCAS(a.status, ST_OK, ST_TIMEOUT_EMPTY);
                 break;
             }
@@ -130,9 +134,9 @@ __global__ void __launch_bounds__(DN_THREADS, 1) k_dense_dec(const DenseArgs a) 
             bulk_g2s(dst, seg.tiles + ((size_t)s * (R / 16) + (size_t)rb * 4) * X::TB, wbytes, &full[st]);
             bulk_g2s(dst + wbytes, a.xh + (size_t)s * abytes, abytes, &full[st]);
         }
-        for (int k = 1; k <= DN_STAGES && issued - k >= 0; ++k) {   // copies in flight land first
+        for (int k = 1; k <= NST && issued - k >= 0; ++k) {         // copies in flight land first
             const int j = issued - k;
-            mbar_wait(&full[j % DN_STAGES], (uint32_t)(j / DN_STAGES) & 1u);
+            mbar_wait(&full[j % NST], (uint32_t)(j / NST) & 1u);
         }
         return;
     }
@@ -152,8 +156,8 @@ __global__ void __launch_bounds__(DN_THREADS, 1) k_dense_dec(const DenseArgs a) 
         for (int c = 0; c < 4; ++c) acc[nt][c] = 0.0f;
     bool ok = true;
     for (int s = s0; s < s1; ++s) {
-        const int i = s - s0, st = i % DN_STAGES;
-        if (!mbar_wait(&full[st], (uint32_t)(i / DN_STAGES) & 1u)) {
+        const int i = s - s0, st = i % NST;
+        if (!mbar_wait(&full[st], (uint32_t)(i / NST) & 1u)) {
             if (lane == 0) atomicCAS(a.status, ST_OK, ST_TIMEOUT_FULL);
             ok = false;
             break;
@@ -325,8 +329,12 @@ int dense_run(const uint8_t *const *tiles, const int *rows, float *const *outs, 
     a.spc = (NS + splits - 1) / splits;
     splits = (NS + a.spc - 1) / a.spc;
     const uint32_t tb = enc == CPG_ENC_Q4 ? ExTile<CPG_ENC_Q4>::TB : ExTile<CPG_ENC_Q8>::TB;
-    const size_t stage = ((size_t)4 * tb + (size_t)T * DN_BROW + 127) & ~size_t(127);
-    const size_t smem = DN_STAGES * stage + 128;
+    const size_t stage = ((size_t)4 * tb + (size_t)((T + 3) & ~3) * DN_BROW + 127) & ~size_t(127);   // as the kernel
+    // as deep a ring as fits: a step of a few sequences has small stages (the weight tiles and a
+    // few token slices), and the copies in flight per SM are what bounds it
+    const int fit = (int)(((size_t)smem_optin() - 4096 - 128) / stage);
+    a.stages = std::max(2, std::min(DN_MAX_STAGES, fit));
+    const size_t smem = a.stages * stage + 128;
     const void *k = enc == CPG_ENC_Q4 ? (const void *)k_dense_dec<CPG_ENC_Q4> : (const void *)k_dense_dec<CPG_ENC_Q8>;
     const int rc = allow_max_smem(k);
     if (rc) return rc;

@@ -795,8 +795,11 @@ int dense_run(const uint8_t *const *tiles, const int *rows, float *const *outs, 
               int *status, cudaStream_t s);
 constexpr int QW_DENSE_DEC_MIN_T = 5, QW_DENSE_DEC_MAX_T = 64;   // steps of several sequences on dense.cu
 
-// Decode tile copies of the attention projections and the lm_head (dense.cu), for steps of
-// QW_DENSE_DEC_MIN_T .. QW_DENSE_DEC_MAX_T sequences, with their operand and split-K buffers.
+// Decode tile copies of the attention projections and the lm_head (dense.cu) with their operand
+// and split-K buffers, built by the first batch of at least QW_DENSE_DEC_MIN_T slots and kept
+// with the model: steps of QW_DENSE_DEC_MIN_T .. QW_DENSE_DEC_MAX_T sequences run their
+// projections and head on the tensor cores. One sequence keeps the streaming GEMV, which is
+// faster at one token (measured: 2.95 against 3.92 ms per token for the whole model).
 struct QwDense {
     std::vector<uint8_t *> attn;                   // 4 per layer: Wq, Wk, Wv, Wo
     uint8_t *head = nullptr;
@@ -833,6 +836,7 @@ struct cpg_qwen3 {
     float *as_part = nullptr;                      // split attention: (T < QW_DENSE_MIN_T, H, AS_SPLIT, 2 + hd)
     int *as_cnt = nullptr;                         // and a counter per (query, head), zero between launches
     size_t ap_smem = 0;                            // shared memory k_attention_prompt may use
+    cpg::QwDense dn;                               // dense.cu tiles and buffers (empty: not built)
     void *ws = nullptr;
     size_t ws_bytes = 0;
     int pos = 0;
@@ -841,6 +845,12 @@ struct cpg_qwen3 {
 
 using namespace cpg;
 
+static void free_dense(QwDense &dn) {
+    for (uint8_t *p : dn.attn) cudaFree(p);
+    cudaFree(dn.head); cudaFree(dn.xh); cudaFree(dn.planes); cudaFree(dn.status); cudaFree(dn.counters);
+    dn = QwDense{};
+}
+
 static void qwen3_free(cpg_qwen3 *m) {
     cudaFree(m->x); cudaFree(m->xn); cudaFree(m->q); cudaFree(m->ao); cudaFree(m->at); cudaFree(m->kv);
     cudaFree(m->logits); cudaFree(m->d_ids); cudaFree(m->d_next); cudaFree(m->ws);
@@ -848,10 +858,54 @@ static void qwen3_free(cpg_qwen3 *m) {
     cudaFree(m->am_v); cudaFree(m->am_i);
     cudaFree(m->dmaps); cudaFree(m->dtab); cudaFree(m->dn_active); cudaFree(m->iota); cudaFree(m->d_status);
     cudaFree(m->x16); cudaFree(m->planes); cudaFree(m->as_part); cudaFree(m->as_cnt);
+    free_dense(m->dn);
     if (m->step_graph) cudaGraphExecDestroy(m->step_graph);
     if (m->h_next) cudaFreeHost(m->h_next);
     if (m->s) cudaStreamDestroy(m->s);
     delete m;
+}
+
+// The dense.cu copies of every projection and of the lm_head, when every matrix is Q4_0 / Q8_0 of
+// a usable shape (otherwise the streaming GEMV and the row kernel serve them). All or nothing.
+static int build_dense(cpg_qwen3 *m) {
+    const int QD = m->H * QW_HD, KDi = m->KV * QW_HD, D = m->D;
+    bool ok = true;
+    for (int l = 0; l < m->L && ok; ++l) {
+        const cpg_qwen3_attn &A = m->attn[l];
+        ok = A.wk.enc == A.wq.enc && A.wv.enc == A.wq.enc && dense_ok(A.wq.enc, QD, D) && dense_ok(A.wk.enc, KDi, D) &&
+             dense_ok(A.wo.enc, D, QD);
+    }
+    if (!ok) return CPG_OK;
+    QwDense &dn = m->dn;
+    int rc = CPG_OK;
+    for (int l = 0; l < m->L && !rc; ++l) {
+        const cpg_qwen3_attn &A = m->attn[l];
+        const cpg_tensor w[4] = {A.wq, A.wk, A.wv, A.wo};
+        const int rows[4] = {QD, KDi, KDi, D}, ks[4] = {D, D, D, QD};
+        for (int i = 0; i < 4 && !rc; ++i) {
+            uint8_t *t = nullptr;
+            rc = dense_build(w[i].p, w[i].enc, rows[i], ks[i], &t, m->s);
+            if (!rc) dn.attn.push_back(t);
+        }
+    }
+    if (!rc && dense_ok(m->lm_head.enc, m->V, D)) rc = dense_build(m->lm_head.p, m->lm_head.enc, m->V, D, &dn.head, m->s);
+    if (rc) {
+        cudaStreamSynchronize(m->s);
+        free_dense(dn);
+        return rc;
+    }
+    const int kmax = QD > D ? QD : D;
+    dn.planes_floats = (size_t)16 * QW_DENSE_DEC_MAX_T * (QD + 2 * KDi > D ? QD + 2 * KDi : D);
+    cudaError_t ce = cudaMalloc(&dn.xh, dense_act_bytes(QW_DENSE_DEC_MAX_T, kmax));
+    if (ce == cudaSuccess) ce = cudaMalloc(&dn.planes, dn.planes_floats * sizeof(float));
+    if (ce == cudaSuccess) ce = cudaMalloc(&dn.status, sizeof(int));
+    if (ce == cudaSuccess) ce = cudaMemsetAsync(dn.status, 0, sizeof(int), m->s);
+    if (ce == cudaSuccess) ce = cudaMalloc(&dn.counters, QW_DENSE_COUNTERS * sizeof(int));
+    if (ce == cudaSuccess) ce = cudaMemsetAsync(dn.counters, 0, QW_DENSE_COUNTERS * sizeof(int), m->s);
+    if (ce == cudaSuccess) ce = cudaStreamSynchronize(m->s);
+    if (ce == cudaSuccess) return CPG_OK;
+    free_dense(dn);
+    return cuda_fail(ce, "cpg_qwen3_batch_create: dense projections");
 }
 
 extern "C" int cpg_qwen3_create(const cpg_qwen3_desc *d, cpg_qwen3 **out) {
@@ -1167,8 +1221,8 @@ static int qwen3_read_next(cpg_qwen3 *m, int *next_id) {
 }
 
 // The projection GEMM's bounded waits (prompts and steps of QW_DENSE_MIN_T tokens or more).
-static int qwen3_status(cpg_qwen3 *m, const char *fn, const int *extra = nullptr) {
-    const int *words[2] = {m->d_status, extra};
+static int qwen3_status(cpg_qwen3 *m, const char *fn) {
+    const int *words[2] = {m->d_status, m->dn.status};
     for (const int *w : words) {
         if (!w) continue;
         int st = 0;
@@ -1276,7 +1330,6 @@ struct cpg_qwen3_batch {
     int *am_i = nullptr, *as_cnt = nullptr;
     int last_rows = 0;
     std::vector<cudaGraphExec_t> graphs; // one step of n sequences, by n
-    QwDense dn;                          // the dense.cu projections and head, when the shapes allow
 };
 
 static void batch_free(cpg_qwen3_batch *b) {
@@ -1285,8 +1338,6 @@ static void batch_free(cpg_qwen3_batch *b) {
     cudaFree(b->kv); cudaFree(b->slot_pos); cudaFree(b->tok_slot); cudaFree(b->tok_pos);
     cudaFree(b->d_next); cudaFree(b->d_step); cudaFree(b->d_out); cudaFree(b->logits); cudaFree(b->am_v);
     cudaFree(b->am_i); cudaFree(b->as_part); cudaFree(b->as_cnt);
-    for (uint8_t *p : b->dn.attn) cudaFree(p);
-    cudaFree(b->dn.head); cudaFree(b->dn.xh); cudaFree(b->dn.planes); cudaFree(b->dn.status); cudaFree(b->dn.counters);
     if (b->h_buf) cudaFreeHost(b->h_buf);
     delete b;
 }
@@ -1328,38 +1379,8 @@ extern "C" int cpg_qwen3_batch_create(cpg_qwen3 *m, int n_slots, int max_ctx, cp
         batch_free(b);
         return cuda_fail(ce, "cpg_qwen3_batch_create: allocation");
     }
-    // steps of QW_DENSE_DEC_MIN_T .. QW_DENSE_DEC_MAX_T sequences: decode tile copies of every
-    // projection and of the lm_head (dense.cu), when every matrix is Q4_0 / Q8_0 of a usable shape
-    const int QD = m->H * QW_HD, KDi = m->KV * QW_HD, D = m->D;
-    bool dn = n_slots >= QW_DENSE_DEC_MIN_T;
-    for (int l = 0; l < m->L && dn; ++l) {
-        const cpg_qwen3_attn &A = m->attn[l];
-        dn = A.wk.enc == A.wq.enc && A.wv.enc == A.wq.enc && dense_ok(A.wq.enc, QD, D) && dense_ok(A.wk.enc, KDi, D) &&
-             dense_ok(A.wo.enc, D, QD);
-    }
-    if (dn) {
-        int rc = CPG_OK;
-        for (int l = 0; l < m->L && !rc; ++l) {
-            const cpg_qwen3_attn &A = m->attn[l];
-            const cpg_tensor w[4] = {A.wq, A.wk, A.wv, A.wo};
-            const int rows[4] = {QD, KDi, KDi, D}, ks[4] = {D, D, D, QD};
-            for (int i = 0; i < 4 && !rc; ++i) {
-                uint8_t *t = nullptr;
-                rc = dense_build(w[i].p, w[i].enc, rows[i], ks[i], &t, m->s);
-                if (!rc) b->dn.attn.push_back(t);
-            }
-        }
-        if (!rc && dense_ok(m->lm_head.enc, m->V, D)) rc = dense_build(m->lm_head.p, m->lm_head.enc, m->V, D, &b->dn.head, m->s);
-        const int kmax = QD > D ? QD : D;
-        b->dn.planes_floats = (size_t)16 * QW_DENSE_DEC_MAX_T * (QD + 2 * KDi > D ? QD + 2 * KDi : D);
-        if (!rc) ce = cudaMalloc(&b->dn.xh, dense_act_bytes(QW_DENSE_DEC_MAX_T, kmax));
-        if (!rc && ce == cudaSuccess) ce = cudaMalloc(&b->dn.planes, b->dn.planes_floats * sizeof(float));
-        if (!rc && ce == cudaSuccess) ce = cudaMalloc(&b->dn.status, sizeof(int));
-        if (!rc && ce == cudaSuccess) ce = cudaMemsetAsync(b->dn.status, 0, sizeof(int), m->s);
-        if (!rc && ce == cudaSuccess) ce = cudaMalloc(&b->dn.counters, QW_DENSE_COUNTERS * sizeof(int));
-        if (!rc && ce == cudaSuccess) ce = cudaMemsetAsync(b->dn.counters, 0, QW_DENSE_COUNTERS * sizeof(int), m->s);
-        if (!rc && ce == cudaSuccess) ce = cudaStreamSynchronize(m->s);
-        if (!rc && ce != cudaSuccess) rc = cuda_fail(ce, "cpg_qwen3_batch_create: dense projections");
+    if (n_slots >= QW_DENSE_DEC_MIN_T && m->dn.attn.empty()) {
+        const int rc = build_dense(m);
         if (rc) {
             batch_free(b);
             return rc;
@@ -1386,7 +1407,7 @@ extern "C" int cpg_qwen3_batch_prefill(cpg_qwen3_batch *b, int slot, const int *
     CPG_CUDA(cudaMemsetAsync(b->slot_pos + slot, 0, sizeof(int), m->s));
     CPG_CUDA(cudaMemcpyAsync(m->d_ids, ids, sizeof(int) * (size_t)n, cudaMemcpyHostToDevice, m->s));
     const QwSeq sq{b->kv, b->S, b->C, b->slot_pos + slot, slot, nullptr, nullptr, n, m->as_part, m->as_cnt,
-                   b->logits, b->am_v, b->am_i, b->d_next, nullptr};
+                   b->logits, b->am_v, b->am_i, b->d_next, m->dn.attn.empty() ? nullptr : &m->dn};
     int rc = qwen3_enqueue(m, sq, n, m->s);
     if (rc) return rc;
     b->h_buf[0] = n;
@@ -1428,7 +1449,7 @@ static int batch_run(cpg_qwen3_batch *b, const int *slots, const int *ids, int n
     CPG_CUDA(cudaMemsetAsync(b->d_step, 0, sizeof(int), m->s));
     if (!b->graphs[n]) {
         const QwSeq sq{b->kv, b->S, b->C, nullptr, -1, b->tok_slot, b->tok_pos, 0, b->as_part, b->as_cnt,
-                       b->logits, b->am_v, b->am_i, b->d_next, b->dn.attn.empty() ? nullptr : &b->dn};
+                       b->logits, b->am_v, b->am_i, b->d_next, m->dn.attn.empty() ? nullptr : &m->dn};
         cudaGraph_t g = nullptr;
         CPG_CUDA(cudaStreamBeginCapture(m->s, cudaStreamCaptureModeThreadLocal));
         int rc = 0;
@@ -1466,7 +1487,7 @@ extern "C" int cpg_qwen3_batch_step(cpg_qwen3_batch *b, const int *slots, const 
     if (rc) return rc;
     CPG_CUDA(cudaMemcpyAsync(next_ids, b->d_out, sizeof(int) * n, cudaMemcpyDeviceToHost, b->m->s));
     CPG_CUDA(cudaStreamSynchronize(b->m->s));
-    return qwen3_status(b->m, "cpg_qwen3_batch_step", b->dn.status);
+    return qwen3_status(b->m, "cpg_qwen3_batch_step");
 }
 
 extern "C" int cpg_qwen3_batch_generate(cpg_qwen3_batch *b, const int *slots, const int *ids, int n, int n_steps,
@@ -1479,7 +1500,7 @@ extern "C" int cpg_qwen3_batch_generate(cpg_qwen3_batch *b, const int *slots, co
     if (rc) return rc;
     CPG_CUDA(cudaMemcpyAsync(out_ids, b->d_out, sizeof(int) * (size_t)n * n_steps, cudaMemcpyDeviceToHost, b->m->s));
     CPG_CUDA(cudaStreamSynchronize(b->m->s));
-    return qwen3_status(b->m, "cpg_qwen3_batch_generate", b->dn.status);
+    return qwen3_status(b->m, "cpg_qwen3_batch_generate");
 }
 
 extern "C" int cpg_qwen3_batch_position(const cpg_qwen3_batch *b, int slot) {

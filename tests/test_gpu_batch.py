@@ -52,18 +52,20 @@ def test_batch_matches_reference_per_sequence(orc, ref):
         gm.close()
 
 
-def test_batch_of_twelve_on_dense_kernel(orc, ref):
-    """12 sequences: the step's projections and lm_head run on the dense tensor-core kernel
-    (5 to 64 token rows: decode tile copies, fp16 hi + lo activations, f32 group scales)."""
+@pytest.mark.parametrize("n", [7, 12])
+def test_batch_on_dense_kernel(orc, ref, n):
+    """7 and 12 sequences: the step's projections and lm_head run on the dense tensor-core kernel
+    (5 to 64 token rows: decode tile copies, fp16 hi + lo activations, f32 group scales); 7 rows
+    leave a partly filled four-token column tile."""
     from cachepotato_b200.qwen3 import Qwen3Batch
     m = _small(orc, 41)
-    prompts = _prompts(m.vocab, list(range(1, 13)), 42)
+    prompts = _prompts(m.vocab, list(range(1, n + 1)), 42)
     n_new = 4
     gm = device_model(m, max_ctx=32)
-    b = Qwen3Batch(gm, 12, 20)
+    b = Qwen3Batch(gm, n, 20)
     try:
         first = [b.prefill(j, p) for j, p in enumerate(prompts)]
-        slots = np.arange(12)[::-1].copy()                       # reversed slot order
+        slots = np.arange(n)[::-1].copy()                        # reversed slot order
         out = b.generate(slots, [first[j] for j in slots], n_new)
         lg = b.logits().cpu().numpy()
         for r, j in enumerate(slots):
