@@ -249,6 +249,18 @@ __device__ __forceinline__ uint32_t lop3_and_xor(uint32_t a, uint32_t b, uint32_
     return r;
 }
 
+// (a0, a1) = fma(d, (s0, s1), (a0, a1)) as one packed f32x2 instruction (sm_100): each lane is
+// an IEEE fma with round to nearest, the same value fmaf gives.
+__device__ __forceinline__ void fma2_f32(float &a0, float &a1, float d, float s0, float s1) {
+    asm("{\n\t.reg .b64 A, B, C;\n\t"
+        "mov.b64 A, {%0, %1};\n\t"
+        "mov.b64 B, {%2, %2};\n\t"
+        "mov.b64 C, {%3, %4};\n\t"
+        "fma.rn.f32x2 A, B, C, A;\n\t"
+        "mov.b64 {%0, %1}, A;\n\t}"
+        : "+f"(a0), "+f"(a1) : "f"(d), "f"(s0), "f"(s1));
+}
+
 __device__ __forceinline__ uint32_t hsub2_u32(uint32_t a, uint32_t b) {
     uint32_t r;
     asm("sub.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));

@@ -78,8 +78,8 @@ __device__ __forceinline__ void dense_slice(const uint8_t *tp, int lane, const u
                     float sj[4];
                     mma_16816(sj, fh[0], bq.x, bq.y, z);
                     mma_16816(sj, fh[1], bq.z, bq.w, sj);
-#pragma unroll
-                    for (int c = 0; c < 4; ++c) acc[nt][c] = fmaf(c >> 1 ? d1 : d0, sj[c], acc[nt][c]);
+                    fma2_f32(acc[nt][0], acc[nt][1], d0, sj[0], sj[1]);
+                    fma2_f32(acc[nt][2], acc[nt][3], d1, sj[2], sj[3]);
                 }
             }
         }
@@ -255,7 +255,8 @@ __global__ void k_tile_matrix(const uint8_t *__restrict__ src, int R, int K, uin
         const int lane = (int)(i & 31);
         const long q = i >> 5;
         const int s = (int)(q / RT), rt = (int)(q - (long)s * RT);
-        tile_build_lane<ENC>(src + (size_t)rt * 16 * rowb + (size_t)s * 8 * X::GB, rowb, out + (size_t)q * X::TB, lane);
+        const uint8_t *t0 = src + (size_t)rt * 16 * rowb + (size_t)s * 8 * X::GB;
+        tile_build_lane<ENC>(t0, t0 + 8 * rowb, rowb, out + (size_t)q * X::TB, lane);
     }
 }
 

@@ -196,8 +196,10 @@ __device__ __forceinline__ void q8_word(uint32_t w, uint32_t &s0, uint32_t &s2) 
 // Decode tile layout of one expert matrix (R rows, Kd values), built once per layer: tile (s, rt)
 // covers rows [16rt, 16rt + 16) and values [256s, 256s + 256) and sits at byte (s·R/16 + rt)·TB,
 // TB = 16 rows × 8 groups × group bytes, so the row tiles of one K slice are contiguous (one bulk
-// copy per matrix and stage). Inside a tile, for group pair P and lane l = 4g + t of the warp that
-// consumes it:
+// copy per matrix and stage). An expert's gate and up matrices form one interleaved matrix of
+// 2·d_exp rows: its tile rt holds gate rows [8rt, 8rt + 8) as tile rows 0-7 and the same up rows as
+// tile rows 8-15, so one MMA row pair (g, g + 8) is feature 8rt + g of both matrices. Inside a
+// tile, for group pair P and lane l = 4g + t of the warp that consumes it:
 //   Q4: 16 B at (32P + l)·16 = row g's two words for this lane, then row g+8's two words;
 //   Q8: 16 B at (32P + l)·16 = row g's four words; row g+8's at 2048 + (32P + l)·16;
 // then the scales: row g's eight fp16 group scales at DB + 32g, row g+8's at DB + 32g + 16
@@ -210,15 +212,18 @@ struct ExTile {
     static constexpr int DB = ENC == CPG_ENC_Q4 ? 2048 : 4096; // scale block offset
 };
 
-// Lane `lane`'s share of building one decode tile from raw rows: src = the tile's first row at
-// its K slice (row stride rowb bytes), dst = the tile. Every lane of a warp writes its words of
-// the four group pairs; lanes t = 0, 1 of each quad also write the scales of rows g, g + 8.
+// Lane `lane`'s share of building one decode tile from raw rows: src = the raw row that becomes
+// tile row 0 and src8 the one that becomes tile row 8, both at the tile's K slice (row stride
+// rowb bytes; src8 = src + 8·rowb for 16 consecutive rows of one matrix), dst = the tile. Every
+// lane of a warp writes its words of the four group pairs; lanes t = 0, 1 of each quad also write
+// the scales of rows g, g + 8.
 template <int ENC>
-__device__ __forceinline__ void tile_build_lane(const uint8_t *src, size_t rowb, uint8_t *dst, int lane) {
+__device__ __forceinline__ void tile_build_lane(const uint8_t *src, const uint8_t *src8, size_t rowb, uint8_t *dst,
+                                                int lane) {
     using X = ExTile<ENC>;
     const int g = lane >> 2, t = lane & 3;
     const uint32_t *rg = reinterpret_cast<const uint32_t *>(src + g * rowb);
-    const uint32_t *r8 = reinterpret_cast<const uint32_t *>(src + (g + 8) * rowb);
+    const uint32_t *r8 = reinterpret_cast<const uint32_t *>(src8 + g * rowb);
     for (int P = 0; P < 4; ++P) {
         uint32_t a1, a2, a3, a4, b1, b2, b3, b4;
         float d0, d1;
@@ -232,7 +237,7 @@ __device__ __forceinline__ void tile_build_lane(const uint8_t *src, size_t rowb,
         }
     }
     if (t < 2) {                                               // lane t = 0: row g, t = 1: row g + 8
-        const uint8_t *row = src + (g + 8 * t) * rowb;
+        const uint8_t *row = (t ? src8 : src) + g * rowb;
         uint32_t w[4];
         for (int j = 0; j < 4; ++j)
             w[j] = (uint32_t)*reinterpret_cast<const uint16_t *>(row + 2 * j * X::GB) |

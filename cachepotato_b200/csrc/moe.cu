@@ -609,14 +609,16 @@ struct ExpertArgs {
     const __half *zero_row;      // operand row for padded token columns (zeroed with the header)
     int *status;
     int *item_ctr;               // dynamic work counter (zeroed with the header)
-    int *dep;                    // KIND_BOTH: per token chunk, gate/up items whose h is stored (zeroed by the router)
+    int *dep;                    // KIND_BOTH: per token chunk, gate/up warps whose h is stored (zeroed by the router)
     int stages;
     const uint8_t *tiles;        // the layer's expert matrices in the decode tile layout, (E, 3)
 };
 
 // An item is one row block of one active expert for one chunk of its tokens; it streams through
 // the stage ring in K slices of 256 values (eight groups per row: 144 B of Q4_0, 272 B of Q8_0).
-// GATEUP: 64 gate rows + the same 64 up rows, warp w holds matrix w & 1, 16-row tile w >> 1.
+// GATEUP: features [64m, 64m + 64) of gate and up, 8 interleaved tiles; warp w holds tile w
+// (gate rows 8w..8w+7 over the same up rows), so each thread ends with the gate and the up sum of
+// its feature and forms h itself.
 // DOWN: 128 rows of Wd, warp w holds tile w. Every warp keeps its rows over the whole K.
 template <int ENC, int KIND>
 struct ExCfg {
@@ -654,97 +656,44 @@ __device__ __forceinline__ void decode_item(const int4 *act, int U, int tiles, i
 }
 
 
-// One group pair of rows g and g+8 from the fragments: 4 MMAs per token tile and the fp32
-// group-scale accumulation (dg/d8: the pair's two scales of row g / g+8 as one fp16 pair).
-template <int NTL>
-__device__ __forceinline__ void pair_mma(const uint32_t (&fr)[4][4], uint32_t dg, uint32_t d8,
-                                         const uint4 (&b)[EX_NCH][2], float (&acc)[EX_NCH][4]) {
-    const float2 fg = __half22float2(*reinterpret_cast<const __half2 *>(&dg));
-    const float2 f8 = __half22float2(*reinterpret_cast<const __half2 *>(&d8));
-    const float dj[2] = {fg.x, f8.x}, dj1[2] = {fg.y, f8.y};   // group 2P / 2P+1, rows g / g+8
-#pragma unroll
-    for (int nt = 0; nt < NTL; ++nt) {
-        const float z[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-        float sj[4], sj1[4];
-        mma_16816(sj, fr[0], b[nt][0].x, b[nt][0].y, z);
-        mma_16816(sj, fr[1], b[nt][0].z, b[nt][0].w, sj);
-        mma_16816(sj1, fr[2], b[nt][1].x, b[nt][1].y, z);
-        mma_16816(sj1, fr[3], b[nt][1].z, b[nt][1].w, sj1);
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-            acc[nt][c] = fmaf(dj[c >> 1], sj[c], acc[nt][c]);
-            acc[nt][c] = fmaf(dj1[c >> 1], sj1[c], acc[nt][c]);
-        }
-    }
-}
-
-// Operand fragments of pair p of the K slice for the NTL token tiles, from the stage's token
-// rows in shared memory (bs = this thread's row in tile 0, already offset by t·32 bytes; tile nt
-// starts `tstride` bytes further per tile).
-template <int NTL, int TSTRIDE>
-__device__ __forceinline__ void load_b_smem(const uint8_t *bs, int p, uint4 (&b)[EX_NCH][2]) {
-#pragma unroll
-    for (int nt = 0; nt < NTL; ++nt) {
-        const uint4 *bp = reinterpret_cast<const uint4 *>(bs + nt * TSTRIDE + p * 128);
-        b[nt][0] = bp[0];
-        b[nt][1] = bp[1];
-    }
-}
-
-// The four group pairs of one K slice of a tile.
+// One K slice of a tile against NTL token tiles: the eight groups one at a time (two k16 MMAs
+// into a fresh sum per token tile, then the group's fp32 scale), so that only one group's
+// fragments (8 registers) and one token tile's operand are live. Holding a whole group pair's
+// fragments and the next pair's operands in registers instead spilled at the kernel's 96
+// registers and measured 4 % slower (k_experts<Q4, BOTH>, 64 tokens).
 template <int ENC, int NTL, int TSTRIDE>
 __device__ __forceinline__ void slice_mma(const uint8_t *tp, int lane, const uint8_t *bs, float (&acc)[EX_NCH][4]) {
     using X = ExTile<ENC>;
     const uint2 *sc = reinterpret_cast<const uint2 *>(tp + X::DB + (lane >> 2) * 32);   // scales, 2 pairs a load
-    uint32_t fr[4][4];
-    if (NTL > 2) {
-        // three or four tiles: one group (half a pair) decoded and applied at a time, which keeps
-        // the live fragments to 8 registers; per tile the accumulation order is the same
 #pragma unroll
-        for (int P = 0; P < 4; ++P) {
-            const uint2 sg = sc[(P >> 1)], s8 = sc[2 + (P >> 1)];
-            const uint32_t dg = P & 1 ? sg.y : sg.x, d8 = P & 1 ? s8.y : s8.x;
-            const float2 fg = __half22float2(*reinterpret_cast<const __half2 *>(&dg));
-            const float2 f8 = __half22float2(*reinterpret_cast<const __half2 *>(&d8));
+    for (int P = 0; P < 4; ++P) {
+        const uint2 sg = sc[(P >> 1)], s8 = sc[2 + (P >> 1)];
+        const uint32_t dg = P & 1 ? sg.y : sg.x, d8 = P & 1 ? s8.y : s8.x;
+        const float2 fg = __half22float2(*reinterpret_cast<const __half2 *>(&dg));
+        const float2 f8 = __half22float2(*reinterpret_cast<const __half2 *>(&d8));
 #pragma unroll
-            for (int hf = 0; hf < 2; ++hf) {                 // group 2P + hf
-                uint32_t fh[2][4];
-                group_frags<ENC>(tp, P, hf, lane, fh);
-                const float d0 = hf ? fg.y : fg.x, d1 = hf ? f8.y : f8.x;   // rows g / g + 8
+        for (int hf = 0; hf < 2; ++hf) {                     // group 2P + hf
+            uint32_t fh[2][4];
+            group_frags<ENC>(tp, P, hf, lane, fh);
+            const float d0 = hf ? fg.y : fg.x, d1 = hf ? f8.y : f8.x;   // rows g / g + 8
 #pragma unroll
-                for (int nt = 0; nt < NTL; ++nt) {
-                    const uint4 bq = *reinterpret_cast<const uint4 *>(bs + nt * TSTRIDE + P * 128 + hf * 16);
-                    const float z[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-                    float sj[4];
-                    mma_16816(sj, fh[0], bq.x, bq.y, z);
-                    mma_16816(sj, fh[1], bq.z, bq.w, sj);
-#pragma unroll
-                    for (int c = 0; c < 4; ++c) acc[nt][c] = fmaf(c >> 1 ? d1 : d0, sj[c], acc[nt][c]);
-                }
+            for (int nt = 0; nt < NTL; ++nt) {
+                const uint4 bq = *reinterpret_cast<const uint4 *>(bs + nt * TSTRIDE + P * 128 + hf * 16);
+                const float z[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                float sj[4];
+                mma_16816(sj, fh[0], bq.x, bq.y, z);
+                mma_16816(sj, fh[1], bq.z, bq.w, sj);
+                fma2_f32(acc[nt][0], acc[nt][1], d0, sj[0], sj[1]);
+                fma2_f32(acc[nt][2], acc[nt][3], d1, sj[2], sj[3]);
             }
         }
-        return;
     }
-    uint4 b0[EX_NCH][2], b1[EX_NCH][2];
-    load_b_smem<NTL, TSTRIDE>(bs, 0, b0);
-    load_b_smem<NTL, TSTRIDE>(bs, 1, b1);
-    uint2 sg = sc[0], s8 = sc[2];
-    tile_frags<ENC>(tp, 0, lane, fr);
-    pair_mma<NTL>(fr, sg.x, s8.x, b0, acc);
-    load_b_smem<NTL, TSTRIDE>(bs, 2, b0);
-    tile_frags<ENC>(tp, 1, lane, fr);
-    pair_mma<NTL>(fr, sg.y, s8.y, b1, acc);
-    load_b_smem<NTL, TSTRIDE>(bs, 3, b1);
-    sg = sc[1];
-    s8 = sc[3];
-    tile_frags<ENC>(tp, 2, lane, fr);
-    pair_mma<NTL>(fr, sg.x, s8.x, b0, acc);
-    tile_frags<ENC>(tp, 3, lane, fr);
-    pair_mma<NTL>(fr, sg.y, s8.y, b1, acc);
 }
 
-// Builds the decode tiles of every expert matrix of a layer from the raw Q4_0/Q8_0 rows: one
-// thread per (matrix, tile, lane). mats: device table (E·3) of matrix pointers, [3e + kind].
+// Builds the decode tiles of every expert of a layer from the raw Q4_0/Q8_0 rows: per expert
+// (3·MB bytes) the interleaved gate/up matrix (2·d_exp rows, tile rt = gate rows [8rt, 8rt + 8)
+// over the same up rows) and then the down matrix; one thread per (expert, tile, lane). mats:
+// device table (E·3) of matrix pointers, [3e + kind].
 template <int ENC>
 __global__ void k_tile_experts(const uint8_t *const *mats, uint8_t *out, int E, int D, int F) {
     using X = ExTile<ENC>;
@@ -754,13 +703,18 @@ __global__ void k_tile_experts(const uint8_t *const *mats, uint8_t *out, int E, 
     for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
         const int lane = (int)(i & 31);
         const long q = i >> 5;
-        const int tile = (int)(q % ntile), mat = (int)(q / ntile);
-        const bool down = mat % 3 == 2;
-        const int RT = (down ? D : F) / 16;
-        const int s = tile / RT, rt = tile - s * RT;
-        const size_t rowb = (size_t)(down ? F : D) / 32 * X::GB;
-        const uint8_t *src = mats[mat] + (size_t)rt * 16 * rowb + (size_t)s * 8 * X::GB;
-        tile_build_lane<ENC>(src, rowb, out + (size_t)mat * MB + (size_t)tile * X::TB, lane);
+        const int e = (int)(q / (3 * ntile)), r = (int)(q - (long)e * 3 * ntile);
+        uint8_t *dst = out + (size_t)e * 3 * MB + (size_t)r * X::TB;
+        if (r < 2 * ntile) {                                   // gate/up: D/256 slices of 2F/16 tiles
+            const int RT = F / 8, s = r / RT, rt = r - s * RT;
+            const size_t rowb = (size_t)D / 32 * X::GB, off = (size_t)rt * 8 * rowb + (size_t)s * 8 * X::GB;
+            tile_build_lane<ENC>(mats[3 * e] + off, mats[3 * e + 1] + off, rowb, dst, lane);
+        } else {                                               // down: F/256 slices of D/16 tiles
+            const int RT = D / 16, s = (r - 2 * ntile) / RT, rt = (r - 2 * ntile) - s * RT;
+            const size_t rowb = (size_t)F / 32 * X::GB;
+            const uint8_t *src = mats[3 * e + 2] + (size_t)rt * 16 * rowb + (size_t)s * 8 * X::GB;
+            tile_build_lane<ENC>(src, src + 8 * rowb, rowb, dst, lane);
+        }
     }
 }
 
@@ -780,9 +734,9 @@ __device__ __forceinline__ bool wait_count_geq(const int *p, int need) {
 
 // KIND_GATEUP, KIND_DOWN: one matrix kind per launch. KIND_BOTH: one launch for the whole
 // block: the gate/up items first, then the down items, from one work counter. A down item needs
-// the h rows of its token chunk, which the chunk's F/64 gate/up items store: each of those bumps
-// the chunk's counter (release) after its stores, and the down item's token-row warp waits for
-// the count (acquire, bounded) before copying the rows. Items are claimed in order, so a down
+// the h rows of its token chunk, which the chunk's F/64 gate/up items store: each consumer warp
+// of those bumps the chunk's counter (release) after its stores, and the down item's token-row
+// warp waits for F/64 × 8 (acquire, bounded) before copying the rows. Items are claimed in order, so a down
 // item only ever waits for gate/up items that running CTAs have already claimed: no CTA needs
 // another to become resident, and the down items fill the SMs the gate/up tail leaves idle.
 template <int ENC, int KIND>
@@ -792,7 +746,7 @@ __global__ void __launch_bounds__((EX_NP + EX_NW) * 32, 2) k_experts(ExpertArgs 
     constexpr bool HAS_GU = KIND != KIND_DOWN, HAS_DN = KIND != KIND_GATEUP;
     // Dynamic shared memory starts after the static arrays, 16-byte aligned only; the stages
     // (bulk copy destinations) are placed on 128 bytes (the launch adds the slack).
-    // Layout: stages | gate-sum exchange | barriers | stage metadata.
+    // Layout: stages | barriers | stage metadata.
     extern __shared__ __align__(16) uint8_t smem_raw[];
     uint8_t *const smem = smem_raw + ((128u - (smem_u32(smem_raw) & 127u)) & 127u);
     __shared__ Perm64 s_perm;
@@ -802,8 +756,7 @@ __global__ void __launch_bounds__((EX_NP + EX_NW) * 32, 2) k_experts(ExpertArgs 
     const int S = a.stages;
     const int tiles_gu = a.F / 64, tiles_dn = a.D / 128;     // row blocks per matrix and chunk
     const int ns_gu = a.D / EX_KSL, ns_dn = a.F / EX_KSL;     // K slices per item
-    float *xbuf = reinterpret_cast<float *>(smem + (size_t)S * C::STAGE);      // (4 tiles, NCH, 32, 2) gate sums
-    uint64_t *full = reinterpret_cast<uint64_t *>(xbuf + 4 * EX_NCH * 64);
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + (size_t)S * C::STAGE);   // STAGE: a multiple of 16
     uint64_t *empty = full + S;
     uint64_t *mready = empty + S;                              // stage metadata written
     StageMeta *meta = reinterpret_cast<StageMeta *>(mready + S);
@@ -870,7 +823,7 @@ __global__ void __launch_bounds__((EX_NP + EX_NW) * 32, 2) k_experts(ExpertArgs 
                 cur = md.item;
                 const bool gu = md.kind == KIND_GATEUP;
                 if (KIND == KIND_BOTH && !gu) {                // h of this chunk stored by its gate/up items
-                    if (!wait_count_geq(a.dep + md.chunk, tiles_gu) && lane == 0)
+                    if (!wait_count_geq(a.dep + md.chunk, tiles_gu * EX_NW) && lane == 0)
                         atomicCAS(a.status + WS_STATUS, ST_OK, ST_TIMEOUT_FULL);
                     __threadfence();
                 }
@@ -935,10 +888,9 @@ __global__ void __launch_bounds__((EX_NP + EX_NW) * 32, 2) k_experts(ExpertArgs 
                 uint8_t *dst = smem + (size_t)st * C::STAGE;
                 // the item's row tiles of K slice sl: contiguous in the tile layout
                 const uint8_t *te = a.tiles + (size_t)(3 * ex.x) * MB;
-                if (gu) {
-                    const size_t toff = ((size_t)sl * (a.F / 16) + (size_t)m * 4) * X::TB;
-                    bulk_g2s(dst, te + toff, 4 * X::TB, &full[st]);
-                    bulk_g2s(dst + 4 * X::TB, te + MB + toff, 4 * X::TB, &full[st]);
+                if (gu) {                                      // 8 interleaved gate/up tiles
+                    const size_t toff = ((size_t)sl * (a.F / 8) + (size_t)m * 8) * X::TB;
+                    bulk_g2s(dst, te + toff, 8 * X::TB, &full[st]);
                 } else {
                     const size_t toff = ((size_t)sl * (a.D / 16) + (size_t)m * 8) * X::TB;
                     bulk_g2s(dst, te + 2 * MB + toff, 8 * X::TB, &full[st]);
@@ -981,8 +933,7 @@ __global__ void __launch_bounds__((EX_NP + EX_NW) * 32, 2) k_experts(ExpertArgs 
         }
         constexpr int TS = 4 * C::BROW;                    // bytes from one 8-column tile's rows to the next
         const uint8_t *bs = smem + (size_t)st * C::STAGE + C::WBYTES + (g >> 1) * C::BROW + (g & 1) * C::LOFF + t * 32;
-        const int tidx = gu ? (cw & 1) * 4 + (cw >> 1) : cw;
-        const uint8_t *tp = smem + (size_t)st * C::STAGE + (size_t)tidx * X::TB;
+        const uint8_t *tp = smem + (size_t)st * C::STAGE + (size_t)cw * X::TB;
         switch (ntl) {
             case 1: slice_mma<ENC, 1, TS>(tp, lane, bs, acc); break;
             case 2: slice_mma<ENC, 2, TS>(tp, lane, bs, acc); break;
@@ -993,37 +944,24 @@ __global__ void __launch_bounds__((EX_NP + EX_NW) * 32, 2) k_experts(ExpertArgs 
         if (md.s != (gu ? ns_gu : ns_dn) - 1) continue;
         // ---------------- epilogue of the item: hi and lo partial sums added in fp32
         if (gu) {
-            const int mat = cw & 1, tile = cw >> 1;
-            float *xb = xbuf + (size_t)tile * EX_NCH * 64;
-            if (mat == 0) {
+            // row g: gate, row g + 8: up, of feature fr
+            const int fr = md.m * 64 + cw * 8 + g;
+            const int pos = (fr & ~63) + s_perm.elem_to_pos[fr & 63];
 #pragma unroll
-                for (int nt = 0; nt < EX_NCH; ++nt)
-                    if (nt < ntl)
-                        *reinterpret_cast<float2 *>(xb + (nt * 32 + lane) * 2) =
-                            make_float2(acc[nt][0] + acc[nt][1], acc[nt][2] + acc[nt][3]);
+            for (int nt = 0; nt < EX_NCH; ++nt) {
+                const int col = nt * 4 + t;                                                   // token of the item
+                if (nt >= ntl || col >= md.cnt) continue;
+                const float gv = acc[nt][0] + acc[nt][1], uv = acc[nt][2] + acc[nt][3];
+                const float h = gv / (1.0f + expf(-gv)) * uv;                                 // kernels.c:416, qwen3_moe.c:219
+                __half *hr = a.h_out + (size_t)(md.off + col) * 2 * a.F;                      // hi | lo
+                split_half(h, hr[pos], hr[a.F + pos]);
             }
-            named_bar_sync(1, EX_NW * 32);
-            if (mat == 1) {
-                const int fr = md.m * 64 + tile * 16 + g;                                     // features fr, fr + 8
-                const int pos0 = (fr & ~63) + s_perm.elem_to_pos[fr & 63];
-                const int pos1 = ((fr + 8) & ~63) + s_perm.elem_to_pos[(fr + 8) & 63];
-#pragma unroll
-                for (int nt = 0; nt < EX_NCH; ++nt) {
-                    const int col = nt * 4 + t;                                               // token of the item
-                    if (nt >= ntl || col >= md.cnt) continue;
-                    const float2 gv = *reinterpret_cast<const float2 *>(xb + (nt * 32 + lane) * 2);
-                    const float u0 = acc[nt][0] + acc[nt][1], u1 = acc[nt][2] + acc[nt][3];
-                    const float h0 = gv.x / (1.0f + expf(-gv.x)) * u0;                        // kernels.c:416,
-                    const float h1 = gv.y / (1.0f + expf(-gv.y)) * u1;                        // qwen3_moe.c:219
-                    __half *hr = a.h_out + (size_t)(md.off + col) * 2 * a.F;                  // hi | lo
-                    split_half(h0, hr[pos0], hr[a.F + pos0]);
-                    split_half(h1, hr[pos1], hr[a.F + pos1]);
+            if (KIND == KIND_BOTH) {
+                __syncwarp();
+                if (lane == 0) {
+                    __threadfence();                       // the warp's h stores before the count
+                    atomicAdd(a.dep + md.chunk, 1);
                 }
-            }
-            named_bar_sync(1, EX_NW * 32);                 // the exchange buffer is free again
-            if (KIND == KIND_BOTH && cw == 0 && lane == 0) {
-                __threadfence();                           // the CTA's h stores before the count
-                atomicAdd(a.dep + md.chunk, 1);
             }
         } else {
             const int row = md.m * 128 + cw * 16 + g;                                         // rows row, row + 8
@@ -1115,7 +1053,7 @@ template <int ENC, int KIND>
 static int plan_kernel(KernelPlan &p, bool deep) {
     using C = ExCfg<ENC, KIND>;
     auto *k = k_experts<ENC, KIND>;
-    const size_t fixed = sizeof(float) * 4 * EX_NCH * 64 + 8 * (sizeof(StageMeta) + 24) + 256;
+    const size_t fixed = 8 * (sizeof(StageMeta) + 24) + 256;
     cudaFuncAttributes fa;
     CPG_CUDA(cudaFuncGetAttributes(&fa, k));
     const size_t limit = (size_t)smem_optin() - fa.sharedSizeBytes;
@@ -1129,7 +1067,7 @@ static int plan_kernel(KernelPlan &p, bool deep) {
     CPG_REQUIRE(fixed + (size_t)S * C::STAGE <= limit, "expert kernel: a %d-byte stage does not fit in shared memory",
                 C::STAGE);
     p.stages = S;
-    p.smem = (size_t)S * C::STAGE + sizeof(float) * 4 * EX_NCH * 64 + S * sizeof(StageMeta) + 3 * S * sizeof(uint64_t) +
+    p.smem = (size_t)S * C::STAGE + S * sizeof(StageMeta) + 3 * S * sizeof(uint64_t) +
              128;                                           // alignment slack
     int rc = allow_max_smem((const void *)k);
     if (rc) return rc;

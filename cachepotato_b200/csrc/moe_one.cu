@@ -106,11 +106,10 @@ __device__ __forceinline__ void tile_one(const uint8_t *tp, const uint8_t *b, in
         mma_16816(sj, fr[1], b0.z, b0.w, sj);
         mma_16816(sj1, fr[2], b1.x, b1.y, z);
         mma_16816(sj1, fr[3], b1.z, b1.w, sj1);
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-            acc[c] = fmaf(c >> 1 ? f8.x : fg.x, sj[c], acc[c]);
-            acc[c] = fmaf(c >> 1 ? f8.y : fg.y, sj1[c], acc[c]);
-        }
+        fma2_f32(acc[0], acc[1], fg.x, sj[0], sj[1]);
+        fma2_f32(acc[0], acc[1], fg.y, sj1[0], sj1[1]);
+        fma2_f32(acc[2], acc[3], f8.x, sj[2], sj[3]);
+        fma2_f32(acc[2], acc[3], f8.y, sj1[2], sj1[3]);
     }
 }
 
@@ -135,7 +134,8 @@ __global__ void __launch_bounds__(O_THREADS, 1) k_moe_one(OneArgs a) {
     const int NB = a.slots;                                         // 16-row bands per round
     const size_t MB = (size_t)D * F / 32 * X::GB;                   // bytes per expert matrix
     // shared memory: xs f32 (D) | xb fp16 hi (D) | xb fp16 lo (D) | red (NW, 2, 32, 4) f32 |
-    // region: phase G (2, nsd, NB) tiles; phase D (K, nsf) tiles, then h as hi | lo per expert
+    // region: phase G (nsd, 2·NB) interleaved gate/up tiles (a 16-row band b of both matrices =
+    // tiles 2b, 2b + 1); phase D (K, nsf) tiles, then h as hi | lo per expert
     float *xs = reinterpret_cast<float *>(smem);
     __half *xb = reinterpret_cast<__half *>(xs + D);
     float *red = reinterpret_cast<float *>(xb + 2 * D);
@@ -269,9 +269,9 @@ __global__ void __launch_bounds__(O_THREADS, 1) k_moe_one(OneArgs a) {
     }
     const int bands = F / 16, n_units = K * bands;
     const int n0 = (int)((long)c * n_units / G), n1 = (int)((long)(c + 1) * n_units / G);
-    // one round: bands [r0, r1) of the range; per (expert chunk, matrix, K slice) one bulk copy of
-    // the chunk's consecutive tiles (contiguous in the tile layout). The bulk operations of one
-    // warp are served one after another, so they are dealt round robin over all warps.
+    // one round: bands [r0, r1) of the range; per (expert chunk, K slice) one bulk copy of the
+    // chunk's consecutive interleaved tiles (contiguous in the tile layout). The bulk operations of
+    // one warp are served one after another, so they are dealt round robin over all warps.
     auto issue_round = [&](int r0, int r1) {
         if (tid == 0) mbar_arrive_expect_tx(&s_bar[0], (uint32_t)(r1 - r0) * 2u * nsd * X::TB);
         __syncthreads();
@@ -279,12 +279,10 @@ __global__ void __launch_bounds__(O_THREADS, 1) k_moe_one(OneArgs a) {
         for (int n = r0; n < r1;) {
             const int j = n / bands, b = n - j * bands, cnt = min(r1 - n, bands - b);
             const uint8_t *te = a.tiles + (size_t)(3 * s_sel_e[j]) * MB;
-            for (int m = 0; m < 2; ++m)
-                for (int s = 0; s < nsd; ++s, ++q)
-                    if (lane == 0 && q % O_NW == warp)
-                        bulk_g2s(region + ((size_t)(m * nsd + s) * NB + (n - r0)) * X::TB,
-                                 te + (size_t)m * MB + ((size_t)s * bands + b) * X::TB, (uint32_t)cnt * X::TB,
-                                 &s_bar[0]);
+            for (int s = 0; s < nsd; ++s, ++q)
+                if (lane == 0 && q % O_NW == warp)
+                    bulk_g2s(region + ((size_t)s * 2 * NB + 2 * (n - r0)) * X::TB,
+                             te + ((size_t)s * 2 * bands + 2 * b) * X::TB, (uint32_t)cnt * 2 * X::TB, &s_bar[0]);
             n += cnt;
         }
     };
@@ -317,20 +315,20 @@ __global__ void __launch_bounds__(O_THREADS, 1) k_moe_one(OneArgs a) {
             const int g = lane >> 2, t = lane & 3;
             for (int s = warp; s < nsd; s += O_NW) {
                 const uint8_t *bp = reinterpret_cast<const uint8_t *>(xb + (g == 1 ? D : 0) + s * EX_KSL) + t * 32;
-                tile_one<ENC>(region + ((size_t)s * NB + k) * X::TB, bp, lane, ag);
-                tile_one<ENC>(region + ((size_t)(nsd + s) * NB + k) * X::TB, bp, lane, au);
+                tile_one<ENC>(region + ((size_t)s * 2 * NB + 2 * k) * X::TB, bp, lane, ag);       // features 16b..+7
+                tile_one<ENC>(region + ((size_t)s * 2 * NB + 2 * k + 1) * X::TB, bp, lane, au);   // 16b+8..+15
             }
             float4 *r4 = reinterpret_cast<float4 *>(red);
             r4[(warp * 2 + 0) * 32 + lane] = make_float4(ag[0], ag[1], ag[2], ag[3]);
             r4[(warp * 2 + 1) * 32 + lane] = make_float4(au[0], au[1], au[2], au[3]);
             __syncthreads();
-            if (tid < 16) {                                          // row tid of the band
-                const int rg = tid & 7, hi8 = tid >> 3;
+            if (tid < 16) {                                          // feature 16b + tid: MMA row rg of
+                const int rg = tid & 7, hi8 = tid >> 3;              // tile 2k + hi8 (gate), rg + 8 (up)
                 float gs = 0.0f, us = 0.0f;
                 for (int w = 0; w < O_NW; ++w) {
-                    const float4 vg = r4[(w * 2 + 0) * 32 + rg * 4], vu = r4[(w * 2 + 1) * 32 + rg * 4];
-                    gs += hi8 ? vg.z + vg.w : vg.x + vg.y;
-                    us += hi8 ? vu.z + vu.w : vu.x + vu.y;
+                    const float4 v = r4[(w * 2 + hi8) * 32 + rg * 4];
+                    gs += v.x + v.y;
+                    us += v.z + v.w;
                 }
                 const float silu = gs / (1.0f + expf(-gs));          // kernels.c:416
                 a.h[(size_t)j * F + b * 16 + tid] = silu * us;      // qwen3_moe.c:219
