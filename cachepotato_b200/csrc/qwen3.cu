@@ -442,7 +442,9 @@ struct AttnSeqs {
     size_t slot_elems;
 };
 constexpr int AS_SPLIT = 16, AS_THREADS = 256;
-__global__ void __launch_bounds__(AS_THREADS) k_attention_split(const float *__restrict__ q, float *__restrict__ kc,
+constexpr int AS_B = 4;                                           // positions per warp with loads in flight
+// At most 64 registers (four blocks per SM): a decode step's 512 blocks stay one wave.
+__global__ void __launch_bounds__(AS_THREADS, 4) k_attention_split(const float *__restrict__ q, float *__restrict__ kc,
                                                                 float *__restrict__ vc, const int *__restrict__ d_pos,
                                                                 int H, int KV, float *__restrict__ part, int *__restrict__ cnt,
                                                                 float *__restrict__ ao, const AttnNorm nr, const AttnSeqs seq) {
@@ -487,13 +489,26 @@ __global__ void __launch_bounds__(AS_THREADS) k_attention_split(const float *__r
                             : *reinterpret_cast<const float4 *>(q + ((size_t)i * H + h) * QW_HD + 4 * lane);
     const float scale = __fsqrt_rn((float)QW_HD);
     const float *kb = kc + (size_t)kh * QW_HD + 4 * lane, *vb = vc + (size_t)kh * QW_HD + 4 * lane;
-    for (int jj = warp; jj < len; jj += AS_THREADS / 32) {
-        const float4 kv = holds_new && j0 + jj == pnew ? *reinterpret_cast<const float4 *>(&s_qk[1][4 * lane])
-                                                       : *reinterpret_cast<const float4 *>(kb + (size_t)(j0 + jj) * ks);
-        float sv = fmaf(qv.x, kv.x, fmaf(qv.y, kv.y, fmaf(qv.z, kv.z, __fmul_rn(qv.w, kv.w))));
+    constexpr int NW = AS_THREADS / 32;
+    // a warp's positions warp, warp + NW, ...: AS_B key rows requested before any is used
+    for (int j = warp; j < len; j += NW * AS_B) {
+        float4 kv[AS_B];
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) sv += __shfl_xor_sync(0xffffffffu, sv, o);
-        if (lane == 0) s_sc[jj] = __fdiv_rn(sv, scale);
+        for (int u = 0; u < AS_B; ++u) {
+            const int jj = j + NW * u;
+            kv[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (jj < len)
+                kv[u] = holds_new && j0 + jj == pnew ? *reinterpret_cast<const float4 *>(&s_qk[1][4 * lane])
+                                                     : *reinterpret_cast<const float4 *>(kb + (size_t)(j0 + jj) * ks);
+        }
+#pragma unroll
+        for (int u = 0; u < AS_B; ++u) {
+            const int jj = j + NW * u;
+            float sv = fmaf(qv.x, kv[u].x, fmaf(qv.y, kv[u].y, fmaf(qv.z, kv[u].z, __fmul_rn(qv.w, kv[u].w))));
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) sv += __shfl_xor_sync(0xffffffffu, sv, o);
+            if (lane == 0 && jj < len) s_sc[jj] = __fdiv_rn(sv, scale);
+        }
     }
     __syncthreads();
     float mx = -INFINITY;
@@ -520,14 +535,26 @@ __global__ void __launch_bounds__(AS_THREADS) k_attention_split(const float *__r
 #pragma unroll
     for (int w = 0; w < AS_THREADS / 32; ++w) sum += s_red[w];
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int jj = warp; jj < len; jj += AS_THREADS / 32) {
-        const float4 v = holds_new && j0 + jj == pnew ? *reinterpret_cast<const float4 *>(&s_qk[2][4 * lane])
-                                                      : *reinterpret_cast<const float4 *>(vb + (size_t)(j0 + jj) * ks);
-        const float p = s_sc[jj];
-        acc.x = fmaf(p, v.x, acc.x);
-        acc.y = fmaf(p, v.y, acc.y);
-        acc.z = fmaf(p, v.z, acc.z);
-        acc.w = fmaf(p, v.w, acc.w);
+    for (int j = warp; j < len; j += NW * AS_B) {                // value rows in flight the same way,
+        float4 vv[AS_B];                                          // added in position order
+#pragma unroll
+        for (int u = 0; u < AS_B; ++u) {
+            const int jj = j + NW * u;
+            vv[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (jj < len)
+                vv[u] = holds_new && j0 + jj == pnew ? *reinterpret_cast<const float4 *>(&s_qk[2][4 * lane])
+                                                     : *reinterpret_cast<const float4 *>(vb + (size_t)(j0 + jj) * ks);
+        }
+#pragma unroll
+        for (int u = 0; u < AS_B; ++u) {
+            const int jj = j + NW * u;
+            if (jj >= len) break;
+            const float p = s_sc[jj];
+            acc.x = fmaf(p, vv[u].x, acc.x);
+            acc.y = fmaf(p, vv[u].y, acc.y);
+            acc.z = fmaf(p, vv[u].z, acc.z);
+            acc.w = fmaf(p, vv[u].w, acc.w);
+        }
     }
     *reinterpret_cast<float4 *>(&s_o[warp][4 * lane]) = acc;
     __syncthreads();
