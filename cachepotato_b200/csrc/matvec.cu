@@ -128,9 +128,17 @@ __device__ __forceinline__ void gemv_pair(const uint32_t *__restrict__ wp, const
                                           int n_in, float (&acc)[NT]) {
     constexpr int GB = ENC == CPG_ENC_Q4 ? 18 : 34;
     constexpr int NW = GB / 2;
+    // independent partial sums per vector (one vector: four FMA chains of 16 instead of one of
+    // 64), added in a fixed order at the end
+    constexpr int NA = NT == 1 ? 4 : NT == 2 ? 2 : 1;
     uint32_t w[NW];
 #pragma unroll
     for (int i = 0; i < NW; ++i) w[i] = wp[i];
+    float part[NT][NA];
+#pragma unroll
+    for (int t = 0; t < NT; ++t)
+#pragma unroll
+        for (int j = 0; j < NA; ++j) part[t][j] = 0.0f;
 #pragma unroll
     for (int half = 0; half < 2; ++half) {
         const int b0 = half * GB;
@@ -145,8 +153,8 @@ __device__ __forceinline__ void gemv_pair(const uint32_t *__restrict__ wp, const
                 const float hi = __fmul_rn((float)sext4(byte >> 4), d);
 #pragma unroll
                 for (int t = 0; t < NT; ++t) {
-                    acc[t] = fmaf(lo, xh[t * n_in + k * np], acc[t]);
-                    acc[t] = fmaf(hi, xh[t * n_in + (k + 16) * np], acc[t]);
+                    part[t][(2 * k) % NA] = fmaf(lo, xh[t * n_in + k * np], part[t][(2 * k) % NA]);
+                    part[t][(2 * k + 1) % NA] = fmaf(hi, xh[t * n_in + (k + 16) * np], part[t][(2 * k + 1) % NA]);
                 }
             }
         } else {
@@ -155,9 +163,15 @@ __device__ __forceinline__ void gemv_pair(const uint32_t *__restrict__ wp, const
                 const int bo = b0 + 2 + k;
                 const float v = __fmul_rn((float)(int)(int8_t)((w[bo / 4] >> ((bo % 4) * 8)) & 0xFFu), d);
 #pragma unroll
-                for (int t = 0; t < NT; ++t) acc[t] = fmaf(v, xh[t * n_in + k * np], acc[t]);
+                for (int t = 0; t < NT; ++t) part[t][k % NA] = fmaf(v, xh[t * n_in + k * np], part[t][k % NA]);
             }
         }
+    }
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+        if constexpr (NA == 4) acc[t] += (part[t][0] + part[t][1]) + (part[t][2] + part[t][3]);
+        else if constexpr (NA == 2) acc[t] += part[t][0] + part[t][1];
+        else acc[t] += part[t][0];
     }
 }
 
