@@ -120,7 +120,10 @@ __device__ __forceinline__ void row_partial(const uint8_t *__restrict__ row, int
 // lane decodes whole 64-value group pairs from there (word stride 9 or 17, odd: no bank
 // conflicts), with the same exact (float)q·d and fp32 FMA as the row-per-warp kernel above.
 constexpr int GV_ROWS = 16;
-constexpr int GV_CONS = 8;                      // consumer warps, two rows each per stage
+// Sixteen consumer warps, one row each per stage: with eight (two rows each) the Q8 lm_head's
+// consumers issued ~0.33 instructions per scheduler cycle; sixteen took whole-model decode from
+// 345 to 351 tok/s (at <= 96 registers a CTA fills an SM's register file: one CTA per SM).
+constexpr int GV_CONS = 16;
 constexpr int GV_MAXT = 4;
 
 template <int ENC, int NT>
@@ -279,8 +282,8 @@ __global__ void __launch_bounds__((GV_CONS + 1) * 32) k_gemv(const GemvArgs a) {
         while (tl >= t0[sg + 1]) ++sg;
         const int r0 = (tl - t0[sg]) * GV_ROWS, n_out = a.seg[sg].n_out, nr = min(GV_ROWS, n_out - r0);
 #pragma unroll
-        for (int rr = 0; rr < 2; ++rr) {
-            const int r = warp * 2 + rr;
+        for (int rr = 0; rr < GV_ROWS / GV_CONS; ++rr) {
+            const int r = warp * (GV_ROWS / GV_CONS) + rr;
             if (r >= nr) break;
             const uint32_t *row = reinterpret_cast<const uint32_t *>(ring + st * stage_bytes + (size_t)r * a.rowbytes);
             float acc[NT];
