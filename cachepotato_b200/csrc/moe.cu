@@ -5,8 +5,8 @@
 //              renormalisation (qwen3_moe.c:178-197). The CTAs of one token tile form a thread-
 //              block cluster (each holds a slice of the experts); after a cluster barrier, CTA r
 //              routes token r of the tile.
-//   k_experts<GATEUP>  per (expert, 64-row tile, chunk of up to 16 tokens): gate and up GEMMs,
-//              h = silu(g)·u (qwen3_moe.c:217-219). Each CTA first groups the (token, slot)
+//   k_experts<GATEUP>  per (expert, 64 features, chunk of up to 12 tokens): gate and up GEMMs
+//              on interleaved gate/up tiles, h = silu(g)·u (qwen3_moe.c:217-219). Each CTA first groups the (token, slot)
 //              pairs by expert in its own shared memory (CTA 0 publishes the table for the
 //              later kernels); batches over EX_GROUP_MAX pairs are grouped by k_group instead.
 //   k_experts<DOWN>    per (expert, 128-row tile, token chunk): y = Wd·h (qwen3_moe.c:220)
@@ -18,7 +18,7 @@
 //
 // Expert kernels: two producer warps fill an mbarrier ring of stages. One thread deals the work
 // items and streams the weight rows from the layer's decode tile copy (k_tile_experts) by one
-// bulk copy per matrix and stage (one 256-value K slice of the item's rows, no multicast); the
+// bulk copy per stage (one 256-value K slice of the item's rows, no multicast); the
 // other warp copies the same K slice of the item's token rows by 16-byte cp.async. Eight
 // consumer warps decode Q4_0 / Q8_0 groups in registers (exact integers in fp16) and feed
 // mma.m16n8k16 with fp32 accumulators; the group scale is applied in fp32 after each group's
